@@ -1,0 +1,477 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Lightning-Indexer decode step (BASELINE.json metric).
+
+Workload (default, BASELINE config 4, the metric's L=32K configuration): 8 indexer layers,
+per layer B=64 sequences with a bf16 key cache of L=32768 x 128 built by W_k from random
+hidden states (LayerNorm + RoPE, random-init sidecar weights), one decode step =
+project x[64,2048] -> q [64,64,128] (bf16) and w [64,64] (f32), dense score, top-2048
+per sequence.  Seeded synthetic data; the per-layer caches (4.3 GB) are far larger than
+the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N>1 runs one process per GPU (torchrun); every rank owns its own 64 sequences per layer
+(batch sharding, weak scaling, no collective on the data path).  Rank 0 prints one JSON
+line.  ``--impl reference`` times the CPU restatement of the reference path (oracle/,
+numpy) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = ("indexer scored keys/sec + per-step score+top-K latency at L=32K, %HBM peak, "
+          "1/2/4/8 B200")
+UNIT = "keys/s"
+
+
+# ----------------------------------------------------------------------------- helpers
+def hbm_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes from a committed ncu summary (``profiles/<name>.txt``)."""
+    path = ROOT / "profiles" / f"{name}.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch_full_size"):
+            return float(line.split("=")[1].split()[0])
+    return None
+
+
+class ClockSampler:
+    """Polls NVML SM clocks and throttle reasons of this rank's GPU during the timed region."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = torch.cuda.get_device_properties(device_index).uuid
+            handle = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if str(uuid) in u or u.endswith(str(uuid)):
+                    handle = h
+            if handle is None:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.nvml, self.handle = pynvml, handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self.ok = False
+        self.period = period_s
+        self._stop = threading.Event()
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"],
+                    "samples": 0}
+        n = self.nvml
+        names = {
+            "gpu_idle": getattr(n, "nvmlClocksEventReasonGpuIdle", 0x1),
+            "sw_power_cap": getattr(n, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(n, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "hw_power_brake_slowdown": getattr(n, "nvmlClocksEventReasonHwPowerBrakeSlowdown",
+                                               0x80),
+        }
+        seen = sorted({k for _, r in self.samples for k, bit in names.items()
+                       if r & bit and k != "gpu_idle"})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": seen, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- workload
+class Config4:
+    """8 layers, B=64 per GPU, L=32768 bf16 keys, top-2048."""
+
+    def __init__(self, device: torch.device, seed: int, layers: int = 8, batch: int = 64,
+                 length: int = 32768, k: int = 2048, hidden: int = 2048):
+        from dsa_b200.sidecar import encode_keys
+
+        self.device, self.layers, self.batch = device, layers, batch
+        self.length, self.k, self.hidden = length, k, hidden
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        std = hidden ** -0.5
+        bf = torch.bfloat16
+        self.wq = [(torch.randn(64 * 128, hidden, generator=g, device=device) * std).to(bf)
+                   for _ in range(layers)]
+        self.ww = [torch.randn(64, hidden, generator=g, device=device) * std
+                   for _ in range(layers)]
+        wk = [(torch.randn(128, hidden, generator=g, device=device) * std).to(bf)
+              for _ in range(layers)]
+        ln_w = torch.ones(128, device=device)
+        ln_b = torch.zeros(128, device=device)
+        pos = torch.arange(length, device=device)
+        self.keys = []
+        for layer in range(layers):
+            cache = torch.empty(batch, length, 128, device=device, dtype=bf)
+            for b in range(batch):
+                h = torch.randn(length, hidden, generator=g, device=device, dtype=bf)
+                cache[b] = encode_keys(h, wk[layer], ln_w, ln_b, pos)
+            self.keys.append(cache)
+        del wk
+        self.x = torch.randn(layers, batch, hidden, generator=g, device=device, dtype=bf)
+        self.qpos = torch.full((batch,), length - 1, device=device, dtype=torch.long)
+        self.scores = torch.empty(batch, length, device=device, dtype=torch.float32)
+        torch.cuda.synchronize(device)
+
+    @property
+    def keys_per_step(self) -> int:
+        return self.layers * self.batch * self.length
+
+    def score_bytes_per_launch(self) -> int:
+        """Algorithmic bytes of one dense-score launch: keys + q (bf16) + w (f32)."""
+        return self.batch * (self.length * 128 * 2 + 64 * 128 * 2 + 64 * 4)
+
+    def step_bytes(self) -> int:
+        """Per step: sum over sequences of L*256 + q + w + k*(4+4) (top-k out)."""
+        return self.layers * self.batch * (self.length * 256 + 64 * 128 * 2 + 64 * 4 +
+                                           self.k * 8)
+
+
+def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
+    from dsa_b200 import score_dense, scores_topk, topk
+    from dsa_b200.sidecar import encode_queries
+
+    wl = Config4(device, seed=1234 + rank, batch=args.batch, length=args.length, k=args.k)
+    stream = torch.cuda.current_stream(device)
+    score_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+    launches = {"n": 0}
+    topk_levels = 1 if wl.length <= 32768 else 2
+
+    def step(record: bool):
+        for layer in range(wl.layers):
+            q, w = encode_queries(wl.x[layer], wl.wq[layer], wl.ww[layer], wl.qpos)
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            score_dense(q, w, wl.keys[layer], out=wl.scores)
+            if record:
+                e1.record(stream)
+                score_events.append((e0, e1))
+                launches["n"] += 1 + topk_levels
+            topk(wl.scores, wl.k, sorted=False, index_dtype=torch.int32)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    ms_step = max_over_ranks(start.elapsed_time(end) / args.steps)
+    score_ms = statistics.fmean(a.elapsed_time(b) for a, b in score_events)
+    score_ms = max_over_ranks(score_ms)
+
+    # ---- end to end through the public API, host buffers, copies inside the region
+    x_host = wl.x.cpu().pin_memory()
+    x_dev = torch.empty_like(wl.x)
+    out_dev = torch.empty(wl.layers, wl.batch, wl.k, device=device, dtype=torch.int32)
+    out_host = torch.empty(out_dev.shape, dtype=torch.int32).pin_memory()
+    ws = torch.empty(0, device=device, dtype=torch.uint8)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        for layer in range(wl.layers):
+            q, w = encode_queries(x_dev[layer], wl.wq[layer], wl.ww[layer], wl.qpos)
+            idx, _ = scores_topk(q, w, wl.keys[layer], wl.k, sorted=False, workspace=ws)
+            out_dev[layer].copy_(idx)
+        out_host.copy_(out_dev, non_blocking=True)
+
+    from dsa_b200 import _capi
+
+    ws = torch.empty(_capi.lib().tdsa_score_topk_workspace_bytes(wl.batch, wl.length, wl.k),
+                     device=device, dtype=torch.uint8)
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_steps = max(3, min(args.steps, 50))
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+        stream.synchronize()  # the step's result is read on the host
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_steps)
+    barrier()
+
+    if rank != 0:
+        return None
+    peak, peak_kind = hbm_peak()
+    achieved = wl.score_bytes_per_launch() / (score_ms * 1e-3) / 1e9
+    keys_total = wl.keys_per_step * world
+    traffic = profile_traffic("score_dense_tc_cfg4")
+    line = {
+        "metric": METRIC,
+        "value": keys_total / (ms_step * 1e-3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) hidden states and random-init sidecar weights "
+                "(N(0,1/2048)); key caches built by W_k + LayerNorm + RoPE",
+        "config": {
+            "workload": "BASELINE config 4: 8 layers x (project, dense score, top-2048) per "
+                        "decode step",
+            "layers": wl.layers, "batch_per_gpu": wl.batch, "global_batch": wl.batch * world,
+            "seq_len": wl.length, "k": wl.k, "heads": 64, "head_dim": 128,
+            "topk_sorted": False, "parallelism": f"batch-sharded dp{world}",
+            "l2": f"no flush: {wl.layers * wl.batch * wl.length * 256 / 1e9:.1f} GB of keys "
+                  "per step per GPU >> 126 MB L2",
+        },
+        "roofline": {
+            "kernel": "score_dense_tc_kernel<bf16>",
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": wl.score_bytes_per_launch(),
+            "avg_launch_us": score_ms * 1e3,
+        },
+        "step_roofline": {
+            "algorithmic_bytes_per_step": wl.step_bytes(),
+            "achieved_gbs": wl.step_bytes() / (ms_step * 1e-3) / 1e9,
+            "frac": wl.step_bytes() / (ms_step * 1e-3) / 1e9 / peak,
+        },
+        "e2e": {
+            "value": keys_total / (e2e_ms * 1e-3),
+            "unit": UNIT,
+            "ms_per_step": e2e_ms,
+            "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
+            "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
+            "api": "dsa_b200.sidecar.encode_queries + dsa_b200.scores_topk (C ABI "
+                   "tdsa_score_topk)",
+        },
+        "gpu_launches": launches["n"],
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
+    return line
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_sample(wl_like, nseq: int):
+    """Host copies of a few config-4 sequences of layer 0 for the CPU restatement."""
+    keys = wl_like.keys[0][:nseq].float().cpu().numpy()
+    x = wl_like.x[0][:nseq].float().cpu().numpy()
+    wq = wl_like.wq[0].float().cpu().numpy()
+    ww = wl_like.ww[0].cpu().numpy()
+    return keys, x, wq, ww
+
+
+def cpu_step(keys, x, wq, ww, k, length):
+    """The reference path on the host: project (sidecar.py:78-87), score
+    (progressive_kernel.py:45-55 / sidecar.py:89-107), top-k (metrics.py:9-22)."""
+    import oracle
+
+    half = 32
+    inv = 10000.0 ** (-np.arange(half, dtype=np.float32) / half)
+    ang = np.float32(length - 1) * inv
+    cos, sin = np.cos(ang), np.sin(ang)
+    for s in range(keys.shape[0]):
+        q = (x[s] @ wq.T).reshape(64, 128)
+        r = q[:, :64]
+        q[:, :64] = np.concatenate((r[:, :half] * cos - r[:, half:] * sin,
+                                    r[:, half:] * cos + r[:, :half] * sin), axis=1)
+        w = (x[s] @ ww.T) * (64 * 128) ** -0.5
+        scores = oracle.full_scores(q, w, keys[s])
+        oracle.stable_topk(scores, k)
+
+
+def cpu_baseline(wl, seconds: float = 10.0) -> dict:
+    nseq = 4
+    keys, x, wq, ww = cpu_sample(wl, nseq)
+    cpu_step(keys[:1], x[:1], wq, ww, wl.k, wl.length)  # warm
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        cpu_step(keys, x, wq, ww, wl.k, wl.length)
+        done += nseq
+    dt = time.perf_counter() - t0
+    return {"value": done * wl.length / dt, "unit": UNIT, "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"{done} sequences of layer 0 (L={wl.length}, project + score + "
+                      f"top-{wl.k}) in {dt:.1f} s, numpy float32 (oracle/), "
+                      f"{os.cpu_count()} threads"}
+
+
+class HostSample:
+    """Config-4-shaped inputs generated on the host (no GPU) for the reference arm."""
+
+    def __init__(self, nseq: int, length: int, k: int, seed: int = 1234):
+        rng = np.random.default_rng(seed)
+        std = 2048 ** -0.5
+        self.k, self.length = k, length
+        self.wq = (rng.standard_normal((8192, 2048), dtype=np.float32) * std)
+        self.ww = (rng.standard_normal((64, 2048), dtype=np.float32) * std)
+        self.x = rng.standard_normal((nseq, 2048), dtype=np.float32)
+        keys = rng.standard_normal((nseq, length, 128), dtype=np.float32)
+        keys -= keys.mean(axis=-1, keepdims=True)
+        keys /= keys.std(axis=-1, keepdims=True) + 1e-6  # LayerNorm-like keys
+        self.keys = keys
+
+
+def run_reference(args) -> dict:
+    nseq = 2
+    hs = HostSample(nseq, args.length, args.k)
+    for _ in range(args.warmup):
+        cpu_step(hs.keys, hs.x, hs.wq, hs.ww, hs.k, hs.length)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(hs.keys, hs.x, hs.wq, hs.ww, hs.k, hs.length)
+    dt = time.perf_counter() - t0
+    value = args.steps * nseq * hs.length / dt
+    sample = (f"each step = {nseq} config-4 sequences (L={hs.length}, project + score + "
+              f"top-{hs.k}) of one layer, numpy float32 restatement of the reference "
+              f"(oracle/), {os.cpu_count()} threads")
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic, seeded (numpy), config-4 shapes",
+        "config": {"workload": "BASELINE config 4 sample on the host cores", "seq_len":
+                   hs.length, "k": hs.k, "sequences_per_step": nseq},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ----------------------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--length", type=int, default=32768)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=device,
+                                             timeout=datetime.timedelta(seconds=120))
+    from dsa_b200.build import build
+
+    if rank == 0 or world == 1:
+        build()
+    if world > 1:
+        torch.distributed.barrier()
+    line = run_ours(args, rank, world, device)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,95 @@
+"""ctypes binding of libtdsa.so (declared in include/tdsa.h).
+
+The library is the product: there is no Python or CPU implementation behind these calls.
+If the library is missing, every call raises RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtdsa.so"
+HEADER = Path(__file__).resolve().parent.parent / "include" / "tdsa.h"
+
+TDSA_OK = 0
+TDSA_ERR_INVALID = 1
+TDSA_ERR_UNSUPPORTED = 2
+TDSA_ERR_CUDA = 3
+TDSA_ERR_TIMEOUT = 4
+TDSA_ERR_ALIGN = 5
+TDSA_ERR_WORKSPACE = 6
+
+TDSA_F32 = 0
+TDSA_F16 = 1
+TDSA_BF16 = 2
+
+i32, i64, vp, sz = C.c_int, C.c_int64, C.c_void_p, C.c_size_t
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "tdsa_version": (C.c_char_p, []),
+    "tdsa_last_error": (C.c_char_p, []),
+    "tdsa_device_status": (i32, [C.POINTER(C.c_int), i32]),
+    "tdsa_score_dense": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp]),
+    "tdsa_topk_workspace_bytes": (sz, [i32, i32, i32]),
+    "tdsa_topk": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, sz, vp]),
+    "tdsa_merge_topk": (i32, [vp, vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp]),
+    "tdsa_score_topk_workspace_bytes": (sz, [i32, i32, i32]),
+    "tdsa_score_topk": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32, vp, i32,
+                              i64, vp, i64, vp, sz, vp]),
+}
+
+_lib: C.CDLL | None = None
+
+
+class TdsaError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"tdsa error {code}: {message}")
+        self.code = code
+
+
+def header_functions() -> list[str]:
+    """Names of the functions include/tdsa.h declares."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(tdsa_\w+)\s*\(", text, re.M)))
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is not built: run `python -m dsa_b200.build` (nvcc, sm_100a)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().tdsa_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int) -> None:
+    if rc == TDSA_OK:
+        return
+    msg = last_error()
+    if rc in (TDSA_ERR_INVALID, TDSA_ERR_ALIGN, TDSA_ERR_WORKSPACE):
+        raise ValueError(msg)
+    raise TdsaError(rc, msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args))
+
+
+def device_status(reset: bool = True) -> int:
+    out = C.c_int(0)
+    check(lib().tdsa_device_status(C.byref(out), 1 if reset else 0))
+    return out.value

@@ -1,0 +1,249 @@
+// extern "C" entry points of libtdsa: argument checks on the host, then the launchers.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tdsa {
+
+namespace {
+
+thread_local std::string g_last_error;
+
+constexpr int kMaxDevices = 64;
+
+// Device status word.  Lives with the module on every device that loads the library.
+__device__ int g_device_status = 0;
+
+int* g_status_ptr[kMaxDevices] = {nullptr};
+int g_sm_count[kMaxDevices] = {0};
+std::mutex g_mutex;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
+
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int device_sm_count(int device) {
+  if (device < 0 || device >= kMaxDevices) return 148;
+  if (g_sm_count[device] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    g_sm_count[device] = n > 0 ? n : 148;
+  }
+  return g_sm_count[device];
+}
+
+int* device_status_ptr() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swizzle) {
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+              cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || !fn)
+        return fail(TDSA_ERR_CUDA, "cuTensorMapEncodeTiled entry point not available");
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+  }
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) s[i] = strides_bytes[i];
+  }
+  const CUresult r = g_encode(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d,
+                              s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TDSA_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
+  return TDSA_OK;
+}
+
+namespace {
+
+int check_score_args(const void* q, int64_t q_bs, const float* w, int64_t w_bs, const void* k,
+                     int64_t k_bs, int64_t k_rs, int dtype, int batch, int length,
+                     const float* out, int64_t o_bs) {
+  if (dtype != TDSA_F32 && dtype != TDSA_F16 && dtype != TDSA_BF16)
+    return fail(TDSA_ERR_INVALID, "dtype must be TDSA_F32, TDSA_F16 or TDSA_BF16");
+  if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
+  if (length < 0) return fail(TDSA_ERR_INVALID, "length must be >= 0");
+  if (length == 0) return TDSA_OK;
+  if (!q || !w || !k || !out) return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (k_rs < kHeadDim) return fail(TDSA_ERR_INVALID, "key row stride must be >= 128");
+  if (batch > 1 && (q_bs < kHeads * kHeadDim || w_bs < kHeads ||
+                    k_bs < static_cast<int64_t>(length) * k_rs || o_bs < length))
+    return fail(TDSA_ERR_INVALID, "batch strides overlap the rows of one sequence");
+  if (dtype != TDSA_F32) {
+    if (!aligned16(q) || !aligned16(k))
+      return fail(TDSA_ERR_ALIGN, "16-bit queries/keys need 16-byte aligned base pointers");
+    if (k_rs % 8 || (batch > 1 && (k_bs % 8 || q_bs % 8)))
+      return fail(TDSA_ERR_ALIGN, "16-bit strides must be multiples of 8 elements");
+  }
+  return TDSA_OK;
+}
+
+int check_topk_out(void* out_idx, int index_bytes, int64_t idx_bs, const float* out_val,
+                   int64_t val_bs, int batch, int k) {
+  if (!out_idx) return fail(TDSA_ERR_INVALID, "out_indices is null");
+  if (index_bytes != 4 && index_bytes != 8)
+    return fail(TDSA_ERR_INVALID, "index_bytes must be 4 or 8");
+  if (batch > 1 && (idx_bs < k || (out_val && val_bs < k)))
+    return fail(TDSA_ERR_INVALID, "output row strides must be >= k");
+  return TDSA_OK;
+}
+
+}  // namespace
+}  // namespace tdsa
+
+using namespace tdsa;
+
+extern "C" {
+
+const char* tdsa_version(void) { return "tdsa-b200 0.1.0 sm_100a"; }
+
+const char* tdsa_last_error(void) { return g_last_error.c_str(); }
+
+int tdsa_device_status(int* status_out, int reset) {
+  if (!status_out) return fail(TDSA_ERR_INVALID, "status_out is null");
+  TDSA_CUDA_CHECK(cudaMemcpyFromSymbol(status_out, g_device_status, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    TDSA_CUDA_CHECK(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)));
+  }
+  return TDSA_OK;
+}
+
+int tdsa_score_dense(const void* queries, int64_t q_batch_stride, const float* weights,
+                     int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                     int64_t k_row_stride, int dtype, int batch, int length, float* scores,
+                     int64_t s_batch_stride, void* stream) {
+  int rc = check_score_args(queries, q_batch_stride, weights, w_batch_stride, keys,
+                            k_batch_stride, k_row_stride, dtype, batch, length, scores,
+                            s_batch_stride);
+  if (rc || length == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TDSA_F32)
+    return launch_score_dense_f32(static_cast<const float*>(queries), q_batch_stride, weights,
+                                  w_batch_stride, static_cast<const float*>(keys),
+                                  k_batch_stride, k_row_stride, batch, length, scores,
+                                  s_batch_stride, st);
+  int* status = device_status_ptr();
+  if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  return launch_score_dense_tc(queries, q_batch_stride, weights, w_batch_stride, keys,
+                               k_batch_stride, k_row_stride, dtype, batch, length, scores,
+                               s_batch_stride, st, status);
+}
+
+size_t tdsa_topk_workspace_bytes(int batch, int length, int k) {
+  if (batch < 1 || length < 1 || k < 1 || k > length) return 0;
+  return topk_workspace_bytes(batch, length, k);
+}
+
+int tdsa_topk(const float* scores, int64_t s_batch_stride, int batch, int length, int k,
+              int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
+              float* out_values, int64_t val_batch_stride, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  if (!scores) return fail(TDSA_ERR_INVALID, "scores is null");
+  if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
+  if (batch > 1 && s_batch_stride < length)
+    return fail(TDSA_ERR_INVALID, "score row stride must be >= length");
+  int rc = check_topk_out(out_indices, index_bytes, idx_batch_stride, out_values,
+                          val_batch_stride, batch, k);
+  if (rc) return rc;
+  return launch_topk(scores, s_batch_stride, nullptr, 0, batch, length, k, sorted ? 1 : 0,
+                     out_indices, index_bytes, idx_batch_stride, out_values, val_batch_stride,
+                     workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_merge_topk(const float* cand_values, const int32_t* cand_indices,
+                    int64_t cand_batch_stride, int batch, int count, int k, int sorted,
+                    void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                    float* out_values, int64_t val_batch_stride, void* stream) {
+  if (!cand_values || !cand_indices) return fail(TDSA_ERR_INVALID, "null candidate pointer");
+  if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
+  if (count > kTopkSegment)
+    return fail(TDSA_ERR_UNSUPPORTED, "merge takes at most 32768 candidates per row");
+  if (batch > 1 && cand_batch_stride < count)
+    return fail(TDSA_ERR_INVALID, "candidate row stride must be >= count");
+  int rc = check_topk_out(out_indices, index_bytes, idx_batch_stride, out_values,
+                          val_batch_stride, batch, k);
+  if (rc) return rc;
+  return launch_topk(cand_values, cand_batch_stride, cand_indices, cand_batch_stride, batch,
+                     count, k, sorted ? 1 : 0, out_indices, index_bytes, idx_batch_stride,
+                     out_values, val_batch_stride, nullptr, 0,
+                     static_cast<cudaStream_t>(stream));
+}
+
+size_t tdsa_score_topk_workspace_bytes(int batch, int length, int k) {
+  if (batch < 1 || length < 1 || k < 1 || k > length) return 0;
+  const size_t scores = (static_cast<size_t>(batch) * length * 4 + 255) & ~size_t(255);
+  return scores + topk_workspace_bytes(batch, length, k);
+}
+
+int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* weights,
+                    int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                    int64_t k_row_stride, int dtype, int batch, int length, int k, int sorted,
+                    void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                    float* out_values, int64_t val_batch_stride, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (length < 1) return fail(TDSA_ERR_INVALID, "length must be >= 1");
+  int rc = topk_check(length, k, sorted);
+  if (rc) return rc;
+  rc = check_topk_out(out_indices, index_bytes, idx_batch_stride, out_values, val_batch_stride,
+                      batch, k);
+  if (rc) return rc;
+  const size_t need = tdsa_score_topk_workspace_bytes(batch, length, k);
+  if (!workspace || workspace_bytes < need)
+    return fail(TDSA_ERR_WORKSPACE, "score_topk workspace missing or too small");
+  float* scores = static_cast<float*>(workspace);
+  const size_t score_bytes = (static_cast<size_t>(batch) * length * 4 + 255) & ~size_t(255);
+  rc = tdsa_score_dense(queries, q_batch_stride, weights, w_batch_stride, keys, k_batch_stride,
+                        k_row_stride, dtype, batch, length, scores, length, stream);
+  if (rc) return rc;
+  return launch_topk(scores, length, nullptr, 0, batch, length, k, sorted ? 1 : 0, out_indices,
+                     index_bytes, idx_batch_stride, out_values, val_batch_stride,
+                     static_cast<uint8_t*>(workspace) + score_bytes, workspace_bytes - score_bytes,
+                     static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,284 @@
+// Dense Lightning-Indexer scoring on the sm_100a tensor cores.
+//
+//   score[b][s] = sum_h w[b][h] * ReLU(q[b][h] . k[b][s]),   H = 64, D = 128
+//
+// One persistent CTA per SM walks a contiguous range of 128-key tiles (tiles of all
+// sequences are numbered b * tiles_per_seq + t).  Warp roles:
+//   warp 0      TMA producer: key tiles [128 keys x 128 dims] into a 5-stage smem ring
+//               (two 64-column boxes, 128-byte swizzle); the sequence's q [64 x 128] into
+//               one of two q slots when the sequence changes.
+//   warp 1      tcgen05 issuer: UMMA M=128 (keys) x N=64 (heads) x K=128 (8 x K16 steps),
+//               A = key tile, B = q, accumulator in TMEM (2 buffers x 64 f32 columns).
+//   warps 2..5  epilogue: each thread owns one key (one TMEM lane), loads its 64 head dots
+//               with tcgen05.ld, applies ReLU * w_h and sums the heads in registers -- no
+//               cross-thread reduction -- and stores one float per key (coalesced).
+// HBM traffic per key = its 256 bytes, read once; q/w per sequence come from L2.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "ptx.cuh"
+#include "score_epilogue.cuh"
+
+namespace tdsa {
+
+namespace {
+
+constexpr int kTileKeys = 128;
+constexpr int kStages = 5;
+constexpr int kStageBytes = kTileKeys * kHeadDim * 2;  // 32 KiB
+constexpr int kHalfBytes = kStageBytes / 2;            // 128 rows x 128 B
+constexpr int kQBytes = kHeads * kHeadDim * 2;         // 16 KiB
+constexpr int kQHalf = kQBytes / 2;                    // 64 rows x 128 B
+constexpr int kAccBufs = 2;
+constexpr int kTmemCols = 128;
+constexpr int kThreads = 192;
+constexpr int kBarrierBytes = 1024;
+constexpr int kSmemBytes = kStages * kStageBytes + 2 * kQBytes + kBarrierBytes + 1024;
+
+struct DenseArgs {
+  const float* w;
+  int64_t w_stride;
+  float* out;
+  int64_t out_stride;
+  int length;
+  int tiles_per_seq;
+  int64_t total_tiles;
+  int* status;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+template <bool kBF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    score_dense_tc_kernel(const __grid_constant__ CUtensorMap kmap,
+                          const __grid_constant__ CUtensorMap qmap, const DenseArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* stage_base = smem;
+  uint8_t* q_base = smem + kStages * kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(q_base + 2 * kQBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* qfull = empty + kStages;
+  uint64_t* qempty = qfull + 2;
+  uint64_t* accfull = qempty + 2;
+  uint64_t* accempty = accfull + kAccBufs;
+  uint64_t* done = accempty + kAccBufs;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t t0 = a.total_tiles * blockIdx.x / gridDim.x;
+  const int64_t t1 = a.total_tiles * (blockIdx.x + 1) / gridDim.x;
+  const int tps = a.tiles_per_seq;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qempty[s], 1);
+    }
+    for (int s = 0; s < kAccBufs; ++s) {
+      mbar_init(&accfull[s], 1);
+      mbar_init(&accempty[s], 4);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&qmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      const uint64_t pol_k = policy_evict_first();
+      const uint64_t pol_q = policy_evict_last();
+      int prev_b = -1;
+      uint32_t qcount = 0, it = 0;
+      for (int64_t t = t0; t < t1; ++t) {
+        const int b = static_cast<int>(t / tps);
+        const int tt = static_cast<int>(t - static_cast<int64_t>(b) * tps);
+        if (b != prev_b) {
+          const uint32_t slot = qcount & 1u, ph = (qcount >> 1) & 1u;
+          if (!mbar_wait(&qempty[slot], ph ^ 1u, abort_flag)) break;
+          mbar_arrive_expect_tx(&qfull[slot], kQBytes);
+          uint8_t* qd = q_base + slot * kQBytes;
+          tma_load_3d(qd, &qmap, &qfull[slot], 0, 0, b, pol_q);
+          tma_load_3d(qd + kQHalf, &qmap, &qfull[slot], 64, 0, b, pol_q);
+          ++qcount;
+          prev_b = b;
+        }
+        const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        uint8_t* dst = stage_base + s * kStageBytes;
+        tma_load_3d(dst, &kmap, &full[s], 0, tt * kTileKeys, b, pol_k);
+        tma_load_3d(dst + kHalfBytes, &kmap, &full[s], 64, tt * kTileKeys, b, pol_k);
+        ++it;
+      }
+      // Let every issued copy land before the CTA can exit (bounded, abort or not).
+      volatile int no_abort = 0;
+      for (uint32_t s = 0; s < kStages && s < it; ++s) {
+        const uint32_t n = (it - s + kStages - 1) / kStages;  // loads issued into stage s
+        mbar_wait(&full[s], (n - 1) & 1u, &no_abort);
+      }
+      for (uint32_t s = 0; s < 2 && s < qcount; ++s) {
+        const uint32_t n = (qcount - s + 1) / 2;
+        mbar_wait(&qfull[s], (n - 1) & 1u, &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ UMMA issuer
+      constexpr uint32_t idesc = umma_idesc_f16(kBF16, 128, kHeads);
+      int prev_b = -1;
+      uint32_t qcount = 0, it = 0, acc_it = 0, slot = 0;
+      for (int64_t t = t0; t < t1; ++t) {
+        const int b = static_cast<int>(t / tps);
+        if (b != prev_b) {
+          if (prev_b >= 0) umma_commit(&qempty[slot]);
+          slot = qcount & 1u;
+          if (!mbar_wait(&qfull[slot], (qcount >> 1) & 1u, abort_flag)) break;
+          ++qcount;
+          prev_b = b;
+        }
+        const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
+        if (!mbar_wait(&accempty[acc], aph ^ 1u, abort_flag)) break;
+        const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+        if (!mbar_wait(&full[s], ph, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(stage_base + s * kStageBytes);
+        const uint32_t b_addr = smem_u32(q_base + slot * kQBytes);
+        const uint32_t d_tmem = tmem_base + acc * kHeads;
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k) {
+          const uint64_t ad = sw128_kmajor_desc(a_addr + (k >> 2) * kHalfBytes + (k & 3) * 32);
+          const uint64_t bd = sw128_kmajor_desc(b_addr + (k >> 2) * kQHalf + (k & 3) * 32);
+          umma_f16(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+        umma_commit(&accfull[acc]);
+        ++it;
+        ++acc_it;
+      }
+      // All MMAs must be complete before TMEM is released.
+      umma_commit(done);
+      volatile int no_abort = 0;
+      mbar_wait(done, 0, &no_abort);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const uint32_t quad = static_cast<uint32_t>(warp & 3);
+    int prev_b = -1;
+    uint32_t acc_it = 0;
+    float wr[kHeads];
+    for (int64_t t = t0; t < t1; ++t) {
+      const int b = static_cast<int>(t / tps);
+      const int tt = static_cast<int>(t - static_cast<int64_t>(b) * tps);
+      if (b != prev_b) {
+        load_head_weights(a.w + static_cast<int64_t>(b) * a.w_stride, wr);
+        prev_b = b;
+      }
+      const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
+      if (!mbar_wait(&accfull[acc], aph, abort_flag)) break;
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      const uint32_t taddr = tmem_base + ((quad * 32u) << 16) + acc * kHeads;
+      tmem_ld32(taddr, r0);
+      tmem_ld32(taddr + 32, r1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accempty[acc]);
+      const float score = relu_weighted_sum(r0, r1, wr);
+      const int row = tt * kTileKeys + static_cast<int>(quad) * 32 + lane;
+      if (row < a.length) a.out[static_cast<int64_t>(b) * a.out_stride + row] = score;
+      ++acc_it;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, TDSA_ERR_TIMEOUT);
+}
+
+template <bool kBF16>
+int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs, const void* k,
+                      int64_t k_bs, int64_t k_rs, int batch, int length, float* out,
+                      int64_t o_bs, cudaStream_t stream, int* status) {
+  const CUtensorMapDataType dt =
+      kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap kmap, qmap;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(length),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t bstride = batch > 1 ? static_cast<uint64_t>(k_bs) * 2
+                                       : static_cast<uint64_t>(k_rs) * 2 * length;
+    const uint64_t strides[2] = {static_cast<uint64_t>(k_rs) * 2, bstride};
+    const uint32_t box[3] = {64, kTileKeys, 1};
+    int rc = encode_tmap(&kmap, dt, 3, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(kHeads),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t bstride = batch > 1 ? static_cast<uint64_t>(q_bs) * 2
+                                       : static_cast<uint64_t>(kHeads * kHeadDim * 2);
+    const uint64_t strides[2] = {static_cast<uint64_t>(kHeadDim) * 2, bstride};
+    const uint32_t box[3] = {64, kHeads, 1};
+    int rc = encode_tmap(&qmap, dt, 3, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  DenseArgs a;
+  a.w = w;
+  a.w_stride = w_bs;
+  a.out = out;
+  a.out_stride = o_bs;
+  a.length = length;
+  a.tiles_per_seq = (length + kTileKeys - 1) / kTileKeys;
+  a.total_tiles = static_cast<int64_t>(a.tiles_per_seq) * batch;
+  a.status = status;
+  const int dev = current_device();
+  const int sms = device_sm_count(dev);
+  const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
+  auto kern = score_dense_tc_kernel<kBF16>;
+  TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemBytes));
+  kern<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(kmap, qmap, a);
+  TDSA_CUDA_CHECK(cudaGetLastError());
+  return TDSA_OK;
+}
+
+}  // namespace
+
+int launch_score_dense_tc(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
+                          const void* k, int64_t k_bs, int64_t k_rs, int dtype, int batch,
+                          int length, float* out, int64_t o_bs, cudaStream_t stream,
+                          int* status) {
+  if (dtype == TDSA_BF16)
+    return launch_dense_tc_t<true>(q, q_bs, w, w_bs, k, k_bs, k_rs, batch, length, out, o_bs,
+                                   stream, status);
+  return launch_dense_tc_t<false>(q, q_bs, w, w_bs, k, k_bs, k_rs, batch, length, out, o_bs,
+                                  stream, status);
+}
+
+}  // namespace tdsa

@@ -1,0 +1,184 @@
+"""Device-tensor API of the indexer path (B200, sm_100a) on top of the C ABI.
+
+Shapes follow the reference project temporal_dsa: H = 64 heads, D = 128 dims,
+``score[s] = sum_h w[h] * ReLU(q[h] . k[s])``.  Inputs must be CUDA tensors; kernels run
+on the current torch stream.  Nothing here computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _capi as capi
+
+HEADS = 64
+HEAD_DIM = 128
+
+_DTYPES = {torch.float32: capi.TDSA_F32, torch.float16: capi.TDSA_F16,
+           torch.bfloat16: capi.TDSA_BF16}
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError("the B200 indexer kernels require CUDA tensors")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _aligned(t: torch.Tensor) -> bool:
+    return t.data_ptr() % 16 == 0
+
+
+def prepare_queries(q: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """[B,64,128] with contiguous rows, 16-byte aligned (small: copied if needed)."""
+    if q.dtype != dtype:
+        raise ValueError("queries and keys must share a dtype")
+    q = q.contiguous()
+    if not _aligned(q):
+        q = q.clone()
+    return q
+
+
+def prepare_weights(w: torch.Tensor) -> torch.Tensor:
+    w = w.to(torch.float32).contiguous()
+    if not _aligned(w):
+        w = w.clone()
+    return w
+
+
+def prepare_keys(keys: torch.Tensor) -> torch.Tensor:
+    """[B,L,128]: unit stride on dims; TMA wants 16-byte aligned base and row/batch strides."""
+    if keys.dtype not in _DTYPES:
+        raise ValueError("keys must be float32, float16 or bfloat16")
+    ok = keys.stride(-1) == 1
+    if ok and keys.dtype != torch.float32:
+        ok = _aligned(keys) and keys.stride(-2) % 8 == 0 and (
+            keys.shape[0] == 1 or keys.stride(0) % 8 == 0)
+    if not ok:
+        keys = keys.contiguous()
+        if keys.dtype != torch.float32 and not _aligned(keys):
+            keys = keys.clone()
+    return keys
+
+
+def as_batched(q: torch.Tensor, w: torch.Tensor, keys: torch.Tensor):
+    """Accepts the single-sequence ([64,128], [64], [L,128]) or batched layout."""
+    single = keys.dim() == 2
+    if single:
+        if q.shape != (HEADS, HEAD_DIM) or w.shape != (HEADS,):
+            raise ValueError("expected queries [64,128] and weights [64]")
+        if keys.shape[1] != HEAD_DIM:
+            raise ValueError("expected keys [L,128]")
+        return q.unsqueeze(0), w.unsqueeze(0), keys.unsqueeze(0), True
+    if keys.dim() != 3 or keys.shape[2] != HEAD_DIM:
+        raise ValueError("expected keys [B,L,128]")
+    b = keys.shape[0]
+    if q.shape != (b, HEADS, HEAD_DIM) or w.shape != (b, HEADS):
+        raise ValueError("expected queries [B,64,128] and weights [B,64]")
+    return q, w, keys, False
+
+
+def score_dense(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Dense indexer scores: [64,128],[64],[L,128] -> [L] or batched -> [B,L] (float32)."""
+    require_cuda(queries, weights, keys)
+    q, w, k, single = as_batched(queries, weights, keys)
+    k = prepare_keys(k)
+    q = prepare_queries(q, k.dtype)
+    w = prepare_weights(w)
+    bsz, length = k.shape[0], k.shape[1]
+    if out is None:
+        out = torch.empty(bsz, length, device=k.device, dtype=torch.float32)
+    elif single:
+        out = out.view(1, -1)
+    if out.dtype != torch.float32 or out.shape != (bsz, length) or out.stride(-1) != 1:
+        raise ValueError("out must be float32 [B,L] with unit last stride")
+    if length:
+        capi.call("tdsa_score_dense", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
+                  k.data_ptr(), k.stride(0), k.stride(1), _DTYPES[k.dtype], bsz, length,
+                  out.data_ptr(), out.stride(0), stream_ptr(k.device))
+    return out[0] if single else out
+
+
+def topk(scores: torch.Tensor, k: int, *, sorted: bool = True,
+         index_dtype: torch.dtype = torch.int64) -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact row-wise top-k with the reference's tie rule -> (indices, values).
+
+    sorted=True: descending score, equal scores by ascending index (stable_topk order);
+    sorted=False: the same set in ascending index order.
+    """
+    require_cuda(scores)
+    if scores.dtype != torch.float32:
+        raise ValueError("scores must be float32")
+    single = scores.dim() == 1
+    s = scores.unsqueeze(0) if single else scores
+    if s.dim() != 2:
+        raise ValueError("scores must be [L] or [B,L]")
+    if s.stride(-1) != 1:
+        s = s.contiguous()
+    bsz, length = s.shape
+    if not 0 < k <= length:
+        raise ValueError(f"k={k} is invalid for {length} values")
+    if index_dtype not in (torch.int32, torch.int64):
+        raise ValueError("index_dtype must be int32 or int64")
+    idx = torch.empty(bsz, k, device=s.device, dtype=index_dtype)
+    val = torch.empty(bsz, k, device=s.device, dtype=torch.float32)
+    nbytes = capi.lib().tdsa_topk_workspace_bytes(bsz, length, k)
+    ws = torch.empty(max(nbytes, 1), device=s.device, dtype=torch.uint8)
+    capi.call("tdsa_topk", s.data_ptr(), s.stride(0), bsz, length, k, int(bool(sorted)),
+              idx.data_ptr(), idx.element_size(), idx.stride(0), val.data_ptr(), val.stride(0),
+              ws.data_ptr(), nbytes, stream_ptr(s.device))
+    return (idx[0], val[0]) if single else (idx, val)
+
+
+def merge_topk(cand_values: torch.Tensor, cand_indices: torch.Tensor, k: int, *,
+               sorted: bool = True, index_dtype: torch.dtype = torch.int64):
+    """Top-k of per-shard candidates (rows in ascending index order) -> (indices, values)."""
+    require_cuda(cand_values, cand_indices)
+    v = cand_values.to(torch.float32).contiguous()
+    i = cand_indices.to(torch.int32).contiguous()
+    single = v.dim() == 1
+    if single:
+        v, i = v.unsqueeze(0), i.unsqueeze(0)
+    bsz, count = v.shape
+    if not 0 < k <= count:
+        raise ValueError(f"k={k} is invalid for {count} candidates")
+    idx = torch.empty(bsz, k, device=v.device, dtype=index_dtype)
+    val = torch.empty(bsz, k, device=v.device, dtype=torch.float32)
+    capi.call("tdsa_merge_topk", v.data_ptr(), i.data_ptr(), v.stride(0), bsz, count, k,
+              int(bool(sorted)), idx.data_ptr(), idx.element_size(), idx.stride(0),
+              val.data_ptr(), val.stride(0), stream_ptr(v.device))
+    return (idx[0], val[0]) if single else (idx, val)
+
+
+def scores_topk(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor, k: int, *,
+                sorted: bool = True, index_dtype: torch.dtype = torch.int32,
+                workspace: torch.Tensor | None = None):
+    """Fused dense score + top-k per sequence -> (indices [B,k], scores [B,k])."""
+    require_cuda(queries, weights, keys)
+    q, w, kk, single = as_batched(queries, weights, keys)
+    kk = prepare_keys(kk)
+    q = prepare_queries(q, kk.dtype)
+    w = prepare_weights(w)
+    bsz, length = kk.shape[0], kk.shape[1]
+    if not 0 < k <= length:
+        raise ValueError(f"k={k} is invalid for {length} keys")
+    idx = torch.empty(bsz, k, device=kk.device, dtype=index_dtype)
+    val = torch.empty(bsz, k, device=kk.device, dtype=torch.float32)
+    nbytes = capi.lib().tdsa_score_topk_workspace_bytes(bsz, length, k)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, device=kk.device, dtype=torch.uint8)
+    capi.call("tdsa_score_topk", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
+              kk.data_ptr(), kk.stride(0), kk.stride(1), _DTYPES[kk.dtype], bsz, length, k,
+              int(bool(sorted)), idx.data_ptr(), idx.element_size(), idx.stride(0),
+              val.data_ptr(), val.stride(0), workspace.data_ptr(), nbytes,
+              stream_ptr(kk.device))
+    return (idx[0], val[0]) if single else (idx, val)
+
+
+def device_status(reset: bool = True) -> int:
+    """OR of error bits raised by kernels on the current device since the last reset."""
+    return capi.device_status(reset)

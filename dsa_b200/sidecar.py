@@ -1,0 +1,90 @@
+"""Batched indexer scoring with the signature of the reference sidecar.
+
+Mirrors ``LightningIndexerSidecar.score_encoded`` (src/temporal_dsa/sidecar.py:89-107):
+queries [B,Q,64,128], weights [B,Q,64], keys [B,L,128] -> scores [B,Q,L] float32.  The
+reference materialises [B,Q,64,L] head dots per key chunk; the B200 kernel keeps them in
+TMEM, so ``key_chunk_size`` is accepted for call-site compatibility and has no effect.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .indexer import HEAD_DIM, HEADS, require_cuda, score_dense
+
+
+def score_encoded(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor, *,
+                  key_chunk_size: int | None = None) -> torch.Tensor:
+    require_cuda(queries, weights, keys)
+    if queries.ndim != 4 or weights.shape != queries.shape[:-1]:
+        raise ValueError("queries must be [batch,query,heads,dim]")
+    if keys.ndim != 3 or keys.shape[0] != queries.shape[0]:
+        raise ValueError("keys must be [batch,key,dim]")
+    if queries.shape[2:] != (HEADS, HEAD_DIM) or keys.shape[2] != HEAD_DIM:
+        raise ValueError("the B200 indexer kernels take 64 heads x 128 dims")
+    if queries.dtype != keys.dtype:
+        raise ValueError("queries and keys must share a dtype")
+    bsz, nq = queries.shape[:2]
+    out = torch.empty(bsz, nq, keys.shape[1], device=keys.device, dtype=torch.float32)
+    for qi in range(nq):
+        score_dense(queries[:, qi], weights[:, qi], keys, out=out[:, qi])
+    return out
+
+
+class SidecarScoring:
+    """Mixin giving a sidecar-like module the B200 ``score_encoded``."""
+
+    def score_encoded(self, queries, weights, keys, *, key_chunk_size=None):
+        return score_encoded(queries, weights, keys, key_chunk_size=key_chunk_size)
+
+
+# --------------------------------------------------------------------------- projection
+# The sidecar's query/key projections (sidecar.py:10-28, :66-87), run as plain library
+# GEMMs (cuBLAS through torch.matmul) and elementwise ops on the device.
+
+def apply_noninterleaved_rope(x: torch.Tensor, positions: torch.Tensor, *,
+                              theta: float = 10_000.0) -> torch.Tensor:
+    """sidecar.py:10-28 -- RoPE on the two halves of the last axis (V3.2 indexer layout)."""
+    if x.shape[-1] % 2:
+        raise ValueError("RoPE dimension must be even")
+    half = x.shape[-1] // 2
+    inv_freq = theta ** (-torch.arange(half, device=x.device, dtype=torch.float32) / half)
+    angles = positions.to(torch.float32).unsqueeze(-1) * inv_freq
+    cos = torch.cos(angles).to(x.dtype)
+    sin = torch.sin(angles).to(x.dtype)
+    while cos.ndim < x.ndim:
+        cos = cos.unsqueeze(-2)
+        sin = sin.unsqueeze(-2)
+    first, second = x[..., :half], x[..., half:]
+    return torch.cat((first * cos - second * sin, second * cos + first * sin), dim=-1)
+
+
+def encode_queries(hidden: torch.Tensor, wq: torch.Tensor, ww: torch.Tensor,
+                   positions: torch.Tensor, *, rope_dim: int = 64,
+                   rope_theta: float = 10_000.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """sidecar.py:78-87 -- hidden [...,2048] -> q [...,64,128] (hidden dtype), w [...,64] f32.
+
+    wq [64*128, 2048] and ww [64, 2048] are the nn.Linear weights; the head weights are
+    computed in float32 and scaled by (64*128)^-1/2 as in the reference.
+    """
+    require_cuda(hidden, wq, ww)
+    q = torch.matmul(hidden, wq.t()).view(*hidden.shape[:-1], HEADS, HEAD_DIM)
+    if rope_dim:
+        q = torch.cat((apply_noninterleaved_rope(q[..., :rope_dim], positions, theta=rope_theta),
+                       q[..., rope_dim:]), dim=-1)
+    w = torch.matmul(hidden.float(), ww.float().t()) * (HEADS * HEAD_DIM) ** -0.5
+    return q, w
+
+
+def encode_keys(hidden: torch.Tensor, wk: torch.Tensor, norm_weight: torch.Tensor,
+                norm_bias: torch.Tensor, positions: torch.Tensor, *, rope_dim: int = 64,
+                rope_theta: float = 10_000.0, eps: float = 1e-6) -> torch.Tensor:
+    """sidecar.py:74-76 -- k = RoPE(LayerNorm(hidden @ wk^T)) [..., 128]."""
+    require_cuda(hidden, wk)
+    k = torch.matmul(hidden, wk.t())
+    k = torch.nn.functional.layer_norm(k, (HEAD_DIM,), norm_weight.to(k.dtype),
+                                       norm_bias.to(k.dtype), eps)
+    if rope_dim:
+        k = torch.cat((apply_noninterleaved_rope(k[..., :rope_dim], positions, theta=rope_theta),
+                       k[..., rope_dim:]), dim=-1)
+    return k

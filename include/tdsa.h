@@ -1,0 +1,119 @@
+/*
+ * tdsa.h -- C ABI of the B200 (sm_100a) Lightning-Indexer decode path.
+ *
+ * Plain pointers, sizes and strides; no framework types.  Every device pointer must point
+ * into memory of the CUDA device current on the calling thread; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).  Calls are asynchronous on `stream` unless noted.
+ * Return value: TDSA_OK or an error code; tdsa_last_error() gives the message
+ * (thread-local).  Argument errors are detected on the host before any launch.
+ *
+ * Index semantics follow the reference project temporal_dsa (psa1582/dsa):
+ *   score[s] = sum_h w[h] * ReLU(q[h] . k[s]),  H = 64 heads, D = 128 dims;
+ *   top-k order = descending score, equal scores by ascending index.
+ * Strides are in elements of the pointed-to type.
+ */
+#ifndef TDSA_H_
+#define TDSA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum tdsa_status {
+  TDSA_OK = 0,
+  TDSA_ERR_INVALID = 1,     /* bad shape, stride, size or pointer argument           */
+  TDSA_ERR_UNSUPPORTED = 2, /* valid request this build does not implement            */
+  TDSA_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed                      */
+  TDSA_ERR_TIMEOUT = 4,     /* device status bit: a bounded in-kernel wait ran out    */
+  TDSA_ERR_ALIGN = 5,       /* a pointer or stride breaks the 16-byte TMA alignment   */
+  TDSA_ERR_WORKSPACE = 6    /* workspace missing or smaller than the query said       */
+};
+
+enum tdsa_dtype { TDSA_F32 = 0, TDSA_F16 = 1, TDSA_BF16 = 2 };
+
+/* Library version string. */
+const char* tdsa_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* tdsa_last_error(void);
+
+/* Reads (and with reset != 0 clears) the device status word of the current device: the
+ * OR of error bits kernels raised (TDSA_ERR_TIMEOUT when a bounded wait ran out).
+ * Synchronous. */
+int tdsa_device_status(int* status_out, int reset);
+
+/*
+ * Dense indexer scores for a batch of independent sequences.
+ * Replaces: full_scores_triton + _full_score_kernel (src/temporal_dsa/progressive_kernel.py:
+ *   362-375, 195-215), torch_full_scores (:45-55) and the batched
+ *   LightningIndexerSidecar.score_encoded (src/temporal_dsa/sidecar.py:89-107, Q = 1).
+ * queries  [batch][64][128] of `dtype` (rows of one sequence contiguous), batch stride
+ *          q_batch_stride (>= 8192);
+ * weights  [batch][64] float32, batch stride w_batch_stride (>= 64);
+ * keys     [batch][length][128] of `dtype`, rows k_row_stride apart (>= 128), sequences
+ *          k_batch_stride apart;
+ * scores   [batch][length] float32 out, batch stride s_batch_stride (>= length).
+ * dtype TDSA_BF16 / TDSA_F16 run on the tcgen05 tensor cores (f32 accumulation);
+ * TDSA_F32 runs an FP32 CUDA-core kernel.  16-bit queries/keys need 16-byte aligned bases
+ * and strides that are multiples of 8 elements (TMA).
+ */
+int tdsa_score_dense(const void* queries, int64_t q_batch_stride, const float* weights,
+                     int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                     int64_t k_row_stride, int dtype, int batch, int length, float* scores,
+                     int64_t s_batch_stride, void* stream);
+
+/* Bytes of device workspace tdsa_topk needs for these sizes (0 if none). */
+size_t tdsa_topk_workspace_bytes(int batch, int length, int k);
+
+/*
+ * Row-wise exact top-k of a [batch][length] float32 score matrix.
+ * Replaces: stable_topk (src/temporal_dsa/metrics.py:9-22) and the torch.topk calls that
+ *   follow the score kernels (scripts/benchmark_progressive_dsa.py:117-169).
+ * sorted != 0: each row in stable_topk order (score descending, ties by ascending index);
+ * sorted == 0: the same index set in ascending index order.
+ * out_indices [batch][k] of index_bytes (4 = int32, 8 = int64), row stride idx_batch_stride;
+ * out_values  [batch][k] float32 or NULL, row stride val_batch_stride.
+ * NaN ranks above +inf; -0.0 equals +0.0.  1 <= k <= length; k <= 8192 when sorted or
+ * when length > 32768.
+ */
+int tdsa_topk(const float* scores, int64_t s_batch_stride, int batch, int length, int k,
+              int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
+              float* out_values, int64_t val_batch_stride, void* workspace,
+              size_t workspace_bytes, void* stream);
+
+/*
+ * Merge candidate lists into a top-k per row (the second level of a sharded top-k: the
+ * global top-k is contained in the union of the shards' local top-k).  New entry point,
+ * no counterpart in the reference (which never shards).
+ * cand_values [batch][count] float32 and cand_indices [batch][count] int32, row stride
+ * cand_batch_stride; within a row the candidates must be in ascending index order (what
+ * tdsa_topk with sorted == 0 produces, concatenated shard by shard).
+ */
+int tdsa_merge_topk(const float* cand_values, const int32_t* cand_indices,
+                    int64_t cand_batch_stride, int batch, int count, int k, int sorted,
+                    void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                    float* out_values, int64_t val_batch_stride, void* stream);
+
+/* Bytes of device workspace tdsa_score_topk needs. */
+size_t tdsa_score_topk_workspace_bytes(int batch, int length, int k);
+
+/*
+ * Dense scores followed by the row-wise top-k (tdsa_score_dense + tdsa_topk), the
+ * "full_plus_topk" step of scripts/benchmark_progressive_dsa.py:117-123.  The scores live
+ * in the caller's workspace.
+ */
+int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* weights,
+                    int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                    int64_t k_row_stride, int dtype, int batch, int length, int k, int sorted,
+                    void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                    float* out_values, int64_t val_batch_stride, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TDSA_H_ */

@@ -1,0 +1,241 @@
+"""GPU parity: dense scoring and top-k through the C ABI against the oracle and goldens.
+
+Tolerances: BF16/FP16 scores within 1e-2 relative, FP32 within 1e-5
+relative.  Both are applied norm-wise -- relative to sum_h |w_h| |q_h . k|, the magnitude a
+score's rounding error scales with -- because the signed head weights can cancel a score
+to ~0, where a plain relative error is undefined.  The tighter 1e-5 norm-wise bound is also
+checked for BF16, since the kernel accumulates exact bf16 products in float32.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests._util import assert_scores_close, assert_topk_equivalent, normwise_bound
+from tests.conftest import bf16_from_bits, cfg1_inputs, load_golden
+
+pytestmark = pytest.mark.gpu
+
+LENGTHS = [1, 17, 63, 64, 65, 127, 128, 129, 192, 256, 257]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from dsa_b200.build import build
+
+    build()
+    yield
+    from dsa_b200 import device_status
+
+    assert device_status() == 0, "a kernel raised a device status bit"
+
+
+def cuda(x, dtype=None):
+    t = torch.as_tensor(np.asarray(x)).cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+@pytest.mark.parametrize("length", LENGTHS)
+def test_full_scores_bf16_matches_reference_golden(length):
+    from dsa_b200.progressive_kernel import full_scores_triton
+
+    g = load_golden("progressive_kernel")
+    q = bf16_from_bits(g["bf16_q"])
+    k = bf16_from_bits(g[f"bf16_L{length}_keys"])
+    w = g["bf16_w"]
+    got = full_scores_triton(cuda(q, torch.bfloat16), cuda(w), cuda(k, torch.bfloat16))
+    assert got.dtype == torch.float32 and got.shape == (length,)
+    scale = normwise_bound(q, w, k)
+    got = got.cpu().numpy()
+    assert_scores_close(got, g[f"bf16_L{length}_scores"], scale, rtol=1e-5, atol=1e-7,
+                        msg="bf16 vs reference golden")
+    assert_scores_close(got, oracle.full_scores(q, w, k), scale, rtol=1e-5, atol=1e-7,
+                        msg="bf16 vs oracle")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("length", [1, 100, 128, 1000, 4099])
+def test_dense_16bit_matches_oracle(dtype, length):
+    gen = torch.Generator().manual_seed(length)
+    q = (torch.randn(64, 128, generator=gen) / math.sqrt(128)).to(dtype)
+    w = torch.randn(64, generator=gen) / 8
+    k = torch.randn(length, 128, generator=gen).to(dtype)
+    from dsa_b200 import score_dense
+
+    got = score_dense(q.cuda(), w.cuda(), k.cuda()).cpu().numpy()
+    qf, kf = q.float().numpy(), k.float().numpy()
+    want = oracle.full_scores(qf, w.numpy(), kf)
+    scale = normwise_bound(qf, w.numpy(), kf)
+    assert_scores_close(got, want, scale, rtol=1e-5, atol=1e-7, msg=str(dtype))
+    # the stated BF16 bar, plain relative with an absolute floor
+    np.testing.assert_allclose(got, want, rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("length", LENGTHS)
+def test_full_scores_f32_matches_reference_golden(length):
+    from dsa_b200 import score_dense
+
+    g = load_golden("progressive_kernel")
+    q, w, k = g["f32_q"], g["f32_w"], g[f"f32_L{length}_keys"]
+    got = score_dense(cuda(q), cuda(w), cuda(k)).cpu().numpy()
+    assert_scores_close(got, g[f"f32_L{length}_scores"], normwise_bound(q, w, k), rtol=1e-5,
+                        msg="f32")
+
+
+def test_config1_f32_scores_and_top512():
+    """BASELINE config 1 (f32, L=4096, top-512, seed 0) against the reference golden."""
+    from dsa_b200 import scores_topk
+
+    g = load_golden("cfg1")
+    q, w, k = cfg1_inputs()
+    idx, val = scores_topk(q.cuda(), w.cuda(), k.cuda(), 512, sorted=True)
+    scale = normwise_bound(q.numpy(), w.numpy(), k.numpy())
+    from dsa_b200 import score_dense
+
+    s = score_dense(q.cuda(), w.cuda(), k.cuda()).cpu().numpy()
+    assert_scores_close(s, g["scores"], scale, rtol=1e-5, msg="cfg1 scores")
+    np.testing.assert_allclose(s, g["scores"], rtol=1e-5, atol=1e-5)
+    assert_topk_equivalent(idx.cpu().numpy(), g["top512"], g["scores"], tol=1e-5,
+                           msg="cfg1 top-512")
+    # our own top-k of our own scores is exactly stable_topk of them
+    np.testing.assert_array_equal(idx.cpu().numpy(), oracle.stable_topk(s, 512))
+    np.testing.assert_array_equal(val.cpu().numpy(), s[idx.cpu().numpy()])
+
+
+def test_config2_batched_bf16_score_topk():
+    """BASELINE config 2 shape: B=32, L=8192 bf16, top-2048, f32 accumulation."""
+    from dsa_b200 import score_dense, scores_topk
+
+    gen = torch.Generator().manual_seed(0)
+    b, length, kk = 32, 8192, 2048
+    q = (torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)).to(torch.bfloat16)
+    w = torch.randn(b, 64, generator=gen) / math.sqrt(64)
+    k = torch.randn(b, length, 128, generator=gen).to(torch.bfloat16)
+    qc, wc, kc = q.cuda(), w.cuda(), k.cuda()
+    scores = score_dense(qc, wc, kc).cpu().numpy()
+    idx, val = scores_topk(qc, wc, kc, kk, sorted=True)
+    idx, val = idx.cpu().numpy(), val.cpu().numpy()
+    for row in range(b):
+        qf, kf = q[row].float().numpy(), k[row].float().numpy()
+        want = oracle.full_scores(qf, w[row].numpy(), kf)
+        scale = normwise_bound(qf, w[row].numpy(), kf)
+        assert_scores_close(scores[row], want, scale, rtol=1e-5, atol=1e-7, msg=f"row {row}")
+        assert_topk_equivalent(idx[row], oracle.stable_topk(want, kk), want,
+                               tol=2e-5 * scale.max(), msg=f"row {row}")
+        np.testing.assert_array_equal(idx[row], oracle.stable_topk(scores[row], kk))
+        np.testing.assert_array_equal(val[row], scores[row][idx[row]])
+
+
+def test_strided_and_sliced_key_cache():
+    """Keys living in a larger cache: row stride 256 elements, batch stride != L*row."""
+    from dsa_b200 import score_dense
+
+    gen = torch.Generator().manual_seed(3)
+    cache = torch.randn(3, 700, 256, generator=gen).to(torch.bfloat16).cuda()
+    keys = cache[:, 5:605, 64:192]  # [3,600,128], row stride 256
+    q = (torch.randn(3, 64, 128, generator=gen) / 11).to(torch.bfloat16).cuda()
+    w = (torch.randn(3, 64, generator=gen) / 8).cuda()
+    got = score_dense(q, w, keys).cpu().numpy()
+    for r in range(3):
+        qf, kf = q[r].float().cpu().numpy(), keys[r].float().cpu().numpy()
+        want = oracle.full_scores(qf, w[r].cpu().numpy(), kf)
+        assert_scores_close(got[r], want, normwise_bound(qf, w[r].cpu().numpy(), kf),
+                            rtol=1e-5, atol=1e-7)
+
+
+def test_score_encoded_matches_reference_golden():
+    from dsa_b200.sidecar import score_encoded
+
+    g = load_golden("batched")
+    got = score_encoded(cuda(g["q"]), cuda(g["w"]), cuda(g["k"]), key_chunk_size=32)
+    got = got.cpu().numpy()
+    for b in range(2):
+        for qi in range(2):
+            scale = normwise_bound(g["q"][b, qi], g["w"][b, qi], g["k"][b])
+            assert_scores_close(got[b, qi], g["encoded"][b, qi], scale, rtol=1e-5)
+    # bf16 inputs (the sidecar's decode dtype)
+    qb = cuda(g["q"], torch.bfloat16)
+    kb = cuda(g["k"], torch.bfloat16)
+    got = score_encoded(qb, cuda(g["w"]), kb).cpu().numpy()
+    want = oracle.score_encoded(qb.float().cpu().numpy(), g["w"], kb.float().cpu().numpy())
+    np.testing.assert_allclose(got, want, rtol=1e-2, atol=1e-3)
+
+
+def test_stable_topk_edge_cases_bit_exact():
+    """Same float values in, stable_topk's exact index list out (ties, -inf, +-0)."""
+    from dsa_b200.metrics import stable_topk
+
+    g = load_golden("topk")
+    for name in g["names"]:
+        x = g[f"{name}_x"]
+        for key in g.files:
+            if key.startswith(f"{name}_k"):
+                k = int(key[len(name) + 2:])
+                got = stable_topk(cuda(x), k).cpu().numpy()
+                np.testing.assert_array_equal(got, g[key], err_msg=key)
+
+
+@pytest.mark.parametrize("length,k", [(1, 1), (5, 5), (1000, 1), (32768, 2048),
+                                      (32769, 2048), (40000, 512), (131072, 2048),
+                                      (300000, 4096), (65536, 8192)])
+@pytest.mark.parametrize("sorted_", [True, False])
+def test_topk_rows_match_oracle(length, k, sorted_):
+    from dsa_b200 import topk
+
+    rng = np.random.default_rng(length + k)
+    s = np.round(rng.normal(size=(2, length)) * 64).astype(np.float32) / 64  # many ties
+    idx, val = topk(cuda(s), k, sorted=sorted_)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=sorted_)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+
+
+def test_topk_unsorted_large_k_single_segment():
+    from dsa_b200 import topk
+
+    rng = np.random.default_rng(9)
+    s = rng.normal(size=(3, 30000)).astype(np.float32)
+    idx, _ = topk(cuda(s), 20000, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), oracle.topk_rows(s, 20000, sorted=False)[0])
+
+
+def test_merge_topk_matches_oracle():
+    from dsa_b200 import merge_topk, topk
+
+    rng = np.random.default_rng(11)
+    s = np.round(rng.normal(size=(4, 65536)) * 16).astype(np.float32) / 16
+    shards = np.split(np.arange(65536), 8)
+    cv, ci = [], []
+    for p in shards:
+        li, lv = topk(cuda(s[:, p]), 1024, sorted=False, index_dtype=torch.int32)
+        cv.append(lv)
+        ci.append(li + int(p[0]))
+    mi, mv = merge_topk(torch.cat(cv, 1), torch.cat(ci, 1), 1024, sorted=True)
+    want_i, want_v = oracle.topk_rows(s, 1024)
+    np.testing.assert_array_equal(mi.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(mv.cpu().numpy(), want_v)
+
+
+def test_api_errors():
+    from dsa_b200 import score_dense, topk
+    from dsa_b200.progressive_kernel import full_scores_triton
+
+    q = torch.zeros(64, 128, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(64, device="cuda")
+    k = torch.zeros(10, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        full_scores_triton(q.float(), w, k)
+    with pytest.raises(ValueError):
+        full_scores_triton(q, w, k.cpu())
+    with pytest.raises(ValueError):
+        score_dense(q[:32], w, k)
+    with pytest.raises(ValueError):
+        topk(torch.zeros(10, device="cuda"), 11)
+    assert score_dense(q, w, k[:0]).shape == (0,)
