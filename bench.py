@@ -183,28 +183,30 @@ class Config4:
 
 
 def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
-    from dsa_b200 import score_dense, scores_topk, topk
-    from dsa_b200.sidecar import encode_queries
+    from dsa_b200.indexer import ScoreTopkPlan
+    from dsa_b200.sidecar import QueryProjector
 
     wl = Config4(device, seed=1234 + rank, batch=args.batch, length=args.length, k=args.k)
     stream = torch.cuda.current_stream(device)
+    proj = [QueryProjector(wl.wq[layer], wl.ww[layer], wl.batch) for layer in range(wl.layers)]
+    plans = [ScoreTopkPlan(proj[layer].q, proj[layer].w, wl.keys[layer], wl.k, sorted=False)
+             for layer in range(wl.layers)]
     score_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
     launches = {"n": 0}
-    topk_levels = 1 if wl.length <= 32768 else 2
 
     def step(record: bool):
         for layer in range(wl.layers):
-            q, w = encode_queries(wl.x[layer], wl.wq[layer], wl.ww[layer], wl.qpos)
+            proj[layer].project(wl.x[layer], wl.qpos)
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            score_dense(q, w, wl.keys[layer], out=wl.scores)
+            plans[layer].score()
             if record:
                 e1.record(stream)
                 score_events.append((e0, e1))
-                launches["n"] += 1 + topk_levels
-            topk(wl.scores, wl.k, sorted=False, index_dtype=torch.int32)
+                launches["n"] += 1 + plans[layer].launches_per_run
+            plans[layer].select()
 
     def barrier():
         if world > 1:
@@ -224,12 +226,14 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     torch.cuda.synchronize(device)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     with ClockSampler(device.index) as clocks:
         start.record(stream)
         for _ in range(args.steps):
             step(True)
         end.record(stream)
         torch.cuda.synchronize(device)
+    torch.cuda.nvtx.range_pop()
     barrier()
     torch.cuda.synchronize(device)
     ms_step = max_over_ranks(start.elapsed_time(end) / args.steps)
@@ -239,22 +243,15 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     # ---- end to end through the public API, host buffers, copies inside the region
     x_host = wl.x.cpu().pin_memory()
     x_dev = torch.empty_like(wl.x)
-    out_dev = torch.empty(wl.layers, wl.batch, wl.k, device=device, dtype=torch.int32)
-    out_host = torch.empty(out_dev.shape, dtype=torch.int32).pin_memory()
-    ws = torch.empty(0, device=device, dtype=torch.uint8)
+    out_host = torch.empty(wl.layers, wl.batch, wl.k, dtype=torch.int32).pin_memory()
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
         for layer in range(wl.layers):
-            q, w = encode_queries(x_dev[layer], wl.wq[layer], wl.ww[layer], wl.qpos)
-            idx, _ = scores_topk(q, w, wl.keys[layer], wl.k, sorted=False, workspace=ws)
-            out_dev[layer].copy_(idx)
-        out_host.copy_(out_dev, non_blocking=True)
+            proj[layer].project(x_dev[layer], wl.qpos)
+            idx, _ = plans[layer].run()
+            out_host[layer].copy_(idx, non_blocking=True)
 
-    from dsa_b200 import _capi
-
-    ws = torch.empty(_capi.lib().tdsa_score_topk_workspace_bytes(wl.batch, wl.length, wl.k),
-                     device=device, dtype=torch.uint8)
     for _ in range(max(3, args.warmup)):
         e2e_step()
     torch.cuda.synchronize(device)
@@ -323,8 +320,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             "ms_per_step": e2e_ms,
             "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
             "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
-            "api": "dsa_b200.sidecar.encode_queries + dsa_b200.scores_topk (C ABI "
-                   "tdsa_score_topk)",
+            "api": "dsa_b200.sidecar.QueryProjector + dsa_b200.indexer.ScoreTopkPlan "
+                   "(C ABI tdsa_query_prep, tdsa_score_dense, tdsa_topk)",
         },
         "gpu_launches": launches["n"],
         "clocks": clocks.summary(),

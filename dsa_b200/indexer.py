@@ -179,6 +179,59 @@ def scores_topk(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor
     return (idx[0], val[0]) if single else (idx, val)
 
 
+class ScoreTopkPlan:
+    """A prepared dense-score + top-k call on fixed device buffers (the decode loop form).
+
+    The caller rewrites ``queries``/``weights`` in place between steps; ``score()`` and
+    ``select()`` are one C-ABI call each with no per-call validation or allocation.
+    Results land in ``scores`` [B,L], ``indices`` [B,k] and ``values`` [B,k].
+    """
+
+    def __init__(self, queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor, k: int,
+                 *, sorted: bool = False, index_dtype: torch.dtype = torch.int32):
+        require_cuda(queries, weights, keys)
+        q, w, kk, _ = as_batched(queries, weights, keys)
+        if not (q.is_contiguous() and _aligned(q) and q.dtype == kk.dtype):
+            raise ValueError("plan queries must be contiguous, 16-byte aligned, keys' dtype")
+        if not (w.dtype == torch.float32 and w.is_contiguous()):
+            raise ValueError("plan weights must be contiguous float32")
+        if prepare_keys(kk) is not kk:
+            raise ValueError("plan keys must already satisfy the TMA layout rules")
+        self.q, self.w, self.keys = q, w, kk
+        self.batch, self.length, self.k = kk.shape[0], kk.shape[1], k
+        if not 0 < k <= self.length:
+            raise ValueError(f"k={k} is invalid for {self.length} keys")
+        dev = kk.device
+        self.scores = torch.empty(self.batch, self.length, device=dev, dtype=torch.float32)
+        self.indices = torch.empty(self.batch, k, device=dev, dtype=index_dtype)
+        self.values = torch.empty(self.batch, k, device=dev, dtype=torch.float32)
+        nbytes = capi.lib().tdsa_topk_workspace_bytes(self.batch, self.length, k)
+        self.workspace = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+        lib = capi.lib()
+        self._score_fn, self._topk_fn = lib.tdsa_score_dense, lib.tdsa_topk
+        self._score_args = (q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0), kk.data_ptr(),
+                            kk.stride(0), kk.stride(1), _DTYPES[kk.dtype], self.batch,
+                            self.length, self.scores.data_ptr(), self.scores.stride(0))
+        self._topk_args = (self.scores.data_ptr(), self.scores.stride(0), self.batch,
+                           self.length, k, int(bool(sorted)), self.indices.data_ptr(),
+                           self.indices.element_size(), self.indices.stride(0),
+                           self.values.data_ptr(), self.values.stride(0),
+                           self.workspace.data_ptr(), nbytes)
+        self.device = dev
+        self.launches_per_run = 1 + (1 if self.length <= 32768 else 2)
+
+    def score(self) -> None:
+        capi.check(self._score_fn(*self._score_args, stream_ptr(self.device)))
+
+    def select(self) -> None:
+        capi.check(self._topk_fn(*self._topk_args, stream_ptr(self.device)))
+
+    def run(self) -> tuple[torch.Tensor, torch.Tensor]:
+        self.score()
+        self.select()
+        return self.indices, self.values
+
+
 def device_status(reset: bool = True) -> int:
     """OR of error bits raised by kernels on the current device since the last reset."""
     return capi.device_status(reset)

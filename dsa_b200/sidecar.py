@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import torch
 
+from . import _capi as capi
 from .indexer import HEAD_DIM, HEADS, require_cuda, score_dense
 
 
@@ -74,6 +75,48 @@ def encode_queries(hidden: torch.Tensor, wq: torch.Tensor, ww: torch.Tensor,
                        q[..., rope_dim:]), dim=-1)
     w = torch.matmul(hidden.float(), ww.float().t()) * (HEADS * HEAD_DIM) ** -0.5
     return q, w
+
+
+class QueryProjector:
+    """Decode-step query projection on fixed buffers: two cuBLAS GEMMs (W_q in the hidden
+    dtype, W_w in float32) and one fused RoPE + weight-scale kernel (tdsa_query_prep).
+
+    ``project(hidden, positions)`` -> (q [B,64,128], w [B,64] float32), written into
+    ``self.q`` / ``self.w`` (stable addresses, so a ScoreTopkPlan can be built on them).
+    """
+
+    def __init__(self, wq: torch.Tensor, ww: torch.Tensor, batch: int, *, rope_dim: int = 64,
+                 rope_theta: float = 10_000.0):
+        require_cuda(wq, ww)
+        if wq.shape[0] != HEADS * HEAD_DIM or ww.shape[0] != HEADS:
+            raise ValueError("expected wq [8192, hidden] and ww [64, hidden]")
+        if wq.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("wq must be bf16 or fp16")
+        dev, hidden = wq.device, wq.shape[1]
+        self.wq_t = wq.t()
+        self.ww_t = ww.to(torch.float32).t()
+        self.dtype = wq.dtype
+        self.batch, self.rope_dim, self.theta = batch, rope_dim, rope_theta
+        self.qraw = torch.empty(batch, HEADS * HEAD_DIM, device=dev, dtype=wq.dtype)
+        self.wraw = torch.empty(batch, HEADS, device=dev, dtype=torch.float32)
+        self.hidden_f32 = torch.empty(batch, hidden, device=dev, dtype=torch.float32)
+        self.q = torch.empty(batch, HEADS, HEAD_DIM, device=dev, dtype=wq.dtype)
+        self.w = torch.empty(batch, HEADS, device=dev, dtype=torch.float32)
+        self._fn = capi.lib().tdsa_query_prep
+        self._dt = capi.TDSA_BF16 if wq.dtype == torch.bfloat16 else capi.TDSA_F16
+
+    def project(self, hidden: torch.Tensor, positions: torch.Tensor):
+        torch.matmul(hidden, self.wq_t, out=self.qraw)
+        self.hidden_f32.copy_(hidden)
+        torch.matmul(self.hidden_f32, self.ww_t, out=self.wraw)
+        if positions.dtype != torch.int64 or not positions.is_contiguous():
+            positions = positions.to(torch.int64).contiguous()
+        capi.check(self._fn(self.qraw.data_ptr(), self.qraw.stride(0), self.wraw.data_ptr(),
+                            self.wraw.stride(0), positions.data_ptr(), self.q.data_ptr(),
+                            HEADS * HEAD_DIM, self.w.data_ptr(), HEADS, self._dt, self.batch,
+                            self.rope_dim, self.theta, (HEADS * HEAD_DIM) ** -0.5,
+                            torch.cuda.current_stream(self.q.device).cuda_stream))
+        return self.q, self.w
 
 
 def encode_keys(hidden: torch.Tensor, wk: torch.Tensor, norm_weight: torch.Tensor,

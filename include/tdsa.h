@@ -112,6 +112,20 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
                     float* out_values, int64_t val_batch_stride, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/*
+ * Query epilogue of the sidecar projection: RoPE on the first rope_dim dims of every head
+ * and the head-weight scale, fused into one pass over the W_q / W_w GEMM outputs.
+ * Replaces: the tail of LightningIndexerSidecar.encode_queries (src/temporal_dsa/
+ *   sidecar.py:78-87) with apply_noninterleaved_rope (:10-28).
+ * qraw [batch][64*128] (dtype TDSA_BF16 or TDSA_F16), row stride qraw_stride;
+ * wraw [batch][64] float32; positions [batch] int64;
+ * q    [batch][64][128] out (same dtype), w [batch][64] float32 out (w = wraw * scale).
+ */
+int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const float* wraw,
+                    int64_t wraw_stride, const int64_t* positions, void* q, int64_t q_stride,
+                    float* w, int64_t w_stride, int dtype, int batch, int rope_dim,
+                    float rope_theta, float weight_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

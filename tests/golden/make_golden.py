@@ -235,6 +235,19 @@ def main() -> None:
                         encoded=enc.numpy(), ids_fixed=ids_fixed.numpy(),
                         ids_dyn=ids_dyn.numpy(), hs_fixed=hs_fixed.numpy(),
                         hs_dyn=hs_dyn.numpy())
+    # ---- sidecar projection (encode_queries / encode_keys) -------------------------------
+    torch.manual_seed(0)
+    sc = LightningIndexerSidecar(hidden_size=16)
+    with torch.no_grad():
+        hq = torch.randn(2, 1, 16, generator=torch.Generator().manual_seed(31))
+        qpos = torch.tensor([[3], [1000]])
+        eq, ew = sc.encode_queries(hq, qpos)
+        hk = torch.randn(1, 5, 16, generator=torch.Generator().manual_seed(32))
+        ek = sc.encode_keys(hk, torch.arange(5).view(1, -1))
+    np.savez_compressed(HERE / "sidecar.npz", wq=sc.wq.weight.detach().numpy(),
+                        ww=sc.weights_proj.weight.detach().numpy(),
+                        wk=sc.wk.weight.detach().numpy(), hq=hq.numpy(), qpos=qpos.numpy(),
+                        q=eq.numpy(), w=ew.numpy(), hk=hk.numpy(), k=ek.numpy())
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

@@ -231,3 +231,19 @@ def test_exact_progressive_prunes_structured_keys():
     top, _, stats, _ = progressive_exact.exact_step(state, q2, w, keys)
     np.testing.assert_array_equal(top, oracle.stable_topk(oracle.full_scores(q2, w, keys), k))
     assert stats["pruned_blocks"] > 0
+
+
+def test_sidecar_projection_matches_reference():
+    from oracle import sidecar as osc
+
+    g = load_golden("sidecar")
+    q, w = osc.encode_queries(g["hq"][:, 0], g["wq"], g["ww"], g["qpos"][:, 0])
+    # the float32 RoPE angle pos * inv_freq carries ~pos * 2^-24 rad of rounding, so at
+    # position 1000 one ulp of inv_freq moves a rotated value by ~1e-4
+    np.testing.assert_allclose(q, g["q"][:, 0], rtol=1e-5, atol=5e-4)
+    np.testing.assert_allclose(w, g["w"][:, 0], rtol=1e-5, atol=1e-7)
+    # encode_keys = RoPE(LayerNorm(h @ wk^T)); LayerNorm(eps=1e-6) with unit affine
+    k = g["hk"][0].astype(np.float64) @ g["wk"].T.astype(np.float64)
+    k = (k - k.mean(-1, keepdims=True)) / np.sqrt(k.var(-1, keepdims=True) + 1e-6)
+    k[:, :64] = osc.apply_noninterleaved_rope(k[:, :64], np.arange(5))
+    np.testing.assert_allclose(k, g["k"][0], rtol=1e-4, atol=1e-5)
