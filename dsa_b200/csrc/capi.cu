@@ -102,16 +102,17 @@ namespace {
 
 int check_score_args(const void* q, int64_t q_bs, const float* w, int64_t w_bs, const void* k,
                      int64_t k_bs, int64_t k_rs, int dtype, int batch, int length,
-                     const float* out, int64_t o_bs) {
+                     const float* out, int64_t o_bs, bool check_out = true) {
   if (dtype != TDSA_F32 && dtype != TDSA_F16 && dtype != TDSA_BF16)
     return fail(TDSA_ERR_INVALID, "dtype must be TDSA_F32, TDSA_F16 or TDSA_BF16");
   if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
   if (length < 0) return fail(TDSA_ERR_INVALID, "length must be >= 0");
   if (length == 0) return TDSA_OK;
-  if (!q || !w || !k || !out) return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (!q || !w || !k || (check_out && !out))
+    return fail(TDSA_ERR_INVALID, "null pointer argument");
   if (k_rs < kHeadDim) return fail(TDSA_ERR_INVALID, "key row stride must be >= 128");
   if (batch > 1 && (q_bs < kHeads * kHeadDim || w_bs < kHeads ||
-                    k_bs < static_cast<int64_t>(length) * k_rs || o_bs < length))
+                    k_bs < static_cast<int64_t>(length) * k_rs || (check_out && o_bs < length)))
     return fail(TDSA_ERR_INVALID, "batch strides overlap the rows of one sequence");
   if (dtype != TDSA_F32) {
     if (!aligned16(q) || !aligned16(k))
@@ -130,6 +131,35 @@ int check_topk_out(void* out_idx, int index_bytes, int64_t idx_bs, const float* 
   if (batch > 1 && (idx_bs < k || (out_val && val_bs < k)))
     return fail(TDSA_ERR_INVALID, "output row strides must be >= k");
   return TDSA_OK;
+}
+
+// Shared set-up of the block-structured entry points (16-bit keys only: tcgen05 path).
+int block_setup(const void* q, int64_t q_bs, const float* w, int64_t w_bs, const void* k,
+                int64_t k_bs, int64_t k_rs, int dtype, int batch, int length, int block_size,
+                BlockArgs& a) {
+  int rc = check_score_args(q, q_bs, w, w_bs, k, k_bs, k_rs, dtype, batch, length, nullptr, 0,
+                            false);
+  if (rc) return rc;
+  if (dtype == TDSA_F32)
+    return fail(TDSA_ERR_UNSUPPORTED, "block kernels take bf16/fp16 queries and keys");
+  if (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128)
+    return fail(TDSA_ERR_UNSUPPORTED, "block_size must be 16, 32, 64 or 128");
+  a.bs = block_size;
+  a.bpt = 128 / block_size;
+  a.length = length;
+  a.nblocks = (length + block_size - 1) / block_size;
+  a.tiles_per_seq = (a.nblocks + a.bpt - 1) / a.bpt;
+  a.total_tiles = static_cast<int64_t>(a.tiles_per_seq) * batch;
+  a.w = w;
+  a.w_stride = w_bs;
+  a.status = device_status_ptr();
+  if (!a.status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  return TDSA_OK;
+}
+
+int block_grid(const BlockArgs& a) {
+  const int sms = device_sm_count(current_device());
+  return static_cast<int>(a.total_tiles < sms ? a.total_tiles : sms);
 }
 
 }  // namespace
@@ -262,6 +292,102 @@ int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const float* wraw,
   return launch_qprep(qraw, qraw_stride, wraw, wraw_stride, positions, q, q_stride, w, w_stride,
                       dtype, batch, rope_dim, rope_theta, weight_scale,
                       static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_h8_block_max(const void* queries, int64_t q_batch_stride, const float* weights,
+                      int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                      int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                      const int32_t* selected_heads, const int8_t* cold_blocks,
+                      float* partial, int64_t p_batch_stride, float* block_max,
+                      int64_t bm_batch_stride, void* stream) {
+  if (length < 1) return fail(TDSA_ERR_INVALID, "length must be >= 1");
+  BlockArgs a;
+  int rc = block_setup(queries, q_batch_stride, weights, w_batch_stride, keys, k_batch_stride,
+                       k_row_stride, dtype, batch, length, block_size, a);
+  if (rc) return rc;
+  if (!selected_heads || !cold_blocks || !partial || !block_max)
+    return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (batch > 1 && (p_batch_stride < length || bm_batch_stride < a.nblocks))
+    return fail(TDSA_ERR_INVALID, "output row strides too small");
+  a.mask = cold_blocks;
+  a.mask_stride = bm_batch_stride;
+  a.selected = selected_heads;
+  a.out = partial;
+  a.out_stride = p_batch_stride;
+  a.block_max = block_max;
+  a.bm_stride = bm_batch_stride;
+  return launch_score_blocks(kModeH8, queries, q_batch_stride, keys, k_batch_stride,
+                             k_row_stride, dtype, batch, a, block_grid(a),
+                             static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_masked_dense(const void* queries, int64_t q_batch_stride, const float* weights,
+                      int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                      int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                      const int8_t* keep_blocks, int64_t keep_batch_stride, float* scores,
+                      int64_t s_batch_stride, void* stream) {
+  if (length < 1) return fail(TDSA_ERR_INVALID, "length must be >= 1");
+  BlockArgs a;
+  int rc = block_setup(queries, q_batch_stride, weights, w_batch_stride, keys, k_batch_stride,
+                       k_row_stride, dtype, batch, length, block_size, a);
+  if (rc) return rc;
+  if (!keep_blocks || !scores) return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (batch > 1 && (s_batch_stride < length || keep_batch_stride < a.nblocks))
+    return fail(TDSA_ERR_INVALID, "row strides too small");
+  a.mask = keep_blocks;
+  a.mask_stride = keep_batch_stride;
+  a.out = scores;
+  a.out_stride = s_batch_stride;
+  return launch_score_blocks(kModeMasked, queries, q_batch_stride, keys, k_batch_stride,
+                             k_row_stride, dtype, batch, a, block_grid(a),
+                             static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_progressive_h8(const void* queries, int64_t q_batch_stride, const float* weights,
+                        int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                        int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                        const int32_t* selected_heads, const int32_t* remaining_heads,
+                        const int8_t* direct_blocks, const float* threshold, float* scores,
+                        int64_t s_batch_stride, int8_t* accepted, float* block_max,
+                        int64_t bm_batch_stride, void* stream) {
+  if (length < 1) return fail(TDSA_ERR_INVALID, "length must be >= 1");
+  BlockArgs a;
+  int rc = block_setup(queries, q_batch_stride, weights, w_batch_stride, keys, k_batch_stride,
+                       k_row_stride, dtype, batch, length, block_size, a);
+  if (rc) return rc;
+  if (!selected_heads || !direct_blocks || !threshold || !scores || !accepted || !block_max)
+    return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (batch > 1 && (s_batch_stride < length || bm_batch_stride < a.nblocks))
+    return fail(TDSA_ERR_INVALID, "row strides too small");
+  a.mask = direct_blocks;
+  a.mask_stride = bm_batch_stride;
+  a.selected = selected_heads;
+  a.remaining = remaining_heads;
+  a.threshold = threshold;
+  a.out = scores;
+  a.out_stride = s_batch_stride;
+  a.block_max = block_max;
+  a.accepted = accepted;
+  a.bm_stride = bm_batch_stride;
+  return launch_score_blocks(kModeProgressive, queries, q_batch_stride, keys, k_batch_stride,
+                             k_row_stride, dtype, batch, a, block_grid(a),
+                             static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_t* accepted,
+                        int64_t a_batch_stride, int batch, int length, int block_size,
+                        float* out_scores, int32_t* out_indices, int64_t out_batch_stride,
+                        int32_t* out_count, void* stream) {
+  if (!scores || !accepted || !out_scores || !out_indices || !out_count)
+    return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (batch < 1 || batch > 65535 || length < 1 || block_size < 1)
+    return fail(TDSA_ERR_INVALID, "bad batch, length or block size");
+  if (batch > 1 && (s_batch_stride < length || out_batch_stride < length ||
+                    a_batch_stride < (length + block_size - 1) / block_size))
+    return fail(TDSA_ERR_INVALID, "row strides too small");
+  return launch_compact_blocks(scores, s_batch_stride, accepted, a_batch_stride, batch, length,
+                               block_size, out_scores, out_indices, out_batch_stride, out_count,
+                               static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

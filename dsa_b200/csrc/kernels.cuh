@@ -20,6 +20,43 @@ int launch_score_dense_f32(const float* q, int64_t q_bs, const float* w, int64_t
                            const float* k, int64_t k_bs, int64_t k_rs, int batch, int length,
                            float* out, int64_t o_bs, cudaStream_t stream);
 
+// ---- block-structured scoring (score_blocks.cu)
+enum BlockMode { kModeH8 = 0, kModeMasked = 1, kModeProgressive = 2, kModeExact = 3 };
+
+struct BlockArgs {
+  int bs = 64;                 // block size: 16, 32, 64 or 128
+  int bpt = 2;                 // blocks per 128-key tile
+  int length = 0;              // keys per sequence
+  int nblocks = 0;             // ceil(length / bs)
+  int tiles_per_seq = 0;       // contiguous tiles: ceil(nblocks / bpt)
+  int64_t total_tiles = 0;     // contiguous tiles of the launch
+  const int32_t* tile_seq = nullptr;     // listed tiles: sequence of tile t
+  const int32_t* tile_blocks = nullptr;  // listed tiles: [t][bpt] block ids, -1 empty
+  const int32_t* tile_count = nullptr;   // listed tiles: device count
+  const int8_t* mask = nullptr;          // per block: cold (H8), keep (masked), direct (prog.)
+  int64_t mask_stride = 0;
+  const int32_t* selected = nullptr;     // 8 head ids (device)
+  const int32_t* remaining = nullptr;    // 56 head ids (device) or null = complement
+  const float* threshold = nullptr;      // progressive promotion threshold (device scalar)
+  const float* w = nullptr;
+  int64_t w_stride = 0;
+  float* out = nullptr;                  // [batch][out_stride] per-key output
+  int64_t out_stride = 0;
+  float* block_max = nullptr;            // [batch][bm_stride]
+  int64_t bm_stride = 0;
+  int8_t* accepted = nullptr;            // [batch][bm_stride]
+  int* status = nullptr;
+};
+
+int launch_score_blocks(int mode, const void* q, int64_t q_bs, const void* k, int64_t k_bs,
+                        int64_t k_rs, int dtype, int batch, const BlockArgs& args, int grid,
+                        cudaStream_t stream);
+
+int launch_compact_blocks(const float* scores, int64_t s_stride, const int8_t* accepted,
+                          int64_t a_stride, int batch, int length, int block_size,
+                          float* out_scores, int32_t* out_indices, int64_t o_stride,
+                          int32_t* out_count, cudaStream_t stream);
+
 size_t topk_workspace_bytes(int batch, int length, int k);
 int topk_check(int length, int k, int sorted);
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,

@@ -1,8 +1,9 @@
 // Exact row-wise top-k by radix select in shared memory (no global sort).
 //
 // One 1024-thread CTA owns one segment of a row (<= 32768 elements, held in shared memory
-// as order-preserving uint32 keys).  Three histogram passes over 11/11/10-bit digits pin
-// the k-th key T exactly (stopping early when a digit bin is taken whole); an ordered
+// as order-preserving uint32 keys).  Up to four histogram passes over 8-bit digits (one
+// private histogram per warp, lanes with equal digits combined before the atomic) pin the
+// k-th key T exactly, stopping early when a digit bin is taken whole; an ordered
 // compaction then takes every key > T plus the first (k - #greater) keys == T in index
 // order, which is the tie rule of the reference's stable_topk (metrics.py:9-22).  The
 // selection is written in ascending index order, or, when sorted output is asked for,
@@ -21,7 +22,7 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-constexpr int kHistBins = 2048;
+constexpr int kBins = 256;  // 8-bit radix digits
 
 struct TopkArgs {
   const float* vals;      // [rows][row_stride]
@@ -76,13 +77,14 @@ __device__ __forceinline__ uint32_t block_suffix_sum(uint32_t v, uint32_t* wsum)
 // Writes {bin, k_rem within the bin, count of the bin} to res[0..2].
 __device__ void find_bin(const uint32_t* hist, int nbins, uint32_t k_rem, uint32_t* wsum,
                          uint32_t* res) {
-  const int per = nbins / kThreads;  // 1 or 2 bins per thread
+  const int per = nbins > kThreads ? nbins / kThreads : 1;
   const int lo = threadIdx.x * per;
   uint32_t local = 0;
-  for (int i = 0; i < per; ++i) local += hist[lo + i];
+  if (lo < nbins)
+    for (int i = 0; i < per; ++i) local += hist[lo + i];
   const uint32_t incl = block_suffix_sum(local, wsum);
   uint32_t above = incl - local;
-  if (above < k_rem && k_rem <= incl) {
+  if (local > 0 && above < k_rem && k_rem <= incl) {
     for (int i = per - 1; i >= 0; --i) {
       const uint32_t c = hist[lo + i];
       if (above + c >= k_rem) {
@@ -97,26 +99,52 @@ __device__ void find_bin(const uint32_t* hist, int nbins, uint32_t k_rem, uint32
   __syncthreads();
 }
 
+// Adds one key digit per active lane to the warp's private histogram; lanes with equal
+// digits are combined first (one shared-memory atomic per distinct digit).
+__device__ __forceinline__ void warp_hist_add(uint32_t* whist, uint32_t digit, bool active) {
+  const unsigned m = __ballot_sync(0xffffffffu, active);
+  if (active) {
+    const unsigned peers = __match_any_sync(m, digit);
+    if ((threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1))
+      atomicAdd(&whist[digit], static_cast<uint32_t>(__popc(peers)));
+  }
+}
+
+// Sums the per-warp histograms into hist[kBins].
+__device__ __forceinline__ void merge_warp_hists(const uint32_t* whist, uint32_t* hist) {
+  __syncthreads();
+  if (threadIdx.x < kBins) {
+    uint32_t s = 0;
+#pragma unroll 8
+    for (int w = 0; w < kWarps; ++w) s += whist[w * kBins + threadIdx.x];
+    hist[threadIdx.x] = s;
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArgs a) {
   extern __shared__ uint32_t sm[];
   __shared__ uint32_t wsum[64];
   __shared__ uint32_t res[4];
   __shared__ uint32_t wcnt[2][kWarps];
+  __shared__ uint32_t hist[kBins];
 
   const int row = blockIdx.y, seg = blockIdx.x;
   const int start = seg * a.chunk;
   const int n = min(a.row_len - start, a.chunk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* keys = sm;
-  uint32_t* hist = sm + a.chunk;
-  uint64_t* pairs = reinterpret_cast<uint64_t*>(sm + ((a.chunk + 1) & ~1) + kHistBins);
+  // per-warp digit histograms; the same space holds the sort pairs after selection
+  uint32_t* whist = sm + ((a.chunk + 1) & ~1);
+  uint32_t* my_hist = whist + warp * kBins;
+  uint64_t* pairs = reinterpret_cast<uint64_t*>(whist);
 
   const float* vrow = a.vals + static_cast<int64_t>(row) * a.vals_stride + start;
   const int32_t* irow = a.idx ? a.idx + static_cast<int64_t>(row) * a.idx_stride + start : nullptr;
 
-  for (int i = tid; i < kHistBins; i += kThreads) hist[i] = 0u;
-  __syncthreads();
-  // Load + first-digit histogram (warp-aggregated: many keys share a few top bins).
+  for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
+  __syncwarp();
+  // Load, convert to order-preserving keys, histogram of the top digit.
   for (int base = 0; base < n; base += kThreads) {
     const int i = base + tid;
     const bool active = i < n;
@@ -125,41 +153,35 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       u = float_to_key(__ldg(vrow + i));
       keys[i] = u;
     }
-    const unsigned m = __ballot_sync(0xffffffffu, active);
-    if (active) {
-      const uint32_t bin = u >> 21;
-      const unsigned peers = __match_any_sync(m, bin);
-      if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
-    }
+    warp_hist_add(my_hist, u >> 24, active);
   }
-  __syncthreads();
+  merge_warp_hists(whist, hist);
 
   const int k = min(a.k, n);
   uint32_t k_rem = static_cast<uint32_t>(k);
-  uint32_t prefix = 0;  // fixed high bits of T
-  int shift = 21;       // keys compare as (u >> shift) against prefix
-  find_bin(hist, kHistBins, k_rem, wsum, res);
-  prefix = res[0];
+  int shift = 24;  // keys compare as (u >> shift) against prefix
+  find_bin(hist, kBins, k_rem, wsum, res);
+  uint32_t prefix = res[0];
   k_rem = res[1];
   bool whole = (res[2] == k_rem);
-  // Remaining digits: bits [10,21) then [0,10).
-  for (int level = 1; level <= 2 && !whole; ++level) {
-    const int nshift = level == 1 ? 10 : 0;
-    const int nbins = level == 1 ? 2048 : 1024;
-    const uint32_t mask = nbins - 1;
-    for (int i = tid; i < nbins; i += kThreads) hist[i] = 0u;
-    __syncthreads();
-    for (int i = tid; i < n; i += kThreads) {
-      const uint32_t u = keys[i];
-      if ((u >> shift) == prefix) atomicAdd(&hist[(u >> nshift) & mask], 1u);
+  // Remaining 8-bit digits; only keys still matching the prefix are counted.
+  for (int nshift = 16; nshift >= 0 && !whole; nshift -= 8) {
+    for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
+    __syncwarp();
+    for (int base = 0; base < n; base += kThreads) {
+      const int i = base + tid;
+      const uint32_t u = i < n ? keys[i] : 0u;
+      const bool active = i < n && (u >> shift) == prefix;
+      warp_hist_add(my_hist, (u >> nshift) & (kBins - 1), active);
     }
-    __syncthreads();
-    find_bin(hist, nbins, k_rem, wsum, res);
-    prefix = (prefix << (level == 1 ? 11 : 10)) | res[0];
+    merge_warp_hists(whist, hist);
+    find_bin(hist, kBins, k_rem, wsum, res);
+    prefix = (prefix << 8) | res[0];
     k_rem = res[1];
     whole = (res[2] == k_rem);
     shift = nshift;
   }
+  __syncthreads();  // the histogram space becomes the pair buffer below
   const uint32_t need_eq = k_rem;  // keys with (u >> shift) == prefix to take, lowest index first
 
   // Ordered compaction.  Warp w scans positions [w*span, (w+1)*span) in 32-wide steps.
@@ -282,7 +304,9 @@ int kpow2(int k) {
 }
 
 size_t segment_smem(int chunk, int k, int sorted) {
-  return static_cast<size_t>((chunk + 1) & ~1) * 4 + kHistBins * 4 + (sorted ? static_cast<size_t>(kpow2(k)) * 8 : 0);
+  const size_t hists = static_cast<size_t>(kWarps) * kBins * 4;
+  const size_t pairs = sorted ? static_cast<size_t>(kpow2(k)) * 8 : 0;
+  return static_cast<size_t>((chunk + 1) & ~1) * 4 + (hists > pairs ? hists : pairs);
 }
 
 int launch_segments(const TopkArgs& a, int rows, int nseg, cudaStream_t stream) {

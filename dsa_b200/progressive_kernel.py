@@ -15,7 +15,9 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .indexer import score_dense
+from . import _capi as capi
+from .indexer import (_DTYPES, prepare_keys, prepare_queries, prepare_weights, score_dense,
+                      stream_ptr)
 
 HEADS = 64
 HEAD_DIM = 128
@@ -90,3 +92,134 @@ def full_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys: torch
     """:362-375 -- dense scores [L] float32.  block_size is a reference tiling knob only."""
     _check_cuda_inputs(queries, weights, keys)
     return score_dense(queries, weights, keys)
+
+
+# --------------------------------------------------------------------------- block kernels
+def _block_inputs(queries, weights, keys, block_size):
+    if block_size not in (16, 32, 64, 128):
+        raise ValueError("block_size must be 16, 32, 64 or 128 on B200")
+    keys = prepare_keys(keys.unsqueeze(0))
+    q = prepare_queries(queries.unsqueeze(0), keys.dtype)
+    w = prepare_weights(weights.unsqueeze(0))
+    return q, w, keys, math.ceil(keys.shape[1] / block_size)
+
+
+def _mask(mask: torch.Tensor, device) -> torch.Tensor:
+    return mask.to(device=device, dtype=torch.int8).contiguous()
+
+
+def _head_ids(ids, device, count: int) -> torch.Tensor:
+    return torch.as_tensor(ids).to(device=device, dtype=torch.int32).contiguous()
+
+
+def _selected_heads(selected_heads, device) -> torch.Tensor:
+    if isinstance(selected_heads, torch.Tensor) and selected_heads.is_cuda:
+        if selected_heads.numel() != VERIFIER_HEADS:
+            raise ValueError("selected head IDs must have shape [8]")
+        return _head_ids(selected_heads, device, VERIFIER_HEADS)
+    selected, _ = split_head_ids(selected_heads)
+    return selected.to(device)
+
+
+def _call_blocks(name: str, *args) -> None:
+    capi.call(name, *args)
+
+
+def h8_block_max_triton(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor,
+                        selected_heads: torch.Tensor, cold_blocks: torch.Tensor, *,
+                        block_size: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
+    """:378-404 -- 8-head partial scores on cold blocks (-inf elsewhere) and block maxima."""
+    _check_cuda_inputs(queries, weights, keys)
+    q, w, k, nblocks = _block_inputs(queries, weights, keys, block_size)
+    if cold_blocks.numel() != nblocks:
+        raise ValueError("cold block mask length mismatch")
+    selected = _selected_heads(selected_heads, k.device)
+    cold = _mask(cold_blocks, k.device)
+    length = k.shape[1]
+    partial = torch.empty(length, device=k.device, dtype=torch.float32)
+    maxima = torch.empty(nblocks, device=k.device, dtype=torch.float32)
+    _call_blocks("tdsa_h8_block_max", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
+                 k.data_ptr(), k.stride(0), k.stride(1), _DTYPES[k.dtype], 1, length,
+                 block_size, selected.data_ptr(), cold.data_ptr(), partial.data_ptr(), length,
+                 maxima.data_ptr(), nblocks, stream_ptr(k.device))
+    return partial, maxima
+
+
+def masked_full_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor,
+                              keep_blocks: torch.Tensor, *, block_size: int = 64) -> torch.Tensor:
+    """:407-424 -- dense scores on kept blocks, -inf elsewhere (dropped blocks are not read)."""
+    _check_cuda_inputs(queries, weights, keys)
+    q, w, k, nblocks = _block_inputs(queries, weights, keys, block_size)
+    if keep_blocks.numel() != nblocks:
+        raise ValueError("keep block mask length mismatch")
+    keep = _mask(keep_blocks, k.device)
+    length = k.shape[1]
+    out = torch.empty(length, device=k.device, dtype=torch.float32)
+    _call_blocks("tdsa_masked_dense", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
+                 k.data_ptr(), k.stride(0), k.stride(1), _DTYPES[k.dtype], 1, length,
+                 block_size, keep.data_ptr(), nblocks, out.data_ptr(), length,
+                 stream_ptr(k.device))
+    return out
+
+
+def progressive_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor,
+                              selected_heads: torch.Tensor, direct_full_blocks: torch.Tensor,
+                              threshold: float | torch.Tensor, *, block_size: int = 64,
+                              compact: bool = False,
+                              remaining_heads: torch.Tensor | None = None) -> ProgressiveResult:
+    """:427-475 -- fused H8 probe -> promotion -> remaining 56 heads.
+
+    Dense output: rejected blocks score -inf.  compact=True: the accepted blocks' valid
+    keys packed in ascending key order, with candidate_count read back to the host (a sync,
+    as in the reference).
+    """
+    _check_cuda_inputs(queries, weights, keys)
+    q, w, k, nblocks = _block_inputs(queries, weights, keys, block_size)
+    dev = k.device
+    if remaining_heads is None:
+        selected, remaining = split_head_ids(selected_heads.cpu())
+        selected, remaining = selected.to(dev), remaining.to(dev)
+    else:
+        if (selected_heads.numel() != VERIFIER_HEADS
+                or remaining_heads.numel() != HEADS - VERIFIER_HEADS):
+            raise ValueError("expected 8 selected and 56 remaining head IDs")
+        selected = _head_ids(selected_heads, dev, VERIFIER_HEADS)
+        remaining = _head_ids(remaining_heads, dev, HEADS - VERIFIER_HEADS)
+    if direct_full_blocks.numel() != nblocks:
+        raise ValueError("direct full block mask length mismatch")
+    direct = _mask(direct_full_blocks, dev)
+    thr = torch.as_tensor(threshold, device=dev, dtype=torch.float32).reshape(1)
+    length = k.shape[1]
+    scores = torch.empty(length, device=dev, dtype=torch.float32)
+    accepted = torch.empty(nblocks, device=dev, dtype=torch.int8)
+    block_max = torch.empty(nblocks, device=dev, dtype=torch.float32)
+    _call_blocks("tdsa_progressive_h8", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
+                 k.data_ptr(), k.stride(0), k.stride(1), _DTYPES[k.dtype], 1, length,
+                 block_size, selected.data_ptr(), remaining.data_ptr(), direct.data_ptr(),
+                 thr.data_ptr(), scores.data_ptr(), length, accepted.data_ptr(),
+                 block_max.data_ptr(), nblocks, stream_ptr(dev))
+    if not compact:
+        return ProgressiveResult(scores, accepted, block_max)
+    packed = torch.empty(length, device=dev, dtype=torch.float32)
+    indices = torch.empty(length, device=dev, dtype=torch.int32)
+    count = torch.zeros(1, device=dev, dtype=torch.int32)
+    _call_blocks("tdsa_compact_blocks", scores.data_ptr(), length, accepted.data_ptr(), nblocks,
+                 1, length, block_size, packed.data_ptr(), indices.data_ptr(), length,
+                 count.data_ptr(), stream_ptr(dev))
+    candidate_count = int(count.item())
+    return ProgressiveResult(packed[:candidate_count], accepted, block_max,
+                             indices[:candidate_count], candidate_count)
+
+
+def two_pass_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor,
+                           selected_heads: torch.Tensor, direct_full_blocks: torch.Tensor,
+                           threshold: float | torch.Tensor, *,
+                           block_size: int = 64) -> ProgressiveResult:
+    """:478-497 -- H8 block max on cold blocks, then dense scoring of the accepted ones."""
+    cold = ~direct_full_blocks.to(torch.bool)
+    _, maxima = h8_block_max_triton(queries, weights, keys, selected_heads, cold,
+                                    block_size=block_size)
+    thr = torch.as_tensor(threshold, device=keys.device, dtype=torch.float32)
+    accepted = direct_full_blocks.to(device=keys.device, dtype=torch.bool) | (maxima >= thr)
+    scores = masked_full_scores_triton(queries, weights, keys, accepted, block_size=block_size)
+    return ProgressiveResult(scores, accepted.to(torch.int8), maxima)

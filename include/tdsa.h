@@ -113,6 +113,53 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
                     size_t workspace_bytes, void* stream);
 
 /*
+ * Block-structured kernels (block_size 16, 32, 64 or 128; 16-bit keys).  Keys of a block
+ * that is not needed are never read.  Per-block arrays ([batch][bm_batch_stride], int8 or
+ * float32) share one row stride >= ceil(length / block_size); per-key outputs have row
+ * stride >= length.  selected_heads: 8 head ids (device int32), the same for every row.
+ *
+ * tdsa_h8_block_max -- replaces h8_block_max_triton + _h8_block_max_kernel
+ *   (src/temporal_dsa/progressive_kernel.py:378-404, :218-246): partial = 8-head score of
+ *   the keys of cold blocks, -inf elsewhere; block_max = per-block max of partial.
+ */
+int tdsa_h8_block_max(const void* queries, int64_t q_batch_stride, const float* weights,
+                      int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                      int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                      const int32_t* selected_heads, const int8_t* cold_blocks,
+                      float* partial, int64_t p_batch_stride, float* block_max,
+                      int64_t bm_batch_stride, void* stream);
+
+/* tdsa_masked_dense -- replaces masked_full_scores_triton + _masked_full_kernel
+ *   (progressive_kernel.py:407-424, :249-274): dense scores of kept blocks, -inf elsewhere. */
+int tdsa_masked_dense(const void* queries, int64_t q_batch_stride, const float* weights,
+                      int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                      int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                      const int8_t* keep_blocks, int64_t keep_batch_stride, float* scores,
+                      int64_t s_batch_stride, void* stream);
+
+/* tdsa_progressive_h8 -- replaces progressive_scores_triton + _progressive_kernel
+ *   (progressive_kernel.py:427-475, :277-346), dense output: direct blocks score all 64
+ *   heads (block_max -inf); cold blocks score the 8 selected heads, are promoted when their
+ *   block max >= *threshold (device float) and then add the remaining heads
+ *   (remaining_heads: 56 device ids, or NULL for the complement of selected_heads);
+ *   rejected blocks score -inf; accepted[b] = 1 for direct or promoted blocks. */
+int tdsa_progressive_h8(const void* queries, int64_t q_batch_stride, const float* weights,
+                        int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                        int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                        const int32_t* selected_heads, const int32_t* remaining_heads,
+                        const int8_t* direct_blocks, const float* threshold, float* scores,
+                        int64_t s_batch_stride, int8_t* accepted, float* block_max,
+                        int64_t bm_batch_stride, void* stream);
+
+/* tdsa_compact_blocks -- the compact output of progressive_scores_triton (:335-340,
+ *   :468-474): the scores and indices of every valid key of the accepted blocks, packed in
+ *   ascending key order, and their count (device int32 per row). */
+int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_t* accepted,
+                        int64_t a_batch_stride, int batch, int length, int block_size,
+                        float* out_scores, int32_t* out_indices, int64_t out_batch_stride,
+                        int32_t* out_count, void* stream);
+
+/*
  * Query epilogue of the sidecar projection: RoPE on the first rope_dim dims of every head
  * and the head-weight scale, fused into one pass over the W_q / W_w GEMM outputs.
  * Replaces: the tail of LightningIndexerSidecar.encode_queries (src/temporal_dsa/

@@ -32,9 +32,14 @@ def test_query_projector_matches_oracle(dtype):
     pos = torch.tensor([0, 17, 32767], device="cuda")
     proj = QueryProjector(wq, ww, 3)
     q, w = proj.project(x, pos)
-    # RoPE on the GEMM's own output: float32 math, one final rounding to the 16-bit dtype
+    # RoPE on the GEMM's own output: float32 math, one final rounding to the 16-bit dtype.
+    # The float32 angle pos * inv_freq is only good to ~pos * 2^-23 rad (one ulp of
+    # inv_freq, which CUDA's powf and numpy may round differently), so the tolerance at
+    # position 32767 is |x| * 32767 * 2^-23 ~ 1.5e-2; small positions are held to 2^-7.
     want_q = osc.rope_heads(proj.qraw.float().cpu().numpy(), pos.cpu().numpy())
-    np.testing.assert_allclose(q.float().cpu().numpy(), want_q, rtol=2 ** -7, atol=1e-4)
+    got_q = q.float().cpu().numpy()
+    np.testing.assert_allclose(got_q[:2], want_q[:2], rtol=2 ** -7, atol=1e-4)
+    np.testing.assert_allclose(got_q[2], want_q[2], rtol=2 ** -7, atol=2e-2)
     want_w = (x.float().cpu().numpy().astype(np.float64) @ ww.cpu().numpy().T.astype(np.float64)
               ) * (64 * 128) ** -0.5
     np.testing.assert_allclose(w.cpu().numpy(), want_w, rtol=1e-5, atol=1e-6)
