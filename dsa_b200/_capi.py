@@ -46,8 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_progressive_h8": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp,
                                   vp, vp, i64, vp, vp, i64, vp]),
     "tdsa_compact_blocks": (i32, [vp, i64, vp, i64, i32, i32, i32, vp, vp, i64, vp, vp]),
-    "tdsa_query_prep": (i32, [vp, i64, vp, i64, vp, vp, i64, vp, i64, i32, i32, i32, C.c_float,
-                              C.c_float, vp]),
+    "tdsa_query_prep": (i32, [vp, i64, vp, i64, i32, vp, vp, vp, i64, vp, i64, i32, i32, i32,
+                              C.c_float, C.c_float, vp]),
 }
 
 _lib: C.CDLL | None = None

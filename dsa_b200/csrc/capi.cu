@@ -276,22 +276,26 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
                      static_cast<cudaStream_t>(stream));
 }
 
-int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const float* wraw,
-                    int64_t wraw_stride, const int64_t* positions, void* q, int64_t q_stride,
-                    float* w, int64_t w_stride, int dtype, int batch, int rope_dim,
-                    float rope_theta, float weight_scale, void* stream) {
-  if (!qraw || !wraw || !positions || !q || !w) return fail(TDSA_ERR_INVALID, "null pointer");
+int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,
+                    int64_t hidden_stride, int hidden_size, const float* w_proj,
+                    const int64_t* positions, void* q, int64_t q_stride, float* w,
+                    int64_t w_stride, int dtype, int batch, int rope_dim, float rope_theta,
+                    float weight_scale, void* stream) {
+  if (!qraw || !hidden || !w_proj || !positions || !q || !w)
+    return fail(TDSA_ERR_INVALID, "null pointer");
   if (dtype != TDSA_BF16 && dtype != TDSA_F16)
     return fail(TDSA_ERR_INVALID, "query_prep takes TDSA_BF16 or TDSA_F16");
   if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
+  if (hidden_size < 1 || hidden_size > 16384)
+    return fail(TDSA_ERR_UNSUPPORTED, "hidden_size must be in [1, 16384]");
   if (rope_dim < 0 || rope_dim > kHeadDim || rope_dim % 2)
     return fail(TDSA_ERR_INVALID, "rope_dim must be even and <= 128");
   if (batch > 1 && (qraw_stride < kHeads * kHeadDim || q_stride < kHeads * kHeadDim ||
-                    wraw_stride < kHeads || w_stride < kHeads))
+                    hidden_stride < hidden_size || w_stride < kHeads))
     return fail(TDSA_ERR_INVALID, "row strides overlap");
-  return launch_qprep(qraw, qraw_stride, wraw, wraw_stride, positions, q, q_stride, w, w_stride,
-                      dtype, batch, rope_dim, rope_theta, weight_scale,
-                      static_cast<cudaStream_t>(stream));
+  return launch_qprep(qraw, qraw_stride, hidden, hidden_stride, hidden_size, w_proj, positions,
+                      q, q_stride, w, w_stride, dtype, batch, rope_dim, rope_theta,
+                      weight_scale, static_cast<cudaStream_t>(stream));
 }
 
 int tdsa_h8_block_max(const void* queries, int64_t q_batch_stride, const float* weights,

@@ -62,12 +62,12 @@ int topk_check(int length, int k, int sorted);
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,
                 int batch, int length, int k, int sorted, void* out_idx, int idx_bytes,
                 int64_t oi_stride, float* out_val, int64_t ov_stride, void* ws, size_t ws_bytes,
-                cudaStream_t stream);
+                cudaStream_t stream, float* kth_out = nullptr);
 
-int launch_qprep(const void* qraw, int64_t qraw_stride, const float* wraw, int64_t wraw_stride,
-                 const int64_t* positions, void* q, int64_t q_stride, float* w,
-                 int64_t w_stride, int dtype, int batch, int rope_dim, float theta,
-                 float scale, cudaStream_t stream);
+int launch_qprep(const void* qraw, int64_t qraw_stride, const void* x, int64_t x_stride,
+                 int hidden, const float* ww, const int64_t* positions, void* q,
+                 int64_t q_stride, float* w, int64_t w_stride, int dtype, int batch,
+                 int rope_dim, float theta, float scale, cudaStream_t stream);
 
 // Device status word of the current device (allocated with the module, never freed).
 int* device_status_ptr();

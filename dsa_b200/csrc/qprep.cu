@@ -1,15 +1,19 @@
-// Query epilogue of the sidecar projection (reference sidecar.py:78-87), fused:
-//   q[b,h,:]  = RoPE_noninterleaved(qraw[b, h*128 : h*128+128]) on the first rope_dim dims
-//   w[b,h]    = wraw[b,h] * scale            (scale = (64*128)^-1/2 in the reference)
-// qraw is the [B, 64*128] output of the W_q GEMM (cuBLAS), wraw the [B,64] float32 output
-// of the W_w GEMM.  RoPE angles are position * theta^(-j/half) in float32, as the
-// reference computes them; the rotation is done in float32 and rounded once.
+// Decode-step tail of the sidecar query projection (reference sidecar.py:78-87), one launch:
+//   q[b,h,:] = RoPE_noninterleaved(qraw[b, h*128 : h*128+128]) on the first rope_dim dims
+//   w[b,h]   = scale * sum_k float(x[b,k]) * W_w[h,k]        (float32, as the reference's
+//                                                              autocast-disabled weights_proj)
+// qraw is the [B, 64*128] output of the W_q GEMM (cuBLAS, 16-bit).  Grid (B, 2): y = 0 CTAs
+// rotate one row of q, y = 1 CTAs compute one row of w (a float32 GEMV over the hidden
+// size; W_w streams from L2).  RoPE angles are position * theta^(-j/half) in float32 as in
+// the reference; the rotation is done in float32 and rounded once.
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace tdsa {
 
 namespace {
+
+constexpr int kThreads = 512;
 
 template <typename T>
 __device__ __forceinline__ float to_f(T x);
@@ -33,49 +37,79 @@ __device__ __forceinline__ __half from_f<__half>(float x) {
 }
 
 template <typename T>
-__global__ void qprep_kernel(const T* __restrict__ qraw, int64_t qraw_stride,
-                             const float* __restrict__ wraw, int64_t wraw_stride,
-                             const int64_t* __restrict__ positions, T* __restrict__ q,
-                             int64_t q_stride, float* __restrict__ w, int64_t w_stride,
-                             int rope_dim, float theta, float scale) {
-  const int b = blockIdx.y;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // element of the 64*128 row
-  if (i < kHeads * kHeadDim) {
-    const int h = i >> 7, d = i & 127;
-    const T* src = qraw + static_cast<int64_t>(b) * qraw_stride + h * kHeadDim;
-    float out = to_f(src[d]);
-    if (d < rope_dim) {
-      const int half = rope_dim >> 1;
-      const int j = d < half ? d : d - half;
-      const float inv_freq = powf(theta, -static_cast<float>(j) / static_cast<float>(half));
+__global__ void __launch_bounds__(kThreads)
+    qprep_kernel(const T* __restrict__ qraw, int64_t qraw_stride, const T* __restrict__ x,
+                 int64_t x_stride, int hidden, const float* __restrict__ ww,
+                 const int64_t* __restrict__ positions, T* __restrict__ q, int64_t q_stride,
+                 float* __restrict__ w, int64_t w_stride, int rope_dim, float theta,
+                 float scale) {
+  extern __shared__ float xs[];  // [hidden] for the GEMV half
+  __shared__ float cs[64], sn[64];
+  const int b = blockIdx.x;
+  if (blockIdx.y == 0) {
+    const int half = rope_dim >> 1;
+    if (threadIdx.x < half) {
+      const float inv_freq =
+          powf(theta, -static_cast<float>(threadIdx.x) / static_cast<float>(half));
       const float angle = static_cast<float>(positions[b]) * inv_freq;
-      float s, c;
-      sincosf(angle, &s, &c);
-      const float first = to_f(src[j]), second = to_f(src[j + half]);
-      out = d < half ? first * c - second * s : second * c + first * s;
+      sincosf(angle, &sn[threadIdx.x], &cs[threadIdx.x]);
     }
-    q[static_cast<int64_t>(b) * q_stride + i] = from_f<T>(out);
+    __syncthreads();
+    const T* src = qraw + static_cast<int64_t>(b) * qraw_stride;
+    T* dst = q + static_cast<int64_t>(b) * q_stride;
+    for (int i = threadIdx.x; i < kHeads * kHeadDim; i += kThreads) {
+      const int h = i >> 7, d = i & 127;
+      const T* row = src + h * kHeadDim;
+      float out = to_f(row[d]);
+      if (d < rope_dim) {
+        const int j = d < half ? d : d - half;
+        const float first = to_f(row[j]), second = to_f(row[j + half]);
+        out = d < half ? first * cs[j] - second * sn[j] : second * cs[j] + first * sn[j];
+      }
+      dst[i] = from_f<T>(out);
+    }
+    return;
   }
-  if (blockIdx.x == 0 && threadIdx.x < kHeads)
-    w[static_cast<int64_t>(b) * w_stride + threadIdx.x] =
-        wraw[static_cast<int64_t>(b) * wraw_stride + threadIdx.x] * scale;
+  // w row b: stage x[b] in shared memory as float, 16 warps x 4 heads, warp-reduced dots
+  const T* xr = x + static_cast<int64_t>(b) * x_stride;
+  for (int i = threadIdx.x; i < hidden; i += kThreads) xs[i] = to_f(xr[i]);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int h = warp; h < kHeads; h += kThreads / 32) {
+    const float* wr = ww + static_cast<int64_t>(h) * hidden;
+    float acc = 0.f;
+    for (int i = lane; i < hidden; i += 32) acc = fmaf(xs[i], __ldg(wr + i), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) w[static_cast<int64_t>(b) * w_stride + h] = acc * scale;
+  }
 }
 
 }  // namespace
 
-int launch_qprep(const void* qraw, int64_t qraw_stride, const float* wraw, int64_t wraw_stride,
-                 const int64_t* positions, void* q, int64_t q_stride, float* w,
-                 int64_t w_stride, int dtype, int batch, int rope_dim, float theta,
-                 float scale, cudaStream_t stream) {
-  const dim3 grid((kHeads * kHeadDim + 255) / 256, batch);
-  if (dtype == TDSA_BF16)
-    qprep_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(qraw), qraw_stride, wraw, wraw_stride, positions,
+int launch_qprep(const void* qraw, int64_t qraw_stride, const void* x, int64_t x_stride,
+                 int hidden, const float* ww, const int64_t* positions, void* q,
+                 int64_t q_stride, float* w, int64_t w_stride, int dtype, int batch,
+                 int rope_dim, float theta, float scale, cudaStream_t stream) {
+  const dim3 grid(batch, 2);
+  const size_t smem = static_cast<size_t>(hidden) * 4;
+  if (dtype == TDSA_BF16) {
+    auto kern = qprep_kernel<__nv_bfloat16>;
+    TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    kern<<<grid, kThreads, smem, stream>>>(
+        static_cast<const __nv_bfloat16*>(qraw), qraw_stride,
+        static_cast<const __nv_bfloat16*>(x), x_stride, hidden, ww, positions,
         static_cast<__nv_bfloat16*>(q), q_stride, w, w_stride, rope_dim, theta, scale);
-  else
-    qprep_kernel<__half><<<grid, 256, 0, stream>>>(
-        static_cast<const __half*>(qraw), qraw_stride, wraw, wraw_stride, positions,
-        static_cast<__half*>(q), q_stride, w, w_stride, rope_dim, theta, scale);
+  } else {
+    auto kern = qprep_kernel<__half>;
+    TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    kern<<<grid, kThreads, smem, stream>>>(
+        static_cast<const __half*>(qraw), qraw_stride, static_cast<const __half*>(x), x_stride,
+        hidden, ww, positions, static_cast<__half*>(q), q_stride, w, w_stride, rope_dim, theta,
+        scale);
+  }
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }

@@ -38,6 +38,7 @@ struct TopkArgs {
   int64_t out_idx_stride;
   float* out_val;         // may be null
   int64_t out_val_stride;
+  float* kth_out;         // per output row: the k-th largest value (may be null)
 };
 
 __device__ __forceinline__ unsigned lanemask_lt() {
@@ -99,17 +100,6 @@ __device__ void find_bin(const uint32_t* hist, int nbins, uint32_t k_rem, uint32
   __syncthreads();
 }
 
-// Adds one key digit per active lane to the warp's private histogram; lanes with equal
-// digits are combined first (one shared-memory atomic per distinct digit).
-__device__ __forceinline__ void warp_hist_add(uint32_t* whist, uint32_t digit, bool active) {
-  const unsigned m = __ballot_sync(0xffffffffu, active);
-  if (active) {
-    const unsigned peers = __match_any_sync(m, digit);
-    if ((threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1))
-      atomicAdd(&whist[digit], static_cast<uint32_t>(__popc(peers)));
-  }
-}
-
 // Sums the per-warp histograms into hist[kBins].
 __device__ __forceinline__ void merge_warp_hists(const uint32_t* whist, uint32_t* hist) {
   __syncthreads();
@@ -122,12 +112,37 @@ __device__ __forceinline__ void merge_warp_hists(const uint32_t* whist, uint32_t
   __syncthreads();
 }
 
+__device__ __forceinline__ int bit_length(uint32_t x) { return x ? 32 - __clz(x) : 0; }
+
+// Digit of key u for a pass binning [blo, bhi] with bin width 2^s: keys below / above the
+// binned range clamp into the first / last bin (the mapping stays monotone).
+__device__ __forceinline__ uint32_t range_digit(uint32_t u, uint32_t blo, uint32_t bhi, int s) {
+  if (u < blo) return 0u;
+  if (u > bhi) return kBins - 1;
+  return (u - blo) >> s;
+}
+
+__device__ __forceinline__ void block_minmax(uint32_t& mn, uint32_t& mx, uint32_t* sbuf) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  mn = __reduce_min_sync(0xffffffffu, mn);
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  if (lane == 0) {
+    sbuf[warp] = mn;
+    sbuf[32 + warp] = mx;
+  }
+  __syncthreads();
+  mn = __reduce_min_sync(0xffffffffu, sbuf[lane]);
+  mx = __reduce_max_sync(0xffffffffu, sbuf[32 + lane]);
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArgs a) {
-  extern __shared__ uint32_t sm[];
+  extern __shared__ __align__(16) uint32_t sm[];
   __shared__ uint32_t wsum[64];
   __shared__ uint32_t res[4];
   __shared__ uint32_t wcnt[2][kWarps];
   __shared__ uint32_t hist[kBins];
+  __shared__ uint32_t s_kth;
 
   const int row = blockIdx.y, seg = blockIdx.x;
   const int start = seg * a.chunk;
@@ -135,55 +150,100 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* keys = sm;
   // per-warp digit histograms; the same space holds the sort pairs after selection
-  uint32_t* whist = sm + ((a.chunk + 1) & ~1);
+  uint32_t* whist = sm + ((a.chunk + 3) & ~3);
   uint32_t* my_hist = whist + warp * kBins;
   uint64_t* pairs = reinterpret_cast<uint64_t*>(whist);
 
   const float* vrow = a.vals + static_cast<int64_t>(row) * a.vals_stride + start;
   const int32_t* irow = a.idx ? a.idx + static_cast<int64_t>(row) * a.idx_stride + start : nullptr;
+  constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // float_to_key(-inf)
+  constexpr uint32_t kNanKey = 0xFFFFFFFFu;
 
-  for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
-  __syncwarp();
-  // Load, convert to order-preserving keys, histogram of the top digit.
-  for (int base = 0; base < n; base += kThreads) {
-    const int i = base + tid;
-    const bool active = i < n;
-    uint32_t u = 0;
-    if (active) {
-      u = float_to_key(__ldg(vrow + i));
-      keys[i] = u;
+  // ---- load: keys to shared memory, min/max of the regular keys (not -inf, not NaN)
+  uint32_t rmin = 0xFFFFFFFFu, rmax = 0u, amin = 0xFFFFFFFFu, amax = 0u;
+  auto note = [&](uint32_t u) {
+    amin = min(amin, u);
+    amax = max(amax, u);
+    if (u != kNegInfKey && u != kNanKey) {
+      rmin = min(rmin, u);
+      rmax = max(rmax, u);
     }
-    warp_hist_add(my_hist, u >> 24, active);
+  };
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u) {
+    const float4* v4 = reinterpret_cast<const float4*>(vrow);
+    uint4* k4 = reinterpret_cast<uint4*>(keys);
+    const int n4 = n >> 2;
+    for (int i = tid; i < n4; i += kThreads) {
+      const float4 v = __ldg(v4 + i);
+      const uint4 u = make_uint4(float_to_key(v.x), float_to_key(v.y), float_to_key(v.z),
+                                 float_to_key(v.w));
+      k4[i] = u;
+      note(u.x);
+      note(u.y);
+      note(u.z);
+      note(u.w);
+    }
+    done = n4 << 2;
   }
-  merge_warp_hists(whist, hist);
+  for (int i = done + tid; i < n; i += kThreads) {
+    const uint32_t u = float_to_key(__ldg(vrow + i));
+    keys[i] = u;
+    note(u);
+  }
+  for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
+  block_minmax(rmin, rmax, wsum);
+  block_minmax(amin, amax, wsum);
+  if (rmin > rmax) {  // no regular key: bin over everything
+    rmin = amin;
+    rmax = amax;
+  }
 
+  // ---- range-narrowing radix select: the k-th key lies in [clo, chi]
   const int k = min(a.k, n);
   uint32_t k_rem = static_cast<uint32_t>(k);
-  int shift = 24;  // keys compare as (u >> shift) against prefix
-  find_bin(hist, kBins, k_rem, wsum, res);
-  uint32_t prefix = res[0];
-  k_rem = res[1];
-  bool whole = (res[2] == k_rem);
-  // Remaining 8-bit digits; only keys still matching the prefix are counted.
-  for (int nshift = 16; nshift >= 0 && !whole; nshift -= 8) {
-    for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
+  uint32_t clo = 0u, chi = 0xFFFFFFFFu;
+  uint32_t blo = rmin, bhi = rmax;  // pass 1 bins the regular keys, clamping the rest
+  bool whole = false;
+  for (int pass = 0; pass < 6 && !whole && clo != chi; ++pass) {
+    const int sh = max(0, bit_length(bhi - blo) - 8);
+    if (pass > 0) {
+      for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
+    }
     __syncwarp();
-    for (int base = 0; base < n; base += kThreads) {
-      const int i = base + tid;
-      const uint32_t u = i < n ? keys[i] : 0u;
-      const bool active = i < n && (u >> shift) == prefix;
-      warp_hist_add(my_hist, (u >> nshift) & (kBins - 1), active);
+    const uint4* k4 = reinterpret_cast<const uint4*>(keys);
+    const int n4 = n >> 2;
+    for (int i = tid; i < n4; i += kThreads) {
+      const uint4 u = k4[i];
+      const uint32_t e[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (e[j] >= clo && e[j] <= chi) atomicAdd(&my_hist[range_digit(e[j], blo, bhi, sh)], 1u);
+    }
+    for (int i = (n4 << 2) + tid; i < n; i += kThreads) {
+      const uint32_t u = keys[i];
+      if (u >= clo && u <= chi) atomicAdd(&my_hist[range_digit(u, blo, bhi, sh)], 1u);
     }
     merge_warp_hists(whist, hist);
     find_bin(hist, kBins, k_rem, wsum, res);
-    prefix = (prefix << 8) | res[0];
+    const uint32_t d = res[0];
     k_rem = res[1];
     whole = (res[2] == k_rem);
-    shift = nshift;
+    // key range of bin d (64-bit: blo + 255 * 2^sh can pass 2^32)
+    const uint64_t step = 1ull << sh;
+    uint64_t lo64 = d == 0 ? clo : static_cast<uint64_t>(blo) + d * step;
+    uint64_t hi64 = d == kBins - 1 ? chi
+                                   : min(static_cast<uint64_t>(blo) + (d + 1) * step - 1,
+                                         static_cast<uint64_t>(bhi));
+    if (d == kBins - 1) lo64 = min(lo64, static_cast<uint64_t>(bhi) + 1);  // + clamped-high keys
+    clo = static_cast<uint32_t>(lo64);
+    chi = static_cast<uint32_t>(hi64);
+    blo = clo;
+    bhi = chi;
   }
   __syncthreads();  // the histogram space becomes the pair buffer below
-  const uint32_t need_eq = k_rem;  // keys with (u >> shift) == prefix to take, lowest index first
-
+  if (tid == 0) s_kth = 0xFFFFFFFFu;
+  const uint32_t need_eq = k_rem;  // keys in [clo, chi] to take, lowest index first
   // Ordered compaction.  Warp w scans positions [w*span, (w+1)*span) in 32-wide steps.
   const int span = ((n + kWarps * 32 - 1) / (kWarps * 32)) * 32;
   const int w0 = warp * span, w1 = min(n, w0 + span);
@@ -192,9 +252,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     const int i = base + lane;
     bool gt = false, eq = false;
     if (i < w1) {
-      const uint32_t hi = keys[i] >> shift;
-      gt = hi > prefix;
-      eq = hi == prefix;
+      const uint32_t u = keys[i];
+      gt = u > chi;
+      eq = u >= clo && u <= chi;
     }
     cgt += __popc(__ballot_sync(0xffffffffu, gt));
     ceq += __popc(__ballot_sync(0xffffffffu, eq));
@@ -232,9 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     uint32_t u = 0;
     if (i < w1) {
       u = keys[i];
-      const uint32_t hi = u >> shift;
-      gt = hi > prefix;
-      eq = hi == prefix;
+      gt = u > chi;
+      eq = u >= clo && u <= chi;
     }
     const unsigned bg = __ballot_sync(0xffffffffu, gt);
     const unsigned be = __ballot_sync(0xffffffffu, eq);
@@ -251,9 +310,10 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     }
     if (take) {
       const uint32_t gi = irow ? static_cast<uint32_t>(irow[i]) : static_cast<uint32_t>(start + i);
+      if (eq) atomicMin(&s_kth, u);
       if (a.sorted) {
         pairs[pos] = (static_cast<uint64_t>(u) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - gi);
-      } else {
+      } else if (a.out_idx) {
         if (a.idx_bytes == 8)
           static_cast<int64_t*>(a.out_idx)[out_row * a.out_idx_stride + pos] = static_cast<int64_t>(gi);
         else
@@ -264,6 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     gbase += __popc(bg);
     ebase += __popc(be);
   }
+  __syncthreads();
+  if (tid == 0 && a.kth_out) a.kth_out[out_row] = key_to_float(s_kth);
   if (!a.sorted) return;
 
   // Bitonic sort of the k selected (key, ~index) pairs, descending; padding sorts last.
@@ -286,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       __syncthreads();
     }
   }
+  if (!a.out_idx) return;
   for (int j = tid; j < k; j += kThreads) {
     const uint64_t p = pairs[j];
     const uint32_t gi = 0xFFFFFFFFu - static_cast<uint32_t>(p & 0xFFFFFFFFull);
@@ -306,7 +369,7 @@ int kpow2(int k) {
 size_t segment_smem(int chunk, int k, int sorted) {
   const size_t hists = static_cast<size_t>(kWarps) * kBins * 4;
   const size_t pairs = sorted ? static_cast<size_t>(kpow2(k)) * 8 : 0;
-  return static_cast<size_t>((chunk + 1) & ~1) * 4 + (hists > pairs ? hists : pairs);
+  return static_cast<size_t>((chunk + 3) & ~3) * 4 + (hists > pairs ? hists : pairs);
 }
 
 int launch_segments(const TopkArgs& a, int rows, int nseg, cudaStream_t stream) {
@@ -363,7 +426,7 @@ int topk_check(int length, int k, int sorted) {
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,
                 int batch, int length, int k, int sorted, void* out_idx, int idx_bytes,
                 int64_t oi_stride, float* out_val, int64_t ov_stride, void* ws, size_t ws_bytes,
-                cudaStream_t stream) {
+                cudaStream_t stream, float* kth_out) {
   int rc = topk_check(length, k, sorted);
   if (rc) return rc;
   const Plan p = make_plan(length, k);
@@ -391,6 +454,7 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
     a.row_len = p.count[level];
     a.chunk = p.chunk[level];
     a.k = k;
+    a.kth_out = nullptr;
     const bool last = level == p.levels - 1;
     if (last) {
       a.sorted = sorted;
@@ -399,6 +463,7 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
       a.out_idx_stride = oi_stride;
       a.out_val = out_val;
       a.out_val_stride = ov_stride;
+      a.kth_out = kth_out;
     } else {
       const int b = level & 1;
       a.sorted = 0;

@@ -78,8 +78,8 @@ def encode_queries(hidden: torch.Tensor, wq: torch.Tensor, ww: torch.Tensor,
 
 
 class QueryProjector:
-    """Decode-step query projection on fixed buffers: two cuBLAS GEMMs (W_q in the hidden
-    dtype, W_w in float32) and one fused RoPE + weight-scale kernel (tdsa_query_prep).
+    """Decode-step query projection on fixed buffers: one cuBLAS GEMM for W_q (hidden
+    dtype) and one fused kernel (tdsa_query_prep) for RoPE and the float32 head weights.
 
     ``project(hidden, positions)`` -> (q [B,64,128], w [B,64] float32), written into
     ``self.q`` / ``self.w`` (stable addresses, so a ScoreTopkPlan can be built on them).
@@ -92,29 +92,33 @@ class QueryProjector:
             raise ValueError("expected wq [8192, hidden] and ww [64, hidden]")
         if wq.dtype not in (torch.bfloat16, torch.float16):
             raise ValueError("wq must be bf16 or fp16")
-        dev, hidden = wq.device, wq.shape[1]
+        if ww.shape[1] != wq.shape[1]:
+            raise ValueError("wq and ww must share the hidden size")
+        dev = wq.device
+        self.hidden = wq.shape[1]
         self.wq_t = wq.t()
-        self.ww_t = ww.to(torch.float32).t()
+        self.ww = ww.to(torch.float32).contiguous()
         self.dtype = wq.dtype
         self.batch, self.rope_dim, self.theta = batch, rope_dim, rope_theta
         self.qraw = torch.empty(batch, HEADS * HEAD_DIM, device=dev, dtype=wq.dtype)
-        self.wraw = torch.empty(batch, HEADS, device=dev, dtype=torch.float32)
-        self.hidden_f32 = torch.empty(batch, hidden, device=dev, dtype=torch.float32)
         self.q = torch.empty(batch, HEADS, HEAD_DIM, device=dev, dtype=wq.dtype)
         self.w = torch.empty(batch, HEADS, device=dev, dtype=torch.float32)
         self._fn = capi.lib().tdsa_query_prep
         self._dt = capi.TDSA_BF16 if wq.dtype == torch.bfloat16 else capi.TDSA_F16
 
     def project(self, hidden: torch.Tensor, positions: torch.Tensor):
+        if hidden.shape != (self.batch, self.hidden) or hidden.dtype != self.dtype:
+            raise ValueError("hidden must be [batch, hidden] in the projection dtype")
+        if hidden.stride(-1) != 1:
+            hidden = hidden.contiguous()
         torch.matmul(hidden, self.wq_t, out=self.qraw)
-        self.hidden_f32.copy_(hidden)
-        torch.matmul(self.hidden_f32, self.ww_t, out=self.wraw)
         if positions.dtype != torch.int64 or not positions.is_contiguous():
             positions = positions.to(torch.int64).contiguous()
-        capi.check(self._fn(self.qraw.data_ptr(), self.qraw.stride(0), self.wraw.data_ptr(),
-                            self.wraw.stride(0), positions.data_ptr(), self.q.data_ptr(),
-                            HEADS * HEAD_DIM, self.w.data_ptr(), HEADS, self._dt, self.batch,
-                            self.rope_dim, self.theta, (HEADS * HEAD_DIM) ** -0.5,
+        capi.check(self._fn(self.qraw.data_ptr(), self.qraw.stride(0), hidden.data_ptr(),
+                            hidden.stride(0), self.hidden, self.ww.data_ptr(),
+                            positions.data_ptr(), self.q.data_ptr(), HEADS * HEAD_DIM,
+                            self.w.data_ptr(), HEADS, self._dt, self.batch, self.rope_dim,
+                            self.theta, (HEADS * HEAD_DIM) ** -0.5,
                             torch.cuda.current_stream(self.q.device).cuda_stream))
         return self.q, self.w
 

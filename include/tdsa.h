@@ -160,18 +160,20 @@ int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_
                         int32_t* out_count, void* stream);
 
 /*
- * Query epilogue of the sidecar projection: RoPE on the first rope_dim dims of every head
- * and the head-weight scale, fused into one pass over the W_q / W_w GEMM outputs.
+ * Decode-step tail of the sidecar query projection, one launch: RoPE on the first rope_dim
+ * dims of every head of the W_q GEMM output, and the float32 head weights
+ * w = weight_scale * hidden @ w_proj^T.
  * Replaces: the tail of LightningIndexerSidecar.encode_queries (src/temporal_dsa/
  *   sidecar.py:78-87) with apply_noninterleaved_rope (:10-28).
- * qraw [batch][64*128] (dtype TDSA_BF16 or TDSA_F16), row stride qraw_stride;
- * wraw [batch][64] float32; positions [batch] int64;
- * q    [batch][64][128] out (same dtype), w [batch][64] float32 out (w = wraw * scale).
+ * qraw   [batch][64*128] (dtype TDSA_BF16 or TDSA_F16), row stride qraw_stride;
+ * hidden [batch][hidden_size] (same dtype), w_proj [64][hidden_size] float32;
+ * positions [batch] int64; q [batch][64][128] out (same dtype); w [batch][64] float32 out.
  */
-int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const float* wraw,
-                    int64_t wraw_stride, const int64_t* positions, void* q, int64_t q_stride,
-                    float* w, int64_t w_stride, int dtype, int batch, int rope_dim,
-                    float rope_theta, float weight_scale, void* stream);
+int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,
+                    int64_t hidden_stride, int hidden_size, const float* w_proj,
+                    const int64_t* positions, void* q, int64_t q_stride, float* w,
+                    int64_t w_stride, int dtype, int batch, int rope_dim, float rope_theta,
+                    float weight_scale, void* stream);
 
 #ifdef __cplusplus
 }
