@@ -394,4 +394,111 @@ int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_
                                static_cast<cudaStream_t>(stream));
 }
 
+size_t tdsa_exact_state_bytes(int batch, int max_length, int k, int block_size) {
+  if (batch < 1 || max_length < 1 || k < 1 || k > max_length ||
+      (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128))
+    return 0;
+  return exact_layout(batch, max_length, k, block_size).total;
+}
+
+static int exact_common(int init, void* state, size_t state_bytes, const void* queries,
+                        int64_t q_batch_stride, const float* weights, int64_t w_batch_stride,
+                        const void* keys, int64_t k_batch_stride, int64_t k_row_stride,
+                        int dtype, int batch, int prev_length, int length, int max_length,
+                        int k, int block_size, int sorted, void* out_indices, int index_bytes,
+                        int64_t idx_batch_stride, float* out_values, int64_t val_batch_stride,
+                        void* stream) {
+  int rc = check_score_args(queries, q_batch_stride, weights, w_batch_stride, keys,
+                            k_batch_stride, k_row_stride, dtype, batch, length, nullptr, 0,
+                            false);
+  if (rc) return rc;
+  if (dtype == TDSA_F32)
+    return fail(TDSA_ERR_UNSUPPORTED, "the exact progressive path takes bf16/fp16 keys");
+  if (length < 1 || length > max_length)
+    return fail(TDSA_ERR_INVALID, "need 1 <= length <= max_length");
+  if (!init && (prev_length < k || prev_length > length))
+    return fail(TDSA_ERR_INVALID, "need k <= prev_length <= length (the cache only grows)");
+  rc = topk_check(length, k, sorted);
+  if (rc) return rc;
+  if (out_indices && index_bytes != 4 && index_bytes != 8)
+    return fail(TDSA_ERR_INVALID, "index_bytes must be 4 or 8");
+  if (batch > 1 && ((out_indices && idx_batch_stride < k) || (out_values && val_batch_stride < k)))
+    return fail(TDSA_ERR_INVALID, "output row strides must be >= k");
+  const size_t need = tdsa_exact_state_bytes(batch, max_length, k, block_size);
+  if (need == 0) return fail(TDSA_ERR_INVALID, "bad state geometry (block_size 16/32/64/128)");
+  if (!state || state_bytes < need)
+    return fail(TDSA_ERR_WORKSPACE, "exact state missing or smaller than tdsa_exact_state_bytes");
+  const ExactLayout L = exact_layout(batch, max_length, k, block_size);
+  return run_exact(init, static_cast<uint8_t*>(state), L, queries, q_batch_stride, weights,
+                   w_batch_stride, keys, k_batch_stride, k_row_stride, dtype, batch,
+                   prev_length, length, max_length, k, block_size, sorted ? 1 : 0, out_indices,
+                   index_bytes, idx_batch_stride, out_values, val_batch_stride,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_exact_init(void* state, size_t state_bytes, const void* queries,
+                    int64_t q_batch_stride, const float* weights, int64_t w_batch_stride,
+                    const void* keys, int64_t k_batch_stride, int64_t k_row_stride, int dtype,
+                    int batch, int length, int max_length, int k, int block_size, int sorted,
+                    void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                    float* out_values, int64_t val_batch_stride, void* stream) {
+  return exact_common(1, state, state_bytes, queries, q_batch_stride, weights, w_batch_stride,
+                      keys, k_batch_stride, k_row_stride, dtype, batch, 0, length, max_length,
+                      k, block_size, sorted, out_indices, index_bytes, idx_batch_stride,
+                      out_values, val_batch_stride, stream);
+}
+
+int tdsa_exact_step(void* state, size_t state_bytes, const void* queries,
+                    int64_t q_batch_stride, const float* weights, int64_t w_batch_stride,
+                    const void* keys, int64_t k_batch_stride, int64_t k_row_stride, int dtype,
+                    int batch, int prev_length, int length, int max_length, int k,
+                    int block_size, int sorted, void* out_indices, int index_bytes,
+                    int64_t idx_batch_stride, float* out_values, int64_t val_batch_stride,
+                    void* stream) {
+  return exact_common(0, state, state_bytes, queries, q_batch_stride, weights, w_batch_stride,
+                      keys, k_batch_stride, k_row_stride, dtype, batch, prev_length, length,
+                      max_length, k, block_size, sorted, out_indices, index_bytes,
+                      idx_batch_stride, out_values, val_batch_stride, stream);
+}
+
+int tdsa_exact_stats(const void* state, size_t state_bytes, int batch, int max_length, int k,
+                     int block_size, uint64_t* stats_out) {
+  const size_t need = tdsa_exact_state_bytes(batch, max_length, k, block_size);
+  if (!state || !stats_out || need == 0 || state_bytes < need)
+    return fail(TDSA_ERR_INVALID, "bad state or geometry");
+  const ExactLayout L = exact_layout(batch, max_length, k, block_size);
+  TDSA_CUDA_CHECK(cudaMemcpy(stats_out, static_cast<const uint8_t*>(state) + L.stats,
+                             static_cast<size_t>(batch) * 64, cudaMemcpyDeviceToHost));
+  return TDSA_OK;
+}
+
+int tdsa_block_key_norms(const double* keys, int tokens, int heads, int dim, int block_size,
+                         double* out, void* stream) {
+  if (!keys || !out) return fail(TDSA_ERR_INVALID, "null pointer");
+  if (tokens < 1 || heads < 1 || dim < 1 || block_size < 1)
+    return fail(TDSA_ERR_INVALID, "tokens, heads, dim and block_size must be positive");
+  return launch_block_key_norms(keys, tokens, heads, dim, block_size, out,
+                                static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_temporal_radius(const double* q_now, const double* q_prev, const double* w_now,
+                         const double* w_prev, const double* block_key_norm, int heads, int dim,
+                         int blocks, double* coeff_workspace, double* out, void* stream) {
+  if (!q_now || !q_prev || !w_now || !w_prev || !block_key_norm || !coeff_workspace || !out)
+    return fail(TDSA_ERR_INVALID, "null pointer");
+  if (heads < 1 || dim < 1 || blocks < 0) return fail(TDSA_ERR_INVALID, "bad sizes");
+  if (blocks == 0) return TDSA_OK;
+  return launch_temporal_radius(q_now, q_prev, w_now, w_prev, block_key_norm, heads, dim,
+                                blocks, coeff_workspace, out, static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_relu_index_score(const double* q, const double* keys, const double* w, int heads,
+                          int dim, int tokens, double* out, void* stream) {
+  if (!q || !keys || !w || !out) return fail(TDSA_ERR_INVALID, "null pointer");
+  if (heads < 1 || dim < 1 || tokens < 0) return fail(TDSA_ERR_INVALID, "bad sizes");
+  if (tokens == 0) return TDSA_OK;
+  return launch_relu_index_score(q, keys, w, heads, dim, tokens, out,
+                                 static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -1,0 +1,437 @@
+// Exact (certified) progressive top-k: the host schedule and its small device kernels.
+//
+// One decode step per sequence (all sequences of the batch advance together):
+//   1. new-key norms: max ||k|| per block for keys appended since the last step;
+//   2. prepare: certified coefficient c = sum_h |w_t-w_p| ||q_p,h|| + |w_t| ||q_t,h-q_p,h||
+//      (reference certified.py:18-48, with one key vector shared by the heads) plus a
+//      rounding slack, per-block bound U_b + maxnorm_b * c (new-key blocks: +inf, as
+//      replay.py:263-266), scores reset to -inf, wave 1 = blocks holding a previous top-k
+//      key or new keys (hot first, replay.py:153-169);
+//   3. wave 1 scored on the tensor cores (exact block maxima as a by-product);
+//   4. tau = k-th largest wave-1 score (>= the seed threshold min(current[prev_topk]));
+//   5. wave 2 = the other blocks whose bound reaches tau; the rest are pruned unread;
+//   6. wave 2 scored; 7. top-k over the scored keys; 8. state update: U_b <- exact block max
+//      (scored) or bound (pruned), q/w kept for the next step, statistics accumulated.
+// Every pruned key has a score strictly below tau <= the k-th largest, so the top-k equals
+// dense scoring's; the scores are bit-identical to the dense kernel's (same MMA tile, same
+// epilogue summation order).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tdsa {
+
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr double kGamma = 0x1p-12;  // relative rounding slack of a computed score
+
+// Squared norm of each appended key, rounded up, folded into its block's max (float bits of
+// non-negative floats order like unsigned integers).  One warp per key.
+__global__ void new_key_norms_kernel(const void* keys, int64_t k_bs, int64_t k_rs, int dtype,
+                                     int first_key, int length, int bs, uint32_t* maxsq,
+                                     int64_t nb_stride) {
+  const int b = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int warps = (blockDim.x >> 5) * gridDim.x;
+  const int64_t base = static_cast<int64_t>(b) * k_bs;
+  for (int key = first_key + blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); key < length;
+       key += warps) {
+    // 4 dims per lane in one 8-byte load (rows are 16-byte aligned: TMA layout rules)
+    const uint2 raw = *reinterpret_cast<const uint2*>(
+        static_cast<const uint16_t*>(keys) + base + static_cast<int64_t>(key) * k_rs + lane * 4);
+    const uint16_t e[4] = {static_cast<uint16_t>(raw.x & 0xFFFFu), static_cast<uint16_t>(raw.x >> 16),
+                           static_cast<uint16_t>(raw.y & 0xFFFFu), static_cast<uint16_t>(raw.y >> 16)};
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float v = dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(e[j]) << 16)
+                                         : __half2float(__ushort_as_half(e[j]));
+      s = __fadd_ru(s, __fmul_ru(v, v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_ru(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (lane == 0) atomicMax(&maxsq[static_cast<int64_t>(b) * nb_stride + key / bs], __float_as_uint(s));
+  }
+}
+
+struct PrepArgs {
+  const void* q;
+  int64_t q_bs;
+  const float* w;
+  int64_t w_bs;
+  const void* qprev;   // [B][8192] 16-bit
+  const float* wprev;  // [B][64]
+  int dtype;
+  int prev_length, length, bs, bpt, k;
+  int64_t nb_stride, l_stride;
+  const float* upper;
+  const uint32_t* maxsq;
+  const int32_t* prev_topk;
+  float* bound;
+  int8_t* flag;
+  float* scores;
+  int32_t* tile_seq;
+  int32_t* tile_blk;
+  int32_t* counter;
+  int init;  // 1: every block is scored (first step)
+};
+
+__device__ __forceinline__ float qelem(const void* q, int dtype, int64_t off) {
+  return dtype == TDSA_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(q)[off])
+                            : __half2float(static_cast<const __half*>(q)[off]);
+}
+
+// Ordered compaction of the blocks with flag == want into tiles of bpt blocks.
+__device__ void emit_tiles(const int8_t* flag, int nb, int want, int bpt, int seq,
+                           int32_t* tile_seq, int32_t* tile_blk, int32_t* counter,
+                           uint32_t* wtot, uint32_t* sbase) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // count
+  uint32_t cnt = 0;
+  for (int b = threadIdx.x; b < nb; b += kThreads) cnt += flag[b] == want;
+  cnt = __reduce_add_sync(0xffffffffu, cnt);
+  if (lane == 0) wtot[warp] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t total = 0;
+    for (int i = 0; i < 32; ++i) total += wtot[i];
+    const int ntiles = static_cast<int>((total + bpt - 1) / bpt);
+    sbase[0] = ntiles ? static_cast<uint32_t>(atomicAdd(counter, ntiles)) : 0u;
+    sbase[1] = 0;  // running position
+    sbase[2] = total;
+  }
+  __syncthreads();
+  const uint32_t tile0 = sbase[0], total = sbase[2];
+  // ordered positions, 1024 blocks per round
+  for (int base = 0; base < nb; base += kThreads) {
+    const int b = base + threadIdx.x;
+    const bool take = b < nb && flag[b] == want;
+    const unsigned bal = __ballot_sync(0xffffffffu, take);
+    if (lane == 0) wtot[warp] = __popc(bal);
+    __syncthreads();
+    uint32_t before = 0, round = 0;
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t c = wtot[i];
+      before += i < warp ? c : 0u;
+      round += c;
+    }
+    const uint32_t pos = sbase[1] + before + __popc(bal & ((1u << lane) - 1u));
+    if (take) {
+      const uint32_t t = tile0 + pos / bpt;
+      tile_blk[static_cast<int64_t>(t) * bpt + pos % bpt] = b;
+      if (pos % bpt == 0) tile_seq[t] = seq;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) sbase[1] += round;
+    __syncthreads();
+  }
+  // pad the last tile with empty slots
+  if (threadIdx.x < bpt && total % bpt) {
+    const uint32_t pos = total + threadIdx.x;
+    if (pos % bpt != 0 && pos / bpt == (total - 1) / bpt)
+      tile_blk[static_cast<int64_t>(tile0 + pos / bpt) * bpt + pos % bpt] = -1;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs a) {
+  __shared__ double coeff[64];
+  __shared__ double c_total;
+  __shared__ uint32_t wtot[32];
+  __shared__ uint32_t sbase[4];
+  const int seq = blockIdx.x;
+  const int nb = (a.length + a.bs - 1) / a.bs;
+  const int first_new = a.init ? 0 : a.prev_length / a.bs;
+  const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
+  int8_t* flag = a.flag + brow;
+
+  if (!a.init) {
+    // coefficient: 16 threads per head, 8 dims each, float64
+    const int h = threadIdx.x >> 4, sub = threadIdx.x & 15;
+    double dd = 0.0, pp = 0.0, nn = 0.0;
+    for (int i = 0; i < 8; ++i) {
+      const int d = sub + 16 * i;
+      const double qn = qelem(a.q, a.dtype, static_cast<int64_t>(seq) * a.q_bs + h * 128 + d);
+      const double qp = qelem(a.qprev, a.dtype, static_cast<int64_t>(seq) * 8192 + h * 128 + d);
+      dd += (qn - qp) * (qn - qp);
+      pp += qp * qp;
+      nn += qn * qn;
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      dd += __shfl_xor_sync(0xffffffffu, dd, o);
+      pp += __shfl_xor_sync(0xffffffffu, pp, o);
+      nn += __shfl_xor_sync(0xffffffffu, nn, o);
+    }
+    if (sub == 0) {
+      const double wn = a.w[static_cast<int64_t>(seq) * a.w_bs + h];
+      const double wp = a.wprev[static_cast<int64_t>(seq) * 64 + h];
+      const double nqp = sqrt(pp), nqn = sqrt(nn), ndq = sqrt(dd);
+      coeff[h] = fabs(wn - wp) * nqp + fabs(wn) * ndq + kGamma * (fabs(wn) * nqn + fabs(wp) * nqp);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double c = 0.0;
+      for (int i = 0; i < 64; ++i) c += coeff[i];
+      c_total = c * (1.0 + 0x1p-40);
+    }
+  }
+  // reset the per-key scores of this step
+  float* srow = a.scores + static_cast<int64_t>(seq) * a.l_stride;
+  for (int i = threadIdx.x; i < a.length; i += kThreads) srow[i] = -INFINITY;
+  __syncthreads();
+  // bounds and flags
+  for (int b = threadIdx.x; b < nb; b += kThreads) {
+    float bnd = INFINITY;
+    if (b < first_new) {
+      const double nrm = static_cast<double>(__fsqrt_ru(__uint_as_float(a.maxsq[brow + b])));
+      bnd = __double2float_ru(static_cast<double>(a.upper[brow + b]) + nrm * c_total);
+    }
+    a.bound[brow + b] = bnd;
+    flag[b] = (a.init || b >= first_new) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!a.init) {
+    const int32_t* top = a.prev_topk + static_cast<int64_t>(seq) * a.k;
+    for (int i = threadIdx.x; i < a.k; i += kThreads) {
+      const int blk = top[i] / a.bs;
+      if (blk >= 0 && blk < nb) flag[blk] = 1;
+    }
+  }
+  __syncthreads();
+  emit_tiles(flag, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counter, wtot, sbase);
+}
+
+// Wave 2: blocks not scored yet whose bound reaches tau.
+__global__ void __launch_bounds__(kThreads)
+    exact_wave2_kernel(int length, int bs, int bpt, int64_t nb_stride, const float* bound,
+                       const float* tau, int8_t* flag, int32_t* tile_seq, int32_t* tile_blk,
+                       int32_t* counter) {
+  __shared__ uint32_t wtot[32];
+  __shared__ uint32_t sbase[4];
+  const int seq = blockIdx.x;
+  const int nb = (length + bs - 1) / bs;
+  const int64_t brow = static_cast<int64_t>(seq) * nb_stride;
+  const float t = tau[seq];
+  for (int b = threadIdx.x; b < nb; b += kThreads)
+    if (flag[brow + b] == 0 && bound[brow + b] >= t) flag[brow + b] = 2;
+  __syncthreads();
+  emit_tiles(flag + brow, nb, 2, bpt, seq, tile_seq, tile_blk, counter, wtot, sbase);
+}
+
+// State update and statistics.
+__global__ void __launch_bounds__(kThreads)
+    exact_finalize_kernel(const void* q, int64_t q_bs, const float* w, int64_t w_bs, int dtype,
+                          int length, int bs, int64_t nb_stride, const int8_t* flag,
+                          const float* bmax, const float* bound, float* upper, void* qprev,
+                          float* wprev, unsigned long long* stats, int new_keys) {
+  __shared__ unsigned long long acc[4];
+  const int seq = blockIdx.x;
+  const int nb = (length + bs - 1) / bs;
+  const int64_t brow = static_cast<int64_t>(seq) * nb_stride;
+  if (threadIdx.x < 4) acc[threadIdx.x] = 0ull;
+  __syncthreads();
+  unsigned long long scored = 0, keys = 0, hot = 0, wave2 = 0;
+  for (int b = threadIdx.x; b < nb; b += kThreads) {
+    const int8_t f = flag[brow + b];
+    upper[brow + b] = f ? bmax[brow + b] : bound[brow + b];
+    if (f) {
+      ++scored;
+      keys += static_cast<unsigned long long>(min(bs, length - b * bs));
+      hot += f == 1;
+      wave2 += f == 2;
+    }
+  }
+  atomicAdd(&acc[0], scored);
+  atomicAdd(&acc[1], keys);
+  atomicAdd(&acc[2], hot);
+  atomicAdd(&acc[3], wave2);
+  // keep q (16-bit bits) and w for the next step's certified coefficient
+  const uint16_t* qs = static_cast<const uint16_t*>(q) + static_cast<int64_t>(seq) * q_bs;
+  uint16_t* qd = static_cast<uint16_t*>(qprev) + static_cast<int64_t>(seq) * 8192;
+  for (int i = threadIdx.x; i < 8192; i += kThreads) qd[i] = qs[i];
+  if (threadIdx.x < 64) wprev[static_cast<int64_t>(seq) * 64 + threadIdx.x] =
+      w[static_cast<int64_t>(seq) * w_bs + threadIdx.x];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long* st = stats + static_cast<int64_t>(seq) * 8;
+    st[0] += 1;                                    // steps
+    st[1] += static_cast<unsigned long long>(nb);  // blocks visited
+    st[2] += acc[0];                               // blocks scored
+    st[3] += static_cast<unsigned long long>(nb) - acc[0];  // blocks pruned
+    st[4] += acc[1];                               // keys scored (read)
+    st[5] += static_cast<unsigned long long>(length);       // keys in the cache
+    st[6] += acc[2];                               // first-wave (hot) blocks
+    st[7] += acc[3];                               // second-wave blocks
+    (void)dtype;
+    (void)new_keys;
+  }
+}
+
+__global__ void copy_indices_kernel(const int32_t* src, int64_t s_stride, void* dst,
+                                    int64_t d_stride, int idx_bytes, int k) {
+  const int row = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x) {
+    const int32_t v = src[static_cast<int64_t>(row) * s_stride + i];
+    if (idx_bytes == 8)
+      static_cast<int64_t*>(dst)[static_cast<int64_t>(row) * d_stride + i] = v;
+    else
+      static_cast<int32_t*>(dst)[static_cast<int64_t>(row) * d_stride + i] = v;
+  }
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+
+ExactLayout exact_layout(int batch, int max_length, int k, int block_size) {
+  ExactLayout L;
+  L.nb_stride = (max_length + block_size - 1) / block_size;
+  L.bpt = 128 / block_size;
+  L.tcap = static_cast<int64_t>(batch) * ((L.nb_stride + L.bpt - 1) / L.bpt);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t nbt = static_cast<size_t>(batch) * L.nb_stride;
+  L.upper = take(nbt * 4);
+  L.maxsq = take(nbt * 4);
+  L.bound = take(nbt * 4);
+  L.bmax = take(nbt * 4);
+  L.flag = take(nbt);
+  L.topk = take(static_cast<size_t>(batch) * k * 4);
+  L.qprev = take(static_cast<size_t>(batch) * 8192 * 2);
+  L.wprev = take(static_cast<size_t>(batch) * 64 * 4);
+  L.scores = take(static_cast<size_t>(batch) * max_length * 4);
+  L.tau = take(static_cast<size_t>(batch) * 4);
+  L.stats = take(static_cast<size_t>(batch) * 8 * 8);
+  L.tile_seq = take(static_cast<size_t>(L.tcap) * 4);
+  L.tile_blk = take(static_cast<size_t>(L.tcap) * L.bpt * 4);
+  L.counters = take(16);
+  L.topk_ws_bytes = topk_workspace_bytes(batch, max_length, k);
+  L.topk_ws = take(L.topk_ws_bytes);
+  L.total = off;
+  return L;
+}
+
+int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int64_t q_bs,
+              const float* w, int64_t w_bs, const void* keys, int64_t k_bs, int64_t k_rs,
+              int dtype, int batch, int prev_length, int length, int max_length, int k,
+              int block_size, int sorted, void* out_idx, int idx_bytes, int64_t idx_bs,
+              float* out_val, int64_t val_bs, cudaStream_t stream) {
+  const int bpt = 128 / block_size;
+  float* upper = reinterpret_cast<float*>(state + L.upper);
+  uint32_t* maxsq = reinterpret_cast<uint32_t*>(state + L.maxsq);
+  float* bound = reinterpret_cast<float*>(state + L.bound);
+  float* bmax = reinterpret_cast<float*>(state + L.bmax);
+  int8_t* flag = reinterpret_cast<int8_t*>(state + L.flag);
+  int32_t* topk = reinterpret_cast<int32_t*>(state + L.topk);
+  void* qprev = state + L.qprev;
+  float* wprev = reinterpret_cast<float*>(state + L.wprev);
+  float* scores = reinterpret_cast<float*>(state + L.scores);
+  float* tau = reinterpret_cast<float*>(state + L.tau);
+  auto* stats = reinterpret_cast<unsigned long long*>(state + L.stats);
+  int32_t* tile_seq = reinterpret_cast<int32_t*>(state + L.tile_seq);
+  int32_t* tile_blk = reinterpret_cast<int32_t*>(state + L.tile_blk);
+  int32_t* counters = reinterpret_cast<int32_t*>(state + L.counters);
+  void* tws = state + L.topk_ws;
+
+  if (init) {
+    TDSA_CUDA_CHECK(cudaMemsetAsync(maxsq, 0, static_cast<size_t>(batch) * L.nb_stride * 4,
+                                    stream));
+    TDSA_CUDA_CHECK(cudaMemsetAsync(stats, 0, static_cast<size_t>(batch) * 64, stream));
+  }
+  TDSA_CUDA_CHECK(cudaMemsetAsync(counters, 0, 16, stream));
+  // 1. norms of the keys appended since the last step (all keys at init)
+  const int first_key = init ? 0 : prev_length;
+  if (length > first_key) {
+    const int nkeys = length - first_key;
+    const int blocks_x = min(148, (nkeys + 7) / 8);
+    new_key_norms_kernel<<<dim3(blocks_x, batch), 256, 0, stream>>>(
+        keys, k_bs, k_rs, dtype, first_key, length, block_size, maxsq, L.nb_stride);
+    TDSA_CUDA_CHECK(cudaGetLastError());
+  }
+  // 2. bounds, flags, wave-1 tiles
+  PrepArgs pa;
+  pa.q = q;
+  pa.q_bs = q_bs;
+  pa.w = w;
+  pa.w_bs = w_bs;
+  pa.qprev = qprev;
+  pa.wprev = wprev;
+  pa.dtype = dtype;
+  pa.prev_length = prev_length;
+  pa.length = length;
+  pa.bs = block_size;
+  pa.bpt = bpt;
+  pa.k = k;
+  pa.nb_stride = L.nb_stride;
+  pa.l_stride = max_length;
+  pa.upper = upper;
+  pa.maxsq = maxsq;
+  pa.prev_topk = topk;
+  pa.bound = bound;
+  pa.flag = flag;
+  pa.scores = scores;
+  pa.tile_seq = tile_seq;
+  pa.tile_blk = tile_blk;
+  pa.counter = counters;
+  pa.init = init;
+  exact_prepare_kernel<<<batch, kThreads, 0, stream>>>(pa);
+  TDSA_CUDA_CHECK(cudaGetLastError());
+
+  BlockArgs ba;
+  ba.bs = block_size;
+  ba.bpt = bpt;
+  ba.length = length;
+  ba.nblocks = (length + block_size - 1) / block_size;
+  ba.tile_seq = tile_seq;
+  ba.tile_blocks = tile_blk;
+  ba.w = w;
+  ba.w_stride = w_bs;
+  ba.out = scores;
+  ba.out_stride = max_length;
+  ba.block_max = bmax;
+  ba.bm_stride = L.nb_stride;
+  ba.status = device_status_ptr();
+  if (!ba.status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  const int grid = device_sm_count(current_device());
+  // 3. wave 1
+  ba.tile_count = counters;
+  int rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
+                               stream);
+  if (rc) return rc;
+  if (!init) {
+    // 4. tau = k-th largest wave-1 score
+    rc = launch_topk(scores, max_length, nullptr, 0, batch, length, k, 0, nullptr, 4, k,
+                     nullptr, 0, tws, L.topk_ws_bytes, stream, tau);
+    if (rc) return rc;
+    // 5. wave-2 list, 6. wave 2
+    exact_wave2_kernel<<<batch, kThreads, 0, stream>>>(length, block_size, bpt, L.nb_stride,
+                                                       bound, tau, flag, tile_seq, tile_blk,
+                                                       counters + 1);
+    TDSA_CUDA_CHECK(cudaGetLastError());
+    ba.tile_count = counters + 1;
+    rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
+                             stream);
+    if (rc) return rc;
+  }
+  // 7. top-k over the scored keys (indices kept as the next step's seeds)
+  rc = launch_topk(scores, max_length, nullptr, 0, batch, length, k, sorted, topk, 4, k, out_val,
+                   val_bs, tws, L.topk_ws_bytes, stream, nullptr);
+  if (rc) return rc;
+  if (out_idx) {
+    copy_indices_kernel<<<dim3((k + 255) / 256, batch), 256, 0, stream>>>(topk, k, out_idx,
+                                                                          idx_bs, idx_bytes, k);
+    TDSA_CUDA_CHECK(cudaGetLastError());
+  }
+  // 8. state update
+  exact_finalize_kernel<<<batch, kThreads, 0, stream>>>(
+      q, q_bs, w, w_bs, dtype, length, block_size, L.nb_stride, flag, bmax, bound, upper, qprev,
+      wprev, stats, length - first_key);
+  TDSA_CUDA_CHECK(cudaGetLastError());
+  return TDSA_OK;
+}
+
+}  // namespace tdsa

@@ -57,6 +57,32 @@ int launch_compact_blocks(const float* scores, int64_t s_stride, const int8_t* a
                           float* out_scores, int32_t* out_indices, int64_t o_stride,
                           int32_t* out_count, cudaStream_t stream);
 
+// ---- exact progressive path (exact.cu)
+struct ExactLayout {
+  size_t upper = 0, maxsq = 0, bound = 0, bmax = 0, flag = 0, topk = 0, qprev = 0, wprev = 0;
+  size_t scores = 0, tau = 0, stats = 0, tile_seq = 0, tile_blk = 0, counters = 0, topk_ws = 0;
+  size_t topk_ws_bytes = 0, total = 0;
+  int64_t nb_stride = 0, tcap = 0;
+  int bpt = 0;
+};
+
+ExactLayout exact_layout(int batch, int max_length, int k, int block_size);
+
+int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int64_t q_bs,
+              const float* w, int64_t w_bs, const void* keys, int64_t k_bs, int64_t k_rs,
+              int dtype, int batch, int prev_length, int length, int max_length, int k,
+              int block_size, int sorted, void* out_idx, int idx_bytes, int64_t idx_bs,
+              float* out_val, int64_t val_bs, cudaStream_t stream);
+
+// ---- certified-bound helpers, float64 (certified.cu)
+int launch_block_key_norms(const double* keys, int tokens, int heads, int dim, int bs,
+                           double* out, cudaStream_t stream);
+int launch_temporal_radius(const double* qn, const double* qp, const double* wn,
+                           const double* wp, const double* norms, int heads, int dim, int nb,
+                           double* coeff_ws, double* out, cudaStream_t stream);
+int launch_relu_index_score(const double* q, const double* keys, const double* w, int heads,
+                            int dim, int tokens, double* out, cudaStream_t stream);
+
 size_t topk_workspace_bytes(int batch, int length, int k);
 int topk_check(int length, int k, int sorted);
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,

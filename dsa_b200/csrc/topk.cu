@@ -1,16 +1,16 @@
-// Exact row-wise top-k by radix select in shared memory (no global sort).
+// Exact row-wise top-k by radix select, keys held in registers (no global sort).
 //
-// One 1024-thread CTA owns one segment of a row (<= 32768 elements, held in shared memory
-// as order-preserving uint32 keys).  Up to four histogram passes over 8-bit digits (one
-// private histogram per warp, lanes with equal digits combined before the atomic) pin the
-// k-th key T exactly, stopping early when a digit bin is taken whole; an ordered
-// compaction then takes every key > T plus the first (k - #greater) keys == T in index
-// order, which is the tie rule of the reference's stable_topk (metrics.py:9-22).  The
-// selection is written in ascending index order, or, when sorted output is asked for,
-// bitonic-sorted in shared memory by (key descending, index ascending).
+// One 1024-thread CTA owns one segment of a row (<= 32768 elements).  Thread t holds the
+// 32 consecutive elements [32t, 32t+32) as order-preserving uint32 keys in registers.
+// Range-narrowing radix passes (256 bins over the live key range, one private histogram
+// per warp in shared memory) pin the k-th key T; every key > T is taken and keys == T are
+// taken lowest index first, which is the tie rule of the reference's stable_topk
+// (metrics.py:9-22).  Because each thread owns a contiguous run, two block-wide scans give
+// every taken key its output position in ascending index order; sorted output is a bitonic
+// sort of the k taken (key, index) pairs in shared memory.
 //
-// Rows longer than one segment run in levels: every segment emits its local top-k in
-// index order, and the candidates (global top-k is a subset of their union) are selected
+// Rows longer than one segment run in levels: every segment emits its local top-k in index
+// order, and the candidates (the global top-k is a subset of their union) are selected
 // again with explicit indices until one segment remains.  The same explicit-index pass
 // merges per-GPU candidates of an L-sharded cache.
 #include "common.cuh"
@@ -22,7 +22,8 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBins = 256;  // 8-bit radix digits
+constexpr int kPer = kTopkSegment / kThreads;  // 32 keys per thread
+constexpr int kBins = 256;
 
 struct TopkArgs {
   const float* vals;      // [rows][row_stride]
@@ -33,7 +34,7 @@ struct TopkArgs {
   int chunk;              // segment length (gridDim.x segments per row)
   int k;
   int sorted;
-  void* out_idx;          // [rows * gridDim.x][out_idx_stride]
+  void* out_idx;          // [rows * gridDim.x][out_idx_stride] (null: k-th value only)
   int idx_bytes;
   int64_t out_idx_stride;
   float* out_val;         // may be null
@@ -41,106 +42,57 @@ struct TopkArgs {
   float* kth_out;         // per output row: the k-th largest value (may be null)
 };
 
-__device__ __forceinline__ unsigned lanemask_lt() {
-  unsigned m;
-  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
-  return m;
-}
-
-// Suffix scan over the block: returns sum of v over threads >= this thread (inclusive).
-__device__ __forceinline__ uint32_t block_suffix_sum(uint32_t v, uint32_t* wsum) {
+// Inclusive block-wide prefix sum of v (thread order), with the block total.
+__device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t* wsum, uint32_t& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t x = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_down_sync(0xffffffffu, x, o);
-    if (lane + o < 32) x += y;
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
   }
-  if (lane == 0) wsum[warp] = x;
+  if (lane == 31) wsum[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    uint32_t t = wsum[lane];
+    const uint32_t t = wsum[lane];
     uint32_t s = t;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_down_sync(0xffffffffu, s, o);
-      if (lane + o < 32) s += y;
+      const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
     }
-    wsum[32 + lane] = s - t;  // sum over warps strictly after `lane`
+    wsum[32 + lane] = s - t;  // exclusive prefix over warps
+    if (lane == 31) wsum[64] = s;
   }
   __syncthreads();
   const uint32_t r = x + wsum[32 + warp];
+  total = wsum[64];
   __syncthreads();
   return r;
 }
 
-// Finds the digit bin holding the k_rem-th largest key among the histogrammed keys.
-// Writes {bin, k_rem within the bin, count of the bin} to res[0..2].
-__device__ void find_bin(const uint32_t* hist, int nbins, uint32_t k_rem, uint32_t* wsum,
-                         uint32_t* res) {
-  const int per = nbins > kThreads ? nbins / kThreads : 1;
-  const int lo = threadIdx.x * per;
-  uint32_t local = 0;
-  if (lo < nbins)
-    for (int i = 0; i < per; ++i) local += hist[lo + i];
-  const uint32_t incl = block_suffix_sum(local, wsum);
-  uint32_t above = incl - local;
-  if (local > 0 && above < k_rem && k_rem <= incl) {
-    for (int i = per - 1; i >= 0; --i) {
-      const uint32_t c = hist[lo + i];
-      if (above + c >= k_rem) {
-        res[0] = lo + i;
-        res[1] = k_rem - above;
-        res[2] = c;
-        break;
-      }
-      above += c;
-    }
-  }
-  __syncthreads();
-}
-
-// Sums the per-warp histograms into hist[kBins].
-__device__ __forceinline__ void merge_warp_hists(const uint32_t* whist, uint32_t* hist) {
-  __syncthreads();
-  if (threadIdx.x < kBins) {
-    uint32_t s = 0;
-#pragma unroll 8
-    for (int w = 0; w < kWarps; ++w) s += whist[w * kBins + threadIdx.x];
-    hist[threadIdx.x] = s;
+// The bin (of kBins) holding the k_rem-th largest counted key: res = {bin, k_rem within the
+// bin, count of the bin}.  Threads 0..255 each own one bin; suffix sums via a reversed scan.
+__device__ void find_bin(const uint32_t* hist, uint32_t k_rem, uint32_t* wsum, uint32_t* res) {
+  // thread t takes bin (kBins-1-t) so the inclusive prefix over threads is a suffix over bins
+  const int t = threadIdx.x;
+  const uint32_t c = t < kBins ? hist[kBins - 1 - t] : 0u;
+  uint32_t total;
+  const uint32_t incl = block_scan(c, wsum, total);
+  if (t < kBins && c > 0 && incl - c < k_rem && k_rem <= incl) {
+    res[0] = kBins - 1 - t;
+    res[1] = k_rem - (incl - c);
+    res[2] = c;
   }
   __syncthreads();
 }
 
 __device__ __forceinline__ int bit_length(uint32_t x) { return x ? 32 - __clz(x) : 0; }
 
-// Digit of key u for a pass binning [blo, bhi] with bin width 2^s: keys below / above the
-// binned range clamp into the first / last bin (the mapping stays monotone).
-__device__ __forceinline__ uint32_t range_digit(uint32_t u, uint32_t blo, uint32_t bhi, int s) {
-  if (u < blo) return 0u;
-  if (u > bhi) return kBins - 1;
-  return (u - blo) >> s;
-}
-
-__device__ __forceinline__ void block_minmax(uint32_t& mn, uint32_t& mx, uint32_t* sbuf) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  mn = __reduce_min_sync(0xffffffffu, mn);
-  mx = __reduce_max_sync(0xffffffffu, mx);
-  if (lane == 0) {
-    sbuf[warp] = mn;
-    sbuf[32 + warp] = mx;
-  }
-  __syncthreads();
-  mn = __reduce_min_sync(0xffffffffu, sbuf[lane]);
-  mx = __reduce_max_sync(0xffffffffu, sbuf[32 + lane]);
-  __syncthreads();
-}
-
 __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArgs a) {
   extern __shared__ __align__(16) uint32_t sm[];
-  __shared__ uint32_t wsum[64];
+  __shared__ uint32_t wsum[72];
   __shared__ uint32_t res[4];
-  __shared__ uint32_t wcnt[2][kWarps];
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t s_kth;
 
@@ -148,169 +100,121 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   const int start = seg * a.chunk;
   const int n = min(a.row_len - start, a.chunk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t* keys = sm;
-  // per-warp digit histograms; the same space holds the sort pairs after selection
-  uint32_t* whist = sm + ((a.chunk + 3) & ~3);
-  uint32_t* my_hist = whist + warp * kBins;
-  uint64_t* pairs = reinterpret_cast<uint64_t*>(whist);
+  uint32_t* my_hist = sm + warp * kBins;  // per-warp histograms (32 KiB) ...
+  uint64_t* pairs = reinterpret_cast<uint64_t*>(sm);  // ... later the sort buffer
 
   const float* vrow = a.vals + static_cast<int64_t>(row) * a.vals_stride + start;
   const int32_t* irow = a.idx ? a.idx + static_cast<int64_t>(row) * a.idx_stride + start : nullptr;
-  constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // float_to_key(-inf)
-  constexpr uint32_t kNanKey = 0xFFFFFFFFu;
+  const int e0 = tid * kPer;  // first element of this thread
+  const int cnt = max(0, min(kPer, n - e0));
 
-  // ---- load: keys to shared memory, min/max of the regular keys (not -inf, not NaN)
-  uint32_t rmin = 0xFFFFFFFFu, rmax = 0u, amin = 0xFFFFFFFFu, amax = 0u;
-  auto note = [&](uint32_t u) {
-    amin = min(amin, u);
-    amax = max(amax, u);
-    if (u != kNegInfKey && u != kNanKey) {
-      rmin = min(rmin, u);
-      rmax = max(rmax, u);
+  // ---- keys to registers; key 0 (below every real key) pads past the end
+  uint32_t key[kPer];
+  if (cnt == kPer && (reinterpret_cast<uintptr_t>(vrow + e0) & 15u) == 0u) {
+    const float4* v4 = reinterpret_cast<const float4*>(vrow + e0);
+#pragma unroll
+    for (int j = 0; j < kPer / 4; ++j) {
+      const float4 v = __ldg(v4 + j);
+      key[4 * j + 0] = float_to_key(v.x);
+      key[4 * j + 1] = float_to_key(v.y);
+      key[4 * j + 2] = float_to_key(v.z);
+      key[4 * j + 3] = float_to_key(v.w);
     }
-  };
-  int done = 0;
-  if ((reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u) {
-    const float4* v4 = reinterpret_cast<const float4*>(vrow);
-    uint4* k4 = reinterpret_cast<uint4*>(keys);
-    const int n4 = n >> 2;
-    for (int i = tid; i < n4; i += kThreads) {
-      const float4 v = __ldg(v4 + i);
-      const uint4 u = make_uint4(float_to_key(v.x), float_to_key(v.y), float_to_key(v.z),
-                                 float_to_key(v.w));
-      k4[i] = u;
-      note(u.x);
-      note(u.y);
-      note(u.z);
-      note(u.w);
-    }
-    done = n4 << 2;
+  } else {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) key[j] = j < cnt ? float_to_key(__ldg(vrow + e0 + j)) : 0u;
   }
-  for (int i = done + tid; i < n; i += kThreads) {
-    const uint32_t u = float_to_key(__ldg(vrow + i));
-    keys[i] = u;
-    note(u);
+  // live key range: min over real keys, max
+  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (j < cnt) {
+      kmin = min(kmin, key[j]);
+      kmax = max(kmax, key[j]);
+    }
+  }
+  kmin = __reduce_min_sync(0xffffffffu, kmin);
+  kmax = __reduce_max_sync(0xffffffffu, kmax);
+  if (lane == 0) {
+    wsum[warp] = kmin;
+    wsum[32 + warp] = kmax;
   }
   for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
-  block_minmax(rmin, rmax, wsum);
-  block_minmax(amin, amax, wsum);
-  if (rmin > rmax) {  // no regular key: bin over everything
-    rmin = amin;
-    rmax = amax;
-  }
+  __syncthreads();
+  kmin = __reduce_min_sync(0xffffffffu, wsum[lane]);
+  kmax = __reduce_max_sync(0xffffffffu, wsum[32 + lane]);
+  __syncthreads();
 
   // ---- range-narrowing radix select: the k-th key lies in [clo, chi]
   const int k = min(a.k, n);
   uint32_t k_rem = static_cast<uint32_t>(k);
-  uint32_t clo = 0u, chi = 0xFFFFFFFFu;
-  uint32_t blo = rmin, bhi = rmax;  // pass 1 bins the regular keys, clamping the rest
+  uint32_t clo = kmin, chi = kmax;
   bool whole = false;
-  for (int pass = 0; pass < 6 && !whole && clo != chi; ++pass) {
-    const int sh = max(0, bit_length(bhi - blo) - 8);
+  for (int pass = 0; pass < 5 && !whole && clo != chi; ++pass) {
+    const int sh = max(0, bit_length(chi - clo) - 8);
     if (pass > 0) {
       for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
+      __syncwarp();
     }
-    __syncwarp();
-    const uint4* k4 = reinterpret_cast<const uint4*>(keys);
-    const int n4 = n >> 2;
-    for (int i = tid; i < n4; i += kThreads) {
-      const uint4 u = k4[i];
-      const uint32_t e[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (e[j] >= clo && e[j] <= chi) atomicAdd(&my_hist[range_digit(e[j], blo, bhi, sh)], 1u);
+    for (int j = 0; j < kPer; ++j) {
+      const uint32_t u = key[j];
+      if (j < cnt && u >= clo && u <= chi) atomicAdd(&my_hist[(u - clo) >> sh], 1u);
     }
-    for (int i = (n4 << 2) + tid; i < n; i += kThreads) {
-      const uint32_t u = keys[i];
-      if (u >= clo && u <= chi) atomicAdd(&my_hist[range_digit(u, blo, bhi, sh)], 1u);
+    __syncthreads();
+    if (tid < kBins) {
+      uint32_t s = 0;
+#pragma unroll 8
+      for (int w = 0; w < kWarps; ++w) s += sm[w * kBins + tid];
+      hist[tid] = s;
     }
-    merge_warp_hists(whist, hist);
-    find_bin(hist, kBins, k_rem, wsum, res);
+    __syncthreads();
+    find_bin(hist, k_rem, wsum, res);
     const uint32_t d = res[0];
     k_rem = res[1];
     whole = (res[2] == k_rem);
-    // key range of bin d (64-bit: blo + 255 * 2^sh can pass 2^32)
-    const uint64_t step = 1ull << sh;
-    uint64_t lo64 = d == 0 ? clo : static_cast<uint64_t>(blo) + d * step;
-    uint64_t hi64 = d == kBins - 1 ? chi
-                                   : min(static_cast<uint64_t>(blo) + (d + 1) * step - 1,
-                                         static_cast<uint64_t>(bhi));
-    if (d == kBins - 1) lo64 = min(lo64, static_cast<uint64_t>(bhi) + 1);  // + clamped-high keys
+    const uint64_t lo64 = static_cast<uint64_t>(clo) + (static_cast<uint64_t>(d) << sh);
+    const uint64_t top = lo64 + (1ull << sh) - 1;
+    const uint64_t hi64 = top < chi ? top : static_cast<uint64_t>(chi);
     clo = static_cast<uint32_t>(lo64);
     chi = static_cast<uint32_t>(hi64);
-    blo = clo;
-    bhi = chi;
   }
-  __syncthreads();  // the histogram space becomes the pair buffer below
-  if (tid == 0) s_kth = 0xFFFFFFFFu;
   const uint32_t need_eq = k_rem;  // keys in [clo, chi] to take, lowest index first
-  // Ordered compaction.  Warp w scans positions [w*span, (w+1)*span) in 32-wide steps.
-  const int span = ((n + kWarps * 32 - 1) / (kWarps * 32)) * 32;
-  const int w0 = warp * span, w1 = min(n, w0 + span);
-  uint32_t cgt = 0, ceq = 0;
-  for (int base = w0; base < w1; base += 32) {
-    const int i = base + lane;
-    bool gt = false, eq = false;
-    if (i < w1) {
-      const uint32_t u = keys[i];
-      gt = u > chi;
-      eq = u >= clo && u <= chi;
-    }
-    cgt += __popc(__ballot_sync(0xffffffffu, gt));
-    ceq += __popc(__ballot_sync(0xffffffffu, eq));
-  }
-  if (lane == 0) {
-    wcnt[0][warp] = cgt;
-    wcnt[1][warp] = ceq;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    // exclusive prefix over warps
-    uint32_t g = wcnt[0][lane], e = wcnt[1][lane];
-    uint32_t gs = g, es = e;
+
+  // ---- ordered output: positions from two block scans over per-thread counts
+  uint32_t ngt = 0, neq = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t yg = __shfl_up_sync(0xffffffffu, gs, o);
-      const uint32_t ye = __shfl_up_sync(0xffffffffu, es, o);
-      if (lane >= o) {
-        gs += yg;
-        es += ye;
-      }
-    }
-    __syncwarp();
-    wcnt[0][lane] = gs - g;
-    wcnt[1][lane] = es - e;
+  for (int j = 0; j < kPer; ++j) {
+    const uint32_t u = key[j];
+    ngt += (j < cnt && u > chi) ? 1u : 0u;
+    neq += (j < cnt && u >= clo && u <= chi) ? 1u : 0u;
   }
-  __syncthreads();
+  uint32_t tot;
+  const uint32_t eq_before = block_scan(neq, wsum, tot) - neq;
+  const uint32_t eq_take = eq_before >= need_eq ? 0u : min(neq, need_eq - eq_before);
+  const uint32_t sel = ngt + eq_take;
+  const uint32_t sel_before = block_scan(sel, wsum, tot) - sel;
+  if (tid == 0) s_kth = 0xFFFFFFFFu;
+  __syncthreads();  // the histograms are dead from here on (pairs may reuse the space)
 
   const int64_t out_row = static_cast<int64_t>(row) * gridDim.x + seg;
-  uint32_t gbase = wcnt[0][warp], ebase = wcnt[1][warp];
-  const unsigned lt = lanemask_lt();
-  for (int base = w0; base < w1; base += 32) {
-    const int i = base + lane;
-    bool gt = false, eq = false;
-    uint32_t u = 0;
-    if (i < w1) {
-      u = keys[i];
-      gt = u > chi;
-      eq = u >= clo && u <= chi;
-    }
-    const unsigned bg = __ballot_sync(0xffffffffu, gt);
-    const unsigned be = __ballot_sync(0xffffffffu, eq);
-    const uint32_t g_before = gbase + __popc(bg & lt);
-    const uint32_t e_before = ebase + __popc(be & lt);
+  uint32_t pos = sel_before, eq_seen = 0, kth_local = 0xFFFFFFFFu;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const uint32_t u = key[j];
     bool take = false;
-    uint32_t pos = 0;
-    if (gt) {
-      take = true;
-      pos = g_before + min(e_before, need_eq);
-    } else if (eq && e_before < need_eq) {
-      take = true;
-      pos = g_before + e_before;
+    if (j < cnt) {
+      if (u > chi) {
+        take = true;
+      } else if (u >= clo) {
+        take = eq_seen < eq_take;
+        ++eq_seen;
+        if (take) kth_local = min(kth_local, u);
+      }
     }
     if (take) {
-      const uint32_t gi = irow ? static_cast<uint32_t>(irow[i]) : static_cast<uint32_t>(start + i);
-      if (eq) atomicMin(&s_kth, u);
+      const int e = e0 + j;
+      const uint32_t gi = irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(start + e);
       if (a.sorted) {
         pairs[pos] = (static_cast<uint64_t>(u) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - gi);
       } else if (a.out_idx) {
@@ -320,10 +224,10 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
           static_cast<int32_t*>(a.out_idx)[out_row * a.out_idx_stride + pos] = static_cast<int32_t>(gi);
         if (a.out_val) a.out_val[out_row * a.out_val_stride + pos] = key_to_float(u);
       }
+      ++pos;
     }
-    gbase += __popc(bg);
-    ebase += __popc(be);
   }
+  if (eq_take) atomicMin(&s_kth, kth_local);
   __syncthreads();
   if (tid == 0 && a.kth_out) a.kth_out[out_row] = key_to_float(s_kth);
   if (!a.sorted) return;
@@ -367,9 +271,10 @@ int kpow2(int k) {
 }
 
 size_t segment_smem(int chunk, int k, int sorted) {
+  (void)chunk;
   const size_t hists = static_cast<size_t>(kWarps) * kBins * 4;
   const size_t pairs = sorted ? static_cast<size_t>(kpow2(k)) * 8 : 0;
-  return static_cast<size_t>((chunk + 3) & ~3) * 4 + (hists > pairs ? hists : pairs);
+  return hists > pairs ? hists : pairs;
 }
 
 int launch_segments(const TopkArgs& a, int rows, int nseg, cudaStream_t stream) {
