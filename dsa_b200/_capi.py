@@ -46,6 +46,15 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_progressive_h8": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp,
                                   vp, vp, i64, vp, vp, i64, vp]),
     "tdsa_compact_blocks": (i32, [vp, i64, vp, i64, i32, i32, i32, vp, vp, i64, vp, vp]),
+    "tdsa_exact_state_bytes": (sz, [i32, i32, i32, i32]),
+    "tdsa_exact_init": (i32, [vp, sz, vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32, i32,
+                              i32, vp, i32, i64, vp, i64, vp]),
+    "tdsa_exact_step": (i32, [vp, sz, vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32, i32,
+                              i32, i32, vp, i32, i64, vp, i64, vp]),
+    "tdsa_exact_stats": (i32, [vp, sz, i32, i32, i32, i32, C.POINTER(C.c_uint64)]),
+    "tdsa_block_key_norms": (i32, [vp, i32, i32, i32, i32, vp, vp]),
+    "tdsa_temporal_radius": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]),
+    "tdsa_relu_index_score": (i32, [vp, vp, vp, i32, i32, i32, vp, vp]),
     "tdsa_query_prep": (i32, [vp, i64, vp, i64, i32, vp, vp, vp, i64, vp, i64, i32, i32, i32,
                               C.c_float, C.c_float, vp]),
 }

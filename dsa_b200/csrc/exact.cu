@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
   __shared__ uint32_t sbase[4];
   const int seq = blockIdx.x;
   const int nb = (a.length + a.bs - 1) / a.bs;
-  const int first_new = a.init ? 0 : a.prev_length / a.bs;
+  // blocks holding keys appended since the last step are never pruned (replay.py:263-266)
+  const int first_new = a.init ? 0 : (a.length > a.prev_length ? a.prev_length / a.bs : nb);
   const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
   int8_t* flag = a.flag + brow;
 

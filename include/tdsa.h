@@ -160,6 +160,58 @@ int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_
                         int32_t* out_count, void* stream);
 
 /*
+ * Exact (certified) progressive top-k over a growing key cache (the schedule of
+ * src/temporal_dsa/replay.py:172-222 with the bound of certified.py:18-48, which the
+ * reference only replays on precomputed scores).  The caller owns `state`
+ * (tdsa_exact_state_bytes bytes of device memory, any contents); tdsa_exact_init scores
+ * densely and fills it, each tdsa_exact_step then seeds from the previous top-k, scores the
+ * blocks holding those keys and the keys appended since the last call (prev_length ..
+ * length), and skips every other block whose certified bound is below the running k-th
+ * score.  The returned top-k equals dense scoring's.  16-bit keys; block_size 16/32/64/128;
+ * batch, max_length, k and block_size must match the state's.  Outputs as tdsa_topk
+ * (out_indices may be NULL).
+ */
+size_t tdsa_exact_state_bytes(int batch, int max_length, int k, int block_size);
+
+int tdsa_exact_init(void* state, size_t state_bytes, const void* queries,
+                    int64_t q_batch_stride, const float* weights, int64_t w_batch_stride,
+                    const void* keys, int64_t k_batch_stride, int64_t k_row_stride, int dtype,
+                    int batch, int length, int max_length, int k, int block_size, int sorted,
+                    void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                    float* out_values, int64_t val_batch_stride, void* stream);
+
+int tdsa_exact_step(void* state, size_t state_bytes, const void* queries,
+                    int64_t q_batch_stride, const float* weights, int64_t w_batch_stride,
+                    const void* keys, int64_t k_batch_stride, int64_t k_row_stride, int dtype,
+                    int batch, int prev_length, int length, int max_length, int k,
+                    int block_size, int sorted, void* out_indices, int index_bytes,
+                    int64_t idx_batch_stride, float* out_values, int64_t val_batch_stride,
+                    void* stream);
+
+/* Accumulated counters per sequence, 8 x uint64 each: steps, blocks visited, blocks scored,
+ * blocks pruned, keys scored, keys in the cache, first-wave blocks, second-wave blocks.
+ * Synchronous (device to host copy). */
+int tdsa_exact_stats(const void* state, size_t state_bytes, int batch, int max_length, int k,
+                     int block_size, uint64_t* stats_out);
+
+/*
+ * Float64 certified-bound helpers, generic in heads and dims (src/temporal_dsa/
+ * certified.py:6-61).  Device pointers to float64.
+ * tdsa_block_key_norms: keys [tokens][heads][dim] -> out [ceil(tokens/bs)][heads], the max
+ *   L2 norm per block and head (:51-61).
+ * tdsa_temporal_radius: out[b] = sum_h block_key_norm[b][h] * (|w_now-w_prev|_h ||q_prev,h||
+ *   + |w_now,h| ||q_now,h - q_prev,h||) (:18-48); coeff_workspace holds `heads` doubles.
+ * tdsa_relu_index_score: out[t] = sum_h w[h] ReLU(q[h] . keys[t]) (:6-15).
+ */
+int tdsa_block_key_norms(const double* keys, int tokens, int heads, int dim, int block_size,
+                         double* out, void* stream);
+int tdsa_temporal_radius(const double* q_now, const double* q_prev, const double* w_now,
+                         const double* w_prev, const double* block_key_norm, int heads, int dim,
+                         int blocks, double* coeff_workspace, double* out, void* stream);
+int tdsa_relu_index_score(const double* q, const double* keys, const double* w, int heads,
+                          int dim, int tokens, double* out, void* stream);
+
+/*
  * Decode-step tail of the sidecar query projection, one launch: RoPE on the first rope_dim
  * dims of every head of the W_q GEMM output, and the float32 head weights
  * w = weight_scale * hidden @ w_proj^T.
