@@ -4,7 +4,7 @@
 //                                                              autocast-disabled weights_proj)
 // qraw is the [B, 64*128] output of the W_q GEMM (cuBLAS, 16-bit).  Grid (B, 2): y = 0 CTAs
 // rotate one row of q, y = 1 CTAs compute one row of w (a float32 GEMV over the hidden
-// size; W_w streams from L2).  RoPE angles are position * theta^(-j/half) in float32 as in
+// size; W_w streams from L2 as independent float4 loads).  RoPE angles are position * theta^(-j/half) in float32 as in
 // the reference; the rotation is done in float32 and rounded once.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(kThreads)
                  const int64_t* __restrict__ positions, T* __restrict__ q, int64_t q_stride,
                  float* __restrict__ w, int64_t w_stride, int rope_dim, float theta,
                  float scale) {
-  extern __shared__ float xs[];  // [hidden] for the GEMV half
+  extern __shared__ float xs[];  // GEMV partials [16][64]
   __shared__ float cs[64], sn[64];
   const int b = blockIdx.x;
   if (blockIdx.y == 0) {
@@ -70,18 +70,47 @@ __global__ void __launch_bounds__(kThreads)
     }
     return;
   }
-  // w row b: stage x[b] in shared memory as float, 16 warps x 4 heads, warp-reduced dots
-  const T* xr = x + static_cast<int64_t>(b) * x_stride;
-  for (int i = threadIdx.x; i < hidden; i += kThreads) xs[i] = to_f(xr[i]);
-  __syncthreads();
+  // w row b: the hidden axis is split over the 16 warps (128 dims per warp per round, 4 per
+  // lane); every lane keeps 64 head partials, so each W_w load is an independent float4 and
+  // the loads of all heads are in flight together.  Fixed-order reductions: lanes, then warps.
+  float* red = xs;  // [16 warps][64 heads]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int h = warp; h < kHeads; h += kThreads / 32) {
-    const float* wr = ww + static_cast<int64_t>(h) * hidden;
-    float acc = 0.f;
-    for (int i = lane; i < hidden; i += 32) acc = fmaf(xs[i], __ldg(wr + i), acc);
+  const T* xr = x + static_cast<int64_t>(b) * x_stride;
+  float acc[kHeads];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) w[static_cast<int64_t>(b) * w_stride + h] = acc * scale;
+  for (int h = 0; h < kHeads; ++h) acc[h] = 0.f;
+  for (int k0 = warp * 128 + lane * 4; k0 < hidden; k0 += (kThreads / 32) * 128) {
+    float xv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xv[j] = k0 + j < hidden ? to_f(xr[k0 + j]) : 0.f;
+    const bool full4 = k0 + 4 <= hidden && (hidden & 3) == 0;
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) {
+      const float* wr = ww + static_cast<int64_t>(h) * hidden + k0;
+      float4 v;
+      if (full4) {
+        v = __ldg(reinterpret_cast<const float4*>(wr));
+      } else {
+        v.x = k0 + 0 < hidden ? __ldg(wr + 0) : 0.f;
+        v.y = k0 + 1 < hidden ? __ldg(wr + 1) : 0.f;
+        v.z = k0 + 2 < hidden ? __ldg(wr + 2) : 0.f;
+        v.w = k0 + 3 < hidden ? __ldg(wr + 3) : 0.f;
+      }
+      acc[h] = fmaf(xv[0], v.x, fmaf(xv[1], v.y, fmaf(xv[2], v.z, fmaf(xv[3], v.w, acc[h]))));
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) {
+    float v = acc[h];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp * kHeads + h] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < kHeads) {
+    float s = 0.f;
+    for (int wi = 0; wi < kThreads / 32; ++wi) s += red[wi * kHeads + threadIdx.x];
+    w[static_cast<int64_t>(b) * w_stride + threadIdx.x] = s * scale;
   }
 }
 
@@ -92,7 +121,7 @@ int launch_qprep(const void* qraw, int64_t qraw_stride, const void* x, int64_t x
                  int64_t q_stride, float* w, int64_t w_stride, int dtype, int batch,
                  int rope_dim, float theta, float scale, cudaStream_t stream) {
   const dim3 grid(batch, 2);
-  const size_t smem = static_cast<size_t>(hidden) * 4;
+  const size_t smem = static_cast<size_t>(kThreads / 32) * kHeads * 4;
   if (dtype == TDSA_BF16) {
     auto kern = qprep_kernel<__nv_bfloat16>;
     TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
