@@ -247,7 +247,8 @@ int tdsa_merge_topk(const float* cand_values, const int32_t* cand_indices,
 size_t tdsa_score_topk_workspace_bytes(int batch, int length, int k) {
   if (batch < 1 || length < 1 || k < 1 || k > length) return 0;
   const size_t scores = (static_cast<size_t>(batch) * length * 4 + 255) & ~size_t(255);
-  return scores + topk_workspace_bytes(batch, length, k);
+  const size_t hist = static_cast<size_t>(batch) * kKeyHistBins * 4;
+  return scores + hist + topk_workspace_bytes(batch, length, k);
 }
 
 int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* weights,
@@ -265,15 +266,71 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
   const size_t need = tdsa_score_topk_workspace_bytes(batch, length, k);
   if (!workspace || workspace_bytes < need)
     return fail(TDSA_ERR_WORKSPACE, "score_topk workspace missing or too small");
-  float* scores = static_cast<float*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* scores = reinterpret_cast<float*>(ws);
   const size_t score_bytes = (static_cast<size_t>(batch) * length * 4 + 255) & ~size_t(255);
-  rc = tdsa_score_dense(queries, q_batch_stride, weights, w_batch_stride, keys, k_batch_stride,
-                        k_row_stride, dtype, batch, length, scores, length, stream);
+  const size_t hist_bytes = static_cast<size_t>(batch) * kKeyHistBins * 4;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(ws + score_bytes);
+  // the score kernel's key histogram lets the top-k skip its first pass (16-bit keys, rows
+  // that fit one top-k segment)
+  const bool use_hist = dtype != TDSA_F32 && length <= kTopkSegment;
+  if (use_hist) {
+    TDSA_CUDA_CHECK(cudaMemsetAsync(hist, 0, hist_bytes, st));
+    rc = check_score_args(queries, q_batch_stride, weights, w_batch_stride, keys,
+                          k_batch_stride, k_row_stride, dtype, batch, length, scores, length);
+    if (rc) return rc;
+    int* status = device_status_ptr();
+    if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+    rc = launch_score_dense_tc(queries, q_batch_stride, weights, w_batch_stride, keys,
+                               k_batch_stride, k_row_stride, dtype, batch, length, scores,
+                               length, st, status, hist);
+  } else {
+    rc = tdsa_score_dense(queries, q_batch_stride, weights, w_batch_stride, keys,
+                          k_batch_stride, k_row_stride, dtype, batch, length, scores, length,
+                          stream);
+  }
   if (rc) return rc;
   return launch_topk(scores, length, nullptr, 0, batch, length, k, sorted ? 1 : 0, out_indices,
                      index_bytes, idx_batch_stride, out_values, val_batch_stride,
-                     static_cast<uint8_t*>(workspace) + score_bytes, workspace_bytes - score_bytes,
-                     static_cast<cudaStream_t>(stream));
+                     ws + score_bytes + hist_bytes, workspace_bytes - score_bytes - hist_bytes,
+                     st, nullptr, use_hist ? hist : nullptr);
+}
+
+int tdsa_score_dense_hist(const void* queries, int64_t q_batch_stride, const float* weights,
+                          int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                          int64_t k_row_stride, int dtype, int batch, int length, float* scores,
+                          int64_t s_batch_stride, uint32_t* key_hist, void* stream) {
+  int rc = check_score_args(queries, q_batch_stride, weights, w_batch_stride, keys,
+                            k_batch_stride, k_row_stride, dtype, batch, length, scores,
+                            s_batch_stride);
+  if (rc || length == 0) return rc;
+  if (dtype == TDSA_F32) return fail(TDSA_ERR_UNSUPPORTED, "key histograms need 16-bit keys");
+  if (!key_hist) return fail(TDSA_ERR_INVALID, "key_hist is null");
+  int* status = device_status_ptr();
+  if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  return launch_score_dense_tc(queries, q_batch_stride, weights, w_batch_stride, keys,
+                               k_batch_stride, k_row_stride, dtype, batch, length, scores,
+                               s_batch_stride, static_cast<cudaStream_t>(stream), status,
+                               key_hist);
+}
+
+int tdsa_topk_hist(const float* scores, int64_t s_batch_stride, int batch, int length, int k,
+                   int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                   float* out_values, int64_t val_batch_stride, uint32_t* key_hist,
+                   void* stream) {
+  if (!scores || !key_hist) return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
+  if (batch > 1 && s_batch_stride < length)
+    return fail(TDSA_ERR_INVALID, "score row stride must be >= length");
+  if (length > kTopkSegment)
+    return fail(TDSA_ERR_UNSUPPORTED, "tdsa_topk_hist takes rows of at most 32768 keys");
+  int rc = check_topk_out(out_indices, index_bytes, idx_batch_stride, out_values,
+                          val_batch_stride, batch, k);
+  if (rc) return rc;
+  return launch_topk(scores, s_batch_stride, nullptr, 0, batch, length, k, sorted ? 1 : 0,
+                     out_indices, index_bytes, idx_batch_stride, out_values, val_batch_stride,
+                     nullptr, 0, static_cast<cudaStream_t>(stream), nullptr, key_hist);
 }
 
 int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,

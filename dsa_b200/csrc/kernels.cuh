@@ -10,11 +10,12 @@ namespace tdsa {
 
 constexpr int kTopkSegment = 32768;    // keys one top-k CTA holds in shared memory
 constexpr int kTopkMaxSorted = 8192;   // largest k sorted in shared memory
+constexpr int kKeyHistBins = 4096;     // score-kernel key histogram: top 12 bits of the key
 
 int launch_score_dense_tc(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
                           const void* k, int64_t k_bs, int64_t k_rs, int dtype, int batch,
                           int length, float* out, int64_t o_bs, cudaStream_t stream,
-                          int* status);
+                          int* status, uint32_t* hist = nullptr);
 
 int launch_score_dense_f32(const float* q, int64_t q_bs, const float* w, int64_t w_bs,
                            const float* k, int64_t k_bs, int64_t k_rs, int batch, int length,
@@ -88,7 +89,7 @@ int topk_check(int length, int k, int sorted);
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,
                 int batch, int length, int k, int sorted, void* out_idx, int idx_bytes,
                 int64_t oi_stride, float* out_val, int64_t ov_stride, void* ws, size_t ws_bytes,
-                cudaStream_t stream, float* kth_out = nullptr);
+                cudaStream_t stream, float* kth_out = nullptr, uint32_t* key_hist = nullptr);
 
 int launch_qprep(const void* qraw, int64_t qraw_stride, const void* x, int64_t x_stride,
                  int hidden, const float* ww, const int64_t* positions, void* q,

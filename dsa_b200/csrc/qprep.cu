@@ -1,11 +1,13 @@
 // Decode-step tail of the sidecar query projection (reference sidecar.py:78-87), one launch:
 //   q[b,h,:] = RoPE_noninterleaved(qraw[b, h*128 : h*128+128]) on the first rope_dim dims
-//   w[b,h]   = scale * sum_k float(x[b,k]) * W_w[h,k]        (float32, as the reference's
-//                                                              autocast-disabled weights_proj)
-// qraw is the [B, 64*128] output of the W_q GEMM (cuBLAS, 16-bit).  Grid (B, 2): y = 0 CTAs
-// rotate one row of q, y = 1 CTAs compute one row of w (a float32 GEMV over the hidden
-// size; W_w streams from L2 as independent float4 loads).  RoPE angles are position * theta^(-j/half) in float32 as in
-// the reference; the rotation is done in float32 and rounded once.
+//   w[b,h]   = scale * sum_k float(x[b,k]) * W_w[h,k]     (float32, as the reference's
+//                                                           autocast-disabled weights_proj)
+// qraw is the [B, 64*128] output of the W_q GEMM (cuBLAS, 16-bit).
+// CTAs [0, B) rotate one row of q each.  The other CTAs tile w by (head, group of 16 batch
+// rows): the head's W_w row is read once into registers (8 dims per thread), each batch
+// row's hidden state is one 16-byte load per thread, and every dot product reduces in a
+// fixed order (lanes, then warps).  RoPE angles are position * theta^(-j/half) in float32
+// as in the reference; the rotation is done in float32 and rounded once.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -13,7 +15,8 @@ namespace tdsa {
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 256;
+constexpr int kRows = 16;  // batch rows per GEMV CTA
 
 template <typename T>
 __device__ __forceinline__ float to_f(T x);
@@ -41,12 +44,12 @@ __global__ void __launch_bounds__(kThreads)
     qprep_kernel(const T* __restrict__ qraw, int64_t qraw_stride, const T* __restrict__ x,
                  int64_t x_stride, int hidden, const float* __restrict__ ww,
                  const int64_t* __restrict__ positions, T* __restrict__ q, int64_t q_stride,
-                 float* __restrict__ w, int64_t w_stride, int rope_dim, float theta,
+                 float* __restrict__ w, int64_t w_stride, int batch, int rope_dim, float theta,
                  float scale) {
-  extern __shared__ float xs[];  // GEMV partials [16][64]
   __shared__ float cs[64], sn[64];
-  const int b = blockIdx.x;
-  if (blockIdx.y == 0) {
+  __shared__ float red[kThreads / 32][kRows];
+  if (static_cast<int>(blockIdx.x) < batch) {
+    const int b = blockIdx.x;
     const int half = rope_dim >> 1;
     if (threadIdx.x < half) {
       const float inv_freq =
@@ -70,47 +73,61 @@ __global__ void __launch_bounds__(kThreads)
     }
     return;
   }
-  // w row b: the hidden axis is split over the 16 warps (128 dims per warp per round, 4 per
-  // lane); every lane keeps 64 head partials, so each W_w load is an independent float4 and
-  // the loads of all heads are in flight together.  Fixed-order reductions: lanes, then warps.
-  float* red = xs;  // [16 warps][64 heads]
+  // GEMV tile: head h, batch rows [b0, b0 + kRows)
+  const int tile = blockIdx.x - batch;
+  const int h = tile % kHeads;
+  const int b0 = (tile / kHeads) * kRows;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const T* xr = x + static_cast<int64_t>(b) * x_stride;
-  float acc[kHeads];
+  float part[kRows];
 #pragma unroll
-  for (int h = 0; h < kHeads; ++h) acc[h] = 0.f;
-  for (int k0 = warp * 128 + lane * 4; k0 < hidden; k0 += (kThreads / 32) * 128) {
-    float xv[4];
+  for (int r = 0; r < kRows; ++r) part[r] = 0.f;
+  for (int k0 = threadIdx.x * 8; k0 < hidden; k0 += kThreads * 8) {
+    float wv[8];
+    const float* wr = ww + static_cast<int64_t>(h) * hidden + k0;
+    const bool full = k0 + 8 <= hidden;
+    if (full && (reinterpret_cast<uintptr_t>(wr) & 15u) == 0u) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(wr));
+      const float4 c = __ldg(reinterpret_cast<const float4*>(wr) + 1);
+      wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+      wv[4] = c.x; wv[5] = c.y; wv[6] = c.z; wv[7] = c.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) xv[j] = k0 + j < hidden ? to_f(xr[k0 + j]) : 0.f;
-    const bool full4 = k0 + 4 <= hidden && (hidden & 3) == 0;
+      for (int j = 0; j < 8; ++j) wv[j] = k0 + j < hidden ? __ldg(wr + j) : 0.f;
+    }
 #pragma unroll
-    for (int h = 0; h < kHeads; ++h) {
-      const float* wr = ww + static_cast<int64_t>(h) * hidden + k0;
-      float4 v;
-      if (full4) {
-        v = __ldg(reinterpret_cast<const float4*>(wr));
-      } else {
-        v.x = k0 + 0 < hidden ? __ldg(wr + 0) : 0.f;
-        v.y = k0 + 1 < hidden ? __ldg(wr + 1) : 0.f;
-        v.z = k0 + 2 < hidden ? __ldg(wr + 2) : 0.f;
-        v.w = k0 + 3 < hidden ? __ldg(wr + 3) : 0.f;
+    for (int r = 0; r < kRows; ++r) {
+      if (b0 + r < batch) {
+        const T* xr = x + static_cast<int64_t>(b0 + r) * x_stride + k0;
+        float xv[8];
+        if (full && (reinterpret_cast<uintptr_t>(xr) & 15u) == 0u) {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr));
+          const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[j] = to_f(e[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[j] = k0 + j < hidden ? to_f(xr[j]) : 0.f;
+        }
+        float acc = part[r];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(xv[j], wv[j], acc);
+        part[r] = acc;
       }
-      acc[h] = fmaf(xv[0], v.x, fmaf(xv[1], v.y, fmaf(xv[2], v.z, fmaf(xv[3], v.w, acc[h]))));
     }
   }
 #pragma unroll
-  for (int h = 0; h < kHeads; ++h) {
-    float v = acc[h];
+  for (int r = 0; r < kRows; ++r) {
+    float v = part[r];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[warp * kHeads + h] = v;
+    if (lane == 0) red[warp][r] = v;
   }
   __syncthreads();
-  if (threadIdx.x < kHeads) {
+  if (threadIdx.x < kRows && b0 + static_cast<int>(threadIdx.x) < batch) {
     float s = 0.f;
-    for (int wi = 0; wi < kThreads / 32; ++wi) s += red[wi * kHeads + threadIdx.x];
-    w[static_cast<int64_t>(b) * w_stride + threadIdx.x] = s * scale;
+#pragma unroll
+    for (int wi = 0; wi < kThreads / 32; ++wi) s += red[wi][threadIdx.x];
+    w[static_cast<int64_t>(b0 + threadIdx.x) * w_stride + h] = s * scale;
   }
 }
 
@@ -120,25 +137,18 @@ int launch_qprep(const void* qraw, int64_t qraw_stride, const void* x, int64_t x
                  int hidden, const float* ww, const int64_t* positions, void* q,
                  int64_t q_stride, float* w, int64_t w_stride, int dtype, int batch,
                  int rope_dim, float theta, float scale, cudaStream_t stream) {
-  const dim3 grid(batch, 2);
-  const size_t smem = static_cast<size_t>(kThreads / 32) * kHeads * 4;
-  if (dtype == TDSA_BF16) {
-    auto kern = qprep_kernel<__nv_bfloat16>;
-    TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-    kern<<<grid, kThreads, smem, stream>>>(
+  const int gemv_ctas = kHeads * ((batch + kRows - 1) / kRows);
+  const dim3 grid(batch + gemv_ctas);
+  if (dtype == TDSA_BF16)
+    qprep_kernel<__nv_bfloat16><<<grid, kThreads, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(qraw), qraw_stride,
         static_cast<const __nv_bfloat16*>(x), x_stride, hidden, ww, positions,
-        static_cast<__nv_bfloat16*>(q), q_stride, w, w_stride, rope_dim, theta, scale);
-  } else {
-    auto kern = qprep_kernel<__half>;
-    TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-    kern<<<grid, kThreads, smem, stream>>>(
+        static_cast<__nv_bfloat16*>(q), q_stride, w, w_stride, batch, rope_dim, theta, scale);
+  else
+    qprep_kernel<__half><<<grid, kThreads, 0, stream>>>(
         static_cast<const __half*>(qraw), qraw_stride, static_cast<const __half*>(x), x_stride,
-        hidden, ww, positions, static_cast<__half*>(q), q_stride, w, w_stride, rope_dim, theta,
-        scale);
-  }
+        hidden, ww, positions, static_cast<__half*>(q), q_stride, w, w_stride, batch, rope_dim,
+        theta, scale);
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }

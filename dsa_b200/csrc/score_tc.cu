@@ -33,6 +33,8 @@ constexpr int kTmemCols = 128;
 constexpr int kThreads = 192;
 constexpr int kBarrierBytes = 1024;
 constexpr int kSmemBytes = kStages * kStageBytes + 2 * kQBytes + kBarrierBytes + 1024;
+constexpr int kHistBins = 4096;  // key histogram bins (top 12 bits of the order-preserving key)
+constexpr int kHistBytes = kHistBins * 4;
 
 struct DenseArgs {
   const float* w;
@@ -42,6 +44,7 @@ struct DenseArgs {
   int length;
   int tiles_per_seq;
   int64_t total_tiles;
+  uint32_t* hist;  // [batch][4096] key histogram (kHist kernels): counts are added
   int* status;
 };
 
@@ -49,7 +52,10 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-template <bool kBF16>
+// kHist: the epilogue also counts every score's order-preserving key by its top 12 bits in a
+// shared-memory histogram, flushed to a.hist[sequence] whenever the CTA moves to the next
+// sequence (the top-k then starts from the bin holding the k-th key instead of a full pass).
+template <bool kBF16, bool kHist>
 __global__ void __launch_bounds__(kThreads, 1)
     score_dense_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap qmap, const DenseArgs a) {
@@ -64,8 +70,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accfull = qempty + 2;
   uint64_t* accempty = accfull + kAccBufs;
   uint64_t* done = accempty + kAccBufs;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* hbar = done + 1;  // epilogue-warp handshake around histogram flushes
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint32_t* shist = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -87,9 +95,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&accempty[s], 4);
     }
     mbar_init(done, 1);
+    mbar_init(hbar, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (kHist)
+    for (int i = threadIdx.x; i < kHistBins; i += kThreads) shist[i] = 0u;
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&kmap);
     prefetch_tmap(&qmap);
@@ -184,13 +195,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // -------------------------------------------------------------- epilogue
     const uint32_t quad = static_cast<uint32_t>(warp & 3);
+    const int etid = (warp - 2) * 32 + lane;  // 0..127 over the epilogue warps
     int prev_b = -1;
-    uint32_t acc_it = 0;
+    uint32_t acc_it = 0, hph = 0;
     float wr[kHeads];
+    // all four epilogue warps meet (bounded wait); false when the CTA aborts
+    auto hist_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(hbar);
+      const bool ok = mbar_wait(hbar, hph & 1u, abort_flag);
+      ++hph;
+      return ok;
+    };
+    auto hist_flush = [&](int seq) -> bool {
+      if (!hist_sync()) return false;
+      uint32_t* dst = a.hist + static_cast<int64_t>(seq) * kHistBins;
+      for (int i = etid; i < kHistBins; i += 128) {
+        const uint32_t c = shist[i];
+        if (c) {
+          atomicAdd(dst + i, c);
+          shist[i] = 0u;
+        }
+      }
+      return hist_sync();
+    };
     for (int64_t t = t0; t < t1; ++t) {
       const int b = static_cast<int>(t / tps);
       const int tt = static_cast<int>(t - static_cast<int64_t>(b) * tps);
       if (b != prev_b) {
+        if (kHist && prev_b >= 0 && !hist_flush(prev_b)) break;
         load_head_weights(a.w + static_cast<int64_t>(b) * a.w_stride, wr);
         prev_b = b;
       }
@@ -207,8 +240,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&accempty[acc]);
       const float score = relu_weighted_sum(r0, r1, wr);
       const int row = tt * kTileKeys + static_cast<int>(quad) * 32 + lane;
-      if (row < a.length) a.out[static_cast<int64_t>(b) * a.out_stride + row] = score;
+      if (row < a.length) {
+        a.out[static_cast<int64_t>(b) * a.out_stride + row] = score;
+        if (kHist) atomicAdd(&shist[float_to_key(score) >> 20], 1u);
+      }
       ++acc_it;
+      if (kHist && t + 1 == t1) hist_flush(b);
     }
   }
 
@@ -224,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <bool kBF16>
 int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs, const void* k,
                       int64_t k_bs, int64_t k_rs, int batch, int length, float* out,
-                      int64_t o_bs, cudaStream_t stream, int* status) {
+                      int64_t o_bs, cudaStream_t stream, int* status, uint32_t* hist) {
   const CUtensorMapDataType dt =
       kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap kmap, qmap;
@@ -257,13 +294,14 @@ int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
   a.tiles_per_seq = (length + kTileKeys - 1) / kTileKeys;
   a.total_tiles = static_cast<int64_t>(a.tiles_per_seq) * batch;
   a.status = status;
+  a.hist = hist;
   const int dev = current_device();
   const int sms = device_sm_count(dev);
   const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
-  auto kern = score_dense_tc_kernel<kBF16>;
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kSmemBytes));
-  kern<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(kmap, qmap, a);
+  const int smem = kSmemBytes + (hist ? kHistBytes : 0);
+  auto kern = hist ? score_dense_tc_kernel<kBF16, true> : score_dense_tc_kernel<kBF16, false>;
+  TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  kern<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(kmap, qmap, a);
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }
@@ -273,12 +311,12 @@ int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
 int launch_score_dense_tc(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
                           const void* k, int64_t k_bs, int64_t k_rs, int dtype, int batch,
                           int length, float* out, int64_t o_bs, cudaStream_t stream,
-                          int* status) {
+                          int* status, uint32_t* hist) {
   if (dtype == TDSA_BF16)
     return launch_dense_tc_t<true>(q, q_bs, w, w_bs, k, k_bs, k_rs, batch, length, out, o_bs,
-                                   stream, status);
+                                   stream, status, hist);
   return launch_dense_tc_t<false>(q, q_bs, w, w_bs, k, k_bs, k_rs, batch, length, out, o_bs,
-                                  stream, status);
+                                  stream, status, hist);
 }
 
 }  // namespace tdsa

@@ -1,20 +1,33 @@
-// Exact row-wise top-k by radix select, keys held in registers (no global sort).
+// Exact row-wise top-k by radix select over a shared-memory copy of the row (no global
+// sort).
 //
-// One 1024-thread CTA owns one segment of a row (<= 32768 elements).  Thread t holds the
-// 32 consecutive elements [32t, 32t+32) as order-preserving uint32 keys in registers.
-// Range-narrowing radix passes (256 bins over the live key range, one private histogram
-// per warp in shared memory) pin the k-th key T; every key > T is taken and keys == T are
-// taken lowest index first, which is the tie rule of the reference's stable_topk
-// (metrics.py:9-22).  Because each thread owns a contiguous run, two block-wide scans give
-// every taken key its output position in ascending index order; sorted output is a bitonic
-// sort of the k taken (key, index) pairs in shared memory.
+// One 1024-thread CTA owns one segment of a row (<= 32768 elements).  The segment is copied
+// into shared memory with one bulk copy and turned in place into order-preserving uint32
+// keys.  Warp w owns elements [w*P, (w+1)*P) (P = keys per warp); slot j of lane l is
+// element w*P + 32j + l, so every pass reads shared memory without bank conflicts and
+// (warp, slot, lane) order is index order.
+//   1. Live range [clo, chi] holding the k-th key: from the score kernel's 12-bit key
+//      histogram when one is given, else the segment's min/max.
+//   2. Range-narrowing radix passes (256 bins, eight private histograms) only until the
+//      keys >= clo fit the candidate list (8192 entries), or the range is one value.
+//   3. One ordered compaction: every key > chi, and the keys in [clo, chi] (all of them
+//      when they fit; otherwise the range is one value and the first ones by index that
+//      complete k), go to the candidate list in index order (warp ballots + one scan over
+//      the 32 warp totals).
+//   4. The list is narrowed to the exact k-th key T; keys > T and the lowest-index keys
+//      == T are taken -- the tie rule of the reference's stable_topk (metrics.py:9-22).
+//      Unsorted output is in ascending index order; sorted output is a bitonic sort of the
+//      k taken (key, index) pairs in shared memory.
 //
 // Rows longer than one segment run in levels: every segment emits its local top-k in index
 // order, and the candidates (the global top-k is a subset of their union) are selected
 // again with explicit indices until one segment remains.  The same explicit-index pass
 // merges per-GPU candidates of an L-sharded cache.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace tdsa {
 
@@ -22,8 +35,8 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-constexpr int kPer = kTopkSegment / kThreads;  // 32 keys per thread
 constexpr int kBins = 256;
+constexpr int kCap = 8192;  // candidate-list entries (keys >= the live range's low end)
 
 struct TopkArgs {
   const float* vals;      // [rows][row_stride]
@@ -40,194 +53,406 @@ struct TopkArgs {
   float* out_val;         // may be null
   int64_t out_val_stride;
   float* kth_out;         // per output row: the k-th largest value (may be null)
+  uint32_t* hist;         // per row [4096] key histogram from the score kernel (single
+                          // segment rows only; consumed and re-zeroed), or null
+  int row_words;          // shared-memory words of the segment copy (reused for sort pairs)
+  int cap;                // candidate-list entries
+  int* status;            // device status word (bounded-wait timeouts)
 };
 
-// Inclusive block-wide prefix sum of v (thread order), with the block total.
-__device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t* wsum, uint32_t& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__device__ __forceinline__ unsigned lanemask_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+__device__ __forceinline__ int bit_length(uint32_t x) { return x ? 32 - __clz(x) : 0; }
+
+// Exclusive prefix over the 32 warps of per-warp values (run by warp 0), into out[32].
+__device__ __forceinline__ void warp_totals_scan(const uint32_t* in, uint32_t* out) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t v = in[lane];
   uint32_t x = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
     if (lane >= o) x += y;
   }
-  if (lane == 31) wsum[warp] = x;
+  out[lane] = x - v;
+}
+
+// Pick the bin of the k_rem-th key from the top out of the eight private histograms and
+// narrow [clo, chi] to it (bin width 2^sh).  Returns with all threads agreeing.
+__device__ __forceinline__ void narrow_to_bin(const uint32_t* hists, uint32_t* hist,
+                                              uint32_t* res, int sh, uint32_t& clo,
+                                              uint32_t& chi, uint32_t& k_rem,
+                                              uint32_t& in_range) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < kBins) {
+    uint32_t s = 0;
+#pragma unroll
+    for (int h = 0; h < 8; ++h) s += hists[h * kBins + tid];
+    hist[tid] = s;
+  }
   __syncthreads();
   if (warp == 0) {
-    const uint32_t t = wsum[lane];
-    uint32_t s = t;
+    // bins from the top: lane l owns bins 255-8l .. 248-8l; suffix sums via a lane scan
+    uint32_t c[8], tot = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      c[i] = hist[kBins - 1 - (lane * 8 + i)];
+      tot += c[i];
+    }
+    uint32_t x = tot;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += y;
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
     }
-    wsum[32 + lane] = s - t;  // exclusive prefix over warps
-    if (lane == 31) wsum[64] = s;
+    uint32_t above = x - tot;
+    if (above < k_rem && k_rem <= x) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (above < k_rem && k_rem <= above + c[i]) {
+          res[0] = kBins - 1 - (lane * 8 + i);
+          res[1] = k_rem - above;
+          res[2] = c[i];
+        }
+        above += c[i];
+      }
+    }
   }
   __syncthreads();
-  const uint32_t r = x + wsum[32 + warp];
-  total = wsum[64];
-  __syncthreads();
-  return r;
+  const uint32_t d = res[0];
+  k_rem = res[1];
+  in_range = res[2];
+  const uint64_t lo64 = static_cast<uint64_t>(clo) + (static_cast<uint64_t>(d) << sh);
+  const uint64_t top = lo64 + (1ull << sh) - 1;
+  const uint64_t hi64 = top < chi ? top : static_cast<uint64_t>(chi);
+  clo = static_cast<uint32_t>(lo64);
+  chi = static_cast<uint32_t>(hi64);
 }
 
-// The bin (of kBins) holding the k_rem-th largest counted key: res = {bin, k_rem within the
-// bin, count of the bin}.  Threads 0..255 each own one bin; suffix sums via a reversed scan.
-__device__ void find_bin(const uint32_t* hist, uint32_t k_rem, uint32_t* wsum, uint32_t* res) {
-  // thread t takes bin (kBins-1-t) so the inclusive prefix over threads is a suffix over bins
-  const int t = threadIdx.x;
-  const uint32_t c = t < kBins ? hist[kBins - 1 - t] : 0u;
-  uint32_t total;
-  const uint32_t incl = block_scan(c, wsum, total);
-  if (t < kBins && c > 0 && incl - c < k_rem && k_rem <= incl) {
-    res[0] = kBins - 1 - t;
-    res[1] = k_rem - (incl - c);
-    res[2] = c;
-  }
-  __syncthreads();
-}
-
-__device__ __forceinline__ int bit_length(uint32_t x) { return x ? 32 - __clz(x) : 0; }
-
+// kPer keys per thread: segments of up to kPer * 1024 keys.
+template <int kPer>
 __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArgs a) {
   extern __shared__ __align__(16) uint32_t sm[];
-  __shared__ uint32_t wsum[72];
+  __shared__ uint32_t wa[kWarps], wb[kWarps], wc[kWarps];
   __shared__ uint32_t res[4];
   __shared__ uint32_t hist[kBins];
-  __shared__ uint32_t s_kth;
+  __shared__ uint32_t s_kth, s_total;
+  __shared__ __align__(8) uint64_t s_bar;
+  __shared__ int s_abort;
 
   const int row = blockIdx.y, seg = blockIdx.x;
   const int start = seg * a.chunk;
   const int n = min(a.row_len - start, a.chunk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t* my_hist = sm + warp * kBins;  // per-warp histograms (32 KiB) ...
-  uint64_t* pairs = reinterpret_cast<uint64_t*>(sm);  // ... later the sort buffer
+  const unsigned lt = lanemask_lt();
+  constexpr int kHists = 8;  // private histograms, one per 4 warps
+  // shared memory: [segment keys | sort pairs][list keys][list indices][8 histograms]
+  uint32_t* keys = sm;
+  uint32_t* list_key = sm + a.row_words;
+  uint32_t* list_idx = list_key + a.cap;
+  uint32_t* hists = list_idx + a.cap;
+  uint32_t* my_hist = hists + (warp & (kHists - 1)) * kBins;
+  uint64_t* pairs = reinterpret_cast<uint64_t*>(sm);  // the segment copy is dead by then
 
   const float* vrow = a.vals + static_cast<int64_t>(row) * a.vals_stride + start;
   const int32_t* irow = a.idx ? a.idx + static_cast<int64_t>(row) * a.idx_stride + start : nullptr;
-  const int e0 = tid * kPer;  // first element of this thread
-  const int cnt = max(0, min(kPer, n - e0));
+  const int wbase = warp * (kPer * 32) + lane;
 
-  // ---- keys to registers; key 0 (below every real key) pads past the end
-  uint32_t key[kPer];
-  if (cnt == kPer && (reinterpret_cast<uintptr_t>(vrow + e0) & 15u) == 0u) {
-    const float4* v4 = reinterpret_cast<const float4*>(vrow + e0);
-#pragma unroll
-    for (int j = 0; j < kPer / 4; ++j) {
-      const float4 v = __ldg(v4 + j);
-      key[4 * j + 0] = float_to_key(v.x);
-      key[4 * j + 1] = float_to_key(v.y);
-      key[4 * j + 2] = float_to_key(v.z);
-      key[4 * j + 3] = float_to_key(v.w);
+  // ---- 0. the segment into shared memory (one bulk copy on the TMA engine when the row
+  // is 16-byte aligned), then to keys in place; each thread converts the elements it
+  // reads in every later segment pass, so no barrier is needed before those passes.
+  const bool bulk = ((reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u) && (n % 4 == 0);
+  if (bulk) {
+    if (tid == 0) {
+      s_abort = 0;
+      mbar_init(&s_bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(n) * 4u;
+      mbar_arrive_expect_tx(&s_bar, bytes);
+      for (uint32_t off = 0; off < bytes; off += 32768u)
+        bulk_load(reinterpret_cast<uint8_t*>(keys) + off,
+                  reinterpret_cast<const uint8_t*>(vrow) + off, min(32768u, bytes - off), &s_bar);
+    }
+    if (!mbar_wait(&s_bar, 0, &s_abort)) {
+      // the copy did not land in time: report, and let the in-flight copy finish
+      if (tid == 0) atomicOr(a.status, TDSA_ERR_TIMEOUT);
+      volatile int no_abort = 0;
+      mbar_wait(&s_bar, 0, &no_abort);
+      return;
+    }
+#pragma unroll 8
+    for (int j = 0; j < kPer; ++j) {
+      const int e = wbase + j * 32;
+      if (e < n) keys[e] = float_to_key(__uint_as_float(keys[e]));
     }
   } else {
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) key[j] = j < cnt ? float_to_key(__ldg(vrow + e0 + j)) : 0u;
-  }
-  // live key range: min over real keys, max
-  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    if (j < cnt) {
-      kmin = min(kmin, key[j]);
-      kmax = max(kmax, key[j]);
-    }
-  }
-  kmin = __reduce_min_sync(0xffffffffu, kmin);
-  kmax = __reduce_max_sync(0xffffffffu, kmax);
-  if (lane == 0) {
-    wsum[warp] = kmin;
-    wsum[32 + warp] = kmax;
-  }
-  for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
-  __syncthreads();
-  kmin = __reduce_min_sync(0xffffffffu, wsum[lane]);
-  kmax = __reduce_max_sync(0xffffffffu, wsum[32 + lane]);
-  __syncthreads();
-
-  // ---- range-narrowing radix select: the k-th key lies in [clo, chi]
-  const int k = min(a.k, n);
-  uint32_t k_rem = static_cast<uint32_t>(k);
-  uint32_t clo = kmin, chi = kmax;
-  bool whole = false;
-  for (int pass = 0; pass < 5 && !whole && clo != chi; ++pass) {
-    const int sh = max(0, bit_length(chi - clo) - 8);
-    if (pass > 0) {
-      for (int i = lane; i < kBins; i += 32) my_hist[i] = 0u;
-      __syncwarp();
-    }
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const uint32_t u = key[j];
-      if (j < cnt && u >= clo && u <= chi) atomicAdd(&my_hist[(u - clo) >> sh], 1u);
-    }
-    __syncthreads();
-    if (tid < kBins) {
-      uint32_t s = 0;
 #pragma unroll 8
-      for (int w = 0; w < kWarps; ++w) s += sm[w * kBins + tid];
-      hist[tid] = s;
+    for (int j = 0; j < kPer; ++j) {
+      const int e = wbase + j * 32;
+      if (e < n) keys[e] = float_to_key(__ldg(vrow + e));
+    }
+  }
+
+  // ---- 1. initial live range
+  const int k = min(a.k, n);
+  uint32_t k_rem = static_cast<uint32_t>(k), in_range = static_cast<uint32_t>(n);
+  uint32_t clo = 0u, chi = 0xFFFFFFFFu;
+  for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
+  if (a.hist) {
+    // The score kernel already counted this row's keys by their top 12 bits: find the bin of
+    // the k-th key (thread t owns bins 4095-4t .. 4092-4t).
+    uint32_t* rh = a.hist + static_cast<int64_t>(row) * kKeyHistBins;
+    uint32_t c[4], tot = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      c[i] = rh[kKeyHistBins - 1 - (4 * tid + i)];
+      tot += c[i];
+    }
+    uint32_t x = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wa[warp] = x;
+    if (tid == 0) res[3] = 0u;
+    __syncthreads();
+    if (warp == 0) warp_totals_scan(wa, wb);
+    __syncthreads();
+    uint32_t above = x - tot + wb[warp];
+    if (above < k_rem && k_rem <= above + tot) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (above < k_rem && k_rem <= above + c[i]) {
+          res[0] = kKeyHistBins - 1 - (4 * tid + i);
+          res[1] = k_rem - above;
+          res[2] = c[i];
+          res[3] = 1u;
+        }
+        above += c[i];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) rh[kKeyHistBins - 1 - (4 * tid + i)] = 0u;  // ready for reuse
+    __syncthreads();
+    if (res[3]) {  // (a histogram that does not describe the row leaves the full range)
+      clo = res[0] << 20;
+      chi = clo | 0xFFFFFu;
+      k_rem = res[1];
+      in_range = res[2];
+    }
+  } else {
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+#pragma unroll 8
+    for (int j = 0; j < kPer; ++j) {
+      const int e = wbase + j * 32;
+      if (e < n) {
+        const uint32_t u = keys[e];
+        kmin = min(kmin, u);
+        kmax = max(kmax, u);
+      }
+    }
+    kmin = __reduce_min_sync(0xffffffffu, kmin);
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    if (lane == 0) {
+      wa[warp] = kmin;
+      wb[warp] = kmax;
     }
     __syncthreads();
-    find_bin(hist, k_rem, wsum, res);
-    const uint32_t d = res[0];
-    k_rem = res[1];
-    whole = (res[2] == k_rem);
-    const uint64_t lo64 = static_cast<uint64_t>(clo) + (static_cast<uint64_t>(d) << sh);
-    const uint64_t top = lo64 + (1ull << sh) - 1;
-    const uint64_t hi64 = top < chi ? top : static_cast<uint64_t>(chi);
-    clo = static_cast<uint32_t>(lo64);
-    chi = static_cast<uint32_t>(hi64);
+    clo = __reduce_min_sync(0xffffffffu, wa[lane]);
+    chi = __reduce_max_sync(0xffffffffu, wb[lane]);
   }
-  const uint32_t need_eq = k_rem;  // keys in [clo, chi] to take, lowest index first
 
-  // ---- ordered output: positions from two block scans over per-thread counts
-  uint32_t ngt = 0, neq = 0;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const uint32_t u = key[j];
-    ngt += (j < cnt && u > chi) ? 1u : 0u;
-    neq += (j < cnt && u >= clo && u <= chi) ? 1u : 0u;
+  // ---- 2. narrow over the segment until the keys >= clo fit the list (k - k_rem keys lie
+  // above the range).  A k larger than the list is written straight to the output, which
+  // needs the exact k-th key first.
+  const bool direct = k > a.cap;
+  bool dirty = false;
+  for (int pass = 0; pass < 4 && clo != chi && in_range != k_rem &&
+                     (direct || static_cast<uint32_t>(k) - k_rem + in_range > a.cap);
+       ++pass) {
+    const int sh = max(0, bit_length(chi - clo) - 8);
+    if (dirty) {
+      for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int j = 0; j < kPer; ++j) {
+      const int e = wbase + j * 32;
+      const uint32_t u = e < n ? keys[e] : 0u;
+      const bool in = e < n && u >= clo && u <= chi;
+      if (in) atomicAdd(&my_hist[(u - clo) >> sh], 1u);
+    }
+    __syncthreads();
+    narrow_to_bin(hists, hist, res, sh, clo, chi, k_rem, in_range);
+    dirty = true;
   }
-  uint32_t tot;
-  const uint32_t eq_before = block_scan(neq, wsum, tot) - neq;
-  const uint32_t eq_take = eq_before >= need_eq ? 0u : min(neq, need_eq - eq_before);
-  const uint32_t sel = ngt + eq_take;
-  const uint32_t sel_before = block_scan(sel, wsum, tot) - sel;
+  // All keys in [clo, chi] join the list when they fit; otherwise the range is one value
+  // (or all of it is taken) and only the first k_rem of them by index do.
+  const bool fits = !direct && static_cast<uint32_t>(k) - k_rem + in_range <= a.cap;
+
+  // ---- 3. ordered compaction of the segment into the list (or the output, when direct)
+  uint32_t gt_w = 0, eq_w = 0;
+#pragma unroll 8
+  for (int j = 0; j < kPer; ++j) {
+    const int e = wbase + j * 32;
+    const uint32_t u = e < n ? keys[e] : 0u;
+    gt_w += __popc(__ballot_sync(0xffffffffu, e < n && u > chi));
+    eq_w += __popc(__ballot_sync(0xffffffffu, e < n && u >= clo && u <= chi));
+  }
+  if (lane == 0) wa[warp] = eq_w;
   if (tid == 0) s_kth = 0xFFFFFFFFu;
-  __syncthreads();  // the histograms are dead from here on (pairs may reuse the space)
+  __syncthreads();
+  if (warp == 0) warp_totals_scan(wa, wb);  // wb = in-range keys in earlier warps
+  __syncthreads();
+  const uint32_t eq_before = wb[warp];
+  const uint32_t eq_take =
+      fits ? eq_w : (eq_before >= k_rem ? 0u : min(eq_w, k_rem - eq_before));
+  if (lane == 0) wa[warp] = gt_w + eq_take;
+  __syncthreads();
+  if (warp == 0) {
+    warp_totals_scan(wa, wc);  // wc = list entries from earlier warps
+    if (lane == 31) s_total = wc[31] + wa[31];
+  }
+  __syncthreads();
 
   const int64_t out_row = static_cast<int64_t>(row) * gridDim.x + seg;
-  uint32_t pos = sel_before, eq_seen = 0, kth_local = 0xFFFFFFFFu;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const uint32_t u = key[j];
-    bool take = false;
-    if (j < cnt) {
-      if (u > chi) {
-        take = true;
-      } else if (u >= clo) {
-        take = eq_seen < eq_take;
-        ++eq_seen;
-        if (take) kth_local = min(kth_local, u);
+  int32_t* oi32 = a.out_idx && a.idx_bytes == 4
+                      ? static_cast<int32_t*>(a.out_idx) + out_row * a.out_idx_stride : nullptr;
+  int64_t* oi64 = a.out_idx && a.idx_bytes == 8
+                      ? static_cast<int64_t*>(a.out_idx) + out_row * a.out_idx_stride : nullptr;
+  float* ov = a.out_idx && a.out_val ? a.out_val + out_row * a.out_val_stride : nullptr;
+  uint32_t kth_local = 0xFFFFFFFFu;
+  {
+    uint32_t pos_base = wc[warp], eq_seen = 0;
+#pragma unroll 4
+    for (int j = 0; j < kPer; ++j) {
+      const int e = wbase + j * 32;
+      const uint32_t u = e < n ? keys[e] : 0u;
+      const bool gt = e < n && u > chi;
+      const bool eq = e < n && u >= clo && u <= chi;
+      bool take = gt || (fits && eq);
+      unsigned bt = __ballot_sync(0xffffffffu, take);
+      if (!fits) {
+        const unsigned be = __ballot_sync(0xffffffffu, eq);
+        if (be) {
+          take = gt || (eq && eq_seen + __popc(be & lt) < eq_take);
+          bt = __ballot_sync(0xffffffffu, take);
+          eq_seen += __popc(be);
+        }
       }
-    }
-    if (take) {
-      const int e = e0 + j;
-      const uint32_t gi = irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(start + e);
-      if (a.sorted) {
-        pairs[pos] = (static_cast<uint64_t>(u) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - gi);
-      } else if (a.out_idx) {
-        if (a.idx_bytes == 8)
-          static_cast<int64_t*>(a.out_idx)[out_row * a.out_idx_stride + pos] = static_cast<int64_t>(gi);
-        else
-          static_cast<int32_t*>(a.out_idx)[out_row * a.out_idx_stride + pos] = static_cast<int32_t>(gi);
-        if (a.out_val) a.out_val[out_row * a.out_val_stride + pos] = key_to_float(u);
+      if (bt) {
+        const uint32_t pos = pos_base + __popc(bt & lt);
+        if (take) {
+          const uint32_t gi =
+              irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(start + e);
+          if (direct) {
+            if (oi32) oi32[pos] = static_cast<int32_t>(gi);
+            if (oi64) oi64[pos] = static_cast<int64_t>(gi);
+            if (ov) ov[pos] = key_to_float(u);
+            if (eq) kth_local = min(kth_local, u);
+          } else if (pos < static_cast<uint32_t>(a.cap)) {
+            list_key[pos] = u;
+            list_idx[pos] = gi;
+          }
+        }
+        pos_base += __popc(bt);
       }
-      ++pos;
     }
   }
-  if (eq_take) atomicMin(&s_kth, kth_local);
+  if (direct) {  // the output is complete; the k-th key is the smallest taken in range
+    kth_local = __reduce_min_sync(0xffffffffu, kth_local);
+    if (lane == 0 && kth_local != 0xFFFFFFFFu) atomicMin(&s_kth, kth_local);
+    __syncthreads();
+    if (tid == 0 && a.kth_out) a.kth_out[out_row] = key_to_float(s_kth);
+    return;
+  }
+  __syncthreads();
+  const int m = min(static_cast<int>(s_total), a.cap);
+
+  // ---- 4. narrow the list to the exact k-th key (keys in the list above chi are taken)
+  for (int pass = 0; pass < 4 && clo != chi && in_range != k_rem; ++pass) {
+    const int sh = max(0, bit_length(chi - clo) - 8);
+    for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < m; i += kThreads) {
+      const uint32_t u = list_key[i];
+      if (u >= clo && u <= chi) atomicAdd(&my_hist[(u - clo) >> sh], 1u);
+    }
+    __syncthreads();
+    narrow_to_bin(hists, hist, res, sh, clo, chi, k_rem, in_range);
+  }
+  const bool whole = in_range == k_rem;  // every key in [clo, chi] is taken
+
+  // Final take over the list in index order: warp w owns list entries [w*span, (w+1)*span).
+  const int span = ((m + kWarps * 32 - 1) / (kWarps * 32)) * 32;
+  const int lbase = warp * span + lane;
+  uint32_t leq_w = 0;
+  if (!whole) {
+    for (int i = lbase; i < warp * span + span; i += 32) {
+      const uint32_t u = i < m ? list_key[i] : 0u;
+      leq_w += __popc(__ballot_sync(0xffffffffu, i < m && u >= clo && u <= chi));
+    }
+    if (lane == 0) wa[warp] = leq_w;
+    __syncthreads();
+    if (warp == 0) warp_totals_scan(wa, wb);
+    __syncthreads();
+  }
+  uint32_t lgt_w = 0, ltake = 0;
+  {
+    // taken entries in earlier warps = list entries before them minus untaken in-range ones
+    const uint32_t eqb = whole ? 0u : wb[warp];
+    ltake = whole ? 0u : (eqb >= k_rem ? 0u : min(leq_w, k_rem - eqb));
+    for (int i = lbase; i < warp * span + span; i += 32) {
+      const uint32_t u = i < m ? list_key[i] : 0u;
+      lgt_w += __popc(__ballot_sync(0xffffffffu, i < m && (u > chi || (whole && u >= clo))));
+    }
+    if (lane == 0) wa[warp] = lgt_w + ltake;
+    __syncthreads();
+    if (warp == 0) warp_totals_scan(wa, wc);
+    __syncthreads();
+  }
+  const bool write_pairs = a.sorted != 0;
+  uint32_t pos_base = wc[warp], eq_seen = 0;
+  for (int i = lbase; i < warp * span + span; i += 32) {
+    const bool valid = i < m;
+    const uint32_t u = valid ? list_key[i] : 0u;
+    const bool eq = valid && u >= clo && u <= chi;
+    const bool gt = valid && (u > chi || (whole && eq));
+    bool take = gt;
+    unsigned bt = __ballot_sync(0xffffffffu, gt);
+    if (!whole) {
+      const unsigned be = __ballot_sync(0xffffffffu, eq);
+      if (be) {
+        take = gt || (eq && eq_seen + __popc(be & lt) < ltake);
+        bt = __ballot_sync(0xffffffffu, take);
+        eq_seen += __popc(be);
+      }
+    }
+    if (take && (eq || whole)) kth_local = min(kth_local, u);
+    const uint32_t pos = pos_base + __popc(bt & lt);
+    if (take && pos < static_cast<uint32_t>(k)) {
+      const uint32_t gi = list_idx[i];
+      if (write_pairs) {
+        // pairs alias the segment copy, which no thread reads any more
+        pairs[pos] = (static_cast<uint64_t>(u) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - gi);
+      } else {
+        if (oi32) oi32[pos] = static_cast<int32_t>(gi);
+        if (oi64) oi64[pos] = static_cast<int64_t>(gi);
+        if (ov) ov[pos] = key_to_float(u);
+      }
+    }
+    pos_base += __popc(bt);
+  }
+  kth_local = __reduce_min_sync(0xffffffffu, kth_local);
+  if (lane == 0 && kth_local != 0xFFFFFFFFu) atomicMin(&s_kth, kth_local);
   __syncthreads();
   if (tid == 0 && a.kth_out) a.kth_out[out_row] = key_to_float(s_kth);
   if (!a.sorted) return;
@@ -256,11 +481,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   for (int j = tid; j < k; j += kThreads) {
     const uint64_t p = pairs[j];
     const uint32_t gi = 0xFFFFFFFFu - static_cast<uint32_t>(p & 0xFFFFFFFFull);
-    if (a.idx_bytes == 8)
-      static_cast<int64_t*>(a.out_idx)[out_row * a.out_idx_stride + j] = static_cast<int64_t>(gi);
-    else
-      static_cast<int32_t*>(a.out_idx)[out_row * a.out_idx_stride + j] = static_cast<int32_t>(gi);
-    if (a.out_val) a.out_val[out_row * a.out_val_stride + j] = key_to_float(static_cast<uint32_t>(p >> 32));
+    if (oi64) oi64[j] = static_cast<int64_t>(gi);
+    if (oi32) oi32[j] = static_cast<int32_t>(gi);
+    if (ov) ov[j] = key_to_float(static_cast<uint32_t>(p >> 32));
   }
 }
 
@@ -270,21 +493,36 @@ int kpow2(int k) {
   return p;
 }
 
-size_t segment_smem(int chunk, int k, int sorted) {
-  (void)chunk;
-  const size_t hists = static_cast<size_t>(kWarps) * kBins * 4;
-  const size_t pairs = sorted ? static_cast<size_t>(kpow2(k)) * 8 : 0;
-  return hists > pairs ? hists : pairs;
+// Words of the segment region: the segment copy, reused for the sort pairs.
+int row_words(int chunk, int k, int sorted) {
+  const int pairs = sorted ? 2 * kpow2(k) : 0;
+  return ((std::max(chunk, pairs) + 3) / 4) * 4;
 }
 
-int launch_segments(const TopkArgs& a, int rows, int nseg, cudaStream_t stream) {
+int list_cap(int chunk) { return std::min(kCap, ((chunk + 3) / 4) * 4); }
+
+size_t segment_smem(int chunk, int k, int sorted) {
+  return static_cast<size_t>(row_words(chunk, k, sorted)) * 4 +
+         static_cast<size_t>(list_cap(chunk)) * 8 + static_cast<size_t>(8) * kBins * 4;
+}
+
+int launch_segments(TopkArgs a, int rows, int nseg, cudaStream_t stream) {
   const size_t smem = segment_smem(a.chunk, a.k, a.sorted);
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(topk_segment_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem)));
-  topk_segment_kernel<<<dim3(nseg, rows), kThreads, smem, stream>>>(a);
-  TDSA_CUDA_CHECK(cudaGetLastError());
-  return TDSA_OK;
+  a.row_words = row_words(a.chunk, a.k, a.sorted);
+  a.cap = list_cap(a.chunk);
+  a.status = device_status_ptr();
+  if (!a.status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  auto run = [&](auto kern) -> int {
+    TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    kern<<<dim3(nseg, rows), kThreads, smem, stream>>>(a);
+    TDSA_CUDA_CHECK(cudaGetLastError());
+    return TDSA_OK;
+  };
+  if (a.chunk <= 4 * kThreads) return run(topk_segment_kernel<4>);
+  if (a.chunk <= 8 * kThreads) return run(topk_segment_kernel<8>);
+  if (a.chunk <= 16 * kThreads) return run(topk_segment_kernel<16>);
+  return run(topk_segment_kernel<32>);
 }
 
 // Level plan: segments per level while the candidate count exceeds one segment.
@@ -295,11 +533,15 @@ struct Plan {
   int count[8] = {0};  // input count of the level
 };
 
-Plan make_plan(int length, int k) {
+// First level: at least ceil(length / 32768) segments; more (up to one per 8k keys, so the
+// merge level stays <= length / 8) when rows are too few to fill the GPU.
+Plan make_plan(int batch, int length, int k, bool single = false) {
   Plan p;
   int count = length;
+  const int nmin = (length + kTopkSegment - 1) / kTopkSegment;
+  const int nmax = std::max(nmin, length / std::max(8 * k, 4096));
+  int nseg = single ? nmin : std::min(std::max(nmin, (128 + batch - 1) / batch), nmax);
   while (true) {
-    const int nseg = (count + kTopkSegment - 1) / kTopkSegment;
     const int chunk = (count + nseg - 1) / nseg;
     p.nseg[p.levels] = nseg;
     p.chunk[p.levels] = chunk;
@@ -307,6 +549,7 @@ Plan make_plan(int length, int k) {
     ++p.levels;
     if (nseg == 1 || p.levels == 8) break;
     count = nseg * k;
+    nseg = (count + kTopkSegment - 1) / kTopkSegment;
   }
   return p;
 }
@@ -314,7 +557,7 @@ Plan make_plan(int length, int k) {
 }  // namespace
 
 size_t topk_workspace_bytes(int batch, int length, int k) {
-  const Plan p = make_plan(length, k);
+  const Plan p = make_plan(batch, length, k);
   if (p.levels <= 1) return 0;
   // two ping-pong candidate buffers (value f32 + index i32), sized by the first level
   const size_t cand = static_cast<size_t>(batch) * p.nseg[0] * k;
@@ -331,10 +574,12 @@ int topk_check(int length, int k, int sorted) {
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,
                 int batch, int length, int k, int sorted, void* out_idx, int idx_bytes,
                 int64_t oi_stride, float* out_val, int64_t ov_stride, void* ws, size_t ws_bytes,
-                cudaStream_t stream, float* kth_out) {
+                cudaStream_t stream, float* kth_out, uint32_t* key_hist) {
   int rc = topk_check(length, k, sorted);
   if (rc) return rc;
-  const Plan p = make_plan(length, k);
+  if (key_hist && length > kTopkSegment)
+    return fail(TDSA_ERR_UNSUPPORTED, "a key histogram needs rows of at most 32768 keys");
+  const Plan p = make_plan(batch, length, k, key_hist != nullptr);
   if (p.levels > 1 && ws_bytes < topk_workspace_bytes(batch, length, k))
     return fail(TDSA_ERR_WORKSPACE, "top-k workspace too small");
   const size_t cand = static_cast<size_t>(batch) * p.nseg[0] * k;
@@ -360,6 +605,7 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
     a.chunk = p.chunk[level];
     a.k = k;
     a.kth_out = nullptr;
+    a.hist = (p.levels == 1) ? key_hist : nullptr;
     const bool last = level == p.levels - 1;
     if (last) {
       a.sorted = sorted;

@@ -113,6 +113,23 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
                     size_t workspace_bytes, void* stream);
 
 /*
+ * The two halves of tdsa_score_topk for callers that keep their own buffers (a decode loop):
+ * tdsa_score_dense_hist is tdsa_score_dense (16-bit keys) that also adds every score's key
+ * histogram (order-preserving uint32 key >> 20, 4096 bins) to key_hist [batch][4096], which
+ * must be zero on entry; tdsa_topk_hist is tdsa_topk for rows of at most 32768 keys that
+ * starts from that histogram instead of a full first pass, and leaves key_hist zeroed again.
+ */
+int tdsa_score_dense_hist(const void* queries, int64_t q_batch_stride, const float* weights,
+                          int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                          int64_t k_row_stride, int dtype, int batch, int length, float* scores,
+                          int64_t s_batch_stride, uint32_t* key_hist, void* stream);
+
+int tdsa_topk_hist(const float* scores, int64_t s_batch_stride, int batch, int length, int k,
+                   int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                   float* out_values, int64_t val_batch_stride, uint32_t* key_hist,
+                   void* stream);
+
+/*
  * Block-structured kernels (block_size 16, 32, 64 or 128; 16-bit keys).  Keys of a block
  * that is not needed are never read.  Per-block arrays ([batch][bm_batch_stride], int8 or
  * float32) share one row stride >= ceil(length / block_size); per-key outputs have row

@@ -206,6 +206,37 @@ def test_topk_unsorted_large_k_single_segment():
     np.testing.assert_array_equal(idx.cpu().numpy(), oracle.topk_rows(s, 20000, sorted=False)[0])
 
 
+@pytest.mark.parametrize("case", ["zeros", "two_values", "clustered", "misaligned"])
+@pytest.mark.parametrize("k", [1, 2048, 8192, 20000])
+@pytest.mark.parametrize("sorted_", [True, False])
+def test_topk_tie_heavy_clustered_and_misaligned_rows(case, k, sorted_):
+    """Rows whose k-th key has far more equal or near-equal neighbours than the candidate
+    list holds, and rows that do not start on a 16-byte boundary."""
+    from dsa_b200 import topk
+
+    if sorted_ and k > 8192:
+        pytest.skip("k > 8192 is unsorted only")
+    rng = np.random.default_rng(k)
+    n = 30000
+    if case == "zeros":
+        s = np.zeros((2, n), np.float32)
+        s[1, -5:] = 1.0  # a few larger keys after all the ties
+    elif case == "two_values":
+        s = np.where(rng.random((2, n)) < 0.7, np.float32(0.5), np.float32(-0.25))
+        s = s.astype(np.float32)
+    elif case == "clustered":
+        s = (1.0 + rng.integers(0, 1 << 14, size=(2, n)) * 2.0 ** -23).astype(np.float32)
+    else:
+        s = rng.normal(size=(2, n + 1)).astype(np.float32)
+    dev = cuda(s)
+    if case == "misaligned":
+        dev, s = dev[:, 1:], s[:, 1:]
+    idx, val = topk(dev, k, sorted=sorted_)
+    want_i, want_v = oracle.topk_rows(np.ascontiguousarray(s), k, sorted=sorted_)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+
+
 def test_merge_topk_matches_oracle():
     from dsa_b200 import merge_topk, topk
 
@@ -239,3 +270,51 @@ def test_api_errors():
     with pytest.raises(ValueError):
         topk(torch.zeros(10, device="cuda"), 11)
     assert score_dense(q, w, k[:0]).shape == (0,)
+
+
+@pytest.mark.parametrize("length", [100, 1000, 32768])
+@pytest.mark.parametrize("sorted_", [True, False])
+def test_score_topk_plan_with_key_histogram_matches_separate_calls(length, sorted_):
+    """The fused path (score kernel histograms keys, top-k starts from it) gives the same
+    result as scoring and a plain top-k, on repeated runs (the histogram is left zeroed)."""
+    from dsa_b200 import score_dense, topk
+    from dsa_b200.indexer import ScoreTopkPlan
+
+    gen = torch.Generator().manual_seed(length)
+    b, k = 3, min(256, length)
+    q = (torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)).to(torch.bfloat16).cuda()
+    w = (torch.randn(b, 64, generator=gen) / 8).cuda()
+    keys = torch.randn(b, length, 128, generator=gen).to(torch.bfloat16).cuda()
+    plan = ScoreTopkPlan(q, w, keys, k, sorted=sorted_, index_dtype=torch.int64)
+    assert plan.use_hist
+    for rep in range(3):
+        if rep:
+            q.mul_(-1 if rep == 1 else 0.5)  # new queries in the same buffers
+        idx, val = plan.run()
+        want_i, want_v = topk(score_dense(q, w, keys), k, sorted=sorted_)
+        assert torch.equal(idx, want_i), rep
+        assert torch.equal(val, want_v), rep
+    assert int(plan.key_hist.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("k,sorted_", [(1, True), (2048, False), (8192, True), (20000, False)])
+def test_score_topk_plan_histogram_path_with_tied_scores(k, sorted_):
+    """All-zero keys give one score value for the whole row: the histogram's k-th bin
+    holds every key, and the tie rule (lowest index first) decides."""
+    from dsa_b200 import score_dense
+    from dsa_b200.indexer import ScoreTopkPlan
+
+    gen = torch.Generator().manual_seed(k)
+    b, length = 2, 32768
+    q = (torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)).to(torch.bfloat16).cuda()
+    w = (torch.randn(b, 64, generator=gen) / 8).cuda()
+    keys = torch.zeros(b, length, 128, dtype=torch.bfloat16, device="cuda")
+    keys[1, 7000:7003] = 1.0  # a few distinct scores in the second row
+    plan = ScoreTopkPlan(q, w, keys, k, sorted=sorted_, index_dtype=torch.int64)
+    assert plan.use_hist
+    idx, val = plan.run()
+    s = score_dense(q, w, keys).cpu().numpy()
+    want_i, want_v = oracle.topk_rows(s, k, sorted=sorted_)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(plan.key_hist.abs().sum()) == 0
