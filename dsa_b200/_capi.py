@@ -39,6 +39,8 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_score_topk_workspace_bytes": (sz, [i32, i32, i32]),
     "tdsa_score_topk": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32, vp, i32,
                               i64, vp, i64, vp, sz, vp]),
+    "tdsa_score_topk_noalloc": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32,
+                                      vp, i32, i64, vp, i64, vp]),
     "tdsa_score_dense_hist": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
                                     vp]),
     "tdsa_topk_hist": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, vp]),

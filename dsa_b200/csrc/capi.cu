@@ -26,6 +26,13 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 
+// Scratch of tdsa_score_topk_noalloc: scores, key histograms and top-k candidates of one
+// call, in the module's static device memory (one copy per device that loads the library),
+// so that call allocates nothing.  Every call on a device shares it.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
 
 }  // namespace
@@ -63,6 +70,28 @@ int* device_status_ptr() {
     g_status_ptr[dev] = static_cast<int*>(p);
   }
   return g_status_ptr[dev];
+}
+
+// Device address of the static scratch on the current device, looked up once per device
+// (the set-up a first call does; it may load the module on that device).
+void* noalloc_scratch() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("tdsa_score_topk_noalloc: no usable current device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error(std::string("tdsa_score_topk_noalloc: cudaGetSymbolAddress failed: ") +
+                cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  return g_noalloc_ptr[dev];
 }
 
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
@@ -295,6 +324,32 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
                      index_bytes, idx_batch_stride, out_values, val_batch_stride,
                      ws + score_bytes + hist_bytes, workspace_bytes - score_bytes - hist_bytes,
                      st, nullptr, use_hist ? hist : nullptr);
+}
+
+int tdsa_score_topk_noalloc(const void* queries, int64_t q_batch_stride, const float* weights,
+                            int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                            int64_t k_row_stride, int dtype, int batch, int length, int k,
+                            int sorted, void* out_indices, int index_bytes,
+                            int64_t idx_batch_stride, float* out_values,
+                            int64_t val_batch_stride, void* stream) {
+  // Sizes are checked before anything touches the device.
+  if (batch < 1 || length < 1 || k < 1 || k > length)
+    return fail(TDSA_ERR_INVALID, "tdsa_score_topk_noalloc: needs batch >= 1 and 1 <= k <= length");
+  const size_t need = tdsa_score_topk_workspace_bytes(batch, length, k);
+  if (need > kNoAllocScratchBytes)
+    return fail(TDSA_ERR_UNSUPPORTED,
+                "tdsa_score_topk_noalloc: this call needs " + std::to_string(need) +
+                    " bytes of scratch; the static scratch holds " +
+                    std::to_string(kNoAllocScratchBytes) +
+                    " (tdsa_score_topk_workspace_bytes(batch, length, k) must not exceed it)");
+  void* scratch = noalloc_scratch();
+  if (!scratch) return TDSA_ERR_CUDA;
+  // The existing path, with the static scratch as its workspace; it zeroes the key
+  // histogram region itself (cudaMemsetAsync) before the score kernel adds to it.
+  return tdsa_score_topk(queries, q_batch_stride, weights, w_batch_stride, keys,
+                         k_batch_stride, k_row_stride, dtype, batch, length, k, sorted,
+                         out_indices, index_bytes, idx_batch_stride, out_values,
+                         val_batch_stride, scratch, kNoAllocScratchBytes, stream);
 }
 
 int tdsa_score_dense_hist(const void* queries, int64_t q_batch_stride, const float* weights,

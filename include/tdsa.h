@@ -113,6 +113,30 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
                     size_t workspace_bytes, void* stream);
 
 /*
+ * tdsa_score_topk without a workspace argument and without any device allocation.  No
+ * counterpart in the reference: it is for callers that cannot allocate device memory at
+ * call time -- C or C++ host code with no device allocator of its own, or a serving loop
+ * that keeps its device footprint fixed after start-up -- and so cannot supply the
+ * workspace tdsa_score_topk asks for.
+ *
+ * Scratch (scores, key histograms, top-k candidates) is one static 16 MiB buffer in the
+ * library's device memory, one per device.  A call needing more than that
+ * (tdsa_score_topk_workspace_bytes(batch, length, k) > 16 MiB, e.g. batch > 113 at length
+ * 32768) returns TDSA_ERR_UNSUPPORTED before touching the device.  The first call on a
+ * device does a one-time set-up (it looks up the buffer's device address, which may load
+ * the library's module on that device): make that first call before any stream capture.
+ * All calls on one device share the buffer, so calls that can overlap in time (different
+ * streams, or host threads) race on it; calls issued in order on one stream do not.
+ * Results are the same as tdsa_score_topk's.
+ */
+int tdsa_score_topk_noalloc(const void* queries, int64_t q_batch_stride, const float* weights,
+                            int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                            int64_t k_row_stride, int dtype, int batch, int length, int k,
+                            int sorted, void* out_indices, int index_bytes,
+                            int64_t idx_batch_stride, float* out_values,
+                            int64_t val_batch_stride, void* stream);
+
+/*
  * The two halves of tdsa_score_topk for callers that keep their own buffers (a decode loop):
  * tdsa_score_dense_hist is tdsa_score_dense (16-bit keys) that also adds every score's key
  * histogram (order-preserving uint32 key >> 20, 4096 bins) to key_hist [batch][4096], which
