@@ -133,7 +133,29 @@ __device__ __forceinline__ void narrow_to_bin(const uint32_t* hists, uint32_t* h
   chi = static_cast<uint32_t>(hi64);
 }
 
-// kPer keys per thread: segments of up to kPer * 1024 keys.
+// Exclusive prefix of v over the CTA (thread order); *total gets the sum.  Two barriers.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* wa, uint32_t* wb,
+                                                    uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wa[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    warp_totals_scan(wa, wb);
+    if (lane == 31) *total = wb[31] + wa[31];
+  }
+  __syncthreads();
+  return wb[warp] + x - v;
+}
+
+// kPer keys per thread: segments of up to kPer * 1024 keys.  Thread t owns the kPer
+// consecutive elements [kPer*t, kPer*t + kPer) (thread order is index order) and visits
+// them rotated by its lane group, so a warp's 32 shared-memory reads hit 32 banks.
 template <int kPer>
 __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArgs a) {
   extern __shared__ __align__(16) uint32_t sm[];
@@ -141,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   __shared__ uint32_t res[4];
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t s_kth, s_total;
-  __shared__ __align__(8) uint64_t s_bar;
+  __shared__ __align__(8) uint64_t s_bar[4];
   __shared__ int s_abort;
 
   const int row = blockIdx.y, seg = blockIdx.x;
@@ -150,8 +172,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const unsigned lt = lanemask_lt();
   constexpr int kHists = 8;  // private histograms, one per 4 warps
-  // shared memory: [segment keys | sort pairs][list keys][list indices][8 histograms]
-  uint32_t* keys = sm;
+  constexpr int kLog = kPer == 32 ? 5 : kPer == 16 ? 4 : kPer == 8 ? 3 : 2;
+  static_assert((1 << kLog) == kPer, "kPer must be 4, 8, 16 or 32");
+  const int rot = lane >> (5 - kLog);
+  const int tbase = tid * kPer;
+  // shared memory: [segment (floats, or keys) | sort pairs][list keys][list indices][hists]
+  float* rowf = reinterpret_cast<float*>(sm);
   uint32_t* list_key = sm + a.row_words;
   uint32_t* list_idx = list_key + a.cap;
   uint32_t* hists = list_idx + a.cap;
@@ -160,51 +186,47 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
 
   const float* vrow = a.vals + static_cast<int64_t>(row) * a.vals_stride + start;
   const int32_t* irow = a.idx ? a.idx + static_cast<int64_t>(row) * a.idx_stride + start : nullptr;
-  const int wbase = warp * (kPer * 32) + lane;
+  const int k = min(a.k, n);
 
-  // ---- 0. the segment into shared memory (one bulk copy on the TMA engine when the row
-  // is 16-byte aligned), then to keys in place; each thread converts the elements it
-  // reads in every later segment pass, so no barrier is needed before those passes.
+  // ---- 0. the segment into shared memory: bulk copies on the TMA engine (32 KB per
+  // mbarrier) when the row is 16-byte aligned, issued before the histogram prologue so
+  // the two overlap; else coalesced loads.  Warp w's elements lie in one 32 KB piece.
   const bool bulk = ((reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u) && (n % 4 == 0);
-  if (bulk) {
-    if (tid == 0) {
-      s_abort = 0;
-      mbar_init(&s_bar, 1);
+  const uint32_t bytes = static_cast<uint32_t>(n) * 4u;
+  const int npieces = static_cast<int>((bytes + 32767u) / 32768u);
+  if (tid == 0) {
+    s_abort = 0;
+    s_kth = 0xFFFFFFFFu;
+    if (bulk) {
+      for (int c = 0; c < npieces; ++c) mbar_init(&s_bar[c], 1);
       fence_mbar_init();
     }
-    __syncthreads();
+  }
+  for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
+  __syncthreads();
+  if (bulk) {
     if (tid == 0) {
-      const uint32_t bytes = static_cast<uint32_t>(n) * 4u;
-      mbar_arrive_expect_tx(&s_bar, bytes);
-      for (uint32_t off = 0; off < bytes; off += 32768u)
-        bulk_load(reinterpret_cast<uint8_t*>(keys) + off,
-                  reinterpret_cast<const uint8_t*>(vrow) + off, min(32768u, bytes - off), &s_bar);
-    }
-    if (!mbar_wait(&s_bar, 0, &s_abort)) {
-      // the copy did not land in time: report, and let the in-flight copy finish
-      if (tid == 0) atomicOr(a.status, TDSA_ERR_TIMEOUT);
-      volatile int no_abort = 0;
-      mbar_wait(&s_bar, 0, &no_abort);
-      return;
-    }
-#pragma unroll 8
-    for (int j = 0; j < kPer; ++j) {
-      const int e = wbase + j * 32;
-      if (e < n) keys[e] = float_to_key(__uint_as_float(keys[e]));
+      for (int c = 0; c < npieces; ++c) {
+        const uint32_t off = static_cast<uint32_t>(c) * 32768u;
+        const uint32_t len = min(32768u, bytes - off);
+        mbar_arrive_expect_tx(&s_bar[c], len);
+        bulk_load(reinterpret_cast<uint8_t*>(rowf) + off,
+                  reinterpret_cast<const uint8_t*>(vrow) + off, len, &s_bar[c]);
+      }
     }
   } else {
+    const int w0 = warp * kPer * 32;
 #pragma unroll 8
     for (int j = 0; j < kPer; ++j) {
-      const int e = wbase + j * 32;
-      if (e < n) keys[e] = float_to_key(__ldg(vrow + e));
+      const int e = w0 + j * 32 + lane;
+      if (e < n) rowf[e] = __ldg(vrow + e);
     }
+    __syncwarp();
   }
 
-  // ---- 1. initial live range
-  const int k = min(a.k, n);
+  // ---- 1. initial live range [clo, chi] holding the k-th key; k - k_rem keys lie above
   uint32_t k_rem = static_cast<uint32_t>(k), in_range = static_cast<uint32_t>(n);
   uint32_t clo = 0u, chi = 0xFFFFFFFFu;
-  for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
   if (a.hist) {
     // The score kernel already counted this row's keys by their top 12 bits: find the bin of
     // the k-th key (thread t owns bins 4095-4t .. 4092-4t).
@@ -215,18 +237,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       c[i] = rh[kKeyHistBins - 1 - (4 * tid + i)];
       tot += c[i];
     }
-    uint32_t x = tot;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) wa[warp] = x;
     if (tid == 0) res[3] = 0u;
-    __syncthreads();
-    if (warp == 0) warp_totals_scan(wa, wb);
-    __syncthreads();
-    uint32_t above = x - tot + wb[warp];
+    uint32_t dummy;
+    uint32_t above = block_excl_scan(tot, wa, wb, &dummy);
     if (above < k_rem && k_rem <= above + tot) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -248,13 +261,23 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       k_rem = res[1];
       in_range = res[2];
     }
-  } else {
+  }
+  if (bulk && tbase < n) mbar_wait(&s_bar[(tbase * 4) >> 15], 0, &s_abort);
+
+  // Keys are computed from the floats on the fly, or (no histogram: the min/max pass
+  // visits every element anyway) converted once in place.
+  const bool stored = a.hist == nullptr;
+  auto key_at = [&](int e) -> uint32_t {
+    return stored ? sm[e] : float_to_key(rowf[e]);
+  };
+  if (stored) {
     uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
 #pragma unroll 8
     for (int j = 0; j < kPer; ++j) {
-      const int e = wbase + j * 32;
+      const int e = tbase + ((j + rot) & (kPer - 1));
       if (e < n) {
-        const uint32_t u = keys[e];
+        const uint32_t u = float_to_key(rowf[e]);
+        sm[e] = u;
         kmin = min(kmin, u);
         kmax = max(kmax, u);
       }
@@ -263,16 +286,26 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     kmax = __reduce_max_sync(0xffffffffu, kmax);
     if (lane == 0) {
       wa[warp] = kmin;
-      wb[warp] = kmax;
+      wc[warp] = kmax;
     }
-    __syncthreads();
+  }
+  __syncthreads();
+  if (s_abort) {
+    // a bulk copy did not land in time: report, and let the copies in flight finish
+    if (tid == 0) {
+      atomicOr(a.status, TDSA_ERR_TIMEOUT);
+      volatile int no_abort = 0;
+      for (int c = 0; c < npieces; ++c) mbar_wait(&s_bar[c], 0, &no_abort);
+    }
+    return;
+  }
+  if (stored) {
     clo = __reduce_min_sync(0xffffffffu, wa[lane]);
-    chi = __reduce_max_sync(0xffffffffu, wb[lane]);
+    chi = __reduce_max_sync(0xffffffffu, wc[lane]);
   }
 
-  // ---- 2. narrow over the segment until the keys >= clo fit the list (k - k_rem keys lie
-  // above the range).  A k larger than the list is written straight to the output, which
-  // needs the exact k-th key first.
+  // ---- 2. narrow over the segment until the keys >= clo fit the list.  A k larger than
+  // the list is written straight to the output, which needs the exact k-th key first.
   const bool direct = k > a.cap;
   bool dirty = false;
   for (int pass = 0; pass < 4 && clo != chi && in_range != k_rem &&
@@ -281,14 +314,15 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     const int sh = max(0, bit_length(chi - clo) - 8);
     if (dirty) {
       for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
+      __syncthreads();
     }
-    __syncthreads();
 #pragma unroll 8
     for (int j = 0; j < kPer; ++j) {
-      const int e = wbase + j * 32;
-      const uint32_t u = e < n ? keys[e] : 0u;
-      const bool in = e < n && u >= clo && u <= chi;
-      if (in) atomicAdd(&my_hist[(u - clo) >> sh], 1u);
+      const int e = tbase + ((j + rot) & (kPer - 1));
+      if (e < n) {
+        const uint32_t u = key_at(e);
+        if (u >= clo && u <= chi) atomicAdd(&my_hist[(u - clo) >> sh], 1u);
+      }
     }
     __syncthreads();
     narrow_to_bin(hists, hist, res, sh, clo, chi, k_rem, in_range);
@@ -298,30 +332,56 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   // (or all of it is taken) and only the first k_rem of them by index do.
   const bool fits = !direct && static_cast<uint32_t>(k) - k_rem + in_range <= a.cap;
 
-  // ---- 3. ordered compaction of the segment into the list (or the output, when direct)
-  uint32_t gt_w = 0, eq_w = 0;
+  // ---- 3. ordered compaction into the list (or the output, when direct): per-thread bit
+  // masks of the elements taken, bit j = element tbase + j, then one scan for positions.
+  uint32_t take = 0;
+  if (fits && !stored && kPer == 32 && clo <= 0xFF800000u) {
+    // Compare the floats themselves: key(x) >= clo  <=>  !(x < f_lo), f_lo the float of
+    // clo (-inf when clo is at or below the key of -inf).  Exact for +-0 (one key) and
+    // NaN (the largest key; every comparison with NaN is false).  Eight conflict-free
+    // 16-byte reads per thread, rotated by lane.
+    const float f_lo = clo <= 0x007FFFFFu ? -INFINITY : key_to_float(clo);
+    const float4* r4 = reinterpret_cast<const float4*>(rowf) + tid * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int qq = (j + lane) & 7;
+      const float4 v = r4[qq];
+      const int e0 = tbase + 4 * qq;
+      uint32_t b = 0;
+      b |= (e0 + 0 < n && !(v.x < f_lo)) ? 1u : 0u;
+      b |= (e0 + 1 < n && !(v.y < f_lo)) ? 2u : 0u;
+      b |= (e0 + 2 < n && !(v.z < f_lo)) ? 4u : 0u;
+      b |= (e0 + 3 < n && !(v.w < f_lo)) ? 8u : 0u;
+      take |= b << (4 * qq);
+    }
+  } else if (fits) {
 #pragma unroll 8
-  for (int j = 0; j < kPer; ++j) {
-    const int e = wbase + j * 32;
-    const uint32_t u = e < n ? keys[e] : 0u;
-    gt_w += __popc(__ballot_sync(0xffffffffu, e < n && u > chi));
-    eq_w += __popc(__ballot_sync(0xffffffffu, e < n && u >= clo && u <= chi));
+    for (int j = 0; j < kPer; ++j) {
+      const int jj = (j + rot) & (kPer - 1);
+      const int e = tbase + jj;
+      if (e < n && key_at(e) >= clo) take |= 1u << jj;
+    }
+  } else {
+    uint32_t gtm = 0, eqm = 0;
+#pragma unroll 8
+    for (int j = 0; j < kPer; ++j) {
+      const int jj = (j + rot) & (kPer - 1);
+      const int e = tbase + jj;
+      if (e < n) {
+        const uint32_t u = key_at(e);
+        if (u > chi) gtm |= 1u << jj;
+        else if (u >= clo) eqm |= 1u << jj;
+      }
+    }
+    uint32_t dummy;
+    const uint32_t eq_before = block_excl_scan(__popc(eqm), wa, wb, &dummy);
+    const uint32_t n_eq = eq_before >= k_rem ? 0u : min(static_cast<uint32_t>(__popc(eqm)),
+                                                        k_rem - eq_before);
+    uint32_t rest = eqm;
+    for (uint32_t i = 0; i < n_eq; ++i) rest &= rest - 1u;  // drop the lowest n_eq
+    take = gtm | (eqm ^ rest);
   }
-  if (lane == 0) wa[warp] = eq_w;
-  if (tid == 0) s_kth = 0xFFFFFFFFu;
-  __syncthreads();
-  if (warp == 0) warp_totals_scan(wa, wb);  // wb = in-range keys in earlier warps
-  __syncthreads();
-  const uint32_t eq_before = wb[warp];
-  const uint32_t eq_take =
-      fits ? eq_w : (eq_before >= k_rem ? 0u : min(eq_w, k_rem - eq_before));
-  if (lane == 0) wa[warp] = gt_w + eq_take;
-  __syncthreads();
-  if (warp == 0) {
-    warp_totals_scan(wa, wc);  // wc = list entries from earlier warps
-    if (lane == 31) s_total = wc[31] + wa[31];
-  }
-  __syncthreads();
+  uint32_t pos = block_excl_scan(__popc(take), wa, wc, &s_total);
 
   const int64_t out_row = static_cast<int64_t>(row) * gridDim.x + seg;
   int32_t* oi32 = a.out_idx && a.idx_bytes == 4
@@ -330,42 +390,22 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
                       ? static_cast<int64_t*>(a.out_idx) + out_row * a.out_idx_stride : nullptr;
   float* ov = a.out_idx && a.out_val ? a.out_val + out_row * a.out_val_stride : nullptr;
   uint32_t kth_local = 0xFFFFFFFFu;
-  {
-    uint32_t pos_base = wc[warp], eq_seen = 0;
-#pragma unroll 4
-    for (int j = 0; j < kPer; ++j) {
-      const int e = wbase + j * 32;
-      const uint32_t u = e < n ? keys[e] : 0u;
-      const bool gt = e < n && u > chi;
-      const bool eq = e < n && u >= clo && u <= chi;
-      bool take = gt || (fits && eq);
-      unsigned bt = __ballot_sync(0xffffffffu, take);
-      if (!fits) {
-        const unsigned be = __ballot_sync(0xffffffffu, eq);
-        if (be) {
-          take = gt || (eq && eq_seen + __popc(be & lt) < eq_take);
-          bt = __ballot_sync(0xffffffffu, take);
-          eq_seen += __popc(be);
-        }
-      }
-      if (bt) {
-        const uint32_t pos = pos_base + __popc(bt & lt);
-        if (take) {
-          const uint32_t gi =
-              irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(start + e);
-          if (direct) {
-            if (oi32) oi32[pos] = static_cast<int32_t>(gi);
-            if (oi64) oi64[pos] = static_cast<int64_t>(gi);
-            if (ov) ov[pos] = key_to_float(u);
-            if (eq) kth_local = min(kth_local, u);
-          } else if (pos < static_cast<uint32_t>(a.cap)) {
-            list_key[pos] = u;
-            list_idx[pos] = gi;
-          }
-        }
-        pos_base += __popc(bt);
-      }
+  while (take) {
+    const int jb = __ffs(take) - 1;
+    take &= take - 1u;
+    const int e = tbase + jb;
+    const uint32_t u = key_at(e);
+    const uint32_t gi = irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(start + e);
+    if (direct) {
+      if (oi32) oi32[pos] = static_cast<int32_t>(gi);
+      if (oi64) oi64[pos] = static_cast<int64_t>(gi);
+      if (ov) ov[pos] = key_to_float(u);
+      if (u <= chi) kth_local = min(kth_local, u);
+    } else if (pos < static_cast<uint32_t>(a.cap)) {
+      list_key[pos] = u;
+      list_idx[pos] = gi;
     }
+    ++pos;
   }
   if (direct) {  // the output is complete; the k-th key is the smallest taken in range
     kth_local = __reduce_min_sync(0xffffffffu, kth_local);
@@ -421,6 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   }
   const bool write_pairs = a.sorted != 0;
   uint32_t pos_base = wc[warp], eq_seen = 0;
+  kth_local = 0xFFFFFFFFu;
   for (int i = lbase; i < warp * span + span; i += 32) {
     const bool valid = i < m;
     const uint32_t u = valid ? list_key[i] : 0u;

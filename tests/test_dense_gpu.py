@@ -318,3 +318,38 @@ def test_score_topk_plan_histogram_path_with_tied_scores(k, sorted_):
     np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
     np.testing.assert_array_equal(val.cpu().numpy(), want_v)
     assert int(plan.key_hist.abs().sum()) == 0
+
+
+def _key_hist(s: np.ndarray) -> np.ndarray:
+    """Per-row counts of the order-preserving uint32 key's top 12 bits (-0 counts as +0)."""
+    b = s.astype(np.float32).view(np.uint32).copy()
+    b[b == 0x80000000] = 0
+    key = np.where(b & 0x80000000, ~b, b | 0x80000000).astype(np.uint32)
+    return np.stack([np.bincount(r >> 20, minlength=4096) for r in key]).astype(np.int32)
+
+
+@pytest.mark.parametrize("length,k,sorted_", [(32768, 2048, False), (30000, 512, True),
+                                              (20000, 20000, False), (32768, 1, True)])
+def test_topk_hist_special_values_with_host_histogram(length, k, sorted_):
+    """tdsa_topk_hist from a histogram made on the host: +-0, +-inf, denormals and ties."""
+    from dsa_b200 import _capi as capi
+
+    rng = np.random.default_rng(length + k)
+    s = np.round(rng.normal(size=(3, length)) * 8).astype(np.float32) / 8
+    s[0, rng.integers(0, length, 300)] = -0.0
+    s[0, rng.integers(0, length, 300)] = 0.0
+    s[1, rng.integers(0, length, 50)] = np.inf
+    s[1, rng.integers(0, length, 50)] = -np.inf
+    s[2, rng.integers(0, length, 400)] = np.float32(1e-45)  # denormal ties
+    s[2, rng.integers(0, length, 400)] = np.float32(-1e-45)
+    dev = cuda(s)
+    hist = cuda(_key_hist(s))
+    idx = torch.empty(3, k, dtype=torch.int64, device="cuda")
+    val = torch.empty(3, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist", dev.data_ptr(), dev.stride(0), 3, length, k, int(sorted_),
+              idx.data_ptr(), 8, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=sorted_)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(hist.abs().sum()) == 0  # consumed and zeroed
