@@ -321,7 +321,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
             "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
             "api": "dsa_b200.sidecar.QueryProjector + dsa_b200.indexer.ScoreTopkPlan "
-                   "(C ABI tdsa_query_prep, tdsa_score_dense, tdsa_topk)",
+                   "(C ABI tdsa_query_prep, tdsa_score_dense_hist, tdsa_topk_hist)",
         },
         "gpu_launches": launches["n"],
         "clocks": clocks.summary(),

@@ -3,7 +3,8 @@
 Product code only: hand-written CUDA kernels in ``csrc/`` behind the C ABI of
 ``include/tdsa.h`` (built into ``_lib/libtdsa.so``), and the Python mirror of the
 reference project's interface for this path (``progressive_kernel``, ``sidecar``,
-``metrics``, ``certified``, ``verifier_scoring``).  There is no CPU implementation.
+``metrics``, ``certified``, ``verifier_scoring``) and the multi-GPU layouts
+(``parallel``).  There is no CPU implementation.
 """
 
 from .indexer import (  # noqa: F401

@@ -1,19 +1,20 @@
 // Exact row-wise top-k by radix select over a shared-memory copy of the row (no global
 // sort).
 //
-// One 1024-thread CTA owns one segment of a row (<= 32768 elements).  The segment is copied
-// into shared memory with one bulk copy and turned in place into order-preserving uint32
-// keys.  Warp w owns elements [w*P, (w+1)*P) (P = keys per warp); slot j of lane l is
-// element w*P + 32j + l, so every pass reads shared memory without bank conflicts and
-// (warp, slot, lane) order is index order.
+// One 1024-thread CTA owns one segment of a row (<= 32768 elements), copied into shared
+// memory by bulk copies (TMA engine, 32 KB per mbarrier).  Thread t owns the P consecutive
+// elements [P*t, P*t + P) (P = segment / 1024 rounded up to 4, 8, 16 or 32), so thread
+// order is index order; a thread visits its elements rotated by its lane group, which
+// keeps a warp's shared-memory reads on 32 distinct banks.
 //   1. Live range [clo, chi] holding the k-th key: from the score kernel's 12-bit key
-//      histogram when one is given, else the segment's min/max.
+//      histogram when one is given (read while the copy is in flight), else the segment's
+//      min/max (that pass also converts the floats to order-preserving keys in place).
 //   2. Range-narrowing radix passes (256 bins, eight private histograms) only until the
 //      keys >= clo fit the candidate list (8192 entries), or the range is one value.
-//   3. One ordered compaction: every key > chi, and the keys in [clo, chi] (all of them
-//      when they fit; otherwise the range is one value and the first ones by index that
-//      complete k), go to the candidate list in index order (warp ballots + one scan over
-//      the 32 warp totals).
+//   3. One ordered compaction: each thread builds a bit mask of its elements to keep
+//      (every key >= clo when they fit; otherwise keys > chi and the lowest-index keys of
+//      the one-value range that complete k), one CTA-wide scan of the mask popcounts gives
+//      list positions, and only the kept elements are written.
 //   4. The list is narrowed to the exact k-th key T; keys > T and the lowest-index keys
 //      == T are taken -- the tie rule of the reference's stable_topk (metrics.py:9-22).
 //      Unsorted output is in ascending index order; sorted output is a bitonic sort of the

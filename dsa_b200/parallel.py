@@ -1,0 +1,94 @@
+"""Multi-GPU sharding of the indexer decode step: one process per GPU, torch.distributed.
+
+Two layouts:
+
+* batch sharding (independent sequences, configs 2 and 4): each rank scores and selects its
+  own sequences.  There is nothing to exchange; ``batch_shard`` only says which rows a rank
+  owns.
+* L sharding (one long context split over GPUs, config 5): rank r holds the contiguous keys
+  [start_r, stop_r) of every sequence, scores them and keeps its local top-k with global
+  indices (local index + start_r).  The candidates of all ranks are all-gathered (NCCL over
+  NVLink on GPUs) and merged by ``tdsa_merge_topk``.  This is exact, ties included: every
+  member of the global top-k is in its own shard's local top-k, the gathered rows are in
+  ascending index order (shards are contiguous and in rank order, each local list is in
+  ascending index order), and the merge applies the same lowest-index-first tie rule.
+
+The reference never shards (its scoring is single-GPU); the merge is new.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from .indexer import merge_topk, scores_topk
+
+Candidates = tuple[torch.Tensor, torch.Tensor]  # values [B, k] f32, indices [B, k] int32
+
+
+def shard_bounds(length: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous key range [start, stop) of `rank`: the first length % world ranks hold one
+    key more than the others."""
+    if not 0 <= rank < world:
+        raise ValueError("rank outside [0, world)")
+    base, extra = divmod(length, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def batch_shard(batch: int, rank: int, world: int) -> slice:
+    """Rows of the batch a rank owns under batch sharding."""
+    start, stop = shard_bounds(batch, rank, world)
+    return slice(start, stop)
+
+
+def local_candidates(queries: torch.Tensor, weights: torch.Tensor, keys_shard: torch.Tensor,
+                     k: int, offset: int) -> Candidates:
+    """Dense scores of this rank's keys and their top-k (unsorted: ascending index order),
+    with indices made global by `offset`."""
+    idx, val = scores_topk(queries, weights, keys_shard, k, sorted=False,
+                           index_dtype=torch.int32)
+    if idx.dim() == 1:
+        idx, val = idx.unsqueeze(0), val.unsqueeze(0)
+    return val, idx + offset
+
+
+def gather_candidates(values: torch.Tensor, indices: torch.Tensor,
+                      group: dist.ProcessGroup | None = None) -> Candidates:
+    """All-gather [B, k] candidate lists of every rank -> [B, world * k], rank-major."""
+    world = dist.get_world_size(group)
+    vs = [torch.empty_like(values) for _ in range(world)]
+    js = [torch.empty_like(indices) for _ in range(world)]
+    dist.all_gather(vs, values.contiguous(), group=group)
+    dist.all_gather(js, indices.contiguous(), group=group)
+    return torch.cat(vs, dim=1), torch.cat(js, dim=1)
+
+
+@dataclass
+class LShardedTopK:
+    """Exact global top-k of a cache sharded along L over the ranks of `group`.
+
+    `local_fn(queries, weights, keys_shard, k, offset)` and `merge_fn(values, indices, k,
+    sorted)` default to the CUDA path (``local_candidates`` and ``merge_topk``); they are
+    parameters so the exchange logic can run with other stand-ins (the CPU tests)."""
+
+    k: int
+    sorted: bool = True
+    group: dist.ProcessGroup | None = None
+    local_fn: Callable[..., Candidates] = local_candidates
+    merge_fn: Callable[..., Candidates] | None = None
+
+    def __call__(self, queries: torch.Tensor, weights: torch.Tensor, keys_shard: torch.Tensor,
+                 offset: int) -> tuple[torch.Tensor, torch.Tensor]:
+        if keys_shard.shape[-2] < self.k:
+            raise ValueError(f"every shard needs at least k={self.k} keys "
+                             f"(this one has {keys_shard.shape[-2]})")
+        values, indices = self.local_fn(queries, weights, keys_shard, self.k, offset)
+        all_v, all_i = gather_candidates(values, indices, self.group)
+        if self.merge_fn is not None:
+            return self.merge_fn(all_v, all_i, self.k, self.sorted)
+        idx, val = merge_topk(all_v, all_i, self.k, sorted=self.sorted)
+        return idx, val

@@ -223,3 +223,42 @@ def two_pass_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys: t
     accepted = direct_full_blocks.to(device=keys.device, dtype=torch.bool) | (maxima >= thr)
     scores = masked_full_scores_triton(queries, weights, keys, accepted, block_size=block_size)
     return ProgressiveResult(scores, accepted.to(torch.int8), maxima)
+
+
+# --------------------------------------------------------------------------- torch-named
+# The reference's torch_* functions (:45-90) are its readable specification of the same
+# math.  Here they keep their names and outputs but run on the B200 kernels (CUDA tensors
+# of any float dtype for the dense one; 16-bit for the progressive one).
+
+def torch_full_scores(queries: torch.Tensor, weights: torch.Tensor,
+                      keys: torch.Tensor) -> torch.Tensor:
+    """:45-55 -- dense scores [L] float32 (float32 keys run the FP32 kernel)."""
+    if queries.shape != (HEADS, HEAD_DIM) or weights.shape != (HEADS,):
+        raise ValueError("expected queries [64,128] and weights [64]")
+    if keys.ndim != 2 or keys.shape[1] != HEAD_DIM:
+        raise ValueError("expected keys [L,128]")
+    if not (queries.is_cuda and weights.is_cuda and keys.is_cuda):
+        raise ValueError("the B200 indexer kernels require CUDA tensors")
+    return score_dense(queries, weights, keys)
+
+
+def torch_progressive_scores(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor,
+                             selected_heads: torch.Tensor, direct_full_blocks: torch.Tensor,
+                             threshold: float, *, block_size: int = 64
+                             ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """:58-90 -- (scores, accepted bool, block_max): the 8-head probe maximum of EVERY block
+    (direct ones included), acceptance = direct or probe max >= threshold, full 64-head
+    scores on accepted blocks and -inf elsewhere.  Two launches: the probe over all blocks,
+    then dense scoring of the accepted blocks (rejected blocks are not read again)."""
+    selected, _ = split_head_ids(selected_heads.cpu())
+    length = keys.shape[0]
+    nblocks = math.ceil(length / block_size)
+    if direct_full_blocks.numel() != nblocks:
+        raise ValueError("direct_full_blocks length mismatch")
+    all_blocks = torch.ones(nblocks, dtype=torch.bool, device=keys.device)
+    _, block_max = h8_block_max_triton(queries, weights, keys, selected.to(keys.device),
+                                       all_blocks, block_size=block_size)
+    accepted = direct_full_blocks.to(device=keys.device, dtype=torch.bool) | (
+        block_max >= float(threshold))
+    scores = masked_full_scores_triton(queries, weights, keys, accepted, block_size=block_size)
+    return scores, accepted, block_max

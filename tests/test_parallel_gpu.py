@@ -1,0 +1,70 @@
+"""GPU parity of the L-sharded top-k: the shard-local top-k + merge equals the whole-row
+top-k bit for bit, emulated in one process (any GPU count) and, with two or more GPUs, as
+two NCCL ranks (config 5 shape)."""
+
+from __future__ import annotations
+
+import math
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from dsa_b200.build import build
+
+    build()
+    yield
+    from dsa_b200 import device_status
+
+    assert device_status() == 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_shard_local_topk_and_merge_equal_whole_row(world):
+    from dsa_b200 import merge_topk, scores_topk
+    from dsa_b200.parallel import local_candidates, shard_bounds
+
+    gen = torch.Generator().manual_seed(world)
+    b, length, k = 4, 40000 + world, 1024
+    q = (torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)).to(torch.bfloat16).cuda()
+    w = (torch.randn(b, 64, generator=gen) / 8).cuda()
+    keys = torch.randn(b, length, 128, generator=gen).to(torch.bfloat16)
+    keys[:, 9000:26000] = keys[:, 9000:9001]  # ties across shard boundaries
+    keys = keys.cuda()
+    vs, js = [], []
+    for r in range(world):
+        start, stop = shard_bounds(length, r, world)
+        v, j = local_candidates(q, w, keys[:, start:stop], k, start)
+        vs.append(v)
+        js.append(j)
+    idx, val = merge_topk(torch.cat(vs, 1), torch.cat(js, 1), k, sorted=True)
+    want_i, want_v = scores_topk(q, w, keys, k, sorted=True)
+    assert torch.equal(idx, want_i) and torch.equal(val, want_v)
+    from dsa_b200 import score_dense
+
+    s = score_dense(q, w, keys).cpu().numpy()
+    np.testing.assert_array_equal(idx.cpu().numpy(), oracle.topk_rows(s, k)[0])
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_l_sharded_topk_two_nccl_ranks(tmp_path):
+    out = tmp_path / "result.txt"
+    worker = os.path.join(os.path.dirname(__file__), "_l_shard_worker.py")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531",
+           worker, str(out)]
+    subprocess.run(cmd, check=True, env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
+    assert out.read_text() == "OK"
