@@ -410,6 +410,40 @@ int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,
                       weight_scale, static_cast<cudaStream_t>(stream));
 }
 
+int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_size,
+                       const void* w_q, int64_t wq_row_stride, const float* w_proj,
+                       const int64_t* positions, void* q, int64_t q_stride, float* w,
+                       int64_t w_stride, int dtype, int batch, int rope_dim, float rope_theta,
+                       float weight_scale, void* qraw, int64_t qraw_stride, void* stream) {
+  if (!hidden || !w_q || !w_proj || !positions || !q || !w)
+    return fail(TDSA_ERR_INVALID, "null pointer");
+  if (dtype != TDSA_BF16 && dtype != TDSA_F16)
+    return fail(TDSA_ERR_INVALID, "query_project takes TDSA_BF16 or TDSA_F16");
+  if (batch < 1 || batch > 65535 * 256)
+    return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535 * 256]");
+  if (hidden_size < 8 || hidden_size > 65536 || hidden_size % 8)
+    return fail(TDSA_ERR_UNSUPPORTED, "hidden_size must be a multiple of 8 in [8, 65536]");
+  if (rope_dim < 0 || rope_dim > kHeadDim || rope_dim % 2)
+    return fail(TDSA_ERR_INVALID, "rope_dim must be even and <= 128");
+  if (wq_row_stride < hidden_size || (batch > 1 && hidden_stride < hidden_size))
+    return fail(TDSA_ERR_INVALID, "row strides overlap");
+  if (batch > 1 && (q_stride < kHeads * kHeadDim || w_stride < kHeads ||
+                    (qraw && qraw_stride < kHeads * kHeadDim)))
+    return fail(TDSA_ERR_INVALID, "row strides overlap");
+  if (!aligned16(hidden) || !aligned16(w_q) || !aligned16(w_proj) || wq_row_stride % 8 ||
+      (batch > 1 && hidden_stride % 8))
+    return fail(TDSA_ERR_ALIGN, "hidden, w_q and w_proj need 16-byte aligned rows (TMA)");
+  if (!aligned16(q) || (qraw && !aligned16(qraw)) ||
+      (batch > 1 && (q_stride % 8 || (qraw && qraw_stride % 8))))
+    return fail(TDSA_ERR_ALIGN, "q and qraw need 16-byte aligned rows");
+  int* status = device_status_ptr();
+  if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  return launch_query_project(hidden, hidden_stride, hidden_size, w_q, wq_row_stride, w_proj,
+                              positions, q, q_stride, w, w_stride, dtype, batch, rope_dim,
+                              rope_theta, weight_scale, qraw, qraw_stride,
+                              static_cast<cudaStream_t>(stream), status);
+}
+
 int tdsa_h8_block_max(const void* queries, int64_t q_batch_stride, const float* weights,
                       int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
                       int64_t k_row_stride, int dtype, int batch, int length, int block_size,

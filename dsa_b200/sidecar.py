@@ -78,15 +78,17 @@ def encode_queries(hidden: torch.Tensor, wq: torch.Tensor, ww: torch.Tensor,
 
 
 class QueryProjector:
-    """Decode-step query projection on fixed buffers: one cuBLAS GEMM for W_q (hidden
-    dtype) and one fused kernel (tdsa_query_prep) for RoPE and the float32 head weights.
+    """Decode-step query projection on fixed buffers, one launch (tdsa_query_project): the
+    W_q GEMM on the tensor cores with RoPE in its epilogue, and the float32 head weights
+    computed from the same staged hidden states.
 
     ``project(hidden, positions)`` -> (q [B,64,128], w [B,64] float32), written into
     ``self.q`` / ``self.w`` (stable addresses, so a ScoreTopkPlan can be built on them).
+    keep_qraw=True also keeps the pre-RoPE projection in ``self.qraw`` [B, 8192].
     """
 
     def __init__(self, wq: torch.Tensor, ww: torch.Tensor, batch: int, *, rope_dim: int = 64,
-                 rope_theta: float = 10_000.0):
+                 rope_theta: float = 10_000.0, keep_qraw: bool = False):
         require_cuda(wq, ww)
         if wq.shape[0] != HEADS * HEAD_DIM or ww.shape[0] != HEADS:
             raise ValueError("expected wq [8192, hidden] and ww [64, hidden]")
@@ -94,31 +96,36 @@ class QueryProjector:
             raise ValueError("wq must be bf16 or fp16")
         if ww.shape[1] != wq.shape[1]:
             raise ValueError("wq and ww must share the hidden size")
+        if wq.shape[1] % 8:
+            raise ValueError("the hidden size must be a multiple of 8")
         dev = wq.device
         self.hidden = wq.shape[1]
-        self.wq_t = wq.t()
+        self.wq = wq if (wq.stride(-1) == 1 and wq.stride(0) % 8 == 0
+                         and wq.data_ptr() % 16 == 0) else wq.contiguous()
         self.ww = ww.to(torch.float32).contiguous()
         self.dtype = wq.dtype
         self.batch, self.rope_dim, self.theta = batch, rope_dim, rope_theta
-        self.qraw = torch.empty(batch, HEADS * HEAD_DIM, device=dev, dtype=wq.dtype)
+        self.qraw = (torch.empty(batch, HEADS * HEAD_DIM, device=dev, dtype=wq.dtype)
+                     if keep_qraw else None)
         self.q = torch.empty(batch, HEADS, HEAD_DIM, device=dev, dtype=wq.dtype)
         self.w = torch.empty(batch, HEADS, device=dev, dtype=torch.float32)
-        self._fn = capi.lib().tdsa_query_prep
+        self._fn = capi.lib().tdsa_query_project
         self._dt = capi.TDSA_BF16 if wq.dtype == torch.bfloat16 else capi.TDSA_F16
 
     def project(self, hidden: torch.Tensor, positions: torch.Tensor):
         if hidden.shape != (self.batch, self.hidden) or hidden.dtype != self.dtype:
             raise ValueError("hidden must be [batch, hidden] in the projection dtype")
-        if hidden.stride(-1) != 1:
-            hidden = hidden.contiguous()
-        torch.matmul(hidden, self.wq_t, out=self.qraw)
+        if hidden.stride(-1) != 1 or hidden.stride(0) % 8 or hidden.data_ptr() % 16:
+            hidden = hidden.contiguous() if hidden.stride(-1) != 1 else hidden.clone()
         if positions.dtype != torch.int64 or not positions.is_contiguous():
             positions = positions.to(torch.int64).contiguous()
-        capi.check(self._fn(self.qraw.data_ptr(), self.qraw.stride(0), hidden.data_ptr(),
-                            hidden.stride(0), self.hidden, self.ww.data_ptr(),
-                            positions.data_ptr(), self.q.data_ptr(), HEADS * HEAD_DIM,
-                            self.w.data_ptr(), HEADS, self._dt, self.batch, self.rope_dim,
-                            self.theta, (HEADS * HEAD_DIM) ** -0.5,
+        capi.check(self._fn(hidden.data_ptr(), hidden.stride(0), self.hidden, self.wq.data_ptr(),
+                            self.wq.stride(0), self.ww.data_ptr(), positions.data_ptr(),
+                            self.q.data_ptr(), HEADS * HEAD_DIM, self.w.data_ptr(), HEADS,
+                            self._dt, self.batch, self.rope_dim, self.theta,
+                            (HEADS * HEAD_DIM) ** -0.5,
+                            self.qraw.data_ptr() if self.qraw is not None else None,
+                            HEADS * HEAD_DIM,
                             torch.cuda.current_stream(self.q.device).cuda_stream))
         return self.q, self.w
 

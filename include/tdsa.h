@@ -253,6 +253,26 @@ int tdsa_relu_index_score(const double* q, const double* keys, const double* w, 
                           int dim, int tokens, double* out, void* stream);
 
 /*
+ * The whole decode-step query projection of the sidecar in one launch (replaces the
+ * W_q GEMM + tdsa_query_prep pair): reference LightningIndexerSidecar.encode_queries,
+ * src/temporal_dsa/sidecar.py:78-87.
+ *   q[b]  = RoPE_noninterleaved(16-bit(hidden[b] @ w_q^T)) viewed [64][128], RoPE on the
+ *           first rope_dim dims of each head (float32 math, one rounding);
+ *   w[b]  = weight_scale * float(hidden[b]) @ w_proj^T  (float32, [64]).
+ * hidden [batch][hidden_size] 16-bit, row stride hidden_stride; w_q [8192][hidden_size]
+ * 16-bit (nn.Linear weight), row stride wq_row_stride; w_proj [64][hidden_size] float32
+ * contiguous; positions [batch] int64.  q [batch][8192] (row stride q_stride), w [batch][64]
+ * (row stride w_stride).  qraw: optional [batch][8192] output of the pre-RoPE projection
+ * (NULL to skip).  hidden_size a multiple of 8; hidden, w_q, w_proj, q and qraw rows
+ * 16-byte aligned.
+ */
+int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_size,
+                       const void* w_q, int64_t wq_row_stride, const float* w_proj,
+                       const int64_t* positions, void* q, int64_t q_stride, float* w,
+                       int64_t w_stride, int dtype, int batch, int rope_dim, float rope_theta,
+                       float weight_scale, void* qraw, int64_t qraw_stride, void* stream);
+
+/*
  * Decode-step tail of the sidecar query projection, one launch: RoPE on the first rope_dim
  * dims of every head of the W_q GEMM output, and the float32 head weights
  * w = weight_scale * hidden @ w_proj^T.
