@@ -410,8 +410,24 @@ int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,
                       weight_scale, static_cast<cudaStream_t>(stream));
 }
 
+size_t tdsa_packed_query_weights_bytes(int hidden_size) {
+  if (hidden_size < 8 || hidden_size > 65536 || hidden_size % 8) return 0;
+  return packed_wq_bytes(hidden_size);
+}
+
+int tdsa_pack_query_weights(const void* w_q, int64_t wq_row_stride, int hidden_size,
+                            void* out, void* stream) {
+  if (!w_q || !out) return fail(TDSA_ERR_INVALID, "null pointer");
+  if (hidden_size < 8 || hidden_size > 65536 || hidden_size % 8)
+    return fail(TDSA_ERR_UNSUPPORTED, "hidden_size must be a multiple of 8 in [8, 65536]");
+  if (wq_row_stride < hidden_size) return fail(TDSA_ERR_INVALID, "row stride < hidden_size");
+  if (!aligned16(out)) return fail(TDSA_ERR_ALIGN, "out must be 16-byte aligned");
+  return launch_pack_wq(w_q, wq_row_stride, hidden_size, out, static_cast<cudaStream_t>(stream));
+}
+
 int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_size,
-                       const void* w_q, int64_t wq_row_stride, const float* w_proj,
+                       const void* w_q, int64_t wq_row_stride, int wq_packed,
+                       const float* w_proj,
                        const int64_t* positions, void* q, int64_t q_stride, float* w,
                        int64_t w_stride, int dtype, int batch, int rope_dim, float rope_theta,
                        float weight_scale, void* qraw, int64_t qraw_stride, void* stream) {
@@ -425,12 +441,14 @@ int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_siz
     return fail(TDSA_ERR_UNSUPPORTED, "hidden_size must be a multiple of 8 in [8, 65536]");
   if (rope_dim < 0 || rope_dim > kHeadDim || rope_dim % 2)
     return fail(TDSA_ERR_INVALID, "rope_dim must be even and <= 128");
-  if (wq_row_stride < hidden_size || (batch > 1 && hidden_stride < hidden_size))
+  if ((!wq_packed && wq_row_stride < hidden_size) ||
+      (batch > 1 && hidden_stride < hidden_size))
     return fail(TDSA_ERR_INVALID, "row strides overlap");
   if (batch > 1 && (q_stride < kHeads * kHeadDim || w_stride < kHeads ||
                     (qraw && qraw_stride < kHeads * kHeadDim)))
     return fail(TDSA_ERR_INVALID, "row strides overlap");
-  if (!aligned16(hidden) || !aligned16(w_q) || !aligned16(w_proj) || wq_row_stride % 8 ||
+  if (!aligned16(hidden) || !aligned16(w_q) || !aligned16(w_proj) ||
+      (!wq_packed && wq_row_stride % 8) ||
       (batch > 1 && hidden_stride % 8))
     return fail(TDSA_ERR_ALIGN, "hidden, w_q and w_proj need 16-byte aligned rows (TMA)");
   if (!aligned16(q) || (qraw && !aligned16(qraw)) ||
@@ -438,7 +456,8 @@ int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_siz
     return fail(TDSA_ERR_ALIGN, "q and qraw need 16-byte aligned rows");
   int* status = device_status_ptr();
   if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
-  return launch_query_project(hidden, hidden_stride, hidden_size, w_q, wq_row_stride, w_proj,
+  return launch_query_project(hidden, hidden_stride, hidden_size, w_q, wq_row_stride,
+                              wq_packed ? 1 : 0, w_proj,
                               positions, q, q_stride, w, w_stride, dtype, batch, rope_dim,
                               rope_theta, weight_scale, qraw, qraw_stride,
                               static_cast<cudaStream_t>(stream), status);

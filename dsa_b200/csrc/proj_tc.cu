@@ -18,6 +18,8 @@
 //               shared memory (they release each stage with the MMA); afterwards: TMEM -> registers, 16-bit rounding, RoPE with the partner
 //               dimension exchanged through shared memory, stores.
 // Every wait is bounded (TDSA_ERR_TIMEOUT in the device status word on expiry).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
@@ -48,9 +50,22 @@ struct ProjArgs {
   int rope_dim;
   float theta;
   float scale;
-  int stages;
+  int packed;               // W_q in the packed tile layout (see pack_wq_kernel)
   int* status;
 };
+
+// Row coordinate of W_q tile (head h, K chunk kc) in the tensor map: natural layout
+// [8192][hidden] (x coordinate kc * 64) or packed [64 heads][nk][128][64] (x = 0).
+__device__ __forceinline__ void wq_coords(const ProjArgs& a, int h, int kc, int nk, int& x,
+                                          int& y) {
+  if (a.packed) {
+    x = 0;
+    y = (h * nk + kc) * 128;
+  } else {
+    x = kc * 64;
+    y = h * 128;
+  }
+}
 
 template <int kN>
 constexpr int stage_bytes() {
@@ -177,7 +192,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* dst = smem + s * kStage;
         mbar_arrive_expect_tx(&full[s], bytes);
         if (gemm) {
-          tma_load_2d(dst, &wmap, &full[s], kc * kKChunk, h * 128, pol_w);
+          int wx, wy;
+          wq_coords(a, h, kc, nk, wx, wy);
+          tma_load_2d(dst, &wmap, &full[s], wx, wy, pol_w);
         } else {
           tma_load_2d(ww_ring + s * kKChunk, &wwmap, &full[s], kc * kKChunk, h, pol_x);
         }
@@ -367,6 +384,333 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, TDSA_ERR_TIMEOUT);
 }
 
+// cos/sin of angle = position * theta^(-j/half), rounded to float32 as the reference computes
+// it.  The angle (|angle| < 2^24) is reduced by 2*pi in double precision (the product
+// n * 2pi and the subtraction are exact to ~2^-53 relative), then the hardware sin/cos
+// approximations take the reduced |r| <= pi (absolute error ~2^-21, far below the 16-bit
+// rounding of q that follows).  Table layout [j][col], row stride `stride`; run by the
+// 128 epilogue threads.
+__device__ __forceinline__ void build_rope_table(const float* spos, const float* sinv, int half,
+                                                 int ncols, int stride, float* tcos,
+                                                 float* tsin) {
+  const int et = threadIdx.x - 64;
+  for (int i = et; i < ncols * half; i += 128) {
+    const int col = i / half, jj = i - col * half;
+    const float ang = spos[col] * sinv[jj];
+    const double n = rint(static_cast<double>(ang) * 0.15915494309189535);
+    const float r = static_cast<float>(fma(-n, 6.283185307179586, static_cast<double>(ang)));
+    tcos[jj * stride + col] = __cosf(r);
+    tsin[jj * stride + col] = __sinf(r);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Batches of at most 64 rows: split-K over a cluster of two CTAs per head, so 128 SMs
+// stream W_q (the 64-CTA form above is bound by what one SM can pull in).  CTA rank r
+// runs the GEMM and the W_w GEMV over its half of the hidden dimension; rank 1 then ships
+// its TMEM partial sums and GEMV partials into rank 0's shared memory (DSMEM stores,
+// mbarrier handshakes at cluster scope), and rank 0 adds them and runs the RoPE epilogue.
+constexpr int kSplitN = 64;
+constexpr int kSplitStages = 8;
+constexpr int kSplitStage = kWTileBytes + kSplitN * kKChunk * 2;  // 24 KiB
+constexpr int kRecvStride = 68;  // floats per received row (16-byte reads on distinct banks)
+constexpr int kEarlyTabBytes = 2 * 32 * (kSplitN + 4) * 4;  // cos/sin table, rope_dim <= 64
+constexpr int kSplitSmem =
+    kSplitStages * (kSplitStage + kWwChunkBytes) + kBarrierBytes + kEarlyTabBytes + 1024;
+
+template <bool kBF16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    proj_splitk_kernel(const __grid_constant__ CUtensorMap wmap,
+                       const __grid_constant__ CUtensorMap xmap,
+                       const __grid_constant__ CUtensorMap wwmap, const ProjArgs a) {
+  constexpr int kN = kSplitN;
+  constexpr int kStages = kSplitStages;
+  constexpr int kStage = kSplitStage;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  float* ww_ring = reinterpret_cast<float*>(smem + kStages * kStage);  // [stages][64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * (kStage + kWwChunkBytes));
+  uint64_t* empty = full + kStages;
+  uint64_t* accfull = empty + kStages;
+  uint64_t* done = accfull + 1;
+  uint64_t* ready = done + 1;  // rank 1: rank 0's ring is free to receive
+  uint64_t* recv = ready + 1;  // rank 0: rank 1's partials have landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(recv + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* spos = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // [64]
+  float* sinv = spos + kN;                                                         // [64]
+  float* wpart = sinv + 64;  // [64] rank 1's GEMV partials (written remotely)
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int h = blockIdx.x >> 1;
+  const int nk = (a.hidden + kKChunk - 1) / kKChunk;
+  const int split = (nk + 1) >> 1;
+  const int kbeg = rank ? split : 0, kend = rank ? nk : split;
+  const int nloc = kend - kbeg;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 5);  // the MMA commit + one arrival per epilogue warp
+    }
+    mbar_init(accfull, 1);
+    mbar_init(done, 1);
+    mbar_init(ready, 128);
+    mbar_init(recv, 128);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&wmap);
+    prefetch_tmap(&xmap);
+    prefetch_tmap(&wwmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int it = 0;
+      for (; it < nloc; ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag)) break;
+        const int kc = kbeg + it;
+        uint8_t* dst = smem + s * kStage;
+        mbar_arrive_expect_tx(&full[s], kStage + kWwChunkBytes);
+        int wx, wy;
+        wq_coords(a, h, kc, nk, wx, wy);
+        tma_load_2d(dst, &wmap, &full[s], wx, wy, pol_w);
+        tma_load_2d(dst + kWTileBytes, &xmap, &full[s], kc * kKChunk, 0, pol_x);
+        tma_load_2d(ww_ring + s * kKChunk, &wwmap, &full[s], kc * kKChunk, h, pol_x);
+      }
+      volatile int no_abort = 0;
+      for (int s = 0; s < kStages && s < it; ++s) {
+        const int n = (it - s + kStages - 1) / kStages;
+        mbar_wait(&full[s], (n - 1) & 1u, &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ UMMA issuer
+      constexpr uint32_t idesc = umma_idesc_f16(kBF16, 128, kN);
+      for (int it = 0; it < nloc; ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(&full[s], (it / kStages) & 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t w_addr = smem_u32(smem + s * kStage);
+        const uint32_t x_addr = w_addr + kWTileBytes;
+#pragma unroll
+        for (int k = 0; k < kKChunk / 16; ++k) {
+          umma_f16(tmem_base, sw128_kmajor_desc(w_addr + k * 32),
+                   sw128_kmajor_desc(x_addr + k * 32), idesc, (it | k) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accfull);
+      umma_commit(done);
+      volatile int no_abort = 0;
+      mbar_wait(done, 0, &no_abort);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue warps
+    const int et = threadIdx.x - 64;  // 0..127
+    const int half = a.rope_dim >> 1;
+    constexpr int kTabStride = kN + 4;
+    // rope_dim <= 64: the cos/sin table has its own region and is built before the first
+    // stage lands (hidden behind the first loads); larger rope_dim builds it in the ring
+    // after the GEMM
+    const bool early = half <= 32;
+    float* etab = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
+    if (rank == 0) {
+      for (int i = et; i < kN; i += 128)
+        spos[i] = static_cast<float>(a.positions[min(i, a.batch - 1)]);
+      if (et < half) sinv[et] = powf(a.theta, -static_cast<float>(et) / static_cast<float>(half));
+      epi_barrier();
+      if (early) build_rope_table(spos, sinv, half, kN, kTabStride, etab, etab + 32 * kTabStride);
+    }
+    // (1) the W_w GEMV over this CTA's half of the hidden dimension (layout as above)
+    constexpr int kPer = kN / 16;
+    const int c = et & 7;
+    float part[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) part[i] = 0.f;
+    bool ok = true;
+    for (int it = 0; it < nloc; ++it) {
+      const int s = it % kStages;
+      if (!mbar_wait(&full[s], (it / kStages) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const float4 wa = *reinterpret_cast<const float4*>(ww_ring + s * kKChunk + c * 8);
+      const float4 wb = *reinterpret_cast<const float4*>(ww_ring + s * kKChunk + c * 8 + 4);
+      const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+      const uint8_t* xt = smem + s * kStage + kWTileBytes;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int r = (et + 128 * i) >> 3;
+        const uint4 v = *reinterpret_cast<const uint4*>(
+            xt + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        float acc = part[i];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(elem16<kBF16>(u[j >> 1], j & 1), wv[j], acc);
+        part[i] = acc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      float v = part[i];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      part[i] = v;  // the row sum (over this CTA's half) in the lanes with c == 0
+    }
+    const uint32_t quad = static_cast<uint32_t>(warp & 3);
+    const int d = static_cast<int>(quad) * 32 + lane;  // this thread's feature (TMEM lane)
+    float* rbuf = reinterpret_cast<float*>(smem);  // rank 0: [128][68] received partials
+    ok = ok && mbar_wait(accfull, 0, abort_flag);
+    if (rank == 1) {
+      // (2a) ship the GEMV row sums and the TMEM partials to rank 0
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int r = (et + 128 * i) >> 3;
+        if (c == 0) st_cluster_f32(mapa_shared(smem_u32(wpart + r), 0), part[i]);
+      }
+      if (ok && mbar_wait_cluster(ready, 0, abort_flag)) {
+        tc_fence_after();
+        const uint32_t dst = mapa_shared(smem_u32(rbuf + d * kRecvStride), 0);
+#pragma unroll 1
+        for (int c0 = 0; c0 < kN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((quad * 32u) << 16) + c0, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; t += 4) {
+            const float f0 = nloc ? __uint_as_float(r[t]) : 0.f;
+            const float f1 = nloc ? __uint_as_float(r[t + 1]) : 0.f;
+            const float f2 = nloc ? __uint_as_float(r[t + 2]) : 0.f;
+            const float f3 = nloc ? __uint_as_float(r[t + 3]) : 0.f;
+            st_cluster_v4(dst + (c0 + t) * 4, f0, f1, f2, f3);
+          }
+        }
+        tc_fence_before();
+      }
+      mbar_arrive_remote(mapa_shared(smem_u32(recv), 0));
+    } else {
+      // (2b) rank 0: tell rank 1 the ring is free, then the summed projection and the
+      // RoPE epilogue
+      mbar_arrive_remote(mapa_shared(smem_u32(ready), 1));
+      const bool j_ok = epi_all(ok && !*abort_flag);
+      const bool rot = d < a.rope_dim;
+      const int j = d < half ? d : d - half;
+      const int partner = d < half ? d + half : d - half;
+      float* ex = rbuf + 128 * kRecvStride;
+      float* tcos = early ? etab : ex + 128 * 36;
+      float* tsin = early ? etab + 32 * kTabStride : tcos + 64 * kTabStride;
+      uint16_t* ostage = reinterpret_cast<uint16_t*>(ex + 128 * 36 + 128 * kTabStride);
+      if (j_ok && !early) build_rope_table(spos, sinv, half, kN, kTabStride, tcos, tsin);
+      const bool got = j_ok && mbar_wait_cluster(recv, 0, abort_flag);
+      if (epi_all(got && !*abort_flag)) {
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int r = (et + 128 * i) >> 3;
+          if (c == 0 && r < a.batch)
+            a.w[static_cast<int64_t>(r) * a.w_stride + h] = (part[i] + wpart[r]) * a.scale;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c0 = 0; c0 < kN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((quad * 32u) << 16) + c0, r);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int t = 0; t < 32; t += 4) {
+            const float4 o = *reinterpret_cast<const float4*>(rbuf + d * kRecvStride + c0 + t);
+            float4 f;
+            f.x = v[t] = round16<kBF16>(__uint_as_float(r[t]) + o.x);
+            f.y = v[t + 1] = round16<kBF16>(__uint_as_float(r[t + 1]) + o.y);
+            f.z = v[t + 2] = round16<kBF16>(__uint_as_float(r[t + 2]) + o.z);
+            f.w = v[t + 3] = round16<kBF16>(__uint_as_float(r[t + 3]) + o.w);
+            *reinterpret_cast<float4*>(ex + d * 36 + t) = f;
+          }
+          epi_barrier();
+          for (int pass = 0; pass < (a.qraw ? 2 : 1); ++pass) {
+#pragma unroll
+            for (int t = 0; t < 32; t += 4) {
+              float o[4] = {v[t], v[t + 1], v[t + 2], v[t + 3]};
+              if (rot && pass == 0) {
+                const float4 ot = *reinterpret_cast<const float4*>(ex + partner * 36 + t);
+                const float4 cs = *reinterpret_cast<const float4*>(tcos + j * kTabStride + c0 + t);
+                const float4 sn = *reinterpret_cast<const float4*>(tsin + j * kTabStride + c0 + t);
+                const float oo[4] = {ot.x, ot.y, ot.z, ot.w};
+                const float cc[4] = {cs.x, cs.y, cs.z, cs.w};
+                const float ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                  o[u] = d < half ? o[u] * cc[u] - oo[u] * ss[u] : o[u] * cc[u] + oo[u] * ss[u];
+              }
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                ostage[(t + u) * 128 + d] = kBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o[u]))
+                                                  : __half_as_ushort(__float2half_rn(o[u]));
+            }
+            epi_barrier();
+            void* dst = pass == 0 ? a.q : a.qraw;
+            const int64_t stride = pass == 0 ? a.q_stride : a.qraw_stride;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int row = g * 8 + (et >> 4), ch = et & 15;
+              const int b = c0 + row;
+              if (b < a.batch) {
+                const uint4 val = *reinterpret_cast<const uint4*>(ostage + row * 128 + ch * 8);
+                *reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + b * stride + h * 128 +
+                                          ch * 8) = val;
+              }
+            }
+            epi_barrier();
+          }
+        }
+        tc_fence_before();
+      }
+    }
+  }
+
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its shared memory
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kN);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, TDSA_ERR_TIMEOUT);
+}
+
+template <bool kBF16>
+int launch_proj_splitk(const CUtensorMap& wmap, const CUtensorMap& xmap,
+                       const CUtensorMap& wwmap, const ProjArgs& a, cudaStream_t stream) {
+  auto kern = proj_splitk_kernel<kBF16>;
+  TDSA_CUDA_CHECK(
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem));
+  kern<<<dim3(2 * kHeads), kThreads, kSplitSmem, stream>>>(wmap, xmap, wwmap, a);
+  TDSA_CUDA_CHECK(cudaGetLastError());
+  return TDSA_OK;
+}
+
 template <bool kBF16, int kN>
 int launch_proj_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& wwmap,
                   const ProjArgs& a, cudaStream_t stream) {
@@ -382,7 +726,8 @@ int launch_proj_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtens
 }  // namespace
 
 int launch_query_project(const void* x, int64_t x_stride, int hidden, const void* wq,
-                         int64_t wq_stride, const float* ww, const int64_t* positions, void* q,
+                         int64_t wq_stride, int packed, const float* ww,
+                         const int64_t* positions, void* q,
                          int64_t q_stride, float* w, int64_t w_stride, int dtype, int batch,
                          int rope_dim, float theta, float scale, void* qraw,
                          int64_t qraw_stride, cudaStream_t stream, int* status) {
@@ -390,9 +735,12 @@ int launch_query_project(const void* x, int64_t x_stride, int hidden, const void
   const CUtensorMapDataType dt =
       dtype == TDSA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap wmap, xmap, wwmap;
+  const int nk = (hidden + kKChunk - 1) / kKChunk;
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(kHeads * 128)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(wq_stride) * 2};
+    // packed: one contiguous 16 KiB block per (head, K chunk) -- whole DRAM pages per tile
+    const uint64_t dims[2] = {static_cast<uint64_t>(packed ? kKChunk : hidden),
+                              static_cast<uint64_t>(kHeads * 128) * (packed ? nk : 1)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(packed ? kKChunk : wq_stride) * 2};
     const uint32_t box[2] = {kKChunk, 128};
     int rc = encode_tmap(&wmap, dt, 2, wq, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -426,15 +774,65 @@ int launch_query_project(const void* x, int64_t x_stride, int hidden, const void
   a.rope_dim = rope_dim;
   a.theta = theta;
   a.scale = scale;
-  a.stages = 0;
+  a.packed = packed;
   a.status = status;
   const bool bf16 = dtype == TDSA_BF16;
+  if (n == 64 && hidden > kKChunk)
+    return bf16 ? launch_proj_splitk<true>(wmap, xmap, wwmap, a, stream)
+                : launch_proj_splitk<false>(wmap, xmap, wwmap, a, stream);
   if (n == 64) return bf16 ? launch_proj_t<true, 64>(wmap, xmap, wwmap, a, stream)
                            : launch_proj_t<false, 64>(wmap, xmap, wwmap, a, stream);
   if (n == 128) return bf16 ? launch_proj_t<true, 128>(wmap, xmap, wwmap, a, stream)
                             : launch_proj_t<false, 128>(wmap, xmap, wwmap, a, stream);
   return bf16 ? launch_proj_t<true, 256>(wmap, xmap, wwmap, a, stream)
               : launch_proj_t<false, 256>(wmap, xmap, wwmap, a, stream);
+}
+
+namespace {
+
+// W_q [8192][hidden] (row stride `stride`) -> packed [64 heads][nk][128 rows][64]: the
+// (head, K chunk) tile the projection streams per stage becomes one contiguous 16 KiB
+// block; K past the hidden size is zero.  One thread per 16-byte chunk.
+__global__ void pack_wq_kernel(const uint16_t* __restrict__ wq, int64_t stride, int hidden,
+                               int nk, uint16_t* __restrict__ out) {
+  const int64_t total = static_cast<int64_t>(kHeads) * 128 * nk * 8;  // 16-byte chunks
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int ch = static_cast<int>(i & 7);       // chunk of 8 within the 64-wide row
+    const int64_t rest = i >> 3;
+    const int r = static_cast<int>(rest % 128);   // row within the head
+    const int64_t tile = rest / 128;              // h * nk + kc
+    const int kc = static_cast<int>(tile % nk);
+    const int h = static_cast<int>(tile / nk);
+    const int k0 = kc * 64 + ch * 8;
+    const uint16_t* src = wq + static_cast<int64_t>(h * 128 + r) * stride + k0;
+    uint16_t v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = k0 + j < hidden ? src[j] : uint16_t(0);
+    uint4 o;
+    o.x = v[0] | (static_cast<uint32_t>(v[1]) << 16);
+    o.y = v[2] | (static_cast<uint32_t>(v[3]) << 16);
+    o.z = v[4] | (static_cast<uint32_t>(v[5]) << 16);
+    o.w = v[6] | (static_cast<uint32_t>(v[7]) << 16);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+}  // namespace
+
+size_t packed_wq_bytes(int hidden) {
+  const size_t nk = static_cast<size_t>((hidden + kKChunk - 1) / kKChunk);
+  return static_cast<size_t>(kHeads) * 128 * nk * kKChunk * 2;
+}
+
+int launch_pack_wq(const void* wq, int64_t stride, int hidden, void* out, cudaStream_t stream) {
+  const int nk = (hidden + kKChunk - 1) / kKChunk;
+  const int64_t chunks = static_cast<int64_t>(kHeads) * 128 * nk * 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((chunks + 255) / 256, 148 * 16));
+  pack_wq_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint16_t*>(wq), stride, hidden,
+                                             nk, static_cast<uint16_t*>(out));
+  TDSA_CUDA_CHECK(cudaGetLastError());
+  return TDSA_OK;
 }
 
 }  // namespace tdsa

@@ -85,10 +85,12 @@ class QueryProjector:
     ``project(hidden, positions)`` -> (q [B,64,128], w [B,64] float32), written into
     ``self.q`` / ``self.w`` (stable addresses, so a ScoreTopkPlan can be built on them).
     keep_qraw=True also keeps the pre-RoPE projection in ``self.qraw`` [B, 8192].
+    packed=True (default) re-lays W_q out once (tdsa_pack_query_weights) so that every tile
+    the kernel streams is one contiguous block.
     """
 
     def __init__(self, wq: torch.Tensor, ww: torch.Tensor, batch: int, *, rope_dim: int = 64,
-                 rope_theta: float = 10_000.0, keep_qraw: bool = False):
+                 rope_theta: float = 10_000.0, keep_qraw: bool = False, packed: bool = True):
         require_cuda(wq, ww)
         if wq.shape[0] != HEADS * HEAD_DIM or ww.shape[0] != HEADS:
             raise ValueError("expected wq [8192, hidden] and ww [64, hidden]")
@@ -100,8 +102,20 @@ class QueryProjector:
             raise ValueError("the hidden size must be a multiple of 8")
         dev = wq.device
         self.hidden = wq.shape[1]
-        self.wq = wq if (wq.stride(-1) == 1 and wq.stride(0) % 8 == 0
-                         and wq.data_ptr() % 16 == 0) else wq.contiguous()
+        wq = wq if (wq.stride(-1) == 1 and wq.stride(0) % 8 == 0
+                    and wq.data_ptr() % 16 == 0) else wq.contiguous()
+        lib = capi.lib()
+        if packed:
+            # one-time re-layout: every (head, 64-wide K chunk) tile one contiguous block
+            nbytes = lib.tdsa_packed_query_weights_bytes(self.hidden)
+            self.wq = torch.empty(nbytes // 2, device=dev, dtype=wq.dtype)
+            capi.check(lib.tdsa_pack_query_weights(wq.data_ptr(), wq.stride(0), self.hidden,
+                                                   self.wq.data_ptr(),
+                                                   torch.cuda.current_stream(dev).cuda_stream))
+            self._wq_stride = 0
+        else:
+            self.wq, self._wq_stride = wq, wq.stride(0)
+        self.packed = bool(packed)
         self.ww = ww.to(torch.float32).contiguous()
         self.dtype = wq.dtype
         self.batch, self.rope_dim, self.theta = batch, rope_dim, rope_theta
@@ -120,7 +134,8 @@ class QueryProjector:
         if positions.dtype != torch.int64 or not positions.is_contiguous():
             positions = positions.to(torch.int64).contiguous()
         capi.check(self._fn(hidden.data_ptr(), hidden.stride(0), self.hidden, self.wq.data_ptr(),
-                            self.wq.stride(0), self.ww.data_ptr(), positions.data_ptr(),
+                            self._wq_stride, int(self.packed), self.ww.data_ptr(),
+                            positions.data_ptr(),
                             self.q.data_ptr(), HEADS * HEAD_DIM, self.w.data_ptr(), HEADS,
                             self._dt, self.batch, self.rope_dim, self.theta,
                             (HEADS * HEAD_DIM) ** -0.5,

@@ -253,6 +253,16 @@ int tdsa_relu_index_score(const double* q, const double* keys, const double* w, 
                           int dim, int tokens, double* out, void* stream);
 
 /*
+ * One-time re-layout of the W_q weight for tdsa_query_project (no reference counterpart:
+ * a weight-packing step): w_q [8192][hidden_size] 16-bit (row stride wq_row_stride) ->
+ * out [64 heads][ceil(hidden_size/64)][128][64], zero past hidden_size.  out holds
+ * tdsa_packed_query_weights_bytes(hidden_size) bytes, 16-byte aligned.
+ */
+size_t tdsa_packed_query_weights_bytes(int hidden_size);
+int tdsa_pack_query_weights(const void* w_q, int64_t wq_row_stride, int hidden_size,
+                            void* out, void* stream);
+
+/*
  * The whole decode-step query projection of the sidecar in one launch (replaces the
  * W_q GEMM + tdsa_query_prep pair): reference LightningIndexerSidecar.encode_queries,
  * src/temporal_dsa/sidecar.py:78-87.
@@ -264,10 +274,14 @@ int tdsa_relu_index_score(const double* q, const double* keys, const double* w, 
  * contiguous; positions [batch] int64.  q [batch][8192] (row stride q_stride), w [batch][64]
  * (row stride w_stride).  qraw: optional [batch][8192] output of the pre-RoPE projection
  * (NULL to skip).  hidden_size a multiple of 8; hidden, w_q, w_proj, q and qraw rows
- * 16-byte aligned.
+ * 16-byte aligned.  wq_packed != 0: w_q is the output of tdsa_pack_query_weights
+ * (wq_row_stride ignored) -- every tile the kernel streams is then one contiguous block,
+ * which HBM serves at full bandwidth; the row-major layout works but reads 128-byte
+ * pieces 4 KB apart.
  */
 int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_size,
-                       const void* w_q, int64_t wq_row_stride, const float* w_proj,
+                       const void* w_q, int64_t wq_row_stride, int wq_packed,
+                       const float* w_proj,
                        const int64_t* positions, void* q, int64_t q_stride, float* w,
                        int64_t w_stride, int dtype, int batch, int rope_dim, float rope_theta,
                        float weight_scale, void* qraw, int64_t qraw_stride, void* stream);

@@ -54,12 +54,14 @@ def _check_rope(q, qraw, pos, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("batch,hidden", [(3, 512), (64, 2048), (130, 1000), (300, 2048)])
-def test_query_project_matches_oracle(dtype, batch, hidden):
+@pytest.mark.parametrize("batch,hidden", [(3, 512), (64, 2048), (5, 64), (40, 1000), (130, 1000),
+                                          (300, 2048)])
+@pytest.mark.parametrize("packed", [True, False])
+def test_query_project_matches_oracle(dtype, batch, hidden, packed):
     from dsa_b200.sidecar import QueryProjector, encode_queries
 
     wq, ww, x, pos = _inputs(dtype, batch, hidden, seed=batch + hidden)
-    proj = QueryProjector(wq, ww, batch, keep_qraw=True)
+    proj = QueryProjector(wq, ww, batch, keep_qraw=True, packed=packed)
     q, w = proj.project(x, pos)
     x64 = x.double().cpu().numpy()
     # the GEMM output rounded once to the 16-bit dtype (accumulation order differs)
@@ -118,14 +120,14 @@ def test_query_project_rejects_bad_arguments():
 
     lib = capi.lib()
     # hidden size not a multiple of 8
-    rc = lib.tdsa_query_project(16, 12, 12, 16, 12, 16, 16, 16, 8192, 16, 64, capi.TDSA_BF16, 1,
-                                64, 1e4, 1.0, None, 0, None)
+    rc = lib.tdsa_query_project(16, 12, 12, 16, 12, 0, 16, 16, 16, 8192, 16, 64, capi.TDSA_BF16,
+                                1, 64, 1e4, 1.0, None, 0, None)
     assert rc == capi.TDSA_ERR_UNSUPPORTED
     # odd rope_dim
-    rc = lib.tdsa_query_project(16, 64, 64, 16, 64, 16, 16, 16, 8192, 16, 64, capi.TDSA_BF16, 1,
-                                63, 1e4, 1.0, None, 0, None)
+    rc = lib.tdsa_query_project(16, 64, 64, 16, 64, 0, 16, 16, 16, 8192, 16, 64, capi.TDSA_BF16,
+                                1, 63, 1e4, 1.0, None, 0, None)
     assert rc == capi.TDSA_ERR_INVALID
     # misaligned hidden pointer
-    rc = lib.tdsa_query_project(18, 64, 64, 16, 64, 16, 16, 16, 8192, 16, 64, capi.TDSA_BF16, 1,
-                                64, 1e4, 1.0, None, 0, None)
+    rc = lib.tdsa_query_project(18, 64, 64, 16, 64, 0, 16, 16, 16, 8192, 16, 64, capi.TDSA_BF16,
+                                1, 64, 1e4, 1.0, None, 0, None)
     assert rc == capi.TDSA_ERR_ALIGN
