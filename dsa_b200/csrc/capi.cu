@@ -410,6 +410,14 @@ int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,
                       weight_scale, static_cast<cudaStream_t>(stream));
 }
 
+int tdsa_selftest_bounded_wait(long long limit_cycles, void* stream) {
+  if (limit_cycles < 0 || limit_cycles > 4000000000LL)
+    return fail(TDSA_ERR_INVALID, "limit_cycles must be in [0, 4e9]");
+  int* status = device_status_ptr();
+  if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  return launch_bounded_wait_selftest(limit_cycles, static_cast<cudaStream_t>(stream), status);
+}
+
 size_t tdsa_packed_query_weights_bytes(int hidden_size) {
   if (hidden_size < 8 || hidden_size > 65536 || hidden_size % 8) return 0;
   return packed_wq_bytes(hidden_size);

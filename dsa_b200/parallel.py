@@ -58,7 +58,10 @@ def local_candidates(queries: torch.Tensor, weights: torch.Tensor, keys_shard: t
 
 def gather_candidates(values: torch.Tensor, indices: torch.Tensor,
                       group: dist.ProcessGroup | None = None) -> Candidates:
-    """All-gather [B, k] candidate lists of every rank -> [B, world * k], rank-major."""
+    """All-gather [B, k] candidate lists of every rank -> [B, world * k], rank-major.
+    Without an initialized process group (one process) the lists are returned as they are."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return values, indices
     world = dist.get_world_size(group)
     vs = [torch.empty_like(values) for _ in range(world)]
     js = [torch.empty_like(indices) for _ in range(world)]

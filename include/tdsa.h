@@ -34,6 +34,15 @@ enum tdsa_status {
 
 enum tdsa_dtype { TDSA_F32 = 0, TDSA_F16 = 1, TDSA_BF16 = 2 };
 
+/*
+ * Failure-path self-test (no reference counterpart): one kernel waits on an mbarrier that
+ * nothing arrives on, with the same bounded loop every in-kernel wait of this library
+ * uses but a limit of `limit_cycles` SM cycles; when the limit runs out it raises
+ * TDSA_ERR_TIMEOUT in the device status word (read it with tdsa_device_status) and
+ * returns.  The context stays usable.  Asynchronous on `stream`.
+ */
+int tdsa_selftest_bounded_wait(long long limit_cycles, void* stream);
+
 /* Library version string. */
 const char* tdsa_version(void);
 
