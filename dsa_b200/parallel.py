@@ -95,3 +95,51 @@ class LShardedTopK:
             return self.merge_fn(all_v, all_i, self.k, self.sorted)
         idx, val = merge_topk(all_v, all_i, self.k, sorted=self.sorted)
         return idx, val
+
+
+class LShardedPlan:
+    """The L-sharded top-k on fixed buffers (the decode-loop form of ``LShardedTopK``).
+
+    Per ``run()``: dense score + unsorted top-k of this rank's keys (``ScoreTopkPlan``),
+    global indices, ONE all-gather of the packed (value bits, index) candidates, a
+    rank-major -> row-major copy, and the merge.  The caller rewrites ``queries`` /
+    ``weights`` in place between steps."""
+
+    def __init__(self, queries: torch.Tensor, weights: torch.Tensor, keys_shard: torch.Tensor,
+                 k: int, offset: int, *, sorted: bool = True,
+                 group: dist.ProcessGroup | None = None):
+        from .indexer import ScoreTopkPlan
+
+        if keys_shard.shape[-2] < k:
+            raise ValueError(f"every shard needs at least k={k} keys")
+        self.plan = ScoreTopkPlan(queries, weights, keys_shard, k, sorted=False,
+                                  index_dtype=torch.int32)
+        self.k, self.offset, self.sorted, self.group = k, int(offset), bool(sorted), group
+        self.world = (dist.get_world_size(group)
+                      if dist.is_available() and dist.is_initialized() else 1)
+        b, dev = self.plan.batch, keys_shard.device
+        self.send = torch.empty(2, b, k, device=dev, dtype=torch.int32)
+        self.recv = torch.empty(self.world, 2, b, k, device=dev, dtype=torch.int32)
+        self.cand = torch.empty(2, b, self.world, k, device=dev, dtype=torch.int32)
+        self.indices = torch.empty(b, k, device=dev, dtype=torch.int64)
+        self.values = torch.empty(b, k, device=dev, dtype=torch.float32)
+
+    def run(self) -> tuple[torch.Tensor, torch.Tensor]:
+        from . import _capi as capi
+        from .indexer import stream_ptr
+
+        self.plan.run()
+        self.send[0].copy_(self.plan.values.view(torch.int32))
+        torch.add(self.plan.indices, self.offset, out=self.send[1])
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        else:
+            self.recv[0].copy_(self.send)
+        self.cand.copy_(self.recv.permute(1, 2, 0, 3))
+        b, count = self.plan.batch, self.world * self.k
+        vals = self.cand[0].view(torch.float32).view(b, count)
+        idx = self.cand[1].view(b, count)
+        capi.call("tdsa_merge_topk", vals.data_ptr(), idx.data_ptr(), count, b, count, self.k,
+                  int(self.sorted), self.indices.data_ptr(), 8, self.indices.stride(0),
+                  self.values.data_ptr(), self.values.stride(0), stream_ptr(vals.device))
+        return self.indices, self.values

@@ -16,7 +16,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
 from dsa_b200 import scores_topk  # noqa: E402
-from dsa_b200.parallel import LShardedTopK, shard_bounds  # noqa: E402
+from dsa_b200.parallel import LShardedPlan, LShardedTopK, shard_bounds  # noqa: E402
 
 
 def main() -> None:
@@ -35,11 +35,14 @@ def main() -> None:
         dev = torch.device("cuda", torch.cuda.current_device())
         shard = keys[:, start:stop].contiguous().to(dev)
         idx, val = LShardedTopK(k, sorted=True)(q.to(dev), w.to(dev), shard, start)
+        plan = LShardedPlan(q.to(dev), w.to(dev), shard, k, start, sorted=True)
+        pidx, pval = plan.run()
         torch.cuda.synchronize()
         if rank == 0:
             want_i, want_v = scores_topk(q.to(dev), w.to(dev), keys.to(dev), k, sorted=True,
                                          index_dtype=torch.int64)
-            ok = torch.equal(idx, want_i) and torch.equal(val, want_v)
+            ok = (torch.equal(idx, want_i) and torch.equal(val, want_v)
+                  and torch.equal(pidx, want_i) and torch.equal(pval, want_v))
             with open(out_path, "w") as f:
                 f.write("OK" if ok else f"MISMATCH {int((idx != want_i).sum())} indices")
         dist.barrier()

@@ -58,6 +58,23 @@ def test_shard_local_topk_and_merge_equal_whole_row(world):
     np.testing.assert_array_equal(idx.cpu().numpy(), oracle.topk_rows(s, k)[0])
 
 
+def test_l_sharded_plan_single_process_equals_whole_row():
+    """LShardedPlan with one rank (no process group): local top-k, packing and merge."""
+    from dsa_b200 import scores_topk
+    from dsa_b200.parallel import LShardedPlan
+
+    gen = torch.Generator().manual_seed(3)
+    b, length, k = 3, 50000, 2048
+    q = (torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)).to(torch.bfloat16).cuda()
+    w = (torch.randn(b, 64, generator=gen) / 8).cuda()
+    keys = torch.randn(b, length, 128, generator=gen).to(torch.bfloat16).cuda()
+    plan = LShardedPlan(q, w, keys, k, 0, sorted=True)
+    for _ in range(2):
+        idx, val = plan.run()
+        want_i, want_v = scores_topk(q, w, keys, k, sorted=True, index_dtype=torch.int64)
+        assert torch.equal(idx, want_i) and torch.equal(val, want_v)
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
 def test_l_sharded_topk_two_nccl_ranks(tmp_path):
