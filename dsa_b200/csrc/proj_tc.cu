@@ -406,17 +406,21 @@ __device__ __forceinline__ void build_rope_table(const float* spos, const float*
 
 // ---------------------------------------------------------------------------------
 // Batches of at most 64 rows: split-K over a cluster of two CTAs per head, so 128 SMs
-// stream W_q (the 64-CTA form above is bound by what one SM can pull in).  CTA rank r
-// runs the GEMM and the W_w GEMV over its half of the hidden dimension; rank 1 then ships
-// its TMEM partial sums and GEMV partials into rank 0's shared memory (DSMEM stores,
-// mbarrier handshakes at cluster scope), and rank 0 adds them and runs the RoPE epilogue.
+// stream W_q.  CTA rank r runs the GEMM and the W_w GEMV over its half of the hidden
+// dimension, then the pair splits the epilogue by batch column: each rank ships the
+// peer's 32 columns of its TMEM partial sums (and the peer's GEMV row sums) with one DSMEM
+// bulk copy into the peer's receive region, adds what it received to its own half, and
+// runs the RoPE epilogue and stores for that half.
 constexpr int kSplitN = 64;
-constexpr int kSplitStages = 8;
+constexpr int kSplitStages = 7;
 constexpr int kSplitStage = kWTileBytes + kSplitN * kKChunk * 2;  // 24 KiB
-constexpr int kRecvStride = 68;  // floats per received row (16-byte reads on distinct banks)
+constexpr int kRecvStride = 36;  // floats per received row (16-byte reads on distinct banks)
 constexpr int kEarlyTabBytes = 2 * 32 * (kSplitN + 4) * 4;  // cos/sin table, rope_dim <= 64
-constexpr int kSplitSmem =
-    kSplitStages * (kSplitStage + kWwChunkBytes) + kBarrierBytes + kEarlyTabBytes + 1024;
+// the peer's partial sums for this rank's 32 columns [128][36] f32, then its 32 GEMV row
+// sums of this rank's rows
+constexpr int kRecvBytes = (128 * kRecvStride + kSplitN / 2) * 4;
+constexpr int kSplitSmem = kSplitStages * (kSplitStage + kWwChunkBytes) + kBarrierBytes +
+                           kEarlyTabBytes + kRecvBytes + 1024;
 
 template <bool kBF16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -433,13 +437,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* accfull = empty + kStages;
   uint64_t* done = accfull + 1;
-  uint64_t* ready = done + 1;  // rank 1: rank 0's ring is free to receive
-  uint64_t* recv = ready + 1;  // rank 0: rank 1's partials have landed
+  uint64_t* recv = done + 1;  // the peer's partials have landed (bulk copy tx)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(recv + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* spos = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // [64]
   float* sinv = spos + kN;                                                         // [64]
-  float* wpart = sinv + 64;  // [64] rank 1's GEMV partials (written remotely)
+  // the peer's partials for this rank's columns (its own region, so the peer ships them as
+  // soon as its GEMM is done); each rank stages what it sends in its own ring
+  float* recv_buf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes +
+                                             kEarlyTabBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -457,8 +463,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     mbar_init(accfull, 1);
     mbar_init(done, 1);
-    mbar_init(ready, 128);
-    mbar_init(recv, 128);
+    mbar_init(recv, 1);
+    mbar_arrive_expect_tx(recv, kRecvBytes);  // completes when the peer's copy has landed
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -533,7 +539,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // after the GEMM
     const bool early = half <= 32;
     float* etab = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
-    if (rank == 0) {
+    {
       for (int i = et; i < kN; i += 128)
         spos[i] = static_cast<float>(a.positions[min(i, a.batch - 1)]);
       if (et < half) sinv[et] = powf(a.theta, -static_cast<float>(et) / static_cast<float>(half));
@@ -581,111 +587,115 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     const uint32_t quad = static_cast<uint32_t>(warp & 3);
     const int d = static_cast<int>(quad) * 32 + lane;  // this thread's feature (TMEM lane)
-    float* rbuf = reinterpret_cast<float*>(smem);  // rank 0: [128][68] received partials
-    ok = ok && mbar_wait(accfull, 0, abort_flag);
-    if (rank == 1) {
-      // (2a) ship the GEMV row sums and the TMEM partials to rank 0
+    // (2) the pair shares the epilogue: rank r finishes batch columns [32r, 32r + 32).
+    // Each rank stages the OTHER half of its partial sums (TMEM columns) and the GEMV row
+    // sums of the other half's rows in its own ring (idle after its GEMM), and one bulk
+    // copy moves them into the peer's receive region, completing on the peer's mbarrier.
+    constexpr int kHalf = kN / 2;
+    const int my0 = static_cast<int>(rank) * kHalf, peer0 = kHalf - my0;
+    // every epilogue warp is past its last read of the ring (the GEMV) before the ring is
+    // reused for staging; the MMA commit alone does not order those reads
+    ok = epi_all(ok) && mbar_wait(accfull, 0, abort_flag);
+    float* stage = reinterpret_cast<float*>(smem);
+    if (ok) {
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld32(tmem_base + ((quad * 32u) << 16) + peer0, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int t = 0; t < 32; t += 4) {
+        float4 f;
+        f.x = __uint_as_float(r[t]);
+        f.y = __uint_as_float(r[t + 1]);
+        f.z = __uint_as_float(r[t + 2]);
+        f.w = __uint_as_float(r[t + 3]);
+        *reinterpret_cast<float4*>(stage + d * kRecvStride + t) = f;
+      }
+      tc_fence_before();
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
-        const int r = (et + 128 * i) >> 3;
-        if (c == 0) st_cluster_f32(mapa_shared(smem_u32(wpart + r), 0), part[i]);
+        const int row = (et + 128 * i) >> 3;
+        if (c == 0 && row >= peer0 && row < peer0 + kHalf)
+          stage[128 * kRecvStride + row - peer0] = part[i];
       }
-      if (ok && mbar_wait_cluster(ready, 0, abort_flag)) {
-        tc_fence_after();
-        const uint32_t dst = mapa_shared(smem_u32(rbuf + d * kRecvStride), 0);
-#pragma unroll 1
-        for (int c0 = 0; c0 < kN; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tmem_base + ((quad * 32u) << 16) + c0, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int t = 0; t < 32; t += 4) {
-            const float f0 = nloc ? __uint_as_float(r[t]) : 0.f;
-            const float f1 = nloc ? __uint_as_float(r[t + 1]) : 0.f;
-            const float f2 = nloc ? __uint_as_float(r[t + 2]) : 0.f;
-            const float f3 = nloc ? __uint_as_float(r[t + 3]) : 0.f;
-            st_cluster_v4(dst + (c0 + t) * 4, f0, f1, f2, f3);
-          }
-        }
-        tc_fence_before();
-      }
-      mbar_arrive_remote(mapa_shared(smem_u32(recv), 0));
-    } else {
-      // (2b) rank 0: tell rank 1 the ring is free, then the summed projection and the
-      // RoPE epilogue
-      mbar_arrive_remote(mapa_shared(smem_u32(ready), 1));
-      const bool j_ok = epi_all(ok && !*abort_flag);
+    }
+    fence_proxy_async_smem();
+    if (epi_all(ok && !*abort_flag) && et == 0)
+      bulk_copy_to_peer(mapa_shared(smem_u32(recv_buf), rank ^ 1u), stage, kRecvBytes,
+                        mapa_shared(smem_u32(recv), rank ^ 1u));
+    {
       const bool rot = d < a.rope_dim;
       const int j = d < half ? d : d - half;
       const int partner = d < half ? d + half : d - half;
-      float* ex = rbuf + 128 * kRecvStride;
+      // the ring past the outgoing stage: exchange rows, late cos/sin table, output staging
+      float* ex = stage + 128 * kRecvStride + kHalf;
       float* tcos = early ? etab : ex + 128 * 36;
       float* tsin = early ? etab + 32 * kTabStride : tcos + 64 * kTabStride;
       uint16_t* ostage = reinterpret_cast<uint16_t*>(ex + 128 * 36 + 128 * kTabStride);
+      const bool j_ok = epi_all(ok && !*abort_flag);
       if (j_ok && !early) build_rope_table(spos, sinv, half, kN, kTabStride, tcos, tsin);
       const bool got = j_ok && mbar_wait_cluster(recv, 0, abort_flag);
       if (epi_all(got && !*abort_flag)) {
+        const float* rbuf = recv_buf;
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
-          const int r = (et + 128 * i) >> 3;
-          if (c == 0 && r < a.batch)
-            a.w[static_cast<int64_t>(r) * a.w_stride + h] = (part[i] + wpart[r]) * a.scale;
+          const int row = (et + 128 * i) >> 3;
+          if (c == 0 && row >= my0 && row < my0 + kHalf && row < a.batch)
+            a.w[static_cast<int64_t>(row) * a.w_stride + h] =
+                (part[i] + rbuf[128 * kRecvStride + row - my0]) * a.scale;
         }
         tc_fence_after();
-#pragma unroll 1
-        for (int c0 = 0; c0 < kN; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tmem_base + ((quad * 32u) << 16) + c0, r);
-          tmem_wait_ld();
-          float v[32];
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((quad * 32u) << 16) + my0, r);
+        tmem_wait_ld();
+        float v[32];
 #pragma unroll
-          for (int t = 0; t < 32; t += 4) {
-            const float4 o = *reinterpret_cast<const float4*>(rbuf + d * kRecvStride + c0 + t);
-            float4 f;
-            f.x = v[t] = round16<kBF16>(__uint_as_float(r[t]) + o.x);
-            f.y = v[t + 1] = round16<kBF16>(__uint_as_float(r[t + 1]) + o.y);
-            f.z = v[t + 2] = round16<kBF16>(__uint_as_float(r[t + 2]) + o.z);
-            f.w = v[t + 3] = round16<kBF16>(__uint_as_float(r[t + 3]) + o.w);
-            *reinterpret_cast<float4*>(ex + d * 36 + t) = f;
-          }
-          epi_barrier();
-          for (int pass = 0; pass < (a.qraw ? 2 : 1); ++pass) {
-#pragma unroll
-            for (int t = 0; t < 32; t += 4) {
-              float o[4] = {v[t], v[t + 1], v[t + 2], v[t + 3]};
-              if (rot && pass == 0) {
-                const float4 ot = *reinterpret_cast<const float4*>(ex + partner * 36 + t);
-                const float4 cs = *reinterpret_cast<const float4*>(tcos + j * kTabStride + c0 + t);
-                const float4 sn = *reinterpret_cast<const float4*>(tsin + j * kTabStride + c0 + t);
-                const float oo[4] = {ot.x, ot.y, ot.z, ot.w};
-                const float cc[4] = {cs.x, cs.y, cs.z, cs.w};
-                const float ss[4] = {sn.x, sn.y, sn.z, sn.w};
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                  o[u] = d < half ? o[u] * cc[u] - oo[u] * ss[u] : o[u] * cc[u] + oo[u] * ss[u];
-              }
-#pragma unroll
-              for (int u = 0; u < 4; ++u)
-                ostage[(t + u) * 128 + d] = kBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o[u]))
-                                                  : __half_as_ushort(__float2half_rn(o[u]));
-            }
-            epi_barrier();
-            void* dst = pass == 0 ? a.q : a.qraw;
-            const int64_t stride = pass == 0 ? a.q_stride : a.qraw_stride;
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int row = g * 8 + (et >> 4), ch = et & 15;
-              const int b = c0 + row;
-              if (b < a.batch) {
-                const uint4 val = *reinterpret_cast<const uint4*>(ostage + row * 128 + ch * 8);
-                *reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + b * stride + h * 128 +
-                                          ch * 8) = val;
-              }
-            }
-            epi_barrier();
-          }
+        for (int t = 0; t < 32; t += 4) {
+          const float4 o = *reinterpret_cast<const float4*>(rbuf + d * kRecvStride + t);
+          float4 f;
+          f.x = v[t] = round16<kBF16>(__uint_as_float(r[t]) + o.x);
+          f.y = v[t + 1] = round16<kBF16>(__uint_as_float(r[t + 1]) + o.y);
+          f.z = v[t + 2] = round16<kBF16>(__uint_as_float(r[t + 2]) + o.z);
+          f.w = v[t + 3] = round16<kBF16>(__uint_as_float(r[t + 3]) + o.w);
+          *reinterpret_cast<float4*>(ex + d * 36 + t) = f;
         }
         tc_fence_before();
+        epi_barrier();
+        for (int pass = 0; pass < (a.qraw ? 2 : 1); ++pass) {
+#pragma unroll
+          for (int t = 0; t < 32; t += 4) {
+            float o[4] = {v[t], v[t + 1], v[t + 2], v[t + 3]};
+            if (rot && pass == 0) {
+              const float4 ot = *reinterpret_cast<const float4*>(ex + partner * 36 + t);
+              const float4 cs = *reinterpret_cast<const float4*>(tcos + j * kTabStride + my0 + t);
+              const float4 sn = *reinterpret_cast<const float4*>(tsin + j * kTabStride + my0 + t);
+              const float oo[4] = {ot.x, ot.y, ot.z, ot.w};
+              const float cc[4] = {cs.x, cs.y, cs.z, cs.w};
+              const float ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                o[u] = d < half ? o[u] * cc[u] - oo[u] * ss[u] : o[u] * cc[u] + oo[u] * ss[u];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              ostage[(t + u) * 128 + d] = kBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o[u]))
+                                                : __half_as_ushort(__float2half_rn(o[u]));
+          }
+          epi_barrier();
+          void* dst = pass == 0 ? a.q : a.qraw;
+          const int64_t stride = pass == 0 ? a.q_stride : a.qraw_stride;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int row = g * 8 + (et >> 4), ch = et & 15;
+            const int b = my0 + row;
+            if (b < a.batch) {
+              const uint4 val = *reinterpret_cast<const uint4*>(ostage + row * 128 + ch * 8);
+              *reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + b * stride + h * 128 +
+                                        ch * 8) = val;
+            }
+          }
+          epi_barrier();
+        }
       }
     }
   }

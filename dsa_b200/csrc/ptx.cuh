@@ -124,6 +124,24 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
+// Bulk copy of this CTA's shared memory into another CTA's (dst and the destination's
+// mbarrier given as shared::cluster addresses); completes as tx bytes on that mbarrier.
+// 16-byte aligned addresses, size a multiple of 16.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const void* src,
+                                                  uint32_t bytes, uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads
+// (bulk copies) of them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Every thread of every CTA of the cluster (a hardware barrier, like __syncthreads).
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile(
