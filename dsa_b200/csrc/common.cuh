@@ -47,6 +47,24 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 
 inline int elem_bytes(int dtype) { return dtype == TDSA_F32 ? 4 : 2; }
 
+// Launch with programmatic stream serialization: the kernel may start while its
+// predecessor on the stream drains, and synchronises itself with pdl_wait (ptx.cuh).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 #define TDSA_CUDA_CHECK(expr)                                                          \
   do {                                                                                 \
     cudaError_t _e = (expr);                                                           \

@@ -177,6 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = gemm ? *tmem_holder : 0u;
+  pdl_wait();  // hidden states and positions may come from the previous kernel
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -482,6 +484,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();  // hidden states and positions may come from the previous kernel
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -716,7 +720,8 @@ int launch_proj_splitk(const CUtensorMap& wmap, const CUtensorMap& xmap,
   auto kern = proj_splitk_kernel<kBF16>;
   TDSA_CUDA_CHECK(
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem));
-  kern<<<dim3(2 * kHeads), kThreads, kSplitSmem, stream>>>(wmap, xmap, wwmap, a);
+  TDSA_CUDA_CHECK(launch_pdl(kern, dim3(2 * kHeads), dim3(kThreads), kSplitSmem, stream, wmap,
+                             xmap, wwmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }
@@ -728,7 +733,7 @@ int launch_proj_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtens
   constexpr int smem = smem_bytes<kN>();
   TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const dim3 grid(2 * kHeads, (a.batch + kN - 1) / kN);
-  kern<<<grid, kThreads, smem, stream>>>(wmap, xmap, wwmap, a);
+  TDSA_CUDA_CHECK(launch_pdl(kern, grid, dim3(kThreads), smem, stream, wmap, xmap, wwmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }

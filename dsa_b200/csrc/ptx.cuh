@@ -65,6 +65,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch (kernels launched with launch_pdl): the prologue before
+// pdl_wait (barrier init, TMEM allocation, tensor-map prefetch) overlaps the previous
+// kernel's tail; pdl_wait returns once the grids this one depends on have completed and
+// their writes are visible (immediately for a normal launch).  pdl_launch_dependents,
+// issued after pdl_wait, lets the next such kernel start its own prologue -- never earlier,
+// so a kernel overlaps only its direct predecessor.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- clusters / DSMEM
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

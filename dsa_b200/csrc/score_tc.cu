@@ -113,6 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();  // q, w and the histogram may come from the previous kernel
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -301,7 +303,8 @@ int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
   const int smem = kSmemBytes + (hist ? kHistBytes : 0);
   auto kern = hist ? score_dense_tc_kernel<kBF16, true> : score_dense_tc_kernel<kBF16, false>;
   TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  kern<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(kmap, qmap, a);
+  TDSA_CUDA_CHECK(launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem,
+                             stream, kmap, qmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }

@@ -205,6 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   }
   for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
   __syncthreads();
+  pdl_wait();  // the scores and the histogram come from the previous kernel
+  pdl_launch_dependents();
   if (bulk) {
     if (tid == 0) {
       for (int c = 0; c < npieces; ++c) {
@@ -557,7 +559,7 @@ int launch_segments(TopkArgs a, int rows, int nseg, cudaStream_t stream) {
   auto run = [&](auto kern) -> int {
     TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem)));
-    kern<<<dim3(nseg, rows), kThreads, smem, stream>>>(a);
+    TDSA_CUDA_CHECK(launch_pdl(kern, dim3(nseg, rows), dim3(kThreads), smem, stream, a));
     TDSA_CUDA_CHECK(cudaGetLastError());
     return TDSA_OK;
   };
