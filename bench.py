@@ -196,7 +196,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     score_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
     launches = {"n": 0}
 
-    def step(record: bool):
+    def step(record: bool, count: bool = False):
         for layer in range(wl.layers):
             proj[layer].project(wl.x[layer], wl.qpos)
             if record:
@@ -207,6 +207,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             if record:
                 e1.record(stream)
                 score_events.append((e0, e1))
+            if count:
                 launches["n"] += 1 + plans[layer].launches_per_run
             plans[layer].select()
 
@@ -232,13 +233,19 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     with ClockSampler(device.index) as clocks:
         start.record(stream)
         for _ in range(args.steps):
-            step(True)
+            step(False, count=True)
         end.record(stream)
         torch.cuda.synchronize(device)
     torch.cuda.nvtx.range_pop()
     barrier()
     torch.cuda.synchronize(device)
     ms_step = max_over_ranks(start.elapsed_time(end) / args.steps)
+    # The score kernel's own launch duration for the roofline: the same steps again, with
+    # CUDA events on the stream around every score launch (kept out of the timed region
+    # above: an event between two launches stops the second from starting early).
+    for _ in range(min(args.steps, 20)):
+        step(True)
+    torch.cuda.synchronize(device)
     score_ms = statistics.fmean(a.elapsed_time(b) for a, b in score_events)
     score_ms = max_over_ranks(score_ms)
 

@@ -24,6 +24,7 @@ namespace {
 
 constexpr int kTileKeys = 128;
 constexpr int kStages = 5;
+constexpr int kQSlots = 2;  // q buffers: the next sequence's q loads while the MMA uses one
 constexpr int kStageBytes = kTileKeys * kHeadDim * 2;  // 32 KiB
 constexpr int kHalfBytes = kStageBytes / 2;            // 128 rows x 128 B
 constexpr int kQBytes = kHeads * kHeadDim * 2;         // 16 KiB
@@ -32,7 +33,7 @@ constexpr int kAccBufs = 2;
 constexpr int kTmemCols = 128;
 constexpr int kThreads = 192;
 constexpr int kBarrierBytes = 1024;
-constexpr int kSmemBytes = kStages * kStageBytes + 2 * kQBytes + kBarrierBytes + 1024;
+constexpr int kSmemBytes = kStages * kStageBytes + kQSlots * kQBytes + kBarrierBytes + 1024;
 constexpr int kHistBins = 4096;  // key histogram bins (top 12 bits of the order-preserving key)
 constexpr int kHistBytes = kHistBins * 4;
 
@@ -63,7 +64,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* stage_base = smem;
   uint8_t* q_base = smem + kStages * kStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(q_base + 2 * kQBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(q_base + kQSlots * kQBytes);
   uint64_t* empty = full + kStages;
   uint64_t* qfull = empty + kStages;
   uint64_t* qempty = qfull + 2;
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = static_cast<int>(t / tps);
         const int tt = static_cast<int>(t - static_cast<int64_t>(b) * tps);
         if (b != prev_b) {
-          const uint32_t slot = qcount & 1u, ph = (qcount >> 1) & 1u;
+          const uint32_t slot = qcount % kQSlots, ph = (qcount / kQSlots) & 1u;
           if (!mbar_wait(&qempty[slot], ph ^ 1u, abort_flag)) break;
           mbar_arrive_expect_tx(&qfull[slot], kQBytes);
           uint8_t* qd = q_base + slot * kQBytes;
@@ -150,8 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t n = (it - s + kStages - 1) / kStages;  // loads issued into stage s
         mbar_wait(&full[s], (n - 1) & 1u, &no_abort);
       }
-      for (uint32_t s = 0; s < 2 && s < qcount; ++s) {
-        const uint32_t n = (qcount - s + 1) / 2;
+      for (uint32_t s = 0; s < kQSlots && s < qcount; ++s) {
+        const uint32_t n = (qcount - s + kQSlots - 1) / kQSlots;
         mbar_wait(&qfull[s], (n - 1) & 1u, &no_abort);
       }
     }
@@ -165,8 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = static_cast<int>(t / tps);
         if (b != prev_b) {
           if (prev_b >= 0) umma_commit(&qempty[slot]);
-          slot = qcount & 1u;
-          if (!mbar_wait(&qfull[slot], (qcount >> 1) & 1u, abort_flag)) break;
+          slot = qcount % kQSlots;
+          if (!mbar_wait(&qfull[slot], (qcount / kQSlots) & 1u, abort_flag)) break;
           ++qcount;
           prev_b = b;
         }
