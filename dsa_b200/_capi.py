@@ -45,6 +45,9 @@ SIGNATURES: dict[str, tuple] = {
                                  i32, C.c_float, C.c_float, vp, i64, vp]),
     "tdsa_packed_query_weights_bytes": (sz, [i32]),
     "tdsa_selftest_bounded_wait": (i32, [C.c_longlong, vp]),
+    "tdsa_hadamard128": (i32, [vp, i64, i64, i32, vp, i64, vp]),
+    "tdsa_select_quantize": (i32, [vp, i64, i64, i32, i32, vp, i32, C.c_double, vp, vp, i64,
+                                   vp]),
     "tdsa_pack_query_weights": (i32, [vp, i64, i32, vp, vp]),
     "tdsa_score_dense_hist": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
                                     vp]),

@@ -410,6 +410,39 @@ int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,
                       weight_scale, static_cast<cudaStream_t>(stream));
 }
 
+int tdsa_hadamard128(const void* in, int64_t in_row_stride, int64_t rows, int dtype, void* out,
+                     int64_t out_row_stride, void* stream) {
+  if (rows < 0) return fail(TDSA_ERR_INVALID, "rows must be >= 0");
+  if (rows == 0) return TDSA_OK;
+  if (!in || !out) return fail(TDSA_ERR_INVALID, "null pointer");
+  if (dtype != TDSA_F32 && dtype != TDSA_BF16 && dtype != TDSA_F16)
+    return fail(TDSA_ERR_INVALID, "unknown dtype");
+  if (rows > 1 && (in_row_stride < 128 || out_row_stride < 128))
+    return fail(TDSA_ERR_INVALID, "row strides must be >= 128");
+  return launch_hadamard128(in, in_row_stride, rows, dtype, out, out_row_stride,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_select_quantize(const void* in, int64_t in_row_stride, int64_t rows, int width,
+                         int dtype, const int8_t* keep, int bits, double scale,
+                         uint32_t* absmax_word, void* out, int64_t out_row_stride,
+                         void* stream) {
+  if (rows < 0 || width < 1) return fail(TDSA_ERR_INVALID, "rows >= 0 and width >= 1");
+  if (rows == 0) return TDSA_OK;
+  if (!in || !out) return fail(TDSA_ERR_INVALID, "null pointer");
+  if (dtype != TDSA_F32 && dtype != TDSA_BF16 && dtype != TDSA_F16)
+    return fail(TDSA_ERR_INVALID, "unknown dtype");
+  if (bits != 0 && bits != 2 && bits != 4 && bits != 8)
+    return fail(TDSA_ERR_INVALID, "bits must be one of 2, 4, 8 (or 0: no quantization)");
+  if (bits && scale <= 0.0 && !absmax_word)
+    return fail(TDSA_ERR_INVALID, "a computed scale needs absmax_word");
+  if (rows > 1 && (in_row_stride < width || out_row_stride < width))
+    return fail(TDSA_ERR_INVALID, "row strides must be >= width");
+  return launch_select_quantize(in, in_row_stride, rows, width, dtype, keep, bits, scale,
+                                absmax_word, out, out_row_stride,
+                                static_cast<cudaStream_t>(stream));
+}
+
 int tdsa_selftest_bounded_wait(long long limit_cycles, void* stream) {
   if (limit_cycles < 0 || limit_cycles > 4000000000LL)
     return fail(TDSA_ERR_INVALID, "limit_cycles must be in [0, 4e9]");

@@ -91,6 +91,12 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
                 int64_t oi_stride, float* out_val, int64_t ov_stride, void* ws, size_t ws_bytes,
                 cudaStream_t stream, float* kth_out = nullptr, uint32_t* key_hist = nullptr);
 
+int launch_hadamard128(const void* in, int64_t in_stride, int64_t rows, int dtype, void* out,
+                       int64_t out_stride, cudaStream_t stream);
+int launch_select_quantize(const void* in, int64_t in_stride, int64_t rows, int width,
+                           int dtype, const int8_t* keep, int bits, double scale,
+                           uint32_t* absmax, void* out, int64_t out_stride,
+                           cudaStream_t stream);
 int launch_bounded_wait_selftest(long long limit_cycles, cudaStream_t stream, int* status);
 size_t packed_wq_bytes(int hidden);
 int launch_pack_wq(const void* wq, int64_t stride, int hidden, void* out, cudaStream_t stream);

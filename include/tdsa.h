@@ -35,6 +35,26 @@ enum tdsa_status {
 enum tdsa_dtype { TDSA_F32 = 0, TDSA_F16 = 1, TDSA_BF16 = 2 };
 
 /*
+ * Dimension-sparse verifier scorer (src/temporal_dsa/verifier_scoring.py:9-139).
+ * tdsa_hadamard128 -- replaces normalized_hadamard (:9-26) for 128-wide rows: out[r] =
+ *   H_128 in[r] / sqrt(128) (orthonormal Walsh-Hadamard, Sylvester order), float32
+ *   arithmetic in the reference's butterfly order, rounded once to `dtype`.
+ * tdsa_select_quantize -- the selection and fake_symmetric_quantize (:29-41) steps of
+ *   score_dim_sparse (:95-139) on [rows][width] rows: out = in on the dimensions with
+ *   keep[d] != 0 (keep: device int8 [width], NULL = all), 0 elsewhere; with bits in
+ *   {2, 4, 8} the kept values become clamp(rint(x / s), -L, L) * s, L = 2^(bits-1) - 1,
+ *   s = scale if scale > 0 else (max |x| over the kept entries) / L (the max is left in
+ *   *absmax_word as float bits).  score_dim_sparse is then tdsa_score_dense on the
+ *   transformed queries and keys.
+ */
+int tdsa_hadamard128(const void* in, int64_t in_row_stride, int64_t rows, int dtype, void* out,
+                     int64_t out_row_stride, void* stream);
+int tdsa_select_quantize(const void* in, int64_t in_row_stride, int64_t rows, int width,
+                         int dtype, const int8_t* keep, int bits, double scale,
+                         uint32_t* absmax_word, void* out, int64_t out_row_stride,
+                         void* stream);
+
+/*
  * Failure-path self-test (no reference counterpart): one kernel waits on an mbarrier that
  * nothing arrives on, with the same bounded loop every in-kernel wait of this library
  * uses but a limit of `limit_cycles` SM cycles; when the limit runs out it raises

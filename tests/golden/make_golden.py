@@ -3,6 +3,7 @@
 Run once, where the reference project is available (it is not on the GPU box):
 
     python tests/golden/make_golden.py --reference-src <path to temporal_dsa's src/>
+    python tests/golden/make_golden.py --reference-src <...> --only verifier   # one fixture
 
 Every output array below is computed by the reference's own functions
 (``temporal_dsa.progressive_kernel``, ``.metrics``, ``.certified``, ``.replay``,
@@ -57,10 +58,16 @@ def bf16_inputs(length: int, seed: int = 1582):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True)
+    ap.add_argument("--only", choices=["verifier"], default=None,
+                    help="regenerate one fixture instead of all of them")
     args = ap.parse_args()
     sys.path.insert(0, args.reference_src)
     from temporal_dsa import certified, metrics, progressive_kernel as pk, replay, verifier_scoring
     from temporal_dsa.sidecar import LightningIndexerSidecar
+
+    if args.only == "verifier":
+        make_verifier(verifier_scoring)
+        return
 
     # ---- dense scores (f32 and bf16) -------------------------------------------------
     out = {}
@@ -248,8 +255,39 @@ def main() -> None:
                         ww=sc.weights_proj.weight.detach().numpy(),
                         wk=sc.wk.weight.detach().numpy(), hq=hq.numpy(), qpos=qpos.numpy(),
                         q=eq.numpy(), w=ew.numpy(), hk=hk.numpy(), k=ek.numpy())
+    make_verifier(verifier_scoring)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
+
+
+def make_verifier(verifier_scoring) -> None:
+    """verifier.npz: normalized_hadamard, fake_symmetric_quantize and score_dim_sparse
+    (verifier_scoring.py:9-139) on seeded 64-head x 128-dim inputs."""
+    g = torch.Generator().manual_seed(41)
+    vq = torch.randn(2, 64, 128, generator=g) / math.sqrt(128)
+    vw = torch.randn(2, 64, generator=g) / 8
+    vk = torch.randn(160, 128, generator=g)
+    dims = torch.tensor(sorted(torch.randperm(128, generator=g)[:32].tolist()))
+    ver = {"q": vq.numpy(), "w": vw.numpy(), "k": vk.numpy(), "dims": dims.numpy()}
+    ver["had_k"] = verifier_scoring.normalized_hadamard(vk).numpy()
+    ver["had_q"] = verifier_scoring.normalized_hadamard(vq).numpy()
+    for bits in (2, 4, 8):
+        qk, sc = verifier_scoring.fake_symmetric_quantize(vk, bits)
+        ver[f"fq{bits}_k"] = qk.numpy()
+        ver[f"fq{bits}_scale"] = np.float64(sc)
+    for rot in ("none", "hadamard"):
+        for bits in (None, 4, 8):
+            s = verifier_scoring.score_dim_sparse(vq, vw, vk, dims, rotation=rot, bits=bits)
+            ver[f"ds_{rot}_{bits or 0}"] = s.numpy()
+    s = verifier_scoring.score_dim_sparse(vq, vw, vk, dims, bits=4, query_scale=0.05,
+                                          key_scale=0.5)
+    ver["ds_none_4_fixed"] = s.numpy()
+    qb, kb = vq.to(torch.bfloat16), vk.to(torch.bfloat16)
+    ver["q_bf16"], ver["k_bf16"] = bf16_bits(qb), bf16_bits(kb)
+    for rot in ("none", "hadamard"):
+        s = verifier_scoring.score_dim_sparse(qb, vw, kb, dims, rotation=rot, bits=8)
+        ver[f"dsb_{rot}_8"] = s.float().numpy()
+    np.savez_compressed(HERE / "verifier.npz", **ver)
 
 
 if __name__ == "__main__":

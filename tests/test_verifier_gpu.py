@@ -16,7 +16,7 @@ import torch
 
 import oracle
 from tests._util import assert_scores_close, normwise_bound
-from tests.conftest import load_golden
+from tests.conftest import bf16_from_bits, load_golden
 
 pytestmark = pytest.mark.gpu
 
@@ -135,3 +135,60 @@ def test_torch_progressive_scores_matches_oracle(block_size):
     fin = same & np.isfinite(ws)
     scale = normwise_bound(qf, w.numpy(), kf)
     assert_scores_close(got_s[fin], ws[fin], scale[fin], rtol=1e-5, atol=1e-7)
+
+
+def test_normalized_hadamard_and_quantizer_match_reference_golden():
+    """verifier_scoring.py:9-41 on float32: the same butterflies and the same quantizer
+    arithmetic as the reference's float32 path."""
+    from dsa_b200.verifier_scoring import fake_symmetric_quantize, normalized_hadamard
+
+    g = load_golden("verifier")
+    hk = normalized_hadamard(torch.from_numpy(g["k"]).cuda()).cpu().numpy()
+    hq = normalized_hadamard(torch.from_numpy(g["q"]).cuda()).cpu().numpy()
+    np.testing.assert_allclose(hk, g["had_k"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(hq, g["had_q"], rtol=1e-6, atol=1e-8)
+    for bits in (2, 4, 8):
+        qk, sc = fake_symmetric_quantize(torch.from_numpy(g["k"]).cuda(), bits)
+        assert sc == pytest.approx(float(g[f"fq{bits}_scale"]), rel=1e-7)
+        np.testing.assert_array_equal(qk.cpu().numpy(), g[f"fq{bits}_k"])
+    with pytest.raises(ValueError):
+        normalized_hadamard(torch.zeros(3, 64, device="cuda"))
+    with pytest.raises(ValueError):
+        fake_symmetric_quantize(torch.zeros(3, 128, device="cuda"), 3)
+
+
+@pytest.mark.parametrize("rotation", ["none", "hadamard"])
+@pytest.mark.parametrize("bits", [None, 4, 8])
+def test_score_dim_sparse_matches_reference_golden(rotation, bits):
+    from dsa_b200.verifier_scoring import score_dim_sparse
+
+    g = load_golden("verifier")
+    q, w, k = (torch.from_numpy(g[n]).cuda() for n in ("q", "w", "k"))
+    got = score_dim_sparse(q, w, k, torch.from_numpy(g["dims"]), rotation=rotation,
+                           bits=bits).cpu().numpy()
+    want = g[f"ds_{rotation}_{bits or 0}"]
+    dims = g["dims"]
+    qs, ks = g["q"][..., dims], g["k"][..., dims]
+    scale = np.stack([(np.abs(g["w"][i])[:, None] * np.abs(qs[i] @ ks.T)).sum(0)
+                      for i in range(2)])
+    assert_scores_close(got, want, scale + 1e-3, rtol=1e-4, atol=1e-6)
+
+
+def test_score_dim_sparse_fixed_scales_bf16_and_full_width():
+    from dsa_b200 import score_dense
+    from dsa_b200.verifier_scoring import score_dim_sparse
+
+    g = load_golden("verifier")
+    q, w, k = (torch.from_numpy(g[n]).cuda() for n in ("q", "w", "k"))
+    got = score_dim_sparse(q, w, k, g["dims"], bits=4, query_scale=0.05, key_scale=0.5)
+    np.testing.assert_allclose(got.cpu().numpy(), g["ds_none_4_fixed"], rtol=1e-4, atol=1e-5)
+    # bf16 inputs: the reference rounds every butterfly stage to bf16, the kernel once
+    qb = torch.from_numpy(bf16_from_bits(g["q_bf16"])).cuda().to(torch.bfloat16)
+    kb = torch.from_numpy(bf16_from_bits(g["k_bf16"])).cuda().to(torch.bfloat16)
+    for rot in ("none", "hadamard"):
+        got = score_dim_sparse(qb, w, kb, g["dims"], rotation=rot, bits=8).cpu().numpy()
+        np.testing.assert_allclose(got, g[f"dsb_{rot}_8"], rtol=5e-2, atol=5e-2)
+    # all 128 dimensions, no rotation: the dense score (reference test_verifier_scoring.py:23-30)
+    full = score_dim_sparse(q, w, k, torch.arange(128)).cpu().numpy()
+    dense = torch.stack([score_dense(q[i], w[i], k) for i in range(2)]).cpu().numpy()
+    np.testing.assert_allclose(full, dense, rtol=1e-6, atol=1e-7)
