@@ -17,6 +17,7 @@
 // epilogue summation order).
 #include "common.cuh"
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace tdsa {
 
@@ -30,6 +31,8 @@ constexpr double kGamma = 0x1p-12;  // relative rounding slack of a computed sco
 __global__ void new_key_norms_kernel(const void* keys, int64_t k_bs, int64_t k_rs, int dtype,
                                      int first_key, int length, int bs, uint32_t* maxsq,
                                      int64_t nb_stride) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
   const int b = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int warps = (blockDim.x >> 5) * gridDim.x;
@@ -134,6 +137,8 @@ __device__ void emit_tiles(const int8_t* flag, int nb, int want, int bpt, int se
 }
 
 __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs a) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
   __shared__ double coeff[64];
   __shared__ double c_total;
   __shared__ uint32_t wtot[32];
@@ -202,21 +207,98 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
   emit_tiles(flag, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counter, wtot, sbase);
 }
 
-// Wave 2: blocks not scored yet whose bound reaches tau.
+// Builds the 4096-bin key histogram (top 12 bits of the order-preserving key) of row `seq`
+// of the scores in shared memory: finite scores by bin, -inf (unscored keys) counted apart
+// so their single bin is not hammered by atomics.  Returns the -inf count (all threads).
+__device__ uint32_t row_histogram(const float* srow, int length, uint32_t* h) {
+  __shared__ uint32_t s_inf;
+  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) h[i] = 0u;
+  if (threadIdx.x == 0) s_inf = 0u;
+  __syncthreads();
+  uint32_t inf = 0;
+  for (int i = threadIdx.x; i < length; i += kThreads) {
+    const float v = srow[i];
+    if (v == -INFINITY) ++inf;
+    else atomicAdd(&h[float_to_key(v) >> 20], 1u);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) inf += __shfl_xor_sync(0xffffffffu, inf, o);
+  if ((threadIdx.x & 31) == 0 && inf) atomicAdd(&s_inf, inf);
+  __syncthreads();
+  return s_inf;
+}
+
+// Wave 2: blocks not scored yet whose bound reaches tau.  tau is the lower edge of the
+// histogram bin that holds the k-th largest wave-1 score: at most that score, so every
+// block pruned against it holds no top-k key (and no top-k launch is needed for it).
 __global__ void __launch_bounds__(kThreads)
     exact_wave2_kernel(int length, int bs, int bpt, int64_t nb_stride, const float* bound,
-                       const float* tau, int8_t* flag, int32_t* tile_seq, int32_t* tile_blk,
-                       int32_t* counter) {
+                       const float* scores, int64_t l_stride, int k, float* tau, int8_t* flag,
+                       int32_t* tile_seq, int32_t* tile_blk, int32_t* counter) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
+  __shared__ uint32_t h[kKeyHistBins];
   __shared__ uint32_t wtot[32];
   __shared__ uint32_t sbase[4];
+  __shared__ float s_tau;
   const int seq = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nb = (length + bs - 1) / bs;
   const int64_t brow = static_cast<int64_t>(seq) * nb_stride;
-  const float t = tau[seq];
+  row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h);
+  // thread t owns bins 4095-4t .. 4092-4t: keys above a thread's bins by a CTA scan
+  uint32_t c[4], tot = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    c[i] = h[kKeyHistBins - 1 - (4 * threadIdx.x + i)];
+    tot += c[i];
+  }
+  uint32_t x = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wtot[warp] = x;
+  if (threadIdx.x == 0) s_tau = -INFINITY;  // fewer than k finite scores: prune nothing
+  __syncthreads();
+  uint32_t above = x - tot;
+  for (int i = 0; i < warp; ++i) above += wtot[i];
+  const uint32_t kk = static_cast<uint32_t>(k);
+  if (above < kk && kk <= above + tot) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (above < kk && kk <= above + c[i]) {
+        const uint32_t bin = kKeyHistBins - 1 - (4 * threadIdx.x + i);
+        const uint32_t lo = bin << 20;
+        // the smallest key of the bin, as a float (bin 0 holds -inf: no pruning; bins
+        // above +inf hold NaN: only blocks that may hold NaN stay)
+        s_tau = bin == 0 ? -INFINITY : (lo > 0xFF800000u ? INFINITY : key_to_float(lo));
+      }
+      above += c[i];
+    }
+  }
+  __syncthreads();
+  const float t = s_tau;
+  if (threadIdx.x == 0) tau[seq] = t;
   for (int b = threadIdx.x; b < nb; b += kThreads)
     if (flag[brow + b] == 0 && bound[brow + b] >= t) flag[brow + b] = 2;
   __syncthreads();
   emit_tiles(flag + brow, nb, 2, bpt, seq, tile_seq, tile_blk, counter, wtot, sbase);
+}
+
+// The final key histogram of each row for the histogram top-k: finite scores by bin, the
+// unscored (-inf) keys in bin 0.  Every bin is stored (no zeroing needed before).
+__global__ void __launch_bounds__(kThreads)
+    exact_row_hist_kernel(const float* scores, int64_t l_stride, int length, uint32_t* hist) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
+  __shared__ uint32_t h[kKeyHistBins];
+  const int seq = blockIdx.x;
+  const uint32_t inf = row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h);
+  uint32_t* dst = hist + static_cast<int64_t>(seq) * kKeyHistBins;
+  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads)
+    dst[i] = h[i] + (i == (0x007FFFFFu >> 20) ? inf : 0u);
 }
 
 // State update and statistics.
@@ -225,6 +307,8 @@ __global__ void __launch_bounds__(kThreads)
                           int length, int bs, int64_t nb_stride, const int8_t* flag,
                           const float* bmax, const float* bound, float* upper, void* qprev,
                           float* wprev, unsigned long long* stats, int new_keys) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
   __shared__ unsigned long long acc[4];
   const int seq = blockIdx.x;
   const int nb = (length + bs - 1) / bs;
@@ -242,14 +326,27 @@ __global__ void __launch_bounds__(kThreads)
       wave2 += f == 2;
     }
   }
-  atomicAdd(&acc[0], scored);
-  atomicAdd(&acc[1], keys);
-  atomicAdd(&acc[2], hot);
-  atomicAdd(&acc[3], wave2);
-  // keep q (16-bit bits) and w for the next step's certified coefficient
-  const uint16_t* qs = static_cast<const uint16_t*>(q) + static_cast<int64_t>(seq) * q_bs;
-  uint16_t* qd = static_cast<uint16_t*>(qprev) + static_cast<int64_t>(seq) * 8192;
-  for (int i = threadIdx.x; i < 8192; i += kThreads) qd[i] = qs[i];
+  // warp sums first: 64-bit shared atomics from every thread on one word serialise
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    scored += __shfl_xor_sync(0xffffffffu, scored, o);
+    keys += __shfl_xor_sync(0xffffffffu, keys, o);
+    hot += __shfl_xor_sync(0xffffffffu, hot, o);
+    wave2 += __shfl_xor_sync(0xffffffffu, wave2, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(&acc[0], scored);
+    atomicAdd(&acc[1], keys);
+    atomicAdd(&acc[2], hot);
+    atomicAdd(&acc[3], wave2);
+  }
+  // keep q (16-bit bits) and w for the next step's certified coefficient (rows are
+  // 16-byte aligned: the scoring kernels' TMA rules)
+  const uint4* qs = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(q) +
+                                                   static_cast<int64_t>(seq) * q_bs);
+  uint4* qd = reinterpret_cast<uint4*>(static_cast<uint16_t*>(qprev) +
+                                       static_cast<int64_t>(seq) * 8192);
+  for (int i = threadIdx.x; i < 8192 / 8; i += kThreads) qd[i] = qs[i];
   if (threadIdx.x < 64) wprev[static_cast<int64_t>(seq) * 64 + threadIdx.x] =
       w[static_cast<int64_t>(seq) * w_bs + threadIdx.x];
   __syncthreads();
@@ -270,6 +367,8 @@ __global__ void __launch_bounds__(kThreads)
 
 __global__ void copy_indices_kernel(const int32_t* src, int64_t s_stride, void* dst,
                                     int64_t d_stride, int idx_bytes, int k) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
   const int row = blockIdx.y;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x) {
     const int32_t v = src[static_cast<int64_t>(row) * s_stride + i];
@@ -310,6 +409,7 @@ ExactLayout exact_layout(int batch, int max_length, int k, int block_size) {
   L.tile_seq = take(static_cast<size_t>(L.tcap) * 4);
   L.tile_blk = take(static_cast<size_t>(L.tcap) * L.bpt * 4);
   L.counters = take(16);
+  L.hist = take(static_cast<size_t>(batch) * kKeyHistBins * 4);
   L.topk_ws_bytes = topk_workspace_bytes(batch, max_length, k);
   L.topk_ws = take(L.topk_ws_bytes);
   L.total = off;
@@ -349,8 +449,9 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   if (length > first_key) {
     const int nkeys = length - first_key;
     const int blocks_x = min(148, (nkeys + 7) / 8);
-    new_key_norms_kernel<<<dim3(blocks_x, batch), 256, 0, stream>>>(
-        keys, k_bs, k_rs, dtype, first_key, length, block_size, maxsq, L.nb_stride);
+    TDSA_CUDA_CHECK(launch_pdl(new_key_norms_kernel, dim3(blocks_x, batch), dim3(256), 0, stream,
+                               keys, k_bs, k_rs, dtype, first_key, length, block_size, maxsq,
+                               L.nb_stride));
     TDSA_CUDA_CHECK(cudaGetLastError());
   }
   // 2. bounds, flags, wave-1 tiles
@@ -379,7 +480,7 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   pa.tile_blk = tile_blk;
   pa.counter = counters;
   pa.init = init;
-  exact_prepare_kernel<<<batch, kThreads, 0, stream>>>(pa);
+  TDSA_CUDA_CHECK(launch_pdl(exact_prepare_kernel, dim3(batch), dim3(kThreads), 0, stream, pa));
   TDSA_CUDA_CHECK(cudaGetLastError());
 
   BlockArgs ba;
@@ -404,33 +505,44 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
                                stream);
   if (rc) return rc;
   if (!init) {
-    // 4. tau = k-th largest wave-1 score
-    rc = launch_topk(scores, max_length, nullptr, 0, batch, length, k, 0, nullptr, 4, k,
-                     nullptr, 0, tws, L.topk_ws_bytes, stream, tau);
-    if (rc) return rc;
-    // 5. wave-2 list, 6. wave 2
-    exact_wave2_kernel<<<batch, kThreads, 0, stream>>>(length, block_size, bpt, L.nb_stride,
-                                                       bound, tau, flag, tile_seq, tile_blk,
-                                                       counters + 1);
+    // 4. tau (a lower bound of the k-th largest wave-1 score), 5. wave-2 list, 6. wave 2
+    TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), 0, stream,
+                               length, block_size, bpt, L.nb_stride,
+                               static_cast<const float*>(bound),
+                               static_cast<const float*>(scores),
+                               static_cast<int64_t>(max_length), k, tau, flag, tile_seq,
+                               tile_blk, counters + 1));
     TDSA_CUDA_CHECK(cudaGetLastError());
     ba.tile_count = counters + 1;
     rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
                              stream);
     if (rc) return rc;
   }
-  // 7. top-k over the scored keys (indices kept as the next step's seeds)
+  // 7. top-k over the scored keys (indices kept as the next step's seeds); rows of one
+  // top-k segment start from their key histogram
+  uint32_t* hist = nullptr;
+  if (length <= kTopkSegment) {
+    hist = reinterpret_cast<uint32_t*>(state + L.hist);
+    TDSA_CUDA_CHECK(launch_pdl(exact_row_hist_kernel, dim3(batch), dim3(kThreads), 0, stream,
+                               static_cast<const float*>(scores),
+                               static_cast<int64_t>(max_length), length, hist));
+    TDSA_CUDA_CHECK(cudaGetLastError());
+  }
   rc = launch_topk(scores, max_length, nullptr, 0, batch, length, k, sorted, topk, 4, k, out_val,
-                   val_bs, tws, L.topk_ws_bytes, stream, nullptr);
+                   val_bs, tws, L.topk_ws_bytes, stream, nullptr, hist);
   if (rc) return rc;
   if (out_idx) {
-    copy_indices_kernel<<<dim3((k + 255) / 256, batch), 256, 0, stream>>>(topk, k, out_idx,
-                                                                          idx_bs, idx_bytes, k);
+    TDSA_CUDA_CHECK(launch_pdl(copy_indices_kernel, dim3((k + 255) / 256, batch), dim3(256), 0,
+                               stream, static_cast<const int32_t*>(topk),
+                               static_cast<int64_t>(k), out_idx, idx_bs, idx_bytes, k));
     TDSA_CUDA_CHECK(cudaGetLastError());
   }
   // 8. state update
-  exact_finalize_kernel<<<batch, kThreads, 0, stream>>>(
-      q, q_bs, w, w_bs, dtype, length, block_size, L.nb_stride, flag, bmax, bound, upper, qprev,
-      wprev, stats, length - first_key);
+  TDSA_CUDA_CHECK(launch_pdl(exact_finalize_kernel, dim3(batch), dim3(kThreads), 0, stream, q,
+                             q_bs, w, w_bs, dtype, length, block_size, L.nb_stride,
+                             static_cast<const int8_t*>(flag), static_cast<const float*>(bmax),
+                             static_cast<const float*>(bound), upper, qprev, wprev, stats,
+                             length - first_key));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }

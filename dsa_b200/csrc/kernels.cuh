@@ -62,6 +62,7 @@ int launch_compact_blocks(const float* scores, int64_t s_stride, const int8_t* a
 struct ExactLayout {
   size_t upper = 0, maxsq = 0, bound = 0, bmax = 0, flag = 0, topk = 0, qprev = 0, wprev = 0;
   size_t scores = 0, tau = 0, stats = 0, tile_seq = 0, tile_blk = 0, counters = 0, topk_ws = 0;
+  size_t hist = 0;  // [batch][4096] key histogram of the step's scores (rows <= 32768)
   size_t topk_ws_bytes = 0, total = 0;
   int64_t nb_stride = 0, tcap = 0;
   int bpt = 0;

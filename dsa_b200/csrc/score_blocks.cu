@@ -126,6 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_wait();  // the tile count, tile lists, q, w and masks may come from the previous kernel
+  pdl_launch_dependents();
   const int64_t total = a.tile_count ? static_cast<int64_t>(*a.tile_count) : a.total_tiles;
   const int64_t t0 = total * blockIdx.x / gridDim.x;
   const int64_t t1 = total * (blockIdx.x + 1) / gridDim.x;
@@ -362,7 +364,7 @@ int launch_t(const CUtensorMap& kmap, const CUtensorMap& qmap, const BlockArgs& 
   auto kern = score_blocks_kernel<kMode, kBF16>;
   TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kSmemBytes));
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(kmap, qmap, a);
+  TDSA_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kThreads), kSmemBytes, stream, kmap, qmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }

@@ -14,7 +14,9 @@ Schedule of one step (per sequence):
   2. bound_b = U_b + maxnorm_b * (c + slack) for blocks fully seen last step; +inf for
      blocks holding keys that are new at this step (replay.py:263-266).
   3. wave 1 scores the hot blocks (those holding a previous top-k key) and new blocks;
-     tau = k-th largest wave-1 score (>= min(current[prev_topk]), the seed threshold).
+     tau = the lower edge of the 4096-bin key histogram bin (top 12 bits of the
+     order-preserving float key) that holds the k-th largest wave-1 score -- a lower
+     bound of that score, read from a histogram instead of a second top-k;
   4. wave 2 scores every other block with bound_b >= tau; the rest are pruned unread.
   5. top-k over the scored keys; U_b <- exact block max (scored) or bound_b (pruned).
 """
@@ -31,6 +33,32 @@ from .indexer import full_scores
 from .topk import stable_topk
 
 GAMMA = 2.0 ** -12
+
+
+def _float_to_key(v: float) -> int:
+    """Order-preserving uint32 key of a float32 (-0 as +0, every NaN above +inf)."""
+    b = int(np.array([v], np.float32).view(np.uint32)[0])
+    if b & 0x7FFFFFFF == 0:
+        b = 0
+    if (b & 0x7F800000) == 0x7F800000 and (b & 0x007FFFFF):
+        return 0xFFFFFFFF
+    return (~b & 0xFFFFFFFF) if b & 0x80000000 else (b | 0x80000000)
+
+
+def _key_to_float(key: int) -> float:
+    b = (key & 0x7FFFFFFF) if key & 0x80000000 else (~key & 0xFFFFFFFF)
+    return float(np.array([b], np.uint32).view(np.float32)[0])
+
+
+def _bin_floor(v: float) -> float:
+    """Smallest float of v's 12-bit key bin (bin 0: -inf; bins past +inf: +inf)."""
+    bin_ = _float_to_key(v) >> 20
+    lo = bin_ << 20
+    if bin_ == 0:
+        return -math.inf
+    if lo > 0xFF800000:
+        return math.inf
+    return _key_to_float(lo)
 
 
 @dataclass
@@ -96,7 +124,7 @@ def exact_step(state: ExactState, q, w, keys):
     full = full_scores(q, w, keys)
     key_block = np.arange(length) // bs
     wave1 = hot[key_block]
-    tau = float(np.partition(full[wave1], -k)[-k])
+    tau = _bin_floor(float(np.partition(full[wave1], -k)[-k])) if wave1.sum() >= k else -math.inf
     wave2_blocks = (~hot) & (bound >= tau)
     scored_blocks = hot | wave2_blocks
     scores = np.where(scored_blocks[key_block], full, np.float32(-np.inf)).astype(np.float32)
