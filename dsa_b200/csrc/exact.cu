@@ -207,45 +207,75 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
   emit_tiles(flag, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counter, wtot, sbase);
 }
 
-// Builds the 4096-bin key histogram (top 12 bits of the order-preserving key) of row `seq`
-// of the scores in shared memory: finite scores by bin, -inf (unscored keys) counted apart
-// so their single bin is not hammered by atomics.  Returns the -inf count (all threads).
-__device__ uint32_t row_histogram(const float* srow, int length, uint32_t* h) {
+constexpr int kHistCopies = 8;  // private copies of the row histogram (one per 4 warps)
+constexpr int kHistCopyBytes = kHistCopies * kKeyHistBins * 4;
+
+// One histogram increment per lane with `in` set, made by the whole warp: the lanes whose
+// bin equals the first active lane's add together with one atomic (clustered scores hit
+// one bin from most lanes), the others add alone.
+__device__ __forceinline__ void add_to_bin(uint32_t* hist, bool in, uint32_t bin) {
+  const unsigned act = __ballot_sync(0xffffffffu, in);
+  if (!act) return;
+  const int lead = __ffs(act) - 1;
+  const uint32_t b0 = __shfl_sync(0xffffffffu, bin, lead);
+  const unsigned same = __ballot_sync(0xffffffffu, in && bin == b0);
+  if ((threadIdx.x & 31) == lead) atomicAdd(&hist[b0], __popc(same));
+  else if (in && bin != b0) atomicAdd(&hist[bin], 1u);
+}
+
+// Counts the 4096-bin key histogram (top 12 bits of the order-preserving key) of one score
+// row into h[0, 4096) (shared memory).  Finite scores go to eight private copies in `hc`
+// (kHistCopies x 4096 words, one per 4 warps) that are summed at the end, so clustered
+// scores do not serialise on a few words; -inf (unscored keys) is counted apart.  Loads
+// are coalesced (thread t reads t, t + 1024, ...).  Returns the -inf count.
+__device__ uint32_t row_histogram(const float* srow, int length, uint32_t* h, uint32_t* hc) {
   __shared__ uint32_t s_inf;
-  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) h[i] = 0u;
+  for (int i = threadIdx.x; i < kHistCopies * kKeyHistBins; i += kThreads) hc[i] = 0u;
   if (threadIdx.x == 0) s_inf = 0u;
   __syncthreads();
+  uint32_t* mine = hc + ((threadIdx.x >> 5) & (kHistCopies - 1)) * kKeyHistBins;
   uint32_t inf = 0;
-  for (int i = threadIdx.x; i < length; i += kThreads) {
-    const float v = srow[i];
-    if (v == -INFINITY) ++inf;
-    else atomicAdd(&h[float_to_key(v) >> 20], 1u);
+  const int span = (length + 31) & ~31;  // whole warps iterate together
+  for (int i = threadIdx.x; i < span; i += kThreads) {
+    const float v = i < length ? srow[i] : -INFINITY;
+    if (i < length && v == -INFINITY) ++inf;
+    add_to_bin(mine, v != -INFINITY, v != -INFINITY ? float_to_key(v) >> 20 : 0u);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) inf += __shfl_xor_sync(0xffffffffu, inf, o);
   if ((threadIdx.x & 31) == 0 && inf) atomicAdd(&s_inf, inf);
   __syncthreads();
+  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {
+    uint32_t t = 0;
+#pragma unroll
+    for (int c = 0; c < kHistCopies; ++c) t += hc[c * kKeyHistBins + i];
+    h[i] = t;
+  }
+  __syncthreads();
   return s_inf;
 }
 
-// Wave 2: blocks not scored yet whose bound reaches tau.  tau is the lower edge of the
-// histogram bin that holds the k-th largest wave-1 score: at most that score, so every
-// block pruned against it holds no top-k key (and no top-k launch is needed for it).
+// Wave 2: blocks not scored yet whose bound reaches tau.  tau is the lower edge of the key
+// bin (top 12 bits, then the next 12 bits inside that bin) that holds the k-th largest
+// wave-1 score: at most that score, so every block pruned against it holds no top-k key
+// (and no top-k launch is needed for it).
 __global__ void __launch_bounds__(kThreads)
     exact_wave2_kernel(int length, int bs, int bpt, int64_t nb_stride, const float* bound,
                        const float* scores, int64_t l_stride, int k, float* tau, int8_t* flag,
                        int32_t* tile_seq, int32_t* tile_blk, int32_t* counter) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
+  extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words
   __shared__ uint32_t h[kKeyHistBins];
   __shared__ uint32_t wtot[32];
   __shared__ uint32_t sbase[4];
   __shared__ float s_tau;
+  __shared__ uint32_t s_bin, s_rank;
   const int seq = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nb = (length + bs - 1) / bs;
   const int64_t brow = static_cast<int64_t>(seq) * nb_stride;
-  row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h);
+  row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h, hcopies);
   // thread t owns bins 4095-4t .. 4092-4t: keys above a thread's bins by a CTA scan
   uint32_t c[4], tot = 0;
 #pragma unroll
@@ -265,20 +295,70 @@ __global__ void __launch_bounds__(kThreads)
   uint32_t above = x - tot;
   for (int i = 0; i < warp; ++i) above += wtot[i];
   const uint32_t kk = static_cast<uint32_t>(k);
+  if (threadIdx.x == 0) s_bin = 0xFFFFFFFFu;
   if (above < kk && kk <= above + tot) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       if (above < kk && kk <= above + c[i]) {
-        const uint32_t bin = kKeyHistBins - 1 - (4 * threadIdx.x + i);
-        const uint32_t lo = bin << 20;
-        // the smallest key of the bin, as a float (bin 0 holds -inf: no pruning; bins
-        // above +inf hold NaN: only blocks that may hold NaN stay)
-        s_tau = bin == 0 ? -INFINITY : (lo > 0xFF800000u ? INFINITY : key_to_float(lo));
+        s_bin = kKeyHistBins - 1 - (4 * threadIdx.x + i);
+        s_rank = kk - above;  // rank of the k-th key inside its bin, from the top
       }
       above += c[i];
     }
   }
   __syncthreads();
+  const uint32_t bin1 = s_bin;
+  if (bin1 != 0xFFFFFFFFu && bin1 != 0u) {
+    // second level: the next 12 key bits of the keys in that bin narrow tau to 2^8 keys
+    const float* srow = scores + static_cast<int64_t>(seq) * l_stride;
+    for (int i = threadIdx.x; i < kHistCopies * kKeyHistBins; i += kThreads) hcopies[i] = 0u;
+    __syncthreads();
+    uint32_t* mine = hcopies + (warp & (kHistCopies - 1)) * kKeyHistBins;
+    const int span = (length + 31) & ~31;
+    for (int i = threadIdx.x; i < span; i += kThreads) {
+      const float v = i < length ? srow[i] : -INFINITY;
+      const uint32_t key = float_to_key(v);
+      const bool in = v != -INFINITY && (key >> 20) == bin1;
+      add_to_bin(mine, in, (key >> 8) & 0xFFFu);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {
+      uint32_t t = 0;
+#pragma unroll
+      for (int c = 0; c < kHistCopies; ++c) t += hcopies[c * kKeyHistBins + i];
+      h[i] = t;
+    }
+    __syncthreads();
+    const uint32_t r = s_rank;
+    uint32_t d[4], dt = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      d[i] = h[kKeyHistBins - 1 - (4 * threadIdx.x + i)];
+      dt += d[i];
+    }
+    uint32_t y = dt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t z = __shfl_up_sync(0xffffffffu, y, o);
+      if (lane >= o) y += z;
+    }
+    if (lane == 31) wtot[warp] = y;
+    __syncthreads();
+    uint32_t ab = y - dt;
+    for (int i = 0; i < warp; ++i) ab += wtot[i];
+    if (ab < r && r <= ab + dt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (ab < r && r <= ab + d[i]) {
+          const uint32_t lo = (bin1 << 20) | ((kKeyHistBins - 1 - (4 * threadIdx.x + i)) << 8);
+          // the smallest key of the sub-bin as a float (past +inf only NaN: +inf)
+          s_tau = lo > 0xFF800000u ? INFINITY : key_to_float(lo);
+        }
+        ab += d[i];
+      }
+    }
+    __syncthreads();
+  }
   const float t = s_tau;
   if (threadIdx.x == 0) tau[seq] = t;
   for (int b = threadIdx.x; b < nb; b += kThreads)
@@ -293,9 +373,11 @@ __global__ void __launch_bounds__(kThreads)
     exact_row_hist_kernel(const float* scores, int64_t l_stride, int length, uint32_t* hist) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
+  extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words
   __shared__ uint32_t h[kKeyHistBins];
   const int seq = blockIdx.x;
-  const uint32_t inf = row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h);
+  const uint32_t inf =
+      row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h, hcopies);
   uint32_t* dst = hist + static_cast<int64_t>(seq) * kKeyHistBins;
   for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads)
     dst[i] = h[i] + (i == (0x007FFFFFu >> 20) ? inf : 0u);
@@ -506,7 +588,11 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   if (rc) return rc;
   if (!init) {
     // 4. tau (a lower bound of the k-th largest wave-1 score), 5. wave-2 list, 6. wave 2
-    TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), 0, stream,
+    TDSA_CUDA_CHECK(cudaFuncSetAttribute(exact_wave2_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kHistCopyBytes));
+    TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), kHistCopyBytes,
+                               stream,
                                length, block_size, bpt, L.nb_stride,
                                static_cast<const float*>(bound),
                                static_cast<const float*>(scores),
@@ -523,7 +609,11 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   uint32_t* hist = nullptr;
   if (length <= kTopkSegment) {
     hist = reinterpret_cast<uint32_t*>(state + L.hist);
-    TDSA_CUDA_CHECK(launch_pdl(exact_row_hist_kernel, dim3(batch), dim3(kThreads), 0, stream,
+    TDSA_CUDA_CHECK(cudaFuncSetAttribute(exact_row_hist_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kHistCopyBytes));
+    TDSA_CUDA_CHECK(launch_pdl(exact_row_hist_kernel, dim3(batch), dim3(kThreads),
+                               kHistCopyBytes, stream,
                                static_cast<const float*>(scores),
                                static_cast<int64_t>(max_length), length, hist));
     TDSA_CUDA_CHECK(cudaGetLastError());

@@ -14,9 +14,9 @@ Schedule of one step (per sequence):
   2. bound_b = U_b + maxnorm_b * (c + slack) for blocks fully seen last step; +inf for
      blocks holding keys that are new at this step (replay.py:263-266).
   3. wave 1 scores the hot blocks (those holding a previous top-k key) and new blocks;
-     tau = the lower edge of the 4096-bin key histogram bin (top 12 bits of the
-     order-preserving float key) that holds the k-th largest wave-1 score -- a lower
-     bound of that score, read from a histogram instead of a second top-k;
+     tau = the lower edge of the key bin (the top 24 bits of the order-preserving float
+     key, found with two 4096-bin histograms) that holds the k-th largest wave-1 score --
+     a lower bound of that score, read from histograms instead of a second top-k;
   4. wave 2 scores every other block with bound_b >= tau; the rest are pruned unread.
   5. top-k over the scored keys; U_b <- exact block max (scored) or bound_b (pruned).
 """
@@ -51,11 +51,12 @@ def _key_to_float(key: int) -> float:
 
 
 def _bin_floor(v: float) -> float:
-    """Smallest float of v's 12-bit key bin (bin 0: -inf; bins past +inf: +inf)."""
-    bin_ = _float_to_key(v) >> 20
-    lo = bin_ << 20
-    if bin_ == 0:
+    """Smallest float of v's key bin at 24-bit resolution: the 12-bit bin of the key, then
+    the next 12 bits inside it (top-level bin 0: -inf; keys past +inf: +inf)."""
+    key = _float_to_key(v)
+    if key >> 20 == 0:
         return -math.inf
+    lo = key & 0xFFFFFF00
     if lo > 0xFF800000:
         return math.inf
     return _key_to_float(lo)
