@@ -33,6 +33,19 @@ __device__ __forceinline__ float key_to_float(uint32_t k) {
   return __uint_as_float(b);
 }
 
+// One histogram increment per lane with `in` set, made by the whole warp: the lanes whose
+// bin equals the first active lane's add together with one atomic (clustered scores hit
+// one bin from most lanes), the others add alone.
+__device__ __forceinline__ void add_to_bin(uint32_t* hist, bool in, uint32_t bin) {
+  const unsigned act = __ballot_sync(0xffffffffu, in);
+  if (!act) return;
+  const int lead = __ffs(act) - 1;
+  const uint32_t b0 = __shfl_sync(0xffffffffu, bin, lead);
+  const unsigned same = __ballot_sync(0xffffffffu, in && bin == b0);
+  if ((threadIdx.x & 31) == lead) atomicAdd(&hist[b0], __popc(same));
+  else if (in && bin != b0) atomicAdd(&hist[bin], 1u);
+}
+
 // ------------------------------------------------------------------ host helpers
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);

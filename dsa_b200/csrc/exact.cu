@@ -210,19 +210,6 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
 constexpr int kHistCopies = 8;  // private copies of the row histogram (one per 4 warps)
 constexpr int kHistCopyBytes = kHistCopies * kKeyHistBins * 4;
 
-// One histogram increment per lane with `in` set, made by the whole warp: the lanes whose
-// bin equals the first active lane's add together with one atomic (clustered scores hit
-// one bin from most lanes), the others add alone.
-__device__ __forceinline__ void add_to_bin(uint32_t* hist, bool in, uint32_t bin) {
-  const unsigned act = __ballot_sync(0xffffffffu, in);
-  if (!act) return;
-  const int lead = __ffs(act) - 1;
-  const uint32_t b0 = __shfl_sync(0xffffffffu, bin, lead);
-  const unsigned same = __ballot_sync(0xffffffffu, in && bin == b0);
-  if ((threadIdx.x & 31) == lead) atomicAdd(&hist[b0], __popc(same));
-  else if (in && bin != b0) atomicAdd(&hist[bin], 1u);
-}
-
 // Counts the 4096-bin key histogram (top 12 bits of the order-preserving key) of one score
 // row into h[0, 4096) (shared memory).  Finite scores go to eight private copies in `hc`
 // (kHistCopies x 4096 words, one per 4 warps) that are summed at the end, so clustered

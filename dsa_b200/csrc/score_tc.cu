@@ -243,10 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&accempty[acc]);
       const float score = relu_weighted_sum(r0, r1, wr);
       const int row = tt * kTileKeys + static_cast<int>(quad) * 32 + lane;
-      if (row < a.length) {
-        a.out[static_cast<int64_t>(b) * a.out_stride + row] = score;
-        if (kHist) atomicAdd(&shist[float_to_key(score) >> 20], 1u);
-      }
+      if (row < a.length) a.out[static_cast<int64_t>(b) * a.out_stride + row] = score;
+      if (kHist) add_to_bin(shist, row < a.length, float_to_key(score) >> 20);
       ++acc_it;
       if (kHist && t + 1 == t1) hist_flush(b);
     }

@@ -322,10 +322,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
 #pragma unroll 8
     for (int j = 0; j < kPer; ++j) {
       const int e = tbase + ((j + rot) & (kPer - 1));
-      if (e < n) {
-        const uint32_t u = key_at(e);
-        if (u >= clo && u <= chi) atomicAdd(&my_hist[(u - clo) >> sh], 1u);
-      }
+      const uint32_t u = e < n ? key_at(e) : 0u;
+      const bool in = e < n && u >= clo && u <= chi;
+      add_to_bin(my_hist, in, in ? (u - clo) >> sh : 0u);
     }
     __syncthreads();
     narrow_to_bin(hists, hist, res, sh, clo, chi, k_rem, in_range);
