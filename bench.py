@@ -337,9 +337,46 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     }
     if world == 1:
         line["latency_b1_l32k"] = single_sequence_latency(wl, proj[0], device)
+        line["trace_emission"] = trace_overhead(wl, proj, plans, device)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
     return line
+
+
+def trace_overhead(wl: Config4, proj, plans, device: torch.device, steps: int = 16) -> dict:
+    """The config-4 step with every layer's score kernel also writing its float16 score-trace
+    row (TraceRecorder, tdsa_score_dense_trace) against the same step without, timed back to
+    back with CUDA events over `steps` steps each."""
+    from dsa_b200.indexer import ScoreTopkPlan
+    from dsa_b200.trace import TraceRecorder
+
+    recs = [TraceRecorder(wl.batch, steps + 3, wl.length, device) for _ in range(wl.layers)]
+    traced = [ScoreTopkPlan(proj[i].q, proj[i].w, wl.keys[i], wl.k, sorted=False,
+                            trace=recs[i]) for i in range(wl.layers)]
+    stream = torch.cuda.current_stream(device)
+
+    def timed(ps, n):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            for layer in range(wl.layers):
+                proj[layer].project(wl.x[layer], wl.qpos)
+                ps[layer].run()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / n
+
+    timed(traced, 3)
+    timed(plans, 3)
+    plain_ms = timed(plans, steps)
+    trace_ms = timed(traced, steps)
+    row_bytes = wl.batch * wl.length * 2
+    del traced, recs
+    return {"ms_per_step": trace_ms, "plain_ms_per_step": plain_ms,
+            "overhead_frac": trace_ms / plain_ms - 1.0,
+            "trace_bytes_per_layer_step": row_bytes,
+            "api": "dsa_b200.trace.TraceRecorder + ScoreTopkPlan(trace=...)"}
 
 
 def single_sequence_latency(wl: Config4, proj, device: torch.device, reps: int = 100) -> dict:

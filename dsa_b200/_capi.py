@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_score_dense_hist": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
                                     vp]),
     "tdsa_topk_hist": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, vp]),
+    "tdsa_score_dense_trace": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
+                                     vp, i64, vp]),
     "tdsa_h8_block_max": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp,
                                 i64, vp, i64, vp]),
     "tdsa_masked_dense": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, i64, vp,

@@ -370,6 +370,27 @@ int tdsa_score_dense_hist(const void* queries, int64_t q_batch_stride, const flo
                                key_hist);
 }
 
+int tdsa_score_dense_trace(const void* queries, int64_t q_batch_stride, const float* weights,
+                           int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                           int64_t k_row_stride, int dtype, int batch, int length,
+                           float* scores, int64_t s_batch_stride, uint32_t* key_hist,
+                           uint16_t* trace, int64_t trace_batch_stride, void* stream) {
+  int rc = check_score_args(queries, q_batch_stride, weights, w_batch_stride, keys,
+                            k_batch_stride, k_row_stride, dtype, batch, length, scores,
+                            s_batch_stride);
+  if (rc || length == 0) return rc;
+  if (dtype == TDSA_F32) return fail(TDSA_ERR_UNSUPPORTED, "score traces need 16-bit keys");
+  if (!trace) return fail(TDSA_ERR_INVALID, "trace is null");
+  if (batch > 1 && trace_batch_stride < length)
+    return fail(TDSA_ERR_INVALID, "trace batch stride must be >= length");
+  int* status = device_status_ptr();
+  if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  return launch_score_dense_tc(queries, q_batch_stride, weights, w_batch_stride, keys,
+                               k_batch_stride, k_row_stride, dtype, batch, length, scores,
+                               s_batch_stride, static_cast<cudaStream_t>(stream), status,
+                               key_hist, trace, trace_batch_stride);
+}
+
 int tdsa_topk_hist(const float* scores, int64_t s_batch_stride, int batch, int length, int k,
                    int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
                    float* out_values, int64_t val_batch_stride, uint32_t* key_hist,

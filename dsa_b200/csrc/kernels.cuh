@@ -15,7 +15,8 @@ constexpr int kKeyHistBins = 4096;     // score-kernel key histogram: top 12 bit
 int launch_score_dense_tc(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
                           const void* k, int64_t k_bs, int64_t k_rs, int dtype, int batch,
                           int length, float* out, int64_t o_bs, cudaStream_t stream,
-                          int* status, uint32_t* hist = nullptr);
+                          int* status, uint32_t* hist = nullptr, void* trace = nullptr,
+                          int64_t trace_bs = 0);
 
 int launch_score_dense_f32(const float* q, int64_t q_bs, const float* w, int64_t w_bs,
                            const float* k, int64_t k_bs, int64_t k_rs, int batch, int length,

@@ -11,7 +11,8 @@
 //               A = key tile, B = q, accumulator in TMEM (2 buffers x 64 f32 columns).
 //   warps 2..5  epilogue: each thread owns one key (one TMEM lane), loads its 64 head dots
 //               with tcgen05.ld, applies ReLU * w_h and sums the heads in registers -- no
-//               cross-thread reduction -- and stores one float per key (coalesced).
+//               cross-thread reduction -- and stores one float per key (coalesced), plus
+//               optionally its float16 rounding into a score-trace row.
 // HBM traffic per key = its 256 bytes, read once; q/w per sequence come from L2.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -46,6 +47,8 @@ struct DenseArgs {
   int tiles_per_seq;
   int64_t total_tiles;
   uint32_t* hist;  // [batch][4096] key histogram (kHist kernels): counts are added
+  __half* trace;   // optional float16 copy of the scores (score trace rows), or null
+  int64_t trace_stride;
   int* status;
 };
 
@@ -243,7 +246,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&accempty[acc]);
       const float score = relu_weighted_sum(r0, r1, wr);
       const int row = tt * kTileKeys + static_cast<int>(quad) * 32 + lane;
-      if (row < a.length) a.out[static_cast<int64_t>(b) * a.out_stride + row] = score;
+      if (row < a.length) {
+        a.out[static_cast<int64_t>(b) * a.out_stride + row] = score;
+        // round to nearest even, as numpy's float32 -> float16 cast of the trace writer
+        if (a.trace)
+          a.trace[static_cast<int64_t>(b) * a.trace_stride + row] = __float2half_rn(score);
+      }
       if (kHist) add_to_bin(shist, row < a.length, float_to_key(score) >> 20);
       ++acc_it;
       if (kHist && t + 1 == t1) hist_flush(b);
@@ -262,7 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <bool kBF16>
 int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs, const void* k,
                       int64_t k_bs, int64_t k_rs, int batch, int length, float* out,
-                      int64_t o_bs, cudaStream_t stream, int* status, uint32_t* hist) {
+                      int64_t o_bs, cudaStream_t stream, int* status, uint32_t* hist,
+                      void* trace, int64_t trace_bs) {
   const CUtensorMapDataType dt =
       kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap kmap, qmap;
@@ -296,6 +305,8 @@ int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
   a.total_tiles = static_cast<int64_t>(a.tiles_per_seq) * batch;
   a.status = status;
   a.hist = hist;
+  a.trace = static_cast<__half*>(trace);
+  a.trace_stride = trace_bs;
   const int dev = current_device();
   const int sms = device_sm_count(dev);
   const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
@@ -313,12 +324,12 @@ int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
 int launch_score_dense_tc(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
                           const void* k, int64_t k_bs, int64_t k_rs, int dtype, int batch,
                           int length, float* out, int64_t o_bs, cudaStream_t stream,
-                          int* status, uint32_t* hist) {
+                          int* status, uint32_t* hist, void* trace, int64_t trace_bs) {
   if (dtype == TDSA_BF16)
     return launch_dense_tc_t<true>(q, q_bs, w, w_bs, k, k_bs, k_rs, batch, length, out, o_bs,
-                                   stream, status, hist);
+                                   stream, status, hist, trace, trace_bs);
   return launch_dense_tc_t<false>(q, q_bs, w, w_bs, k, k_bs, k_rs, batch, length, out, o_bs,
-                                  stream, status, hist);
+                                  stream, status, hist, trace, trace_bs);
 }
 
 }  // namespace tdsa

@@ -184,11 +184,14 @@ class ScoreTopkPlan:
 
     The caller rewrites ``queries``/``weights`` in place between steps; ``score()`` and
     ``select()`` are one C-ABI call each with no per-call validation or allocation.
-    Results land in ``scores`` [B,L], ``indices`` [B,k] and ``values`` [B,k].
+    Results land in ``scores`` [B,L], ``indices`` [B,k] and ``values`` [B,k].  With a
+    ``trace`` (``dsa_b200.trace.TraceRecorder``) every ``score()`` also writes the next
+    float16 trace row from the score kernel (16-bit keys).
     """
 
     def __init__(self, queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor, k: int,
-                 *, sorted: bool = False, index_dtype: torch.dtype = torch.int32):
+                 *, sorted: bool = False, index_dtype: torch.dtype = torch.int32,
+                 trace=None):
         require_cuda(queries, weights, keys)
         q, w, kk, _ = as_batched(queries, weights, keys)
         if not (q.is_contiguous() and _aligned(q) and q.dtype == kk.dtype):
@@ -238,8 +241,23 @@ class ScoreTopkPlan:
         self.device = dev
         # kernels per run(): score + top-k (one level, or two or more when the top-k splits)
         self.launches_per_run = 2 if self.use_hist or nbytes == 0 else 3
+        self.trace = trace
+        if trace is not None:
+            if kk.dtype == torch.float32:
+                raise ValueError("score traces need bfloat16 or float16 keys")
+            if trace.batch != self.batch or trace.max_length < self.length:
+                raise ValueError("the trace recorder does not fit this plan's batch and length")
+            if trace.buffer.device != dev:
+                raise ValueError("the trace recorder's buffer is on another device")
+            self._trace_args = self._score_args[:12] + (
+                self.key_hist.data_ptr() if self.use_hist else None,)
 
     def score(self) -> None:
+        if self.trace is not None:
+            row, row_bs = self.trace.take_row(self.length)
+            capi.check(capi.lib().tdsa_score_dense_trace(*self._trace_args, row, row_bs,
+                                                         stream_ptr(self.device)))
+            return
         capi.check(self._score_fn(*self._score_args, stream_ptr(self.device)))
 
     def select(self) -> None:

@@ -177,6 +177,20 @@ int tdsa_score_dense_hist(const void* queries, int64_t q_batch_stride, const flo
                           int64_t k_row_stride, int dtype, int batch, int length, float* scores,
                           int64_t s_batch_stride, uint32_t* key_hist, void* stream);
 
+/*
+ * tdsa_score_dense_hist (key_hist may be null: no histogram) that also writes every score
+ * rounded to float16 (round to nearest even) at trace[b * trace_batch_stride + s] for s <
+ * length; nothing else of the trace is touched.  This emits one row of a score trace per
+ * call from the score kernel itself: temporal_dsa/training.py:146-175 (evaluate_and_trace)
+ * builds the same row on the host as score_encoded(...).float().cpu().numpy()
+ * .astype(np.float16), padded with -inf to the trace width, and trace.py:34-61 saves it.
+ */
+int tdsa_score_dense_trace(const void* queries, int64_t q_batch_stride, const float* weights,
+                           int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                           int64_t k_row_stride, int dtype, int batch, int length,
+                           float* scores, int64_t s_batch_stride, uint32_t* key_hist,
+                           uint16_t* trace, int64_t trace_batch_stride, void* stream);
+
 int tdsa_topk_hist(const float* scores, int64_t s_batch_stride, int batch, int length, int k,
                    int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
                    float* out_values, int64_t val_batch_stride, uint32_t* key_hist,

@@ -2,8 +2,8 @@
 
 This package restates, in numpy, the algorithms of the reference project
 ``temporal_dsa`` (psa1582/dsa) for the indexer hot path: dense scoring,
-stable top-K, the H8 progressive probe, the certified temporal bound and the
-block-replay filter.  Every function cites the reference file:line it follows
+stable top-K, the H8 progressive probe, the certified temporal bound, the
+block-replay filter and the score-trace rows.  Every function cites the reference file:line it follows
 (paths are relative to the reference project's root).
 
 It exists to CHECK the CUDA path, never to stand in for it.  Only ``tests/``,
@@ -35,3 +35,4 @@ from .indexer import (  # noqa: F401
 )
 from .topk import stable_topk, topk_rows, merge_topk  # noqa: F401
 from .certified import block_key_norms, temporal_score_radius  # noqa: F401
+from .trace import trace_matrix  # noqa: F401

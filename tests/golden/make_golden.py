@@ -4,10 +4,11 @@ Run once, where the reference project is available (it is not on the GPU box):
 
     python tests/golden/make_golden.py --reference-src <path to temporal_dsa's src/>
     python tests/golden/make_golden.py --reference-src <...> --only verifier   # one fixture
+    python tests/golden/make_golden.py --reference-src <...> --only trace
 
 Every output array below is computed by the reference's own functions
 (``temporal_dsa.progressive_kernel``, ``.metrics``, ``.certified``, ``.replay``,
-``.sidecar``, ``.verifier_scoring``).  Inputs are seeded; small inputs are stored
+``.sidecar``, ``.verifier_scoring``, ``.trace``).  Inputs are seeded; small inputs are stored
 verbatim (bf16 tensors as their uint16 bit patterns), the config-1 key cache is
 regenerated from its seed and pinned by a SHA-256 of its bytes.
 """
@@ -58,7 +59,7 @@ def bf16_inputs(length: int, seed: int = 1582):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True)
-    ap.add_argument("--only", choices=["verifier"], default=None,
+    ap.add_argument("--only", choices=["verifier", "trace"], default=None,
                     help="regenerate one fixture instead of all of them")
     args = ap.parse_args()
     sys.path.insert(0, args.reference_src)
@@ -67,6 +68,9 @@ def main() -> None:
 
     if args.only == "verifier":
         make_verifier(verifier_scoring)
+        return
+    if args.only == "trace":
+        make_trace()
         return
 
     # ---- dense scores (f32 and bf16) -------------------------------------------------
@@ -256,6 +260,7 @@ def main() -> None:
                         wk=sc.wk.weight.detach().numpy(), hq=hq.numpy(), qpos=qpos.numpy(),
                         q=eq.numpy(), w=ew.numpy(), hk=hk.numpy(), k=ek.numpy())
     make_verifier(verifier_scoring)
+    make_trace()
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 
@@ -288,6 +293,39 @@ def make_verifier(verifier_scoring) -> None:
         s = verifier_scoring.score_dim_sparse(qb, vw, kb, dims, rotation=rot, bits=8)
         ver[f"dsb_{rot}_8"] = s.float().numpy()
     np.savez_compressed(HERE / "verifier.npz", **ver)
+
+
+def trace_rows() -> tuple[list[np.ndarray], dict]:
+    """Seeded float32 score rows of growing length for the trace fixture, with values that
+    round to +-inf (65520 is the float16 halfway point above 65504), to float16 subnormals
+    and to zero, plus the trace's identifying fields."""
+    rng = np.random.default_rng(11)
+    lengths = [5, 9, 12, 16]
+    rows = [(rng.normal(size=n) * 3).astype(np.float32) for n in lengths]
+    rows[1][:6] = [70000.0, -70000.0, 65520.0, 65519.0, 1e-8, 3e-6]
+    rows[2][:3] = [1.0 / 3.0, -0.0, 2049.0]
+    fields = {"layer": 7, "workload": "synthetic", "prompt_id": "seed11",
+              "metadata": {"query_ids": [4, 8, 11, 15], "research_sidecar": True,
+                           "source": None}}
+    return rows, fields
+
+
+def make_trace() -> None:
+    """trace_rows.npz: the float32 rows; trace_ref.npz: those rows written by the reference's
+    trace writer -- float16 rows padded with -inf to the widest (training.py:166-178),
+    int32 lengths, saved by trace.save_trace (trace.py:34-48)."""
+    from temporal_dsa.trace import ScoreTrace, save_trace
+
+    rows, f = trace_rows()
+    lengths = np.asarray([r.size for r in rows], dtype=np.int32)
+    padded = np.full((len(rows), int(lengths.max())), -np.inf, dtype=np.float16)
+    for i, r in enumerate(rows):
+        padded[i, : r.size] = r.astype(np.float16)
+    save_trace(HERE / "trace_ref.npz",
+               ScoreTrace(scores=padded, lengths=lengths, layer=f["layer"],
+                          workload=f["workload"], prompt_id=f["prompt_id"],
+                          metadata=f["metadata"]))
+    np.savez_compressed(HERE / "trace_rows.npz", rows=np.concatenate(rows), lengths=lengths)
 
 
 if __name__ == "__main__":
