@@ -162,6 +162,7 @@ class Config4:
                 h = torch.randn(length, hidden, generator=g, device=device, dtype=bf)
                 cache[b] = encode_keys(h, wk[layer], ln_w, ln_b, pos)
             self.keys.append(cache)
+        self.wk0, self.ln_w, self.ln_b = wk[0], ln_w, ln_b
         del wk
         self.x = torch.randn(layers, batch, hidden, generator=g, device=device, dtype=bf)
         self.qpos = torch.full((batch,), length - 1, device=device, dtype=torch.long)
@@ -338,9 +339,66 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     if world == 1:
         line["latency_b1_l32k"] = single_sequence_latency(wl, proj[0], device)
         line["trace_emission"] = trace_overhead(wl, proj, plans, device)
+        line["key_append"] = key_append_latency(wl, device)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
     return line
+
+
+def key_append_latency(wl: Config4, device: torch.device, per_graph: int = 20,
+                       replays: int = 20) -> dict:
+    """The decode step's key append for one layer at config 4 (B sequences, hidden 2048):
+    one tdsa_key_append launch (W_k GEMV + LayerNorm + RoPE + cache store) against the torch
+    composition of the reference's encode_keys plus the cache write.  Each is captured
+    `per_graph` times into a CUDA graph (no host launch cost in the number); the graph is
+    replayed `replays` times between CUDA events, time per append = total / (replays *
+    per_graph)."""
+    from dsa_b200.sidecar import KeyAppender, encode_keys
+
+    app = KeyAppender(wl.wk0, wl.ln_w, wl.ln_b)
+    cache = torch.zeros(wl.batch, 8, 128, device=device, dtype=torch.bfloat16)
+    x = wl.x[0]
+    pos = wl.qpos
+    slots = torch.zeros(wl.batch, device=device, dtype=torch.long)
+    rows = torch.arange(wl.batch, device=device)
+
+    def fused():
+        app.append(x, pos, cache, slots)
+
+    def composed():
+        cache[rows, slots] = encode_keys(x, wl.wk0, wl.ln_w, wl.ln_b, pos)
+
+    def timed(fn):
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(per_graph):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        stream = torch.cuda.current_stream(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        del graph
+        return e0.elapsed_time(e1) / (replays * per_graph) * 1e3
+
+    fused_us, torch_us = timed(fused), timed(composed)
+    return {"us_per_launch": fused_us, "torch_composition_us": torch_us,
+            "batch": wl.batch, "hidden": wl.hidden,
+            "bytes_per_launch": 128 * wl.hidden * 2 + wl.batch * (wl.hidden * 2 + 256),
+            "method": f"CUDA graph of {per_graph} appends, {replays} replays, events",
+            "api": "dsa_b200.sidecar.KeyAppender (C ABI tdsa_key_append)"}
 
 
 def trace_overhead(wl: Config4, proj, plans, device: torch.device, steps: int = 16) -> dict:

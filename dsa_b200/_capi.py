@@ -20,6 +20,7 @@ TDSA_ERR_CUDA = 3
 TDSA_ERR_TIMEOUT = 4
 TDSA_ERR_ALIGN = 5
 TDSA_ERR_WORKSPACE = 6
+TDSA_STATUS_RANGE = 8  # device status bit: a device-side index was out of range
 
 TDSA_F32 = 0
 TDSA_F16 = 1
@@ -52,6 +53,8 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_score_dense_hist": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
                                     vp]),
     "tdsa_topk_hist": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, vp]),
+    "tdsa_key_append": (i32, [vp, i64, i32, vp, i64, vp, vp, C.c_float, vp, vp, vp, i64, i64,
+                              i64, i32, i32, i32, C.c_float, vp]),
     "tdsa_score_dense_trace": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
                                      vp, i64, vp]),
     "tdsa_h8_block_max": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp,

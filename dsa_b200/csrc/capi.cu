@@ -487,6 +487,39 @@ int tdsa_pack_query_weights(const void* w_q, int64_t wq_row_stride, int hidden_s
   return launch_pack_wq(w_q, wq_row_stride, hidden_size, out, static_cast<cudaStream_t>(stream));
 }
 
+int tdsa_key_append(const void* hidden, int64_t hidden_stride, int hidden_size,
+                    const void* w_k, int64_t wk_row_stride, const float* ln_weight,
+                    const float* ln_bias, float eps, const int64_t* positions,
+                    const int64_t* slots, void* cache, int64_t cache_batch_stride,
+                    int64_t cache_row_stride, int64_t cache_rows, int dtype, int batch,
+                    int rope_dim, float rope_theta, void* stream) {
+  if (!hidden || !w_k || !positions || !cache) return fail(TDSA_ERR_INVALID, "null pointer");
+  if (dtype != TDSA_BF16 && dtype != TDSA_F16)
+    return fail(TDSA_ERR_INVALID, "key_append takes TDSA_BF16 or TDSA_F16");
+  if (batch < 1 || batch > (1 << 20)) return fail(TDSA_ERR_INVALID, "batch must be in [1, 2^20]");
+  if (hidden_size < 8 || hidden_size % 8)
+    return fail(TDSA_ERR_UNSUPPORTED, "hidden_size must be a positive multiple of 8");
+  if (rope_dim < 0 || rope_dim > kHeadDim || rope_dim % 2)
+    return fail(TDSA_ERR_INVALID, "rope_dim must be even and in [0, 128]");
+  if (!(eps >= 0.f)) return fail(TDSA_ERR_INVALID, "eps must be >= 0");
+  if (wk_row_stride < hidden_size || (batch > 1 && hidden_stride < hidden_size))
+    return fail(TDSA_ERR_INVALID, "row strides must be >= hidden_size");
+  if (cache_rows < 1 || cache_row_stride < kHeadDim ||
+      (batch > 1 && cache_batch_stride < cache_rows * cache_row_stride))
+    return fail(TDSA_ERR_INVALID, "cache strides do not hold [batch][cache_rows][128]");
+  if (!aligned16(hidden) || !aligned16(w_k) || wk_row_stride % 8 ||
+      (batch > 1 && hidden_stride % 8))
+    return fail(TDSA_ERR_ALIGN, "hidden and w_k need 16-byte aligned rows");
+  if (reinterpret_cast<uintptr_t>(cache) % 2)
+    return fail(TDSA_ERR_ALIGN, "cache must be 2-byte aligned");
+  int* status = device_status_ptr();
+  if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  return launch_key_append(hidden, hidden_stride, hidden_size, w_k, wk_row_stride, ln_weight,
+                           ln_bias, eps, positions, slots, cache, cache_batch_stride,
+                           cache_row_stride, cache_rows, dtype, batch, rope_dim, rope_theta,
+                           status, static_cast<cudaStream_t>(stream));
+}
+
 int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_size,
                        const void* w_q, int64_t wq_row_stride, int wq_packed,
                        const float* w_proj,

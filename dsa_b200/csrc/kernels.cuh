@@ -102,6 +102,13 @@ int launch_select_quantize(const void* in, int64_t in_stride, int64_t rows, int 
 int launch_bounded_wait_selftest(long long limit_cycles, cudaStream_t stream, int* status);
 size_t packed_wq_bytes(int hidden);
 int launch_pack_wq(const void* wq, int64_t stride, int hidden, void* out, cudaStream_t stream);
+// ---- decode-step key append (key_append.cu)
+int launch_key_append(const void* hidden, int64_t hidden_stride, int hidden_size,
+                      const void* wk, int64_t wk_stride, const float* ln_w, const float* ln_b,
+                      float eps, const int64_t* positions, const int64_t* slots, void* cache,
+                      int64_t cache_bs, int64_t cache_rs, int64_t cache_rows, int dtype,
+                      int batch, int rope_dim, float theta, int* status, cudaStream_t stream);
+
 int launch_query_project(const void* x, int64_t x_stride, int hidden, const void* wq,
                          int64_t wq_stride, int packed, const float* ww,
                          const int64_t* positions, void* q,

@@ -78,6 +78,18 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- cp.async (16 bytes)
+// Asynchronous 16-byte global -> shared copy (L2 only); many can be in flight per thread.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+// Wait for all of this thread's cp.async copies (then a barrier publishes them).
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- clusters / DSMEM
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -157,3 +157,71 @@ def encode_keys(hidden: torch.Tensor, wk: torch.Tensor, norm_weight: torch.Tenso
         k = torch.cat((apply_noninterleaved_rope(k[..., :rope_dim], positions, theta=rope_theta),
                        k[..., rope_dim:]), dim=-1)
     return k
+
+
+class KeyAppender:
+    """Decode-step key append, one launch (tdsa_key_append): for each sequence the new
+    token's key RoPE(LayerNorm(hidden @ wk^T)) (sidecar.py:74-76) is computed and written
+    straight into that sequence's cache row.
+
+    ``append(hidden [B, hidden], positions [B], cache [B, L, 128], slots=None)``: the key of
+    sequence b goes to ``cache[b, slots[b]]`` (``slots=None``: ``positions[b]``).  A slot
+    outside ``[0, L)`` is skipped and raises TDSA_STATUS_RANGE in the device status word.
+    """
+
+    def __init__(self, wk: torch.Tensor, norm_weight: torch.Tensor | None = None,
+                 norm_bias: torch.Tensor | None = None, *, rope_dim: int = 64,
+                 rope_theta: float = 10_000.0, eps: float = 1e-6):
+        require_cuda(wk)
+        if wk.dim() != 2 or wk.shape[0] != HEAD_DIM:
+            raise ValueError("expected wk [128, hidden]")
+        if wk.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("wk must be bf16 or fp16")
+        if wk.shape[1] % 8:
+            raise ValueError("the hidden size must be a multiple of 8")
+        dev = wk.device
+        self.wk = wk if (wk.stride(-1) == 1 and wk.stride(0) % 8 == 0
+                         and wk.data_ptr() % 16 == 0) else wk.contiguous()
+        self.hidden, self.dtype = wk.shape[1], wk.dtype
+        self.norm_weight = (None if norm_weight is None
+                            else norm_weight.to(dev, torch.float32).contiguous())
+        self.norm_bias = (None if norm_bias is None
+                          else norm_bias.to(dev, torch.float32).contiguous())
+        for t in (self.norm_weight, self.norm_bias):
+            if t is not None and t.shape != (HEAD_DIM,):
+                raise ValueError("LayerNorm weight and bias must be [128]")
+        self.rope_dim, self.theta, self.eps = int(rope_dim), float(rope_theta), float(eps)
+        # the kernel reads W_k before it waits on the previous kernel of the stream: the
+        # weights must be complete before the first append
+        torch.cuda.current_stream(dev).synchronize()
+        self._fn = capi.lib().tdsa_key_append
+        self._dt = capi.TDSA_BF16 if wk.dtype == torch.bfloat16 else capi.TDSA_F16
+
+    def append(self, hidden: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor,
+               slots: torch.Tensor | None = None) -> torch.Tensor:
+        require_cuda(hidden, positions, cache)
+        batch = hidden.shape[0]
+        if hidden.shape != (batch, self.hidden) or hidden.dtype != self.dtype:
+            raise ValueError("hidden must be [batch, hidden] in the weights' dtype")
+        if cache.dim() != 3 or cache.shape[0] != batch or cache.shape[2] != HEAD_DIM:
+            raise ValueError("cache must be [batch, L, 128]")
+        if cache.dtype != self.dtype or cache.stride(-1) != 1:
+            raise ValueError("cache must share the weights' dtype with unit last stride")
+        if hidden.stride(-1) != 1 or hidden.stride(0) % 8 or hidden.data_ptr() % 16:
+            hidden = hidden.contiguous() if hidden.stride(-1) != 1 else hidden.clone()
+        positions = positions.to(torch.int64).contiguous()
+        if positions.shape != (batch,):
+            raise ValueError("positions must be [batch]")
+        if slots is not None:
+            slots = slots.to(torch.int64).contiguous()
+            if slots.shape != (batch,):
+                raise ValueError("slots must be [batch]")
+        capi.check(self._fn(
+            hidden.data_ptr(), hidden.stride(0), self.hidden, self.wk.data_ptr(),
+            self.wk.stride(0),
+            self.norm_weight.data_ptr() if self.norm_weight is not None else None,
+            self.norm_bias.data_ptr() if self.norm_bias is not None else None, self.eps,
+            positions.data_ptr(), slots.data_ptr() if slots is not None else None,
+            cache.data_ptr(), cache.stride(0), cache.stride(1), cache.shape[1], self._dt, batch,
+            self.rope_dim, self.theta, torch.cuda.current_stream(cache.device).cuda_stream))
+        return cache

@@ -32,6 +32,10 @@ enum tdsa_status {
   TDSA_ERR_WORKSPACE = 6    /* workspace missing or smaller than the query said       */
 };
 
+/* Device status bit (tdsa_device_status) besides TDSA_ERR_TIMEOUT: a device-side index
+ * (a key-append slot) was outside its buffer; that store was skipped. */
+#define TDSA_STATUS_RANGE 8
+
 enum tdsa_dtype { TDSA_F32 = 0, TDSA_F16 = 1, TDSA_BF16 = 2 };
 
 /*
@@ -55,6 +59,31 @@ int tdsa_select_quantize(const void* in, int64_t in_row_stride, int64_t rows, in
                          void* stream);
 
 /*
+ * Decode-step key append.
+ * Replaces: LightningIndexerSidecar.encode_keys (src/temporal_dsa/sidecar.py:74-76) for one
+ *   new token per sequence, followed by the write of that key into the cache.
+ * For b < batch: raw = hidden[b] @ w_k^T (float32 accumulation, rounded to `dtype`, the
+ *   Linear's output), y = LayerNorm(raw) (float32, biased variance, eps, then *ln_weight
+ *   + ln_bias; NULL weight = 1, NULL bias = 0), RoPE on the first rope_dim features
+ *   (non-interleaved halves, angle = float32(positions[b]) * rope_theta^(-j/(rope_dim/2)),
+ *   sidecar.py:10-28), stored rounded to `dtype` at cache[b * cache_batch_stride +
+ *   slot * cache_row_stride + 0..127], slot = slots[b] (slots NULL: positions[b]).
+ *   A slot outside [0, cache_rows) skips that row's store and raises TDSA_STATUS_RANGE.
+ *   w_k is read as a constant (fetched before the wait on the previous kernel of `stream`):
+ *   it must not be written by a kernel still running on that stream.
+ * hidden [batch][hidden_size] and w_k [128][hidden_size] are 16-bit (dtype TDSA_BF16 or
+ *   TDSA_F16), 16-byte aligned, row strides multiples of 8 elements; hidden_size a
+ *   multiple of 8; positions/slots device int64 [batch]; rope_dim even, <= 128.
+ * One launch on `stream`.
+ */
+int tdsa_key_append(const void* hidden, int64_t hidden_stride, int hidden_size,
+                    const void* w_k, int64_t wk_row_stride, const float* ln_weight,
+                    const float* ln_bias, float eps, const int64_t* positions,
+                    const int64_t* slots, void* cache, int64_t cache_batch_stride,
+                    int64_t cache_row_stride, int64_t cache_rows, int dtype, int batch,
+                    int rope_dim, float rope_theta, void* stream);
+
+/*
  * Failure-path self-test (no reference counterpart): one kernel waits on an mbarrier that
  * nothing arrives on, with the same bounded loop every in-kernel wait of this library
  * uses but a limit of `limit_cycles` SM cycles; when the limit runs out it raises
@@ -70,7 +99,8 @@ const char* tdsa_version(void);
 const char* tdsa_last_error(void);
 
 /* Reads (and with reset != 0 clears) the device status word of the current device: the
- * OR of error bits kernels raised (TDSA_ERR_TIMEOUT when a bounded wait ran out).
+ * OR of error bits kernels raised (TDSA_ERR_TIMEOUT when a bounded wait ran out,
+ * TDSA_STATUS_RANGE when a device-side index was out of range).
  * Synchronous. */
 int tdsa_device_status(int* status_out, int reset);
 

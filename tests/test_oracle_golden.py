@@ -243,10 +243,17 @@ def test_sidecar_projection_matches_reference():
     np.testing.assert_allclose(q, g["q"][:, 0], rtol=1e-5, atol=5e-4)
     np.testing.assert_allclose(w, g["w"][:, 0], rtol=1e-5, atol=1e-7)
     # encode_keys = RoPE(LayerNorm(h @ wk^T)); LayerNorm(eps=1e-6) with unit affine
-    k = g["hk"][0].astype(np.float64) @ g["wk"].T.astype(np.float64)
-    k = (k - k.mean(-1, keepdims=True)) / np.sqrt(k.var(-1, keepdims=True) + 1e-6)
-    k[:, :64] = osc.apply_noninterleaved_rope(k[:, :64], np.arange(5))
+    k = osc.encode_keys(g["hk"][0], g["wk"], np.arange(5))
     np.testing.assert_allclose(k, g["k"][0], rtol=1e-4, atol=1e-5)
+    # the 16-bit rounding helper used for the Linear's output, against torch's casts
+    import torch
+
+    x = np.array([1.0, 1.00390625, 1.005859375, -3.0e38, 65520.0, 1e-9, 0.1, -2.5])
+    want = torch.from_numpy(x.astype(np.float32)).to(torch.bfloat16).double().numpy()
+    np.testing.assert_array_equal(osc.round_to(x, "bf16"), want)
+    with np.errstate(over="ignore"):
+        want = torch.from_numpy(x).to(torch.float16).double().numpy()
+    np.testing.assert_array_equal(osc.round_to(x, "f16"), want)
 
 
 def test_verifier_dim_sparse_oracle_matches_reference_golden():
