@@ -5,10 +5,11 @@ Run once, where the reference project is available (it is not on the GPU box):
     python tests/golden/make_golden.py --reference-src <path to temporal_dsa's src/>
     python tests/golden/make_golden.py --reference-src <...> --only verifier   # one fixture
     python tests/golden/make_golden.py --reference-src <...> --only trace
+    python tests/golden/make_golden.py --reference-src <...> --only approx
 
 Every output array below is computed by the reference's own functions
 (``temporal_dsa.progressive_kernel``, ``.metrics``, ``.certified``, ``.replay``,
-``.sidecar``, ``.verifier_scoring``, ``.trace``).  Inputs are seeded; small inputs are stored
+``.sidecar``, ``.verifier_scoring``, ``.trace``, ``.approx``, ``.verifier``).  Inputs are seeded; small inputs are stored
 verbatim (bf16 tensors as their uint16 bit patterns), the config-1 key cache is
 regenerated from its seed and pinned by a SHA-256 of its bytes.
 """
@@ -59,7 +60,7 @@ def bf16_inputs(length: int, seed: int = 1582):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True)
-    ap.add_argument("--only", choices=["verifier", "trace"], default=None,
+    ap.add_argument("--only", choices=["verifier", "trace", "approx"], default=None,
                     help="regenerate one fixture instead of all of them")
     args = ap.parse_args()
     sys.path.insert(0, args.reference_src)
@@ -71,6 +72,9 @@ def main() -> None:
         return
     if args.only == "trace":
         make_trace()
+        return
+    if args.only == "approx":
+        make_approx()
         return
 
     # ---- dense scores (f32 and bf16) -------------------------------------------------
@@ -261,6 +265,7 @@ def main() -> None:
                         q=eq.numpy(), w=ew.numpy(), hk=hk.numpy(), k=ek.numpy())
     make_verifier(verifier_scoring)
     make_trace()
+    make_approx()
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 
@@ -326,6 +331,111 @@ def make_trace() -> None:
                           workload=f["workload"], prompt_id=f["prompt_id"],
                           metadata=f["metadata"]))
     np.savez_compressed(HERE / "trace_rows.npz", rows=np.concatenate(rows), lengths=lengths)
+
+
+def policy_trace(seed: int, steps: int = 7, length0: int = 1500, growth: int = 37):
+    """A seeded decode-like score trace: every step appends `growth` keys; scores drift
+    slowly (a persistent per-key level plus small noise) and a few regions jump, so blocks
+    go hot and cold.  Returns float32 rows of increasing length."""
+    rng = np.random.default_rng(seed)
+    total = length0 + growth * (steps - 1)
+    level = (rng.normal(size=total) * 1.5).astype(np.float32)
+    rows = []
+    for t in range(steps):
+        length = length0 + growth * t
+        row = level[:length] + (rng.normal(size=length) * 0.35).astype(np.float32)
+        for _ in range(3):
+            a = int(rng.integers(0, length - 80))
+            row[a:a + 64] += np.float32(rng.uniform(1.5, 4.0))
+        rows.append(row.astype(np.float32))
+    return rows
+
+
+APPROX_POLICIES = {
+    # name: (ApproxPolicy keyword arguments, history_mode, block_size, fallback values)
+    "static_addr": (dict(name="static", gamma=0.5), "own", 64, None),
+    "dyn_addr": (dict(name="dynamic", gamma=0.25, dynamic_threshold=True), "own", 64, None),
+    "dyn_prevmax": (dict(name="dynamic_pm", gamma=0.1, dynamic_threshold=True,
+                         order="previous_max"), "own", 32, None),
+    "dyn_bucket": (dict(name="bucket", gamma=0.2, dynamic_threshold=True, order="bucket8",
+                        cold_streak=2), "own", 64, None),
+    "ema_risk": (dict(name="ema", gamma=0.3, dynamic_threshold=True, order="predicted_risk",
+                      risk_model="ema", ema_alpha=0.7, volatility_lambda=0.5, age_slope=0.05),
+                 "own", 64, None),
+    "refresh_age": (dict(name="refresh", gamma=0.0, refresh_interval=3, age_cap=2,
+                         recent_window=100), "own", 128, None),
+    "oracle_order": (dict(name="oracle", gamma=0.4, dynamic_threshold=True,
+                          order="oracle_current"), "own", 16, None),
+    "teacher": (dict(name="teacher", gamma=0.2, dynamic_threshold=True), "teacher", 64, None),
+    "fallback": (dict(name="fallback", gamma=0.3, fallback_threshold=0.5), "own", 64,
+                 [0.0, 0.1, 0.9, 0.2, 0.7, 0.0, 0.3]),
+    "full": (dict(name="full"), "own", 64, None),
+}
+
+
+def make_approx() -> None:
+    """approx.npz: approx.replay_step (approx.py:129-364) and verifier.verifier_step
+    (verifier.py:173-375) run by the reference over seeded traces, per policy and step:
+    the selection, the details, the next state and the counting metrics."""
+    from temporal_dsa.approx import ApproxPolicy, initialize_state, replay_step
+    from temporal_dsa.verifier import VerifierConfig, verifier_step
+
+    k = 128
+    out = {"k": np.int64(k)}
+    metric_keys = ["qk_scored", "blocks_refreshed", "blocks_skipped", "exact_match", "recall",
+                   "tau_seed", "tau_final", "full_refresh", "newly_hot_count",
+                   "newly_hot_missed", "missed_count", "worst_missed_rank", "index_mass_ratio",
+                   "top128_recall", "seed_blocks_touched", "physical_b16_blocks",
+                   "physical_b128_blocks", "cache256_hbm_keys", "metadata_bytes",
+                   "net_bf16_reduction"]
+    out["metric_keys"] = np.array(metric_keys)
+    for pi, (tag, (kw, mode, bs, fb)) in enumerate(APPROX_POLICIES.items()):
+        rows = policy_trace(100 + pi)
+        pol = ApproxPolicy(**kw)
+        out[f"{tag}_bs"] = np.int64(bs)
+        out[f"{tag}_mode"] = np.array(mode)
+        for t, r in enumerate(rows):
+            out[f"{tag}_s{t}_scores"] = r
+        state = initialize_state(rows[0], k=k, block_size=bs)
+        out[f"{tag}_s0_topk"] = state.topk
+        out[f"{tag}_s0_cold"] = state.cold_streak
+        for t in range(1, len(rows)):
+            state, m, d = replay_step(state, rows[t], policy=pol, k=k, block_size=bs, step=t,
+                                      history_mode=mode, previous_length=rows[t - 1].size,
+                                      fallback_value=None if fb is None else fb[t])
+            p = f"{tag}_s{t}_"
+            for name in ("approximate", "baseline", "evaluated", "refreshed_blocks",
+                         "skipped_blocks", "missed_ranks"):
+                out[p + name] = d[name]
+            for name in ("last_max", "ema", "volatility", "age", "cold_streak"):
+                out[p + name] = getattr(state, name)
+            out[p + "metrics"] = np.array([float(m[key]) for key in metric_keys])
+    # verifier_step: global-budget and fixed-threshold promotion over a dimension-sparse
+    # stand-in for the verifier scores (the current scores plus noise)
+    cfg = VerifierConfig(name="dimv", path="dim", width=32, score_ratio=0.25,
+                         block_size=64, rescue_fraction=0.1)
+    pol = ApproxPolicy(name="dynamic", gamma=0.2, dynamic_threshold=True)
+    rows = policy_trace(300)
+    rng = np.random.default_rng(301)
+    for mode, thr in (("budget", None), ("thresh", 2.5)):
+        state = initialize_state(rows[0], k=k, block_size=64)
+        for t in range(1, len(rows)):
+            vs = (rows[t] + rng.normal(size=rows[t].size) * 0.3).astype(np.float32)
+            state, m, d = verifier_step(state, rows[t], vs, policy=pol, config=cfg, k=k, step=t,
+                                        previous_length=rows[t - 1].size,
+                                        promotion_threshold=thr)
+            p = f"ver_{mode}_s{t}_"
+            out[p + "vscores"] = vs
+            for name in ("approximate", "rescued_blocks", "exact_candidates", "block_ranking"):
+                out[p + name] = d[name]
+            for name in ("last_max", "ema", "volatility", "age", "cold_streak"):
+                out[p + name] = getattr(state, name)
+            out[p + "metrics"] = np.array([float(m[key]) for key in (
+                "rescue_blocks", "rescue_exact_tokens", "candidate_union_tokens", "recall",
+                "cold_blocks_scanned", "cold_tokens_scanned")])
+    for t, r in enumerate(rows):
+        out[f"ver_s{t}_scores"] = r
+    np.savez_compressed(HERE / "approx.npz", **out)
 
 
 if __name__ == "__main__":
