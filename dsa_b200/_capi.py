@@ -28,6 +28,30 @@ TDSA_BF16 = 2
 
 i32, i64, vp, sz = C.c_int, C.c_int64, C.c_void_p, C.c_size_t
 
+
+class TdsaPolicy(C.Structure):
+    """struct tdsa_policy (include/tdsa.h)."""
+    _fields_ = [("gamma", C.c_double), ("ema_alpha", C.c_double),
+                ("volatility_lambda", C.c_double), ("age_slope", C.c_double),
+                ("cold_streak", i32), ("dynamic_threshold", i32), ("order", i32),
+                ("buckets", i32), ("age_cap", i32), ("recent_window", i32), ("risk_model", i32)]
+
+
+class TdsaRescue(C.Structure):
+    """struct tdsa_rescue (include/tdsa.h)."""
+    _fields_ = [("rescue_fraction", C.c_double), ("promotion_threshold", C.c_double),
+                ("use_threshold", i32)]
+
+
+TDSA_ORDER_ADDRESS, TDSA_ORDER_PREVIOUS_MAX = 0, 1
+TDSA_ORDER_BUCKET, TDSA_ORDER_ORACLE_CURRENT = 2, 3
+TDSA_RISK_LAST_MAX, TDSA_RISK_EMA = 0, 1
+POLICY_STATS = ["ERROR", "TAU_SEED", "TAU_FINAL", "SCORED", "UNION", "REFRESHED", "SKIPPED",
+                "RESCUED", "COLD_BLOCKS", "SEED_BLOCKS", "PHYS16", "PHYS32", "PHYS64", "PHYS128",
+                "TOP128", "TOP256", "TOP512", "TOP1024", "TOP2048", "MISSED", "WORST_MISSED",
+                "NEWLY_HOT", "NEWLY_HOT_MISSED", "MASS_NUM", "MASS_DEN", "BLOCKS"]
+TDSA_POLICY_NSTATS = len(POLICY_STATS)
+
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "tdsa_version": (C.c_char_p, []),
@@ -55,6 +79,13 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_topk_hist": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, vp]),
     "tdsa_key_append": (i32, [vp, i64, i32, vp, i64, vp, vp, C.c_float, vp, vp, vp, i64, i64,
                               i64, i32, i32, i32, C.c_float, vp]),
+    "tdsa_policy_state_bytes": (sz, [i32, i32, i32]),
+    "tdsa_policy_state_offsets": (i32, [i32, i32, i32, C.POINTER(C.c_int64)]),
+    "tdsa_policy_workspace_bytes": (sz, [i32, i32, i32, i32]),
+    "tdsa_policy_init": (i32, [vp, sz, vp, i64, i32, i32, i32, i32, i32, vp, sz, vp]),
+    "tdsa_policy_step": (i32, [vp, sz, vp, i64, vp, i64, i32, i32, i32, i32, i32, i32,
+                               C.POINTER(TdsaPolicy), i32, i32, C.POINTER(TdsaRescue), vp, sz,
+                               vp, i64, vp, vp, vp, vp]),
     "tdsa_score_dense_trace": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
                                      vp, i64, vp]),
     "tdsa_h8_block_max": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp,

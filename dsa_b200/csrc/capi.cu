@@ -487,6 +487,128 @@ int tdsa_pack_query_weights(const void* w_q, int64_t wq_row_stride, int hidden_s
   return launch_pack_wq(w_q, wq_row_stride, hidden_size, out, static_cast<cudaStream_t>(stream));
 }
 
+size_t tdsa_policy_state_bytes(int batch, int k, int max_blocks) {
+  if (batch < 1 || k < 1 || max_blocks < 1) return 0;
+  return policy_state_bytes(batch, k, max_blocks, nullptr);
+}
+
+int tdsa_policy_state_offsets(int batch, int k, int max_blocks, int64_t* offsets8) {
+  if (!offsets8 || batch < 1 || k < 1 || max_blocks < 1)
+    return fail(TDSA_ERR_INVALID, "bad policy state shape");
+  policy_state_bytes(batch, k, max_blocks, offsets8);
+  return TDSA_OK;
+}
+
+namespace {
+struct PolicyWs {
+  size_t masked, cmax, base_new, approx, topk, total;
+};
+PolicyWs policy_ws(int batch, int length, int k, int nbc) {
+  const size_t B = static_cast<size_t>(batch);
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  PolicyWs w;
+  size_t o = 0;
+  w.masked = o;   o = up(o + B * length * 4);
+  w.cmax = o;     o = up(o + B * nbc * 4);
+  w.base_new = o; o = up(o + B * k * 4);
+  w.approx = o;   o = up(o + B * k * 4);
+  w.topk = o;     o = up(o + topk_workspace_bytes(batch, length, k));
+  w.total = o;
+  return w;
+}
+
+int policy_checks(const void* state, size_t state_bytes, const float* scores, int64_t s_stride,
+                  int batch, int length, int k, int block_size, int max_blocks) {
+  if (!state || !scores) return fail(TDSA_ERR_INVALID, "null pointer");
+  if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
+  if (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128)
+    return fail(TDSA_ERR_UNSUPPORTED, "block_size must be 16, 32, 64 or 128");
+  if (k < 1 || k > length) return fail(TDSA_ERR_INVALID, "K cannot exceed the current length");
+  if (k > 2048) return fail(TDSA_ERR_UNSUPPORTED, "the policy takes k <= 2048");
+  if (length > 131072) return fail(TDSA_ERR_UNSUPPORTED, "the policy takes length <= 131072");
+  const int nb = (length + block_size - 1) / block_size;
+  if (max_blocks < nb || max_blocks > 4096)
+    return fail(TDSA_ERR_INVALID, "need ceil(length/block_size) <= max_blocks <= 4096");
+  if (batch > 1 && s_stride < length)
+    return fail(TDSA_ERR_INVALID, "score row stride must be >= length");
+  if (state_bytes < policy_state_bytes(batch, k, max_blocks, nullptr))
+    return fail(TDSA_ERR_WORKSPACE, "policy state buffer too small");
+  return TDSA_OK;
+}
+}  // namespace
+
+size_t tdsa_policy_workspace_bytes(int batch, int max_length, int k, int max_blocks) {
+  if (batch < 1 || max_length < 1 || k < 1 || k > max_length || max_blocks < 1) return 0;
+  return policy_ws(batch, max_length, k, max_blocks).total;
+}
+
+int tdsa_policy_init(void* state, size_t state_bytes, const float* scores, int64_t s_stride,
+                     int batch, int length, int k, int block_size, int max_blocks,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = policy_checks(state, state_bytes, scores, s_stride, batch, length, k, block_size,
+                         max_blocks);
+  if (rc) return rc;
+  const PolicyWs w = policy_ws(batch, length, k, max_blocks);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(TDSA_ERR_WORKSPACE, "policy workspace missing or too small");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  return launch_policy(1, static_cast<uint8_t*>(state), batch, k, max_blocks, scores,
+                       batch > 1 ? s_stride : length, nullptr, 0, length, length, block_size,
+                       nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0,
+                       reinterpret_cast<int32_t*>(ws + w.base_new), nullptr, ws + w.topk,
+                       w.total - w.topk, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int tdsa_policy_step(void* state, size_t state_bytes, const float* scores, int64_t s_stride,
+                     const float* verifier_scores, int64_t v_stride, int batch, int length,
+                     int previous_length, int k, int block_size, int max_blocks,
+                     const tdsa_policy* policy, int history_mode, int full_refresh,
+                     const tdsa_rescue* rescue, void* workspace, size_t workspace_bytes,
+                     uint32_t* evaluated_bits, int64_t bits_stride, uint8_t* block_flags,
+                     int32_t* ranking, double* stats, void* stream) {
+  int rc = policy_checks(state, state_bytes, scores, s_stride, batch, length, k, block_size,
+                         max_blocks);
+  if (rc) return rc;
+  if (!policy || !evaluated_bits || !block_flags || !stats)
+    return fail(TDSA_ERR_INVALID, "null policy, evaluated_bits, block_flags or stats");
+  if (history_mode != 0 && history_mode != 1)
+    return fail(TDSA_ERR_INVALID, "history_mode must be 0 (own) or 1 (teacher)");
+  if (policy->order < TDSA_ORDER_ADDRESS || policy->order > TDSA_ORDER_ORACLE_CURRENT)
+    return fail(TDSA_ERR_INVALID, "unknown block order");
+  if (policy->order == TDSA_ORDER_BUCKET && policy->buckets < 1)
+    return fail(TDSA_ERR_INVALID, "bucket order needs buckets >= 1");
+  if (policy->risk_model != TDSA_RISK_LAST_MAX && policy->risk_model != TDSA_RISK_EMA)
+    return fail(TDSA_ERR_INVALID, "unknown risk model");
+  if (rescue) {
+    if (!verifier_scores) return fail(TDSA_ERR_INVALID, "a rescue step needs verifier scores");
+    if (history_mode != 0) return fail(TDSA_ERR_INVALID, "the verifier step runs in own mode");
+    if (!rescue->use_threshold && !(rescue->rescue_fraction >= 0 && rescue->rescue_fraction <= 1))
+      return fail(TDSA_ERR_INVALID, "rescue_fraction must be in [0, 1]");
+    if (batch > 1 && v_stride < length)
+      return fail(TDSA_ERR_INVALID, "verifier score row stride must be >= length");
+  }
+  if (previous_length < 0) return fail(TDSA_ERR_INVALID, "previous_length must be >= 0");
+  if (bits_stride < (length + 31) / 32 && batch > 1)
+    return fail(TDSA_ERR_INVALID, "bits_stride must be >= ceil(length / 32)");
+  if (policy_decide_smem_bytes(length, block_size, k) > 227 * 1024)
+    return fail(TDSA_ERR_UNSUPPORTED, "this length / block size / k needs too much shared memory");
+  const PolicyWs w = policy_ws(batch, length, k, max_blocks);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(TDSA_ERR_WORKSPACE, "policy workspace missing or too small");
+  int* status = device_status_ptr();
+  if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  return launch_policy(
+      0, static_cast<uint8_t*>(state), batch, k, max_blocks, scores,
+      batch > 1 ? s_stride : length, rescue ? verifier_scores : nullptr,
+      batch > 1 ? v_stride : length, length, previous_length, block_size, policy, history_mode,
+      full_refresh, rescue, reinterpret_cast<float*>(ws + w.masked),
+      reinterpret_cast<float*>(ws + w.cmax), block_flags, ranking, evaluated_bits,
+      batch > 1 ? bits_stride : (length + 31) / 32, reinterpret_cast<int32_t*>(ws + w.base_new),
+      reinterpret_cast<int32_t*>(ws + w.approx), ws + w.topk, w.total - w.topk, stats, status,
+      static_cast<cudaStream_t>(stream));
+}
+
 int tdsa_key_append(const void* hidden, int64_t hidden_stride, int hidden_size,
                     const void* w_k, int64_t wk_row_stride, const float* ln_weight,
                     const float* ln_bias, float eps, const int64_t* positions,

@@ -6,6 +6,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "../../include/tdsa.h"
+
 namespace tdsa {
 
 constexpr int kTopkSegment = 32768;    // keys one top-k CTA holds in shared memory
@@ -102,6 +104,17 @@ int launch_select_quantize(const void* in, int64_t in_stride, int64_t rows, int 
 int launch_bounded_wait_selftest(long long limit_cycles, cudaStream_t stream, int* status);
 size_t packed_wq_bytes(int hidden);
 int launch_pack_wq(const void* wq, int64_t stride, int hidden, void* out, cudaStream_t stream);
+// ---- temporal policy state machine (policy.cu)
+size_t policy_state_bytes(int batch, int k, int nbc, int64_t* offsets);
+size_t policy_decide_smem_bytes(int length, int bs, int k);
+int launch_policy(int init, uint8_t* state, int batch, int k, int nbc, const float* scores,
+                  int64_t s_stride, const float* vscores, int64_t v_stride, int length,
+                  int prev_length, int bs, const tdsa_policy* pol, int teacher,
+                  int full_refresh, const tdsa_rescue* rescue, float* masked, float* cmax,
+                  uint8_t* flags, int32_t* ranking, uint32_t* ebits, int64_t e_stride,
+                  int32_t* base_new, int32_t* approx, void* topk_ws, size_t topk_ws_bytes,
+                  double* stats, int* status, cudaStream_t stream);
+
 // ---- decode-step key append (key_append.cu)
 int launch_key_append(const void* hidden, int64_t hidden_stride, int hidden_size,
                       const void* wk, int64_t wk_stride, const float* ln_w, const float* ln_b,

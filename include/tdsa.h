@@ -84,6 +84,102 @@ int tdsa_key_append(const void* hidden, int64_t hidden_stride, int hidden_size,
                     int rope_dim, float rope_theta, void* stream);
 
 /*
+ * Temporal policy state machine on the device (no host round trip per step).
+ * Replaces: approx.initialize_state / approx.replay_step (src/temporal_dsa/approx.py:112-364)
+ *   and verifier.verifier_step's rescue and rerank (src/temporal_dsa/verifier.py:103-375),
+ *   which the reference runs in numpy on a copy of each step's scores
+ *   (scripts/evaluate_teacher_forced.py:163-230).
+ * State (per sequence, opaque buffer of tdsa_policy_state_bytes; tdsa_policy_state_offsets
+ *   gives the byte offsets of its arrays): topk and baseline_topk [batch][k] int32 (stable
+ *   top-k order), last_max, ema, volatility [batch][max_blocks] float32, age, cold_streak
+ *   [batch][max_blocks] int16, and the block count each sequence's arrays hold.
+ * tdsa_policy_init -- initialize_state for `batch` rows of `length` scores.
+ * tdsa_policy_step -- replay_step (rescue NULL) or verifier_step (rescue given, with the
+ *   verifier scores): history_mode 0 = "own", 1 = "teacher"; full_refresh is the host's
+ *   (policy.name == "full" or refresh_interval divides step or fallback) flag.  The new
+ *   selection is left in the state's topk.  Outputs: evaluated_bits [batch][bits_stride]
+ *   (bit j = key j read, after any rescue), block_flags [batch][max_blocks] (bit0 forced,
+ *   bit1 read by the policy, bit2 rescued, bit3 holds a seed key, bit4 holds a cold key),
+ *   ranking [batch][max_blocks] (rescue: cold blocks by verifier maximum; may be NULL),
+ *   stats [batch][TDSA_POLICY_NSTATS] (TDSA_PST_*; TDSA_PST_ERROR = 1 when the seed is not
+ *   k distinct keys below length: the state is then unchanged).
+ * Limits: k <= 2048, block_size 16/32/64/128, ceil(length/block_size) <= max_blocks <= 4096,
+ *   length <= 131072.  Scores are expected finite (a key whose score is -inf ties with the
+ *   keys the policy did not read).  All device buffers; asynchronous on `stream`.
+ */
+enum tdsa_block_order {
+  TDSA_ORDER_ADDRESS = 0,
+  TDSA_ORDER_PREVIOUS_MAX = 1, /* also "predicted_risk" */
+  TDSA_ORDER_BUCKET = 2,       /* "bucketN", N in tdsa_policy.buckets */
+  TDSA_ORDER_ORACLE_CURRENT = 3
+};
+enum tdsa_risk_model { TDSA_RISK_LAST_MAX = 0, TDSA_RISK_EMA = 1 };
+
+typedef struct tdsa_policy { /* approx.py:15-39 ApproxPolicy */
+  double gamma;
+  double ema_alpha;
+  double volatility_lambda;
+  double age_slope;
+  int cold_streak;
+  int dynamic_threshold;
+  int order;  /* tdsa_block_order */
+  int buckets;
+  int age_cap; /* < 0: none */
+  int recent_window;
+  int risk_model; /* tdsa_risk_model */
+} tdsa_policy;
+
+typedef struct tdsa_rescue { /* verifier.py:15-43 VerifierConfig + promotion threshold */
+  double rescue_fraction;
+  double promotion_threshold;
+  int use_threshold; /* 0: rescue ceil(rescue_fraction * cold blocks) best blocks */
+} tdsa_rescue;
+
+enum tdsa_policy_stat {
+  TDSA_PST_ERROR = 0,
+  TDSA_PST_TAU_SEED,
+  TDSA_PST_TAU_FINAL,
+  TDSA_PST_SCORED,     /* keys the temporal policy read (seed + refreshed blocks) */
+  TDSA_PST_UNION,      /* keys read after the rescue */
+  TDSA_PST_REFRESHED,
+  TDSA_PST_SKIPPED,
+  TDSA_PST_RESCUED,
+  TDSA_PST_COLD_BLOCKS,
+  TDSA_PST_SEED_BLOCKS,
+  TDSA_PST_PHYS16, /* 16/32/64/128-key blocks holding a key read */
+  TDSA_PST_PHYS32,
+  TDSA_PST_PHYS64,
+  TDSA_PST_PHYS128,
+  TDSA_PST_TOP128, /* baseline[:N] members in the selection, N = 128 ... 2048 */
+  TDSA_PST_TOP256,
+  TDSA_PST_TOP512,
+  TDSA_PST_TOP1024,
+  TDSA_PST_TOP2048,
+  TDSA_PST_MISSED,
+  TDSA_PST_WORST_MISSED,
+  TDSA_PST_NEWLY_HOT,
+  TDSA_PST_NEWLY_HOT_MISSED,
+  TDSA_PST_MASS_NUM, /* sum exp(score - max baseline score) over the selection */
+  TDSA_PST_MASS_DEN, /* ... over the baseline */
+  TDSA_PST_BLOCKS,
+  TDSA_POLICY_NSTATS
+};
+
+size_t tdsa_policy_state_bytes(int batch, int k, int max_blocks);
+int tdsa_policy_state_offsets(int batch, int k, int max_blocks, int64_t* offsets8);
+size_t tdsa_policy_workspace_bytes(int batch, int max_length, int k, int max_blocks);
+int tdsa_policy_init(void* state, size_t state_bytes, const float* scores, int64_t s_stride,
+                     int batch, int length, int k, int block_size, int max_blocks,
+                     void* workspace, size_t workspace_bytes, void* stream);
+int tdsa_policy_step(void* state, size_t state_bytes, const float* scores, int64_t s_stride,
+                     const float* verifier_scores, int64_t v_stride, int batch, int length,
+                     int previous_length, int k, int block_size, int max_blocks,
+                     const tdsa_policy* policy, int history_mode, int full_refresh,
+                     const tdsa_rescue* rescue, void* workspace, size_t workspace_bytes,
+                     uint32_t* evaluated_bits, int64_t bits_stride, uint8_t* block_flags,
+                     int32_t* ranking, double* stats, void* stream);
+
+/*
  * Failure-path self-test (no reference counterpart): one kernel waits on an mbarrier that
  * nothing arrives on, with the same bounded loop every in-kernel wait of this library
  * uses but a limit of `limit_cycles` SM cycles; when the limit runs out it raises

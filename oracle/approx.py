@@ -69,13 +69,15 @@ def initialize_state(scores, *, k: int, block_size: int) -> SimpleNamespace:
 
 
 def policy_risk(policy, last_max, ema, volatility, age) -> np.ndarray:
-    """approx.py:186-198 -- float64 risk per block."""
+    """approx.py:186-198 -- float64 risk per block, summed left to right.  The reference's
+    ``volatility_lambda * volatility`` multiplies a float32 array by a Python float, which
+    NumPy 2 evaluates in float32; ``age_slope * age`` (int16 array) is float64."""
     slope = policy.age_slope * age.astype(np.float64)
     if policy.risk_model == "last_max":
         return last_max.astype(np.float64) + policy.gamma + slope
     if policy.risk_model == "ema":
-        return (ema.astype(np.float64) + policy.volatility_lambda * volatility.astype(np.float64)
-                + policy.gamma + slope)
+        spread = (np.float32(policy.volatility_lambda) * volatility.astype(np.float32))
+        return ema.astype(np.float64) + spread.astype(np.float64) + policy.gamma + slope
     raise ValueError(f"unknown risk model: {policy.risk_model}")
 
 
