@@ -340,9 +340,76 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         line["latency_b1_l32k"] = single_sequence_latency(wl, proj[0], device)
         line["trace_emission"] = trace_overhead(wl, proj, plans, device)
         line["key_append"] = key_append_latency(wl, device)
+        line["policy_step"] = policy_step_latency(wl, device,
+                                                  cpu=not args.no_cpu_baseline)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
     return line
+
+
+def policy_step_latency(wl: Config4, device: torch.device, steps: int = 8,
+                        cpu: bool = True) -> dict:
+    """The temporal policy's decode step (approx.replay_step, dynamic threshold, address
+    order, block 64) for the config-4 batch: every sequence's state on the device, one
+    tdsa_policy_step per decode step (dense top-k, decide, selection top-k, finalize).
+    Scores are a seeded drifting trace (a persistent per-key level, small noise, one jumping
+    region per step) growing by one key per step.  Timed with CUDA events over `steps`
+    steps; the CPU leg times the numpy restatement of the same step on one sequence."""
+    from dsa_b200.approx import ApproxPolicy, PolicyPlan
+
+    # the rows end at the config's length (32768): the top-k kernels then hold each row in
+    # one segment, as in the config-4 step
+    b, k, bs = wl.batch, wl.k, 64
+    length0 = wl.length - (steps + 4)
+    g = torch.Generator(device=device)
+    g.manual_seed(99)
+    total = length0 + steps + 4
+    level = torch.randn(b, total, generator=g, device=device) * 1.5
+    rows = []
+    for t in range(steps + 4):
+        n = length0 + t
+        row = level[:, :n] + torch.randn(b, n, generator=g, device=device) * 0.35
+        a0 = (t * 977) % (n - 200)
+        row[:, a0:a0 + 128] += 2.5
+        rows.append(row.contiguous())
+    pol = ApproxPolicy(name="dynamic", gamma=0.25, dynamic_threshold=True)
+    plan = PolicyPlan(b, total, k, bs, device)
+    plan.init(rows[0])
+    for t in range(1, 4):
+        plan.step(rows[t], pol, step=t, previous_length=rows[t - 1].shape[1])
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for t in range(4, 4 + steps):
+        plan.step(rows[t], pol, step=t, previous_length=rows[t - 1].shape[1])
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    us = e0.elapsed_time(e1) / steps * 1e3
+    st = plan.stats_host()
+    out = {"us_per_step": us, "batch": b, "length": length0, "k": k, "block_size": bs,
+           "policy": "dynamic threshold, address order, gamma 0.25",
+           "sequence_steps_per_s": b / (us * 1e-6),
+           "blocks_refreshed_mean": statistics.fmean(r["REFRESHED"] for r in st),
+           "blocks": int(st[0]["BLOCKS"]),
+           "api": "dsa_b200.approx.PolicyPlan (C ABI tdsa_policy_step)"}
+    if cpu:
+        from types import SimpleNamespace
+
+        from oracle import approx as oa
+
+        r0 = rows[3][0].cpu().numpy()
+        r1 = rows[4][0].cpu().numpy()
+        ns = SimpleNamespace(**{**pol.__dict__})
+        state = oa.initialize_state(r0, k=k, block_size=bs)
+        t0 = time.perf_counter()
+        oa.replay_step(state, r1, policy=ns, k=k, block_size=bs, step=4,
+                       previous_length=r0.size)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"sequence_steps_per_s": 1.0 / dt, "cores": 1, "kind": "port",
+                               "sample": "one sequence-step of the numpy restatement "
+                                         "(oracle/approx.py), single thread"}
+    return out
 
 
 def key_append_latency(wl: Config4, device: torch.device, per_graph: int = 20,

@@ -11,12 +11,15 @@
 //                           top-k lists) and the step's statistics
 //
 // The dynamic threshold (the running k-th best score of everything read so far, which
-// decides the next block) is inherently sequential over the visiting order.  One warp walks
-// the order; the running top-k is kept as two ascending lists of 64-bit items -- a main list
-// of k items and a pending list of recent insertions -- so a block whose unseen keys beat
-// the current minimum costs one warp sort of those keys, one warp merge into the pending
-// list and a binary search for the items that drop out; blocks that are skipped or add
-// nothing cost a few instructions.  Items are (order-preserving score key << 32) |
+// decides the next block) is sequential over the visiting order.  The CTA walks the order
+// in windows of up to 32 positions, holding the running top-k as two ascending lists of
+// 64-bit items (a main list of k items and a short pending list of insertions).  Per
+// window: one warp per candidate block (a block not already below the threshold) collects
+// its unseen items above the threshold; the CTA sorts them (bitonic), merges them into the
+// pending list (merge path) and one warp finds the items that drop out (32-way search).
+// If every candidate still passes against the threshold after all of them, that is the
+// exact outcome (each saw a threshold no higher); otherwise the window is retried one block
+// at a time.  The window doubles after each success.  Items are (order-preserving score key << 32) |
 // (0xFFFFFFFF - index): larger item = higher score, then lower index, the reference heap's
 // order (approx.py:214-236).
 #include <algorithm>
@@ -31,7 +34,11 @@ namespace tdsa {
 namespace {
 
 constexpr int kPolThreads = 1024;
-constexpr int kPendCap = 512;  // pending list capacity (>= the largest block, 128)
+constexpr int kPendCap = 2048;   // pending list capacity (>= the window capacity)
+constexpr int kWindowCap = 1024; // items one window may insert at once (>= a block, 128)
+static_assert(kWindowCap <= kPendCap, "a window must fit the pending list");
+constexpr int kMaxWindow = 128;  // positions of the visiting order one window may span
+static_assert(kMaxWindow % 32 == 0, "whole warps of candidates");
 
 __device__ __forceinline__ uint64_t item_of(float s, int idx) {
   return (static_cast<uint64_t>(float_to_key(s)) << 32) |
@@ -99,26 +106,6 @@ __device__ void cta_sort_keys(uint64_t* key, int n) {
   __syncthreads();
 }
 
-// ascending bitonic sort of n (power of two, <= 128) keys by one warp
-__device__ void warp_sort_keys(uint64_t* key, int n, int lane) {
-  for (int size = 2; size <= n; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      __syncwarp();
-      for (int i = lane; i < (n >> 1); i += 32) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool up = (lo & size) == 0;
-        const uint64_t kl = key[lo], kh = key[hi];
-        if ((kl > kh) == up) {
-          key[lo] = kh;
-          key[hi] = kl;
-        }
-      }
-    }
-  }
-  __syncwarp();
-}
-
 // number of elements the first d outputs of merge(x, y) take from x (distinct items)
 __device__ __forceinline__ int merge_split(const uint64_t* x, int n1, const uint64_t* y, int n2,
                                            int d) {
@@ -133,20 +120,40 @@ __device__ __forceinline__ int merge_split(const uint64_t* x, int n1, const uint
   return lo;
 }
 
-// out = merge(x[0..n1), y[0..n2)), ascending, by one warp (merge path)
-__device__ void warp_merge(const uint64_t* x, int n1, const uint64_t* y, int n2, uint64_t* out,
-                           int lane) {
-  const int n = n1 + n2;
-  const int per = (n + 31) >> 5;
-  const int d0 = min(n, lane * per), d1 = min(n, d0 + per);
-  int i = merge_split(x, n1, y, n2, d0), j = d0 - i;
-  for (int o = d0; o < d1; ++o) {
-    if (j >= n2 || (i < n1 && x[i] < y[j]))
-      out[o] = x[i++];
-    else
-      out[o] = y[j++];
+// merge_split by a whole warp: a 32-way search (every lane probes one split point per
+// round), the same answer on every lane
+__device__ __forceinline__ int warp_split(const uint64_t* x, int n1, const uint64_t* y, int n2,
+                                          int d, int lane) {
+  int lo = d > n2 ? d - n2 : 0, hi = d < n1 ? d : n1;
+  while (lo < hi) {
+    const int step = (hi - lo + 31) >> 5;
+    const int a = lo + lane * step;
+    const bool pred = a < hi && x[a] < y[d - 1 - a];  // true on a prefix of the lanes
+    const int cnt = __popc(__ballot_sync(0xffffffffu, pred));
+    const int nlo = cnt ? lo + (cnt - 1) * step + 1 : lo;
+    const int nhi = (cnt < 32 && lo + cnt * step < hi) ? lo + cnt * step : hi;
+    lo = nlo;
+    hi = nhi;
   }
-  __syncwarp();
+  return lo;
+}
+
+// out = merge(x[0..n1), y[0..n2)), ascending, by the whole CTA (merge path); ends with a
+// barrier
+__device__ void cta_merge(const uint64_t* x, int n1, const uint64_t* y, int n2, uint64_t* out) {
+  const int n = n1 + n2;
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int d0 = min(n, static_cast<int>(threadIdx.x) * per), d1 = min(n, d0 + per);
+  if (d0 < d1) {
+    int i = merge_split(x, n1, y, n2, d0), j = d0 - i;
+    for (int o = d0; o < d1; ++o) {
+      if (j >= n2 || (i < n1 && x[i] < y[j]))
+        out[o] = x[i++];
+      else
+        out[o] = y[j++];
+    }
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ float block_reduce_min(float v, float* red) {
@@ -182,6 +189,114 @@ __device__ __forceinline__ T block_reduce_sum(T v, T* red) {
   return red[0];
 }
 
+// sums of N per-thread counters over the CTA in one pass (red: >= 32 * N ints); every
+// thread gets the totals
+template <int N>
+__device__ __forceinline__ void block_reduce_sum_n(int (&v)[N], int* red) {
+#pragma unroll
+  for (int q = 0; q < N; ++q)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(0xffffffffu, v[q], o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0)
+#pragma unroll
+    for (int q = 0; q < N; ++q) red[q * 32 + (threadIdx.x >> 5)] = v[q];
+  __syncthreads();
+  if (threadIdx.x < 32) {
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+      int x = threadIdx.x < (blockDim.x >> 5) ? red[q * 32 + threadIdx.x] : 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (threadIdx.x == 0) red[q * 32] = x;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < N; ++q) v[q] = red[q * 32];
+  __syncthreads();
+}
+
+// ascending bitonic sort of up to 64 keys held two per lane (lane l: elements 2l, 2l+1),
+// by shuffles; every lane returns its two sorted elements
+__device__ __forceinline__ void warp_sort64(uint64_t& x0, uint64_t& x1, int lane) {
+  for (int size = 2; size <= 64; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride == 1) {
+        const bool up = ((2 * lane) & size) == 0;
+        if ((x0 > x1) == up) {
+          const uint64_t t = x0;
+          x0 = x1;
+          x1 = t;
+        }
+      } else {
+        const int ls = stride >> 1;  // partner lane distance
+        const uint64_t y0 = __shfl_xor_sync(0xffffffffu, x0, ls);
+        const uint64_t y1 = __shfl_xor_sync(0xffffffffu, x1, ls);
+        const bool lower = (lane & ls) == 0;
+        const bool up = ((2 * lane) & size) == 0;
+        // the lower element of each pair keeps min when ascending
+        const bool keep_min = lower == up;
+        x0 = keep_min ? (x0 < y0 ? x0 : y0) : (x0 > y0 ? x0 : y0);
+        x1 = keep_min ? (x1 < y1 ? x1 : y1) : (x1 > y1 ? x1 : y1);
+      }
+    }
+  }
+}
+
+// ascending bitonic sort of n keys (a power of two, 64 <= n <= 2 * blockDim.x), two per
+// thread (thread t: elements 2t, 2t+1): partners within a warp by shuffles, farther ones
+// through shared memory
+__device__ void cta_sort_keys_reg(uint64_t* key, int n) {
+  __syncthreads();  // the keys were written by other threads
+  const int t = threadIdx.x, lane = t & 31;
+  // whole warps are active or not (n >= 64); idle warps only meet the barriers
+  const bool act = 2 * t < n;
+  uint64_t x0 = act ? key[2 * t] : 0ull, x1 = act ? key[2 * t + 1] : 0ull;
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const bool up = ((2 * t) & size) == 0;
+      if (stride > 32) {  // partner in another warp: through shared memory
+        __syncthreads();
+        if (act) {
+          key[2 * t] = x0;
+          key[2 * t + 1] = x1;
+        }
+        __syncthreads();
+        const int ts2 = stride >> 1;  // partner thread distance
+        if (act) {
+          const int pt = t ^ ts2;
+          const uint64_t y0 = key[2 * pt], y1 = key[2 * pt + 1];
+          const bool keep_min = ((t & ts2) == 0) == up;
+          x0 = keep_min ? (x0 < y0 ? x0 : y0) : (x0 > y0 ? x0 : y0);
+          x1 = keep_min ? (x1 < y1 ? x1 : y1) : (x1 > y1 ? x1 : y1);
+        }
+      } else if (act) {
+        if (stride == 1) {
+          if ((x0 > x1) == up) {
+            const uint64_t tmp = x0;
+            x0 = x1;
+            x1 = tmp;
+          }
+        } else {
+          const int ls = stride >> 1;
+          const uint64_t y0 = __shfl_xor_sync(0xffffffffu, x0, ls);
+          const uint64_t y1 = __shfl_xor_sync(0xffffffffu, x1, ls);
+          const bool keep_min = ((lane & ls) == 0) == up;
+          x0 = keep_min ? (x0 < y0 ? x0 : y0) : (x0 > y0 ? x0 : y0);
+          x1 = keep_min ? (x1 < y1 ? x1 : y1) : (x1 > y1 ? x1 : y1);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (act) {
+    key[2 * t] = x0;
+    key[2 * t + 1] = x1;
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ int block_reduce_min_int(int v, int* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -198,10 +313,19 @@ __device__ __forceinline__ int block_reduce_min_int(int v, int* red) {
   return red[0];
 }
 
+// control state of the dynamic-threshold walk (shared by the CTA)
+struct WalkCtl {
+  uint64_t T;   // the running minimum item (the threshold)
+  double ts;    // its score
+  int a_sel, p_sel, ha, na, hp, np;  // main list mains[a_sel][ha..na), pending [hp..np)
+  int pos, w, ncand, tot;
+  int cand[kMaxWindow], cnt[kMaxWindow], off[kMaxWindow];
+};
+
 // shared-memory carve of the decide kernel
 struct DecideSmem {
   int words, nb, nbp, kp;
-  size_t bits, risk, cmax, fl, skey, sidx, A, A2, P, P2, C, red, total;
+  size_t bits, risk, cmax, fl, skey, sidx, A, A2, P, P2, C, CI, ctl, red, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -225,11 +349,13 @@ __host__ __device__ inline DecideSmem decide_smem(int length, int bs, int k) {
   d.A2 = o;    o = align_up(o + sizeof(uint64_t) * d.kp, 16);
   d.P = o;     o = align_up(o + sizeof(uint64_t) * kPendCap, 16);
   d.P2 = o;    o = align_up(o + sizeof(uint64_t) * kPendCap, 16);
-  d.C = o;     o = align_up(o + sizeof(uint64_t) * 128, 16);
+  d.C = o;     o = align_up(o + sizeof(uint64_t) * kWindowCap, 16);
+  d.CI = o;    o = align_up(o + sizeof(uint64_t) * 32 * bs, 16);
+  d.ctl = o;   o = align_up(o + sizeof(WalkCtl), 16);
   d.bits = o;  o = align_up(o + sizeof(uint32_t) * d.words, 16);
   d.cmax = o;  o = align_up(o + sizeof(float) * d.nb, 16);
   d.sidx = o;  o = align_up(o + sizeof(uint32_t) * d.nbp, 16);
-  d.red = o;   o = align_up(o + 64 * sizeof(double), 16);
+  d.red = o;   o = align_up(o + 32 * 12 * sizeof(int), 16);
   d.fl = o;    o = align_up(o + d.nb, 16);
   d.total = o;
   return d;
@@ -324,13 +450,17 @@ __global__ void __launch_bounds__(kPolThreads, 1) policy_decide_kernel(const Pol
   uint64_t* P = reinterpret_cast<uint64_t*>(sm + d.P);
   uint64_t* P2 = reinterpret_cast<uint64_t*>(sm + d.P2);
   uint64_t* C = reinterpret_cast<uint64_t*>(sm + d.C);
+  uint64_t* CI = reinterpret_cast<uint64_t*>(sm + d.CI);  // [32][bs] items per candidate
+  WalkCtl* ctl = reinterpret_cast<WalkCtl*>(sm + d.ctl);
   double* red = reinterpret_cast<double*>(sm + d.red);
+  int* ired = reinterpret_cast<int*>(sm + d.red);
 
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = a.length, bs = a.bs, nb = d.nb, k = a.k;
+  const int lbs = __ffs(bs) - 1;  // block sizes are powers of two
   const float* s = a.scores + b * a.s_stride;
   const int64_t so = static_cast<int64_t>(b) * a.nbc;
   const int nb_prev = a.nblocks[b];
@@ -369,40 +499,61 @@ __global__ void __launch_bounds__(kPolThreads, 1) policy_decide_kernel(const Pol
     return;
   }
 
-  // per-block maxima, risk (approx.py:186-198) and forced reads (:241-248)
-  for (int blk = warp; blk < nb; blk += kPolThreads / 32) {
-    const int lo = blk * bs, n = min(bs, L - lo);
-    float m = -INFINITY;
+  // risk (approx.py:186-198) and forced reads (:241-248): one thread per block, the state
+  // arrays read coalesced; whether the block holds a seed key comes from the bitmap
+  for (int blk = tid; blk < nb; blk += kPolThreads) {
+    const int16_t ag = a.age[so + blk];
+    const double slope = a.age_slope * static_cast<double>(ag);
+    double r;
+    if (a.risk_ema) {
+      const float spread = __fmul_rn(static_cast<float>(a.vol_lambda), a.vol[so + blk]);
+      r = __dadd_rn(__dadd_rn(__dadd_rn(static_cast<double>(a.ema[so + blk]),
+                                        static_cast<double>(spread)),
+                              a.gamma),
+                    slope);
+    } else {
+      r = __dadd_rn(__dadd_rn(static_cast<double>(a.last_max[so + blk]), a.gamma), slope);
+    }
+    risk[blk] = r;
+    bool forced = a.full_refresh != 0;
+    forced |= a.prev_length < L && blk >= a.prev_length / bs;
+    forced |= a.recent_window > 0 && blk >= max(0, L - a.recent_window) / bs;
+    forced |= a.age_cap >= 0 && ag >= a.age_cap;
+    forced |= a.cold[so + blk] < a.cold_streak;
     bool has_seed = false;
-    for (int e = lane; e < n; e += 32) {
-      const int j = lo + e;
-      m = nan_max(m, s[j]);
-      has_seed |= (bits[j >> 5] >> (j & 31)) & 1u;
+    const int lo = blk * bs, hi = min(L, lo + bs);
+    for (int w = lo >> 5; w <= (hi - 1) >> 5; ++w) {
+      uint32_t word = bits[w];
+      const int w0 = w * 32;
+      if (lo > w0) word &= ~0u << (lo - w0);
+      if (hi < w0 + 32) word &= (1u << (hi - w0)) - 1u;
+      has_seed |= word != 0;
+    }
+    fl[blk] = (forced ? 1u : 0u) | (has_seed ? 8u : 0u);
+  }
+  // per-block maxima (numpy's NaN-propagating max): a warp takes four blocks at a time so
+  // their loads are in flight together
+  for (int blk0 = warp; blk0 < nb; blk0 += 4 * (kPolThreads / 32)) {
+    float m[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int blk = blk0 + u * (kPolThreads / 32);
+      m[u] = -INFINITY;
+      if (blk < nb) {
+        const int lo = blk * bs, n = min(bs, L - lo);
+        for (int e = lane; e < n; e += 32) m[u] = nan_max(m[u], s[lo + e]);
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, o));
-    has_seed = __any_sync(0xffffffffu, has_seed);
-    if (lane == 0) {
-      cmax[blk] = m;
-      a.cmax[so + blk] = m;
-      const double slope = a.age_slope * static_cast<double>(a.age[so + blk]);
-      double r;
-      if (a.risk_ema) {
-        const float spread = __fmul_rn(static_cast<float>(a.vol_lambda), a.vol[so + blk]);
-        r = __dadd_rn(__dadd_rn(__dadd_rn(static_cast<double>(a.ema[so + blk]),
-                                          static_cast<double>(spread)),
-                                a.gamma),
-                      slope);
-      } else {
-        r = __dadd_rn(__dadd_rn(static_cast<double>(a.last_max[so + blk]), a.gamma), slope);
+    for (int u = 0; u < 4; ++u) {
+      const int blk = blk0 + u * (kPolThreads / 32);
+      float mu = m[u];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mu = nan_max(mu, __shfl_xor_sync(0xffffffffu, mu, o));
+      if (lane == 0 && blk < nb) {
+        cmax[blk] = mu;
+        a.cmax[so + blk] = mu;
       }
-      risk[blk] = r;
-      bool forced = a.full_refresh != 0;
-      forced |= a.prev_length < L && blk >= a.prev_length / bs;
-      forced |= a.recent_window > 0 && blk >= max(0, L - a.recent_window) / bs;
-      forced |= a.age_cap >= 0 && a.age[so + blk] >= a.age_cap;
-      forced |= a.cold[so + blk] < a.cold_streak;
-      fl[blk] = (forced ? 1u : 0u) | (has_seed ? 8u : 0u);
     }
   }
   __syncthreads();
@@ -448,75 +599,225 @@ __global__ void __launch_bounds__(kPolThreads, 1) policy_decide_kernel(const Pol
     // the running top-k starts as the seed items, ascending
     for (int i = tid; i < d.kp; i += kPolThreads)
       A[i] = i < k ? item_of(s[seed[i]], seed[i]) : ~0ull;
-    cta_sort_keys(A, d.kp);
-    if (warp == 0) {
-      uint64_t* Ac = A;
-      uint64_t* An = A2;
-      uint64_t* Pc = P;
-      uint64_t* Pn = P2;
-      int ha = 0, na = k, hp = 0, np_ = 0;
-      auto tmin = [&]() -> uint64_t {
-        uint64_t t = ha < na ? Ac[ha] : ~0ull;
-        if (hp < np_ && Pc[hp] < t) t = Pc[hp];
-        return t;
-      };
-      uint64_t T = tmin();
-      double ts = static_cast<double>(item_score(T));
-      for (int pos = 0; pos < nb; ++pos) {
-        const int blk = static_cast<int>(sidx[pos]);
-        const uint8_t f = fl[blk];
-        if (!(f & 1u) && risk[blk] < ts) continue;
-        __syncwarp();
-        if (lane == 0) fl[blk] = f | 2u;
-        const int lo = blk * bs, n = min(bs, L - lo);
-        int m = 0;
-        for (int e0 = 0; e0 < n; e0 += 32) {
-          const int e = e0 + lane;
-          bool c = false;
-          uint64_t it = 0;
-          if (e < n) {
-            const int j = lo + e;
-            if (!((bits[j >> 5] >> (j & 31)) & 1u)) {
-              it = item_of(s[j], j);
-              c = it > T;
-            }
-          }
-          const unsigned bal = __ballot_sync(0xffffffffu, c);
-          if (c) C[m + __popc(bal & ((1u << lane) - 1u))] = it;
-          m += __popc(bal);
-        }
-        if (m == 0) continue;
-        const int mp = pow2_at_least(m, 2);
-        for (int e = m + lane; e < mp; e += 32) C[e] = ~0ull;
-        warp_sort_keys(C, mp, lane);
-        if ((np_ - hp) + m > kPendCap) {  // fold the pending list into the main list
-          warp_merge(Ac + ha, na - ha, Pc + hp, np_ - hp, An, lane);
-          uint64_t* t = Ac;
-          Ac = An;
-          An = t;
-          na = na - ha + (np_ - hp);
-          ha = 0;
-          hp = np_ = 0;
-        }
-        warp_merge(Pc + hp, np_ - hp, C, m, Pn, lane);
-        {
-          uint64_t* t = Pc;
-          Pc = Pn;
-          Pn = t;
-        }
-        np_ = np_ - hp + m;
-        hp = 0;
-        // drop the m smallest of main + pending: the first `take` of main, the rest pending
-        int take = 0;
-        if (lane == 0) take = merge_split(Ac + ha, na - ha, Pc, np_, m);
-        take = __shfl_sync(0xffffffffu, take, 0);
-        ha += take;
-        hp += m - take;
-        T = tmin();
-        ts = static_cast<double>(item_score(T));
-      }
+    if (d.kp >= 64 && d.kp <= 2 * kPolThreads)
+      cta_sort_keys_reg(A, d.kp);
+    else
+      cta_sort_keys(A, d.kp);
+    auto mains = [&](int sel) { return sel ? A2 : A; };
+    auto pends = [&](int sel) { return sel ? P2 : P; };
+    if (tid == 0) {
+      ctl->a_sel = ctl->p_sel = 0;
+      ctl->ha = 0;
+      ctl->na = k;
+      ctl->hp = ctl->np = 0;
+      ctl->T = A[0];
+      ctl->ts = static_cast<double>(item_score(A[0]));
+      ctl->pos = 0;
+      ctl->w = 1;
     }
     __syncthreads();
+    const unsigned below = (1u << lane) - 1u;
+    while (ctl->pos < nb) {
+      const int pos = ctl->pos, w = ctl->w;
+      const double ts = ctl->ts;
+      const uint64_t T = ctl->T;
+      // (a) the window's candidates: blocks not already below the threshold (a block that
+      // is not a candidate now is skipped for good: the threshold only rises)
+      if (warp == 0) {
+        int base = 0;
+        for (int q = 0; q < w; q += 32) {
+          const int p = pos + q + lane;
+          int blk = 0;
+          bool cand = false;
+          if (q + lane < w && p < nb) {
+            blk = static_cast<int>(sidx[p]);
+            cand = (fl[blk] & 1u) || !(risk[blk] < ts);
+          }
+          const unsigned cm = __ballot_sync(0xffffffffu, cand);
+          if (cand) ctl->cand[base + __popc(cm & below)] = blk;
+          base += __popc(cm);
+        }
+        if (lane == 0) ctl->ncand = base;
+      }
+      __syncthreads();
+      const int ncand = ctl->ncand;
+      if (ncand == 0) {
+        __syncthreads();
+        if (tid == 0) {
+          ctl->pos = pos + w;
+          ctl->w = min(kMaxWindow, 2 * w);
+        }
+        __syncthreads();
+        continue;
+      }
+      // (b) each warp loads its candidates' scores (up to kMaxWindow / 32 blocks, the loads
+      // in flight together), keeps them in registers and counts the items above T
+      constexpr int kPer = kMaxWindow / (kPolThreads / 32);  // candidates per warp (4)
+      float sv[kPer][4];
+      uint32_t take_mask[kPer];
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int c = warp + r * (kPolThreads / 32);
+        const int blk = c < ncand ? ctl->cand[c] : 0;
+        const int lo = blk * bs, n = c < ncand ? min(bs, L - lo) : 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int e = q * 32 + lane;
+          sv[r][q] = e < n ? s[lo + e] : 0.f;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int c = warp + r * (kPolThreads / 32);
+        take_mask[r] = 0u;
+        if (c < ncand) {  // warp-uniform
+          const int lo = ctl->cand[c] * bs, n = min(bs, L - lo);
+          int m = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int e = q * 32 + lane;
+            bool take = false;
+            if (e < n) {
+              const int j = lo + e;
+              take = !((bits[j >> 5] >> (j & 31)) & 1u) && item_of(sv[r][q], j) > T;
+            }
+            take_mask[r] |= take ? (1u << q) : 0u;
+            m += __popc(__ballot_sync(0xffffffffu, take));
+          }
+          if (lane == 0) ctl->cnt[c] = m;
+        }
+      }
+      __syncthreads();
+      // (c) offsets of the candidates' items (warp 0, four candidates per lane)
+      if (warp == 0) {
+        int loc[kMaxWindow / 32], sum = 0;
+#pragma unroll
+        for (int r = 0; r < kMaxWindow / 32; ++r) {
+          const int c = lane * (kMaxWindow / 32) + r;
+          loc[r] = c < ncand ? ctl->cnt[c] : 0;
+          sum += loc[r];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        int run = incl - sum;
+#pragma unroll
+        for (int r = 0; r < kMaxWindow / 32; ++r) {
+          const int c = lane * (kMaxWindow / 32) + r;
+          if (c < ncand) ctl->off[c] = run;
+          run += loc[r];
+        }
+        if (lane == 31) ctl->tot = incl;
+      }
+      __syncthreads();
+      const int tot = ctl->tot;
+      if (tot == 0 || tot > kWindowCap) {
+        // nothing enters: the threshold stays and every candidate is read; too many items
+        // for one window (never with one block): a quarter of the window
+        if (tot == 0)
+          for (int c = tid; c < ncand; c += kPolThreads) fl[ctl->cand[c]] |= 2u;
+        __syncthreads();
+        if (tid == 0) {
+          if (tot == 0) {
+            ctl->pos = pos + w;
+            ctl->w = min(kMaxWindow, 2 * w);
+          } else {
+            ctl->w = max(1, w / 4);
+          }
+        }
+        __syncthreads();
+        continue;
+      }
+      // (d) write the items at their offsets (each candidate's warp) and sort them
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int c = warp + r * (kPolThreads / 32);
+        if (c < ncand) {  // warp-uniform
+          const int lo = ctl->cand[c] * bs;
+          int m = ctl->off[c];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const bool take = (take_mask[r] >> q) & 1u;
+            const unsigned bal = __ballot_sync(0xffffffffu, take);
+            if (take) C[m + __popc(bal & below)] = item_of(sv[r][q], lo + q * 32 + lane);
+            m += __popc(bal);
+          }
+        }
+      }
+      const int mp = pow2_at_least(tot, 2);
+      for (int i = tot + tid; i < mp; i += kPolThreads) C[i] = ~0ull;
+      __syncthreads();
+      if (mp <= 64) {
+        if (warp == 0) {
+          uint64_t x0 = 2 * lane < mp ? C[2 * lane] : ~0ull;
+          uint64_t x1 = 2 * lane + 1 < mp ? C[2 * lane + 1] : ~0ull;
+          warp_sort64(x0, x1, lane);
+          if (2 * lane < mp) {
+            C[2 * lane] = x0;
+            C[2 * lane + 1] = x1;
+          }
+        }
+        __syncthreads();
+      } else if (mp <= 2 * kPolThreads) {
+        cta_sort_keys_reg(C, mp);
+      } else {
+        cta_sort_keys(C, mp);
+      }
+      // (e) fold the pending list into the main list when it outgrows the insertions or
+      // its capacity (same set, one sorted list); merge the items into the pending list
+      {
+        const int live = ctl->np - ctl->hp;
+        if (live + tot > kPendCap || live > 4 * max(tot, 64)) {
+          cta_merge(mains(ctl->a_sel) + ctl->ha, ctl->na - ctl->ha,
+                    pends(ctl->p_sel) + ctl->hp, live, mains(ctl->a_sel ^ 1));
+          if (tid == 0) {
+            ctl->a_sel ^= 1;
+            ctl->na = ctl->na - ctl->ha + live;
+            ctl->ha = 0;
+            ctl->hp = ctl->np = 0;
+          }
+          __syncthreads();
+        }
+      }
+      const uint64_t* Am = mains(ctl->a_sel);
+      uint64_t* Pn = pends(ctl->p_sel ^ 1);
+      const int ha = ctl->ha, na = ctl->na;
+      const int npn = ctl->np - ctl->hp + tot;
+      cta_merge(pends(ctl->p_sel) + ctl->hp, ctl->np - ctl->hp, C, tot, Pn);
+      // (f) drop the tot smallest of main + merged pending; the speculation holds if every
+      // candidate still passes against the resulting threshold (each saw one no higher)
+      if (warp == 0) {
+        const int take = warp_split(Am + ha, na - ha, Pn, npn, tot, lane);
+        uint64_t te = ha + take < na ? Am[ha + take] : ~0ull;
+        if (tot - take < npn && Pn[tot - take] < te) te = Pn[tot - take];
+        const double tes = static_cast<double>(item_score(te));
+        bool ok = true;
+        for (int c = lane; c < ncand; c += 32) {
+          const int blk = ctl->cand[c];
+          ok &= (fl[blk] & 1u) || !(risk[blk] < tes);
+        }
+        const bool commit = w == 1 || __all_sync(0xffffffffu, ok);
+        if (commit) {
+          for (int c = lane; c < ncand; c += 32) fl[ctl->cand[c]] |= 2u;
+          if (lane == 0) {
+            ctl->p_sel ^= 1;
+            ctl->np = npn;
+            ctl->hp = tot - take;
+            ctl->ha = ha + take;
+            ctl->T = te;
+            ctl->ts = tes;
+            ctl->pos = pos + w;
+            ctl->w = min(kMaxWindow, 2 * w);
+          }
+        } else if (lane == 0) {
+          ctl->w = max(1, w / 4);  // retry from the same position with a smaller window
+        }
+      }
+      __syncthreads();
+    }
   }
 
   // the verifier's rescue (verifier.py:186-233): the cold keys' verifier maxima per block,
@@ -572,54 +873,53 @@ __global__ void __launch_bounds__(kPolThreads, 1) policy_decide_kernel(const Pol
   // outputs: masked row, keys-read bitmap, flags; counts
   float* mrow = a.masked + static_cast<int64_t>(b) * L;
   for (int j = tid; j < L; j += kPolThreads) {
-    const bool ev = ((bits[j >> 5] >> (j & 31)) & 1u) || (fl[j / bs] & 6u);
+    const bool ev = ((bits[j >> 5] >> (j & 31)) & 1u) || (fl[j >> lbs] & 6u);
     mrow[j] = ev ? s[j] : -INFINITY;
   }
-  int ev_count = 0, union_count = 0, refreshed = 0, rescued = 0, seed_blocks = 0;
-  int phys[4] = {0, 0, 0, 0};  // blocks of 16/32/64/128 keys with a key read
+  // keys-read bitmap (seed bits, then whole refreshed / rescued blocks) and the counts
+  int tally[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};  // temporal, union, 4 x physical, 3 x flags
   uint32_t* eb = a.ebits + b * a.e_stride;
+  auto block_mask = [&](int w, uint8_t bit) -> uint32_t {
+    uint32_t m = 0u;
+    const int w0 = w * 32;
+    for (int blk = w0 >> lbs; blk <= min(nb - 1, (w0 + 31) >> lbs); ++blk) {
+      if (!(fl[blk] & bit)) continue;
+      const int lo = max(w0, blk * bs), hi = min(min(L, w0 + 32), (blk + 1) * bs);
+      if (hi > lo) m |= ((hi - lo == 32) ? ~0u : ((1u << (hi - lo)) - 1u)) << (lo - w0);
+    }
+    return m;
+  };
   for (int w = tid; w < d.words; w += kPolThreads) {
-    uint32_t word = bits[w], word_u;
-    for (int e = 0; e < 32; ++e) {
-      const int j = w * 32 + e;
-      if (j < L && (fl[j / bs] & 2u)) word |= 1u << e;
-    }
-    word_u = word;
-    for (int e = 0; e < 32; ++e) {
-      const int j = w * 32 + e;
-      if (j < L && (fl[j / bs] & 4u)) word_u |= 1u << e;
-    }
+    const uint32_t word = bits[w] | block_mask(w, 2u);
+    const uint32_t word_u = word | block_mask(w, 4u);
     eb[w] = word_u;
-    ev_count += __popc(word);
-    union_count += __popc(word_u);
-    phys[0] += ((word_u & 0xFFFFu) != 0) + ((word_u >> 16) != 0);
-    phys[1] += word_u != 0;
+    tally[0] += __popc(word);
+    tally[1] += __popc(word_u);
+    tally[2] += ((word_u & 0xFFFFu) != 0) + ((word_u >> 16) != 0);
+    tally[3] += word_u != 0;
   }
-  // 64- and 128-key physical blocks: words 2p, 2p+1 (and 4p..4p+3)
   __syncthreads();
+  // 64- and 128-key physical blocks: words 2p, 2p+1 (and 4p..4p+3)
   for (int p = tid; p < (d.words + 1) / 2; p += kPolThreads) {
     const uint32_t w0 = eb[2 * p], w1 = 2 * p + 1 < d.words ? eb[2 * p + 1] : 0u;
-    phys[2] += (w0 | w1) != 0;
+    tally[4] += (w0 | w1) != 0;
   }
   for (int p = tid; p < (d.words + 3) / 4; p += kPolThreads) {
     uint32_t w = 0;
     for (int q = 0; q < 4; ++q)
       if (4 * p + q < d.words) w |= eb[4 * p + q];
-    phys[3] += w != 0;
+    tally[5] += w != 0;
   }
   for (int blk = tid; blk < nb; blk += kPolThreads) {
-    refreshed += (fl[blk] >> 1) & 1u;
-    rescued += (fl[blk] >> 2) & 1u;
-    seed_blocks += (fl[blk] >> 3) & 1u;
+    tally[6] += (fl[blk] >> 1) & 1u;
+    tally[7] += (fl[blk] >> 2) & 1u;
+    tally[8] += (fl[blk] >> 3) & 1u;
     a.flags[so + blk] = fl[blk];
   }
-  const int ev_total = block_reduce_sum<int>(ev_count, reinterpret_cast<int*>(red));
-  const int union_total = block_reduce_sum<int>(union_count, reinterpret_cast<int*>(red));
-  const int ref_total = block_reduce_sum<int>(refreshed, reinterpret_cast<int*>(red));
-  const int res_total = block_reduce_sum<int>(rescued, reinterpret_cast<int*>(red));
-  const int sb_total = block_reduce_sum<int>(seed_blocks, reinterpret_cast<int*>(red));
-  int phys_total[4];
-  for (int q = 0; q < 4; ++q) phys_total[q] = block_reduce_sum<int>(phys[q], reinterpret_cast<int*>(red));
+  block_reduce_sum_n<10>(tally, ired);
+  const int ev_total = tally[0], union_total = tally[1], ref_total = tally[6], res_total = tally[7],
+            sb_total = tally[8];
+  const int phys_total[4] = {tally[2], tally[3], tally[4], tally[5]};
   if (tid == 0) {
     st[TDSA_PST_ERROR] = 0.0;
     if (!a.rescue) st[TDSA_PST_COLD_BLOCKS] = 0.0;

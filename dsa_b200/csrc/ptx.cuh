@@ -85,6 +85,12 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
                "l"(gmem_src)
                : "memory");
 }
+// Asynchronous 4-byte global -> shared copy (any 4-byte aligned address).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
 // Wait for all of this thread's cp.async copies (then a barrier publishes them).
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
