@@ -77,6 +77,10 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_score_dense_hist": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, vp, i64, vp,
                                     vp]),
     "tdsa_topk_hist": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, vp]),
+    "tdsa_key_hist_bytes": (sz, [i32, i32]),
+    "tdsa_topk_levels": (i32, [i32, i32, i32, i32]),
+    "tdsa_topk_hist_ws": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, vp, sz,
+                                vp]),
     "tdsa_key_append": (i32, [vp, i64, i32, vp, i64, vp, vp, C.c_float, vp, vp, vp, i64, i64,
                               i64, i32, i32, i32, C.c_float, vp]),
     "tdsa_policy_state_bytes": (sz, [i32, i32, i32]),

@@ -273,11 +273,21 @@ int tdsa_merge_topk(const float* cand_values, const int32_t* cand_indices,
                      static_cast<cudaStream_t>(stream));
 }
 
+int tdsa_topk_levels(int batch, int length, int k, int with_key_hist) {
+  if (batch < 1 || length < 1 || k < 1 || k > length) return 0;
+  return topk_levels(batch, length, k, with_key_hist);
+}
+
+size_t tdsa_key_hist_bytes(int batch, int length) {
+  if (batch < 1 || length < 1) return 0;
+  const size_t segs = (static_cast<size_t>(length) + kTopkSegment - 1) / kTopkSegment;
+  return static_cast<size_t>(batch) * segs * kKeyHistBins * 4;
+}
+
 size_t tdsa_score_topk_workspace_bytes(int batch, int length, int k) {
   if (batch < 1 || length < 1 || k < 1 || k > length) return 0;
   const size_t scores = (static_cast<size_t>(batch) * length * 4 + 255) & ~size_t(255);
-  const size_t hist = static_cast<size_t>(batch) * kKeyHistBins * 4;
-  return scores + hist + topk_workspace_bytes(batch, length, k);
+  return scores + tdsa_key_hist_bytes(batch, length) + topk_workspace_bytes(batch, length, k);
 }
 
 int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* weights,
@@ -299,11 +309,11 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* scores = reinterpret_cast<float*>(ws);
   const size_t score_bytes = (static_cast<size_t>(batch) * length * 4 + 255) & ~size_t(255);
-  const size_t hist_bytes = static_cast<size_t>(batch) * kKeyHistBins * 4;
+  const size_t hist_bytes = tdsa_key_hist_bytes(batch, length);
   uint32_t* hist = reinterpret_cast<uint32_t*>(ws + score_bytes);
-  // the score kernel's key histogram lets the top-k skip its first pass (16-bit keys, rows
-  // that fit one top-k segment)
-  const bool use_hist = dtype != TDSA_F32 && length <= kTopkSegment;
+  // the score kernel's key histograms (one per 32768-key segment) let the top-k skip its
+  // first passes (16-bit keys)
+  const bool use_hist = dtype != TDSA_F32;
   if (use_hist) {
     TDSA_CUDA_CHECK(cudaMemsetAsync(hist, 0, hist_bytes, st));
     rc = check_score_args(queries, q_batch_stride, weights, w_batch_stride, keys,
@@ -407,6 +417,24 @@ int tdsa_topk_hist(const float* scores, int64_t s_batch_stride, int batch, int l
   return launch_topk(scores, s_batch_stride, nullptr, 0, batch, length, k, sorted ? 1 : 0,
                      out_indices, index_bytes, idx_batch_stride, out_values, val_batch_stride,
                      nullptr, 0, static_cast<cudaStream_t>(stream), nullptr, key_hist);
+}
+
+int tdsa_topk_hist_ws(const float* scores, int64_t s_batch_stride, int batch, int length,
+                      int k, int sorted, void* out_indices, int index_bytes,
+                      int64_t idx_batch_stride, float* out_values, int64_t val_batch_stride,
+                      uint32_t* key_hist, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (!scores || !key_hist) return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
+  if (batch > 1 && s_batch_stride < length)
+    return fail(TDSA_ERR_INVALID, "score row stride must be >= length");
+  int rc = check_topk_out(out_indices, index_bytes, idx_batch_stride, out_values,
+                          val_batch_stride, batch, k);
+  if (rc) return rc;
+  return launch_topk(scores, s_batch_stride, nullptr, 0, batch, length, k, sorted ? 1 : 0,
+                     out_indices, index_bytes, idx_batch_stride, out_values, val_batch_stride,
+                     workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr,
+                     key_hist);
 }
 
 int tdsa_query_prep(const void* qraw, int64_t qraw_stride, const void* hidden,

@@ -89,6 +89,7 @@ int launch_relu_index_score(const double* q, const double* keys, const double* w
                             int dim, int tokens, double* out, cudaStream_t stream);
 
 size_t topk_workspace_bytes(int batch, int length, int k);
+int topk_levels(int batch, int length, int k, int hist);
 int topk_check(int length, int k, int sorted);
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,
                 int batch, int length, int k, int sorted, void* out_idx, int idx_bytes,

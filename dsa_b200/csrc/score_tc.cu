@@ -37,6 +37,8 @@ constexpr int kBarrierBytes = 1024;
 constexpr int kSmemBytes = kStages * kStageBytes + kQSlots * kQBytes + kBarrierBytes + 1024;
 constexpr int kHistBins = 4096;  // key histogram bins (top 12 bits of the order-preserving key)
 constexpr int kHistBytes = kHistBins * 4;
+constexpr int kHistSegment = 32768;  // keys per histogram (one top-k segment)
+static_assert(kHistSegment == 256 * kTileKeys, "a segment is 256 tiles");
 
 struct DenseArgs {
   const float* w;
@@ -46,7 +48,9 @@ struct DenseArgs {
   int length;
   int tiles_per_seq;
   int64_t total_tiles;
-  uint32_t* hist;  // [batch][4096] key histogram (kHist kernels): counts are added
+  uint32_t* hist;  // [batch][hist_segs][4096] key histograms (kHist kernels), one per
+                   // 32768-key segment of a row: counts are added
+  int hist_segs;
   __half* trace;   // optional float16 copy of the scores (score trace rows), or null
   int64_t trace_stride;
   int* status;
@@ -57,8 +61,9 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 // kHist: the epilogue also counts every score's order-preserving key by its top 12 bits in a
-// shared-memory histogram, flushed to a.hist[sequence] whenever the CTA moves to the next
-// sequence (the top-k then starts from the bin holding the k-th key instead of a full pass).
+// shared-memory histogram, flushed to a.hist[sequence][segment] whenever the CTA moves to
+// the next sequence or 32768-key segment (the top-k then starts each segment from the bin
+// holding its k-th key instead of a full pass).
 template <bool kBF16, bool kHist>
 __global__ void __launch_bounds__(kThreads, 1)
     score_dense_tc_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -202,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- epilogue
     const uint32_t quad = static_cast<uint32_t>(warp & 3);
     const int etid = (warp - 2) * 32 + lane;  // 0..127 over the epilogue warps
-    int prev_b = -1;
+    int prev_b = -1, prev_slot = -1;
     uint32_t acc_it = 0, hph = 0;
     float wr[kHeads];
     // all four epilogue warps meet (bounded wait); false when the CTA aborts
@@ -213,9 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++hph;
       return ok;
     };
-    auto hist_flush = [&](int seq) -> bool {
+    auto hist_flush = [&](int slot) -> bool {
       if (!hist_sync()) return false;
-      uint32_t* dst = a.hist + static_cast<int64_t>(seq) * kHistBins;
+      uint32_t* dst = a.hist + static_cast<int64_t>(slot) * kHistBins;
       for (int i = etid; i < kHistBins; i += 128) {
         const uint32_t c = shist[i];
         if (c) {
@@ -228,8 +233,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int64_t t = t0; t < t1; ++t) {
       const int b = static_cast<int>(t / tps);
       const int tt = static_cast<int>(t - static_cast<int64_t>(b) * tps);
+      if (kHist) {  // one histogram per (sequence, 32768-key segment): 256 tiles
+        const int slot = b * a.hist_segs + (tt >> 8);
+        if (slot != prev_slot) {
+          if (prev_slot >= 0 && !hist_flush(prev_slot)) break;
+          prev_slot = slot;
+        }
+      }
       if (b != prev_b) {
-        if (kHist && prev_b >= 0 && !hist_flush(prev_b)) break;
         load_head_weights(a.w + static_cast<int64_t>(b) * a.w_stride, wr);
         prev_b = b;
       }
@@ -254,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (kHist) add_to_bin(shist, row < a.length, float_to_key(score) >> 20);
       ++acc_it;
-      if (kHist && t + 1 == t1) hist_flush(b);
+      if (kHist && t + 1 == t1) hist_flush(prev_slot);
     }
   }
 
@@ -305,6 +316,7 @@ int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
   a.total_tiles = static_cast<int64_t>(a.tiles_per_seq) * batch;
   a.status = status;
   a.hist = hist;
+  a.hist_segs = (length + kHistSegment - 1) / kHistSegment;
   a.trace = static_cast<__half*>(trace);
   a.trace_stride = trace_bs;
   const int dev = current_device();

@@ -54,8 +54,13 @@ struct TopkArgs {
   float* out_val;         // may be null
   int64_t out_val_stride;
   float* kth_out;         // per output row: the k-th largest value (may be null)
-  uint32_t* hist;         // per row [4096] key histogram from the score kernel (single
-                          // segment rows only; consumed and re-zeroed), or null
+  uint32_t* hist;         // per (row, segment) [4096] key histogram of this level's input
+                          // (from the score kernel, or from the previous level); consumed
+                          // and re-zeroed, or null
+  uint32_t* next_hist;    // per row [4096]: this level adds the key bins of the entries it
+                          // outputs, for a one-segment next level (or null)
+  int pad_to_k;           // a level feeding another: a segment shorter than k fills its
+                          // remaining output slots with (-inf, index 0x7FFFFFFF)
   int row_words;          // shared-memory words of the segment copy (reused for sort pairs)
   int cap;                // candidate-list entries
   int* status;            // device status word (bounded-wait timeouts)
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   if (a.hist) {
     // The score kernel already counted this row's keys by their top 12 bits: find the bin of
     // the k-th key (thread t owns bins 4095-4t .. 4092-4t).
-    uint32_t* rh = a.hist + static_cast<int64_t>(row) * kKeyHistBins;
+    uint32_t* rh = a.hist + (static_cast<int64_t>(row) * gridDim.x + seg) * kKeyHistBins;
     uint32_t c[4], tot = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -391,6 +396,17 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   int64_t* oi64 = a.out_idx && a.idx_bytes == 8
                       ? static_cast<int64_t*>(a.out_idx) + out_row * a.out_idx_stride : nullptr;
   float* ov = a.out_idx && a.out_val ? a.out_val + out_row * a.out_val_stride : nullptr;
+  if (a.pad_to_k && n < a.k) {
+    // pads rank below every real candidate of the next level (-inf, then the largest index)
+    for (int j = n + tid; j < a.k; j += kThreads) {
+      if (oi32) oi32[j] = 0x7FFFFFFF;
+      if (ov) ov[j] = -INFINITY;
+    }
+    if (tid == 0 && a.next_hist)
+      atomicAdd(a.next_hist + static_cast<int64_t>(row) * kKeyHistBins +
+                    (float_to_key(-INFINITY) >> 20),
+                static_cast<uint32_t>(a.k - n));
+  }
   uint32_t kth_local = 0xFFFFFFFFu;
   while (take) {
     const int jb = __ffs(take) - 1;
@@ -481,6 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     }
     if (take && (eq || whole)) kth_local = min(kth_local, u);
     const uint32_t pos = pos_base + __popc(bt & lt);
+    if (a.next_hist)  // the next level starts from the bins of what this segment passes on
+      add_to_bin(a.next_hist + static_cast<int64_t>(row) * kKeyHistBins,
+                 take && pos < static_cast<uint32_t>(k), u >> 20);
     if (take && pos < static_cast<uint32_t>(k)) {
       const uint32_t gi = list_idx[i];
       if (write_pairs) {
@@ -578,14 +597,17 @@ struct Plan {
 
 // First level: at least ceil(length / 32768) segments; more (up to one per 8k keys, so the
 // merge level stays <= length / 8) when rows are too few to fill the GPU.
-Plan make_plan(int batch, int length, int k, bool single = false) {
+// With per-segment key histograms (`hist`) the first level uses the histograms' fixed
+// 32768-key segments.
+Plan make_plan(int batch, int length, int k, bool hist = false) {
   Plan p;
   int count = length;
   const int nmin = (length + kTopkSegment - 1) / kTopkSegment;
   const int nmax = std::max(nmin, length / std::max(8 * k, 4096));
-  int nseg = single ? nmin : std::min(std::max(nmin, (128 + batch - 1) / batch), nmax);
+  int nseg = hist ? nmin : std::min(std::max(nmin, (128 + batch - 1) / batch), nmax);
   while (true) {
-    const int chunk = (count + nseg - 1) / nseg;
+    const int chunk = (hist && p.levels == 0 && nseg > 1) ? kTopkSegment
+                                                           : (count + nseg - 1) / nseg;
     p.nseg[p.levels] = nseg;
     p.chunk[p.levels] = chunk;
     p.count[p.levels] = count;
@@ -601,10 +623,16 @@ Plan make_plan(int batch, int length, int k, bool single = false) {
 
 size_t topk_workspace_bytes(int batch, int length, int k) {
   const Plan p = make_plan(batch, length, k);
-  if (p.levels <= 1) return 0;
-  // two ping-pong candidate buffers (value f32 + index i32), sized by the first level
-  const size_t cand = static_cast<size_t>(batch) * p.nseg[0] * k;
-  return 2 * cand * 8 + 256;
+  const Plan ph = make_plan(batch, length, k, true);
+  if (p.levels <= 1 && ph.levels <= 1) return 0;
+  // two ping-pong candidate buffers (value f32 + index i32), sized by the first level (the
+  // larger of the two plans), then the next-level key histograms [batch][4096]
+  const size_t cand = static_cast<size_t>(batch) * std::max(p.nseg[0], ph.nseg[0]) * k;
+  return 2 * cand * 8 + 256 + static_cast<size_t>(batch) * kKeyHistBins * 4;
+}
+
+int topk_levels(int batch, int length, int k, int hist) {
+  return make_plan(batch, length, k, hist != 0).levels;
 }
 
 int topk_check(int length, int k, int sorted) {
@@ -620,21 +648,25 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
                 cudaStream_t stream, float* kth_out, uint32_t* key_hist) {
   int rc = topk_check(length, k, sorted);
   if (rc) return rc;
-  if (key_hist && length > kTopkSegment)
-    return fail(TDSA_ERR_UNSUPPORTED, "a key histogram needs rows of at most 32768 keys");
   const Plan p = make_plan(batch, length, k, key_hist != nullptr);
   if (p.levels > 1 && ws_bytes < topk_workspace_bytes(batch, length, k))
     return fail(TDSA_ERR_WORKSPACE, "top-k workspace too small");
-  const size_t cand = static_cast<size_t>(batch) * p.nseg[0] * k;
+  const Plan pn = make_plan(batch, length, k);
+  const size_t cand = static_cast<size_t>(batch) * std::max(p.nseg[0], pn.nseg[0]) * k;
   float* bufv[2] = {nullptr, nullptr};
   int32_t* bufi[2] = {nullptr, nullptr};
+  uint32_t* lvl_hist = nullptr;  // [batch][4096]: a level's output bins for a one-segment next
   if (p.levels > 1) {
     uint8_t* base = static_cast<uint8_t*>(ws);
     bufv[0] = reinterpret_cast<float*>(base);
     bufi[0] = reinterpret_cast<int32_t*>(base + cand * 4);
     bufv[1] = reinterpret_cast<float*>(base + cand * 8);
     bufi[1] = reinterpret_cast<int32_t*>(base + cand * 12);
+    lvl_hist = reinterpret_cast<uint32_t*>(base + 2 * cand * 8 + 256);
+    TDSA_CUDA_CHECK(cudaMemsetAsync(lvl_hist, 0, static_cast<size_t>(batch) * kKeyHistBins * 4,
+                                    stream));
   }
+  uint32_t* in_hist = key_hist;
   const float* in_v = scores;
   const int32_t* in_i = idx;
   int64_t in_vs = s_stride, in_is = idx_stride;
@@ -648,8 +680,12 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
     a.chunk = p.chunk[level];
     a.k = k;
     a.kth_out = nullptr;
-    a.hist = (p.levels == 1) ? key_hist : nullptr;
+    a.pad_to_k = 0;
+    a.hist = in_hist;
     const bool last = level == p.levels - 1;
+    // the next level, when it is one segment, starts from this level's output bins
+    a.next_hist = (!last && p.nseg[level + 1] == 1) ? lvl_hist : nullptr;
+    in_hist = a.next_hist;
     if (last) {
       a.sorted = sorted;
       a.out_idx = out_idx;
@@ -661,6 +697,7 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
     } else {
       const int b = level & 1;
       a.sorted = 0;
+      a.pad_to_k = 1;
       a.out_idx = bufi[b];
       a.idx_bytes = 4;
       a.out_idx_stride = k;

@@ -209,13 +209,15 @@ class ScoreTopkPlan:
         self.indices = torch.empty(self.batch, k, device=dev, dtype=index_dtype)
         self.values = torch.empty(self.batch, k, device=dev, dtype=torch.float32)
         lib = capi.lib()
-        # 16-bit keys in rows of one top-k segment: the score kernel also histograms the
-        # keys and the top-k starts from that histogram (which it leaves zeroed again)
-        self.use_hist = kk.dtype != torch.float32 and self.length <= 32768
-        nbytes = 0
+        # 16-bit keys: the score kernel also histograms the keys (one histogram per 32768-key
+        # segment) and the top-k starts from those histograms (which it leaves zeroed again)
+        self.use_hist = kk.dtype != torch.float32
+        nbytes = lib.tdsa_topk_workspace_bytes(self.batch, self.length, k)
+        self.workspace = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
         if self.use_hist:
-            self.key_hist = torch.zeros(self.batch, 4096, device=dev, dtype=torch.int32)
-            self._score_fn, self._topk_fn = lib.tdsa_score_dense_hist, lib.tdsa_topk_hist
+            hbytes = lib.tdsa_key_hist_bytes(self.batch, self.length)
+            self.key_hist = torch.zeros(hbytes // 4, device=dev, dtype=torch.int32)
+            self._score_fn, self._topk_fn = lib.tdsa_score_dense_hist, lib.tdsa_topk_hist_ws
             self._score_args = (q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
                                 kk.data_ptr(), kk.stride(0), kk.stride(1), _DTYPES[kk.dtype],
                                 self.batch, self.length, self.scores.data_ptr(),
@@ -224,10 +226,8 @@ class ScoreTopkPlan:
                                self.length, k, int(bool(sorted)), self.indices.data_ptr(),
                                self.indices.element_size(), self.indices.stride(0),
                                self.values.data_ptr(), self.values.stride(0),
-                               self.key_hist.data_ptr())
+                               self.key_hist.data_ptr(), self.workspace.data_ptr(), nbytes)
         else:
-            nbytes = lib.tdsa_topk_workspace_bytes(self.batch, self.length, k)
-            self.workspace = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
             self._score_fn, self._topk_fn = lib.tdsa_score_dense, lib.tdsa_topk
             self._score_args = (q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
                                 kk.data_ptr(), kk.stride(0), kk.stride(1), _DTYPES[kk.dtype],
@@ -239,8 +239,9 @@ class ScoreTopkPlan:
                                self.values.data_ptr(), self.values.stride(0),
                                self.workspace.data_ptr(), nbytes)
         self.device = dev
-        # kernels per run(): score + top-k (one level, or two or more when the top-k splits)
-        self.launches_per_run = 2 if self.use_hist or nbytes == 0 else 3
+        # kernels per run(): score + top-k (one level, or more when the row splits)
+        self.launches_per_run = 1 + capi.lib().tdsa_topk_levels(self.batch, self.length, k,
+                                                                int(self.use_hist))
         self.trace = trace
         if trace is not None:
             if kk.dtype == torch.float32:

@@ -294,10 +294,22 @@ int tdsa_score_topk_noalloc(const void* queries, int64_t q_batch_stride, const f
 /*
  * The two halves of tdsa_score_topk for callers that keep their own buffers (a decode loop):
  * tdsa_score_dense_hist is tdsa_score_dense (16-bit keys) that also adds every score's key
- * histogram (order-preserving uint32 key >> 20, 4096 bins) to key_hist [batch][4096], which
- * must be zero on entry; tdsa_topk_hist is tdsa_topk for rows of at most 32768 keys that
- * starts from that histogram instead of a full first pass, and leaves key_hist zeroed again.
+ * histogram (order-preserving uint32 key >> 20, 4096 bins) to key_hist, one histogram per
+ * 32768-key segment of each row: [batch][ceil(length / 32768)][4096]
+ * (tdsa_key_hist_bytes), which must be zero on entry.  tdsa_topk_hist is tdsa_topk for
+ * rows of at most 32768 keys that starts from that histogram instead of a full first pass,
+ * and leaves key_hist zeroed again; tdsa_topk_hist_ws takes any length with the workspace
+ * of tdsa_topk_workspace_bytes (every first-level segment starts from its histogram, and a
+ * one-segment merge level from the bins the first level passes on).
  */
+size_t tdsa_key_hist_bytes(int batch, int length);
+/* Kernel launches (levels) of one top-k call; with_key_hist: tdsa_topk_hist_ws's plan. */
+int tdsa_topk_levels(int batch, int length, int k, int with_key_hist);
+int tdsa_topk_hist_ws(const float* scores, int64_t s_batch_stride, int batch, int length,
+                      int k, int sorted, void* out_indices, int index_bytes,
+                      int64_t idx_batch_stride, float* out_values, int64_t val_batch_stride,
+                      uint32_t* key_hist, void* workspace, size_t workspace_bytes,
+                      void* stream);
 int tdsa_score_dense_hist(const void* queries, int64_t q_batch_stride, const float* weights,
                           int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
                           int64_t k_row_stride, int dtype, int batch, int length, float* scores,

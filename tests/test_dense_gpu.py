@@ -272,7 +272,7 @@ def test_api_errors():
     assert score_dense(q, w, k[:0]).shape == (0,)
 
 
-@pytest.mark.parametrize("length", [100, 1000, 32768])
+@pytest.mark.parametrize("length", [100, 1000, 32768, 32769, 40000, 65536, 100000])
 @pytest.mark.parametrize("sorted_", [True, False])
 def test_score_topk_plan_with_key_histogram_matches_separate_calls(length, sorted_):
     """The fused path (score kernel histograms keys, top-k starts from it) gives the same
@@ -291,21 +291,30 @@ def test_score_topk_plan_with_key_histogram_matches_separate_calls(length, sorte
         if rep:
             q.mul_(-1 if rep == 1 else 0.5)  # new queries in the same buffers
         idx, val = plan.run()
-        want_i, want_v = topk(score_dense(q, w, keys), k, sorted=sorted_)
+        s = score_dense(q, w, keys)
+        want_i, want_v = topk(s, k, sorted=sorted_)
         assert torch.equal(idx, want_i), rep
         assert torch.equal(val, want_v), rep
+        if length > 32768:  # rows of several segments: the oracle as well
+            oi, ov = oracle.topk_rows(s.cpu().numpy(), k, sorted=sorted_)
+            np.testing.assert_array_equal(idx.cpu().numpy(), oi)
+            np.testing.assert_array_equal(val.cpu().numpy(), ov)
     assert int(plan.key_hist.abs().sum()) == 0
 
 
-@pytest.mark.parametrize("k,sorted_", [(1, True), (2048, False), (8192, True), (20000, False)])
-def test_score_topk_plan_histogram_path_with_tied_scores(k, sorted_):
+@pytest.mark.parametrize("k,sorted_,length", [(1, True, 32768), (2048, False, 32768),
+                                              (8192, True, 32768), (20000, False, 32768),
+                                              (2048, False, 70000), (8192, True, 70000),
+                                              (1, True, 40000)])
+def test_score_topk_plan_histogram_path_with_tied_scores(k, sorted_, length):
     """All-zero keys give one score value for the whole row: the histogram's k-th bin
-    holds every key, and the tie rule (lowest index first) decides."""
+    holds every key, and the tie rule (lowest index first) decides -- within one segment
+    and across the segments and merge level of longer rows."""
     from dsa_b200 import score_dense
     from dsa_b200.indexer import ScoreTopkPlan
 
     gen = torch.Generator().manual_seed(k)
-    b, length = 2, 32768
+    b = 2
     q = (torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)).to(torch.bfloat16).cuda()
     w = (torch.randn(b, 64, generator=gen) / 8).cuda()
     keys = torch.zeros(b, length, 128, dtype=torch.bfloat16, device="cuda")
@@ -353,3 +362,68 @@ def test_topk_hist_special_values_with_host_histogram(length, k, sorted_):
     np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
     np.testing.assert_array_equal(val.cpu().numpy(), want_v)
     assert int(hist.abs().sum()) == 0  # consumed and zeroed
+
+
+def _key_hist_segments(s: np.ndarray, seg: int = 32768) -> np.ndarray:
+    """[rows][ceil(L / seg)][4096] per-segment key histograms (tdsa_key_hist_bytes layout)."""
+    parts = [_key_hist(s[:, i:i + seg]) for i in range(0, s.shape[1], seg)]
+    return np.stack(parts, axis=1).astype(np.int32)
+
+
+@pytest.mark.parametrize("length,k,sorted_", [(40000, 2048, False), (70000, 512, True),
+                                              (65536, 8192, False), (100000, 1, True)])
+def test_topk_hist_ws_segments_with_host_histograms(length, k, sorted_):
+    """tdsa_topk_hist_ws over rows of several segments, each started from its own histogram
+    (made on the host), with special values and ties; the histograms end zeroed."""
+    from dsa_b200 import _capi as capi
+
+    rng = np.random.default_rng(length + k)
+    s = np.round(rng.normal(size=(3, length)) * 8).astype(np.float32) / 8
+    s[0, rng.integers(0, length, 300)] = -0.0
+    s[1, rng.integers(0, length, 50)] = np.inf
+    s[1, rng.integers(0, length, 50)] = -np.inf
+    s[2, rng.integers(0, length, 400)] = np.float32(1e-45)
+    dev = cuda(s)
+    hist = cuda(_key_hist_segments(s))
+    lib = capi.lib()
+    assert hist.numel() * 4 == lib.tdsa_key_hist_bytes(3, length)
+    nbytes = lib.tdsa_topk_workspace_bytes(3, length, k)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device="cuda")
+    idx = torch.empty(3, k, dtype=torch.int64, device="cuda")
+    val = torch.empty(3, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist_ws", dev.data_ptr(), dev.stride(0), 3, length, k, int(sorted_),
+              idx.data_ptr(), 8, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=sorted_)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(hist.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("sorted_", [True, False])
+def test_topk_hist_ws_short_tail_segment_with_minus_inf_ties(sorted_):
+    """The last 32768-key segment is shorter than k, so the merge level receives padding;
+    most keys score -inf, so the k-th key is -inf and real -inf keys (lowest index first)
+    must win over the padding."""
+    from dsa_b200 import _capi as capi
+
+    length, k = 32768 * 2 + 100, 2048
+    rng = np.random.default_rng(7)
+    s = np.full((2, length), -np.inf, dtype=np.float32)
+    for r in range(2):
+        live = rng.choice(length, 1000, replace=False)
+        s[r, live] = rng.normal(size=1000).astype(np.float32)
+    s[1, -50:] = 3.0  # ties inside the short tail segment
+    dev = cuda(s)
+    hist = cuda(_key_hist_segments(s))
+    lib = capi.lib()
+    nbytes = lib.tdsa_topk_workspace_bytes(2, length, k)
+    ws = torch.full((max(nbytes, 1),), 0x7F, dtype=torch.uint8, device="cuda")  # not zero
+    idx = torch.empty(2, k, dtype=torch.int64, device="cuda")
+    val = torch.empty(2, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist_ws", dev.data_ptr(), dev.stride(0), 2, length, k, int(sorted_),
+              idx.data_ptr(), 8, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=sorted_)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
