@@ -687,6 +687,7 @@ def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
+    prog = cfg5_progressive(args, rank, world, device, b, start, stop, k, w)
     if rank != 0:
         return None
     return {
@@ -700,7 +701,58 @@ def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
                    "parallelism": f"L-sharded x{world}",
                    "timing": "CUDA graph of one step replayed back to back, events, max over "
                              "ranks"},
+        "progressive": prog,
     }
+
+
+def cfg5_progressive(args, rank, world, device, b, start, stop, k, w) -> dict:
+    """Config 5's progressive variant: the exact certified progressive top-k per shard
+    (LShardedExact, block 64), queries drifting as AR(1) with rho = 0.95, one key appended
+    per step to the last rank's range, the candidates merged over NCCL every step.  Timed
+    with CUDA events over the steps (host launches included), max over ranks."""
+    from dsa_b200.parallel import LShardedExact
+
+    steps = min(args.steps, 32)
+    rho = 0.95
+    g = torch.Generator(device=device)
+    g.manual_seed(55)
+    own = stop - start
+    extra = steps if rank == world - 1 else 0
+    shard = torch.randn(b, own + extra, 128, generator=g, device=device).to(torch.bfloat16)
+    qf = torch.randn(b, 64, 128, generator=g, device=device) / math.sqrt(128)
+    qs = []
+    for _ in range(steps + 1):
+        qs.append(qf.to(torch.bfloat16))
+        qf = rho * qf + math.sqrt(1 - rho * rho) * torch.randn(
+            b, 64, 128, generator=g, device=device) / math.sqrt(128)
+    ex = LShardedExact(b, own + extra, k, start, block_size=64, sorted=False)
+    ex.init(qs[0], w, shard[:, :own])
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for t in range(steps):
+        n = own + (t + 1 if rank == world - 1 else 0)
+        ex.step(qs[t + 1], w, shard[:, :n])
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+    st = ex.stats()
+    read = sum(x["keys_scored"] for x in st) / max(1, sum(x["keys_total"] for x in st))
+    pruned = sum(x["blocks_pruned"] for x in st)
+    vals = torch.tensor([ms, read, pruned], device=device, dtype=torch.float64)
+    if world > 1:
+        mx = vals.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        sm = vals.clone()
+        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
+        ms, read, pruned = float(mx[0]), float(sm[1]) / world, float(sm[2])
+    return {"ms_per_step": ms, "steps": steps, "keys_read_fraction": read,
+            "blocks_pruned": int(pruned), "queries": "AR(1) rho 0.95, i.i.d. N(0,1) keys",
+            "api": "dsa_b200.parallel.LShardedExact (tdsa_exact_step + all-gather + "
+                   "tdsa_merge_topk)"}
 
 
 # ----------------------------------------------------------------------------- CPU arm

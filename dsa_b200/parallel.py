@@ -97,6 +97,41 @@ class LShardedTopK:
         return idx, val
 
 
+class _CandidateMerge:
+    """The exchange step of an L-sharded top-k on fixed buffers: the rank's local top-k
+    (values f32, indices i32 already global) packed into one all-gather, reordered rank-major
+    -> row-major, and merged by tdsa_merge_topk."""
+
+    def __init__(self, batch: int, k: int, *, sorted: bool, group, device):
+        self.batch, self.k, self.sorted, self.group = batch, k, bool(sorted), group
+        self.world = (dist.get_world_size(group)
+                      if dist.is_available() and dist.is_initialized() else 1)
+        self.send = torch.empty(2, batch, k, device=device, dtype=torch.int32)
+        self.recv = torch.empty(self.world, 2, batch, k, device=device, dtype=torch.int32)
+        self.cand = torch.empty(2, batch, self.world, k, device=device, dtype=torch.int32)
+        self.indices = torch.empty(batch, k, device=device, dtype=torch.int64)
+        self.values = torch.empty(batch, k, device=device, dtype=torch.float32)
+
+    def __call__(self, values: torch.Tensor, indices: torch.Tensor, offset: int):
+        from . import _capi as capi
+        from .indexer import stream_ptr
+
+        self.send[0].copy_(values.view(torch.int32))
+        torch.add(indices, offset, out=self.send[1])
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        else:
+            self.recv[0].copy_(self.send)
+        self.cand.copy_(self.recv.permute(1, 2, 0, 3))
+        b, count = self.batch, self.world * self.k
+        vals = self.cand[0].view(torch.float32).view(b, count)
+        idx = self.cand[1].view(b, count)
+        capi.call("tdsa_merge_topk", vals.data_ptr(), idx.data_ptr(), count, b, count, self.k,
+                  int(self.sorted), self.indices.data_ptr(), 8, self.indices.stride(0),
+                  self.values.data_ptr(), self.values.stride(0), stream_ptr(vals.device))
+        return self.indices, self.values
+
+
 class LShardedPlan:
     """The L-sharded top-k on fixed buffers (the decode-loop form of ``LShardedTopK``).
 
@@ -115,31 +150,48 @@ class LShardedPlan:
         self.plan = ScoreTopkPlan(queries, weights, keys_shard, k, sorted=False,
                                   index_dtype=torch.int32)
         self.k, self.offset, self.sorted, self.group = k, int(offset), bool(sorted), group
-        self.world = (dist.get_world_size(group)
-                      if dist.is_available() and dist.is_initialized() else 1)
-        b, dev = self.plan.batch, keys_shard.device
-        self.send = torch.empty(2, b, k, device=dev, dtype=torch.int32)
-        self.recv = torch.empty(self.world, 2, b, k, device=dev, dtype=torch.int32)
-        self.cand = torch.empty(2, b, self.world, k, device=dev, dtype=torch.int32)
-        self.indices = torch.empty(b, k, device=dev, dtype=torch.int64)
-        self.values = torch.empty(b, k, device=dev, dtype=torch.float32)
+        self.merge = _CandidateMerge(self.plan.batch, k, sorted=sorted, group=group,
+                                     device=keys_shard.device)
+        self.world = self.merge.world
 
     def run(self) -> tuple[torch.Tensor, torch.Tensor]:
-        from . import _capi as capi
-        from .indexer import stream_ptr
-
         self.plan.run()
-        self.send[0].copy_(self.plan.values.view(torch.int32))
-        torch.add(self.plan.indices, self.offset, out=self.send[1])
-        if self.world > 1:
-            dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
-        else:
-            self.recv[0].copy_(self.send)
-        self.cand.copy_(self.recv.permute(1, 2, 0, 3))
-        b, count = self.plan.batch, self.world * self.k
-        vals = self.cand[0].view(torch.float32).view(b, count)
-        idx = self.cand[1].view(b, count)
-        capi.call("tdsa_merge_topk", vals.data_ptr(), idx.data_ptr(), count, b, count, self.k,
-                  int(self.sorted), self.indices.data_ptr(), 8, self.indices.stride(0),
-                  self.values.data_ptr(), self.values.stride(0), stream_ptr(vals.device))
-        return self.indices, self.values
+        return self.merge(self.plan.values, self.plan.indices, self.offset)
+
+
+class LShardedExact:
+    """The exact certified progressive top-k of an L-sharded, append-only key cache.
+
+    Each rank runs the exact progressive path (``ExactProgressiveTopK``) over its own
+    contiguous key range, so its local top-k is exact: it prunes only blocks whose certified
+    bound is below its local k-th score, which is at most the global k-th score.  The global
+    top-k is in the union of the local ones; the candidates are all-gathered and merged as in
+    ``LShardedPlan``.  New keys are appended to the last rank's range (the other ranges stay
+    fixed), so every rank's cache is append-only."""
+
+    def __init__(self, batch: int, max_shard_length: int, k: int, offset: int, *,
+                 block_size: int = 64, dtype: torch.dtype = torch.bfloat16,
+                 device: torch.device | str | None = None, sorted: bool = True,
+                 group: dist.ProcessGroup | None = None):
+        from .progressive_exact import ExactProgressiveTopK
+
+        self.exact = ExactProgressiveTopK(batch, max_shard_length, k, block_size=block_size,
+                                          dtype=dtype, device=device, sorted=False,
+                                          index_dtype=torch.int32)
+        self.k, self.offset = k, int(offset)
+        self.merge = _CandidateMerge(batch, k, sorted=sorted, group=group,
+                                     device=self.exact.device)
+        self.world = self.merge.world
+
+    def init(self, queries, weights, keys_shard):
+        if keys_shard.shape[-2] < self.k:
+            raise ValueError(f"every shard needs at least k={self.k} keys")
+        idx, val = self.exact.init(queries, weights, keys_shard)
+        return self.merge(val, idx, self.offset)
+
+    def step(self, queries, weights, keys_shard):
+        idx, val = self.exact.step(queries, weights, keys_shard)
+        return self.merge(val, idx, self.offset)
+
+    def stats(self) -> list[dict]:
+        return self.exact.stats()

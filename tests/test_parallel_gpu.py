@@ -75,6 +75,49 @@ def test_l_sharded_plan_single_process_equals_whole_row():
         assert torch.equal(idx, want_i) and torch.equal(val, want_v)
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_l_sharded_exact_progressive_equals_dense_every_step(world):
+    """Exact progressive top-k per shard (append-only: new keys go to the last shard) plus
+    the merge equals the whole-row dense top-k at every step, with block-structured keys
+    and slowly drifting queries so that shards prune blocks."""
+    from dsa_b200 import merge_topk, scores_topk
+    from dsa_b200.parallel import LShardedExact, shard_bounds
+
+    gen = torch.Generator().manual_seed(50 + world)
+    b, base, steps, k, bs = 2, 24576, 6, 512, 64
+    total = base + steps
+    # keys: a per-block level times a shared direction, so most blocks score far below
+    # the hot ones and the certified bound prunes them
+    level = torch.randn(b, total // bs + 1, 1, generator=gen) * 0.2
+    level[:, ::37] += 3.0
+    keys = (level.repeat_interleave(bs, 1)[:, :total] * torch.randn(1, 1, 128, generator=gen)
+            + 0.05 * torch.randn(b, total, 128, generator=gen)).to(torch.bfloat16).cuda()
+    q = torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)
+    w = (torch.randn(b, 64, generator=gen) / 8).cuda()
+    bounds = [shard_bounds(base, r, world) for r in range(world)]
+    parts = [LShardedExact(b, (stop - start) + steps, k, start, block_size=bs, sorted=True)
+             for start, stop in bounds]
+    pruned = 0
+    for t in range(steps):
+        length = base + t
+        qt = q.to(torch.bfloat16).cuda()
+        vs, js = [], []
+        for r, (start, stop) in enumerate(bounds):
+            stop = length if r == world - 1 else stop
+            fn = parts[r].init if t == 0 else parts[r].step
+            idx_r, val_r = fn(qt, w, keys[:, start:stop])
+            vs.append(val_r)
+            js.append(idx_r.to(torch.int32))
+        idx, val = merge_topk(torch.cat(vs, 1), torch.cat(js, 1), k, sorted=True)
+        want_i, want_v = scores_topk(qt, w, keys[:, :length], k, sorted=True,
+                                     index_dtype=torch.int64)
+        assert torch.equal(idx, want_i) and torch.equal(val, want_v), t
+        q = 0.995 * q + 0.005 * torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)
+    for part in parts:
+        pruned += sum(st["blocks_pruned"] for st in part.stats())
+    assert pruned > 0
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
 def test_l_sharded_topk_two_nccl_ranks(tmp_path):
