@@ -572,7 +572,7 @@ def single_sequence_latency(wl: Config4, proj, device: torch.device, reps: int =
                "method": "CUDA graph of ScoreTopkPlan.run (tdsa_score_dense_hist + "
                          "tdsa_topk_hist); L2 flushed before each replay; events",
                "reference_l40s_us": 87.04,
-               "reference_source": "dense score + torch.topk, K=2048, L40S (BASELINE.md)"}
+               "reference_source": "the reference's published dense score + torch.topk, K=2048, L40S"}
         del graph
     return out
 
