@@ -549,8 +549,8 @@ int policy_checks(const void* state, size_t state_bytes, const float* scores, in
                   int batch, int length, int k, int block_size, int max_blocks) {
   if (!state || !scores) return fail(TDSA_ERR_INVALID, "null pointer");
   if (batch < 1 || batch > 65535) return fail(TDSA_ERR_INVALID, "batch must be in [1, 65535]");
-  if (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128)
-    return fail(TDSA_ERR_UNSUPPORTED, "block_size must be 16, 32, 64 or 128");
+  if (block_size < 1 || block_size > 128 || (block_size & (block_size - 1)))
+    return fail(TDSA_ERR_UNSUPPORTED, "the policy takes power-of-two block sizes up to 128");
   if (k < 1 || k > length) return fail(TDSA_ERR_INVALID, "K cannot exceed the current length");
   if (k > 2048) return fail(TDSA_ERR_UNSUPPORTED, "the policy takes k <= 2048");
   if (length > 131072) return fail(TDSA_ERR_UNSUPPORTED, "the policy takes length <= 131072");

@@ -325,7 +325,7 @@ struct WalkCtl {
 // shared-memory carve of the decide kernel
 struct DecideSmem {
   int words, nb, nbp, kp;
-  size_t bits, risk, cmax, fl, skey, sidx, A, A2, P, P2, C, CI, ctl, red, total;
+  size_t bits, risk, cmax, fl, skey, sidx, A, A2, P, P2, C, ctl, red, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -350,7 +350,6 @@ __host__ __device__ inline DecideSmem decide_smem(int length, int bs, int k) {
   d.P = o;     o = align_up(o + sizeof(uint64_t) * kPendCap, 16);
   d.P2 = o;    o = align_up(o + sizeof(uint64_t) * kPendCap, 16);
   d.C = o;     o = align_up(o + sizeof(uint64_t) * kWindowCap, 16);
-  d.CI = o;    o = align_up(o + sizeof(uint64_t) * 32 * bs, 16);
   d.ctl = o;   o = align_up(o + sizeof(WalkCtl), 16);
   d.bits = o;  o = align_up(o + sizeof(uint32_t) * d.words, 16);
   d.cmax = o;  o = align_up(o + sizeof(float) * d.nb, 16);
@@ -450,7 +449,6 @@ __global__ void __launch_bounds__(kPolThreads, 1) policy_decide_kernel(const Pol
   uint64_t* P = reinterpret_cast<uint64_t*>(sm + d.P);
   uint64_t* P2 = reinterpret_cast<uint64_t*>(sm + d.P2);
   uint64_t* C = reinterpret_cast<uint64_t*>(sm + d.C);
-  uint64_t* CI = reinterpret_cast<uint64_t*>(sm + d.CI);  // [32][bs] items per candidate
   WalkCtl* ctl = reinterpret_cast<WalkCtl*>(sm + d.ctl);
   double* red = reinterpret_cast<double*>(sm + d.red);
   int* ired = reinterpret_cast<int*>(sm + d.red);

@@ -103,7 +103,7 @@ int tdsa_key_append(const void* hidden, int64_t hidden_stride, int hidden_size,
  *   ranking [batch][max_blocks] (rescue: cold blocks by verifier maximum; may be NULL),
  *   stats [batch][TDSA_POLICY_NSTATS] (TDSA_PST_*; TDSA_PST_ERROR = 1 when the seed is not
  *   k distinct keys below length: the state is then unchanged).
- * Limits: k <= 2048, block_size 16/32/64/128, ceil(length/block_size) <= max_blocks <= 4096,
+ * Limits: k <= 2048, block_size a power of two <= 128, ceil(length/block_size) <= max_blocks <= 4096,
  *   length <= 131072.  Scores are expected finite (a key whose score is -inf ties with the
  *   keys the policy did not read).  All device buffers; asynchronous on `stream`.
  */
