@@ -256,8 +256,12 @@ class ScoreTopkPlan:
     def score(self) -> None:
         if self.trace is not None:
             row, row_bs = self.trace.take_row(self.length)
-            capi.check(capi.lib().tdsa_score_dense_trace(*self._trace_args, row, row_bs,
-                                                         stream_ptr(self.device)))
+            rc = capi.lib().tdsa_score_dense_trace(*self._trace_args, row, row_bs,
+                                                   stream_ptr(self.device))
+            if rc != capi.TDSA_OK:  # the row was not written: give it back
+                self.trace.step -= 1
+                self.trace.lengths[self.trace.step] = 0
+            capi.check(rc)
             return
         capi.check(self._score_fn(*self._score_args, stream_ptr(self.device)))
 
