@@ -1,6 +1,8 @@
 // extern "C" entry points of libtdsa: argument checks on the host, then the launchers.
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -58,6 +60,29 @@ int device_sm_count(int device) {
     g_sm_count[device] = n > 0 ? n : 148;
   }
   return g_sm_count[device];
+}
+
+cudaError_t ensure_dynamic_smem(const void* kernel, int bytes) {
+  // cudaFuncSetAttribute costs host time on every launch; remember, per device and kernel,
+  // the largest dynamic shared memory size already set
+  static std::mutex m;
+  static std::vector<std::pair<const void*, int>> seen[kMaxDevices];
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices)
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  std::lock_guard<std::mutex> lock(m);
+  for (auto& e : seen[dev]) {
+    if (e.first != kernel) continue;
+    if (e.second >= bytes) return cudaSuccess;
+    const cudaError_t rc =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (rc == cudaSuccess) e.second = bytes;
+    return rc;
+  }
+  const cudaError_t rc =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (rc == cudaSuccess) seen[dev].emplace_back(kernel, bytes);
+  return rc;
 }
 
 int* device_status_ptr() {

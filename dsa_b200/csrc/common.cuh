@@ -53,6 +53,10 @@ int fail(int code, const std::string& msg);
 int device_sm_count(int device);
 int current_device();
 
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes), called only when the
+// kernel has not had at least `bytes` set on the current device yet.
+cudaError_t ensure_dynamic_smem(const void* kernel, int bytes);
+
 // Encodes a tiled tensor map (driver entry point fetched through the runtime).
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,

@@ -575,9 +575,8 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   if (rc) return rc;
   if (!init) {
     // 4. tau (a lower bound of the k-th largest wave-1 score), 5. wave-2 list, 6. wave 2
-    TDSA_CUDA_CHECK(cudaFuncSetAttribute(exact_wave2_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kHistCopyBytes));
+    TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_wave2_kernel),
+                                        kHistCopyBytes));
     TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), kHistCopyBytes,
                                stream,
                                length, block_size, bpt, L.nb_stride,
@@ -596,9 +595,8 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   uint32_t* hist = nullptr;
   if (length <= kTopkSegment) {
     hist = reinterpret_cast<uint32_t*>(state + L.hist);
-    TDSA_CUDA_CHECK(cudaFuncSetAttribute(exact_row_hist_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kHistCopyBytes));
+    TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_row_hist_kernel),
+                                        kHistCopyBytes));
     TDSA_CUDA_CHECK(launch_pdl(exact_row_hist_kernel, dim3(batch), dim3(kThreads),
                                kHistCopyBytes, stream,
                                static_cast<const float*>(scores),

@@ -253,7 +253,7 @@ int launch_key_append(const void* hidden, int64_t hidden_stride, int hidden_size
   const int clusters = (batch + kKaSeqs - 1) / kKaSeqs;
   auto kern = dtype == TDSA_BF16 ? key_append_kernel<true> : key_append_kernel<false>;
   TDSA_CUDA_CHECK(
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kKaSmem));
+      ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kKaSmem));
   TDSA_CUDA_CHECK(launch_pdl(kern, dim3(static_cast<unsigned>(clusters * kKaCluster)),
                              dim3(kKaThreads), kKaSmem, stream, a));
   TDSA_CUDA_CHECK(cudaGetLastError());

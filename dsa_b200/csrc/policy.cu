@@ -1143,9 +1143,8 @@ int launch_policy(int init, uint8_t* state, int batch, int k, int nbc, const flo
     a.promotion_threshold = rescue->promotion_threshold;
   }
   const size_t smem = decide_smem(length, bs, k).total;
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(policy_decide_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem)));
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(policy_decide_kernel),
+                                      static_cast<int>(smem)));
   TDSA_CUDA_CHECK(launch_pdl(policy_decide_kernel, dim3(batch), dim3(kPolThreads), smem, stream,
                              a));
   // the selection: stable top-k of the keys read
@@ -1154,9 +1153,8 @@ int launch_policy(int init, uint8_t* state, int batch, int k, int nbc, const flo
   if (rc) return rc;
   const size_t fsmem = align_up(2 * static_cast<size_t>((length + 31) / 32) * 4 + nbc, 16) +
                        64 * sizeof(double);
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(policy_finalize_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(fsmem)));
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(policy_finalize_kernel),
+                                      static_cast<int>(fsmem)));
   TDSA_CUDA_CHECK(launch_pdl(policy_finalize_kernel, dim3(batch), dim3(kPolThreads), fsmem,
                              stream, a));
   TDSA_CUDA_CHECK(cudaGetLastError());

@@ -719,7 +719,7 @@ int launch_proj_splitk(const CUtensorMap& wmap, const CUtensorMap& xmap,
                        const CUtensorMap& wwmap, const ProjArgs& a, cudaStream_t stream) {
   auto kern = proj_splitk_kernel<kBF16>;
   TDSA_CUDA_CHECK(
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem));
+      ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSplitSmem));
   TDSA_CUDA_CHECK(launch_pdl(kern, dim3(2 * kHeads), dim3(kThreads), kSplitSmem, stream, wmap,
                              xmap, wwmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
@@ -731,7 +731,7 @@ int launch_proj_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtens
                   const ProjArgs& a, cudaStream_t stream) {
   auto kern = proj_tc_kernel<kBF16, kN>;
   constexpr int smem = smem_bytes<kN>();
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   const dim3 grid(2 * kHeads, (a.batch + kN - 1) / kN);
   TDSA_CUDA_CHECK(launch_pdl(kern, grid, dim3(kThreads), smem, stream, wmap, xmap, wwmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());

@@ -362,8 +362,7 @@ template <int kMode, bool kBF16>
 int launch_t(const CUtensorMap& kmap, const CUtensorMap& qmap, const BlockArgs& a, int grid,
              cudaStream_t stream) {
   auto kern = score_blocks_kernel<kMode, kBF16>;
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kSmemBytes));
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBytes));
   TDSA_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kThreads), kSmemBytes, stream, kmap, qmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;

@@ -99,9 +99,8 @@ __global__ void __launch_bounds__(kThreads)
 int launch_score_dense_f32(const float* q, int64_t q_bs, const float* w, int64_t w_bs,
                            const float* k, int64_t k_bs, int64_t k_rs, int batch, int length,
                            float* out, int64_t o_bs, cudaStream_t stream) {
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(score_dense_f32_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kSmemBytes));
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(score_dense_f32_kernel),
+                                      kSmemBytes));
   const dim3 grid((length + kKeys - 1) / kKeys, batch);
   score_dense_f32_kernel<<<grid, kThreads, kSmemBytes, stream>>>(q, q_bs, w, w_bs, k, k_bs,
                                                                   k_rs, length, out, o_bs);

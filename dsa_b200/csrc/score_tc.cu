@@ -324,7 +324,7 @@ int launch_dense_tc_t(const void* q, int64_t q_bs, const float* w, int64_t w_bs,
   const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
   const int smem = kSmemBytes + (hist ? kHistBytes : 0);
   auto kern = hist ? score_dense_tc_kernel<kBF16, true> : score_dense_tc_kernel<kBF16, false>;
-  TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   TDSA_CUDA_CHECK(launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem,
                              stream, kmap, qmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());

@@ -575,8 +575,8 @@ int launch_segments(TopkArgs a, int rows, int nseg, cudaStream_t stream) {
   a.status = device_status_ptr();
   if (!a.status) return fail(TDSA_ERR_CUDA, "device status word not available");
   auto run = [&](auto kern) -> int {
-    TDSA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
+    TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern),
+                                        static_cast<int>(smem)));
     TDSA_CUDA_CHECK(launch_pdl(kern, dim3(nseg, rows), dim3(kThreads), smem, stream, a));
     TDSA_CUDA_CHECK(cudaGetLastError());
     return TDSA_OK;
