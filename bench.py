@@ -583,11 +583,13 @@ def run_cfg3(args, device: torch.device) -> dict:
     (rho 0.95), fixed w, bf16: the exact certified progressive top-2048 (block 64) and dense
     score + top-2048, each run for all steps back to back between two CUDA events (per-step
     average; at B=1 both are bound by host launch time, not by the ~10 us of GPU work).
-    The exact top-k is compared with dense at every step.  A second, block-structured trace
+    The exact path runs in its decode-loop form (ExactProgressivePlan: fixed buffers, the
+    query rewritten in place each step).  The exact top-k is compared with dense at every
+    step.  A second, block-structured trace
     (10% of 64-key blocks at norm x3, the rest x0.05; slowly drifting queries, rho 0.999;
     positive weights) is a case where the certified bound prunes blocks unread."""
     from dsa_b200 import score_dense, topk
-    from dsa_b200.progressive_exact import ExactProgressiveTopK
+    from dsa_b200.progressive_exact import ExactProgressivePlan
 
     steps, l0, k, bs = max(args.steps, 8), 16384, 2048, 64
     res = {}
@@ -610,13 +612,19 @@ def run_cfg3(args, device: torch.device) -> dict:
         for _ in range(steps):
             q = rho * q + innov * torch.randn(64, 128, generator=g) / math.sqrt(128)
             qs.append(q.to(torch.bfloat16).to(device).unsqueeze(0))
-        w1 = w.unsqueeze(0)
-        ex = ExactProgressiveTopK(1, l0 + steps, k, block_size=bs, sorted=False)
-        ex.init(qs[0], w1, keys[:, :l0])
+        w1 = w.unsqueeze(0).contiguous()
+        # the decode-loop form: fixed query / weight / cache buffers, the query rewritten in
+        # place every step (as a projection kernel would), one C call per step
+        qbuf = qs[0].clone()
+        ex = ExactProgressivePlan(qbuf, w1, keys, k, block_size=bs, sorted=False)
+        ex.init(l0)
         torch.cuda.synchronize(device)
         e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        got = []
         e[0].record()
-        got = [ex.step(qs[t], w1, keys[:, :l0 + t + 1])[0].clone() for t in range(steps)]
+        for t in range(steps):
+            qbuf.copy_(qs[t])
+            got.append(ex.step(l0 + t + 1)[0].clone())
         e[1].record()
         e[2].record()
         want = [topk(score_dense(qs[t], w1, keys[:, :l0 + t + 1]), k, sorted=False)[0]

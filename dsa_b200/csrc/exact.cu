@@ -15,6 +15,8 @@
 // Every pruned key has a score strictly below tau <= the k-th largest, so the top-k equals
 // dense scoring's; the scores are bit-identical to the dense kernel's (same MMA tile, same
 // epilogue summation order).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
@@ -249,7 +251,8 @@ __device__ uint32_t row_histogram(const float* srow, int length, uint32_t* h, ui
 __global__ void __launch_bounds__(kThreads)
     exact_wave2_kernel(int length, int bs, int bpt, int64_t nb_stride, const float* bound,
                        const float* scores, int64_t l_stride, int k, float* tau, int8_t* flag,
-                       int32_t* tile_seq, int32_t* tile_blk, int32_t* counter) {
+                       int32_t* tile_seq, int32_t* tile_blk, int32_t* counter,
+                       const uint32_t* hist_in) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
   extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words
@@ -262,7 +265,13 @@ __global__ void __launch_bounds__(kThreads)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nb = (length + bs - 1) / bs;
   const int64_t brow = static_cast<int64_t>(seq) * nb_stride;
-  row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h, hcopies);
+  if (hist_in) {  // the first level came from row_hist_part_kernel
+    const uint32_t* src = hist_in + static_cast<int64_t>(seq) * kKeyHistBins;
+    for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) h[i] = src[i];
+    __syncthreads();
+  } else {
+    row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h, hcopies);
+  }
   // thread t owns bins 4095-4t .. 4092-4t: keys above a thread's bins by a CTA scan
   uint32_t c[4], tot = 0;
 #pragma unroll
@@ -352,6 +361,28 @@ __global__ void __launch_bounds__(kThreads)
     if (flag[brow + b] == 0 && bound[brow + b] >= t) flag[brow + b] = 2;
   __syncthreads();
   emit_tiles(flag + brow, nb, 2, bpt, seq, tile_seq, tile_blk, counter, wtot, sbase);
+}
+
+// Part of a row's key histogram, added to hist[seq] (zero before the launch): CTA
+// blockIdx.x of gridDim.x takes one contiguous chunk of the row, so a small batch still
+// spreads over many SMs.  Finite scores by bin, the unscored (-inf) keys in bin 0.
+__global__ void __launch_bounds__(kThreads)
+    row_hist_part_kernel(const float* scores, int64_t l_stride, int length, uint32_t* hist) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
+  extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words
+  __shared__ uint32_t h[kKeyHistBins];
+  const int seq = blockIdx.y;
+  const int chunk = ((length + gridDim.x - 1) / gridDim.x + 31) & ~31;
+  const int lo = min(length, static_cast<int>(blockIdx.x) * chunk);
+  const int n = min(chunk, length - lo);
+  const uint32_t inf =
+      row_histogram(scores + static_cast<int64_t>(seq) * l_stride + lo, n, h, hcopies);
+  uint32_t* dst = hist + static_cast<int64_t>(seq) * kKeyHistBins;
+  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {
+    const uint32_t c = h[i] + (i == (0x007FFFFFu >> 20) ? inf : 0u);
+    if (c) atomicAdd(dst + i, c);
+  }
 }
 
 // The final key histogram of each row for the histogram top-k: finite scores by bin, the
@@ -573,8 +604,28 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   int rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
                                stream);
   if (rc) return rc;
+  // Rows of a small batch are histogrammed by several CTAs each (the one-CTA-per-row pass
+  // is latency-bound): row_hist_part_kernel into a zeroed buffer.
+  const int parts = std::max(1, std::min({16, 148 / batch, (length + 2047) / 2048}));
+  uint32_t* hbuf = reinterpret_cast<uint32_t*>(state + L.hist);
+  auto part_hist = [&]() -> int {
+    TDSA_CUDA_CHECK(cudaMemsetAsync(hbuf, 0, static_cast<size_t>(batch) * kKeyHistBins * 4,
+                                    stream));
+    TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(row_hist_part_kernel),
+                                        kHistCopyBytes));
+    TDSA_CUDA_CHECK(launch_pdl(row_hist_part_kernel, dim3(parts, batch), dim3(kThreads),
+                               kHistCopyBytes, stream, static_cast<const float*>(scores),
+                               static_cast<int64_t>(max_length), length, hbuf));
+    TDSA_CUDA_CHECK(cudaGetLastError());
+    return TDSA_OK;
+  };
   if (!init) {
     // 4. tau (a lower bound of the k-th largest wave-1 score), 5. wave-2 list, 6. wave 2
+    const bool split = parts > 1 && length <= kTopkSegment;
+    if (split) {
+      rc = part_hist();
+      if (rc) return rc;
+    }
     TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_wave2_kernel),
                                         kHistCopyBytes));
     TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), kHistCopyBytes,
@@ -583,7 +634,8 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
                                static_cast<const float*>(bound),
                                static_cast<const float*>(scores),
                                static_cast<int64_t>(max_length), k, tau, flag, tile_seq,
-                               tile_blk, counters + 1));
+                               tile_blk, counters + 1,
+                               static_cast<const uint32_t*>(split ? hbuf : nullptr)));
     TDSA_CUDA_CHECK(cudaGetLastError());
     ba.tile_count = counters + 1;
     rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
@@ -594,14 +646,18 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   // top-k segment start from their key histogram
   uint32_t* hist = nullptr;
   if (length <= kTopkSegment) {
-    hist = reinterpret_cast<uint32_t*>(state + L.hist);
-    TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_row_hist_kernel),
-                                        kHistCopyBytes));
-    TDSA_CUDA_CHECK(launch_pdl(exact_row_hist_kernel, dim3(batch), dim3(kThreads),
-                               kHistCopyBytes, stream,
-                               static_cast<const float*>(scores),
-                               static_cast<int64_t>(max_length), length, hist));
-    TDSA_CUDA_CHECK(cudaGetLastError());
+    hist = hbuf;
+    if (parts > 1) {
+      rc = part_hist();
+      if (rc) return rc;
+    } else {
+      TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_row_hist_kernel),
+                                          kHistCopyBytes));
+      TDSA_CUDA_CHECK(launch_pdl(exact_row_hist_kernel, dim3(batch), dim3(kThreads),
+                                 kHistCopyBytes, stream, static_cast<const float*>(scores),
+                                 static_cast<int64_t>(max_length), length, hist));
+      TDSA_CUDA_CHECK(cudaGetLastError());
+    }
   }
   rc = launch_topk(scores, max_length, nullptr, 0, batch, length, k, sorted, topk, 4, k, out_val,
                    val_bs, tws, L.topk_ws_bytes, stream, nullptr, hist);

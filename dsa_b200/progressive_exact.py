@@ -93,3 +93,63 @@ class ExactProgressiveTopK:
                                                self.batch, self.max_length, self.k,
                                                self.block_size, buf))
         return [dict(zip(STAT_NAMES, buf[8 * b: 8 * b + 8])) for b in range(self.batch)]
+
+
+class ExactProgressivePlan:
+    """The exact progressive path on fixed buffers (the decode-loop form).
+
+    ``queries`` [B,64,128] and ``weights`` [B,64] float32 are rewritten in place by the
+    caller between steps, and new keys are appended to ``keys`` [B, max_length, 128] (the
+    cache buffer, read up to the step's length).  ``init(length)`` / ``step(length)`` are one
+    C call each with no per-call validation or allocation; the selection lands in
+    ``indices`` / ``values`` [B, k]."""
+
+    def __init__(self, queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor, k: int,
+                 *, block_size: int = 64, sorted: bool = True,
+                 index_dtype: torch.dtype = torch.int32):
+        require_cuda(queries, weights, keys)
+        q, w, kk, _ = as_batched(queries, weights, keys)
+        if not (q.is_contiguous() and q.data_ptr() % 16 == 0 and q.dtype == kk.dtype):
+            raise ValueError("plan queries must be contiguous, 16-byte aligned, keys' dtype")
+        if not (w.dtype == torch.float32 and w.is_contiguous()):
+            raise ValueError("plan weights must be contiguous float32")
+        if prepare_keys(kk) is not kk:
+            raise ValueError("plan keys must already satisfy the TMA layout rules")
+        self.q, self.w, self.keys = q, w, kk
+        self.batch, self.max_length = kk.shape[0], kk.shape[1]
+        self.exact = ExactProgressiveTopK(self.batch, self.max_length, k, block_size=block_size,
+                                          dtype=kk.dtype, device=kk.device, sorted=sorted,
+                                          index_dtype=index_dtype)
+        self.indices = torch.empty(self.batch, k, device=kk.device, dtype=index_dtype)
+        self.values = torch.empty(self.batch, k, device=kk.device, dtype=torch.float32)
+        ex = self.exact
+        self._head = (ex.state.data_ptr(), ex.state_bytes, q.data_ptr(), q.stride(0),
+                      w.data_ptr(), w.stride(0), kk.data_ptr(), kk.stride(0), kk.stride(1),
+                      _DTYPES[kk.dtype], self.batch)
+        self._tail = (self.max_length, k, block_size, int(bool(sorted)),
+                      self.indices.data_ptr(), self.indices.element_size(),
+                      self.indices.stride(0), self.values.data_ptr(), self.values.stride(0))
+        self.length = 0
+
+    def init(self, length: int):
+        """First step over keys [:, :length]: dense scores, top-k, block maxima, key norms."""
+        if not 0 < length <= self.max_length:
+            raise ValueError("length outside the key buffer")
+        capi.check(capi.lib().tdsa_exact_init(*self._head, length, *self._tail,
+                                              stream_ptr(self.keys.device)))
+        self.length = self.exact.length = length
+        return self.indices, self.values
+
+    def step(self, length: int):
+        """Next decode step over keys [:, :length] (length >= the previous one)."""
+        if self.length == 0:
+            raise RuntimeError("call init() first")
+        if not self.length <= length <= self.max_length:
+            raise ValueError("the cache is append-only and bounded by the key buffer")
+        capi.check(capi.lib().tdsa_exact_step(*self._head, self.length, length, *self._tail,
+                                              stream_ptr(self.keys.device)))
+        self.length = self.exact.length = length
+        return self.indices, self.values
+
+    def stats(self) -> list[dict]:
+        return self.exact.stats()

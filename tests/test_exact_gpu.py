@@ -80,6 +80,33 @@ def test_exact_progressive_equals_dense_every_step(block_size):
     assert st[0]["keys_scored"] <= st[0]["keys_total"]
 
 
+@pytest.mark.parametrize("block_size", [32, 64])
+def test_exact_plan_matches_function_form(block_size):
+    """ExactProgressivePlan (fixed buffers, one C call per step) returns what the function
+    form returns, step for step, on a cache that grows inside its buffer."""
+    from dsa_b200.progressive_exact import ExactProgressivePlan, ExactProgressiveTopK
+
+    batch, l0, steps, k = 2, 3000, 5, 128
+    keys, qs, w = ar1_trace(9 + block_size, batch, l0, steps)
+    cache = keys.cuda()
+    wc = w.cuda().contiguous()
+    qbuf = qs[0].cuda().clone()
+    plan = ExactProgressivePlan(qbuf, wc, cache, k, block_size=block_size, sorted=True,
+                                index_dtype=torch.int64)
+    ref = ExactProgressiveTopK(batch, l0 + steps, k, block_size=block_size)
+    got_i, got_v = plan.init(l0)
+    want_i, want_v = ref.init(qbuf, wc, cache[:, :l0])
+    assert torch.equal(got_i, want_i) and torch.equal(got_v, want_v)
+    for step in range(1, steps + 1):
+        qbuf.copy_(qs[step].cuda())
+        got_i, got_v = plan.step(l0 + step)
+        want_i, want_v = ref.step(qbuf, wc, cache[:, :l0 + step])
+        assert torch.equal(got_i, want_i) and torch.equal(got_v, want_v), step
+    assert plan.stats() == ref.stats()
+    with pytest.raises(ValueError):
+        plan.step(l0)  # append-only
+
+
 def test_exact_progressive_prunes_structured_cache_and_stays_exact():
     """Blocks of small-norm keys next to a few large ones: the bound must skip them."""
     from dsa_b200 import score_dense, topk
