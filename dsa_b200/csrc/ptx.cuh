@@ -121,6 +121,15 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t raddr, float a) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(raddr), "f"(a) : "memory");
 }
 
+__device__ __forceinline__ void st_cluster_u32(uint32_t raddr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(raddr), "r"(v) : "memory");
+}
+
+// Atomic add (no return) to a shared-memory word of any CTA of the cluster.
+__device__ __forceinline__ void red_cluster_add_u32(uint32_t raddr, uint32_t v) {
+  asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(raddr), "r"(v) : "memory");
+}
+
 // Arrive on an mbarrier of another CTA of the cluster, releasing this thread's prior writes
 // (shared::cluster included) at cluster scope.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t raddr) {
@@ -171,6 +180,17 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const vo
 // (bulk copies) of them.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// The two halves of cluster_sync_all, for work between them: arrive releases this thread's
+// prior writes (shared::cluster included); wait returns once every thread of the cluster
+// has arrived.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // Every thread of every CTA of the cluster (a hardware barrier, like __syncthreads).

@@ -25,6 +25,7 @@
 // again with explicit indices until one segment remains.  The same explicit-index pass
 // merges per-GPU candidates of an L-sharded cache.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -549,6 +550,241 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Cluster top-k: one row of up to 32768 keys over the kC CTAs of a cluster, for batches too
+// small to fill the GPU one CTA per row.  Unsorted output, one level, and the score kernel's
+// 12-bit key histogram of the row.  CTA r of the cluster holds keys
+// [r*kPer*1024, (r+1)*kPer*1024) in registers: warp w the 32*kPer keys from
+// r*kPer*1024 + w*32*kPer, in chunks of 32*kV (kV = min(kPer, 4)) with lane l holding kV
+// consecutive keys of each chunk, so every load is one coalesced 128-512 byte access and
+// index order is (rank, warp, chunk, lane, element).
+//   1. The bin of the k-th key in the score kernel's histogram (every CTA scans it; the
+//      histogram loads go out with the score loads).
+//   2. Then bits 19..8 and 7..0 of the key: each CTA counts its keys of the live range into a
+//      local histogram, adds the non-zero bins into every CTA's copy of the cluster's
+//      histogram (distributed shared memory, `red.shared::cluster`), one cluster barrier,
+//      and every CTA picks the same bin.  Narrowing stops once the range holds exactly the
+//      keys still to take, or is one key.
+//   3. Keys above the range are taken, and the lowest-index keys inside it complete k (the
+//      tie rule of stable_topk, metrics.py:9-22).  Output positions follow index order: the
+//      CTAs' (above, inside) counts go to every CTA of the cluster, warps are offset by a
+//      CTA scan of their totals, lanes by a warp scan per chunk.
+// The row's histogram is zeroed for the next score launch after every CTA has read it.
+constexpr int kClusterHistWords = 2 * kKeyHistBins + 256;  // cluster levels 2 and 3
+
+// The bin of the k_rem-th key counted from the top, thread t holding the counts c[0..3] of
+// bins nbins-1-4t .. nbins-4-4t (zeros past nbins): res = {bin, k_rem within the bin, the
+// bin's count, 1}, or res[3] = 0 when the counts total less than k_rem.  Three CTA
+// barriers; all threads return with res readable.
+__device__ __forceinline__ void pick_bin(const uint32_t (&c)[4], int nbins, uint32_t k_rem,
+                                         uint32_t* wa, uint32_t* wb, uint32_t* res) {
+  const int tid = threadIdx.x;
+  const uint32_t tot = c[0] + c[1] + c[2] + c[3];
+  if (tid == 0) res[3] = 0u;
+  uint32_t dummy;
+  uint32_t above = block_excl_scan(tot, wa, wb, &dummy);
+  if (above < k_rem && k_rem <= above + tot) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (above < k_rem && k_rem <= above + c[i]) {
+        res[0] = static_cast<uint32_t>(nbins - 1 - (4 * tid + i));
+        res[1] = k_rem - above;
+        res[2] = c[i];
+        res[3] = 1u;
+      }
+      above += c[i];
+    }
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void bins_from_top(const uint32_t* h, int nbins, uint32_t (&c)[4]) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = 4 * tid + i < nbins ? h[nbins - 1 - (4 * tid + i)] : 0u;
+}
+
+template <int kPer, int kC>
+__global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)
+    topk_cluster_kernel(const TopkArgs a) {
+  static_assert(kPer >= 1 && kPer <= 16 && (kPer & (kPer - 1)) == 0, "kPer: 1..16, power of 2");
+  constexpr int kV = kPer < 4 ? kPer : 4;  // consecutive keys per lane in a chunk
+  constexpr int kChunks = kPer / kV;
+  constexpr uint32_t kVMask = (1u << kV) - 1u;
+  extern __shared__ __align__(16) uint32_t csm[];
+  __shared__ uint32_t hloc[kKeyHistBins];  // this CTA's keys of the live range, by bin
+  __shared__ uint32_t wa[kWarps], wb[kWarps], res[4];
+  __shared__ uint32_t s_cnt[kC];  // per rank: above | inside << 16
+  uint32_t* hred2 = csm;                     // cluster counts, bits 19..8 (4096 bins)
+  uint32_t* hred1 = csm + kKeyHistBins;      // bits 31..20, when the histogram is unusable
+  uint32_t* hred3 = csm + 2 * kKeyHistBins;  // cluster counts, bits 7..0 (256 bins)
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t rank = cluster_ctarank();
+  const int row = blockIdx.y;
+  const int n = a.row_len;
+  const uint32_t k = static_cast<uint32_t>(min(a.k, n));
+  const int wbase = static_cast<int>(rank) * (kPer * kThreads) + warp * (32 * kPer);
+
+  for (int i = tid; i < kClusterHistWords; i += kThreads) csm[i] = 0u;
+  cluster_arrive();  // waited for before the first add into a peer's histogram
+  pdl_wait();        // the scores and the histogram come from the previous kernel
+  pdl_launch_dependents();
+
+  // ---- the row's histogram counts and the keys (loads issued together)
+  uint32_t* gh = a.hist + static_cast<int64_t>(row) * kKeyHistBins;
+  uint32_t c4[4];
+  bins_from_top(gh, kKeyHistBins, c4);
+  const float* vrow = a.vals + static_cast<int64_t>(row) * a.vals_stride;
+  const bool vec = (reinterpret_cast<uintptr_t>(vrow) & (kV * 4 - 1)) == 0;
+  uint32_t u[kPer];
+  uint32_t valid = 0;  // bit i: key i of this lane lies inside the row
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    const int e0 = wbase + j * 32 * kV + lane * kV;
+    if (vec && e0 + kV <= n) {
+      if constexpr (kV == 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(vrow + e0));
+        u[4 * j] = float_to_key(v.x);
+        u[4 * j + 1] = float_to_key(v.y);
+        u[4 * j + 2] = float_to_key(v.z);
+        u[4 * j + 3] = float_to_key(v.w);
+      } else if constexpr (kV == 2) {
+        const float2 v = __ldg(reinterpret_cast<const float2*>(vrow + e0));
+        u[2 * j] = float_to_key(v.x);
+        u[2 * j + 1] = float_to_key(v.y);
+      } else {
+        u[j] = float_to_key(__ldg(vrow + e0));
+      }
+      valid |= kVMask << (j * kV);
+    } else {
+#pragma unroll
+      for (int s = 0; s < kV; ++s) {
+        const bool in = e0 + s < n;
+        u[j * kV + s] = in ? float_to_key(__ldg(vrow + e0 + s)) : 0u;
+        valid |= (in ? 1u : 0u) << (j * kV + s);
+      }
+    }
+  }
+
+  // ---- 1. the k-th key's top-12-bit bin from the score kernel's histogram
+  uint32_t clo = 0u, chi = 0xFFFFFFFFu, k_rem = k, in_range = static_cast<uint32_t>(n);
+  pick_bin(c4, kKeyHistBins, k_rem, wa, wb, res);
+  int level = 0;
+  if (res[3]) {
+    clo = res[0] << 20;
+    chi = clo | 0xFFFFFu;
+    k_rem = res[1];
+    in_range = res[2];
+    level = 1;
+  }
+  cluster_wait();  // every CTA's cluster histograms are zero
+
+  // ---- 2. cluster narrowing levels (level 0 only when the histogram does not describe
+  // the row: its counts total less than k)
+  for (; level < 3 && clo != chi && in_range != k_rem; ++level) {
+    const int sh = level == 0 ? 20 : level == 1 ? 8 : 0;
+    const int nb = level == 2 ? 256 : kKeyHistBins;
+    uint32_t* hr = level == 0 ? hred1 : level == 1 ? hred2 : hred3;
+    for (int i = tid; i < nb; i += kThreads) hloc[i] = 0u;
+    __syncthreads();
+    // a range holding many keys (ties) is counted with per-warp aggregation
+    const bool heavy = in_range > static_cast<uint32_t>(n) / 16u;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const bool in = ((valid >> i) & 1u) && u[i] >= clo && u[i] <= chi;
+      const uint32_t bin = (u[i] >> sh) & static_cast<uint32_t>(nb - 1);
+      if (heavy) add_to_bin(hloc, in, in ? bin : 0u);
+      else if (in) atomicAdd(&hloc[bin], 1u);
+    }
+    __syncthreads();
+    for (int i = tid; i < nb; i += kThreads) {
+      const uint32_t c = hloc[i];
+      if (c) {
+        const uint32_t la = smem_u32(hr + i);
+#pragma unroll
+        for (int r = 0; r < kC; ++r) red_cluster_add_u32(mapa_shared(la, r), c);
+      }
+    }
+    cluster_sync_all();
+    bins_from_top(hr, nb, c4);
+    pick_bin(c4, nb, k_rem, wa, wb, res);
+    if (!res[3]) break;  // counts short of k_rem: the histogram did not match the scores
+    clo |= res[0] << sh;
+    chi = clo | ((1u << sh) - 1u);
+    k_rem = res[1];
+    in_range = res[2];
+  }
+
+  // ---- 3. take: keys above chi, and the first k_rem keys of [clo, chi] in index order
+  uint32_t gtm = 0u, eqm = 0u;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    if ((valid >> i) & 1u) {
+      if (u[i] > chi) gtm |= 1u << i;
+      else if (u[i] >= clo) eqm |= 1u << i;
+    }
+  }
+  // warp totals (above | inside << 16) -> warp offsets in the CTA -> CTA offsets in the row
+  const uint32_t wt = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(__popc(gtm)) |
+                                                         (static_cast<uint32_t>(__popc(eqm)) << 16));
+  if (lane == 0) wa[warp] = wt;
+  __syncthreads();
+  if (warp == 0) {
+    warp_totals_scan(wa, wb);
+    __syncwarp();
+    const uint32_t cta_total = wb[31] + wa[31];
+    if (lane < kC) st_cluster_u32(mapa_shared(smem_u32(&s_cnt[rank]), lane), cta_total);
+  }
+  cluster_sync_all();  // the last access to a peer's shared memory
+  for (int i = static_cast<int>(rank) * (kKeyHistBins / kC) + tid;
+       i < static_cast<int>(rank + 1) * (kKeyHistBins / kC); i += kThreads)
+    gh[i] = 0u;  // every CTA of the cluster has read the histogram: ready for reuse
+  uint32_t run = wb[warp];
+  for (uint32_t r = 0; r < rank; ++r) run += s_cnt[r];
+
+  const int64_t orow = static_cast<int64_t>(row);
+  int32_t* oi32 = a.out_idx && a.idx_bytes == 4
+                      ? static_cast<int32_t*>(a.out_idx) + orow * a.out_idx_stride : nullptr;
+  int64_t* oi64 = a.out_idx && a.idx_bytes == 8
+                      ? static_cast<int64_t*>(a.out_idx) + orow * a.out_idx_stride : nullptr;
+  float* ov = a.out_val ? a.out_val + orow * a.out_val_stride : nullptr;
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    const uint32_t g = (gtm >> (j * kV)) & kVMask, q = (eqm >> (j * kV)) & kVMask;
+    const uint32_t mine = static_cast<uint32_t>(__popc(g)) | (static_cast<uint32_t>(__popc(q)) << 16);
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t chunk_total = __shfl_sync(0xffffffffu, incl, 31);
+    if (g | q) {
+      const uint32_t before = run + incl - mine;
+      uint32_t gtb = before & 0xFFFFu, eqb = before >> 16;
+      const int e0 = wbase + j * 32 * kV + lane * kV;
+#pragma unroll
+      for (int s = 0; s < kV; ++s) {
+        uint32_t pos = 0xFFFFFFFFu;
+        if ((g >> s) & 1u) {
+          pos = gtb + min(eqb, k_rem);
+          ++gtb;
+        } else if ((q >> s) & 1u) {
+          if (eqb < k_rem) pos = gtb + eqb;
+          ++eqb;
+        }
+        if (pos < k) {
+          if (oi32) oi32[pos] = e0 + s;
+          if (oi64) oi64[pos] = e0 + s;
+          if (ov) ov[pos] = key_to_float(u[j * kV + s]);
+        }
+      }
+    }
+    run += chunk_total;
+  }
+}
+
 int kpow2(int k) {
   int p = 1;
   while (p < k) p <<= 1;
@@ -585,6 +821,65 @@ int launch_segments(TopkArgs a, int rows, int nseg, cudaStream_t stream) {
   if (a.chunk <= 8 * kThreads) return run(topk_segment_kernel<8>);
   if (a.chunk <= 16 * kThreads) return run(topk_segment_kernel<16>);
   return run(topk_segment_kernel<32>);
+}
+
+template <int kC>
+int launch_cluster(const TopkArgs& a, int rows, int per, cudaStream_t stream) {
+  auto run = [&](auto kern) -> int {
+    constexpr int smem = kClusterHistWords * 4;
+    TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
+    TDSA_CUDA_CHECK(launch_pdl(kern, dim3(kC, rows), dim3(kThreads), smem, stream, a));
+    TDSA_CUDA_CHECK(cudaGetLastError());
+    return TDSA_OK;
+  };
+  if (per <= 1) return run(topk_cluster_kernel<1, kC>);
+  if (per <= 2) return run(topk_cluster_kernel<2, kC>);
+  if (per <= 4) return run(topk_cluster_kernel<4, kC>);
+  if constexpr (kC <= 4) {
+    if (per <= 8) return run(topk_cluster_kernel<8, kC>);
+  }
+  if constexpr (kC <= 2) return run(topk_cluster_kernel<16, kC>);
+  return fail(TDSA_ERR_UNSUPPORTED, "cluster top-k: row too long for the cluster");
+}
+
+// Clusters of kC top-k CTAs the current device runs at once (one CTA per SM), queried once
+// per device; 0 when the query fails.
+template <int kC>
+int max_active_clusters() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    const void* kern = reinterpret_cast<const void*>(topk_cluster_kernel<4, kC>);
+    constexpr int smem = kClusterHistWords * 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kC, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int nc = 0;
+    if (ensure_dynamic_smem(kern, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      nc = 0;
+    }
+    cache[dev] = nc > 0 ? nc : -1;
+  }
+  return cache[dev] > 0 ? cache[dev] : 0;
+}
+
+// CTAs per row for the cluster top-k: the largest of 8, 4, 2 that runs the whole batch in
+// one wave, leaves each CTA at least 2048 keys and each thread at most 8 (measured on
+// B200 at 32768 keys per row, k = 2048: 8 CTAs 7.3 us, 4 CTAs 9.0 us, one CTA 10.5-12.7 us,
+// but 2 CTAs of 16 keys per thread 12.2-14.5 us); 1 = one CTA per row (topk_segment_kernel).
+int cluster_size(int batch, int length) {
+  if (length >= 8 * 2048 && batch <= max_active_clusters<8>()) return 8;
+  if (length >= 4 * 2048 && length <= 4 * 8 * kThreads && batch <= max_active_clusters<4>())
+    return 4;
+  if (length >= 2 * 2048 && length <= 2 * 8 * kThreads && batch <= max_active_clusters<2>())
+    return 2;
+  return 1;
 }
 
 // Level plan: segments per level while the candidate count exceeds one segment.
@@ -651,6 +946,29 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
   const Plan p = make_plan(batch, length, k, key_hist != nullptr);
   if (p.levels > 1 && ws_bytes < topk_workspace_bytes(batch, length, k))
     return fail(TDSA_ERR_WORKSPACE, "top-k workspace too small");
+  if (p.levels == 1 && key_hist && !idx && !sorted && !kth_out) {
+    // one level of few rows: the cluster top-k spreads each row over several SMs
+    const int c = cluster_size(batch, length);
+    if (c > 1) {
+      TopkArgs a = {};
+      a.vals = scores;
+      a.vals_stride = s_stride;
+      a.row_len = length;
+      a.chunk = length;
+      a.k = k;
+      a.out_idx = out_idx;
+      a.idx_bytes = idx_bytes;
+      a.out_idx_stride = oi_stride;
+      a.out_val = out_val;
+      a.out_val_stride = ov_stride;
+      a.hist = key_hist;
+      const int cap = c * kThreads;
+      const int per = (length + cap - 1) / cap;
+      if (c == 2) return launch_cluster<2>(a, batch, per, stream);
+      if (c == 4) return launch_cluster<4>(a, batch, per, stream);
+      return launch_cluster<8>(a, batch, per, stream);
+    }
+  }
   const Plan pn = make_plan(batch, length, k);
   const size_t cand = static_cast<size_t>(batch) * std::max(p.nseg[0], pn.nseg[0]) * k;
   float* bufv[2] = {nullptr, nullptr};

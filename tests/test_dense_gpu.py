@@ -427,3 +427,62 @@ def test_topk_hist_ws_short_tail_segment_with_minus_inf_ties(sorted_):
     want_i, want_v = oracle.topk_rows(s, k, sorted=sorted_)
     np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
     np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+
+
+@pytest.mark.parametrize("batch,length,k", [
+    (1, 32768, 2048),   # 8 CTAs per row, 4 keys per thread
+    (1, 16384, 1),      # 8 CTAs, 2 keys per thread
+    (1, 8192, 8192),    # 4 CTAs, k = length
+    (1, 5000, 777),     # 2 CTAs, 4 keys per thread, the last threads partly outside the row
+    (2, 4096, 2048),    # 2 CTAs, 2 keys per thread
+    (9, 32768, 20000),  # 8 CTAs per row, k above the list capacity of one CTA
+    (20, 32768, 2048),  # 4 CTAs per row, 8 keys per thread
+    (64, 32768, 2048),  # 2 CTAs per row, 16 keys per thread (the config-4 shape)
+    (40, 30001, 513),   # 2 CTAs per row, odd row stride (unaligned rows: scalar loads)
+])
+def test_cluster_topk_rows_match_oracle(batch, length, k):
+    """The cluster top-k (a row over 2-8 CTAs, unsorted, from the score kernel's histogram)
+    against stable_topk: rounded normals (heavy ties), +-0, +-inf, denormals, and one row
+    of a single value; the histograms end zeroed."""
+    from dsa_b200 import _capi as capi
+
+    rng = np.random.default_rng(batch * 7 + length + k)
+    s = np.round(rng.normal(size=(batch, length)) * 64).astype(np.float32) / 64
+    s[0, rng.integers(0, length, length // 50)] = -0.0
+    s[0, rng.integers(0, length, length // 50)] = 0.0
+    if batch > 1:
+        s[1] = 0.25  # one value: the tie rule alone decides
+    if batch > 2:
+        s[2, rng.integers(0, length, 50)] = np.inf
+        s[2, rng.integers(0, length, length // 3)] = -np.inf
+        s[-1, rng.integers(0, length, 400)] = np.float32(1e-45)
+    dev = cuda(s)
+    hist = cuda(_key_hist(s))
+    idx = torch.empty(batch, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(batch, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist", dev.data_ptr(), dev.stride(0), batch, length, k, 0,
+              idx.data_ptr(), 4, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(hist.abs().sum()) == 0  # consumed and zeroed
+
+
+def test_cluster_topk_falls_back_when_histogram_is_short():
+    """A histogram whose counts total less than k does not describe the row: the cluster
+    kernel narrows from the full key range itself and still returns stable_topk."""
+    from dsa_b200 import _capi as capi
+
+    rng = np.random.default_rng(3)
+    s = rng.normal(size=(2, 32768)).astype(np.float32)
+    dev = cuda(s)
+    hist = torch.zeros(2, 4096, dtype=torch.int32, device="cuda")
+    idx = torch.empty(2, 2048, dtype=torch.int64, device="cuda")
+    val = torch.empty(2, 2048, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist", dev.data_ptr(), dev.stride(0), 2, 32768, 2048, 0,
+              idx.data_ptr(), 8, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, 2048, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
