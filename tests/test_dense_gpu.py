@@ -442,8 +442,8 @@ def test_topk_hist_ws_short_tail_segment_with_minus_inf_ties(sorted_):
 ])
 def test_cluster_topk_rows_match_oracle(batch, length, k):
     """The cluster top-k (a row over 2-8 CTAs, unsorted, from the score kernel's histogram)
-    against stable_topk: rounded normals (heavy ties), +-0, +-inf, denormals, and one row
-    of a single value; the histograms end zeroed."""
+    against stable_topk: rounded normals (heavy ties), +-0, +-inf, denormals, one row of a
+    single value and one of -inf only; the histograms end zeroed."""
     from dsa_b200 import _capi as capi
 
     rng = np.random.default_rng(batch * 7 + length + k)
@@ -456,6 +456,8 @@ def test_cluster_topk_rows_match_oracle(batch, length, k):
         s[2, rng.integers(0, length, 50)] = np.inf
         s[2, rng.integers(0, length, length // 3)] = -np.inf
         s[-1, rng.integers(0, length, 400)] = np.float32(1e-45)
+    if batch > 3:
+        s[3] = -np.inf  # the k-th key is -inf: every key of the row ties
     dev = cuda(s)
     hist = cuda(_key_hist(s))
     idx = torch.empty(batch, k, dtype=torch.int32, device="cuda")
