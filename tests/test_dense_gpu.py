@@ -488,3 +488,19 @@ def test_cluster_topk_falls_back_when_histogram_is_short():
     want_i, want_v = oracle.topk_rows(s, 2048, sorted=False)
     np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
     np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+
+
+def test_graph_capture_of_first_plan_run():
+    """ScoreTopkPlan.run captured into a CUDA graph before it ever ran, in a fresh process
+    (one-time setup such as kernel attributes and the cluster-size query happens inside
+    the capture), for the cluster top-k (8 and 4 CTAs per row) and one CTA per row."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, PYTHONPATH=str(root))
+    res = subprocess.run([sys.executable, str(root / "tests" / "_graph_capture_worker.py")],
+                         cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stderr[-2000:]
