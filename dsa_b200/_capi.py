@@ -27,6 +27,7 @@ TDSA_F16 = 1
 TDSA_BF16 = 2
 
 i32, i64, vp, sz = C.c_int, C.c_int64, C.c_void_p, C.c_size_t
+TDSA_IPC_HANDLE_BYTES = 64
 
 
 class TdsaPolicy(C.Structure):
@@ -61,6 +62,12 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_topk_workspace_bytes": (sz, [i32, i32, i32]),
     "tdsa_topk": (i32, [vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, sz, vp]),
     "tdsa_merge_topk": (i32, [vp, vp, i64, i32, i32, i32, i32, vp, i32, i64, vp, i64, vp]),
+    "tdsa_exchange_bytes": (sz, [i32, i32, i32]),
+    "tdsa_exchange_create": (i32, [i32, i32, i32, i32, C.POINTER(vp), vp]),
+    "tdsa_exchange_connect": (i32, [vp, vp]),
+    "tdsa_exchange_publish": (i32, [vp, vp, vp, i64, i32, vp]),
+    "tdsa_exchange_merge": (i32, [vp, i32, vp, i32, i64, vp, i64, vp]),
+    "tdsa_exchange_destroy": (i32, [vp]),
     "tdsa_score_topk_workspace_bytes": (sz, [i32, i32, i32]),
     "tdsa_score_topk": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32, vp, i32,
                               i64, vp, i64, vp, sz, vp]),

@@ -125,6 +125,24 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t raddr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(raddr), "r"(v) : "memory");
 }
 
+// ---------------------------------------------------------------- peer memory (NVLink)
+// A flag word written by another GPU: acquire at system scope.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy global writes before later async-proxy (bulk copy)
+// reads of the same memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Atomic add (no return) to a shared-memory word of any CTA of the cluster.
 __device__ __forceinline__ void red_cluster_add_u32(uint32_t raddr, uint32_t v) {
   asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(raddr), "r"(v) : "memory");

@@ -65,6 +65,8 @@ struct TopkArgs {
   int row_words;          // shared-memory words of the segment copy (reused for sort pairs)
   int cap;                // candidate-list entries
   int* status;            // device status word (bounded-wait timeouts)
+  int gather;             // merge of an exchange: gather the rows from peer memory first
+  PeerGather pg;
 };
 
 __device__ __forceinline__ unsigned lanemask_lt() {
@@ -160,6 +162,62 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* wa, ui
   return wb[warp] + x - v;
 }
 
+// Merge of an exchange: wait (bounded) until every rank has published this row for the
+// current epoch, then copy the ranks' candidate rows (peer memory over NVLink, loads that
+// bypass L1) into this row of the local scratch, which the selection then reads as its
+// input (a.vals / a.idx).  A wait that runs out raises TDSA_ERR_TIMEOUT and leaves the
+// scratch as it was.
+__device__ void gather_peer_row(const TopkArgs& a, int row) {
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_late;
+  const PeerGather& g = a.pg;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_epoch = *reinterpret_cast<volatile const uint32_t*>(g.own + g.ctr_off);
+    s_late = 0;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch, parity = epoch & 1u;
+  if (tid < g.world) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(g.own + g.flags_off) +
+                        (static_cast<int64_t>(parity) * g.world + tid) * g.rows + row;
+    const long long t0 = clock64();
+    while (ld_acquire_sys(f) != epoch) {
+      if (clock64() - t0 > kWaitLimitCycles) {
+        s_late = 1;
+        atomicOr(a.status, TDSA_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_late) {
+    const int64_t count = static_cast<int64_t>(g.world) * g.k;
+    float* dv = reinterpret_cast<float*>(g.own + g.scratch_v_off) + row * count;
+    int32_t* di = reinterpret_cast<int32_t*>(g.own + g.scratch_i_off) + row * count;
+    const int64_t src_row = (static_cast<int64_t>(parity) * g.rows + row) * g.k;
+    for (int r = 0; r < g.world; ++r) {
+      const float* sv = reinterpret_cast<const float*>(g.peer_base[r] + g.vals_off) + src_row;
+      const int32_t* si = reinterpret_cast<const int32_t*>(g.peer_base[r] + g.idx_off) + src_row;
+      float* ov = dv + static_cast<int64_t>(r) * g.k;
+      int32_t* oi = di + static_cast<int64_t>(r) * g.k;
+      if ((g.k & 3) == 0) {
+        for (int e = tid; e < g.k / 4; e += blockDim.x) {
+          reinterpret_cast<float4*>(ov)[e] = __ldcv(reinterpret_cast<const float4*>(sv) + e);
+          reinterpret_cast<int4*>(oi)[e] = __ldcv(reinterpret_cast<const int4*>(si) + e);
+        }
+      } else {
+        for (int e = tid; e < g.k; e += blockDim.x) {
+          ov[e] = __ldcv(sv + e);
+          oi[e] = __ldcv(si + e);
+        }
+      }
+    }
+  }
+  fence_proxy_async_global();  // the bulk copies of the selection read these stores
+  __syncthreads();
+}
+
 // kPer keys per thread: segments of up to kPer * 1024 keys.  Thread t owns the kPer
 // consecutive elements [kPer*t, kPer*t + kPer) (thread order is index order) and visits
 // them rotated by its lane group, so a warp's 32 shared-memory reads hit 32 banks.
@@ -213,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   __syncthreads();
   pdl_wait();  // the scores and the histogram come from the previous kernel
   pdl_launch_dependents();
+  if (a.gather) gather_peer_row(a, row);
   if (bulk) {
     if (tid == 0) {
       for (int c = 0; c < npieces; ++c) {
@@ -989,7 +1048,7 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
   const int32_t* in_i = idx;
   int64_t in_vs = s_stride, in_is = idx_stride;
   for (int level = 0; level < p.levels; ++level) {
-    TopkArgs a;
+    TopkArgs a = {};
     a.vals = in_v;
     a.vals_stride = in_vs;
     a.idx = in_i;
@@ -1033,6 +1092,33 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
     }
   }
   return TDSA_OK;
+}
+
+int launch_merge_peers(const PeerGather& g, int sorted, void* out_idx, int idx_bytes,
+                       int64_t oi_stride, float* out_val, int64_t ov_stride,
+                       cudaStream_t stream) {
+  const int count = g.world * g.k;
+  int rc = topk_check(count, g.k, sorted);
+  if (rc) return rc;
+  if (count > kTopkSegment)
+    return fail(TDSA_ERR_UNSUPPORTED, "an exchange merges at most 32768 candidates per row");
+  TopkArgs a = {};
+  a.vals = reinterpret_cast<const float*>(g.own + g.scratch_v_off);
+  a.vals_stride = count;
+  a.idx = reinterpret_cast<const int32_t*>(g.own + g.scratch_i_off);
+  a.idx_stride = count;
+  a.row_len = count;
+  a.chunk = count;
+  a.k = g.k;
+  a.sorted = sorted;
+  a.out_idx = out_idx;
+  a.idx_bytes = idx_bytes;
+  a.out_idx_stride = oi_stride;
+  a.out_val = out_val;
+  a.out_val_stride = ov_stride;
+  a.gather = 1;
+  a.pg = g;
+  return launch_segments(a, g.rows, 1, stream);
 }
 
 }  // namespace tdsa

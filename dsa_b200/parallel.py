@@ -132,17 +132,98 @@ class _CandidateMerge:
         return self.indices, self.values
 
 
+class PeerExchange:
+    """The exchange step of an L-sharded top-k over peer memory (NVLink) instead of an
+    all-gather: ``tdsa_exchange_publish`` writes this rank's candidates into its exchange
+    region and raises its per-row flag in every rank's region, ``tdsa_exchange_merge`` waits
+    per row for every rank's flag, pulls the rows from peer memory and selects the global
+    top-k -- one launch each, no collective library call on the data path.  The regions
+    are shared once through CUDA IPC (handles all-gathered over `group`); all ranks must be
+    on one node.  Call ``close()`` on every rank when done: it waits for all ranks before
+    freeing the region the others read."""
+
+    def __init__(self, batch: int, k: int, *, sorted: bool, group, device):
+        import ctypes as C
+
+        from . import _capi as capi
+
+        dist_on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if dist_on else 1
+        self.rank = dist.get_rank(group) if dist_on else 0
+        self.batch, self.k, self.sorted, self.group = batch, k, bool(sorted), group
+        self.device = torch.device(device)
+        handle = (C.c_uint8 * capi.TDSA_IPC_HANDLE_BYTES)()
+        ptr = C.c_void_p()
+        capi.call("tdsa_exchange_create", self.world, self.rank, batch, k, C.byref(ptr),
+                  handle)
+        self._ex = ptr
+        mine = torch.tensor(bytearray(handle), dtype=torch.uint8, device=self.device)
+        if self.world > 1:
+            every = torch.empty(self.world, capi.TDSA_IPC_HANDLE_BYTES, dtype=torch.uint8,
+                                device=self.device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+        else:
+            every = mine.view(1, -1)
+        blob = bytes(every.cpu().numpy().tobytes())
+        try:
+            capi.call("tdsa_exchange_connect", self._ex, blob)
+        except Exception:
+            capi.lib().tdsa_exchange_destroy(self._ex)
+            self._ex = None
+            raise
+        self.indices = torch.empty(batch, k, device=self.device, dtype=torch.int64)
+        self.values = torch.empty(batch, k, device=self.device, dtype=torch.float32)
+
+    def __call__(self, values: torch.Tensor, indices: torch.Tensor, offset: int):
+        from . import _capi as capi
+        from .indexer import stream_ptr
+
+        if self._ex is None:
+            raise RuntimeError("exchange is closed")
+        if values.dtype != torch.float32 or indices.dtype != torch.int32:
+            raise ValueError("candidates must be float32 values and int32 indices")
+        if values.stride() != indices.stride() or values.stride(-1) != 1:
+            raise ValueError("values and indices need the same row-contiguous layout")
+        s = stream_ptr(self.device)
+        capi.call("tdsa_exchange_publish", self._ex, values.data_ptr(), indices.data_ptr(),
+                  values.stride(0), int(offset), s)
+        capi.call("tdsa_exchange_merge", self._ex, int(self.sorted), self.indices.data_ptr(),
+                  8, self.indices.stride(0), self.values.data_ptr(), self.values.stride(0), s)
+        return self.indices, self.values
+
+    def close(self) -> None:
+        """Free the exchange region once every rank is past its last merge."""
+        from . import _capi as capi
+
+        if self._ex is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        ex, self._ex = self._ex, None
+        capi.call("tdsa_exchange_destroy", ex)
+
+
+def _make_exchange(kind: str, batch: int, k: int, *, sorted: bool, group, device):
+    if kind == "allgather":
+        return _CandidateMerge(batch, k, sorted=sorted, group=group, device=device)
+    if kind == "peer":
+        return PeerExchange(batch, k, sorted=sorted, group=group, device=device)
+    raise ValueError("exchange must be 'allgather' or 'peer'")
+
+
 class LShardedPlan:
     """The L-sharded top-k on fixed buffers (the decode-loop form of ``LShardedTopK``).
 
     Per ``run()``: dense score + unsorted top-k of this rank's keys (``ScoreTopkPlan``),
     global indices, ONE all-gather of the packed (value bits, index) candidates, a
     rank-major -> row-major copy, and the merge.  The caller rewrites ``queries`` /
-    ``weights`` in place between steps."""
+    ``weights`` in place between steps.  ``exchange="peer"`` replaces the all-gather, copy
+    and merge by ``PeerExchange`` (peer memory, one node)."""
 
     def __init__(self, queries: torch.Tensor, weights: torch.Tensor, keys_shard: torch.Tensor,
                  k: int, offset: int, *, sorted: bool = True,
-                 group: dist.ProcessGroup | None = None):
+                 group: dist.ProcessGroup | None = None, exchange: str = "allgather"):
         from .indexer import ScoreTopkPlan
 
         if keys_shard.shape[-2] < k:
@@ -150,13 +231,17 @@ class LShardedPlan:
         self.plan = ScoreTopkPlan(queries, weights, keys_shard, k, sorted=False,
                                   index_dtype=torch.int32)
         self.k, self.offset, self.sorted, self.group = k, int(offset), bool(sorted), group
-        self.merge = _CandidateMerge(self.plan.batch, k, sorted=sorted, group=group,
-                                     device=keys_shard.device)
+        self.merge = _make_exchange(exchange, self.plan.batch, k, sorted=sorted, group=group,
+                                    device=keys_shard.device)
         self.world = self.merge.world
 
     def run(self) -> tuple[torch.Tensor, torch.Tensor]:
         self.plan.run()
         return self.merge(self.plan.values, self.plan.indices, self.offset)
+
+    def close(self) -> None:
+        if hasattr(self.merge, "close"):
+            self.merge.close()
 
 
 class LShardedExact:
@@ -172,15 +257,15 @@ class LShardedExact:
     def __init__(self, batch: int, max_shard_length: int, k: int, offset: int, *,
                  block_size: int = 64, dtype: torch.dtype = torch.bfloat16,
                  device: torch.device | str | None = None, sorted: bool = True,
-                 group: dist.ProcessGroup | None = None):
+                 group: dist.ProcessGroup | None = None, exchange: str = "allgather"):
         from .progressive_exact import ExactProgressiveTopK
 
         self.exact = ExactProgressiveTopK(batch, max_shard_length, k, block_size=block_size,
                                           dtype=dtype, device=device, sorted=False,
                                           index_dtype=torch.int32)
         self.k, self.offset = k, int(offset)
-        self.merge = _CandidateMerge(batch, k, sorted=sorted, group=group,
-                                     device=self.exact.device)
+        self.merge = _make_exchange(exchange, batch, k, sorted=sorted, group=group,
+                                    device=self.exact.device)
         self.world = self.merge.world
 
     def init(self, queries, weights, keys_shard):
@@ -195,3 +280,7 @@ class LShardedExact:
 
     def stats(self) -> list[dict]:
         return self.exact.stats()
+
+    def close(self) -> None:
+        if hasattr(self.merge, "close"):
+            self.merge.close()

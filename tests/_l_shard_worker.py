@@ -34,17 +34,34 @@ def main() -> None:
         start, stop = shard_bounds(length, rank, world)
         dev = torch.device("cuda", torch.cuda.current_device())
         shard = keys[:, start:stop].contiguous().to(dev)
-        idx, val = LShardedTopK(k, sorted=True)(q.to(dev), w.to(dev), shard, start)
-        plan = LShardedPlan(q.to(dev), w.to(dev), shard, k, start, sorted=True)
+        qd, wd = q.to(dev), w.to(dev)
+        idx, val = LShardedTopK(k, sorted=True)(qd, wd, shard, start)
+        plan = LShardedPlan(qd, wd, shard, k, start, sorted=True)
+        peer = LShardedPlan(qd, wd, shard, k, start, sorted=True, exchange="peer")
         pidx, pval = plan.run()
+        xidx, xval = peer.run()
         torch.cuda.synchronize()
+        want_i, want_v = scores_topk(qd, wd, keys.to(dev), k, sorted=True,
+                                     index_dtype=torch.int64)
+        ok = (torch.equal(idx, want_i) and torch.equal(val, want_v)
+              and torch.equal(pidx, want_i) and torch.equal(pval, want_v)
+              and torch.equal(xidx, want_i) and torch.equal(xval, want_v))
+        msg = "" if ok else f"step 0: {int((xidx != want_i).sum())} peer-exchange indices differ"
+        # later steps: new queries in place; the peer exchange reuses both region parities
+        for step in range(1, 5):
+            qd.copy_((qd.float() * 0.9 + 0.1 * torch.randn(b, 64, 128, generator=gen).to(dev)
+                      / math.sqrt(128)).to(torch.bfloat16))
+            pidx, pval = plan.run()
+            xidx, xval = peer.run()
+            torch.cuda.synchronize()
+            if not (torch.equal(pidx, xidx) and torch.equal(pval, xval)):
+                ok, msg = False, msg or f"step {step}: peer exchange != all-gather"
+        peer.close()
+        flag = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if rank == 0:
-            want_i, want_v = scores_topk(q.to(dev), w.to(dev), keys.to(dev), k, sorted=True,
-                                         index_dtype=torch.int64)
-            ok = (torch.equal(idx, want_i) and torch.equal(val, want_v)
-                  and torch.equal(pidx, want_i) and torch.equal(pval, want_v))
             with open(out_path, "w") as f:
-                f.write("OK" if ok else f"MISMATCH {int((idx != want_i).sum())} indices")
+                f.write("OK" if int(flag) == 1 else f"MISMATCH {msg or 'on another rank'}")
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -75,6 +75,54 @@ def test_l_sharded_plan_single_process_equals_whole_row():
         assert torch.equal(idx, want_i) and torch.equal(val, want_v)
 
 
+@pytest.mark.parametrize("sorted_", [True, False])
+def test_peer_exchange_single_rank_equals_allgather_every_step(sorted_):
+    """The peer-memory exchange in one process (world 1: the rank publishes into and merges
+    from its own region) returns what the all-gather merge returns, over steps that reuse
+    both parities of the region, with ties and a nonzero shard offset."""
+    from dsa_b200.parallel import LShardedPlan
+
+    gen = torch.Generator().manual_seed(13)
+    b, length, k = 8, 20000, 2048
+    q = (torch.randn(b, 64, 128, generator=gen) / math.sqrt(128)).to(torch.bfloat16).cuda()
+    w = (torch.randn(b, 64, generator=gen) / 8).cuda()
+    keys = torch.randn(b, length, 128, generator=gen).to(torch.bfloat16).cuda()
+    keys[:, 5000:9000] = keys[:, 5000:5001]  # a run of tied scores
+    peer = LShardedPlan(q, w, keys, k, 777, sorted=sorted_, exchange="peer")
+    ref = LShardedPlan(q, w, keys, k, 777, sorted=sorted_)
+    try:
+        for step in range(5):
+            got_i, got_v = peer.run()
+            want_i, want_v = ref.run()
+            assert torch.equal(got_i, want_i) and torch.equal(got_v, want_v), step
+            q.copy_((q.float() * 0.9 + 0.1 * torch.randn(b, 64, 128, generator=gen).cuda()
+                     / math.sqrt(128)).to(torch.bfloat16))
+    finally:
+        peer.close()
+
+
+def test_peer_exchange_argument_errors():
+    import ctypes as C
+
+    from dsa_b200 import _capi as capi
+
+    lib = capi.lib()
+    ptr = C.c_void_p()
+    handle = (C.c_uint8 * capi.TDSA_IPC_HANDLE_BYTES)()
+    assert lib.tdsa_exchange_create(0, 0, 8, 2048, C.byref(ptr), handle) == capi.TDSA_ERR_INVALID
+    assert lib.tdsa_exchange_create(2, 2, 8, 2048, C.byref(ptr), handle) == capi.TDSA_ERR_INVALID
+    assert lib.tdsa_exchange_create(16, 0, 8, 4096, C.byref(ptr), handle) == \
+        capi.TDSA_ERR_UNSUPPORTED  # 65536 candidates per row
+    assert lib.tdsa_exchange_create(1, 0, 8, 2048, C.byref(ptr), handle) == capi.TDSA_OK
+    try:
+        out = torch.empty(8, 2048, dtype=torch.int64, device="cuda")
+        # not connected yet
+        assert lib.tdsa_exchange_merge(ptr, 0, out.data_ptr(), 8, 2048, None, 0, None) == \
+            capi.TDSA_ERR_INVALID
+    finally:
+        assert lib.tdsa_exchange_destroy(ptr) == capi.TDSA_OK
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_l_sharded_exact_progressive_equals_dense_every_step(world):
     """Exact progressive top-k per shard (append-only: new keys go to the last shard) plus
