@@ -652,8 +652,9 @@ def run_cfg3(args, device: torch.device) -> dict:
 def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
     """BASELINE config 5: B=8 sequences, L=131072 bf16 keys sharded along L over the ranks;
     each rank scores its range, keeps its top-2048 with global indices, and the candidates
-    are all-gathered (NCCL) and merged -- the exact global top-2048.  Total work is fixed
-    (strong scaling); value = all keys scored / step time (max over ranks)."""
+    are exchanged over peer memory (tdsa_exchange_*; the NCCL all-gather + merge is timed
+    beside it) and merged -- the exact global top-2048.  Total work is fixed (strong
+    scaling); value = all keys scored / step time (max over ranks)."""
     from dsa_b200.parallel import LShardedPlan, shard_bounds
 
     b, length, k = 8, 131072, 2048
@@ -663,38 +664,47 @@ def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
     q = (torch.randn(b, 64, 128, generator=g, device=device) / math.sqrt(128)).to(torch.bfloat16)
     w = torch.randn(b, 64, generator=g, device=device) / 8
     shard = torch.randn(b, stop - start, 128, generator=g, device=device).to(torch.bfloat16)
-    sharded = LShardedPlan(q, w, shard, k, start, sorted=False)
-    for _ in range(args.warmup):
-        sharded.run()
-    torch.cuda.synchronize(device)
-    # One step (score, top-k levels, packing, all-gather, merge) as a CUDA graph, so the
-    # step is timed without host launch gaps; every rank captures the same sequence.
-    graph = torch.cuda.CUDAGraph()
-    cap = torch.cuda.Stream(device)
-    cap.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.graph(graph, stream=cap):
-        sharded.run()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize(device)
-    graph.replay()
-    torch.cuda.synchronize(device)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
+    def timed(exchange: str):
+        sharded = LShardedPlan(q, w, shard, k, start, sorted=False, exchange=exchange)
+        for _ in range(args.warmup):
+            sharded.run()
+        torch.cuda.synchronize(device)
+        # One step (score, top-k levels, exchange, merge) as a CUDA graph, so the step is
+        # timed without host launch gaps; every rank captures the same sequence.
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(device)
+        cap.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.graph(graph, stream=cap):
+            out = sharded.run()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
         graph.replay()
-    e1.record()
-    torch.cuda.synchronize(device)
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        torch.distributed.barrier()
-    del graph  # (holds NCCL work: released before the process group is destroyed)
-    if world > 1:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            torch.distributed.barrier()
+        del graph  # (may hold NCCL work: released before the process group is destroyed)
+        if world > 1:
+            t = torch.tensor([ms], device=device, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        result = (out[0].clone(), out[1].clone())
+        sharded.close()
+        return ms, result
+
+    # the product path exchanges over peer memory; the NCCL all-gather is timed beside it
+    ms, (pi, pv) = timed("peer")
+    ms_ag, (ai, av) = timed("allgather")
+    agree = bool(torch.equal(pi, ai) and torch.equal(pv, av))
     prog = cfg5_progressive(args, rank, world, device, b, start, stop, k, w)
     if rank != 0:
         return None
@@ -705,10 +715,15 @@ def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic, seeded N(0,1) (config 5)",
         "config": {"workload": "BASELINE config 5: B=8, L=131072 sharded along L, top-2048 "
-                               "merged over NCCL", "keys_per_rank": stop - start,
+                               "merged after a peer-memory exchange",
+                   "keys_per_rank": stop - start,
                    "parallelism": f"L-sharded x{world}",
                    "timing": "CUDA graph of one step replayed back to back, events, max over "
                              "ranks"},
+        "exchange": {"kind": "peer memory, one tdsa_exchange_topk launch per step",
+                     "allgather_ms_per_step": ms_ag,
+                     "allgather_value": b * length / (ms_ag * 1e-3),
+                     "results_agree": agree},
         "progressive": prog,
     }
 
@@ -716,7 +731,8 @@ def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
 def cfg5_progressive(args, rank, world, device, b, start, stop, k, w) -> dict:
     """Config 5's progressive variant: the exact certified progressive top-k per shard
     (LShardedExact, block 64), queries drifting as AR(1) with rho = 0.95, one key appended
-    per step to the last rank's range, the candidates merged over NCCL every step.  Timed
+    per step to the last rank's range, the candidates exchanged over peer memory and merged
+    every step.  Timed
     with CUDA events over the steps (host launches included), max over ranks."""
     from dsa_b200.parallel import LShardedExact
 
@@ -733,7 +749,7 @@ def cfg5_progressive(args, rank, world, device, b, start, stop, k, w) -> dict:
         qs.append(qf.to(torch.bfloat16))
         qf = rho * qf + math.sqrt(1 - rho * rho) * torch.randn(
             b, 64, 128, generator=g, device=device) / math.sqrt(128)
-    ex = LShardedExact(b, own + extra, k, start, block_size=64, sorted=False)
+    ex = LShardedExact(b, own + extra, k, start, block_size=64, sorted=False, exchange="peer")
     ex.init(qs[0], w, shard[:, :own])
     torch.cuda.synchronize(device)
     if world > 1:
@@ -748,6 +764,7 @@ def cfg5_progressive(args, rank, world, device, b, start, stop, k, w) -> dict:
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1) / steps
     st = ex.stats()
+    ex.close()
     read = sum(x["keys_scored"] for x in st) / max(1, sum(x["keys_total"] for x in st))
     pruned = sum(x["blocks_pruned"] for x in st)
     vals = torch.tensor([ms, read, pruned], device=device, dtype=torch.float64)
@@ -759,8 +776,7 @@ def cfg5_progressive(args, rank, world, device, b, start, stop, k, w) -> dict:
         ms, read, pruned = float(mx[0]), float(sm[1]) / world, float(sm[2])
     return {"ms_per_step": ms, "steps": steps, "keys_read_fraction": read,
             "blocks_pruned": int(pruned), "queries": "AR(1) rho 0.95, i.i.d. N(0,1) keys",
-            "api": "dsa_b200.parallel.LShardedExact (tdsa_exact_step + all-gather + "
-                   "tdsa_merge_topk)"}
+            "api": "dsa_b200.parallel.LShardedExact (tdsa_exact_step + tdsa_exchange_topk)"}
 
 
 # ----------------------------------------------------------------------------- CPU arm

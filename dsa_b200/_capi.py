@@ -65,8 +65,7 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_exchange_bytes": (sz, [i32, i32, i32]),
     "tdsa_exchange_create": (i32, [i32, i32, i32, i32, C.POINTER(vp), vp]),
     "tdsa_exchange_connect": (i32, [vp, vp]),
-    "tdsa_exchange_publish": (i32, [vp, vp, vp, i64, i32, vp]),
-    "tdsa_exchange_merge": (i32, [vp, i32, vp, i32, i64, vp, i64, vp]),
+    "tdsa_exchange_topk": (i32, [vp, vp, vp, i64, i32, i32, vp, i32, i64, vp, i64, vp]),
     "tdsa_exchange_destroy": (i32, [vp]),
     "tdsa_score_topk_workspace_bytes": (sz, [i32, i32, i32]),
     "tdsa_score_topk": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32, vp, i32,

@@ -1,20 +1,15 @@
 // Candidate exchange of an L-sharded top-k over peer memory (NVLink / NVSwitch), in place
-// of an all-gather.  New: the reference never shards (its scoring runs on one GPU).
+// of an all-gather + merge.  New: the reference never shards (its scoring runs on one GPU).
 //
 // Every rank allocates one exchange region (layout in kernels.cuh, PeerGather) and shares
-// it with the node's other ranks through CUDA IPC.  A step is two launches per rank:
-//   1. exchange_publish_kernel: one CTA per row copies the rank's local top-k (values, and
-//      indices made global by the shard offset) into its own region under the step's
-//      parity, then, after a system-scope fence, stores the step's epoch into that row's
-//      flag in every rank's region (a plain store over NVLink);
-//   2. the merge (topk.cu, topk_segment_kernel with gather set): each CTA waits for its
-//      row's flag from every rank (bounded), pulls the ranks' rows from peer memory into
-//      local scratch and selects the global top-k.
-// Two parities make the reuse safe: a rank publishes step s + 2 (same parity as s) only
-// after its merge of step s + 1, which needed every rank's step s + 1 flags, each set after
-// that rank's merge of step s had finished reading.  Loads and stores only; no multicast.
+// it with the node's other ranks through CUDA IPC.  A step is ONE launch per rank
+// (launch_exchange_topk, topk.cu): each CTA publishes its row of the rank's local top-k into
+// the region, raises that row's flag in every rank's region with a system-scope release
+// store (a plain store over NVLink for a peer), waits (bounded) for the row's flag from
+// every rank, pulls the ranks' rows from their regions and selects the global top-k -- the
+// collective and the selection in one kernel.  Loads and stores only; no multicast.
 #include <cstring>
-#include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -34,8 +29,6 @@ struct tdsa_exchange {
 namespace tdsa {
 
 namespace {
-
-constexpr int kPublishThreads = 256;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -57,41 +50,6 @@ size_t exchange_layout(int world, int rows, int k, PeerGather& g) {
   g.scratch_i_off = static_cast<int64_t>(off);
   off = align_up(off + scratch, 256);
   return off;
-}
-
-__global__ void __launch_bounds__(kPublishThreads)
-    exchange_publish_kernel(PeerGather g, const float* vals, const int32_t* idx,
-                            int64_t stride, int32_t offset) {
-  pdl_wait();  // the local top-k comes from the previous kernel
-  pdl_launch_dependents();
-  uint32_t* ctr = reinterpret_cast<uint32_t*>(g.own + g.ctr_off);
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ctr) + 1u, parity = epoch & 1u;
-  const int row = blockIdx.x, tid = threadIdx.x;
-  const int64_t dst_row = (static_cast<int64_t>(parity) * g.rows + row) * g.k;
-  float* dv = reinterpret_cast<float*>(g.own + g.vals_off) + dst_row;
-  int32_t* di = reinterpret_cast<int32_t*>(g.own + g.idx_off) + dst_row;
-  const float* sv = vals + static_cast<int64_t>(row) * stride;
-  const int32_t* si = idx + static_cast<int64_t>(row) * stride;
-  for (int e = tid; e < g.k; e += kPublishThreads) {
-    dv[e] = sv[e];
-    di[e] = si[e] + offset;
-  }
-  __syncthreads();
-  if (tid < g.world) {
-    __threadfence_system();  // the row (written by the whole CTA) before the flag
-    uint32_t* f = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(g.peer_base[tid]) +
-                                              g.flags_off) +
-                  (static_cast<int64_t>(parity) * g.world + g.rank) * g.rows + row;
-    st_release_sys(f, epoch);
-  }
-  // the epoch advances once every CTA has read it
-  if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(ctr + 1, 1u) == gridDim.x - 1u) {
-      ctr[1] = 0u;
-      *reinterpret_cast<volatile uint32_t*>(ctr) = epoch;
-    }
-  }
 }
 
 }  // namespace
@@ -182,31 +140,26 @@ int tdsa_exchange_connect(tdsa_exchange* ex, const void* handles) {
   return TDSA_OK;
 }
 
-int tdsa_exchange_publish(tdsa_exchange* ex, const float* values, const int32_t* indices,
-                          int64_t batch_stride, int32_t index_offset, void* stream) {
-  if (!ex || !values || !indices) return fail(TDSA_ERR_INVALID, "null pointer argument");
-  if (!ex->connected) return fail(TDSA_ERR_INVALID, "exchange not connected");
-  if (ex->rows > 1 && batch_stride < ex->k)
-    return fail(TDSA_ERR_INVALID, "candidate row stride must be >= k");
-  TDSA_CUDA_CHECK(tdsa::launch_pdl(tdsa::exchange_publish_kernel, dim3(ex->rows),
-                                   dim3(tdsa::kPublishThreads), 0,
-                                   static_cast<cudaStream_t>(stream), ex->g, values, indices,
-                                   batch_stride, index_offset));
-  TDSA_CUDA_CHECK(cudaGetLastError());
-  return TDSA_OK;
-}
-
-int tdsa_exchange_merge(tdsa_exchange* ex, int sorted, void* out_indices, int index_bytes,
-                        int64_t idx_batch_stride, float* out_values, int64_t val_batch_stride,
-                        void* stream) {
-  if (!ex || !out_indices) return fail(TDSA_ERR_INVALID, "null pointer argument");
+int tdsa_exchange_topk(tdsa_exchange* ex, const float* values, const int32_t* indices,
+                       int64_t batch_stride, int32_t index_offset, int sorted,
+                       void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                       float* out_values, int64_t val_batch_stride, void* stream) {
+  if (!ex || !values || !indices || !out_indices)
+    return fail(TDSA_ERR_INVALID, "null pointer argument");
   if (!ex->connected) return fail(TDSA_ERR_INVALID, "exchange not connected");
   if (index_bytes != 4 && index_bytes != 8) return fail(TDSA_ERR_INVALID, "index_bytes: 4 or 8");
+  if (ex->rows > 1 && batch_stride < ex->k)
+    return fail(TDSA_ERR_INVALID, "candidate row stride must be >= k");
   if (ex->rows > 1 && (idx_batch_stride < ex->k || (out_values && val_batch_stride < ex->k)))
     return fail(TDSA_ERR_INVALID, "output row stride must be >= k");
-  return tdsa::launch_merge_peers(ex->g, sorted ? 1 : 0, out_indices, index_bytes,
-                                  idx_batch_stride, out_values, val_batch_stride,
-                                  static_cast<cudaStream_t>(stream));
+  tdsa::PeerGather g = ex->g;
+  g.local_vals = values;
+  g.local_idx = indices;
+  g.local_stride = batch_stride;
+  g.offset = index_offset;
+  return tdsa::launch_exchange_topk(g, sorted ? 1 : 0, out_indices, index_bytes,
+                                    idx_batch_stride, out_values, val_batch_stride,
+                                    static_cast<cudaStream_t>(stream));
 }
 
 int tdsa_exchange_destroy(tdsa_exchange* ex) {

@@ -88,13 +88,13 @@ int launch_temporal_radius(const double* qn, const double* qp, const double* wn,
 int launch_relu_index_score(const double* q, const double* keys, const double* w, int heads,
                             int dim, int tokens, double* out, cudaStream_t stream);
 
-// The exchange of an L-sharded merge over peer memory (exchange.cu publishes, topk.cu
-// merges).  Every rank owns one exchange region, mapped into the node's other ranks through
-// CUDA IPC:
+// The exchange of an L-sharded merge over peer memory (exchange.cu: the region and the C
+// ABI; topk.cu: the kernel).  Every rank owns one exchange region, mapped into the node's
+// other ranks through CUDA IPC:
 //   vals [2][rows][k] f32, idx [2][rows][k] i32: the rank's candidates, by step parity;
 //   flags [2][world][rows] u32: (parity, src, row) holds the step's epoch once rank src has
 //     published that row;
-//   ctr [4] u32: the epoch of the last published step, a CTA counter;
+//   ctr [4] u32: the epoch of the last step, a CTA counter;
 //   scratch vals / idx [rows][world * k]: the merge's gathered rows (local only).
 constexpr int kMaxExchangeWorld = 16;
 struct PeerGather {
@@ -102,12 +102,17 @@ struct PeerGather {
   uint8_t* own;                     // this rank's region
   int world, rank, rows, k;
   int64_t vals_off, idx_off, flags_off, ctr_off, scratch_v_off, scratch_i_off;
+  const float* local_vals;          // this step's local top-k [rows][k] (from the previous
+  const int32_t* local_idx;         // kernel), indices local to the shard
+  int64_t local_stride;
+  int32_t offset;                   // the shard's first global index
 };
-// Merge level of an exchange: each CTA waits (bounded) for its row's flag from every rank,
-// copies the ranks' candidate rows into its scratch row, and selects the top-k.
-int launch_merge_peers(const PeerGather& g, int sorted, void* out_idx, int idx_bytes,
-                       int64_t oi_stride, float* out_val, int64_t ov_stride,
-                       cudaStream_t stream);
+// One launch per step: each CTA publishes its row of the local top-k into the region and
+// raises that row's flag in every rank's region, waits (bounded) for the row's flag from
+// every rank, copies the ranks' rows into its scratch row and selects the top-k.
+int launch_exchange_topk(const PeerGather& g, int sorted, void* out_idx, int idx_bytes,
+                         int64_t oi_stride, float* out_val, int64_t ov_stride,
+                         cudaStream_t stream);
 
 size_t topk_workspace_bytes(int batch, int length, int k);
 int topk_levels(int batch, int length, int k, int hist);

@@ -67,6 +67,7 @@ struct TopkArgs {
   int* status;            // device status word (bounded-wait timeouts)
   int gather;             // merge of an exchange: gather the rows from peer memory first
   PeerGather pg;
+  int hist_segs;          // cluster top-k: the row's 32768-key histogram segments (summed)
 };
 
 __device__ __forceinline__ unsigned lanemask_lt() {
@@ -162,27 +163,58 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* wa, ui
   return wb[warp] + x - v;
 }
 
-// Merge of an exchange: wait (bounded) until every rank has published this row for the
-// current epoch, then copy the ranks' candidate rows (peer memory over NVLink, loads that
-// bypass L1) into this row of the local scratch, which the selection then reads as its
-// input (a.vals / a.idx).  A wait that runs out raises TDSA_ERR_TIMEOUT and leaves the
-// scratch as it was.
+// Merge of an exchange (topk_segment_kernel with a.gather set), before the selection:
+//   1. the step's epoch is the region's last one + 1; the grid's last CTA to read it stores
+//      it back for the next step;
+//   2. this rank's row of the local top-k (indices made global) goes into the region under
+//      the epoch's parity, and one release store per rank (system scope: over NVLink for a
+//      peer) puts the epoch into that rank's flag (parity, this rank, row);
+//   3. a bounded wait until every rank's flag for this row holds the epoch (acquire);
+//   4. the ranks' rows are copied from their regions (loads that bypass L1) into this row of
+//      the local scratch, which the selection reads as its input (a.vals / a.idx).
+// A wait that runs out raises TDSA_ERR_TIMEOUT and leaves the scratch as it was.  Reuse is
+// safe with two parities: a rank publishes step s + 2 only after its step s + 1 merge saw
+// every rank's step s + 1 flag, raised at the start of that rank's next launch after its
+// step s merge had finished reading.
 __device__ void gather_peer_row(const TopkArgs& a, int row) {
   __shared__ uint32_t s_epoch;
   __shared__ int s_late;
   const PeerGather& g = a.pg;
   const int tid = threadIdx.x;
+  uint32_t* ctr = reinterpret_cast<uint32_t*>(g.own + g.ctr_off);
   if (tid == 0) {
-    s_epoch = *reinterpret_cast<volatile const uint32_t*>(g.own + g.ctr_off);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ctr) + 1u;
+    s_epoch = epoch;
     s_late = 0;
+    __threadfence();
+    if (atomicAdd(ctr + 1, 1u) == gridDim.x * gridDim.y - 1u) {  // every CTA has read it
+      ctr[1] = 0u;
+      *reinterpret_cast<volatile uint32_t*>(ctr) = epoch;
+    }
   }
   __syncthreads();
   const uint32_t epoch = s_epoch, parity = epoch & 1u;
+  const int64_t slot = (static_cast<int64_t>(parity) * g.rows + row) * g.k;
+  {
+    float* dv = reinterpret_cast<float*>(g.own + g.vals_off) + slot;
+    int32_t* di = reinterpret_cast<int32_t*>(g.own + g.idx_off) + slot;
+    const float* sv = g.local_vals + static_cast<int64_t>(row) * g.local_stride;
+    const int32_t* si = g.local_idx + static_cast<int64_t>(row) * g.local_stride;
+    for (int e = tid; e < g.k; e += blockDim.x) {
+      dv[e] = sv[e];
+      di[e] = si[e] + g.offset;
+    }
+  }
+  __syncthreads();  // the row, written by the whole CTA, before the release stores
   if (tid < g.world) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(g.own + g.flags_off) +
-                        (static_cast<int64_t>(parity) * g.world + tid) * g.rows + row;
+    uint32_t* f = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(g.peer_base[tid]) +
+                                              g.flags_off) +
+                  (static_cast<int64_t>(parity) * g.world + g.rank) * g.rows + row;
+    st_release_sys(f, epoch);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(g.own + g.flags_off) +
+                           (static_cast<int64_t>(parity) * g.world + tid) * g.rows + row;
     const long long t0 = clock64();
-    while (ld_acquire_sys(f) != epoch) {
+    while (ld_acquire_sys(mine) != epoch) {
       if (clock64() - t0 > kWaitLimitCycles) {
         s_late = 1;
         atomicOr(a.status, TDSA_ERR_TIMEOUT);
@@ -195,10 +227,9 @@ __device__ void gather_peer_row(const TopkArgs& a, int row) {
     const int64_t count = static_cast<int64_t>(g.world) * g.k;
     float* dv = reinterpret_cast<float*>(g.own + g.scratch_v_off) + row * count;
     int32_t* di = reinterpret_cast<int32_t*>(g.own + g.scratch_i_off) + row * count;
-    const int64_t src_row = (static_cast<int64_t>(parity) * g.rows + row) * g.k;
     for (int r = 0; r < g.world; ++r) {
-      const float* sv = reinterpret_cast<const float*>(g.peer_base[r] + g.vals_off) + src_row;
-      const int32_t* si = reinterpret_cast<const int32_t*>(g.peer_base[r] + g.idx_off) + src_row;
+      const float* sv = reinterpret_cast<const float*>(g.peer_base[r] + g.vals_off) + slot;
+      const int32_t* si = reinterpret_cast<const int32_t*>(g.peer_base[r] + g.idx_off) + slot;
       float* ov = dv + static_cast<int64_t>(r) * g.k;
       int32_t* oi = di + static_cast<int64_t>(r) * g.k;
       if ((g.k & 3) == 0) {
@@ -610,9 +641,11 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
 }
 
 // ---------------------------------------------------------------------------------------
-// Cluster top-k: one row of up to 32768 keys over the kC CTAs of a cluster, for batches too
-// small to fill the GPU one CTA per row.  Unsorted output, one level, and the score kernel's
-// 12-bit key histogram of the row.  CTA r of the cluster holds keys
+// Cluster top-k: one row over the kC CTAs of a cluster, for batches too small to fill the
+// GPU one CTA per row: rows of up to 32768 keys (one histogram segment) over 2-8 CTAs, and
+// rows of up to 131072 keys over 8 CTAs in place of the levels.  Unsorted output, and the
+// score kernel's 12-bit key histograms of the row's 32768-key segments (summed).  CTA r of
+// the cluster holds keys
 // [r*kPer*1024, (r+1)*kPer*1024) in registers: warp w the 32*kPer keys from
 // r*kPer*1024 + w*32*kPer, in chunks of 32*kV (kV = min(kPer, 4)) with lane l holding kV
 // consecutive keys of each chunk, so every load is one coalesced 128-512 byte access and
@@ -691,9 +724,15 @@ __global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
 
   // ---- the row's histogram counts and the keys (loads issued together)
-  uint32_t* gh = a.hist + static_cast<int64_t>(row) * kKeyHistBins;
+  uint32_t* gh = a.hist + static_cast<int64_t>(row) * a.hist_segs * kKeyHistBins;
   uint32_t c4[4];
   bins_from_top(gh, kKeyHistBins, c4);
+  for (int sg = 1; sg < a.hist_segs; ++sg) {  // a row of several segments: their sum
+    uint32_t t4[4];
+    bins_from_top(gh + sg * kKeyHistBins, kKeyHistBins, t4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c4[i] += t4[i];
+  }
   const float* vrow = a.vals + static_cast<int64_t>(row) * a.vals_stride;
   const bool vec = (reinterpret_cast<uintptr_t>(vrow) & (kV * 4 - 1)) == 0;
   uint32_t u[kPer];
@@ -796,11 +835,17 @@ __global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane < kC) st_cluster_u32(mapa_shared(smem_u32(&s_cnt[rank]), lane), cta_total);
   }
   cluster_sync_all();  // the last access to a peer's shared memory
-  for (int i = static_cast<int>(rank) * (kKeyHistBins / kC) + tid;
-       i < static_cast<int>(rank + 1) * (kKeyHistBins / kC); i += kThreads)
-    gh[i] = 0u;  // every CTA of the cluster has read the histogram: ready for reuse
-  uint32_t run = wb[warp];
-  for (uint32_t r = 0; r < rank; ++r) run += s_cnt[r];
+  for (int sg = 0; sg < a.hist_segs; ++sg)
+    for (int i = static_cast<int>(rank) * (kKeyHistBins / kC) + tid;
+         i < static_cast<int>(rank + 1) * (kKeyHistBins / kC); i += kThreads)
+      gh[sg * kKeyHistBins + i] = 0u;  // every CTA has read the histogram: ready for reuse
+  // running (above, inside) counts before this warp's keys: 32-bit each, since a row of
+  // several segments can hold more than 65535 of either (the packed halves hold one CTA's)
+  uint32_t run_gt = wb[warp] & 0xFFFFu, run_eq = wb[warp] >> 16;
+  for (uint32_t r = 0; r < rank; ++r) {
+    run_gt += s_cnt[r] & 0xFFFFu;
+    run_eq += s_cnt[r] >> 16;
+  }
 
   const int64_t orow = static_cast<int64_t>(row);
   int32_t* oi32 = a.out_idx && a.idx_bytes == 4
@@ -820,8 +865,8 @@ __global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)
     }
     const uint32_t chunk_total = __shfl_sync(0xffffffffu, incl, 31);
     if (g | q) {
-      const uint32_t before = run + incl - mine;
-      uint32_t gtb = before & 0xFFFFu, eqb = before >> 16;
+      const uint32_t ex = incl - mine;
+      uint32_t gtb = run_gt + (ex & 0xFFFFu), eqb = run_eq + (ex >> 16);
       const int e0 = wbase + j * 32 * kV + lane * kV;
 #pragma unroll
       for (int s = 0; s < kV; ++s) {
@@ -840,7 +885,8 @@ __global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
-    run += chunk_total;
+    run_gt += chunk_total & 0xFFFFu;
+    run_eq += chunk_total >> 16;
   }
 }
 
@@ -894,10 +940,8 @@ int launch_cluster(const TopkArgs& a, int rows, int per, cudaStream_t stream) {
   if (per <= 1) return run(topk_cluster_kernel<1, kC>);
   if (per <= 2) return run(topk_cluster_kernel<2, kC>);
   if (per <= 4) return run(topk_cluster_kernel<4, kC>);
-  if constexpr (kC <= 4) {
-    if (per <= 8) return run(topk_cluster_kernel<8, kC>);
-  }
-  if constexpr (kC <= 2) return run(topk_cluster_kernel<16, kC>);
+  if (per <= 8) return run(topk_cluster_kernel<8, kC>);
+  if (per <= 16) return run(topk_cluster_kernel<16, kC>);
   return fail(TDSA_ERR_UNSUPPORTED, "cluster top-k: row too long for the cluster");
 }
 
@@ -1005,9 +1049,13 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
   const Plan p = make_plan(batch, length, k, key_hist != nullptr);
   if (p.levels > 1 && ws_bytes < topk_workspace_bytes(batch, length, k))
     return fail(TDSA_ERR_WORKSPACE, "top-k workspace too small");
-  if (p.levels == 1 && key_hist && !idx && !sorted && !kth_out) {
-    // one level of few rows: the cluster top-k spreads each row over several SMs
-    const int c = cluster_size(batch, length);
+  if (key_hist && !idx && !sorted && !kth_out) {
+    // few rows: the cluster top-k spreads each row over several SMs -- a one-segment row
+    // over 2 to 8 CTAs, a longer one (up to 131072 keys, several histogram segments) over
+    // 8 CTAs in place of the levels
+    const int c = p.levels == 1 ? cluster_size(batch, length)
+                  : (length <= 8 * kThreads * 16 && batch <= max_active_clusters<8>()) ? 8
+                                                                                      : 1;
     if (c > 1) {
       TopkArgs a = {};
       a.vals = scores;
@@ -1021,6 +1069,7 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
       a.out_val = out_val;
       a.out_val_stride = ov_stride;
       a.hist = key_hist;
+      a.hist_segs = (length + kTopkSegment - 1) / kTopkSegment;
       const int cap = c * kThreads;
       const int per = (length + cap - 1) / cap;
       if (c == 2) return launch_cluster<2>(a, batch, per, stream);
@@ -1094,9 +1143,9 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
   return TDSA_OK;
 }
 
-int launch_merge_peers(const PeerGather& g, int sorted, void* out_idx, int idx_bytes,
-                       int64_t oi_stride, float* out_val, int64_t ov_stride,
-                       cudaStream_t stream) {
+int launch_exchange_topk(const PeerGather& g, int sorted, void* out_idx, int idx_bytes,
+                         int64_t oi_stride, float* out_val, int64_t ov_stride,
+                         cudaStream_t stream) {
   const int count = g.world * g.k;
   int rc = topk_check(count, g.k, sorted);
   if (rc) return rc;

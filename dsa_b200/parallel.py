@@ -134,13 +134,13 @@ class _CandidateMerge:
 
 class PeerExchange:
     """The exchange step of an L-sharded top-k over peer memory (NVLink) instead of an
-    all-gather: ``tdsa_exchange_publish`` writes this rank's candidates into its exchange
-    region and raises its per-row flag in every rank's region, ``tdsa_exchange_merge`` waits
-    per row for every rank's flag, pulls the rows from peer memory and selects the global
-    top-k -- one launch each, no collective library call on the data path.  The regions
-    are shared once through CUDA IPC (handles all-gathered over `group`); all ranks must be
-    on one node.  Call ``close()`` on every rank when done: it waits for all ranks before
-    freeing the region the others read."""
+    all-gather: one ``tdsa_exchange_topk`` launch per step writes this rank's candidates
+    into its exchange region, raises its per-row flag in every rank's region, waits per row
+    for every rank's flag, pulls the rows from peer memory and selects the global top-k --
+    no collective library call on the data path.  The regions are shared once through CUDA
+    IPC (handles all-gathered over `group`); all ranks must be on one node.  Call
+    ``close()`` on every rank when done: it waits for all ranks before freeing the region
+    the others read."""
 
     def __init__(self, batch: int, k: int, *, sorted: bool, group, device):
         import ctypes as C
@@ -184,11 +184,10 @@ class PeerExchange:
             raise ValueError("candidates must be float32 values and int32 indices")
         if values.stride() != indices.stride() or values.stride(-1) != 1:
             raise ValueError("values and indices need the same row-contiguous layout")
-        s = stream_ptr(self.device)
-        capi.call("tdsa_exchange_publish", self._ex, values.data_ptr(), indices.data_ptr(),
-                  values.stride(0), int(offset), s)
-        capi.call("tdsa_exchange_merge", self._ex, int(self.sorted), self.indices.data_ptr(),
-                  8, self.indices.stride(0), self.values.data_ptr(), self.values.stride(0), s)
+        capi.call("tdsa_exchange_topk", self._ex, values.data_ptr(), indices.data_ptr(),
+                  values.stride(0), int(offset), int(self.sorted), self.indices.data_ptr(), 8,
+                  self.indices.stride(0), self.values.data_ptr(), self.values.stride(0),
+                  stream_ptr(self.device))
         return self.indices, self.values
 
     def close(self) -> None:

@@ -260,16 +260,16 @@ int tdsa_merge_topk(const float* cand_values, const int32_t* cand_indices,
  * tdsa_exchange_create allocates this rank's exchange region (tdsa_exchange_bytes) and
  * writes its CUDA IPC handle (TDSA_IPC_HANDLE_BYTES bytes); the caller gathers every rank's
  * handle, rank-major, and passes them to tdsa_exchange_connect (synchronous).  Each step,
- * every rank calls, on its stream, in the same order:
- *   tdsa_exchange_publish(values [batch][k] f32, indices [batch][k] int32 local to the shard,
- *                         row stride, index_offset = the shard's first global index);
- *   tdsa_exchange_merge(...) -> the global top-k of the batch rows (index_bytes 4 or 8).
- * The merge waits, per row and bounded (about a second), for every rank's publish of the
- * same step; a wait that runs out raises TDSA_ERR_TIMEOUT in the device status word and
- * leaves that row's output undefined.  Candidates within a rank's row must be in ascending
- * index order (tdsa_topk with sorted == 0), and world * k <= 32768.
- * tdsa_exchange_destroy (synchronous) must run on every rank only after all ranks' last
- * merge has finished (a barrier), since peers read this rank's region.
+ * every rank calls tdsa_exchange_topk on its stream with its local top-k: values
+ * [batch][k] float32 and indices [batch][k] int32 local to the shard (ascending index
+ * order within a row, as tdsa_topk with sorted == 0 gives), row stride batch_stride, and
+ * index_offset = the shard's first global index.  One launch publishes the rows into the
+ * region, waits per row and bounded (about a second) for every rank's rows of the same
+ * step, pulls them over NVLink and writes the global top-k (index_bytes 4 or 8).  A wait
+ * that runs out raises TDSA_ERR_TIMEOUT in the device status word and leaves that row's
+ * output undefined.  world * k <= 32768.  tdsa_exchange_destroy (synchronous) must run on
+ * every rank only after all ranks' last step has finished (a barrier), since peers read
+ * this rank's region.
  */
 #define TDSA_IPC_HANDLE_BYTES 64
 typedef struct tdsa_exchange tdsa_exchange;
@@ -277,11 +277,10 @@ size_t tdsa_exchange_bytes(int world, int batch, int k);
 int tdsa_exchange_create(int world, int rank, int batch, int k, tdsa_exchange** out,
                          void* ipc_handle_out);
 int tdsa_exchange_connect(tdsa_exchange* ex, const void* handles);
-int tdsa_exchange_publish(tdsa_exchange* ex, const float* values, const int32_t* indices,
-                          int64_t batch_stride, int32_t index_offset, void* stream);
-int tdsa_exchange_merge(tdsa_exchange* ex, int sorted, void* out_indices, int index_bytes,
-                        int64_t idx_batch_stride, float* out_values, int64_t val_batch_stride,
-                        void* stream);
+int tdsa_exchange_topk(tdsa_exchange* ex, const float* values, const int32_t* indices,
+                       int64_t batch_stride, int32_t index_offset, int sorted,
+                       void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                       float* out_values, int64_t val_batch_stride, void* stream);
 int tdsa_exchange_destroy(tdsa_exchange* ex);
 
 /* Bytes of device workspace tdsa_score_topk needs. */

@@ -504,3 +504,38 @@ def test_graph_capture_of_first_plan_run():
     res = subprocess.run([sys.executable, str(root / "tests" / "_graph_capture_worker.py")],
                          cwd=root, env=env, capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stderr[-2000:]
+
+
+@pytest.mark.parametrize("batch,length,k", [
+    (8, 131072, 2048),   # config 5 on one GPU: 16 keys per thread over 8 CTAs
+    (8, 65536, 2048),    # config 5 on two GPUs
+    (15, 100001, 512),   # odd length, the last segment short
+    (2, 131072, 8192),   # every key of row 0 tied: 131072 in the range, above 16 bits
+])
+def test_cluster_topk_long_rows_match_oracle(batch, length, k):
+    """Rows of several histogram segments selected in one cluster launch (8 CTAs, the
+    segments' histograms summed) against stable_topk: ties, +-0, -inf runs, a fully tied
+    row (its in-range count exceeds 16 bits); the histograms end zeroed."""
+    from dsa_b200 import _capi as capi
+
+    rng = np.random.default_rng(length + k)
+    s = np.round(rng.normal(size=(batch, length)) * 64).astype(np.float32) / 64
+    if batch == 2:
+        s[0] = 0.5
+    if batch > 1:
+        s[1, rng.integers(0, length, length // 4)] = -np.inf
+        s[1, rng.integers(0, length, 100)] = -0.0
+    dev = cuda(s)
+    hist = cuda(_key_hist_segments(s))
+    lib = capi.lib()
+    nbytes = lib.tdsa_topk_workspace_bytes(batch, length, k)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device="cuda")
+    idx = torch.empty(batch, k, dtype=torch.int64, device="cuda")
+    val = torch.empty(batch, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist_ws", dev.data_ptr(), dev.stride(0), batch, length, k, 0,
+              idx.data_ptr(), 8, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(hist.abs().sum()) == 0

@@ -77,7 +77,7 @@ def test_l_sharded_plan_single_process_equals_whole_row():
 
 @pytest.mark.parametrize("sorted_", [True, False])
 def test_peer_exchange_single_rank_equals_allgather_every_step(sorted_):
-    """The peer-memory exchange in one process (world 1: the rank publishes into and merges
+    """The peer-memory exchange in one process (world 1: the rank publishes into and pulls
     from its own region) returns what the all-gather merge returns, over steps that reuse
     both parities of the region, with ties and a nonzero shard offset."""
     from dsa_b200.parallel import LShardedPlan
@@ -116,8 +116,11 @@ def test_peer_exchange_argument_errors():
     assert lib.tdsa_exchange_create(1, 0, 8, 2048, C.byref(ptr), handle) == capi.TDSA_OK
     try:
         out = torch.empty(8, 2048, dtype=torch.int64, device="cuda")
+        vals = torch.zeros(8, 2048, device="cuda")
+        idx = torch.zeros(8, 2048, dtype=torch.int32, device="cuda")
         # not connected yet
-        assert lib.tdsa_exchange_merge(ptr, 0, out.data_ptr(), 8, 2048, None, 0, None) == \
+        assert lib.tdsa_exchange_topk(ptr, vals.data_ptr(), idx.data_ptr(), 2048, 0, 0,
+                                      out.data_ptr(), 8, 2048, None, 0, None) == \
             capi.TDSA_ERR_INVALID
     finally:
         assert lib.tdsa_exchange_destroy(ptr) == capi.TDSA_OK
