@@ -50,3 +50,54 @@ def test_selftest_rejects_bad_limit():
     from dsa_b200 import _capi as capi
 
     assert capi.lib().tdsa_selftest_bounded_wait(-1, None) == capi.TDSA_ERR_INVALID
+
+
+def test_exchange_wait_for_a_silent_peer_times_out():
+    """A two-rank peer exchange whose other rank (a helper process holding its region on the
+    same GPU, launching nothing) never publishes: each row's bounded wait gives up after
+    about a second, the device status word reports TDSA_ERR_TIMEOUT, and the context keeps
+    working.  Only this process launches a kernel that waits."""
+    import ctypes as C
+    import os
+    import subprocess
+    import sys
+
+    from dsa_b200 import _capi as capi
+    from dsa_b200 import device_status, topk
+
+    rows, k = 2, 64
+    helper = os.path.join(os.path.dirname(__file__), "_exchange_silent_peer.py")
+    proc = subprocess.Popen([sys.executable, helper, str(rows), str(k)],
+                            stdin=subprocess.PIPE, stdout=subprocess.PIPE, text=True)
+    lib = capi.lib()
+    ex = C.c_void_p()
+    try:
+        peer_handle = bytes.fromhex(proc.stdout.readline().strip())
+        assert len(peer_handle) == capi.TDSA_IPC_HANDLE_BYTES
+        mine = (C.c_uint8 * capi.TDSA_IPC_HANDLE_BYTES)()
+        capi.call("tdsa_exchange_create", 2, 0, rows, k, C.byref(ex), mine)
+        capi.call("tdsa_exchange_connect", ex, bytes(mine) + peer_handle)
+        assert device_status(reset=True) == 0
+        vals = torch.randn(rows, k, device="cuda")
+        idx = torch.arange(rows * k, dtype=torch.int32, device="cuda").view(rows, k) % k
+        out_i = torch.empty(rows, k, dtype=torch.int64, device="cuda")
+        out_v = torch.empty(rows, k, device="cuda")
+        capi.call("tdsa_exchange_topk", ex, vals.data_ptr(), idx.data_ptr(), k, 0, 0,
+                  out_i.data_ptr(), 8, k, out_v.data_ptr(), k,
+                  torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert device_status(reset=True) == capi.TDSA_ERR_TIMEOUT
+        # the context is intact
+        x = torch.randn(3, 5000, device="cuda")
+        got_i, got_v = topk(x, 100, sorted=True)
+        want_v, _ = torch.sort(x, dim=1, descending=True)
+        assert torch.equal(got_v, want_v[:, :100])
+        assert device_status(reset=True) == 0
+    finally:
+        if ex.value:
+            torch.cuda.synchronize()
+            lib.tdsa_exchange_destroy(ex)
+        proc.stdin.write("done\n")
+        proc.stdin.flush()
+        proc.wait(timeout=60)
+    assert proc.returncode == 0
