@@ -580,18 +580,20 @@ def single_sequence_latency(wl: Config4, proj, device: torch.device, reps: int =
 # ----------------------------------------------------------------------------- cfg3 / cfg5
 def run_cfg3(args, device: torch.device) -> dict:
     """one sequence, L = 16384 growing by one key per step, AR(1) queries
-    (rho 0.95), fixed w, bf16: the exact certified progressive top-2048 (block 64) and dense
-    score + top-2048, each run for all steps back to back between two CUDA events (per-step
-    average; at B=1 both are bound by host launch time, not by the ~10 us of GPU work).
-    The exact path runs in its decode-loop form (ExactProgressivePlan: fixed buffers, the
-    query rewritten in place each step).  The exact top-k is compared with dense at every
-    step.  A second, block-structured trace
-    (10% of 64-key blocks at norm x3, the rest x0.05; slowly drifting queries, rho 0.999;
-    positive weights) is a case where the certified bound prunes blocks unread."""
+    (rho 0.95), fixed w, bf16: the exact certified progressive top-2048 at block sizes
+    16/32/64/128, and dense score + top-2048, each run for all steps back to back between two
+    CUDA events (per-step average; at B=1 both are bound by host launch time, not by the
+    ~10 us of GPU work).  The exact path runs in its decode-loop form (ExactProgressivePlan:
+    fixed buffers, the query rewritten in place each step).  The exact top-k is compared with
+    dense at every step.  Bytes read per step count the keys actually scored (256 B each) and
+    8 B of block metadata per visited block, the seed gathers included.  A second,
+    block-structured trace (10% of 64-key blocks at norm x3, the rest x0.05; slowly drifting
+    queries, rho 0.999; positive weights) is a case where the certified bound prunes blocks
+    unread."""
     from dsa_b200 import score_dense, topk
     from dsa_b200.progressive_exact import ExactProgressivePlan
 
-    steps, l0, k, bs = max(args.steps, 8), 16384, 2048, 64
+    steps, l0, k, data_block = max(args.steps, 8), 16384, 2048, 64
     res = {}
     for trace in ("iid", "structured"):
         g = torch.Generator().manual_seed(0)
@@ -603,48 +605,61 @@ def run_cfg3(args, device: torch.device) -> dict:
         else:
             rho, innov = 0.999, 0.02
             w = (torch.randn(64, generator=g).abs() / 8).to(device)
-            nb = (l0 + steps + bs - 1) // bs
+            nb = (l0 + steps + data_block - 1) // data_block
             scale = torch.where(torch.rand(nb, generator=g) < 0.1, 3.0, 0.05)
-            keys = torch.randn(l0 + steps, 128, generator=g) * scale.repeat_interleave(bs)[
-                :l0 + steps, None]
+            keys = torch.randn(l0 + steps, 128, generator=g) * scale.repeat_interleave(
+                data_block)[:l0 + steps, None]
         keys = keys.to(torch.bfloat16).to(device).unsqueeze(0)
         qs = []
         for _ in range(steps):
             q = rho * q + innov * torch.randn(64, 128, generator=g) / math.sqrt(128)
             qs.append(q.to(torch.bfloat16).to(device).unsqueeze(0))
         w1 = w.unsqueeze(0).contiguous()
-        # the decode-loop form: fixed query / weight / cache buffers, the query rewritten in
-        # place every step (as a projection kernel would), one C call per step
-        qbuf = qs[0].clone()
-        ex = ExactProgressivePlan(qbuf, w1, keys, k, block_size=bs, sorted=False)
-        ex.init(l0)
-        torch.cuda.synchronize(device)
         e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        got = []
-        e[0].record()
-        for t in range(steps):
-            qbuf.copy_(qs[t])
-            got.append(ex.step(l0 + t + 1)[0].clone())
-        e[1].record()
+        topk(score_dense(qs[0], w1, keys[:, :l0 + 1]), k, sorted=False)  # untimed first use
+        torch.cuda.synchronize(device)
         e[2].record()
         want = [topk(score_dense(qs[t], w1, keys[:, :l0 + t + 1]), k, sorted=False)[0]
                 for t in range(steps)]
         e[3].record()
         torch.cuda.synchronize(device)
-        st = ex.stats()[0]
-        res[trace] = {"exact_us_per_step": e[0].elapsed_time(e[1]) * 1e3 / steps,
-                      "dense_us_per_step": e[2].elapsed_time(e[3]) * 1e3 / steps,
-                      "exact_equals_dense_every_step": all(torch.equal(x, y)
-                                                           for x, y in zip(got, want)),
-                      "keys_read_fraction": st["keys_scored"] / max(1, st["keys_total"]),
-                      "blocks_pruned": st["blocks_pruned"],
-                      "blocks_visited": st["blocks_visited"]}
+        dense_us = e[2].elapsed_time(e[3]) * 1e3 / steps
+        sweep = {}
+        for bs in (16, 32, 64, 128):
+            # the decode-loop form: fixed query / weight / cache buffers, the query rewritten
+            # in place every step (as a projection kernel would), one C call per step
+            qbuf = qs[0].clone()
+            ex = ExactProgressivePlan(qbuf, w1, keys, k, block_size=bs, sorted=False)
+            ex.init(l0)
+            torch.cuda.synchronize(device)
+            st0 = ex.stats()[0]
+            got = []
+            e[0].record()
+            for t in range(steps):
+                qbuf.copy_(qs[t])
+                got.append(ex.step(l0 + t + 1)[0].clone())
+            e[1].record()
+            torch.cuda.synchronize(device)
+            st = {n: v - st0[n] for n, v in ex.stats()[0].items()}
+            bytes_read = st["keys_scored"] * 256 + st["blocks_visited"] * 8
+            sweep[str(bs)] = {
+                "exact_us_per_step": e[0].elapsed_time(e[1]) * 1e3 / steps,
+                "exact_equals_dense_every_step": all(torch.equal(x, y)
+                                                     for x, y in zip(got, want)),
+                "keys_read_fraction": st["keys_scored"] / max(1, st["keys_total"]),
+                "key_bytes_read_per_step": bytes_read / steps,
+                "dense_key_bytes_per_step": st["keys_total"] * 256 / steps,
+                "blocks_pruned": st["blocks_pruned"],
+                "blocks_visited": st["blocks_visited"]}
+        res[trace] = {"dense_us_per_step": dense_us, "block_sizes": sweep}
+    head = res["iid"]["block_sizes"]["64"]
     return {
         "metric": "exact progressive top-2048 decode step latency (config 3)",
-        "value": res["iid"]["exact_us_per_step"], "unit": "us", "higher_is_better": False,
+        "value": head["exact_us_per_step"], "unit": "us", "higher_is_better": False,
         "n_gpus": 1, "steps": steps, "dtype": "bf16", "data": "synthetic, seeded (config 3)",
-        "config": {"workload": "BASELINE config 3: B=1, L=16384+t, AR(1) rho 0.95, block 64",
-                   "k": k, "block_size": bs},
+        "config": {"workload": "BASELINE config 3: B=1, L=16384+t, AR(1) rho 0.95; value at "
+                               "block 64, all four block sizes under traces.*.block_sizes",
+                   "k": k, "block_size": 64},
         "traces": res,
     }
 
