@@ -249,6 +249,17 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     torch.cuda.synchronize(device)
     score_ms = statistics.fmean(a.elapsed_time(b) for a, b in score_events)
     score_ms = max_over_ranks(score_ms)
+    # Per-step spread (median, p5, p95 as the reference's benchmark reports them): one event
+    # between consecutive steps, in a pass of its own after the timed region.
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(min(args.steps, 50) + 1)]
+    marks[0].record(stream)
+    for m in marks[1:]:
+        step(False)
+        m.record(stream)
+    torch.cuda.synchronize(device)
+    per_step = sorted(a.elapsed_time(b) for a, b in zip(marks, marks[1:]))
+    spread = {name: max_over_ranks(per_step[min(len(per_step) - 1, int(q * len(per_step)))])
+              for name, q in (("p5", 0.05), ("median", 0.5), ("p95", 0.95))}
 
     # ---- end to end through the public API, host buffers, copies inside the region.  The
     # step is one CUDA graph: layer l's hidden states come in on a copy stream and layer
@@ -323,6 +334,9 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": ms_step,
+        "ms_per_step_spread": {**spread, "steps": len(per_step),
+                               "method": "events between consecutive steps, a pass after "
+                                         "the timed region; max over ranks"},
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
