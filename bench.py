@@ -388,6 +388,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         line["key_append"] = key_append_latency(wl, device)
         line["policy_step"] = policy_step_latency(wl, device,
                                                   cpu=not args.no_cpu_baseline)
+        if not args.no_reference_gpu:
+            line["reference_gpu"] = reference_gpu(wl, proj[0], device)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
     return line
@@ -592,6 +594,132 @@ def single_sequence_latency(wl: Config4, proj, device: torch.device, reps: int =
 
 
 # ----------------------------------------------------------------------------- cfg3 / cfg5
+def reference_gpu(wl: Config4, proj, device: torch.device, reps: int = 100) -> dict:
+    """The reference's own GPU code on this B200, beside ours on the same inputs.  Imported
+    unmodified from its offline install under baseline/_ref (absent: "unavailable").
+
+    - B = 1, L = 32768: ``full_scores_triton`` (its Triton scorer, progressive_kernel.py:
+      362-375) then ``torch.topk(scores, 2048, sorted=False)``, the path of its published
+      L40S figure (scripts/benchmark_progressive_dsa.py:117-124).  Timed as that script
+      times it: eager launches, events around the path, L2 flushed before each repetition;
+      and as one CUDA graph, which removes host launch time.  Ours is timed the same two ways
+      (ScoreTopkPlan.run).
+    - one config-4 layer, B = 64: the sidecar's ``score_encoded`` (sidecar.py:89-107, the
+      batched torch path its callers use) then ``torch.topk``, against one layer of ours
+      (score + top-k), events, best of a few repetitions."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "temporal_dsa").is_dir():
+        return {"unavailable": "no offline install of the reference under baseline/_ref"}
+    sys.path.insert(0, str(ref_dir))
+    try:
+        from temporal_dsa.progressive_kernel import full_scores_triton
+        from temporal_dsa.sidecar import LightningIndexerSidecar
+    except Exception as exc:  # noqa: BLE001 -- reported, not fatal
+        return {"unavailable": f"import failed: {type(exc).__name__}: {exc}"}
+    finally:
+        sys.path.remove(str(ref_dir))
+    from dsa_b200.indexer import ScoreTopkPlan
+
+    k = wl.k
+    flush = torch.empty(256 << 20, device=device, dtype=torch.uint8)
+
+    def eager_us(fn, n):
+        times = []
+        for _ in range(n):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize(device)
+            times.append(a.elapsed_time(b) * 1e3)
+        times.sort()
+        return {"us_median": times[len(times) // 2], "us_p5": times[int(0.05 * len(times))],
+                "us_p95": times[min(len(times) - 1, int(0.95 * len(times)))]}
+
+    def graph_us(fn, n):
+        fn()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=torch.cuda.Stream(device)):
+            fn()
+        res = eager_us(graph.replay, n)
+        del graph
+        return res
+
+    def guarded(fn):
+        try:
+            return fn()
+        except Exception as exc:  # noqa: BLE001 -- reported in the line, not fatal
+            return {"unavailable": f"{type(exc).__name__}: {exc}"}
+
+    out = {"source": "baseline/_ref (the reference installed unmodified, offline)"}
+    q1, w1, k1 = proj.q[0].contiguous(), proj.w[0].contiguous(), wl.keys[0][0].contiguous()
+    ref_path = lambda: torch.topk(full_scores_triton(q1, w1, k1), k, sorted=False)  # noqa: E731
+    plan = ScoreTopkPlan(proj.q[:1], proj.w[:1], wl.keys[0][:1], k, sorted=False)
+
+    def overlap():
+        for _ in range(5):  # Triton's JIT compile, then warm
+            ref_path()
+        plan.run()
+        torch.cuda.synchronize(device)
+        ref_idx = ref_path()[1].to(torch.int64)
+        ours = plan.run()[0][0].to(torch.int64)
+        return int(torch.isin(ref_idx, ours).sum())
+
+    b1 = {"top_k_overlap": guarded(overlap), "k": k}
+    b1["reference_triton_topk_eager"] = guarded(lambda: eager_us(ref_path, reps))
+    b1["ours_eager"] = guarded(lambda: eager_us(plan.run, reps))
+    b1["reference_triton_topk_graph"] = guarded(lambda: graph_us(ref_path, reps))
+    b1["ours_graph"] = guarded(lambda: graph_us(plan.run, reps))
+    b1["method"] = ("L2 flushed (256 MB write) before each repetition, events around the "
+                    "path; eager = one launch sequence per repetition as the reference's "
+                    "benchmark does, graph = one CUDA graph replay; top_k_overlap = keys "
+                    "in both top-k sets (scores differ by float rounding, so near-ties at "
+                    "the k-th key may differ)")
+    out["b1_l32k"] = b1
+    try:
+        sidecar = LightningIndexerSidecar().to(device)
+        qb = proj.q.unsqueeze(1)                    # [64, 1, 64, 128] bf16
+        wb = proj.w.unsqueeze(1)                    # [64, 1, 64] f32
+        keys = wl.keys[0]
+        ref_layer = lambda: torch.topk(  # noqa: E731
+            sidecar.score_encoded(qb, wb, keys)[:, 0], k, dim=-1, sorted=False)
+        plan = ScoreTopkPlan(proj.q, proj.w, keys, k, sorted=False)
+
+        def best_ms(fn, n=5):
+            fn()
+            torch.cuda.synchronize(device)
+            best = float("inf")
+            for _ in range(n):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                torch.cuda.synchronize(device)
+                best = min(best, a.elapsed_time(b))
+            return best
+
+        ref_ms, our_ms = best_ms(ref_layer), best_ms(plan.run)
+        nkeys = wl.batch * wl.length
+        out["cfg4_layer"] = {
+            "reference_score_encoded_topk_ms": ref_ms,
+            "reference_keys_per_s": nkeys / (ref_ms * 1e-3),
+            "ours_ms": our_ms,
+            "ours_keys_per_s": nkeys / (our_ms * 1e-3),
+            "batch": wl.batch, "seq_len": wl.length, "k": k,
+            "method": "one layer, inputs resident, events, best of 5",
+        }
+        del sidecar
+    except Exception as exc:  # noqa: BLE001
+        out["cfg4_layer"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    del flush
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_cfg3(args, device: torch.device) -> dict:
     """one sequence, L = 16384 growing by one key per step, AR(1) queries
     (rho 0.95), fixed w, bf16: the exact certified progressive top-2048 at block sizes
@@ -916,6 +1044,8 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU code (baseline/_ref)")
     ap.add_argument("--workload", choices=["cfg4", "cfg3", "cfg5"], default="cfg4",
                     help="cfg4 (default): the BASELINE metric's workload; cfg3: exact "
                          "progressive trace; cfg5: L-sharded top-k")
