@@ -594,6 +594,87 @@ def single_sequence_latency(wl: Config4, proj, device: torch.device, reps: int =
 
 
 # ----------------------------------------------------------------------------- cfg3 / cfg5
+def guarded(fn):
+    """fn()'s result, or {"unavailable": why} when it raises (a comparator measurement that
+    cannot run is reported in the line, not fatal)."""
+    try:
+        return fn()
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+
+
+def progressive_pair(q1, w1, k1, k: int, eager_us, graph_us, reps: int) -> dict:
+    """The reference's block-pruned Triton variants against ours, at its published primary
+    configuration (scripts/benchmark_progressive_dsa.py:31-32, :172-195): L = 32768,
+    blocks of 64, a random 59.4 % of blocks direct, the threshold promoting 10 % of the
+    cold blocks, 8 probe heads by |w|, then top-2048.  Each side runs its own public API and
+    its own top-k on the same inputs."""
+    from temporal_dsa import progressive_kernel as ref
+
+    from dsa_b200 import progressive_kernel as ours
+    from dsa_b200.indexer import topk as our_topk
+
+    dev, bs = k1.device, 64
+    nb = (k1.shape[0] + bs - 1) // bs
+    sel, rem = ref.split_head_ids(ref.dynamic_head_ids(w1).cpu())
+    sel, rem = sel.to(dev), rem.to(dev)
+    order = torch.randperm(nb, generator=torch.Generator().manual_seed(1582))
+    direct = torch.zeros(nb, dtype=torch.bool)
+    direct[order[:round(0.594227 * nb)]] = True
+    direct = direct.to(dev)
+    cold = ~direct
+    _, maxima = ref.h8_block_max_triton(q1, w1, k1, sel, cold, block_size=bs)
+    vals = maxima[cold]
+    rank = max(1, vals.numel() - max(1, round(0.10 * vals.numel())) + 1)
+    thr = torch.kthvalue(vals, rank).values.reshape(1).float()
+
+    def ref_fused():
+        r = ref.progressive_scores_triton(q1, w1, k1, sel, direct, thr, block_size=bs,
+                                          remaining_heads=rem)
+        return torch.topk(r.scores, k, sorted=False).indices, r
+
+    def our_fused():
+        r = ours.progressive_scores_triton(q1, w1, k1, sel, direct, thr, block_size=bs,
+                                           remaining_heads=rem)
+        return our_topk(r.scores, k, sorted=False)[0], r
+
+    def ref_two():
+        r = ref.two_pass_scores_triton(q1, w1, k1, sel, direct, thr, block_size=bs)
+        return torch.topk(r.scores, k, sorted=False).indices, r
+
+    def our_two():
+        r = ours.two_pass_scores_triton(q1, w1, k1, sel, direct, thr, block_size=bs)
+        return our_topk(r.scores, k, sorted=False)[0], r
+
+    for fn in (ref_fused, our_fused, ref_two, our_two):  # JIT compile and warm
+        fn()
+    torch.cuda.synchronize(dev)
+    (ri, rr), (oi, orr) = ref_fused(), our_fused()
+    return {
+        "threshold": float(thr.item()),
+        "direct_blocks": int(direct.sum().item()), "blocks": nb,
+        # the threshold is one cold block's probe maximum, so float rounding of the probe
+        # can flip that block
+        "accepted_blocks_differing": int((rr.accepted_blocks.to(torch.int8)
+                                          != orr.accepted_blocks.to(torch.int8)).sum()),
+        "accepted_blocks": int(orr.accepted_blocks.to(torch.int64).sum()),
+        "top_k_overlap": int(torch.isin(ri.to(torch.int64), oi.to(torch.int64)).sum()),
+        "reference_fused_topk": eager_us(ref_fused, reps),
+        "ours_fused_topk": eager_us(our_fused, reps),
+        "reference_two_pass_topk": eager_us(ref_two, reps),
+        "ours_two_pass_topk": eager_us(our_two, reps),
+        "graph": {name: guarded(lambda fn=fn: graph_us(fn, reps))
+                  for name, fn in (("reference_fused_topk", ref_fused),
+                                   ("ours_fused_topk", our_fused),
+                                   ("reference_two_pass_topk", ref_two),
+                                   ("ours_two_pass_topk", our_two))},
+        "method": "eager public-API calls (outputs allocated per call on both sides), L2 "
+                  "flushed before each repetition, events; fused = progressive_scores_triton "
+                  "(dense output) + top-k, two_pass = two_pass_scores_triton + top-k; "
+                  "graph = the same calls captured once and replayed (no host time)",
+    }
+
+
 def reference_gpu(wl: Config4, proj, device: torch.device, reps: int = 100) -> dict:
     """The reference's own GPU code on this B200, beside ours on the same inputs.  Imported
     unmodified from its offline install under baseline/_ref (absent: "unavailable").
@@ -648,12 +729,6 @@ def reference_gpu(wl: Config4, proj, device: torch.device, reps: int = 100) -> d
         del graph
         return res
 
-    def guarded(fn):
-        try:
-            return fn()
-        except Exception as exc:  # noqa: BLE001 -- reported in the line, not fatal
-            return {"unavailable": f"{type(exc).__name__}: {exc}"}
-
     out = {"source": "baseline/_ref (the reference installed unmodified, offline)"}
     q1, w1, k1 = proj.q[0].contiguous(), proj.w[0].contiguous(), wl.keys[0][0].contiguous()
     ref_path = lambda: torch.topk(full_scores_triton(q1, w1, k1), k, sorted=False)  # noqa: E731
@@ -679,6 +754,8 @@ def reference_gpu(wl: Config4, proj, device: torch.device, reps: int = 100) -> d
                     "in both top-k sets (scores differ by float rounding, so near-ties at "
                     "the k-th key may differ)")
     out["b1_l32k"] = b1
+    out["progressive_b1_l32k"] = guarded(
+        lambda: progressive_pair(q1, w1, k1, k, eager_us, graph_us, reps))
     try:
         sidecar = LightningIndexerSidecar().to(device)
         qb = proj.q.unsqueeze(1)                    # [64, 1, 64, 128] bf16
