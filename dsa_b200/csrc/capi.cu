@@ -258,9 +258,16 @@ int tdsa_score_dense(const void* queries, int64_t q_batch_stride, const float* w
                                s_batch_stride, st, status);
 }
 
+// Bytes of the key histograms that let a few unsorted rows of one segment take the cluster
+// top-k (several SMs per row) instead of one CTA per row segment; 0 when it does not apply.
+static size_t topk_row_hist_bytes(int batch, int length) {
+  return topk_cluster_rows(batch, length) > 1 ? static_cast<size_t>(batch) * kKeyHistBins * 4
+                                              : 0;
+}
+
 size_t tdsa_topk_workspace_bytes(int batch, int length, int k) {
   if (batch < 1 || length < 1 || k < 1 || k > length) return 0;
-  return topk_workspace_bytes(batch, length, k);
+  return std::max(topk_workspace_bytes(batch, length, k), topk_row_hist_bytes(batch, length));
 }
 
 int tdsa_topk(const float* scores, int64_t s_batch_stride, int batch, int length, int k,
@@ -274,6 +281,18 @@ int tdsa_topk(const float* scores, int64_t s_batch_stride, int batch, int length
   int rc = check_topk_out(out_indices, index_bytes, idx_batch_stride, out_values,
                           val_batch_stride, batch, k);
   if (rc) return rc;
+  const size_t hist_bytes = topk_row_hist_bytes(batch, length);
+  if (!sorted && hist_bytes && workspace && workspace_bytes >= hist_bytes &&
+      (reinterpret_cast<uintptr_t>(workspace) & 15u) == 0 && topk_check(length, k, 0) == 0) {
+    // few unsorted rows: histogram each row over several CTAs, then the cluster top-k
+    uint32_t* hist = static_cast<uint32_t*>(workspace);
+    rc = launch_row_hist_parts(scores, batch > 1 ? s_batch_stride : length, batch, length, hist,
+                               static_cast<cudaStream_t>(stream));
+    if (rc) return rc;
+    return launch_topk(scores, s_batch_stride, nullptr, 0, batch, length, k, 0, out_indices,
+                       index_bytes, idx_batch_stride, out_values, val_batch_stride, nullptr, 0,
+                       static_cast<cudaStream_t>(stream), nullptr, hist);
+  }
   return launch_topk(scores, s_batch_stride, nullptr, 0, batch, length, k, sorted ? 1 : 0,
                      out_indices, index_bytes, idx_batch_stride, out_values, val_batch_stride,
                      workspace, workspace_bytes, static_cast<cudaStream_t>(stream));

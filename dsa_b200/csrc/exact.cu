@@ -483,6 +483,19 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace
 
+int launch_row_hist_parts(const float* scores, int64_t l_stride, int batch, int length,
+                          uint32_t* hist, cudaStream_t stream) {
+  const int parts = std::max(1, std::min({16, 148 / batch, (length + 2047) / 2048}));
+  TDSA_CUDA_CHECK(cudaMemsetAsync(hist, 0, static_cast<size_t>(batch) * kKeyHistBins * 4,
+                                  stream));
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(row_hist_part_kernel),
+                                      kHistCopyBytes));
+  TDSA_CUDA_CHECK(launch_pdl(row_hist_part_kernel, dim3(parts, batch), dim3(kThreads),
+                             kHistCopyBytes, stream, scores, l_stride, length, hist));
+  TDSA_CUDA_CHECK(cudaGetLastError());
+  return TDSA_OK;
+}
+
 ExactLayout exact_layout(int batch, int max_length, int k, int block_size) {
   ExactLayout L;
   L.nb_stride = (max_length + block_size - 1) / block_size;

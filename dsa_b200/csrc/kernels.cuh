@@ -115,6 +115,12 @@ int launch_exchange_topk(const PeerGather& g, int sorted, void* out_idx, int idx
                          cudaStream_t stream);
 
 size_t topk_workspace_bytes(int batch, int length, int k);
+// CTAs per row the cluster top-k would use for rows of one histogram segment (1: none).
+int topk_cluster_rows(int batch, int length);
+// Key histograms [batch][4096] of score rows (<= 32768 keys), each row split over up to 16
+// CTAs; hist is zeroed first.
+int launch_row_hist_parts(const float* scores, int64_t l_stride, int batch, int length,
+                          uint32_t* hist, cudaStream_t stream);
 int topk_levels(int batch, int length, int k, int hist);
 int topk_check(int length, int k, int sorted);
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,

@@ -1019,6 +1019,10 @@ Plan make_plan(int batch, int length, int k, bool hist = false) {
 
 }  // namespace
 
+int topk_cluster_rows(int batch, int length) {
+  return length <= kTopkSegment ? cluster_size(batch, length) : 1;
+}
+
 size_t topk_workspace_bytes(int batch, int length, int k) {
   const Plan p = make_plan(batch, length, k);
   const Plan ph = make_plan(batch, length, k, true);
