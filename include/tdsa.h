@@ -220,7 +220,11 @@ int tdsa_score_dense(const void* queries, int64_t q_batch_stride, const float* w
                      int64_t k_row_stride, int dtype, int batch, int length, float* scores,
                      int64_t s_batch_stride, void* stream);
 
-/* Bytes of device workspace tdsa_topk needs for these sizes (0 if none). */
+/* Bytes of device workspace tdsa_topk needs for these sizes (0 if none).  For a batch of
+ * rows of at most 32768 keys too small to fill the GPU one CTA per row, it also covers the
+ * rows' key histograms: given at least this much (16-byte aligned), unsorted calls spread
+ * each row over several SMs (a split histogram pass, then the cluster selection); with
+ * less, they take the one-CTA-per-segment levels. */
 size_t tdsa_topk_workspace_bytes(int batch, int length, int k);
 
 /*
