@@ -27,6 +27,7 @@ import sys
 import threading
 import time
 from pathlib import Path
+from types import SimpleNamespace
 
 import numpy as np
 import torch
@@ -37,6 +38,21 @@ sys.path.insert(0, str(ROOT))
 METRIC = ("indexer scored keys/sec + per-step score+top-K latency at L=32K, %HBM peak, "
           "1/2/4/8 B200")
 UNIT = "keys/s"
+DATA = ("synthetic: seeded N(0,1) hidden states and random-init sidecar weights "
+        "(N(0,1/2048)); key caches built by W_k + LayerNorm + RoPE")
+
+
+def config4_dict(layers: int, batch: int, length: int, k: int, world: int) -> dict:
+    """The `config` of the config-4 line (both arms print the same one)."""
+    return {
+        "workload": "BASELINE config 4: 8 layers x (project, dense score, top-2048) per "
+                    "decode step",
+        "layers": layers, "batch_per_gpu": batch, "global_batch": batch * world,
+        "seq_len": length, "k": k, "heads": 64, "head_dim": 128,
+        "topk_sorted": False, "parallelism": f"batch-sharded dp{world}",
+        "l2": f"no flush: {layers * batch * length * 256 / 1e9:.1f} GB of keys per step per "
+              "GPU >> 126 MB L2",
+    }
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -133,38 +149,80 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- workload
+def _generator(device: torch.device, *parts: int) -> torch.Generator:
+    """A generator seeded from `parts`, so that any one layer or cache row of the workload
+    can be drawn on its own (the reference arm draws a sample of it)."""
+    seed = 0
+    for p in parts:
+        seed = (seed * 1_000_003 + int(p)) % (1 << 62)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def synth_keys(hidden: torch.Tensor, wk: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+    """Key rows of the sidecar's key encoder (RoPE(LayerNorm(hidden @ W_k^T)), unit LayerNorm
+    affine, eps 1e-6, RoPE on the first 64 dims, theta 1e4), written with plain torch ops.
+    Input synthesis only: both arms of the bench build their caches with it."""
+    k = torch.nn.functional.layer_norm(torch.matmul(hidden, wk.t()), (128,), eps=1e-6)
+    half = 32
+    inv = 10000.0 ** (-torch.arange(half, device=k.device, dtype=torch.float32) / half)
+    ang = positions.to(torch.float32).unsqueeze(-1) * inv
+    cos, sin = torch.cos(ang).to(k.dtype), torch.sin(ang).to(k.dtype)
+    a, b = k[..., :half], k[..., half:64]
+    return torch.cat((a * cos - b * sin, b * cos + a * sin, k[..., 64:]), dim=-1)
+
+
+class LayerWeights:
+    """One layer's random-init sidecar weights (N(0, 1/hidden), as the reference's
+    reset_parameters draws them): W_q [8192, hidden] and W_k [128, hidden] in bf16, the head
+    weight projection W_w [64, hidden] in float32."""
+
+    def __init__(self, device: torch.device, seed: int, layer: int, hidden: int):
+        g = _generator(device, seed, 1, layer)
+        std = hidden ** -0.5
+        self.wq = (torch.randn(64 * 128, hidden, generator=g, device=device) * std).to(
+            torch.bfloat16)
+        self.ww = torch.randn(64, hidden, generator=g, device=device) * std
+        self.wk = (torch.randn(128, hidden, generator=g, device=device) * std).to(torch.bfloat16)
+
+
+def cache_row(device: torch.device, seed: int, layer: int, row: int, wk: torch.Tensor,
+              length: int, hidden: int) -> torch.Tensor:
+    """Key cache of sequence `row` of `layer`: W_k over seeded N(0,1) hidden states."""
+    g = _generator(device, seed, 2, layer, row)
+    h = torch.randn(length, hidden, generator=g, device=device, dtype=torch.bfloat16)
+    return synth_keys(h, wk, torch.arange(length, device=device))
+
+
+def decode_hidden(device: torch.device, seed: int, layers: int, batch: int,
+                  hidden: int) -> torch.Tensor:
+    """The decode step's hidden states x [layers, batch, hidden] (bf16, N(0,1))."""
+    g = _generator(device, seed, 3)
+    return torch.randn(layers, batch, hidden, generator=g, device=device, dtype=torch.bfloat16)
+
+
 class Config4:
     """8 layers, B=64 per GPU, L=32768 bf16 keys, top-2048."""
 
     def __init__(self, device: torch.device, seed: int, layers: int = 8, batch: int = 64,
                  length: int = 32768, k: int = 2048, hidden: int = 2048):
-        from dsa_b200.sidecar import encode_keys
-
         self.device, self.layers, self.batch = device, layers, batch
-        self.length, self.k, self.hidden = length, k, hidden
-        g = torch.Generator(device=device)
-        g.manual_seed(seed)
-        std = hidden ** -0.5
-        bf = torch.bfloat16
-        self.wq = [(torch.randn(64 * 128, hidden, generator=g, device=device) * std).to(bf)
-                   for _ in range(layers)]
-        self.ww = [torch.randn(64, hidden, generator=g, device=device) * std
-                   for _ in range(layers)]
-        wk = [(torch.randn(128, hidden, generator=g, device=device) * std).to(bf)
-              for _ in range(layers)]
-        ln_w = torch.ones(128, device=device)
-        ln_b = torch.zeros(128, device=device)
-        pos = torch.arange(length, device=device)
+        self.length, self.k, self.hidden, self.seed = length, k, hidden, seed
+        weights = [LayerWeights(device, seed, layer, hidden) for layer in range(layers)]
+        self.wq = [lw.wq for lw in weights]
+        self.ww = [lw.ww for lw in weights]
         self.keys = []
         for layer in range(layers):
-            cache = torch.empty(batch, length, 128, device=device, dtype=bf)
+            cache = torch.empty(batch, length, 128, device=device, dtype=torch.bfloat16)
             for b in range(batch):
-                h = torch.randn(length, hidden, generator=g, device=device, dtype=bf)
-                cache[b] = encode_keys(h, wk[layer], ln_w, ln_b, pos)
+                cache[b] = cache_row(device, seed, layer, b, weights[layer].wk, length, hidden)
             self.keys.append(cache)
-        self.wk0, self.ln_w, self.ln_b = wk[0], ln_w, ln_b
-        del wk
-        self.x = torch.randn(layers, batch, hidden, generator=g, device=device, dtype=bf)
+        self.wk0 = weights[0].wk
+        self.ln_w = torch.ones(128, device=device)
+        self.ln_b = torch.zeros(128, device=device)
+        del weights
+        self.x = decode_hidden(device, seed, layers, batch, hidden)
         self.qpos = torch.full((batch,), length - 1, device=device, dtype=torch.long)
         self.scores = torch.empty(batch, length, device=device, dtype=torch.float32)
         torch.cuda.synchronize(device)
@@ -319,6 +377,9 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     assert torch.equal(out_host[wl.layers - 1], plans[wl.layers - 1].indices.cpu())
     del graph
     barrier()
+    # config 5's L-sharded step (score, local top-k, the exchange of the ranks' candidates:
+    # the path's one collective) on these N GPUs, as an extra key of this line
+    cfg5 = None if args.no_extras else run_cfg5(args, rank, world, device)
 
     if rank != 0:
         return None
@@ -341,17 +402,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic: seeded N(0,1) hidden states and random-init sidecar weights "
-                "(N(0,1/2048)); key caches built by W_k + LayerNorm + RoPE",
-        "config": {
-            "workload": "BASELINE config 4: 8 layers x (project, dense score, top-2048) per "
-                        "decode step",
-            "layers": wl.layers, "batch_per_gpu": wl.batch, "global_batch": wl.batch * world,
-            "seq_len": wl.length, "k": wl.k, "heads": 64, "head_dim": 128,
-            "topk_sorted": False, "parallelism": f"batch-sharded dp{world}",
-            "l2": f"no flush: {wl.layers * wl.batch * wl.length * 256 / 1e9:.1f} GB of keys "
-                  "per step per GPU >> 126 MB L2",
-        },
+        "data": DATA,
+        "config": config4_dict(wl.layers, wl.batch, wl.length, wl.k, world),
         "roofline": {
             "kernel": "score_dense_tc_kernel<bf16>",
             "bound": "hbm",
@@ -390,8 +442,12 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
                                                   cpu=not args.no_cpu_baseline)
         if not args.no_reference_gpu:
             line["reference_gpu"] = reference_gpu(wl, proj[0], device)
+        if not args.no_extras:
+            line["cfg3"] = run_cfg3(device, 64)
+    if cfg5 is not None:
+        line["cfg5"] = cfg5
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(wl, seconds=args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(wl, plans[0].indices, seconds=args.cpu_seconds)
     return line
 
 
@@ -442,8 +498,6 @@ def policy_step_latency(wl: Config4, device: torch.device, steps: int = 8,
            "blocks": int(st[0]["BLOCKS"]),
            "api": "dsa_b200.approx.PolicyPlan (C ABI tdsa_policy_step)"}
     if cpu:
-        from types import SimpleNamespace
-
         from oracle import approx as oa
 
         r0 = rows[3][0].cpu().numpy()
@@ -797,22 +851,22 @@ def reference_gpu(wl: Config4, proj, device: torch.device, reps: int = 100) -> d
     return out
 
 
-def run_cfg3(args, device: torch.device) -> dict:
+def run_cfg3(device: torch.device, steps: int) -> dict:
     """one sequence, L = 16384 growing by one key per step, AR(1) queries
     (rho 0.95), fixed w, bf16: the exact certified progressive top-2048 at block sizes
-    16/32/64/128, and dense score + top-2048, each run for all steps back to back between two
-    CUDA events (per-step average; at B=1 both are bound by host launch time, not by the
-    ~10 us of GPU work).  The exact path runs in its decode-loop form (ExactProgressivePlan:
-    fixed buffers, the query rewritten in place each step).  The exact top-k is compared with
-    dense at every step.  Bytes read per step count the keys actually scored (256 B each) and
-    8 B of block metadata per visited block, the seed gathers included.  A second,
-    block-structured trace (10% of 64-key blocks at norm x3, the rest x0.05; slowly drifting
-    queries, rho 0.999; positive weights) is a case where the certified bound prunes blocks
-    unread."""
-    from dsa_b200 import score_dense, topk
+    16/32/64/128, against dense score + top-2048.  Both run in their decode-loop forms on
+    fixed buffers (ExactProgressivePlan: one C call per step; dense: one ScoreTopkPlan per
+    step's length, built before the timing), all steps back to back between two CUDA events
+    (per-step average, host launch time included, as a decode loop issues them).  The exact
+    top-k is compared with dense at every step.  Bytes read per step count the keys actually
+    scored (256 B each) and 8 B of block metadata per visited block, the seed gathers
+    included.  A second, block-structured trace (10% of 64-key blocks at norm x3, the rest
+    x0.05; slowly drifting queries, rho 0.999; positive weights) is a case where the
+    certified bound prunes blocks unread."""
+    from dsa_b200.indexer import ScoreTopkPlan
     from dsa_b200.progressive_exact import ExactProgressivePlan
 
-    steps, l0, k, data_block = max(args.steps, 8), 16384, 2048, 64
+    l0, k, data_block = 16384, 2048, 64
     res = {}
     for trace in ("iid", "structured"):
         g = torch.Generator().manual_seed(0)
@@ -835,19 +889,24 @@ def run_cfg3(args, device: torch.device) -> dict:
             qs.append(q.to(torch.bfloat16).to(device).unsqueeze(0))
         w1 = w.unsqueeze(0).contiguous()
         e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        topk(score_dense(qs[0], w1, keys[:, :l0 + 1]), k, sorted=False)  # untimed first use
+        qbuf = qs[0].clone()
+        dense = [ScoreTopkPlan(qbuf, w1, keys[:, :l0 + t + 1], k, sorted=False)
+                 for t in range(steps)]
+        dense[0].run()  # untimed first use
         torch.cuda.synchronize(device)
+        want = []
         e[2].record()
-        want = [topk(score_dense(qs[t], w1, keys[:, :l0 + t + 1]), k, sorted=False)[0]
-                for t in range(steps)]
+        for t in range(steps):
+            qbuf.copy_(qs[t])
+            want.append(dense[t].run()[0].clone())
         e[3].record()
         torch.cuda.synchronize(device)
         dense_us = e[2].elapsed_time(e[3]) * 1e3 / steps
+        del dense
         sweep = {}
         for bs in (16, 32, 64, 128):
             # the decode-loop form: fixed query / weight / cache buffers, the query rewritten
             # in place every step (as a projection kernel would), one C call per step
-            qbuf = qs[0].clone()
             ex = ExactProgressivePlan(qbuf, w1, keys, k, block_size=bs, sorted=False)
             ex.init(l0)
             torch.cuda.synchronize(device)
@@ -879,6 +938,9 @@ def run_cfg3(args, device: torch.device) -> dict:
         "config": {"workload": "BASELINE config 3: B=1, L=16384+t, AR(1) rho 0.95; value at "
                                "block 64, all four block sizes under traces.*.block_sizes",
                    "k": k, "block_size": 64},
+        "exact_equals_dense_every_step": all(v["exact_equals_dense_every_step"]
+                                             for r in res.values()
+                                             for v in r["block_sizes"].values()),
         "traces": res,
     }
 
@@ -897,47 +959,61 @@ def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
     g.manual_seed(5)
     q = (torch.randn(b, 64, 128, generator=g, device=device) / math.sqrt(128)).to(torch.bfloat16)
     w = torch.randn(b, 64, generator=g, device=device) / 8
-    shard = torch.randn(b, stop - start, 128, generator=g, device=device).to(torch.bfloat16)
+    # the whole cache is drawn on every rank and sliced, so every N shards the same keys
+    shard = torch.randn(b, length, 128, generator=g, device=device).to(torch.bfloat16)
+    shard = shard[:, start:stop].contiguous()
+    torch.cuda.empty_cache()
+
     def timed(exchange: str):
         sharded = LShardedPlan(q, w, shard, k, start, sorted=False, exchange=exchange)
         for _ in range(args.warmup):
             sharded.run()
         torch.cuda.synchronize(device)
-        # One step (score, top-k levels, exchange, merge) as a CUDA graph, so the step is
-        # timed without host launch gaps; every rank captures the same sequence.
-        graph = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream(device)
-        cap.wait_stream(torch.cuda.current_stream(device))
-        with torch.cuda.graph(graph, stream=cap):
-            out = sharded.run()
-        torch.cuda.synchronize(device)
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(device)
-        graph.replay()
-        torch.cuda.synchronize(device)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
+
+        def graph_ms(fn) -> float:
+            # one step as a CUDA graph, so the step is timed without host launch gaps;
+            # every rank captures the same sequence
+            graph = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream(device)
+            cap.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.graph(graph, stream=cap):
+                fn()
+            torch.cuda.synchronize(device)
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize(device)
             graph.replay()
-        e1.record()
-        torch.cuda.synchronize(device)
-        ms = e0.elapsed_time(e1) / args.steps
-        if world > 1:
-            torch.distributed.barrier()
-        del graph  # (may hold NCCL work: released before the process group is destroyed)
-        if world > 1:
-            t = torch.tensor([ms], device=device, dtype=torch.float64)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
-        result = (out[0].clone(), out[1].clone())
+            torch.cuda.synchronize(device)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            if world > 1:
+                torch.distributed.barrier()
+            del graph  # (may hold NCCL work: released before the process group is destroyed)
+            return max_over(e0.elapsed_time(e1) / args.steps)
+
+        ms = graph_ms(sharded.run)
+        result = (sharded.merge.indices.clone(), sharded.merge.values.clone())
+        # this rank's part alone (score + local top-k, no exchange): the rest of the step
+        # is the exchange (waiting for the slowest rank, the pull and the merge)
+        local_ms = graph_ms(sharded.plan.run)
         sharded.close()
-        return ms, result
+        return ms, local_ms, result
+
+    def max_over(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
 
     # the product path exchanges over peer memory; the NCCL all-gather is timed beside it
-    ms, (pi, pv) = timed("peer")
-    ms_ag, (ai, av) = timed("allgather")
+    ms, local_ms, (pi, pv) = timed("peer")
+    ms_ag, _, (ai, av) = timed("allgather")
     agree = bool(torch.equal(pi, ai) and torch.equal(pv, av))
     prog = cfg5_progressive(args, rank, world, device, b, start, stop, k, w)
     if rank != 0:
@@ -955,6 +1031,11 @@ def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:
                    "timing": "CUDA graph of one step replayed back to back, events, max over "
                              "ranks"},
         "exchange": {"kind": "peer memory, one tdsa_exchange_topk launch per step",
+                     "local_ms_per_step": local_ms,
+                     "exchange_ms_per_step": ms - local_ms,
+                     "exchange_share": (ms - local_ms) / ms,
+                     "local_part": "score + top-k of this rank's keys (ScoreTopkPlan), "
+                                   "max over ranks",
                      "allgather_ms_per_step": ms_ag,
                      "allgather_value": b * length / (ms_ag * 1e-3),
                      "results_agree": agree},
@@ -1014,18 +1095,103 @@ def cfg5_progressive(args, rank, world, device, b, start, stop, k, w) -> dict:
 
 
 # ----------------------------------------------------------------------------- CPU arm
-def cpu_sample(wl_like, nseq: int):
-    """Host copies of a few config-4 sequences of layer 0 for the CPU restatement."""
-    keys = wl_like.keys[0][:nseq].float().cpu().numpy()
-    x = wl_like.x[0][:nseq].float().cpu().numpy()
-    wq = wl_like.wq[0].float().cpu().numpy()
-    ww = wl_like.ww[0].cpu().numpy()
-    return keys, x, wq, ww
+REF_DIR = ROOT / "baseline" / "_ref"
 
 
-def cpu_step(keys, x, wq, ww, k, length):
-    """The reference path on the host: project (sidecar.py:78-87), score
-    (progressive_kernel.py:45-55 / sidecar.py:89-107), top-k (metrics.py:9-22)."""
+def host_threads() -> int:
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def import_reference():
+    """The reference package (temporal_dsa) installed unmodified under baseline/_ref, or
+    None when it is absent or does not import."""
+    if not (REF_DIR / "temporal_dsa").is_dir():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    try:
+        from temporal_dsa import progressive_kernel, sidecar
+    except Exception:  # noqa: BLE001 -- the port stands in, and the line says so
+        return None
+    return SimpleNamespace(progressive_kernel=progressive_kernel, sidecar=sidecar)
+
+
+class HostSample:
+    """Host copies of the first `rows` sequences of config 4's layer 0: W_q (bf16), W_w
+    (float32), the decode hidden states (bf16) and the bf16 key caches.  The same seeded
+    draws as the GPU arm's workload (`Config4`), so both arms score the same keys."""
+
+    def __init__(self, wq, ww, x, keys, k: int):
+        self.wq, self.ww, self.x, self.keys, self.k = wq, ww, x, keys, k
+        self.rows, self.length = keys.shape[0], keys.shape[1]
+        self.pos = torch.full((self.rows,), self.length - 1, dtype=torch.long)
+
+    @classmethod
+    def from_workload(cls, wl: Config4, rows: int) -> "HostSample":
+        return cls(wl.wq[0].cpu(), wl.ww[0].cpu(), wl.x[0, :rows].cpu(),
+                   wl.keys[0][:rows].cpu(), wl.k)
+
+    @classmethod
+    def generate(cls, rows: int, length: int, k: int, seed: int = 1234, layers: int = 8,
+                 batch: int = 64, hidden: int = 2048) -> "HostSample":
+        """Draws only layer 0 and `rows` caches (on the GPU when there is one: the draws
+        then equal the GPU arm's exactly)."""
+        device = torch.device("cuda" if torch.cuda.is_available() else "cpu")
+        lw = LayerWeights(device, seed, 0, hidden)
+        keys = torch.stack([cache_row(device, seed, 0, r, lw.wk, length, hidden)
+                            for r in range(rows)])
+        x = decode_hidden(device, seed, layers, batch, hidden)[0, :rows]
+        return cls(lw.wq.cpu(), lw.ww.cpu(), x.cpu(), keys.cpu(), k)
+
+
+class ReferenceCPU:
+    """The reference's own torch path on the host cores, imported unmodified: the
+    sidecar's decode-step query projection ``LightningIndexerSidecar.encode_queries``
+    (sidecar.py:78-87, W_q in bf16 as its callers run it, W_w in float32), then per sequence
+    ``torch_full_scores`` (progressive_kernel.py:45-55: the bf16 cache upcast to float32)
+    and ``torch.topk(scores, k, sorted=False)`` (scripts/benchmark_progressive_dsa.py:
+    117-124).  Per sequence, ``torch_full_scores`` runs 2x faster on the host than the
+    batched ``score_encoded`` einsum (sidecar.py:89-107), so it is the one timed."""
+
+    def __init__(self, ref, sample: HostSample):
+        sc = ref.sidecar.LightningIndexerSidecar()
+        sc.wq.to(torch.bfloat16)
+        with torch.no_grad():
+            sc.wq.weight.copy_(sample.wq)
+            sc.weights_proj.weight.copy_(sample.ww)
+        self.sidecar, self.sample = sc, sample
+        self.full_scores = ref.progressive_kernel.torch_full_scores
+
+    def run(self, rows: range) -> list[torch.Tensor]:
+        s = self.sample
+        out = []
+        with torch.no_grad():
+            sel = list(rows)
+            q, w = self.sidecar.encode_queries(s.x[sel].unsqueeze(1), s.pos[sel].unsqueeze(1))
+            for i, r in enumerate(sel):
+                scores = self.full_scores(q[i, 0], w[i, 0], s.keys[r])
+                out.append(torch.topk(scores, s.k, sorted=False).indices)
+        return out
+
+
+def cpu_step_port(keys, x, wq, ww, k, length):
+    """The oracle port of the same path (numpy float32), used only when the reference
+    install is absent: project (sidecar.py:78-87), score (progressive_kernel.py:45-55),
+    top-k (metrics.py:9-22)."""
     import oracle
 
     half = 32
@@ -1038,74 +1204,103 @@ def cpu_step(keys, x, wq, ww, k, length):
         q[:, :64] = np.concatenate((r[:, :half] * cos - r[:, half:] * sin,
                                     r[:, half:] * cos + r[:, :half] * sin), axis=1)
         w = (x[s] @ ww.T) * (64 * 128) ** -0.5
-        scores = oracle.full_scores(q, w, keys[s])
-        oracle.stable_topk(scores, k)
+        oracle.stable_topk(oracle.full_scores(q, w, keys[s]), k)
 
 
-def cpu_baseline(wl, seconds: float = 10.0) -> dict:
-    nseq = 4
-    keys, x, wq, ww = cpu_sample(wl, nseq)
-    cpu_step(keys[:1], x[:1], wq, ww, wl.k, wl.length)  # warm
+class PortCPU:
+    """ReferenceCPU's stand-in over the oracle port (same sample, same step)."""
+
+    def __init__(self, sample: HostSample):
+        self.sample = sample
+        self.keys = sample.keys.float().numpy()
+        self.x = sample.x.float().numpy()
+        self.wq = sample.wq.float().numpy()
+        self.ww = sample.ww.numpy()
+
+    def run(self, rows: range):
+        sel = list(rows)
+        cpu_step_port(self.keys[sel], self.x[sel], self.wq, self.ww, self.sample.k,
+                      self.sample.length)
+        return None
+
+
+def cpu_runner(sample: HostSample):
+    """(runner, kind, description) for the host path: the reference's own code when its
+    install is present, else the oracle port."""
+    torch.set_num_threads(host_threads())
+    ref = import_reference()
+    if ref is not None:
+        return (ReferenceCPU(ref, sample), "reference",
+                "the reference's own torch code from baseline/_ref: encode_queries, "
+                "torch_full_scores, torch.topk(sorted=False)")
+    return (PortCPU(sample), "port",
+            "numpy float32 restatement (oracle/): the reference install is absent")
+
+
+def cpu_baseline(wl: Config4, ours_idx: torch.Tensor | None, seconds: float = 10.0) -> dict:
+    """The host path timed on this box's cores over sequences of layer 0 of the same
+    workload, for about `seconds`; with the reference's code, its top-k sets are compared
+    with the GPU arm's for the same sequences."""
+    rows = min(8, wl.batch)
+    sample = HostSample.from_workload(wl, rows)
+    runner, kind, what = cpu_runner(sample)
+    first = runner.run(range(rows))  # warm (and the sets compared below)
     done, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds:
-        cpu_step(keys, x, wq, ww, wl.k, wl.length)
-        done += nseq
+        runner.run(range(rows))
+        done += rows
     dt = time.perf_counter() - t0
-    return {"value": done * wl.length / dt, "unit": UNIT, "cores": os.cpu_count(),
-            "kind": "port",
-            "sample": f"{done} sequences of layer 0 (L={wl.length}, project + score + "
-                      f"top-{wl.k}) in {dt:.1f} s, numpy float32 (oracle/), "
-                      f"{os.cpu_count()} threads"}
+    out = {"value": done * wl.length / dt, "unit": UNIT, "cores": host_threads(), "kind": kind,
+           "cpu_model": cpu_model(),
+           "sample": f"{done} sequences of layer 0 (L={wl.length}, project + score + "
+                     f"top-{wl.k}) in {dt:.1f} s; {what}; torch threads {host_threads()}"}
+    if first is not None and ours_idx is not None:
+        ours = ours_idx[:rows].cpu().to(torch.int64)
+        out["top_k_agreement"] = {
+            "keys_in_both": int(sum(torch.isin(a.to(torch.int64), b).sum()
+                                    for a, b in zip(first, ours))),
+            "of": rows * wl.k,
+            "note": "the reference scores in float32 from the same bf16 inputs; keys whose "
+                    "scores tie the k-th within rounding may differ"}
+    return out
 
 
-class HostSample:
-    """Config-4-shaped inputs generated on the host (no GPU) for the reference arm."""
-
-    def __init__(self, nseq: int, length: int, k: int, seed: int = 1234):
-        rng = np.random.default_rng(seed)
-        std = 2048 ** -0.5
-        self.k, self.length = k, length
-        self.wq = (rng.standard_normal((8192, 2048), dtype=np.float32) * std)
-        self.ww = (rng.standard_normal((64, 2048), dtype=np.float32) * std)
-        self.x = rng.standard_normal((nseq, 2048), dtype=np.float32)
-        keys = rng.standard_normal((nseq, length, 128), dtype=np.float32)
-        keys -= keys.mean(axis=-1, keepdims=True)
-        keys /= keys.std(axis=-1, keepdims=True) + 1e-6  # LayerNorm-like keys
-        self.keys = keys
-
-
-def run_reference(args) -> dict:
-    nseq = 2
-    hs = HostSample(nseq, args.length, args.k)
+def run_reference(args, world: int) -> dict:
+    """`--impl reference`: the reference's own host path (ReferenceCPU) on all host cores,
+    each step one bounded sample of the config-4 workload (`args.ref_rows` sequences of layer
+    0, the same seeded draws as the GPU arm's)."""
+    rows = args.ref_rows
+    sample = HostSample.generate(rows, args.length, args.k)
+    runner, kind, what = cpu_runner(sample)
     for _ in range(args.warmup):
-        cpu_step(hs.keys, hs.x, hs.wq, hs.ww, hs.k, hs.length)
+        runner.run(range(rows))
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_step(hs.keys, hs.x, hs.wq, hs.ww, hs.k, hs.length)
+        runner.run(range(rows))
     dt = time.perf_counter() - t0
-    value = args.steps * nseq * hs.length / dt
-    sample = (f"each step = {nseq} config-4 sequences (L={hs.length}, project + score + "
-              f"top-{hs.k}) of one layer, numpy float32 restatement of the reference "
-              f"(oracle/), {os.cpu_count()} threads")
+    value = args.steps * rows * sample.length / dt
+    desc = (f"each step = {rows} config-4 sequences of layer 0 (L={sample.length}, project + "
+            f"score + top-{sample.k}); {what}; torch threads {host_threads()}")
+    cfg = config4_dict(8, args.batch, sample.length, sample.k, world)
     return {
         "impl": "reference",
         "metric": METRIC,
         "value": value,
         "unit": UNIT,
-        "n_gpus": args.gpus,
+        "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic, seeded (numpy), config-4 shapes",
-        "config": {"workload": "BASELINE config 4 sample on the host cores", "seq_len":
-                   hs.length, "k": hs.k, "sequences_per_step": nseq},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "dtype": "bf16",
+        "data": DATA,
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": host_threads(), "kind": kind,
+                         "cpu_model": cpu_model(), "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
     }
 
 
@@ -1120,9 +1315,13 @@ def main() -> None:
     ap.add_argument("--length", type=int, default=32768)
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-rows", type=int, default=8,
+                    help="--impl reference: config-4 sequences per step on the host")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU code (baseline/_ref)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config-3 and config-5 keys of the default line")
     ap.add_argument("--workload", choices=["cfg4", "cfg3", "cfg5"], default="cfg4",
                     help="cfg4 (default): the BASELINE metric's workload; cfg3: exact "
                          "progressive trace; cfg5: L-sharded top-k")
@@ -1133,7 +1332,7 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+            print(json.dumps(run_reference(args, world)), flush=True)
         return
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1151,7 +1350,7 @@ def main() -> None:
     if world > 1:
         torch.distributed.barrier()
     if args.workload == "cfg3":
-        line = run_cfg3(args, device) if rank == 0 else None
+        line = run_cfg3(device, max(args.steps, 8)) if rank == 0 else None
     elif args.workload == "cfg5":
         line = run_cfg5(args, rank, world, device)
     else:
