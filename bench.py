@@ -892,7 +892,9 @@ def run_cfg3(device: torch.device, steps: int) -> dict:
         qbuf = qs[0].clone()
         dense = [ScoreTopkPlan(qbuf, w1, keys[:, :l0 + t + 1], k, sorted=False)
                  for t in range(steps)]
-        dense[0].run()  # untimed first use
+        for t in range(steps):  # untimed pass: every plan's first use, clocks up
+            qbuf.copy_(qs[t])
+            dense[t].run()
         torch.cuda.synchronize(device)
         want = []
         e[2].record()
@@ -907,6 +909,15 @@ def run_cfg3(device: torch.device, steps: int) -> dict:
         for bs in (16, 32, 64, 128):
             # the decode-loop form: fixed query / weight / cache buffers, the query rewritten
             # in place every step (as a projection kernel would), one C call per step
+            # an untimed run of a few steps first (the same kernels at this block size)
+            qbuf.copy_(qs[0])
+            warm = ExactProgressivePlan(qbuf, w1, keys, k, block_size=bs, sorted=False)
+            warm.init(l0)
+            for t in range(min(steps, 8)):
+                qbuf.copy_(qs[t])
+                warm.step(l0 + t + 1)
+            del warm
+            qbuf.copy_(qs[0])
             ex = ExactProgressivePlan(qbuf, w1, keys, k, block_size=bs, sorted=False)
             ex.init(l0)
             torch.cuda.synchronize(device)
@@ -1272,8 +1283,13 @@ def run_reference(args, world: int) -> dict:
     rows = args.ref_rows
     sample = HostSample.generate(rows, args.length, args.k)
     runner, kind, what = cpu_runner(sample)
-    for _ in range(args.warmup):
+    # warm-up: the W steps, and at least 3 s (thread pools and the allocator reach their
+    # steady state)
+    t0 = time.perf_counter()
+    done = 0
+    while done < args.warmup or time.perf_counter() - t0 < 3.0:
         runner.run(range(rows))
+        done += 1
     t0 = time.perf_counter()
     for _ in range(args.steps):
         runner.run(range(rows))
@@ -1315,7 +1331,7 @@ def main() -> None:
     ap.add_argument("--length", type=int, default=32768)
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--ref-rows", type=int, default=8,
+    ap.add_argument("--ref-rows", type=int, default=16,
                     help="--impl reference: config-4 sequences per step on the host")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true",

@@ -102,6 +102,8 @@ SIGNATURES: dict[str, tuple] = {
                                 i64, vp, i64, vp]),
     "tdsa_masked_dense": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, i64, vp,
                                 i64, vp]),
+    "tdsa_two_pass": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp, vp,
+                            i64, vp, vp, i64, vp]),
     "tdsa_progressive_h8": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp,
                                   vp, vp, i64, vp, vp, i64, vp]),
     "tdsa_compact_blocks": (i32, [vp, i64, vp, i64, i32, i32, i32, vp, vp, i64, vp, vp]),

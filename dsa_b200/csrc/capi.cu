@@ -801,6 +801,47 @@ int tdsa_masked_dense(const void* queries, int64_t q_batch_stride, const float* 
                              static_cast<cudaStream_t>(stream));
 }
 
+int tdsa_two_pass(const void* queries, int64_t q_batch_stride, const float* weights,
+                  int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                  int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                  const int32_t* selected_heads, const int8_t* direct_blocks,
+                  const float* threshold, float* scores, int64_t s_batch_stride,
+                  int8_t* accepted, float* block_max, int64_t bm_batch_stride, void* stream) {
+  if (length < 1) return fail(TDSA_ERR_INVALID, "length must be >= 1");
+  BlockArgs a;
+  int rc = block_setup(queries, q_batch_stride, weights, w_batch_stride, keys, k_batch_stride,
+                       k_row_stride, dtype, batch, length, block_size, a);
+  if (rc) return rc;
+  if (!selected_heads || !direct_blocks || !threshold || !scores || !accepted || !block_max)
+    return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (batch > 1 && (s_batch_stride < length || bm_batch_stride < a.nblocks))
+    return fail(TDSA_ERR_INVALID, "row strides too small");
+  // 1. the 8-head probe maximum of every cold (non-direct) block; no partial scores kept
+  a.mask = direct_blocks;
+  a.mask_stride = bm_batch_stride;
+  a.mask_invert = 1;
+  a.selected = selected_heads;
+  a.block_max = block_max;
+  a.bm_stride = bm_batch_stride;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = launch_score_blocks(kModeH8, queries, q_batch_stride, keys, k_batch_stride, k_row_stride,
+                           dtype, batch, a, block_grid(a), st);
+  if (rc) return rc;
+  // 2. dense scores of the accepted blocks (direct, or probe max >= threshold), the
+  // acceptance written per block; rejected blocks are not read
+  BlockArgs m = a;
+  m.mask_invert = 0;
+  m.selected = nullptr;
+  m.block_max = nullptr;
+  m.accept_max = block_max;
+  m.threshold = threshold;
+  m.accepted = accepted;
+  m.out = scores;
+  m.out_stride = s_batch_stride;
+  return launch_score_blocks(kModeMasked, queries, q_batch_stride, keys, k_batch_stride,
+                             k_row_stride, dtype, batch, m, block_grid(m), st);
+}
+
 int tdsa_progressive_h8(const void* queries, int64_t q_batch_stride, const float* weights,
                         int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
                         int64_t k_row_stride, int dtype, int batch, int length, int block_size,

@@ -1,17 +1,23 @@
 // Exact (certified) progressive top-k: the host schedule and its small device kernels.
 //
-// One decode step per sequence (all sequences of the batch advance together):
-//   1. new-key norms: max ||k|| per block for keys appended since the last step;
-//   2. prepare: certified coefficient c = sum_h |w_t-w_p| ||q_p,h|| + |w_t| ||q_t,h-q_p,h||
-//      (reference certified.py:18-48, with one key vector shared by the heads) plus a
-//      rounding slack, per-block bound U_b + maxnorm_b * c (new-key blocks: +inf, as
-//      replay.py:263-266), scores reset to -inf, wave 1 = blocks holding a previous top-k
-//      key or new keys (hot first, replay.py:153-169);
-//   3. wave 1 scored on the tensor cores (exact block maxima as a by-product);
-//   4. tau = k-th largest wave-1 score (>= the seed threshold min(current[prev_topk]));
-//   5. wave 2 = the other blocks whose bound reaches tau; the rest are pruned unread;
-//   6. wave 2 scored; 7. top-k over the scored keys; 8. state update: U_b <- exact block max
-//      (scored) or bound (pruned), q/w kept for the next step, statistics accumulated.
+// One decode step per sequence (all sequences of the batch advance together), five
+// launches chained by programmatic dependent launch:
+//   1. prepare (one CTA per sequence): the previous step's state update (U_b <- exact block
+//      max of a scored block, its bound when pruned), the norms of the keys appended since
+//      (max ||k|| per block), the certified coefficient
+//      c = sum_h |w_t-w_p| ||q_p,h|| + |w_t| ||q_t,h-q_p,h|| (reference certified.py:18-48,
+//      one key vector shared by the heads) plus a rounding slack, q/w kept for the next
+//      step, per-block bounds U_b + maxnorm_b * c (blocks with new keys: +inf, as
+//      replay.py:263-266), and wave 1 = the blocks holding a previous top-k key or new keys
+//      (hot first, replay.py:153-169);
+//   2. wave 1 scored on the tensor cores; the epilogue adds every score to the row's key
+//      histogram and writes the exact block maxima;
+//   3. wave2 (one CTA per sequence): tau = the lower edge of the key bin holding the k-th
+//      largest wave-1 score (>= the seed threshold min(current[prev_topk])), wave 2 = the
+//      other blocks whose bound reaches tau; the rest are pruned unread, their keys set to
+//      -inf and counted in the histogram; statistics;
+//   4. wave 2 scored (histogram as in 2);
+//   5. top-k over the row from its histogram, the indices also kept as the next step's seeds.
 // Every pruned key has a score strictly below tau <= the k-th largest, so the top-k equals
 // dense scoring's; the scores are bit-identical to the dense kernel's (same MMA tile, same
 // epilogue summation order).
@@ -27,36 +33,43 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr double kGamma = 0x1p-12;  // relative rounding slack of a computed score
+constexpr int kFoldKeys = 1024;     // appends up to this many keys are normed in prepare
+constexpr uint32_t kNegInfBin = 0x007FFFFFu >> 20;  // histogram bin of the -inf key
 
-// Squared norm of each appended key, rounded up, folded into its block's max (float bits of
-// non-negative floats order like unsigned integers).  One warp per key.
+// Squared norm of key `key`, rounded up, folded into its block's max (float bits of
+// non-negative floats order like unsigned integers).  Called by one whole warp.
+__device__ __forceinline__ void fold_key_norm(const void* keys, int64_t base, int64_t k_rs,
+                                              int dtype, int key, int bs, uint32_t* maxsq_row) {
+  const int lane = threadIdx.x & 31;
+  // 4 dims per lane in one 8-byte load (rows are 16-byte aligned: TMA layout rules)
+  const uint2 raw = *reinterpret_cast<const uint2*>(
+      static_cast<const uint16_t*>(keys) + base + static_cast<int64_t>(key) * k_rs + lane * 4);
+  const uint16_t e[4] = {static_cast<uint16_t>(raw.x & 0xFFFFu), static_cast<uint16_t>(raw.x >> 16),
+                         static_cast<uint16_t>(raw.y & 0xFFFFu), static_cast<uint16_t>(raw.y >> 16)};
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float v = dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(e[j]) << 16)
+                                       : __half2float(__ushort_as_half(e[j]));
+    s = __fadd_ru(s, __fmul_ru(v, v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = __fadd_ru(s, __shfl_xor_sync(0xffffffffu, s, o));
+  if (lane == 0) atomicMax(&maxsq_row[key / bs], __float_as_uint(s));
+}
+
+// Norms of many appended keys (the first step, or a large append): one warp per key.
 __global__ void new_key_norms_kernel(const void* keys, int64_t k_bs, int64_t k_rs, int dtype,
                                      int first_key, int length, int bs, uint32_t* maxsq,
                                      int64_t nb_stride) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
   const int b = blockIdx.y;
-  const int lane = threadIdx.x & 31;
   const int warps = (blockDim.x >> 5) * gridDim.x;
-  const int64_t base = static_cast<int64_t>(b) * k_bs;
   for (int key = first_key + blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); key < length;
-       key += warps) {
-    // 4 dims per lane in one 8-byte load (rows are 16-byte aligned: TMA layout rules)
-    const uint2 raw = *reinterpret_cast<const uint2*>(
-        static_cast<const uint16_t*>(keys) + base + static_cast<int64_t>(key) * k_rs + lane * 4);
-    const uint16_t e[4] = {static_cast<uint16_t>(raw.x & 0xFFFFu), static_cast<uint16_t>(raw.x >> 16),
-                           static_cast<uint16_t>(raw.y & 0xFFFFu), static_cast<uint16_t>(raw.y >> 16)};
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float v = dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(e[j]) << 16)
-                                         : __half2float(__ushort_as_half(e[j]));
-      s = __fadd_ru(s, __fmul_ru(v, v));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s = __fadd_ru(s, __shfl_xor_sync(0xffffffffu, s, o));
-    if (lane == 0) atomicMax(&maxsq[static_cast<int64_t>(b) * nb_stride + key / bs], __float_as_uint(s));
-  }
+       key += warps)
+    fold_key_norm(keys, static_cast<int64_t>(b) * k_bs, k_rs, dtype, key, bs,
+                  maxsq + static_cast<int64_t>(b) * nb_stride);
 }
 
 struct PrepArgs {
@@ -64,20 +77,24 @@ struct PrepArgs {
   int64_t q_bs;
   const float* w;
   int64_t w_bs;
-  const void* qprev;   // [B][8192] 16-bit
-  const float* wprev;  // [B][64]
+  void* qprev;   // [B][8192] 16-bit
+  float* wprev;  // [B][64]
+  const void* keys;
+  int64_t k_bs, k_rs;
   int dtype;
   int prev_length, length, bs, bpt, k;
-  int64_t nb_stride, l_stride;
-  const float* upper;
-  const uint32_t* maxsq;
+  int fold_norms;  // 1: the keys [prev_length, length) are normed here
+  int64_t nb_stride;
+  float* upper;
+  uint32_t* maxsq;
+  const float* bmax;
   const int32_t* prev_topk;
   float* bound;
   int8_t* flag;
-  float* scores;
   int32_t* tile_seq;
   int32_t* tile_blk;
-  int32_t* counter;
+  int32_t* counters;  // [0]: wave-1 tiles (zero on entry), [1]: wave-2 tiles (zeroed here)
+  unsigned long long* stats;
   int init;  // 1: every block is scored (first step)
 };
 
@@ -147,11 +164,18 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
   __shared__ uint32_t sbase[4];
   const int seq = blockIdx.x;
   const int nb = (a.length + a.bs - 1) / a.bs;
+  const int prev_nb = (a.prev_length + a.bs - 1) / a.bs;
   // blocks holding keys appended since the last step are never pruned (replay.py:263-266)
   const int first_new = a.init ? 0 : (a.length > a.prev_length ? a.prev_length / a.bs : nb);
   const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
   int8_t* flag = a.flag + brow;
+  if (seq == 0 && threadIdx.x == 0) a.counters[1] = 0;  // wave 2's list (used after this)
 
+  if (a.fold_norms) {  // few appended keys: one warp per key, into blocks >= first_new
+    for (int key = a.prev_length + (threadIdx.x >> 5); key < a.length; key += kThreads / 32)
+      fold_key_norm(a.keys, static_cast<int64_t>(seq) * a.k_bs, a.k_rs, a.dtype, key, a.bs,
+                    a.maxsq + brow);
+  }
   if (!a.init) {
     // coefficient: 16 threads per head, 8 dims each, float64
     const int h = threadIdx.x >> 4, sub = threadIdx.x & 15;
@@ -183,16 +207,31 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
       c_total = c * (1.0 + 0x1p-40);
     }
   }
-  // reset the per-key scores of this step
-  float* srow = a.scores + static_cast<int64_t>(seq) * a.l_stride;
-  for (int i = threadIdx.x; i < a.length; i += kThreads) srow[i] = -INFINITY;
-  __syncthreads();
-  // bounds and flags
+  __syncthreads();  // every read of qprev / wprev is done
+  // keep q (16-bit bits) and w for the next step's coefficient (rows are 16-byte aligned:
+  // the scoring kernels' TMA rules)
+  {
+    const uint4* qs = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.q) +
+                                                     static_cast<int64_t>(seq) * a.q_bs);
+    uint4* qd = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.qprev) +
+                                         static_cast<int64_t>(seq) * 8192);
+    for (int i = threadIdx.x; i < 8192 / 8; i += kThreads) qd[i] = qs[i];
+    if (threadIdx.x < 64)
+      a.wprev[static_cast<int64_t>(seq) * 64 + threadIdx.x] =
+          a.w[static_cast<int64_t>(seq) * a.w_bs + threadIdx.x];
+  }
+  // the previous step's state update, then this step's bounds and flags (block b is
+  // updated and read by the same thread)
   for (int b = threadIdx.x; b < nb; b += kThreads) {
     float bnd = INFINITY;
     if (b < first_new) {
+      float u = a.upper[brow + b];
+      if (b < prev_nb) {
+        u = flag[b] ? a.bmax[brow + b] : a.bound[brow + b];
+        a.upper[brow + b] = u;
+      }
       const double nrm = static_cast<double>(__fsqrt_ru(__uint_as_float(a.maxsq[brow + b])));
-      bnd = __double2float_ru(static_cast<double>(a.upper[brow + b]) + nrm * c_total);
+      bnd = __double2float_ru(static_cast<double>(u) + nrm * c_total);
     }
     a.bound[brow + b] = bnd;
     flag[b] = (a.init || b >= first_new) ? 1 : 0;
@@ -204,9 +243,17 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
       const int blk = top[i] / a.bs;
       if (blk >= 0 && blk < nb) flag[blk] = 1;
     }
+  } else if (threadIdx.x == 0) {  // the first step scores every block
+    unsigned long long* st = a.stats + static_cast<int64_t>(seq) * 8;
+    st[0] += 1;
+    st[1] += static_cast<unsigned long long>(nb);
+    st[2] += static_cast<unsigned long long>(nb);
+    st[4] += static_cast<unsigned long long>(a.length);
+    st[5] += static_cast<unsigned long long>(a.length);
+    st[6] += static_cast<unsigned long long>(nb);
   }
   __syncthreads();
-  emit_tiles(flag, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counter, wtot, sbase);
+  emit_tiles(flag, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters, wtot, sbase);
 }
 
 constexpr int kHistCopies = 8;  // private copies of the row histogram (one per 4 warps)
@@ -245,33 +292,50 @@ __device__ uint32_t row_histogram(const float* srow, int length, uint32_t* h, ui
 }
 
 // Wave 2: blocks not scored yet whose bound reaches tau.  tau is the lower edge of the key
-// bin (top 12 bits, then the next 12 bits inside that bin) that holds the k-th largest
-// wave-1 score: at most that score, so every block pruned against it holds no top-k key
-// (and no top-k launch is needed for it).
-__global__ void __launch_bounds__(kThreads)
-    exact_wave2_kernel(int length, int bs, int bpt, int64_t nb_stride, const float* bound,
-                       const float* scores, int64_t l_stride, int k, float* tau, int8_t* flag,
-                       int32_t* tile_seq, int32_t* tile_blk, int32_t* counter,
-                       const uint32_t* hist_in) {
+// bin (top 12 bits from the wave-1 histogram, then the next 12 bits inside that bin) that
+// holds the k-th largest wave-1 score: at most that score, so every block pruned against it
+// holds no top-k key.  Pruned keys are set to -inf in the score row; with `hist_for_topk`
+// they are counted in the -inf bin of the histogram (which the top-k then consumes),
+// otherwise the histogram is cleared for the next step.
+struct Wave2Args {
+  int length, bs, bpt, k;
+  int64_t nb_stride, l_stride;
+  const float* bound;
+  float* scores;
+  float* tau;
+  int8_t* flag;
+  int32_t* tile_seq;
+  int32_t* tile_blk;
+  int32_t* counters;  // [1]: wave-2 tiles; [0] is cleared for the next step's wave 1
+  uint32_t* hist;     // [B][4096]: the wave-1 scores' key histogram
+  int hist_for_topk;
+  unsigned long long* stats;
+};
+
+__global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
   extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words
   __shared__ uint32_t h[kKeyHistBins];
   __shared__ uint32_t wtot[32];
   __shared__ uint32_t sbase[4];
+  __shared__ unsigned long long acc[5];
   __shared__ float s_tau;
   __shared__ uint32_t s_bin, s_rank;
   const int seq = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nb = (length + bs - 1) / bs;
-  const int64_t brow = static_cast<int64_t>(seq) * nb_stride;
-  if (hist_in) {  // the first level came from row_hist_part_kernel
-    const uint32_t* src = hist_in + static_cast<int64_t>(seq) * kKeyHistBins;
-    for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) h[i] = src[i];
-    __syncthreads();
-  } else {
-    row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h, hcopies);
+  const int nb = (a.length + a.bs - 1) / a.bs;
+  const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
+  const int8_t* flag = a.flag + brow;
+  float* srow = a.scores + static_cast<int64_t>(seq) * a.l_stride;
+  uint32_t* grow = a.hist + static_cast<int64_t>(seq) * kKeyHistBins;
+  if (seq == 0 && threadIdx.x == 0) a.counters[0] = 0;  // wave 1 of this step is done
+  if (threadIdx.x < 5) acc[threadIdx.x] = 0ull;
+  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {
+    h[i] = grow[i];
+    if (!a.hist_for_topk) grow[i] = 0u;
   }
+  __syncthreads();
   // thread t owns bins 4095-4t .. 4092-4t: keys above a thread's bins by a CTA scan
   uint32_t c[4], tot = 0;
 #pragma unroll
@@ -286,11 +350,11 @@ __global__ void __launch_bounds__(kThreads)
     if (lane >= o) x += y;
   }
   if (lane == 31) wtot[warp] = x;
-  if (threadIdx.x == 0) s_tau = -INFINITY;  // fewer than k finite scores: prune nothing
+  if (threadIdx.x == 0) s_tau = -INFINITY;  // fewer than k wave-1 scores: prune nothing
   __syncthreads();
   uint32_t above = x - tot;
   for (int i = 0; i < warp; ++i) above += wtot[i];
-  const uint32_t kk = static_cast<uint32_t>(k);
+  const uint32_t kk = static_cast<uint32_t>(a.k);
   if (threadIdx.x == 0) s_bin = 0xFFFFFFFFu;
   if (above < kk && kk <= above + tot) {
 #pragma unroll
@@ -305,23 +369,24 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   const uint32_t bin1 = s_bin;
   if (bin1 != 0xFFFFFFFFu && bin1 != 0u) {
-    // second level: the next 12 key bits of the keys in that bin narrow tau to 2^8 keys
-    const float* srow = scores + static_cast<int64_t>(seq) * l_stride;
+    // second level: the next 12 key bits of the wave-1 keys in that bin (the row holds
+    // stale scores outside the wave-1 blocks) narrow tau to 2^8 keys
     for (int i = threadIdx.x; i < kHistCopies * kKeyHistBins; i += kThreads) hcopies[i] = 0u;
     __syncthreads();
     uint32_t* mine = hcopies + (warp & (kHistCopies - 1)) * kKeyHistBins;
-    const int span = (length + 31) & ~31;
+    const int span = (a.length + 31) & ~31;
     for (int i = threadIdx.x; i < span; i += kThreads) {
-      const float v = i < length ? srow[i] : -INFINITY;
+      const bool scored = i < a.length && flag[i / a.bs] == 1;
+      const float v = scored ? srow[i] : -INFINITY;
       const uint32_t key = float_to_key(v);
-      const bool in = v != -INFINITY && (key >> 20) == bin1;
+      const bool in = scored && (key >> 20) == bin1;
       add_to_bin(mine, in, (key >> 8) & 0xFFFu);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {
       uint32_t t = 0;
 #pragma unroll
-      for (int c = 0; c < kHistCopies; ++c) t += hcopies[c * kKeyHistBins + i];
+      for (int cc = 0; cc < kHistCopies; ++cc) t += hcopies[cc * kKeyHistBins + i];
       h[i] = t;
     }
     __syncthreads();
@@ -356,16 +421,66 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
   }
   const float t = s_tau;
-  if (threadIdx.x == 0) tau[seq] = t;
-  for (int b = threadIdx.x; b < nb; b += kThreads)
-    if (flag[brow + b] == 0 && bound[brow + b] >= t) flag[brow + b] = 2;
+  if (threadIdx.x == 0) a.tau[seq] = t;
+  int8_t* fl = a.flag + brow;
+  unsigned long long scored = 0, keys = 0, hot = 0, second = 0, pruned_keys = 0;
+  for (int b = threadIdx.x; b < nb; b += kThreads) {
+    int8_t f = fl[b];
+    if (f == 0 && a.bound[brow + b] >= t) {
+      f = 2;
+      fl[b] = 2;
+    }
+    const unsigned long long n = static_cast<unsigned long long>(min(a.bs, a.length - b * a.bs));
+    if (f) {
+      ++scored;
+      keys += n;
+      hot += f == 1;
+      second += f == 2;
+    } else {
+      pruned_keys += n;
+    }
+  }
+  // warp sums first: 64-bit shared atomics from every thread on one word serialise
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    scored += __shfl_xor_sync(0xffffffffu, scored, o);
+    keys += __shfl_xor_sync(0xffffffffu, keys, o);
+    hot += __shfl_xor_sync(0xffffffffu, hot, o);
+    second += __shfl_xor_sync(0xffffffffu, second, o);
+    pruned_keys += __shfl_xor_sync(0xffffffffu, pruned_keys, o);
+  }
+  if (lane == 0) {
+    atomicAdd(&acc[0], scored);
+    atomicAdd(&acc[1], keys);
+    atomicAdd(&acc[2], hot);
+    atomicAdd(&acc[3], second);
+    atomicAdd(&acc[4], pruned_keys);
+  }
   __syncthreads();
-  emit_tiles(flag + brow, nb, 2, bpt, seq, tile_seq, tile_blk, counter, wtot, sbase);
+  // pruned keys score -inf (the top-k reads the whole row)
+  if (acc[4]) {
+    for (int i = threadIdx.x; i < a.length; i += kThreads)
+      if (fl[i / a.bs] == 0) srow[i] = -INFINITY;
+  }
+  if (threadIdx.x == 0) {
+    if (a.hist_for_topk && acc[4]) atomicAdd(&grow[kNegInfBin], static_cast<uint32_t>(acc[4]));
+    unsigned long long* st = a.stats + static_cast<int64_t>(seq) * 8;
+    st[0] += 1;                                    // steps
+    st[1] += static_cast<unsigned long long>(nb);  // blocks visited
+    st[2] += acc[0];                               // blocks scored
+    st[3] += static_cast<unsigned long long>(nb) - acc[0];  // blocks pruned
+    st[4] += acc[1];                               // keys scored (read)
+    st[5] += static_cast<unsigned long long>(a.length);     // keys in the cache
+    st[6] += acc[2];                               // first-wave (hot) blocks
+    st[7] += acc[3];                               // second-wave blocks
+  }
+  emit_tiles(fl, nb, 2, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters + 1, wtot, sbase);
 }
 
 // Part of a row's key histogram, added to hist[seq] (zero before the launch): CTA
 // blockIdx.x of gridDim.x takes one contiguous chunk of the row, so a small batch still
-// spreads over many SMs.  Finite scores by bin, the unscored (-inf) keys in bin 0.
+// spreads over many SMs.  Finite scores by bin; the unscored (-inf) keys are counted in
+// the bin of the -inf key itself (0x007FFFFF >> 20 = 7), as the cluster top-k expects.
 __global__ void __launch_bounds__(kThreads)
     row_hist_part_kernel(const float* scores, int64_t l_stride, int length, uint32_t* hist) {
   pdl_wait();  // every global access follows the previous kernel
@@ -385,107 +500,13 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// The final key histogram of each row for the histogram top-k: finite scores by bin, the
-// unscored (-inf) keys in bin 0.  Every bin is stored (no zeroing needed before).
-__global__ void __launch_bounds__(kThreads)
-    exact_row_hist_kernel(const float* scores, int64_t l_stride, int length, uint32_t* hist) {
-  pdl_wait();  // every global access follows the previous kernel
-  pdl_launch_dependents();
-  extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words
-  __shared__ uint32_t h[kKeyHistBins];
-  const int seq = blockIdx.x;
-  const uint32_t inf =
-      row_histogram(scores + static_cast<int64_t>(seq) * l_stride, length, h, hcopies);
-  uint32_t* dst = hist + static_cast<int64_t>(seq) * kKeyHistBins;
-  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads)
-    dst[i] = h[i] + (i == (0x007FFFFFu >> 20) ? inf : 0u);
-}
-
-// State update and statistics.
-__global__ void __launch_bounds__(kThreads)
-    exact_finalize_kernel(const void* q, int64_t q_bs, const float* w, int64_t w_bs, int dtype,
-                          int length, int bs, int64_t nb_stride, const int8_t* flag,
-                          const float* bmax, const float* bound, float* upper, void* qprev,
-                          float* wprev, unsigned long long* stats, int new_keys) {
-  pdl_wait();  // every global access follows the previous kernel
-  pdl_launch_dependents();
-  __shared__ unsigned long long acc[4];
-  const int seq = blockIdx.x;
-  const int nb = (length + bs - 1) / bs;
-  const int64_t brow = static_cast<int64_t>(seq) * nb_stride;
-  if (threadIdx.x < 4) acc[threadIdx.x] = 0ull;
-  __syncthreads();
-  unsigned long long scored = 0, keys = 0, hot = 0, wave2 = 0;
-  for (int b = threadIdx.x; b < nb; b += kThreads) {
-    const int8_t f = flag[brow + b];
-    upper[brow + b] = f ? bmax[brow + b] : bound[brow + b];
-    if (f) {
-      ++scored;
-      keys += static_cast<unsigned long long>(min(bs, length - b * bs));
-      hot += f == 1;
-      wave2 += f == 2;
-    }
-  }
-  // warp sums first: 64-bit shared atomics from every thread on one word serialise
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    scored += __shfl_xor_sync(0xffffffffu, scored, o);
-    keys += __shfl_xor_sync(0xffffffffu, keys, o);
-    hot += __shfl_xor_sync(0xffffffffu, hot, o);
-    wave2 += __shfl_xor_sync(0xffffffffu, wave2, o);
-  }
-  if ((threadIdx.x & 31) == 0) {
-    atomicAdd(&acc[0], scored);
-    atomicAdd(&acc[1], keys);
-    atomicAdd(&acc[2], hot);
-    atomicAdd(&acc[3], wave2);
-  }
-  // keep q (16-bit bits) and w for the next step's certified coefficient (rows are
-  // 16-byte aligned: the scoring kernels' TMA rules)
-  const uint4* qs = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(q) +
-                                                   static_cast<int64_t>(seq) * q_bs);
-  uint4* qd = reinterpret_cast<uint4*>(static_cast<uint16_t*>(qprev) +
-                                       static_cast<int64_t>(seq) * 8192);
-  for (int i = threadIdx.x; i < 8192 / 8; i += kThreads) qd[i] = qs[i];
-  if (threadIdx.x < 64) wprev[static_cast<int64_t>(seq) * 64 + threadIdx.x] =
-      w[static_cast<int64_t>(seq) * w_bs + threadIdx.x];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long* st = stats + static_cast<int64_t>(seq) * 8;
-    st[0] += 1;                                    // steps
-    st[1] += static_cast<unsigned long long>(nb);  // blocks visited
-    st[2] += acc[0];                               // blocks scored
-    st[3] += static_cast<unsigned long long>(nb) - acc[0];  // blocks pruned
-    st[4] += acc[1];                               // keys scored (read)
-    st[5] += static_cast<unsigned long long>(length);       // keys in the cache
-    st[6] += acc[2];                               // first-wave (hot) blocks
-    st[7] += acc[3];                               // second-wave blocks
-    (void)dtype;
-    (void)new_keys;
-  }
-}
-
-__global__ void copy_indices_kernel(const int32_t* src, int64_t s_stride, void* dst,
-                                    int64_t d_stride, int idx_bytes, int k) {
-  pdl_wait();  // every global access follows the previous kernel
-  pdl_launch_dependents();
-  const int row = blockIdx.y;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x) {
-    const int32_t v = src[static_cast<int64_t>(row) * s_stride + i];
-    if (idx_bytes == 8)
-      static_cast<int64_t*>(dst)[static_cast<int64_t>(row) * d_stride + i] = v;
-    else
-      static_cast<int32_t*>(dst)[static_cast<int64_t>(row) * d_stride + i] = v;
-  }
-}
-
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace
 
 int launch_row_hist_parts(const float* scores, int64_t l_stride, int batch, int length,
                           uint32_t* hist, cudaStream_t stream) {
-  const int parts = std::max(1, std::min({16, 148 / batch, (length + 2047) / 2048}));
+  const int parts = std::max(1, std::min({16, device_sm_count(current_device()) / batch, (length + 2047) / 2048}));
   TDSA_CUDA_CHECK(cudaMemsetAsync(hist, 0, static_cast<size_t>(batch) * kKeyHistBins * 4,
                                   stream));
   TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(row_hist_part_kernel),
@@ -549,25 +570,32 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   int32_t* tile_seq = reinterpret_cast<int32_t*>(state + L.tile_seq);
   int32_t* tile_blk = reinterpret_cast<int32_t*>(state + L.tile_blk);
   int32_t* counters = reinterpret_cast<int32_t*>(state + L.counters);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(state + L.hist);
   void* tws = state + L.topk_ws;
+  // rows of one top-k segment select from the histogram the score waves build
+  const bool hist_for_topk = length <= kTopkSegment;
 
   if (init) {
     TDSA_CUDA_CHECK(cudaMemsetAsync(maxsq, 0, static_cast<size_t>(batch) * L.nb_stride * 4,
                                     stream));
     TDSA_CUDA_CHECK(cudaMemsetAsync(stats, 0, static_cast<size_t>(batch) * 64, stream));
+    TDSA_CUDA_CHECK(cudaMemsetAsync(counters, 0, 16, stream));
+    TDSA_CUDA_CHECK(cudaMemsetAsync(hist, 0, static_cast<size_t>(batch) * kKeyHistBins * 4,
+                                    stream));
   }
-  TDSA_CUDA_CHECK(cudaMemsetAsync(counters, 0, 16, stream));
-  // 1. norms of the keys appended since the last step (all keys at init)
+  // 1. norms of the appended keys: many (the first step) in a kernel of their own, a few
+  // inside prepare
   const int first_key = init ? 0 : prev_length;
-  if (length > first_key) {
-    const int nkeys = length - first_key;
-    const int blocks_x = min(148, (nkeys + 7) / 8);
+  const int nkeys = length - first_key;
+  const bool fold = !init && nkeys <= kFoldKeys;
+  if (nkeys > 0 && !fold) {
+    const int blocks_x = std::min(device_sm_count(current_device()), (nkeys + 7) / 8);
     TDSA_CUDA_CHECK(launch_pdl(new_key_norms_kernel, dim3(blocks_x, batch), dim3(256), 0, stream,
                                keys, k_bs, k_rs, dtype, first_key, length, block_size, maxsq,
                                L.nb_stride));
     TDSA_CUDA_CHECK(cudaGetLastError());
   }
-  // 2. bounds, flags, wave-1 tiles
+  // 2. state update, bounds, flags, wave-1 tiles
   PrepArgs pa;
   pa.q = q;
   pa.q_bs = q_bs;
@@ -575,23 +603,27 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   pa.w_bs = w_bs;
   pa.qprev = qprev;
   pa.wprev = wprev;
+  pa.keys = keys;
+  pa.k_bs = k_bs;
+  pa.k_rs = k_rs;
   pa.dtype = dtype;
-  pa.prev_length = prev_length;
+  pa.prev_length = init ? 0 : prev_length;
   pa.length = length;
   pa.bs = block_size;
   pa.bpt = bpt;
   pa.k = k;
+  pa.fold_norms = fold ? 1 : 0;
   pa.nb_stride = L.nb_stride;
-  pa.l_stride = max_length;
   pa.upper = upper;
   pa.maxsq = maxsq;
+  pa.bmax = bmax;
   pa.prev_topk = topk;
   pa.bound = bound;
   pa.flag = flag;
-  pa.scores = scores;
   pa.tile_seq = tile_seq;
   pa.tile_blk = tile_blk;
-  pa.counter = counters;
+  pa.counters = counters;
+  pa.stats = stats;
   pa.init = init;
   TDSA_CUDA_CHECK(launch_pdl(exact_prepare_kernel, dim3(batch), dim3(kThreads), 0, stream, pa));
   TDSA_CUDA_CHECK(cudaGetLastError());
@@ -612,83 +644,53 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   ba.status = device_status_ptr();
   if (!ba.status) return fail(TDSA_ERR_CUDA, "device status word not available");
   const int grid = device_sm_count(current_device());
-  // 3. wave 1
+  // 3. wave 1 (every block at the first step), its scores into the row histogram; the
+  // first step keeps the histogram only for the top-k
   ba.tile_count = counters;
+  ba.hist = (init && !hist_for_topk) ? nullptr : hist;
   int rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
                                stream);
   if (rc) return rc;
-  // Rows of a small batch are histogrammed by several CTAs each (the one-CTA-per-row pass
-  // is latency-bound): row_hist_part_kernel into a zeroed buffer.
-  const int parts = std::max(1, std::min({16, 148 / batch, (length + 2047) / 2048}));
-  uint32_t* hbuf = reinterpret_cast<uint32_t*>(state + L.hist);
-  auto part_hist = [&]() -> int {
-    TDSA_CUDA_CHECK(cudaMemsetAsync(hbuf, 0, static_cast<size_t>(batch) * kKeyHistBins * 4,
-                                    stream));
-    TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(row_hist_part_kernel),
-                                        kHistCopyBytes));
-    TDSA_CUDA_CHECK(launch_pdl(row_hist_part_kernel, dim3(parts, batch), dim3(kThreads),
-                               kHistCopyBytes, stream, static_cast<const float*>(scores),
-                               static_cast<int64_t>(max_length), length, hbuf));
-    TDSA_CUDA_CHECK(cudaGetLastError());
-    return TDSA_OK;
-  };
-  if (!init) {
-    // 4. tau (a lower bound of the k-th largest wave-1 score), 5. wave-2 list, 6. wave 2
-    const bool split = parts > 1 && length <= kTopkSegment;
-    if (split) {
-      rc = part_hist();
-      if (rc) return rc;
-    }
+  if (init) {
+    // the next step's prepare appends its tiles from zero (a step's wave2 kernel clears it)
+    TDSA_CUDA_CHECK(cudaMemsetAsync(counters, 0, 4, stream));
+  } else {
+    // 4. tau, wave-2 list, pruned keys, statistics; 5. wave 2
+    Wave2Args wa;
+    wa.length = length;
+    wa.bs = block_size;
+    wa.bpt = bpt;
+    wa.k = k;
+    wa.nb_stride = L.nb_stride;
+    wa.l_stride = max_length;
+    wa.bound = bound;
+    wa.scores = scores;
+    wa.tau = tau;
+    wa.flag = flag;
+    wa.tile_seq = tile_seq;
+    wa.tile_blk = tile_blk;
+    wa.counters = counters;
+    wa.hist = hist;
+    wa.hist_for_topk = hist_for_topk ? 1 : 0;
+    wa.stats = stats;
     TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_wave2_kernel),
                                         kHistCopyBytes));
     TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), kHistCopyBytes,
-                               stream,
-                               length, block_size, bpt, L.nb_stride,
-                               static_cast<const float*>(bound),
-                               static_cast<const float*>(scores),
-                               static_cast<int64_t>(max_length), k, tau, flag, tile_seq,
-                               tile_blk, counters + 1,
-                               static_cast<const uint32_t*>(split ? hbuf : nullptr)));
+                               stream, wa));
     TDSA_CUDA_CHECK(cudaGetLastError());
     ba.tile_count = counters + 1;
+    ba.hist = hist_for_topk ? hist : nullptr;
     rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
                              stream);
     if (rc) return rc;
   }
-  // 7. top-k over the scored keys (indices kept as the next step's seeds); rows of one
-  // top-k segment start from their key histogram
-  uint32_t* hist = nullptr;
-  if (length <= kTopkSegment) {
-    hist = hbuf;
-    if (parts > 1) {
-      rc = part_hist();
-      if (rc) return rc;
-    } else {
-      TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_row_hist_kernel),
-                                          kHistCopyBytes));
-      TDSA_CUDA_CHECK(launch_pdl(exact_row_hist_kernel, dim3(batch), dim3(kThreads),
-                                 kHistCopyBytes, stream, static_cast<const float*>(scores),
-                                 static_cast<int64_t>(max_length), length, hist));
-      TDSA_CUDA_CHECK(cudaGetLastError());
-    }
-  }
-  rc = launch_topk(scores, max_length, nullptr, 0, batch, length, k, sorted, topk, 4, k, out_val,
-                   val_bs, tws, L.topk_ws_bytes, stream, nullptr, hist);
-  if (rc) return rc;
-  if (out_idx) {
-    TDSA_CUDA_CHECK(launch_pdl(copy_indices_kernel, dim3((k + 255) / 256, batch), dim3(256), 0,
-                               stream, static_cast<const int32_t*>(topk),
-                               static_cast<int64_t>(k), out_idx, idx_bs, idx_bytes, k));
-    TDSA_CUDA_CHECK(cudaGetLastError());
-  }
-  // 8. state update
-  TDSA_CUDA_CHECK(launch_pdl(exact_finalize_kernel, dim3(batch), dim3(kThreads), 0, stream, q,
-                             q_bs, w, w_bs, dtype, length, block_size, L.nb_stride,
-                             static_cast<const int8_t*>(flag), static_cast<const float*>(bmax),
-                             static_cast<const float*>(bound), upper, qprev, wprev, stats,
-                             length - first_key));
-  TDSA_CUDA_CHECK(cudaGetLastError());
-  return TDSA_OK;
+  // 6. top-k over the row (from its histogram when it is one segment); the indices are also
+  // kept as the next step's seeds
+  void* oi = out_idx ? out_idx : topk;
+  return launch_topk(scores, max_length, nullptr, 0, batch, length, k, sorted, oi,
+                     out_idx ? idx_bytes : 4, out_idx ? idx_bs : k, out_val, val_bs, tws,
+                     L.topk_ws_bytes, stream, nullptr, hist_for_topk ? hist : nullptr,
+                     out_idx ? topk : nullptr, k);
 }
 
 }  // namespace tdsa

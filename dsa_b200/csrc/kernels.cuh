@@ -49,6 +49,12 @@ struct BlockArgs {
   float* block_max = nullptr;            // [batch][bm_stride]
   int64_t bm_stride = 0;
   int8_t* accepted = nullptr;            // [batch][bm_stride]
+  int mask_invert = 0;                   // H8: a block is cold where the mask is zero
+  const float* accept_max = nullptr;     // masked: keep = mask || accept_max >= *threshold
+                                         // ([batch][bm_stride]), written to `accepted`
+  uint32_t* hist = nullptr;              // exact: [batch][4096] key histogram (top 12 bits
+                                         // of the order-preserving key) the epilogue adds
+                                         // every scored key to
   int* status = nullptr;
 };
 
@@ -126,7 +132,8 @@ int topk_check(int length, int k, int sorted);
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,
                 int batch, int length, int k, int sorted, void* out_idx, int idx_bytes,
                 int64_t oi_stride, float* out_val, int64_t ov_stride, void* ws, size_t ws_bytes,
-                cudaStream_t stream, float* kth_out = nullptr, uint32_t* key_hist = nullptr);
+                cudaStream_t stream, float* kth_out = nullptr, uint32_t* key_hist = nullptr,
+                int32_t* mirror = nullptr, int64_t mirror_stride = 0);
 
 int launch_hadamard128(const void* in, int64_t in_stride, int64_t rows, int dtype, void* out,
                        int64_t out_stride, cudaStream_t stream);

@@ -37,6 +37,7 @@ constexpr int kTmemCols = 128;
 constexpr int kThreads = 192;
 constexpr int kBarrierBytes = 1024;
 constexpr int kSmemBytes = kStages * kStageBytes + 2 * kQBytes + kBarrierBytes + 1024;
+constexpr int kHistSmemBytes = kKeyHistBins * 4;  // exact mode with a key histogram
 constexpr int kMaxSlots = 8;  // blocks per tile at bs = 16
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -66,11 +67,21 @@ __device__ __forceinline__ void get_tile(const BlockArgs& a, int64_t t, Tile& ti
   }
 }
 
+// The launch's per-block mask: cold (H8, or direct blocks inverted), keep (masked; with
+// `accept_max`, the second half of the two-pass path: kept when direct or when the block's
+// probe maximum reaches the threshold), direct (progressive).
+template <int kMode>
+__device__ __forceinline__ bool mask_set(const BlockArgs& a, int seq, int blk) {
+  const bool m = a.mask[static_cast<int64_t>(seq) * a.mask_stride + blk] != 0;
+  if (kMode == kModeMasked && a.accept_max != nullptr)
+    return m || a.accept_max[static_cast<int64_t>(seq) * a.bm_stride + blk] >= *a.threshold;
+  return m != (a.mask_invert != 0);
+}
+
 template <int kMode>
 __device__ __forceinline__ bool block_loaded(const BlockArgs& a, int seq, int blk) {
   if (blk < 0) return false;
-  if (kMode == kModeH8 || kMode == kModeMasked)
-    return a.mask[static_cast<int64_t>(seq) * a.mask_stride + blk] != 0;
+  if (kMode == kModeH8 || kMode == kModeMasked) return mask_set<kMode>(a, seq, blk);
   return true;
 }
 
@@ -120,9 +131,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accempty = accfull + kAccBufs;
   uint64_t* grp = accempty + kAccBufs;  // epilogue group-max exchange, one per TMEM buffer
   uint64_t* done = grp + kAccBufs;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* hbar = done + 1;  // epilogue-warp handshake around histogram flushes
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* gmax = reinterpret_cast<float*>(tmem_holder + 4);  // [kAccBufs][8]
+  // exact mode with a histogram: 4096 bins behind the barrier region
+  uint32_t* shist = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
+  const bool use_hist = kMode == kModeExact && a.hist != nullptr;
+  if (use_hist)
+    for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) shist[i] = 0u;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -149,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&grp[s], 4);
     }
     mbar_init(done, 1);
+    mbar_init(hbar, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -261,21 +279,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const float thr = (kMode == kModeProgressive) ? *a.threshold : 0.f;
     int prev_seq = -1;
-    uint32_t acc_it = 0;
+    uint32_t acc_it = 0, hph = 0;
     float wr[kHeads];
     Tile tile;
+    const int etid = (warp - 2) * 32 + lane;  // 0..127 over the epilogue warps
+    // all four epilogue warps meet (bounded wait); false when the CTA aborts
+    auto hist_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(hbar);
+      const bool ok = mbar_wait(hbar, hph & 1u, abort_flag);
+      ++hph;
+      return ok;
+    };
+    // adds this CTA's counts of sequence `seq` to its row histogram and clears them
+    auto hist_flush = [&](int seq) -> bool {
+      if (!hist_sync()) return false;
+      uint32_t* dst = a.hist + static_cast<int64_t>(seq) * kKeyHistBins;
+      for (int i = etid; i < kKeyHistBins; i += 128) {
+        const uint32_t c = shist[i];
+        if (c) {
+          atomicAdd(dst + i, c);
+          shist[i] = 0u;
+        }
+      }
+      return hist_sync();
+    };
     for (int64_t t = t0; t < t1; ++t) {
       get_tile(a, t, tile);
       const int seq = tile.seq;
       if (seq != prev_seq) {
+        if (use_hist && prev_seq >= 0 && !hist_flush(prev_seq)) break;
         load_head_weights(a.w + static_cast<int64_t>(seq) * a.w_stride, wr);
         prev_seq = seq;
       }
       const int blk = tile.block[slot_j];
       const int key = blk * bs + ingroup;
       const bool valid = blk >= 0 && key < a.length;
-      const int64_t mrow = static_cast<int64_t>(seq) * a.mask_stride;
-      const bool flag = (kMode != kModeExact && blk >= 0) ? a.mask[mrow + blk] != 0 : false;
+      const bool flag = (kMode != kModeExact && blk >= 0) ? mask_set<kMode>(a, seq, blk) : false;
 
       const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
       if (!mbar_wait(&accfull[acc], aph, abort_flag)) break;
@@ -336,9 +376,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!accept) out = -INFINITY;
       }
 
-      if (valid) a.out[static_cast<int64_t>(seq) * a.out_stride + key] = out;
+      if (valid && (kMode != kModeH8 || a.out != nullptr))
+        a.out[static_cast<int64_t>(seq) * a.out_stride + key] = out;
+      if (use_hist) add_to_bin(shist, valid, float_to_key(out) >> 20);
       if (blk >= 0 && ingroup == 0) {
-        if (kMode == kModeH8 || kMode == kModeExact) {
+        if (kMode == kModeMasked) {
+          if (a.accepted) a.accepted[static_cast<int64_t>(seq) * a.bm_stride + blk] = flag ? 1 : 0;
+        } else if (kMode == kModeH8 || kMode == kModeExact) {
           a.block_max[static_cast<int64_t>(seq) * a.bm_stride + blk] = bmax;
         } else if (kMode == kModeProgressive) {
           a.block_max[static_cast<int64_t>(seq) * a.bm_stride + blk] = flag ? -INFINITY : bmax;
@@ -346,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       ++acc_it;
+      if (use_hist && t + 1 == t1) hist_flush(seq);
     }
   }
 
@@ -362,8 +407,9 @@ template <int kMode, bool kBF16>
 int launch_t(const CUtensorMap& kmap, const CUtensorMap& qmap, const BlockArgs& a, int grid,
              cudaStream_t stream) {
   auto kern = score_blocks_kernel<kMode, kBF16>;
-  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBytes));
-  TDSA_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kThreads), kSmemBytes, stream, kmap, qmap, a));
+  const int smem = kSmemBytes + (a.hist ? kHistSmemBytes : 0);
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
+  TDSA_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, kmap, qmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }

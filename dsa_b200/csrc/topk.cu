@@ -68,6 +68,9 @@ struct TopkArgs {
   int gather;             // merge of an exchange: gather the rows from peer memory first
   PeerGather pg;
   int hist_segs;          // cluster top-k: the row's 32768-key histogram segments (summed)
+  int32_t* mirror;        // the last level also writes its indices here, int32
+                          // ([rows][mirror_stride]; null: not)
+  int64_t mirror_stride;
 };
 
 __device__ __forceinline__ unsigned lanemask_lt() {
@@ -487,6 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   int64_t* oi64 = a.out_idx && a.idx_bytes == 8
                       ? static_cast<int64_t*>(a.out_idx) + out_row * a.out_idx_stride : nullptr;
   float* ov = a.out_idx && a.out_val ? a.out_val + out_row * a.out_val_stride : nullptr;
+  int32_t* om = a.mirror ? a.mirror + out_row * a.mirror_stride : nullptr;
   if (a.pad_to_k && n < a.k) {
     // pads rank below every real candidate of the next level (-inf, then the largest index)
     for (int j = n + tid; j < a.k; j += kThreads) {
@@ -508,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     if (direct) {
       if (oi32) oi32[pos] = static_cast<int32_t>(gi);
       if (oi64) oi64[pos] = static_cast<int64_t>(gi);
+      if (om) om[pos] = static_cast<int32_t>(gi);
       if (ov) ov[pos] = key_to_float(u);
       if (u <= chi) kth_local = min(kth_local, u);
     } else if (pos < static_cast<uint32_t>(a.cap)) {
@@ -599,6 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       } else {
         if (oi32) oi32[pos] = static_cast<int32_t>(gi);
         if (oi64) oi64[pos] = static_cast<int64_t>(gi);
+        if (om) om[pos] = static_cast<int32_t>(gi);
         if (ov) ov[pos] = key_to_float(u);
       }
     }
@@ -636,6 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     const uint32_t gi = 0xFFFFFFFFu - static_cast<uint32_t>(p & 0xFFFFFFFFull);
     if (oi64) oi64[j] = static_cast<int64_t>(gi);
     if (oi32) oi32[j] = static_cast<int32_t>(gi);
+    if (om) om[j] = static_cast<int32_t>(gi);
     if (ov) ov[j] = key_to_float(static_cast<uint32_t>(p >> 32));
   }
 }
@@ -853,6 +860,7 @@ __global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)
   int64_t* oi64 = a.out_idx && a.idx_bytes == 8
                       ? static_cast<int64_t*>(a.out_idx) + orow * a.out_idx_stride : nullptr;
   float* ov = a.out_val ? a.out_val + orow * a.out_val_stride : nullptr;
+  int32_t* om = a.mirror ? a.mirror + orow * a.mirror_stride : nullptr;
 #pragma unroll
   for (int j = 0; j < kChunks; ++j) {
     const uint32_t g = (gtm >> (j * kV)) & kVMask, q = (eqm >> (j * kV)) & kVMask;
@@ -881,6 +889,7 @@ __global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)
         if (pos < k) {
           if (oi32) oi32[pos] = e0 + s;
           if (oi64) oi64[pos] = e0 + s;
+          if (om) om[pos] = e0 + s;
           if (ov) ov[pos] = key_to_float(u[j * kV + s]);
         }
       }
@@ -946,7 +955,8 @@ int launch_cluster(const TopkArgs& a, int rows, int per, cudaStream_t stream) {
 }
 
 // Clusters of kC top-k CTAs the current device runs at once (one CTA per SM), queried once
-// per device; 0 when the query fails.
+// per device; 0 when the query fails (a failed query is not cached: the next call asks
+// again, e.g. once the device has a context).
 template <int kC>
 int max_active_clusters() {
   static std::mutex mu;
@@ -954,7 +964,7 @@ int max_active_clusters() {
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return 0;
   std::lock_guard<std::mutex> lock(mu);
-  if (cache[dev] == 0) {
+  if (cache[dev] <= 0) {
     const void* kern = reinterpret_cast<const void*>(topk_cluster_kernel<4, kC>);
     constexpr int smem = kClusterHistWords * 4;
     cudaLaunchConfig_t cfg = {};
@@ -967,9 +977,9 @@ int max_active_clusters() {
       cudaGetLastError();
       nc = 0;
     }
-    cache[dev] = nc > 0 ? nc : -1;
+    cache[dev] = nc > 0 ? nc : 0;
   }
-  return cache[dev] > 0 ? cache[dev] : 0;
+  return cache[dev];
 }
 
 // CTAs per row for the cluster top-k: the largest of 8, 4, 2 that runs the whole batch in
@@ -1047,7 +1057,8 @@ int topk_check(int length, int k, int sorted) {
 int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64_t idx_stride,
                 int batch, int length, int k, int sorted, void* out_idx, int idx_bytes,
                 int64_t oi_stride, float* out_val, int64_t ov_stride, void* ws, size_t ws_bytes,
-                cudaStream_t stream, float* kth_out, uint32_t* key_hist) {
+                cudaStream_t stream, float* kth_out, uint32_t* key_hist, int32_t* mirror,
+                int64_t mirror_stride) {
   int rc = topk_check(length, k, sorted);
   if (rc) return rc;
   const Plan p = make_plan(batch, length, k, key_hist != nullptr);
@@ -1074,6 +1085,8 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
       a.out_val_stride = ov_stride;
       a.hist = key_hist;
       a.hist_segs = (length + kTopkSegment - 1) / kTopkSegment;
+      a.mirror = mirror;
+      a.mirror_stride = mirror_stride;
       const int cap = c * kThreads;
       const int per = (length + cap - 1) / cap;
       if (c == 2) return launch_cluster<2>(a, batch, per, stream);
@@ -1124,6 +1137,8 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
       a.out_val = out_val;
       a.out_val_stride = ov_stride;
       a.kth_out = kth_out;
+      a.mirror = mirror;
+      a.mirror_stride = mirror_stride;
     } else {
       const int b = level & 1;
       a.sorted = 0;

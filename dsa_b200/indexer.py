@@ -24,7 +24,15 @@ def require_cuda(*tensors: torch.Tensor) -> None:
             raise ValueError("the B200 indexer kernels require CUDA tensors")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    """The cudaStream_t of torch's current stream on `device` (the raw-handle accessor
+    torch's own generated code uses; it costs a tenth of building a Stream object)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None
+                           else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -103,6 +111,32 @@ def score_dense(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor
     return out[0] if single else out
 
 
+_WORKSPACE_BYTES: dict[tuple[int, int, int, int], int] = {}
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def topk_workspace(device: torch.device, batch: int, length: int,
+                   k: int) -> tuple[torch.Tensor, int]:
+    """Scratch of the size ``tdsa_topk`` asks for -> (buffer, bytes).  Outside CUDA-graph
+    capture one buffer per (device, stream) is kept and reused: calls on one stream run in
+    order, so they can share it, and the next call needs no allocation (it only grows).
+    During a capture a fresh buffer is returned, which the graph keeps."""
+    key = (device.index, batch, length, k)
+    nbytes = _WORKSPACE_BYTES.get(key)
+    if nbytes is None:
+        with torch.cuda.device(device):  # the size depends on the device (cluster occupancy)
+            nbytes = capi.lib().tdsa_topk_workspace_bytes(batch, length, k)
+        _WORKSPACE_BYTES[key] = nbytes
+    if torch.cuda.is_current_stream_capturing():
+        return torch.empty(max(nbytes, 1), device=device, dtype=torch.uint8), nbytes
+    skey = (device.index, stream_ptr(device))
+    ws = _WORKSPACES.get(skey)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1), device=device, dtype=torch.uint8)
+        _WORKSPACES[skey] = ws
+    return ws, nbytes
+
+
 def topk(scores: torch.Tensor, k: int, *, sorted: bool = True,
          index_dtype: torch.dtype = torch.int64) -> tuple[torch.Tensor, torch.Tensor]:
     """Exact row-wise top-k with the reference's tie rule -> (indices, values).
@@ -113,25 +147,27 @@ def topk(scores: torch.Tensor, k: int, *, sorted: bool = True,
     require_cuda(scores)
     if scores.dtype != torch.float32:
         raise ValueError("scores must be float32")
-    single = scores.dim() == 1
-    s = scores.unsqueeze(0) if single else scores
-    if s.dim() != 2:
+    nd = scores.dim()
+    if nd not in (1, 2):
         raise ValueError("scores must be [L] or [B,L]")
-    if s.stride(-1) != 1:
-        s = s.contiguous()
-    bsz, length = s.shape
+    s = scores if scores.stride(-1) == 1 else scores.contiguous()
+    if nd == 1:
+        bsz, length, s_stride = 1, s.shape[0], s.shape[0]
+    else:
+        (bsz, length), s_stride = s.shape, s.stride(0)
     if not 0 < k <= length:
         raise ValueError(f"k={k} is invalid for {length} values")
     if index_dtype not in (torch.int32, torch.int64):
         raise ValueError("index_dtype must be int32 or int64")
-    idx = torch.empty(bsz, k, device=s.device, dtype=index_dtype)
-    val = torch.empty(bsz, k, device=s.device, dtype=torch.float32)
-    nbytes = capi.lib().tdsa_topk_workspace_bytes(bsz, length, k)
-    ws = torch.empty(max(nbytes, 1), device=s.device, dtype=torch.uint8)
-    capi.call("tdsa_topk", s.data_ptr(), s.stride(0), bsz, length, k, int(bool(sorted)),
-              idx.data_ptr(), idx.element_size(), idx.stride(0), val.data_ptr(), val.stride(0),
-              ws.data_ptr(), nbytes, stream_ptr(s.device))
-    return (idx[0], val[0]) if single else (idx, val)
+    dev = s.device
+    shape = (k,) if nd == 1 else (bsz, k)
+    idx = torch.empty(shape, device=dev, dtype=index_dtype)
+    val = torch.empty(shape, device=dev, dtype=torch.float32)
+    ws, nbytes = topk_workspace(dev, bsz, length, k)
+    capi.call("tdsa_topk", s.data_ptr(), s_stride, bsz, length, k, int(bool(sorted)),
+              idx.data_ptr(), idx.element_size(), k, val.data_ptr(), k, ws.data_ptr(), nbytes,
+              stream_ptr(dev))
+    return idx, val
 
 
 def merge_topk(cand_values: torch.Tensor, cand_indices: torch.Tensor, k: int, *,

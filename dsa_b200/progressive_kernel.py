@@ -16,8 +16,7 @@ import numpy as np
 import torch
 
 from . import _capi as capi
-from .indexer import (_DTYPES, prepare_keys, prepare_queries, prepare_weights, score_dense,
-                      stream_ptr)
+from .indexer import _DTYPES, score_dense, stream_ptr
 
 HEADS = 64
 HEAD_DIM = 128
@@ -95,21 +94,67 @@ def full_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys: torch
 
 
 # --------------------------------------------------------------------------- block kernels
+class _Single:
+    """One sequence's q [64,128], w [64] and keys [L,128] in the kernels' layout, with the
+    accessors of a batch of one (the batch strides of a single sequence are unused)."""
+
+    __slots__ = ("q", "w", "k", "length", "device", "dtype")
+
+    def __init__(self, queries, weights, keys):
+        k = keys
+        if not (k.stride(1) == 1 and k.stride(0) % 8 == 0 and k.data_ptr() % 16 == 0):
+            k = k.contiguous()
+            if k.data_ptr() % 16:
+                k = k.clone()
+        q = queries
+        if not (q.is_contiguous() and q.data_ptr() % 16 == 0):
+            q = q.contiguous()
+            if q.data_ptr() % 16:
+                q = q.clone()
+        w = weights
+        if not (w.dtype == torch.float32 and w.is_contiguous()):
+            w = w.to(torch.float32).contiguous()
+        self.q, self.w, self.k = q, w, k
+        self.length, self.device, self.dtype = k.shape[0], k.device, k.dtype
+
+    def head(self) -> tuple:
+        """(q, q stride, w, w stride, keys, batch stride, row stride, dtype, batch, length)"""
+        return (self.q.data_ptr(), 0, self.w.data_ptr(), 0, self.k.data_ptr(), 0,
+                self.k.stride(0), _DTYPES[self.dtype], 1, self.length)
+
+
 def _block_inputs(queries, weights, keys, block_size):
     if block_size not in (16, 32, 64, 128):
         raise ValueError("block_size must be 16, 32, 64 or 128 on B200")
-    keys = prepare_keys(keys.unsqueeze(0))
-    q = prepare_queries(queries.unsqueeze(0), keys.dtype)
-    w = prepare_weights(weights.unsqueeze(0))
-    return q, w, keys, math.ceil(keys.shape[1] / block_size)
+    one = _Single(queries, weights, keys)
+    return one, math.ceil(one.length / block_size)
+
+
+_BYTE_MASKS = (torch.bool, torch.int8, torch.uint8)
 
 
 def _mask(mask: torch.Tensor, device) -> torch.Tensor:
+    """A block mask the kernels read as one byte per block (nonzero = set): bool, int8 and
+    uint8 masks already on the device are passed as they are, others are converted."""
+    if mask.dtype in _BYTE_MASKS and mask.device == device and mask.is_contiguous():
+        return mask
     return mask.to(device=device, dtype=torch.int8).contiguous()
 
 
 def _head_ids(ids, device, count: int) -> torch.Tensor:
+    if (isinstance(ids, torch.Tensor) and ids.dtype == torch.int32 and ids.device == device
+            and ids.is_contiguous()):
+        return ids
     return torch.as_tensor(ids).to(device=device, dtype=torch.int32).contiguous()
+
+
+def _threshold(threshold, device) -> torch.Tensor:
+    """The promotion threshold as a one-element float32 device tensor (a scalar is copied
+    in; a device tensor is read by the kernel in place)."""
+    if (isinstance(threshold, torch.Tensor) and threshold.dtype == torch.float32
+            and threshold.device == device and threshold.numel() == 1):
+        return threshold
+    return torch.as_tensor(threshold, device=device, dtype=torch.float32).reshape(1)
 
 
 def _selected_heads(selected_heads, device) -> torch.Tensor:
@@ -130,18 +175,17 @@ def h8_block_max_triton(queries: torch.Tensor, weights: torch.Tensor, keys: torc
                         block_size: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
     """:378-404 -- 8-head partial scores on cold blocks (-inf elsewhere) and block maxima."""
     _check_cuda_inputs(queries, weights, keys)
-    q, w, k, nblocks = _block_inputs(queries, weights, keys, block_size)
+    one, nblocks = _block_inputs(queries, weights, keys, block_size)
     if cold_blocks.numel() != nblocks:
         raise ValueError("cold block mask length mismatch")
-    selected = _selected_heads(selected_heads, k.device)
-    cold = _mask(cold_blocks, k.device)
-    length = k.shape[1]
-    partial = torch.empty(length, device=k.device, dtype=torch.float32)
-    maxima = torch.empty(nblocks, device=k.device, dtype=torch.float32)
-    _call_blocks("tdsa_h8_block_max", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
-                 k.data_ptr(), k.stride(0), k.stride(1), _DTYPES[k.dtype], 1, length,
-                 block_size, selected.data_ptr(), cold.data_ptr(), partial.data_ptr(), length,
-                 maxima.data_ptr(), nblocks, stream_ptr(k.device))
+    dev = one.device
+    selected = _selected_heads(selected_heads, dev)
+    cold = _mask(cold_blocks, dev)
+    partial = torch.empty(one.length, device=dev, dtype=torch.float32)
+    maxima = torch.empty(nblocks, device=dev, dtype=torch.float32)
+    _call_blocks("tdsa_h8_block_max", *one.head(), block_size, selected.data_ptr(),
+                 cold.data_ptr(), partial.data_ptr(), one.length, maxima.data_ptr(), nblocks,
+                 stream_ptr(dev))
     return partial, maxima
 
 
@@ -149,16 +193,14 @@ def masked_full_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys
                               keep_blocks: torch.Tensor, *, block_size: int = 64) -> torch.Tensor:
     """:407-424 -- dense scores on kept blocks, -inf elsewhere (dropped blocks are not read)."""
     _check_cuda_inputs(queries, weights, keys)
-    q, w, k, nblocks = _block_inputs(queries, weights, keys, block_size)
+    one, nblocks = _block_inputs(queries, weights, keys, block_size)
     if keep_blocks.numel() != nblocks:
         raise ValueError("keep block mask length mismatch")
-    keep = _mask(keep_blocks, k.device)
-    length = k.shape[1]
-    out = torch.empty(length, device=k.device, dtype=torch.float32)
-    _call_blocks("tdsa_masked_dense", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
-                 k.data_ptr(), k.stride(0), k.stride(1), _DTYPES[k.dtype], 1, length,
-                 block_size, keep.data_ptr(), nblocks, out.data_ptr(), length,
-                 stream_ptr(k.device))
+    dev = one.device
+    keep = _mask(keep_blocks, dev)
+    out = torch.empty(one.length, device=dev, dtype=torch.float32)
+    _call_blocks("tdsa_masked_dense", *one.head(), block_size, keep.data_ptr(), nblocks,
+                 out.data_ptr(), one.length, stream_ptr(dev))
     return out
 
 
@@ -174,8 +216,8 @@ def progressive_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys
     as in the reference).
     """
     _check_cuda_inputs(queries, weights, keys)
-    q, w, k, nblocks = _block_inputs(queries, weights, keys, block_size)
-    dev = k.device
+    one, nblocks = _block_inputs(queries, weights, keys, block_size)
+    dev = one.device
     if remaining_heads is None:
         selected, remaining = split_head_ids(selected_heads.cpu())
         selected, remaining = selected.to(dev), remaining.to(dev)
@@ -188,16 +230,14 @@ def progressive_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys
     if direct_full_blocks.numel() != nblocks:
         raise ValueError("direct full block mask length mismatch")
     direct = _mask(direct_full_blocks, dev)
-    thr = torch.as_tensor(threshold, device=dev, dtype=torch.float32).reshape(1)
-    length = k.shape[1]
+    thr = _threshold(threshold, dev)
+    length = one.length
     scores = torch.empty(length, device=dev, dtype=torch.float32)
     accepted = torch.empty(nblocks, device=dev, dtype=torch.int8)
     block_max = torch.empty(nblocks, device=dev, dtype=torch.float32)
-    _call_blocks("tdsa_progressive_h8", q.data_ptr(), q.stride(0), w.data_ptr(), w.stride(0),
-                 k.data_ptr(), k.stride(0), k.stride(1), _DTYPES[k.dtype], 1, length,
-                 block_size, selected.data_ptr(), remaining.data_ptr(), direct.data_ptr(),
-                 thr.data_ptr(), scores.data_ptr(), length, accepted.data_ptr(),
-                 block_max.data_ptr(), nblocks, stream_ptr(dev))
+    _call_blocks("tdsa_progressive_h8", *one.head(), block_size, selected.data_ptr(),
+                 remaining.data_ptr(), direct.data_ptr(), thr.data_ptr(), scores.data_ptr(),
+                 length, accepted.data_ptr(), block_max.data_ptr(), nblocks, stream_ptr(dev))
     if not compact:
         return ProgressiveResult(scores, accepted, block_max)
     packed = torch.empty(length, device=dev, dtype=torch.float32)
@@ -215,14 +255,24 @@ def two_pass_scores_triton(queries: torch.Tensor, weights: torch.Tensor, keys: t
                            selected_heads: torch.Tensor, direct_full_blocks: torch.Tensor,
                            threshold: float | torch.Tensor, *,
                            block_size: int = 64) -> ProgressiveResult:
-    """:478-497 -- H8 block max on cold blocks, then dense scoring of the accepted ones."""
-    cold = ~direct_full_blocks.to(torch.bool)
-    _, maxima = h8_block_max_triton(queries, weights, keys, selected_heads, cold,
-                                    block_size=block_size)
-    thr = torch.as_tensor(threshold, device=keys.device, dtype=torch.float32)
-    accepted = direct_full_blocks.to(device=keys.device, dtype=torch.bool) | (maxima >= thr)
-    scores = masked_full_scores_triton(queries, weights, keys, accepted, block_size=block_size)
-    return ProgressiveResult(scores, accepted.to(torch.int8), maxima)
+    """:478-497 -- H8 block max on cold blocks, then dense scoring of the accepted ones
+    (direct, or probe max >= threshold): one C call (tdsa_two_pass), two launches."""
+    _check_cuda_inputs(queries, weights, keys)
+    one, nblocks = _block_inputs(queries, weights, keys, block_size)
+    if direct_full_blocks.numel() != nblocks:
+        raise ValueError("direct full block mask length mismatch")
+    dev = one.device
+    selected = _selected_heads(selected_heads, dev)
+    direct = _mask(direct_full_blocks, dev)
+    thr = _threshold(threshold, dev)
+    length = one.length
+    scores = torch.empty(length, device=dev, dtype=torch.float32)
+    accepted = torch.empty(nblocks, device=dev, dtype=torch.int8)
+    maxima = torch.empty(nblocks, device=dev, dtype=torch.float32)
+    _call_blocks("tdsa_two_pass", *one.head(), block_size, selected.data_ptr(),
+                 direct.data_ptr(), thr.data_ptr(), scores.data_ptr(), length,
+                 accepted.data_ptr(), maxima.data_ptr(), nblocks, stream_ptr(dev))
+    return ProgressiveResult(scores, accepted, maxima)
 
 
 # --------------------------------------------------------------------------- torch-named

@@ -11,7 +11,7 @@ from __future__ import annotations
 import torch
 
 from . import _capi as capi
-from .indexer import HEAD_DIM, HEADS, require_cuda, score_dense
+from .indexer import HEAD_DIM, HEADS, require_cuda, score_dense, stream_ptr
 
 
 def score_encoded(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor, *,
@@ -111,7 +111,7 @@ class QueryProjector:
             self.wq = torch.empty(nbytes // 2, device=dev, dtype=wq.dtype)
             capi.check(lib.tdsa_pack_query_weights(wq.data_ptr(), wq.stride(0), self.hidden,
                                                    self.wq.data_ptr(),
-                                                   torch.cuda.current_stream(dev).cuda_stream))
+                                                   stream_ptr(dev)))
             self._wq_stride = 0
         else:
             self.wq, self._wq_stride = wq, wq.stride(0)
@@ -141,7 +141,7 @@ class QueryProjector:
                             (HEADS * HEAD_DIM) ** -0.5,
                             self.qraw.data_ptr() if self.qraw is not None else None,
                             HEADS * HEAD_DIM,
-                            torch.cuda.current_stream(self.q.device).cuda_stream))
+                            stream_ptr(self.q.device)))
         return self.q, self.w
 
 
@@ -223,5 +223,5 @@ class KeyAppender:
             self.norm_bias.data_ptr() if self.norm_bias is not None else None, self.eps,
             positions.data_ptr(), slots.data_ptr() if slots is not None else None,
             cache.data_ptr(), cache.stride(0), cache.stride(1), cache.shape[1], self._dt, batch,
-            self.rope_dim, self.theta, torch.cuda.current_stream(cache.device).cuda_stream))
+            self.rope_dim, self.theta, stream_ptr(cache.device)))
         return cache
