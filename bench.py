@@ -860,14 +860,26 @@ def run_cfg3(device: torch.device, steps: int) -> dict:
     (per-step average, host launch time included, as a decode loop issues them).  The exact
     top-k is compared with dense at every step.  Bytes read per step count the keys actually
     scored (256 B each) and 8 B of block metadata per visited block, the seed gathers
-    included.  A second, block-structured trace (10% of 64-key blocks at norm x3, the rest
-    x0.05; slowly drifting queries, rho 0.999; positive weights) is a case where the
-    certified bound prunes blocks unread."""
+    included.  A second, block-structured trace (25% of 64-key blocks at norm x3 -- more
+    keys than k -- the rest x0.05; slowly drifting queries, rho 0.999; positive weights) is a
+    case where the certified bound prunes blocks unread.  `batched` repeats both traces at a
+    config-4 shape (64 sequences of 32768 keys, block 64), where the step is bound by key
+    bytes rather than launch latency."""
     from dsa_b200.indexer import ScoreTopkPlan
     from dsa_b200.progressive_exact import ExactProgressivePlan
 
     l0, k, data_block = 16384, 2048, 64
     res = {}
+    # about 0.2 s of scoring first, so that both traces are timed at steady clocks
+    wq = torch.randn(1, 64, 128, device=device).to(torch.bfloat16)
+    wk = torch.randn(1, l0, 128, device=device).to(torch.bfloat16)
+    wplan = ScoreTopkPlan(wq, torch.randn(1, 64, device=device), wk, k, sorted=False)
+    t_end = time.perf_counter() + 0.2
+    while time.perf_counter() < t_end:
+        for _ in range(50):
+            wplan.run()
+        torch.cuda.synchronize(device)
+    del wplan, wq, wk
     for trace in ("iid", "structured"):
         g = torch.Generator().manual_seed(0)
         q = torch.randn(64, 128, generator=g) / math.sqrt(128)
@@ -879,7 +891,7 @@ def run_cfg3(device: torch.device, steps: int) -> dict:
             rho, innov = 0.999, 0.02
             w = (torch.randn(64, generator=g).abs() / 8).to(device)
             nb = (l0 + steps + data_block - 1) // data_block
-            scale = torch.where(torch.rand(nb, generator=g) < 0.1, 3.0, 0.05)
+            scale = torch.where(torch.rand(nb, generator=g) < 0.25, 3.0, 0.05)
             keys = torch.randn(l0 + steps, 128, generator=g) * scale.repeat_interleave(
                 data_block)[:l0 + steps, None]
         keys = keys.to(torch.bfloat16).to(device).unsqueeze(0)
@@ -942,6 +954,9 @@ def run_cfg3(device: torch.device, steps: int) -> dict:
                 "blocks_visited": st["blocks_visited"]}
         res[trace] = {"dense_us_per_step": dense_us, "block_sizes": sweep}
     head = res["iid"]["block_sizes"]["64"]
+    batched = {trace: exact_batched(device, trace) for trace in ("iid", "structured")}
+    sketch = {f"{trace}_b{b}_l{n}": sketch_step(device, trace, b, n)
+              for trace in ("iid", "structured") for b, n in ((1, 16384), (64, 32768))}
     return {
         "metric": "exact progressive top-2048 decode step latency (config 3)",
         "value": head["exact_us_per_step"], "unit": "us", "higher_is_better": False,
@@ -953,7 +968,178 @@ def run_cfg3(device: torch.device, steps: int) -> dict:
                                              for r in res.values()
                                              for v in r["block_sizes"].values()),
         "traces": res,
+        "batched": batched,
+        "sketch": sketch,
     }
+
+
+def sketch_step(device: torch.device, trace: str, batch: int, length: int, steps: int = 16,
+                k: int = 2048) -> dict:
+    """The certified INT8 sketch top-k (dsa_b200.sketch) against dense score + top-k over
+    decode steps of a growing cache: each step appends one key per sequence and sketches it
+    (tdsa_sketch_keys), then SketchTopkPlan.run; dense runs one ScoreTopkPlan per length.
+    i.i.d. keys with AR(1) rho 0.95 queries, or the block-structured cache (25% of 64-key
+    blocks at norm x3, rho 0.999 drift).  Bytes per step: 136 per key (the sketch) plus 256
+    per key read in full; dense reads 256 per key.  CUDA events over `steps` steps."""
+    from dsa_b200.indexer import ScoreTopkPlan
+    from dsa_b200.sketch import BYTES_PER_KEY, KeySketch, SketchTopkPlan
+
+    g = torch.Generator(device=device)
+    g.manual_seed(44)
+    total = length + steps
+    keys = torch.randn(batch, total, 128, generator=g, device=device)
+    if trace == "iid":
+        rho, innov = 0.95, math.sqrt(1 - 0.95 ** 2)
+        w = torch.randn(batch, 64, generator=g, device=device) / 8
+    else:
+        rho, innov = 0.999, 0.02
+        w = torch.randn(batch, 64, generator=g, device=device).abs() / 8
+        nb = (total + 63) // 64
+        scale = torch.where(torch.rand(batch, nb, generator=g, device=device) < 0.25, 3.0, 0.05)
+        keys *= scale.repeat_interleave(64, dim=1)[:, :total, None]
+    keys = keys.to(torch.bfloat16)
+    q = torch.randn(batch, 64, 128, generator=g, device=device) / math.sqrt(128)
+    qs = []
+    for _ in range(steps):
+        q = rho * q + innov * torch.randn(batch, 64, 128, generator=g, device=device) / \
+            math.sqrt(128)
+        qs.append(q.to(torch.bfloat16))
+    qbuf = qs[0].clone()
+    dense = [ScoreTopkPlan(qbuf, w, keys[:, :length + t + 1], k, sorted=False)
+             for t in range(steps)]
+    sk = KeySketch(batch, total, device)
+    sk.update(keys, 0, length)
+    plan = SketchTopkPlan(qbuf, w, keys, sk, k, sorted=False)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def run_dense(record):
+        out = []
+        for t in range(steps):
+            qbuf.copy_(qs[t])
+            idx = dense[t].run()[0]
+            if record:
+                out.append(idx.clone())
+        return out
+
+    def run_sketch(first, record):
+        out = []
+        for t in range(steps):
+            qbuf.copy_(qs[t])
+            n = length + t + 1
+            if first:
+                sk.update(keys, n - 1, n)
+            idx = plan.run(n)[0]
+            if record:
+                out.append(idx.clone())
+        return out
+
+    run_dense(False)
+    run_sketch(True, False)  # sketches the appended keys; warm
+    torch.cuda.synchronize(device)
+    e[0].record()
+    want = run_dense(True)
+    e[1].record()
+    c0 = plan.counters.clone()
+    e[2].record()
+    got = run_sketch(False, True)
+    e[3].record()
+    torch.cuda.synchronize(device)
+    c = (plan.counters - c0).sum(dim=0).tolist()
+    keys_total = batch * sum(length + t + 1 for t in range(steps))
+    # the sketch of the appended key, timed on its own
+    e2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    e2[0].record()
+    for t in range(steps):
+        sk.update(keys, length + t, length + t + 1)
+    e2[1].record()
+    torch.cuda.synchronize(device)
+    del dense, plan, sk
+    return {"sketch_us_per_step": e[2].elapsed_time(e[3]) * 1e3 / steps,
+            "sketch_append_us": e2[0].elapsed_time(e2[1]) * 1e3 / steps,
+            "dense_us_per_step": e[0].elapsed_time(e[1]) * 1e3 / steps,
+            "sketch_equals_dense_every_step": all(torch.equal(x, y) for x, y in zip(got, want)),
+            "keys_read_fraction": c[0] / keys_total,
+            "candidate_fraction": c[1] / keys_total,
+            "bytes_per_key": BYTES_PER_KEY + 256 * c[0] / keys_total,
+            "dense_bytes_per_key": 256,
+            "batch": batch, "seq_len": length, "k": k, "steps": steps}
+
+
+def exact_batched(device: torch.device, trace: str, batch: int = 64, length: int = 32768,
+                  steps: int = 16, k: int = 2048, bs: int = 64) -> dict:
+    """The exact progressive top-k at a config-4 shape (B = 64, L = 32768 growing by one key
+    per step, block 64) against dense score + top-k (one ScoreTopkPlan per length), on
+    i.i.d. keys (AR(1) rho 0.95 queries) or the block-structured cache of run_cfg3 (25% of
+    blocks at norm x3, rho 0.999 drift), CUDA events over `steps` steps each."""
+    from dsa_b200.indexer import ScoreTopkPlan
+    from dsa_b200.progressive_exact import ExactProgressivePlan
+
+    g = torch.Generator(device=device)
+    g.manual_seed(33)
+    total = length + steps
+    keys = torch.randn(batch, total, 128, generator=g, device=device)
+    if trace == "iid":
+        rho, innov = 0.95, math.sqrt(1 - 0.95 ** 2)
+        w = torch.randn(batch, 64, generator=g, device=device) / 8
+    else:
+        rho, innov = 0.999, 0.02
+        w = torch.randn(batch, 64, generator=g, device=device).abs() / 8
+        nb = (total + bs - 1) // bs
+        scale = torch.where(torch.rand(batch, nb, generator=g, device=device) < 0.25, 3.0, 0.05)
+        keys *= scale.repeat_interleave(bs, dim=1)[:, :total, None]
+    keys = keys.to(torch.bfloat16)
+    q = torch.randn(batch, 64, 128, generator=g, device=device) / math.sqrt(128)
+    qs = []
+    for _ in range(steps + 1):
+        qs.append(q.to(torch.bfloat16))
+        q = rho * q + innov * torch.randn(batch, 64, 128, generator=g, device=device) / \
+            math.sqrt(128)
+    qbuf = qs[0].clone()
+    dense = [ScoreTopkPlan(qbuf, w, keys[:, :length + t + 1], k, sorted=False)
+             for t in range(steps)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def run_dense(record: bool):
+        out = []
+        for t in range(steps):
+            qbuf.copy_(qs[t + 1])
+            idx = dense[t].run()[0]
+            if record:
+                out.append(idx.clone())
+        return out
+
+    run_dense(False)
+    torch.cuda.synchronize(device)
+    e[0].record()
+    want = run_dense(True)
+    e[1].record()
+    torch.cuda.synchronize(device)
+    qbuf.copy_(qs[0])
+    ex = ExactProgressivePlan(qbuf, w, keys, k, block_size=bs, sorted=False)
+    ex.init(length)
+    torch.cuda.synchronize(device)
+    st0 = ex.stats()
+    got = []
+    e[2].record()
+    for t in range(steps):
+        qbuf.copy_(qs[t + 1])
+        got.append(ex.step(length + t + 1)[0].clone())
+    e[3].record()
+    torch.cuda.synchronize(device)
+    st = ex.stats()
+    scored = sum(b["keys_scored"] - a["keys_scored"] for a, b in zip(st0, st))
+    keys_total = sum(b["keys_total"] - a["keys_total"] for a, b in zip(st0, st))
+    visited = sum(b["blocks_visited"] - a["blocks_visited"] for a, b in zip(st0, st))
+    pruned = sum(b["blocks_pruned"] - a["blocks_pruned"] for a, b in zip(st0, st))
+    del dense, ex
+    return {"exact_us_per_step": e[2].elapsed_time(e[3]) * 1e3 / steps,
+            "dense_us_per_step": e[0].elapsed_time(e[1]) * 1e3 / steps,
+            "exact_equals_dense_every_step": all(torch.equal(x, y) for x, y in zip(got, want)),
+            "keys_read_fraction": scored / max(1, keys_total),
+            "key_bytes_read_per_step": (scored * 256 + visited * 8) / steps,
+            "dense_key_bytes_per_step": keys_total * 256 / steps,
+            "blocks_pruned_fraction": pruned / max(1, visited),
+            "batch": batch, "seq_len": length, "block_size": bs, "steps": steps}
 
 
 def run_cfg5(args, rank: int, world: int, device: torch.device) -> dict | None:

@@ -107,6 +107,11 @@ SIGNATURES: dict[str, tuple] = {
     "tdsa_progressive_h8": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp,
                                   vp, vp, i64, vp, vp, i64, vp]),
     "tdsa_compact_blocks": (i32, [vp, i64, vp, i64, i32, i32, i32, vp, vp, i64, vp, vp]),
+    "tdsa_sketch_keys": (i32, [vp, i64, i64, i32, i32, i32, i32, vp, i64, vp, vp, i64, vp]),
+    "tdsa_sketch_topk_workspace_bytes": (sz, [i32, i32, i32]),
+    "tdsa_sketch_workspace_offsets": (i32, [i32, i32, i32, C.POINTER(C.c_int64)]),
+    "tdsa_sketch_topk": (i32, [vp, i64, vp, i64, vp, i64, i64, i32, vp, i64, vp, vp, i64, i32,
+                               i32, i32, i32, i32, vp, i32, i64, vp, i64, vp, vp, sz, vp]),
     "tdsa_exact_state_bytes": (sz, [i32, i32, i32, i32]),
     "tdsa_exact_init": (i32, [vp, sz, vp, i64, vp, i64, vp, i64, i64, i32, i32, i32, i32, i32, i32,
                               i32, vp, i32, i64, vp, i64, vp]),

@@ -889,6 +889,80 @@ int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_
                                static_cast<cudaStream_t>(stream));
 }
 
+int tdsa_sketch_keys(const void* keys, int64_t k_batch_stride, int64_t k_row_stride, int dtype,
+                     int batch, int first, int length, int8_t* sketch,
+                     int64_t sketch_batch_stride, float* scales, void* bounds,
+                     int64_t scale_batch_stride, void* stream) {
+  if (!keys || !sketch || !scales || !bounds) return fail(TDSA_ERR_INVALID, "null pointer argument");
+  if (dtype != TDSA_BF16 && dtype != TDSA_F16)
+    return fail(TDSA_ERR_UNSUPPORTED, "the key sketch takes bf16/fp16 keys");
+  if (batch < 1 || batch > 65535 || first < 0 || first > length)
+    return fail(TDSA_ERR_INVALID, "need batch in [1, 65535] and 0 <= first <= length");
+  if (k_row_stride < kHeadDim || (batch > 1 && (k_batch_stride < static_cast<int64_t>(length) * k_row_stride ||
+                                                sketch_batch_stride < static_cast<int64_t>(length) * kHeadDim ||
+                                                scale_batch_stride < length)))
+    return fail(TDSA_ERR_INVALID, "strides overlap the rows of one sequence");
+  if (!aligned16(keys) || k_row_stride % 8 || (batch > 1 && k_batch_stride % 8) ||
+      !aligned16(sketch) || (batch > 1 && sketch_batch_stride % 16) ||
+      (reinterpret_cast<uintptr_t>(scales) & 3u) || (reinterpret_cast<uintptr_t>(bounds) & 3u))
+    return fail(TDSA_ERR_ALIGN, "keys and the sketch need 16-byte aligned rows (TMA)");
+  return launch_sketch_keys(keys, k_batch_stride, k_row_stride, dtype, batch, first, length,
+                            sketch, sketch_batch_stride, scales, bounds, scale_batch_stride,
+                            static_cast<cudaStream_t>(stream));
+}
+
+size_t tdsa_sketch_topk_workspace_bytes(int batch, int max_length, int k) {
+  if (batch < 1 || max_length < 1 || k < 1 || k > max_length) return 0;
+  return sketch_workspace_bytes(batch, max_length, k);
+}
+
+int tdsa_sketch_workspace_offsets(int batch, int max_length, int k, int64_t* offsets) {
+  if (!offsets || batch < 1 || max_length < 1 || k < 1 || k > max_length)
+    return fail(TDSA_ERR_INVALID, "bad geometry");
+  sketch_workspace_offsets(batch, max_length, k, offsets);
+  return TDSA_OK;
+}
+
+int tdsa_sketch_topk(const void* queries, int64_t q_batch_stride, const float* weights,
+                     int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                     int64_t k_row_stride, int dtype, const int8_t* sketch,
+                     int64_t sketch_batch_stride, const float* scales, const void* bounds,
+                     int64_t scale_batch_stride, int batch, int length, int max_length, int k,
+                     int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                     float* out_values, int64_t val_batch_stride, uint64_t* stats,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_score_args(queries, q_batch_stride, weights, w_batch_stride, keys,
+                            k_batch_stride, k_row_stride, dtype, batch, length, nullptr, 0,
+                            false);
+  if (rc) return rc;
+  if (dtype == TDSA_F32) return fail(TDSA_ERR_UNSUPPORTED, "the key sketch takes bf16/fp16 keys");
+  if (length < k || length > max_length)
+    return fail(TDSA_ERR_INVALID, "need k <= length <= max_length");
+  rc = topk_check(length, k, sorted);
+  if (rc) return rc;
+  rc = check_topk_out(out_indices, index_bytes, idx_batch_stride, out_values, val_batch_stride,
+                      batch, k);
+  if (rc) return rc;
+  if (!out_indices) return fail(TDSA_ERR_INVALID, "out_indices is null");
+  if (!sketch || !scales || !bounds) return fail(TDSA_ERR_INVALID, "null sketch argument");
+  if (!aligned16(sketch) || (batch > 1 && sketch_batch_stride % 16) ||
+      (reinterpret_cast<uintptr_t>(scales) & 3u) || (reinterpret_cast<uintptr_t>(bounds) & 3u))
+    return fail(TDSA_ERR_ALIGN, "the sketch needs 16-byte aligned rows (TMA)");
+  if (batch > 1 && (sketch_batch_stride < static_cast<int64_t>(length) * kHeadDim ||
+                    scale_batch_stride < length))
+    return fail(TDSA_ERR_INVALID, "sketch strides overlap the rows of one sequence");
+  const size_t need = sketch_workspace_bytes(batch, max_length, k);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(TDSA_ERR_WORKSPACE,
+                "workspace missing, unaligned (256 B) or smaller than tdsa_sketch_topk_workspace_bytes");
+  return run_sketch_topk(queries, q_batch_stride, weights, w_batch_stride, keys, k_batch_stride,
+                         k_row_stride, dtype, sketch, sketch_batch_stride, scales, bounds,
+                         scale_batch_stride, batch, length, max_length, k, sorted ? 1 : 0,
+                         out_indices, index_bytes, idx_batch_stride, out_values,
+                         val_batch_stride, reinterpret_cast<unsigned long long*>(stats),
+                         workspace, static_cast<cudaStream_t>(stream));
+}
+
 size_t tdsa_exact_state_bytes(int batch, int max_length, int k, int block_size) {
   if (batch < 1 || max_length < 1 || k < 1 || k > max_length ||
       (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128))

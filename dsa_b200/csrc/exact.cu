@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
+#include "tiles.cuh"
 
 namespace tdsa {
 
@@ -98,68 +99,12 @@ struct PrepArgs {
   int init;  // 1: every block is scored (first step)
 };
 
-__device__ __forceinline__ float qelem(const void* q, int dtype, int64_t off) {
-  return dtype == TDSA_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(q)[off])
-                            : __half2float(static_cast<const __half*>(q)[off]);
-}
-
-// Ordered compaction of the blocks with flag == want into tiles of bpt blocks.
-__device__ void emit_tiles(const int8_t* flag, int nb, int want, int bpt, int seq,
-                           int32_t* tile_seq, int32_t* tile_blk, int32_t* counter,
-                           uint32_t* wtot, uint32_t* sbase) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // count
-  uint32_t cnt = 0;
-  for (int b = threadIdx.x; b < nb; b += kThreads) cnt += flag[b] == want;
-  cnt = __reduce_add_sync(0xffffffffu, cnt);
-  if (lane == 0) wtot[warp] = cnt;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t total = 0;
-    for (int i = 0; i < 32; ++i) total += wtot[i];
-    const int ntiles = static_cast<int>((total + bpt - 1) / bpt);
-    sbase[0] = ntiles ? static_cast<uint32_t>(atomicAdd(counter, ntiles)) : 0u;
-    sbase[1] = 0;  // running position
-    sbase[2] = total;
-  }
-  __syncthreads();
-  const uint32_t tile0 = sbase[0], total = sbase[2];
-  // ordered positions, 1024 blocks per round
-  for (int base = 0; base < nb; base += kThreads) {
-    const int b = base + threadIdx.x;
-    const bool take = b < nb && flag[b] == want;
-    const unsigned bal = __ballot_sync(0xffffffffu, take);
-    if (lane == 0) wtot[warp] = __popc(bal);
-    __syncthreads();
-    uint32_t before = 0, round = 0;
-    for (int i = 0; i < 32; ++i) {
-      const uint32_t c = wtot[i];
-      before += i < warp ? c : 0u;
-      round += c;
-    }
-    const uint32_t pos = sbase[1] + before + __popc(bal & ((1u << lane) - 1u));
-    if (take) {
-      const uint32_t t = tile0 + pos / bpt;
-      tile_blk[static_cast<int64_t>(t) * bpt + pos % bpt] = b;
-      if (pos % bpt == 0) tile_seq[t] = seq;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) sbase[1] += round;
-    __syncthreads();
-  }
-  // pad the last tile with empty slots
-  if (threadIdx.x < bpt && total % bpt) {
-    const uint32_t pos = total + threadIdx.x;
-    if (pos % bpt != 0 && pos / bpt == (total - 1) / bpt)
-      tile_blk[static_cast<int64_t>(tile0 + pos / bpt) * bpt + pos % bpt] = -1;
-  }
-}
-
 __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs a) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
   __shared__ double coeff[64];
   __shared__ double c_total;
+  static_assert(kThreads == 8192 / 8, "one thread per 8 query elements");
   __shared__ uint32_t wtot[32];
   __shared__ uint32_t sbase[4];
   const int seq = blockIdx.x;
@@ -176,50 +121,59 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
       fold_key_norm(a.keys, static_cast<int64_t>(seq) * a.k_bs, a.k_rs, a.dtype, key, a.bs,
                     a.maxsq + brow);
   }
-  if (!a.init) {
-    // coefficient: 16 threads per head, 8 dims each, float64
-    const int h = threadIdx.x >> 4, sub = threadIdx.x & 15;
-    double dd = 0.0, pp = 0.0, nn = 0.0;
-    for (int i = 0; i < 8; ++i) {
-      const int d = sub + 16 * i;
-      const double qn = qelem(a.q, a.dtype, static_cast<int64_t>(seq) * a.q_bs + h * 128 + d);
-      const double qp = qelem(a.qprev, a.dtype, static_cast<int64_t>(seq) * 8192 + h * 128 + d);
-      dd += (qn - qp) * (qn - qp);
-      pp += qp * qp;
-      nn += qn * qn;
-    }
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) {
-      dd += __shfl_xor_sync(0xffffffffu, dd, o);
-      pp += __shfl_xor_sync(0xffffffffu, pp, o);
-      nn += __shfl_xor_sync(0xffffffffu, nn, o);
-    }
-    if (sub == 0) {
-      const double wn = a.w[static_cast<int64_t>(seq) * a.w_bs + h];
-      const double wp = a.wprev[static_cast<int64_t>(seq) * 64 + h];
-      const double nqp = sqrt(pp), nqn = sqrt(nn), ndq = sqrt(dd);
-      coeff[h] = fabs(wn - wp) * nqp + fabs(wn) * ndq + kGamma * (fabs(wn) * nqn + fabs(wp) * nqp);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double c = 0.0;
-      for (int i = 0; i < 64; ++i) c += coeff[i];
-      c_total = c * (1.0 + 0x1p-40);
-    }
-  }
-  __syncthreads();  // every read of qprev / wprev is done
-  // keep q (16-bit bits) and w for the next step's coefficient (rows are 16-byte aligned:
-  // the scoring kernels' TMA rules)
+  // Thread t owns q elements [8t, 8t + 8) (one 16-byte load; rows are 16-byte aligned: the
+  // scoring kernels' TMA rules): 16 threads per head.  It reads the previous step's copy of
+  // the same elements, then stores the current ones in its place for the next step.
   {
-    const uint4* qs = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.q) +
-                                                     static_cast<int64_t>(seq) * a.q_bs);
-    uint4* qd = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.qprev) +
-                                         static_cast<int64_t>(seq) * 8192);
-    for (int i = threadIdx.x; i < 8192 / 8; i += kThreads) qd[i] = qs[i];
-    if (threadIdx.x < 64)
-      a.wprev[static_cast<int64_t>(seq) * 64 + threadIdx.x] =
-          a.w[static_cast<int64_t>(seq) * a.w_bs + threadIdx.x];
+    const int h = threadIdx.x >> 4;
+    const uint4 qv = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.q) +
+                                                    static_cast<int64_t>(seq) * a.q_bs)[threadIdx.x];
+    uint4* qp4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.qprev) +
+                                          static_cast<int64_t>(seq) * 8192) + threadIdx.x;
+    const float wn = a.w[static_cast<int64_t>(seq) * a.w_bs + h];
+    float* wp_row = a.wprev + static_cast<int64_t>(seq) * 64;
+    if (!a.init) {
+      // coefficient in float64
+      const uint4 pv = *qp4;
+      const double wp = wp_row[h];
+      const uint32_t nw[4] = {qv.x, qv.y, qv.z, qv.w}, pw[4] = {pv.x, pv.y, pv.z, pv.w};
+      double dd = 0.0, pp = 0.0, nn = 0.0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint16_t nb16 = static_cast<uint16_t>(nw[j >> 1] >> (16 * (j & 1)));
+        const uint16_t pb16 = static_cast<uint16_t>(pw[j >> 1] >> (16 * (j & 1)));
+        const double qn = a.dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(nb16) << 16)
+                                               : __half2float(__ushort_as_half(nb16));
+        const double qpv = a.dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(pb16) << 16)
+                                                : __half2float(__ushort_as_half(pb16));
+        dd += (qn - qpv) * (qn - qpv);
+        pp += qpv * qpv;
+        nn += qn * qn;
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        dd += __shfl_xor_sync(0xffffffffu, dd, o);
+        pp += __shfl_xor_sync(0xffffffffu, pp, o);
+        nn += __shfl_xor_sync(0xffffffffu, nn, o);
+      }
+      if ((threadIdx.x & 15) == 0) {
+        const double nqp = sqrt(pp), nqn = sqrt(nn), ndq = sqrt(dd);
+        coeff[h] = fabs(wn - wp) * nqp + fabs(wn) * ndq +
+                   kGamma * (fabs(wn) * nqn + fabs(wp) * nqp);
+      }
+    }
+    *qp4 = qv;
+    __syncthreads();  // every read of wprev (and coeff written)
+    if ((threadIdx.x & 15) == 0) wp_row[h] = wn;
+    if (!a.init && threadIdx.x < 32) {
+      // the 64 head terms summed in a fixed order (lane l: heads l and l + 32)
+      double c = coeff[threadIdx.x] + coeff[threadIdx.x + 32];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+      if (threadIdx.x == 0) c_total = c * (1.0 + 0x1p-40);
+    }
   }
+  __syncthreads();
   // the previous step's state update, then this step's bounds and flags (block b is
   // updated and read by the same thread)
   for (int b = threadIdx.x; b < nb; b += kThreads) {
@@ -374,13 +328,23 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
     for (int i = threadIdx.x; i < kHistCopies * kKeyHistBins; i += kThreads) hcopies[i] = 0u;
     __syncthreads();
     uint32_t* mine = hcopies + (warp & (kHistCopies - 1)) * kKeyHistBins;
-    const int span = (a.length + 31) & ~31;
-    for (int i = threadIdx.x; i < span; i += kThreads) {
-      const bool scored = i < a.length && flag[i / a.bs] == 1;
-      const float v = scored ? srow[i] : -INFINITY;
-      const uint32_t key = float_to_key(v);
-      const bool in = scored && (key >> 20) == bin1;
-      add_to_bin(mine, in, (key >> 8) & 0xFFFu);
+    // 8 independent loads per thread in flight (the pass is bound by load latency)
+    constexpr int kUnroll = 8;
+    for (int base = 0; base < a.length; base += kThreads * kUnroll) {
+      float v[kUnroll];
+      bool scored[kUnroll];
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) {
+        const int i = base + j * kThreads + static_cast<int>(threadIdx.x);
+        const bool in_row = i < a.length;
+        scored[j] = in_row && flag[i / a.bs] == 1;
+        v[j] = in_row ? srow[i] : -INFINITY;
+      }
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) {
+        const uint32_t key = float_to_key(v[j]);
+        add_to_bin(mine, scored[j] && (key >> 20) == bin1, (key >> 8) & 0xFFFu);
+      }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {

@@ -135,6 +135,19 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
                 cudaStream_t stream, float* kth_out = nullptr, uint32_t* key_hist = nullptr,
                 int32_t* mirror = nullptr, int64_t mirror_stride = 0);
 
+// ---- certified INT8 key sketch (sketch.cu)
+size_t sketch_workspace_bytes(int batch, int max_length, int k);
+void sketch_workspace_offsets(int batch, int max_length, int k, int64_t* out);
+int launch_sketch_keys(const void* keys, int64_t k_bs, int64_t k_rs, int dtype, int batch,
+                       int first, int length, int8_t* sketch, int64_t sk_bs, float* scale,
+                       void* bounds, int64_t sc_bs, cudaStream_t stream);
+int run_sketch_topk(const void* q, int64_t q_bs, const float* w, int64_t w_bs, const void* keys,
+                    int64_t k_bs, int64_t k_rs, int dtype, const int8_t* sketch, int64_t sk_bs,
+                    const float* scale, const void* bounds, int64_t sc_bs, int batch,
+                    int length, int max_length, int k, int sorted, void* out_idx,
+                    int idx_bytes, int64_t idx_bs, float* out_val, int64_t val_bs,
+                    unsigned long long* stats, void* ws, cudaStream_t stream);
+
 int launch_hadamard128(const void* in, int64_t in_stride, int64_t rows, int dtype, void* out,
                        int64_t out_stride, cudaStream_t stream);
 int launch_select_quantize(const void* in, int64_t in_stride, int64_t rows, int width,

@@ -338,6 +338,24 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
          (1ull << 46) | (2ull << 61);
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::i8 (signed 8-bit inputs, s32 accum).
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor for kind::i8: signed A and B (format 1), s32 accumulation (format
+// 2), both operands K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_s8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 // Instruction descriptor for kind::f16 with f32 accumulation, both operands K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, int m, int n) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |

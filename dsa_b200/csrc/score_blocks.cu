@@ -143,14 +143,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  pdl_wait();  // the tile count, tile lists, q, w and masks may come from the previous kernel
-  pdl_launch_dependents();
-  const int64_t total = a.tile_count ? static_cast<int64_t>(*a.tile_count) : a.total_tiles;
-  const int64_t t0 = total * blockIdx.x / gridDim.x;
-  const int64_t t1 = total * (blockIdx.x + 1) / gridDim.x;
   const int bs = a.bs;
   const uint32_t box_bytes = static_cast<uint32_t>(bs) * 128u;  // one half (64 dims)
 
+  // prologue (touches no memory the previous kernel writes): barriers, tensor maps, TMEM --
+  // under programmatic dependent launch it overlaps the previous kernel's tail
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -182,6 +179,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();  // the tile count, tile lists, q, w and masks may come from the previous kernel
+  pdl_launch_dependents();
+  const int64_t total = a.tile_count ? static_cast<int64_t>(*a.tile_count) : a.total_tiles;
+  const int64_t t0 = total * blockIdx.x / gridDim.x;
+  const int64_t t1 = total * (blockIdx.x + 1) / gridDim.x;
 
   if (warp == 0) {
     if (lane == 0) {

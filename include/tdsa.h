@@ -394,6 +394,18 @@ int tdsa_masked_dense(const void* queries, int64_t q_batch_stride, const float* 
                       const int8_t* keep_blocks, int64_t keep_batch_stride, float* scores,
                       int64_t s_batch_stride, void* stream);
 
+/* tdsa_two_pass -- replaces two_pass_scores_triton (progressive_kernel.py:478-497) in one
+ *   call: block_max = the 8-head probe maximum of every cold block (direct_blocks[b] == 0;
+ *   -inf for direct blocks), accepted[b] = direct or block_max >= *threshold (device float),
+ *   scores = dense scores of the accepted blocks, -inf elsewhere.  Two launches; rejected
+ *   blocks are read by the probe only, and the probe's partial scores are not stored. */
+int tdsa_two_pass(const void* queries, int64_t q_batch_stride, const float* weights,
+                  int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                  int64_t k_row_stride, int dtype, int batch, int length, int block_size,
+                  const int32_t* selected_heads, const int8_t* direct_blocks,
+                  const float* threshold, float* scores, int64_t s_batch_stride,
+                  int8_t* accepted, float* block_max, int64_t bm_batch_stride, void* stream);
+
 /* tdsa_progressive_h8 -- replaces progressive_scores_triton + _progressive_kernel
  *   (progressive_kernel.py:427-475, :277-346), dense output: direct blocks score all 64
  *   heads (block_max -inf); cold blocks score the 8 selected heads, are promoted when their
@@ -415,6 +427,46 @@ int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_
                         int64_t a_batch_stride, int batch, int length, int block_size,
                         float* out_scores, int32_t* out_indices, int64_t out_batch_stride,
                         int32_t* out_count, void* stream);
+
+/*
+ * Certified INT8 key sketch (no reference counterpart: the reference quantizes with one
+ * symmetric scale per tensor and uses the result as an approximate verifier score,
+ * fake_symmetric_quantize / score_dim_sparse in src/temporal_dsa/verifier_scoring.py:29-41,
+ * :95-139; here the quantization is per key and comes with a certified error bound, so the
+ * top-k it feeds stays exact).
+ *
+ * tdsa_sketch_keys -- sketches keys [first, length) of a 16-bit cache: sketch[b][key] =
+ *   128 int8 values rint(k / s) (row stride 128 bytes, batch stride sketch_batch_stride
+ *   bytes), scales[b][key] = s = max|k_i| / 127, bounds[b][key] = two float16 values
+ *   (residual norm >= ||k - s k^||, norm >= ||s k^||), both rounded up; scales and bounds share
+ *   scale_batch_stride (elements).  A key holding a non-finite value gets scale 0 and
+ *   infinite bounds (always read in full).  136 bytes per key.
+ *
+ * tdsa_sketch_topk -- the exact top-k (as tdsa_topk of tdsa_score_dense's scores, ties
+ *   included) that reads each key's sketch and the full 16-bit keys only of the 16-key blocks
+ *   holding a key whose certified upper bound reaches tau, a lower bound of the k-th score
+ *   (the k-th largest certified lower bound).  Five launches; workspace of
+ *   tdsa_sketch_topk_workspace_bytes(batch, max_length, k) bytes, 256-byte aligned, any
+ *   contents (max_length >= length sets its row strides).  stats (device, may be NULL):
+ *   per row two uint64 counters the call adds to: keys read in full, keys whose upper bound
+ *   reached tau.  tdsa_sketch_workspace_offsets gives the byte offsets of the workspace's
+ *   upper bounds, lower bounds, scores (float32 [batch][max_length] each) and tau (float32
+ *   [batch]) of the last call, for checks.
+ */
+int tdsa_sketch_keys(const void* keys, int64_t k_batch_stride, int64_t k_row_stride, int dtype,
+                     int batch, int first, int length, int8_t* sketch,
+                     int64_t sketch_batch_stride, float* scales, void* bounds,
+                     int64_t scale_batch_stride, void* stream);
+size_t tdsa_sketch_topk_workspace_bytes(int batch, int max_length, int k);
+int tdsa_sketch_workspace_offsets(int batch, int max_length, int k, int64_t* offsets);
+int tdsa_sketch_topk(const void* queries, int64_t q_batch_stride, const float* weights,
+                     int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
+                     int64_t k_row_stride, int dtype, const int8_t* sketch,
+                     int64_t sketch_batch_stride, const float* scales, const void* bounds,
+                     int64_t scale_batch_stride, int batch, int length, int max_length, int k,
+                     int sorted, void* out_indices, int index_bytes, int64_t idx_batch_stride,
+                     float* out_values, int64_t val_batch_stride, uint64_t* stats,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Exact (certified) progressive top-k over a growing key cache (the schedule of
