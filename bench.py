@@ -1059,7 +1059,7 @@ def sketch_step(device: torch.device, trace: str, batch: int, length: int, steps
             "dense_us_per_step": e[0].elapsed_time(e[1]) * 1e3 / steps,
             "sketch_equals_dense_every_step": all(torch.equal(x, y) for x, y in zip(got, want)),
             "keys_read_fraction": c[0] / keys_total,
-            "candidate_fraction": c[1] / keys_total,
+            "blocks_read": c[1],
             "bytes_per_key": BYTES_PER_KEY + 256 * c[0] / keys_total,
             "dense_bytes_per_key": 256,
             "batch": batch, "seq_len": length, "k": k, "steps": steps}

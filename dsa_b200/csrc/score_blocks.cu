@@ -115,9 +115,12 @@ __device__ __forceinline__ uint64_t head_mask(const int32_t* ids, int n) {
   return m;
 }
 
+// kmap loads one block (bs rows); kmap_tile loads 128 rows, used for a tile whose blocks are
+// consecutive and all needed (two large boxes instead of 2 * bpt small ones).
 template <int kMode, bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
     score_blocks_kernel(const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap kmap_tile,
                         const __grid_constant__ CUtensorMap qmap, const BlockArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -169,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&kmap);
+    prefetch_tmap(&kmap_tile);
     prefetch_tmap(&qmap);
   }
   if (warp == 1) {
@@ -208,15 +212,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
         uint32_t nload = 0;
-        for (int j = 0; j < a.bpt; ++j) nload += block_loaded<kMode>(a, tile.seq, tile.block[j]);
-        mbar_arrive_expect_tx(&full[s], nload * box_bytes * 2u);
-        uint8_t* dst = stage_base + s * kStageBytes;
+        bool consecutive = a.bpt > 1;
         for (int j = 0; j < a.bpt; ++j) {
-          const int blk = tile.block[j];
-          if (!block_loaded<kMode>(a, tile.seq, blk)) continue;
-          tma_load_3d(dst + j * box_bytes, &kmap, &full[s], 0, blk * bs, tile.seq, pol_k);
-          tma_load_3d(dst + kHalfBytes + j * box_bytes, &kmap, &full[s], 64, blk * bs, tile.seq,
-                      pol_k);
+          const bool ld = block_loaded<kMode>(a, tile.seq, tile.block[j]);
+          nload += ld;
+          consecutive = consecutive && ld && tile.block[j] == tile.block[0] + j;
+        }
+        uint8_t* dst = stage_base + s * kStageBytes;
+        if (consecutive) {  // the tile is 128 consecutive keys: two large boxes
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          const int row0 = tile.block[0] * bs;
+          tma_load_3d(dst, &kmap_tile, &full[s], 0, row0, tile.seq, pol_k);
+          tma_load_3d(dst + kHalfBytes, &kmap_tile, &full[s], 64, row0, tile.seq, pol_k);
+        } else {
+          mbar_arrive_expect_tx(&full[s], nload * box_bytes * 2u);
+          for (int j = 0; j < a.bpt; ++j) {
+            const int blk = tile.block[j];
+            if (!block_loaded<kMode>(a, tile.seq, blk)) continue;
+            tma_load_3d(dst + j * box_bytes, &kmap, &full[s], 0, blk * bs, tile.seq, pol_k);
+            tma_load_3d(dst + kHalfBytes + j * box_bytes, &kmap, &full[s], 64, blk * bs,
+                        tile.seq, pol_k);
+          }
         }
         ++it;
       }
@@ -406,21 +422,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int kMode, bool kBF16>
-int launch_t(const CUtensorMap& kmap, const CUtensorMap& qmap, const BlockArgs& a, int grid,
-             cudaStream_t stream) {
+int launch_t(const CUtensorMap& kmap, const CUtensorMap& kmap_tile, const CUtensorMap& qmap,
+             const BlockArgs& a, int grid, cudaStream_t stream) {
   auto kern = score_blocks_kernel<kMode, kBF16>;
   const int smem = kSmemBytes + (a.hist ? kHistSmemBytes : 0);
   TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
-  TDSA_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, kmap, qmap, a));
+  TDSA_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, kmap, kmap_tile,
+                             qmap, a));
   TDSA_CUDA_CHECK(cudaGetLastError());
   return TDSA_OK;
 }
 
 template <int kMode>
-int launch_mode(bool bf16, const CUtensorMap& kmap, const CUtensorMap& qmap, const BlockArgs& a,
-                int grid, cudaStream_t stream) {
-  return bf16 ? launch_t<kMode, true>(kmap, qmap, a, grid, stream)
-              : launch_t<kMode, false>(kmap, qmap, a, grid, stream);
+int launch_mode(bool bf16, const CUtensorMap& kmap, const CUtensorMap& kmap_tile,
+                const CUtensorMap& qmap, const BlockArgs& a, int grid, cudaStream_t stream) {
+  return bf16 ? launch_t<kMode, true>(kmap, kmap_tile, qmap, a, grid, stream)
+              : launch_t<kMode, false>(kmap, kmap_tile, qmap, a, grid, stream);
 }
 
 }  // namespace
@@ -452,17 +469,26 @@ int make_key_maps(const void* q, int64_t q_bs, const void* k, int64_t k_bs, int6
 int launch_score_blocks(int mode, const void* q, int64_t q_bs, const void* k, int64_t k_bs,
                         int64_t k_rs, int dtype, int batch, const BlockArgs& args, int grid,
                         cudaStream_t stream) {
-  CUtensorMap kmap, qmap;
+  CUtensorMap kmap, kmap_tile, qmap;
   int rc = make_key_maps(q, q_bs, k, k_bs, k_rs, dtype, batch, args.length, args.bs, &kmap,
                          &qmap);
   if (rc) return rc;
+  if (args.bs == kTileKeys) {
+    kmap_tile = kmap;
+  } else {
+    rc = make_key_maps(q, q_bs, k, k_bs, k_rs, dtype, batch, args.length, kTileKeys,
+                       &kmap_tile, &qmap);
+    if (rc) return rc;
+  }
   const bool bf16 = dtype == TDSA_BF16;
   switch (mode) {
-    case kModeH8: return launch_mode<kModeH8>(bf16, kmap, qmap, args, grid, stream);
-    case kModeMasked: return launch_mode<kModeMasked>(bf16, kmap, qmap, args, grid, stream);
+    case kModeH8: return launch_mode<kModeH8>(bf16, kmap, kmap_tile, qmap, args, grid, stream);
+    case kModeMasked:
+      return launch_mode<kModeMasked>(bf16, kmap, kmap_tile, qmap, args, grid, stream);
     case kModeProgressive:
-      return launch_mode<kModeProgressive>(bf16, kmap, qmap, args, grid, stream);
-    case kModeExact: return launch_mode<kModeExact>(bf16, kmap, qmap, args, grid, stream);
+      return launch_mode<kModeProgressive>(bf16, kmap, kmap_tile, qmap, args, grid, stream);
+    case kModeExact:
+      return launch_mode<kModeExact>(bf16, kmap, kmap_tile, qmap, args, grid, stream);
     default: return fail(TDSA_ERR_INVALID, "unknown block scoring mode");
   }
 }

@@ -5,11 +5,11 @@
 // s_k = max|k_i| / 127, and two norms rounded up to float16: r_k >= ||k - s_k k^|| (the
 // quantization residual) and n_k >= ||s_k k^||.  128 + 4 + 4 = 136 bytes per key.
 //
-// Query of one step (sketch_query_kernel): per head h an INT8 pair q^hi, q^lo with
-// q~_h = s_h (q^hi + q^lo / 256) and the exact residual d_h = q_h - q~_h; per sequence
+// Query of one step (sketch_query_kernel): per head h INT8 values q^_h = rint(q_h / s_h),
+// s_h = max|q_h| / 127, q~_h = s_h q^_h and the exact residual d_h = q_h - q~_h; per sequence
 // G = sum_h |w_h| ||q_h|| and D = sum_h |w_h| ||d_h||.
 //
-// Bound: with the head dots q_h . k and their sketch q~_h . s_k k^ (two int8 MMAs, exact in
+// Bound: with the head dots q_h . k and their sketch q~_h . s_k k^ (an int8 MMA, exact in
 // int32), |q_h.k - q~_h.s_k k^| <= ||q_h|| r_k + ||d_h|| n_k, and ReLU is 1-Lipschitz, so the
 // score S = sum_h w_h ReLU(q_h . k) (reference progressive_kernel.py:45-55) lies within
 // gap_k = G r_k + D n_k of the sketch score S~ (plus a 2^-14 relative allowance for the
@@ -36,13 +36,14 @@ namespace {
 constexpr int kTileKeys = 128;
 constexpr int kStages = 8;
 constexpr int kStageBytes = kTileKeys * kHeadDim;  // 16 KiB of int8 sketch rows
-constexpr int kQRows = 2 * kHeads;                 // the hi rows, then the lo rows
-constexpr int kQBytes = kQRows * kHeadDim;         // 16 KiB
+constexpr int kQRows = kHeads;                     // one int8 row per head
+constexpr int kQBytes = kQRows * kHeadDim;         // 8 KiB
 constexpr int kQSlots = 2;
 constexpr int kAccBufs = 2;
-constexpr int kAccCols = 2 * kHeads;            // hi and lo accumulators of one tile
-constexpr int kTmemCols = kAccBufs * kAccCols;  // 256
-constexpr int kThreads = 192;
+constexpr int kAccCols = kHeads;                // one s32 accumulator column per head
+constexpr int kTmemCols = kAccBufs * kAccCols;  // 128
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, taking alternate tiles
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kBarrierBytes = 1024;
 constexpr int kHistBytes = kKeyHistBins * 4;
 constexpr int kSmemBytes =
@@ -50,7 +51,6 @@ constexpr int kSmemBytes =
 constexpr int kSelThreads = kTileListThreads;  // the selection kernel emits tile lists
 constexpr int kHistCopies = 8;
 constexpr int kHistCopyBytes = kHistCopies * kKeyHistBins * 4;
-constexpr float kLoScale = 1.0f / 256.0f;
 constexpr uint32_t kNegInfBin = 0x007FFFFFu >> 20;  // histogram bin of the -inf key
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -64,6 +64,20 @@ __device__ __forceinline__ void decode4(uint2 raw, int dtype, float (&v)[4]) {
   for (int j = 0; j < 4; ++j)
     v[j] = dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(e[j]) << 16)
                               : __half2float(__ushort_as_half(e[j]));
+}
+
+// int32 -> float32, exact for |x| < 2^22, with one integer and one float add (full rate;
+// the conversion unit runs at a quarter of that): the bits of x + 1.5 * 2^23 read as a float
+// are 1.5 * 2^23 + x (a float ulp of 1 there).  Written in PTX so that the pair stays two
+// adds.
+__device__ __forceinline__ float small_int_to_float(uint32_t x) {
+  float r;
+  asm("{\n\t.reg .b32 t;\n\t"
+      "add.s32 t, %1, 0x4B400000;\n\t"
+      "sub.rn.f32 %0, t, 0f4B400000;\n\t}"
+      : "=f"(r)
+      : "r"(x));
+  return r;
 }
 
 __device__ __forceinline__ int q8(float x) {
@@ -148,24 +162,27 @@ struct QueryArgs {
   const float* w;
   int64_t w_bs;
   int dtype;
-  int8_t* qhl;       // [B][128][128]: rows 0..63 the hi parts, 64..127 the lo parts
+  int8_t* qhl;       // [B][64][128]: the int8 query rows
   float* wq;         // [B][64]: w_h * s_h
   float* gd;         // [B][2]: G, D (rounded up; D with the float32 allowance)
   uint32_t* hist_l;  // [B][4096]: cleared for the bound kernel
   int32_t* counter;  // tile counter: cleared for the selection kernel
 };
 
-// One CTA of 256 threads per sequence, one warp per head at a time (4 dims per lane).
-__global__ void __launch_bounds__(256) sketch_query_kernel(const QueryArgs a) {
+constexpr int kQueryThreads = 1024;  // 32 warps: two heads each
+
+// One CTA per sequence, one warp per head at a time (4 dims per lane).
+__global__ void __launch_bounds__(kQueryThreads) sketch_query_kernel(const QueryArgs a) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
-  __shared__ double sg[8], sdd[8];
+  constexpr int kWarps = kQueryThreads / 32;
+  __shared__ double sg[kWarps], sdd[kWarps];
   const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint32_t* hrow = a.hist_l + static_cast<int64_t>(b) * kKeyHistBins;
-  for (int i = threadIdx.x; i < kKeyHistBins; i += 256) hrow[i] = 0u;
+  for (int i = threadIdx.x; i < kKeyHistBins; i += kQueryThreads) hrow[i] = 0u;
   if (b == 0 && threadIdx.x == 0) *a.counter = 0;
   double g = 0.0, d = 0.0;
-  for (int h = warp; h < kHeads; h += 8) {
+  for (int h = warp; h < kHeads; h += kWarps) {
     const uint2 raw = *reinterpret_cast<const uint2*>(
         static_cast<const uint16_t*>(a.q) + static_cast<int64_t>(b) * a.q_bs + h * kHeadDim +
         lane * 4);
@@ -177,25 +194,19 @@ __global__ void __launch_bounds__(256) sketch_query_kernel(const QueryArgs a) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float s = m > 0.f ? m / 127.f : 0.f;
-    int hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+    int qq[4] = {0, 0, 0, 0};
     double dq2 = 0.0, qq2 = 0.0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (s > 0.f) {
-        hi[j] = q8(v[j] / s);
-        const double rho = static_cast<double>(v[j]) - static_cast<double>(s) * hi[j];
-        lo[j] = q8(static_cast<float>(rho * 256.0 / s));
-      }
-      const double dl = static_cast<double>(v[j]) -
-                        static_cast<double>(s) * (hi[j] + lo[j] * (1.0 / 256.0));
+      if (s > 0.f) qq[j] = q8(v[j] / s);
+      const double dl = static_cast<double>(v[j]) - static_cast<double>(s) * qq[j];
       dq2 += dl * dl;
       qq2 += static_cast<double>(v[j]) * v[j];
     }
     dq2 = warp_sum(dq2);
     qq2 = warp_sum(qq2);
     int8_t* row = a.qhl + static_cast<int64_t>(b) * kQBytes;
-    reinterpret_cast<uint32_t*>(row + h * kHeadDim)[lane] = pack4(hi);
-    reinterpret_cast<uint32_t*>(row + (kHeads + h) * kHeadDim)[lane] = pack4(lo);
+    reinterpret_cast<uint32_t*>(row + h * kHeadDim)[lane] = pack4(qq);
     if (lane == 0) {
       const float wh = a.w[static_cast<int64_t>(b) * a.w_bs + h];
       a.wq[static_cast<int64_t>(b) * kHeads + h] = wh * s;
@@ -210,7 +221,7 @@ __global__ void __launch_bounds__(256) sketch_query_kernel(const QueryArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     double gt = 0.0, dt = 0.0;
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < kWarps; ++i) {
       gt += sg[i];
       dt += sdd[i];
     }
@@ -228,8 +239,9 @@ struct BoundArgs {
   const float* scale;
   const __half2* bounds;
   int64_t sc_bs;
-  float* upper;  // [B][o_bs]
-  float* lower;
+  float* upper;      // [B][ub_bs]: per 16-key block, the largest upper bound of its keys
+  int64_t ub_bs;
+  float* lower;      // [B][o_bs]: per key
   int64_t o_bs;
   uint32_t* hist_l;  // [B][4096]: bins of the lower bounds (added)
   int length;
@@ -239,9 +251,9 @@ struct BoundArgs {
 };
 
 // The dense kernel's pipeline (score_tc.cu) on the INT8 sketch: warp 0 loads 16 KiB sketch
-// tiles (128 keys x 128 bytes) and each sequence's 16 KiB hi/lo query by TMA; warp 1 issues
-// per tile two K=128 int8 MMAs (4 x K32 each, hi and lo queries, s32 accumulators in TMEM);
-// warps 2..5 own one key each: S~ = s_k sum_h (w_h s_h) ReLU(hi_h + lo_h / 256), then the
+// tiles (128 keys x 128 bytes) and each sequence's 8 KiB int8 query by TMA; warp 1 issues
+// per tile one K=128 int8 MMA (4 x K32, s32 accumulators in TMEM); warps 2..5 own one key
+// each: S~ = s_k sum_h (w_h s_h) ReLU(acc_h), then the
 // bounds, and the lower bound's key bin into the row histogram.
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_bounds_kernel(const __grid_constant__ CUtensorMap smap,
@@ -279,10 +291,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kAccBufs; ++s) {
       mbar_init(&accfull[s], 1);
-      mbar_init(&accempty[s], 4);
+      mbar_init(&accempty[s], 4);  // the four warps of the buffer's half
     }
     mbar_init(done, 1);
-    mbar_init(hbar, 4);
+    mbar_init(hbar, kEpiWarps);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -360,12 +372,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b_addr = smem_u32(q_base + slot * kQBytes);
         const uint32_t d_tmem = tmem_base + acc * kAccCols;
 #pragma unroll
-        for (int k = 0; k < kHeadDim / 32; ++k) {
-          const uint64_t ad = sw128_kmajor_desc(a_addr + k * 32);
-          umma_i8(d_tmem, ad, sw128_kmajor_desc(b_addr + k * 32), idesc, k > 0 ? 1u : 0u);
-          umma_i8(d_tmem + kHeads, ad, sw128_kmajor_desc(b_addr + kHeads * kHeadDim + k * 32),
-                  idesc, k > 0 ? 1u : 0u);
-        }
+        for (int k = 0; k < kHeadDim / 32; ++k)
+          umma_i8(d_tmem, sw128_kmajor_desc(a_addr + k * 32),
+                  sw128_kmajor_desc(b_addr + k * 32), idesc, k > 0 ? 1u : 0u);
         umma_commit(&empty[s]);
         umma_commit(&accfull[acc]);
         ++it;
@@ -377,10 +386,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- epilogue
+    // warp w reads TMEM lanes 32 * (w % 4); warps 2..5 take the CTA's even tiles
+    // (accumulator buffer 0), warps 6..9 the odd ones (buffer 1)
     const uint32_t quad = static_cast<uint32_t>(warp & 3);
+    const uint32_t half = static_cast<uint32_t>(warp - 2) >> 2;
     const int etid = (warp - 2) * 32 + lane;
     int prev_b = -1;
-    uint32_t acc_it = 0, hph = 0;
+    uint32_t mine = 0, hph = 0;
     float wr[kHeads];
     float G = 0.f, D = 0.f;
     auto hist_sync = [&]() -> bool {
@@ -393,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto hist_flush = [&](int b) -> bool {
       if (!hist_sync()) return false;
       uint32_t* dst = a.hist_l + static_cast<int64_t>(b) * kKeyHistBins;
-      for (int i = etid; i < kKeyHistBins; i += 128) {
+      for (int i = etid; i < kKeyHistBins; i += 32 * kEpiWarps) {
         const uint32_t c = shist[i];
         if (c) {
           atomicAdd(dst + i, c);
@@ -402,11 +414,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return hist_sync();
     };
+    bool ok = true;
     for (int64_t t = t0; t < t1; ++t) {
       const int b = static_cast<int>(t / tps);
       const int tt = static_cast<int>(t - static_cast<int64_t>(b) * tps);
       if (b != prev_b) {
-        if (prev_b >= 0 && !hist_flush(prev_b)) break;
+        if (prev_b >= 0 && !hist_flush(prev_b)) {
+          ok = false;
+          break;
+        }
         const float* wqb = a.wq + static_cast<int64_t>(b) * kHeads;
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) wr[h] = __ldg(wqb + h);
@@ -414,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         D = __ldg(a.gd + 2 * b + 1);
         prev_b = b;
       }
+      if (static_cast<uint32_t>((t - t0) & 1) != half) continue;
       const int row = tt * kTileKeys + static_cast<int>(quad) * 32 + lane;
       const bool valid = row < a.length;
       float sk = 0.f, r = 0.f, n = 0.f;
@@ -424,49 +441,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         r = __low2float(bb);
         n = __high2float(bb);
       }
-      const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
-      if (!mbar_wait(&accfull[acc], aph, abort_flag)) break;
+      const uint32_t aph = mine & 1u;
+      if (!mbar_wait(&accfull[half], aph, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((quad * 32u) << 16) + acc * kAccCols;
+      const uint32_t taddr = tmem_base + ((quad * 32u) << 16) + half * kAccCols;
       float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        uint32_t hv[32], lv[32];
-        tmem_ld32(taddr + part * 32, hv);
-        tmem_ld32(taddr + kHeads + part * 32, lv);
+      {
+        uint32_t h0[32], h1[32];
+        tmem_ld32(taddr, h0);
+        tmem_ld32(taddr + 32, h1);
         tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&accempty[half]);
+        // |acc| <= 128 * 127 * 127 < 2^22: exact conversions
 #pragma unroll
         for (int h = 0; h < 32; h += 4) {
-          const float a0 = fmaf(static_cast<float>(static_cast<int32_t>(lv[h + 0])), kLoScale,
-                                static_cast<float>(static_cast<int32_t>(hv[h + 0])));
-          const float a1 = fmaf(static_cast<float>(static_cast<int32_t>(lv[h + 1])), kLoScale,
-                                static_cast<float>(static_cast<int32_t>(hv[h + 1])));
-          const float a2 = fmaf(static_cast<float>(static_cast<int32_t>(lv[h + 2])), kLoScale,
-                                static_cast<float>(static_cast<int32_t>(hv[h + 2])));
-          const float a3 = fmaf(static_cast<float>(static_cast<int32_t>(lv[h + 3])), kLoScale,
-                                static_cast<float>(static_cast<int32_t>(hv[h + 3])));
-          s0 = fmaf(wr[part * 32 + h + 0], fmaxf(a0, 0.f), s0);
-          s1 = fmaf(wr[part * 32 + h + 1], fmaxf(a1, 0.f), s1);
-          s2 = fmaf(wr[part * 32 + h + 2], fmaxf(a2, 0.f), s2);
-          s3 = fmaf(wr[part * 32 + h + 3], fmaxf(a3, 0.f), s3);
+          s0 = fmaf(wr[h + 0], fmaxf(small_int_to_float(h0[h + 0]), 0.f), s0);
+          s1 = fmaf(wr[h + 1], fmaxf(small_int_to_float(h0[h + 1]), 0.f), s1);
+          s2 = fmaf(wr[h + 2], fmaxf(small_int_to_float(h0[h + 2]), 0.f), s2);
+          s3 = fmaf(wr[h + 3], fmaxf(small_int_to_float(h0[h + 3]), 0.f), s3);
+        }
+#pragma unroll
+        for (int h = 0; h < 32; h += 4) {
+          s0 = fmaf(wr[32 + h + 0], fmaxf(small_int_to_float(h1[h + 0]), 0.f), s0);
+          s1 = fmaf(wr[32 + h + 1], fmaxf(small_int_to_float(h1[h + 1]), 0.f), s1);
+          s2 = fmaf(wr[32 + h + 2], fmaxf(small_int_to_float(h1[h + 2]), 0.f), s2);
+          s3 = fmaf(wr[32 + h + 3], fmaxf(small_int_to_float(h1[h + 3]), 0.f), s3);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&accempty[acc]);
       const float sketch_score = sk * ((s0 + s1) + (s2 + s3));
       const float gap = __fmaf_ru(G, r, __fmul_ru(D, n));
       const float up = __fadd_ru(sketch_score, gap);
       const float lo = __fsub_rd(sketch_score, gap);
-      if (valid) {
-        const int64_t o = static_cast<int64_t>(b) * a.o_bs + row;
-        a.upper[o] = up;
-        a.lower[o] = lo;
-      }
+      if (valid) a.lower[static_cast<int64_t>(b) * a.o_bs + row] = lo;
+      // the block's largest upper bound: 16 lanes hold one 16-key block
+      float ub = valid ? up : -INFINITY;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ub = fmaxf(ub, __shfl_xor_sync(0xffffffffu, ub, o));
+      if ((lane & 15) == 0 && row < a.length)
+        a.upper[static_cast<int64_t>(b) * a.ub_bs + (row >> 4)] = ub;
       add_to_bin(shist, valid, float_to_key(lo) >> 20);
-      ++acc_it;
-      if (t + 1 == t1) hist_flush(b);
+      ++mine;
     }
+    if (ok && prev_b >= 0) hist_flush(prev_b);
   }
 
   __syncthreads();
@@ -480,8 +501,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- selection
 struct SelectArgs {
-  const float* upper;
-  const float* lower;
+  const float* upper;  // [B][nb_stride] block maxima of the upper bounds
+  const float* lower;  // [B][o_bs]
   int64_t o_bs;
   uint32_t* hist_l;  // [B][4096] lower-bound bins: read, then cleared
   uint32_t* hist;    // [B][4096] the exact pass's key histogram: cleared, -inf keys counted
@@ -493,7 +514,7 @@ struct SelectArgs {
   int32_t* tile_blk;
   int32_t* counter;
   float* tau;
-  unsigned long long* stats;  // [B][2]: keys read, candidate keys (added); or null
+  unsigned long long* stats;  // [B][2]: keys read, blocks read (added); or null
   int length, k;
 };
 
@@ -515,7 +536,7 @@ __global__ void __launch_bounds__(kSelThreads) sketch_select_kernel(const Select
   const int nb = (a.length + 15) / 16;
   uint32_t* lrow = a.hist_l + static_cast<int64_t>(seq) * kKeyHistBins;
   uint32_t* frow = a.hist + static_cast<int64_t>(seq) * kKeyHistBins;
-  const float* up = a.upper + static_cast<int64_t>(seq) * a.o_bs;
+  const float* up = a.upper + static_cast<int64_t>(seq) * a.nb_stride;
   const float* lo = a.lower + static_cast<int64_t>(seq) * a.o_bs;
   int8_t* fl = a.flag + static_cast<int64_t>(seq) * a.nb_stride;
   if (threadIdx.x < 2) acc[threadIdx.x] = 0ull;
@@ -618,48 +639,34 @@ __global__ void __launch_bounds__(kSelThreads) sketch_select_kernel(const Select
   }
   const float tau = s_tau;
   if (threadIdx.x == 0) a.tau[seq] = tau;
-  // block flags: a warp covers 32 consecutive keys = two 16-key blocks
-  unsigned long long cand = 0, read = 0;
-  {
-    constexpr int kUnroll = 4;
-    for (int base = 0; base < a.length; base += kSelThreads * kUnroll) {
-      float u[kUnroll];
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const int i = base + j * kSelThreads + static_cast<int>(threadIdx.x);
-        u[j] = i < a.length ? up[i] : -INFINITY;
-      }
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const int i = base + j * kSelThreads + static_cast<int>(threadIdx.x);
-        const bool take = i < a.length && u[j] >= tau;
-        const unsigned bal = __ballot_sync(0xffffffffu, take);
-        cand += take;
-        const int blk = i >> 4;
-        if ((lane & 15) == 0 && blk < nb) {
-          const bool any = ((bal >> (lane & 16)) & 0xFFFFu) != 0u;
-          fl[blk] = any ? 1 : 0;
-          if (any) read += static_cast<unsigned long long>(min(16, a.length - blk * 16));
-        }
-      }
+  // block flags: read a block when its largest upper bound reaches tau
+  unsigned long long read = 0, nread = 0;
+  for (int blk = threadIdx.x; blk < nb; blk += kSelThreads) {
+    const bool take = up[blk] >= tau;
+    fl[blk] = take ? 1 : 0;
+    if (take) {
+      read += static_cast<unsigned long long>(min(16, a.length - blk * 16));
+      ++nread;
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    cand += __shfl_xor_sync(0xffffffffu, cand, o);
     read += __shfl_xor_sync(0xffffffffu, read, o);
+    nread += __shfl_xor_sync(0xffffffffu, nread, o);
   }
   if (lane == 0) {
     atomicAdd(&acc[0], read);
-    atomicAdd(&acc[1], cand);
+    atomicAdd(&acc[1], nread);
   }
   __syncthreads();
   const unsigned long long keys_read = acc[0];
-  // keys of blocks that are not read score -inf (the top-k reads the whole row)
+  // keys of blocks that are not read score -inf (the top-k reads the whole row): one 16-key
+  // block is four 16-byte stores (rows are 16-byte aligned and padded to whole blocks)
   if (keys_read < static_cast<unsigned long long>(a.length)) {
-    float* srow = a.scores + static_cast<int64_t>(seq) * a.o_bs;
-    for (int i = threadIdx.x; i < a.length; i += kSelThreads)
-      if (fl[i >> 4] == 0) srow[i] = -INFINITY;
+    float4* srow = reinterpret_cast<float4*>(a.scores + static_cast<int64_t>(seq) * a.o_bs);
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    for (int i = threadIdx.x; i < nb * 4; i += kSelThreads)
+      if (fl[i >> 2] == 0) srow[i] = ninf;
   }
   if (threadIdx.x == 0) {
     if (a.hist_for_topk)
@@ -678,7 +685,7 @@ struct SketchLayout {
   size_t qhl = 0, wq = 0, gd = 0, upper = 0, lower = 0, scores = 0, hist_l = 0, hist = 0;
   size_t flag = 0, bmax = 0, tau = 0, tile_seq = 0, tile_blk = 0, counter = 0, topk_ws = 0;
   size_t topk_ws_bytes = 0, total = 0;
-  int64_t nb_stride = 0, tcap = 0;
+  int64_t nb_stride = 0, tcap = 0, ld = 0;
 };
 
 SketchLayout sketch_layout(int batch, int max_length, int k) {
@@ -691,11 +698,12 @@ SketchLayout sketch_layout(int batch, int max_length, int k) {
     off = align256(off + bytes);
     return o;
   };
-  const size_t rowf = static_cast<size_t>(batch) * max_length * 4;
+  L.ld = L.nb_stride * 16;  // rows padded to whole 16-key blocks (16-byte aligned)
+  const size_t rowf = static_cast<size_t>(batch) * L.ld * 4;
   L.qhl = take(static_cast<size_t>(batch) * kQBytes);
   L.wq = take(static_cast<size_t>(batch) * kHeads * 4);
   L.gd = take(static_cast<size_t>(batch) * 8);
-  L.upper = take(rowf);
+  L.upper = take(static_cast<size_t>(batch) * L.nb_stride * 4);
   L.lower = take(rowf);
   L.scores = take(rowf);
   L.hist_l = take(static_cast<size_t>(batch) * kKeyHistBins * 4);
@@ -724,6 +732,8 @@ void sketch_workspace_offsets(int batch, int max_length, int k, int64_t* out) {
   out[1] = static_cast<int64_t>(L.lower);
   out[2] = static_cast<int64_t>(L.scores);
   out[3] = static_cast<int64_t>(L.tau);
+  out[4] = L.nb_stride;
+  out[5] = L.ld;
 }
 
 int launch_sketch_keys(const void* keys, int64_t k_bs, int64_t k_rs, int dtype, int batch,
@@ -766,7 +776,7 @@ int run_sketch_topk(const void* q, int64_t q_bs, const float* w, int64_t w_bs, c
   if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
   const bool hist_for_topk = length <= kTopkSegment;
 
-  // 1. the step's int8 query pair, G and D; the histogram and tile counter cleared
+  // 1. the step's int8 query, G and D; the histogram and tile counter cleared
   QueryArgs qa;
   qa.q = q;
   qa.q_bs = q_bs;
@@ -778,7 +788,8 @@ int run_sketch_topk(const void* q, int64_t q_bs, const float* w, int64_t w_bs, c
   qa.gd = gd;
   qa.hist_l = hist_l;
   qa.counter = counter;
-  TDSA_CUDA_CHECK(launch_pdl(sketch_query_kernel, dim3(batch), dim3(256), 0, stream, qa));
+  TDSA_CUDA_CHECK(launch_pdl(sketch_query_kernel, dim3(batch), dim3(kQueryThreads), 0, stream,
+                             qa));
   TDSA_CUDA_CHECK(cudaGetLastError());
 
   // 2. sketch bounds of every key (int8 MMAs), lower bounds into the row histograms
@@ -811,8 +822,9 @@ int run_sketch_topk(const void* q, int64_t q_bs, const float* w, int64_t w_bs, c
   ba.bounds = static_cast<const __half2*>(bounds);
   ba.sc_bs = sc_bs;
   ba.upper = upper;
+  ba.ub_bs = L.nb_stride;
   ba.lower = lower;
-  ba.o_bs = max_length;
+  ba.o_bs = L.ld;
   ba.hist_l = hist_l;
   ba.length = length;
   ba.tiles_per_seq = (length + kTileKeys - 1) / kTileKeys;
@@ -830,7 +842,7 @@ int run_sketch_topk(const void* q, int64_t q_bs, const float* w, int64_t w_bs, c
   SelectArgs sa;
   sa.upper = upper;
   sa.lower = lower;
-  sa.o_bs = max_length;
+  sa.o_bs = L.ld;
   sa.hist_l = hist_l;
   sa.hist = hist;
   sa.hist_for_topk = hist_for_topk ? 1 : 0;
@@ -862,7 +874,7 @@ int run_sketch_topk(const void* q, int64_t q_bs, const float* w, int64_t w_bs, c
   xa.w = w;
   xa.w_stride = w_bs;
   xa.out = scores;
-  xa.out_stride = max_length;
+  xa.out_stride = L.ld;
   xa.block_max = bmax;
   xa.bm_stride = L.nb_stride;
   xa.hist = hist_for_topk ? hist : nullptr;
@@ -872,7 +884,7 @@ int run_sketch_topk(const void* q, int64_t q_bs, const float* w, int64_t w_bs, c
   if (rc) return rc;
 
   // 5. top-k of the row (from its histogram when it is one segment)
-  return launch_topk(scores, max_length, nullptr, 0, batch, length, k, sorted, out_idx,
+  return launch_topk(scores, L.ld, nullptr, 0, batch, length, k, sorted, out_idx,
                      idx_bytes, idx_bs, out_val, val_bs, at(L.topk_ws), L.topk_ws_bytes, stream,
                      nullptr, hist_for_topk ? hist : nullptr);
 }

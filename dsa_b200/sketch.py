@@ -116,24 +116,26 @@ class SketchTopkPlan:
         return self.indices, self.values
 
     def stats(self) -> list[dict]:
-        """Accumulated per-sequence counters: keys read in full, keys whose certified upper
-        bound reached tau (reads device memory: synchronous)."""
+        """Accumulated per-sequence counters: keys read in full, 16-key blocks read (reads
+        device memory: synchronous)."""
         c = self.counters.cpu().tolist()
-        return [{"keys_read": r[0], "candidates": r[1]} for r in c]
+        return [{"keys_read": r[0], "blocks_read": r[1]} for r in c]
 
     def bounds(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """Views of the last run's certified bounds: upper, lower [B, length] and tau [B]."""
-        off = (C.c_int64 * 4)()
+        """Views of the last run's certified bounds: the largest upper bound of every 16-key
+        block [B, ceil(length / 16)], the lower bound of every key [B, length], tau [B]."""
+        off = (C.c_int64 * 6)()
         capi.check(capi.lib().tdsa_sketch_workspace_offsets(self.batch, self.max_length,
                                                             self.k, off))
-        n = self.batch * self.max_length * 4
+        nb_stride, ld = off[4], off[5]
 
-        def rows(o):
-            return self.workspace[o:o + n].view(torch.float32).view(
-                self.batch, self.max_length)[:, :self.length]
+        def rows(o, width, used):
+            n = self.batch * width * 4
+            return self.workspace[o:o + n].view(torch.float32).view(self.batch, width)[:, :used]
 
         tau = self.workspace[off[3]:off[3] + 4 * self.batch].view(torch.float32)
-        return rows(off[0]), rows(off[1]), tau
+        return (rows(off[0], nb_stride, (self.length + 15) // 16),
+                rows(off[1], ld, self.length), tau)
 
 
 def sketch_topk(queries: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor,

@@ -448,10 +448,11 @@ int tdsa_compact_blocks(const float* scores, int64_t s_batch_stride, const int8_
  *   (the k-th largest certified lower bound).  Five launches; workspace of
  *   tdsa_sketch_topk_workspace_bytes(batch, max_length, k) bytes, 256-byte aligned, any
  *   contents (max_length >= length sets its row strides).  stats (device, may be NULL):
- *   per row two uint64 counters the call adds to: keys read in full, keys whose upper bound
- *   reached tau.  tdsa_sketch_workspace_offsets gives the byte offsets of the workspace's
- *   upper bounds, lower bounds, scores (float32 [batch][max_length] each) and tau (float32
- *   [batch]) of the last call, for checks.
+ *   per row two uint64 counters the call adds to: keys read in full, 16-key blocks read.
+ *   tdsa_sketch_workspace_offsets fills offsets[6] for checks of the last call: the byte
+ *   offsets of the blocks' largest upper bounds (float32 [batch][block stride]), the keys'
+ *   lower bounds and scores (float32 [batch][row stride] each) and tau (float32 [batch]),
+ *   then the block stride and the row stride (elements).
  */
 int tdsa_sketch_keys(const void* keys, int64_t k_batch_stride, int64_t k_row_stride, int dtype,
                      int batch, int first, int length, int8_t* sketch,

@@ -4,8 +4,9 @@
   the reference's symmetric quantizer of verifier_scoring.py:29-41 applied per key) bit for
   bit; its float16 norms are never below the exact float64 ones and within float16 rounding
   of them.
-- The certified bounds hold: for every key, lower <= the float64 score <= upper, and
-  tau <= the k-th largest float64 score.
+- The certified bounds hold: every key's lower bound and every 16-key block's upper bound
+  enclose the float64 scores, tau <= the k-th largest float64 score, and every block holding
+  a top-k key is read.
 - The sketch top-k equals dense scoring's top-k (``scores_topk``) bit for bit -- indices and
   values, sorted and unsorted, ties included -- on i.i.d. and block-structured caches, at
   ragged lengths, k = length, and over decode steps of a growing cache.
@@ -85,15 +86,22 @@ def test_sketch_bounds_are_certified(kind):
     plan.run()
     up, lo, tau = plan.bounds()
     up, lo, tau = up.cpu().numpy(), lo.cpu().numpy(), tau.cpu().numpy()
+    nb = (length + 15) // 16
     for b in range(batch):
         exact = oracle.relu_index_score(q[b].float().cpu().numpy(),
                                         keys[b].float().cpu().numpy(), w[b].cpu().numpy())
-        assert np.all(lo[b] <= exact) and np.all(exact <= up[b]), kind
+        assert np.all(lo[b] <= exact), kind
+        padded = np.full(nb * 16, -np.inf)
+        padded[:length] = exact
+        assert np.all(padded.reshape(nb, 16).max(axis=1) <= up[b]), kind
         assert tau[b] <= np.sort(exact)[-k]
+        # every block holding a top-k key is read
+        top_blocks = np.unique(np.argsort(-exact, kind="stable")[:k] // 16)
+        assert np.all(up[b][top_blocks] >= tau[b])
     st = plan.stats()
     for b in range(batch):
-        assert st[b]["candidates"] <= st[b]["keys_read"] <= length
-        assert st[b]["candidates"] >= k
+        assert k <= st[b]["keys_read"] <= length
+        assert st[b]["keys_read"] <= 16 * st[b]["blocks_read"] < st[b]["keys_read"] + 16
     if kind == "structured":  # most blocks hold small keys far below the k-th score
         assert all(s["keys_read"] < length // 2 for s in st)
 
