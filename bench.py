@@ -1524,9 +1524,10 @@ def main() -> None:
                     help="skip timing the reference's own GPU code (baseline/_ref)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the config-3 and config-5 keys of the default line")
-    ap.add_argument("--workload", choices=["cfg4", "cfg3", "cfg5"], default="cfg4",
+    ap.add_argument("--workload", choices=["cfg4", "cfg3", "cfg5", "sketch"], default="cfg4",
                     help="cfg4 (default): the BASELINE metric's workload; cfg3: exact "
-                         "progressive trace; cfg5: L-sharded top-k")
+                         "progressive trace; cfg5: L-sharded top-k; sketch: the certified "
+                         "key sketch at B=64, L=32768")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -1553,6 +1554,9 @@ def main() -> None:
         torch.distributed.barrier()
     if args.workload == "cfg3":
         line = run_cfg3(device, max(args.steps, 8)) if rank == 0 else None
+    elif args.workload == "sketch":
+        line = ({trace: sketch_step(device, trace, 64, 32768, steps=args.steps)
+                 for trace in ("structured", "iid")} if rank == 0 else None)
     elif args.workload == "cfg5":
         line = run_cfg5(args, rank, world, device)
     else:

@@ -315,7 +315,9 @@ int tdsa_score_topk(const void* queries, int64_t q_batch_stride, const float* we
  * 32768) returns TDSA_ERR_UNSUPPORTED before touching the device.  The first call on a
  * device does a one-time set-up (it looks up the buffer's device address, which may load
  * the library's module on that device): make that first call before any stream capture.
- * All calls on one device share the buffer, so calls that can overlap in time (different
+ * The looked-up address is kept for the life of the process: after a device reset (or a
+ * reset of the primary context) the library must be reloaded before this entry point is
+ * used again.  All calls on one device share the buffer, so calls that can overlap in time (different
  * streams, or host threads) race on it; calls issued in order on one stream do not.
  * Results are the same as tdsa_score_topk's.
  */

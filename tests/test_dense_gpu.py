@@ -539,3 +539,31 @@ def test_cluster_topk_long_rows_match_oracle(batch, length, k):
     np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
     np.testing.assert_array_equal(val.cpu().numpy(), want_v)
     assert int(hist.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("batch,length,k", [(1, 32768, 2048), (3, 16384, 1024),
+                                            (4, 20000, 512)])
+def test_topk_device_histogram_special_rows(batch, length, k):
+    """tdsa_topk on a few unsorted rows of one segment: the row histograms are built on the
+    device (row_hist_part_kernel, up to 16 CTAs per row adding into one histogram) and the
+    cluster top-k starts from them.  Rows with -inf runs, +inf, -0.0, ties, and one row of
+    -inf only, against stable_topk (NaN is left out: the reference's stable_topk returns
+    fewer than k indices for a row holding NaN, metrics.py:18-21)."""
+    from dsa_b200 import _capi as capi
+    from dsa_b200 import topk
+
+    # the workspace covers the device histograms: the split path is the one taken
+    assert capi.lib().tdsa_topk_workspace_bytes(batch, length, k) >= batch * 4096 * 4
+    rng = np.random.default_rng(batch * 11 + length)
+    s = np.round(rng.normal(size=(batch, length)) * 64).astype(np.float32) / 64
+    s[0, rng.integers(0, length, length // 3)] = -np.inf
+    s[0, rng.integers(0, length, 40)] = np.inf
+    s[0, rng.integers(0, length, 200)] = -0.0
+    if batch > 1:
+        s[1, 1000:4000] = -np.inf
+    if batch > 2:
+        s[2] = -np.inf  # every key ties at -inf
+    idx, val = topk(cuda(s), k, sorted=False, index_dtype=torch.int64)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
