@@ -484,6 +484,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // W_q and W_w are constant inputs, so they need not wait for the previous kernel: the
+  // first ring stages' weight tiles load now, and the rest of this CTA's W_q tiles -- plus,
+  // for the CTAs of heads 0..31, those of head h + 32, whose CTAs start late when the
+  // previous kernel still holds SMs -- are prefetched into L2 while that kernel finishes.
+  const int pre = nloc < kStages ? nloc : kStages;
+  if (warp == 0 && lane == 0) {
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    for (int it = 0; it < pre; ++it) {
+      const int kc = kbeg + it;
+      mbar_arrive_expect_tx(&full[it], kStage + kWwChunkBytes);
+      int wx, wy;
+      wq_coords(a, h, kc, nk, wx, wy);
+      tma_load_2d(smem + it * kStage, &wmap, &full[it], wx, wy, pol_w);
+      tma_load_2d(ww_ring + it * kKChunk, &wwmap, &full[it], kc * kKChunk, h, pol_x);
+    }
+    for (int kc = kbeg + pre; kc < kend; ++kc) {
+      int wx, wy;
+      wq_coords(a, h, kc, nk, wx, wy);
+      tma_prefetch_l2_2d(&wmap, wx, wy);
+    }
+    if (h < kHeads / 2)
+      for (int kc = kbeg; kc < kend; ++kc) {
+        int wx, wy;
+        wq_coords(a, h + kHeads / 2, kc, nk, wx, wy);
+        tma_prefetch_l2_2d(&wmap, wx, wy);
+      }
+  }
   pdl_wait();  // hidden states and positions may come from the previous kernel
   pdl_launch_dependents();
 
@@ -495,9 +523,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int it = 0;
       for (; it < nloc; ++it) {
         const int s = it % kStages;
-        if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag)) break;
         const int kc = kbeg + it;
         uint8_t* dst = smem + s * kStage;
+        if (it < pre) {  // the weights of this stage are already on their way
+          tma_load_2d(dst + kWTileBytes, &xmap, &full[s], kc * kKChunk, 0, pol_x);
+          continue;
+        }
+        if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag)) break;
         mbar_arrive_expect_tx(&full[s], kStage + kWwChunkBytes);
         int wx, wy;
         wq_coords(a, h, kc, nk, wx, wy);

@@ -8,11 +8,13 @@
 //               (two 64-column boxes, 128-byte swizzle); the sequence's q [64 x 128] into
 //               one of two q slots when the sequence changes.
 //   warp 1      tcgen05 issuer: UMMA M=128 (keys) x N=64 (heads) x K=128 (8 x K16 steps),
-//               A = key tile, B = q, accumulator in TMEM (2 buffers x 64 f32 columns).
-//   warps 2..5  epilogue: each thread owns one key (one TMEM lane), loads its 64 head dots
-//               with tcgen05.ld, applies ReLU * w_h and sums the heads in registers -- no
-//               cross-thread reduction -- and stores one float per key (coalesced), plus
-//               optionally its float16 rounding into a score-trace row.
+//               A = key tile, B = q, accumulator in TMEM (4 buffers x 64 f32 columns).
+//   warps 2..9  epilogue, two groups of four warps taking alternate tiles (one warp alone
+//               per TMEM lane quadrant does not keep up with the key stream): each thread
+//               owns one key (one TMEM lane), loads its 64 head dots with tcgen05.ld,
+//               applies ReLU * w_h and sums the heads in registers -- no cross-thread
+//               reduction -- and stores one float per key (coalesced), plus optionally its
+//               float16 rounding into a score-trace row.
 // HBM traffic per key = its 256 bytes, read once; q/w per sequence come from L2.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -30,13 +32,14 @@ constexpr int kStageBytes = kTileKeys * kHeadDim * 2;  // 32 KiB
 constexpr int kHalfBytes = kStageBytes / 2;            // 128 rows x 128 B
 constexpr int kQBytes = kHeads * kHeadDim * 2;         // 16 KiB
 constexpr int kQHalf = kQBytes / 2;                    // 64 rows x 128 B
-constexpr int kAccBufs = 2;
-constexpr int kTmemCols = 128;
-constexpr int kThreads = 192;
+constexpr int kEpiGroups = 2;  // epilogue groups of four warps, alternate tiles
+constexpr int kAccBufs = 4;    // TMEM accumulators: two per epilogue group
+constexpr int kTmemCols = kAccBufs * kHeads;
+constexpr int kThreads = 64 + 128 * kEpiGroups;
 constexpr int kBarrierBytes = 1024;
 constexpr int kSmemBytes = kStages * kStageBytes + kQSlots * kQBytes + kBarrierBytes + 1024;
 constexpr int kHistBins = 4096;  // key histogram bins (top 12 bits of the order-preserving key)
-constexpr int kHistBytes = kHistBins * 4;
+constexpr int kHistBytes = kHistBins * 4 * kEpiGroups;  // one histogram per epilogue group
 constexpr int kHistSegment = 32768;  // keys per histogram (one top-k segment)
 static_assert(kHistSegment == 256 * kTileKeys, "a segment is 256 tiles");
 
@@ -61,9 +64,9 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 // kHist: the epilogue also counts every score's order-preserving key by its top 12 bits in a
-// shared-memory histogram, flushed to a.hist[sequence][segment] whenever the CTA moves to
-// the next sequence or 32768-key segment (the top-k then starts each segment from the bin
-// holding its k-th key instead of a full pass).
+// shared-memory histogram (one per epilogue group), flushed to a.hist[sequence][segment]
+// whenever the group moves to the next sequence or 32768-key segment (the top-k then starts
+// each segment from the bin holding its k-th key instead of a full pass).
 template <bool kBF16, bool kHist>
 __global__ void __launch_bounds__(kThreads, 1)
     score_dense_tc_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -79,8 +82,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accfull = qempty + 2;
   uint64_t* accempty = accfull + kAccBufs;
   uint64_t* done = accempty + kAccBufs;
-  uint64_t* hbar = done + 1;  // epilogue-warp handshake around histogram flushes
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hbar + 1);
+  uint64_t* hbar = done + 1;  // [kEpiGroups] epilogue-group handshakes around histogram flushes
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hbar + kEpiGroups);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint32_t* shist = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
 
@@ -101,15 +104,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kAccBufs; ++s) {
       mbar_init(&accfull[s], 1);
-      mbar_init(&accempty[s], 4);
+      mbar_init(&accempty[s], 4);  // the four warps of the group that owns the buffer
     }
     mbar_init(done, 1);
-    mbar_init(hbar, 4);
+    for (int g = 0; g < kEpiGroups; ++g) mbar_init(&hbar[g], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (kHist)
-    for (int i = threadIdx.x; i < kHistBins; i += kThreads) shist[i] = 0u;
+    for (int i = threadIdx.x; i < kHistBins * kEpiGroups; i += kThreads) shist[i] = 0u;
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&kmap);
     prefetch_tmap(&qmap);
@@ -179,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++qcount;
           prev_b = b;
         }
-        const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
+        const uint32_t acc = acc_it % kAccBufs, aph = (acc_it / kAccBufs) & 1u;
         if (!mbar_wait(&accempty[acc], aph ^ 1u, abort_flag)) break;
         const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
         if (!mbar_wait(&full[s], ph, abort_flag)) break;
@@ -205,16 +208,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- epilogue
+    // group g (warps 2 + 4g .. 5 + 4g, one per TMEM lane quadrant) takes the CTA's local
+    // tiles i = g, g + 2, ... from accumulator i % 4
     const uint32_t quad = static_cast<uint32_t>(warp & 3);
-    const int etid = (warp - 2) * 32 + lane;  // 0..127 over the epilogue warps
+    const int group = (warp - 2) >> 2;
+    const int etid = (warp - 2 - 4 * group) * 32 + lane;  // 0..127 within the group
+    uint32_t* ghist = shist + group * kHistBins;
+    uint64_t* gbar = hbar + group;
     int prev_b = -1, prev_slot = -1;
-    uint32_t acc_it = 0, hph = 0;
+    uint32_t hph = 0;
     float wr[kHeads];
-    // all four epilogue warps meet (bounded wait); false when the CTA aborts
+    // the group's four warps meet (bounded wait); false when the CTA aborts
     auto hist_sync = [&]() -> bool {
       __syncwarp();
-      if (lane == 0) mbar_arrive(hbar);
-      const bool ok = mbar_wait(hbar, hph & 1u, abort_flag);
+      if (lane == 0) mbar_arrive(gbar);
+      const bool ok = mbar_wait(gbar, hph & 1u, abort_flag);
       ++hph;
       return ok;
     };
@@ -222,21 +230,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!hist_sync()) return false;
       uint32_t* dst = a.hist + static_cast<int64_t>(slot) * kHistBins;
       for (int i = etid; i < kHistBins; i += 128) {
-        const uint32_t c = shist[i];
+        const uint32_t c = ghist[i];
         if (c) {
           atomicAdd(dst + i, c);
-          shist[i] = 0u;
+          ghist[i] = 0u;
         }
       }
       return hist_sync();
     };
-    for (int64_t t = t0; t < t1; ++t) {
+    bool ok = true;
+    for (int64_t t = t0 + group; t < t1; t += kEpiGroups) {
+      const uint32_t acc_it = static_cast<uint32_t>(t - t0);
       const int b = static_cast<int>(t / tps);
       const int tt = static_cast<int>(t - static_cast<int64_t>(b) * tps);
       if (kHist) {  // one histogram per (sequence, 32768-key segment): 256 tiles
         const int slot = b * a.hist_segs + (tt >> 8);
         if (slot != prev_slot) {
-          if (prev_slot >= 0 && !hist_flush(prev_slot)) break;
+          if (prev_slot >= 0 && !hist_flush(prev_slot)) {
+            ok = false;
+            break;
+          }
           prev_slot = slot;
         }
       }
@@ -244,8 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_head_weights(a.w + static_cast<int64_t>(b) * a.w_stride, wr);
         prev_b = b;
       }
-      const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
-      if (!mbar_wait(&accfull[acc], aph, abort_flag)) break;
+      const uint32_t acc = acc_it % kAccBufs, aph = (acc_it / kAccBufs) & 1u;
+      if (!mbar_wait(&accfull[acc], aph, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t r0[32], r1[32];
       const uint32_t taddr = tmem_base + ((quad * 32u) << 16) + acc * kHeads;
@@ -263,10 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (a.trace)
           a.trace[static_cast<int64_t>(b) * a.trace_stride + row] = __float2half_rn(score);
       }
-      if (kHist) add_to_bin(shist, row < a.length, float_to_key(score) >> 20);
-      ++acc_it;
-      if (kHist && t + 1 == t1) hist_flush(prev_slot);
+      if (kHist) add_to_bin(ghist, row < a.length, float_to_key(score) >> 20);
     }
+    if (kHist && ok && prev_slot >= 0) hist_flush(prev_slot);
   }
 
   __syncthreads();

@@ -123,6 +123,9 @@ class QueryProjector:
                      if keep_qraw else None)
         self.q = torch.empty(batch, HEADS, HEAD_DIM, device=dev, dtype=wq.dtype)
         self.w = torch.empty(batch, HEADS, device=dev, dtype=torch.float32)
+        # the kernel reads W_q and W_w before it waits on the previous kernel of the stream:
+        # the packed weights must be complete before the first projection
+        torch.cuda.current_stream(dev).synchronize()
         self._fn = capi.lib().tdsa_query_project
         self._dt = capi.TDSA_BF16 if wq.dtype == torch.bfloat16 else capi.TDSA_F16
 

@@ -548,7 +548,10 @@ int tdsa_pack_query_weights(const void* w_q, int64_t wq_row_stride, int hidden_s
  * 16-byte aligned.  wq_packed != 0: w_q is the output of tdsa_pack_query_weights
  * (wq_row_stride ignored) -- every tile the kernel streams is then one contiguous block,
  * which HBM serves at full bandwidth; the row-major layout works but reads 128-byte
- * pieces 4 KB apart.
+ * pieces 4 KB apart.  The launch reads w_q and w_proj (constant weights) before it waits on
+ * the previous kernel of the stream (programmatic dependent launch), so they must not be
+ * written by the kernel issued right before it on the same stream; only hidden and
+ * positions may come from that kernel.
  */
 int tdsa_query_project(const void* hidden, int64_t hidden_stride, int hidden_size,
                        const void* w_q, int64_t wq_row_stride, int wq_packed,
