@@ -4,7 +4,7 @@
 //
 // One persistent CTA per SM walks a contiguous range of 128-key tiles (tiles of all
 // sequences are numbered b * tiles_per_seq + t).  Warp roles:
-//   warp 0      TMA producer: key tiles [128 keys x 128 dims] into a 5-stage smem ring
+//   warp 0      TMA producer: key tiles [128 keys x 128 dims] into a 4-stage smem ring
 //               (two 64-column boxes, 128-byte swizzle); the sequence's q [64 x 128] into
 //               one of two q slots when the sequence changes.
 //   warp 1      tcgen05 issuer: UMMA M=128 (keys) x N=64 (heads) x K=128 (8 x K16 steps),
@@ -26,7 +26,7 @@ namespace tdsa {
 namespace {
 
 constexpr int kTileKeys = 128;
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kQSlots = 2;  // q buffers: the next sequence's q loads while the MMA uses one
 constexpr int kStageBytes = kTileKeys * kHeadDim * 2;  // 32 KiB
 constexpr int kHalfBytes = kStageBytes / 2;            // 128 rows x 128 B
