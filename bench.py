@@ -444,6 +444,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             line["reference_gpu"] = reference_gpu(wl, proj[0], device)
         if not args.no_extras:
             line["cfg3"] = run_cfg3(device, 64)
+            line["f32_dense"] = f32_dense_rate(device)
     if cfg5 is not None:
         line["cfg5"] = cfg5
     if world == 1 and not args.no_cpu_baseline:
@@ -512,6 +513,54 @@ def policy_step_latency(wl: Config4, device: torch.device, steps: int = 8,
                                "sample": "one sequence-step of the numpy restatement "
                                          "(oracle/approx.py), single thread"}
     return out
+
+
+def f32_dense_rate(device: torch.device, batch: int = 16, length: int = 32768,
+                   reps: int = 10) -> dict:
+    """Dense scoring of a float32 key cache (config 1's dtype) at L = 32768: the tensor-core
+    path (error-compensated TF32, score_dense_tf32_kernel) against HBM, and the FP32
+    CUDA-core kernel on the same keys in rows of 129 floats (an odd stride sends
+    tdsa_score_dense there).  Eager tdsa_score_dense calls, L2 flushed (256 MB write) before
+    each, CUDA events around the call; mean over `reps`."""
+    from dsa_b200 import score_dense
+
+    g = _generator(device, 32)
+    q = torch.randn(batch, 64, 128, device=device, generator=g) / math.sqrt(128)
+    w = torch.randn(batch, 64, device=device, generator=g) / 8
+    keys = torch.randn(batch, length, 128, device=device, generator=g)
+    odd = torch.zeros(batch, length, 129, device=device)
+    odd[:, :, :128] = keys
+    odd_keys = odd[:, :, :128]
+    out = torch.empty(batch, length, device=device)
+    flush = torch.empty(256 << 20, device=device, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(k):
+        for _ in range(3):
+            score_dense(q, w, k, out=out)
+        total = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            score_dense(q, w, k, out=out)
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            total += a.elapsed_time(b)
+        return total / reps * 1e3
+
+    tc_us = timed(keys)
+    simt_us = timed(odd_keys)
+    nbytes = batch * (length * 128 * 4 + 64 * 128 * 4 + 64 * 4 + length * 4)
+    peak, kind = hbm_peak()
+    gbs = nbytes / (tc_us * 1e-6) / 1e9
+    return {"batch": batch, "seq_len": length, "dtype": "f32",
+            "tensor_core_us": tc_us, "tensor_core_gbs": gbs, "frac_of_hbm": gbs / peak,
+            "peak_gbs": peak, "peak_kind": kind, "algorithmic_bytes": nbytes,
+            "fp32_cuda_core_us": simt_us, "keys_per_s": batch * length / (tc_us * 1e-6),
+            "method": "eager tdsa_score_dense, L2 flushed before each call, events, "
+                      f"mean of {reps}"}
 
 
 def key_append_latency(wl: Config4, device: torch.device, per_graph: int = 20,

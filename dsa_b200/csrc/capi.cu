@@ -246,13 +246,20 @@ int tdsa_score_dense(const void* queries, int64_t q_batch_stride, const float* w
                             s_batch_stride);
   if (rc || length == 0) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == TDSA_F32)
-    return launch_score_dense_f32(static_cast<const float*>(queries), q_batch_stride, weights,
-                                  w_batch_stride, static_cast<const float*>(keys),
-                                  k_batch_stride, k_row_stride, batch, length, scores,
-                                  s_batch_stride, st);
   int* status = device_status_ptr();
   if (!status) return fail(TDSA_ERR_CUDA, "device status word not available");
+  if (dtype == TDSA_F32) {
+    const float* q = static_cast<const float*>(queries);
+    const float* k = static_cast<const float*>(keys);
+    // tensor cores (3 x TF32) when the layout admits TMA, else exact FP32 FMAs
+    if (score_dense_tf32_supported(q, q_batch_stride, k, k_batch_stride, k_row_stride, batch))
+      return launch_score_dense_tf32(q, q_batch_stride, weights, w_batch_stride, k,
+                                     k_batch_stride, k_row_stride, batch, length, scores,
+                                     s_batch_stride, st, status);
+    return launch_score_dense_f32(q, q_batch_stride, weights, w_batch_stride, k,
+                                  k_batch_stride, k_row_stride, batch, length, scores,
+                                  s_batch_stride, st);
+  }
   return launch_score_dense_tc(queries, q_batch_stride, weights, w_batch_stride, keys,
                                k_batch_stride, k_row_stride, dtype, batch, length, scores,
                                s_batch_stride, st, status);

@@ -20,6 +20,14 @@ int launch_score_dense_tc(const void* q, int64_t q_bs, const float* w, int64_t w
                           int* status, uint32_t* hist = nullptr, void* trace = nullptr,
                           int64_t trace_bs = 0);
 
+// Error-compensated TF32 scoring of float32 keys on the tensor cores (score_tf32.cu); needs
+// 16-byte aligned q and keys and strides that are multiples of 4 floats.
+bool score_dense_tf32_supported(const float* q, int64_t q_bs, const float* k, int64_t k_bs,
+                                int64_t k_rs, int batch);
+int launch_score_dense_tf32(const float* q, int64_t q_bs, const float* w, int64_t w_bs,
+                            const float* k, int64_t k_bs, int64_t k_rs, int batch, int length,
+                            float* out, int64_t o_bs, cudaStream_t stream, int* status);
+
 int launch_score_dense_f32(const float* q, int64_t q_bs, const float* w, int64_t w_bs,
                            const float* k, int64_t k_bs, int64_t k_rs, int batch, int length,
                            float* out, int64_t o_bs, cudaStream_t stream);

@@ -211,9 +211,12 @@ int tdsa_device_status(int* status_out, int reset);
  * keys     [batch][length][128] of `dtype`, rows k_row_stride apart (>= 128), sequences
  *          k_batch_stride apart;
  * scores   [batch][length] float32 out, batch stride s_batch_stride (>= length).
- * dtype TDSA_BF16 / TDSA_F16 run on the tcgen05 tensor cores (f32 accumulation);
- * TDSA_F32 runs an FP32 CUDA-core kernel.  16-bit queries/keys need 16-byte aligned bases
- * and strides that are multiples of 8 elements (TMA).
+ * dtype TDSA_BF16 / TDSA_F16 run on the tcgen05 tensor cores (f32 accumulation).
+ * TDSA_F32 runs on the tensor cores as error-compensated TF32 (q_hi.k_hi + q_lo.k_hi +
+ * q_hi.k_lo, relative error ~2^-21 per product) when queries and keys have 16-byte aligned
+ * bases and strides that are multiples of 4 floats, else an FP32 CUDA-core kernel.  16-bit
+ * queries/keys need 16-byte aligned bases and strides that are multiples of 8 elements
+ * (TMA).
  */
 int tdsa_score_dense(const void* queries, int64_t q_batch_stride, const float* weights,
                      int64_t w_batch_stride, const void* keys, int64_t k_batch_stride,
