@@ -512,6 +512,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_prefetch_l2_2d(&wmap, wx, wy);
       }
   }
+  // the RoPE frequencies depend on the arguments only
+  if (threadIdx.x >= 64 && threadIdx.x - 64 < (a.rope_dim >> 1)) {
+    const int jj = threadIdx.x - 64, hf = a.rope_dim >> 1;
+    sinv[jj] = powf(a.theta, -static_cast<float>(jj) / static_cast<float>(hf));
+  }
   pdl_wait();  // hidden states and positions may come from the previous kernel
   pdl_launch_dependents();
 
@@ -570,19 +575,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64;  // 0..127
     const int half = a.rope_dim >> 1;
     constexpr int kTabStride = kN + 4;
-    // rope_dim <= 64: the cos/sin table has its own region and is built before the first
-    // stage lands (hidden behind the first loads); larger rope_dim builds it in the ring
-    // after the GEMM
+    // rope_dim <= 64: the cos/sin table has its own region and is built right after the
+    // GEMV (while the last MMAs run); larger rope_dim builds it in the ring after the GEMM
     const bool early = half <= 32;
     float* etab = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
-    {
-      for (int i = et; i < kN; i += 128)
-        spos[i] = static_cast<float>(a.positions[min(i, a.batch - 1)]);
-      if (et < half) sinv[et] = powf(a.theta, -static_cast<float>(et) / static_cast<float>(half));
-      epi_barrier();
-      if (early) build_rope_table(spos, sinv, half, kN, kTabStride, etab, etab + 32 * kTabStride);
-    }
-    // (1) the W_w GEMV over this CTA's half of the hidden dimension (layout as above)
+    // this thread's position (kN <= 128): the load is consumed after the GEMV, so its
+    // latency hides behind it
+    static_assert(kN <= 128, "one position per epilogue thread");
+    const int64_t my_pos = et < kN ? a.positions[min(et, a.batch - 1)] : 0;
+    // (1) the W_w GEMV over this CTA's half of the hidden dimension (layout as above), started
+    // as soon as the first stage lands: the ring's stages are released by these warps too
     constexpr int kPer = kN / 16;
     const int c = et & 7;
     float part[kPer];
@@ -621,6 +623,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       v += __shfl_xor_sync(0xffffffffu, v, 4);
       part[i] = v;  // the row sum (over this CTA's half) in the lanes with c == 0
     }
+    // the positions, then (rope_dim <= 64) the cos/sin table in its own region, while the
+    // last MMAs finish
+    if (et < kN) spos[et] = static_cast<float>(my_pos);
+    epi_barrier();
+    if (early) build_rope_table(spos, sinv, half, kN, kTabStride, etab, etab + 32 * kTabStride);
     const uint32_t quad = static_cast<uint32_t>(warp & 3);
     const int d = static_cast<int>(quad) * 32 + lane;  // this thread's feature (TMEM lane)
     // (2) the pair shares the epilogue: rank r finishes batch columns [32r, 32r + 32).
