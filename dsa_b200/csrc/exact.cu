@@ -212,6 +212,11 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
 
 constexpr int kHistCopies = 8;  // private copies of the row histogram (one per 4 warps)
 constexpr int kHistCopyBytes = kHistCopies * kKeyHistBins * 4;
+// dynamic shared memory of the wave-2 kernel: the copies plus one flag byte per block (the
+// static part holds another 16 KB histogram)
+constexpr int kWave2MaxSmem = 200 * 1024;
+constexpr int kMaxHistSegs = 64;  // 32768-key histogram segments per sequence (2^21 keys)
+static_assert(kTopkSegment == 1 << 15, "a key's histogram segment is its index >> 15");
 
 // Counts the 4096-bin key histogram (top 12 bits of the order-preserving key) of one score
 // row into h[0, 4096) (shared memory).  Finite scores go to eight private copies in `hc`
@@ -248,9 +253,8 @@ __device__ uint32_t row_histogram(const float* srow, int length, uint32_t* h, ui
 // Wave 2: blocks not scored yet whose bound reaches tau.  tau is the lower edge of the key
 // bin (top 12 bits from the wave-1 histogram, then the next 12 bits inside that bin) that
 // holds the k-th largest wave-1 score: at most that score, so every block pruned against it
-// holds no top-k key.  Pruned keys are set to -inf in the score row; with `hist_for_topk`
-// they are counted in the -inf bin of the histogram (which the top-k then consumes),
-// otherwise the histogram is cleared for the next step.
+// holds no top-k key.  Pruned keys are set to -inf in the score row and counted in the -inf
+// bin of their segment's histogram, which the top-k then consumes (and clears).
 struct Wave2Args {
   int length, bs, bpt, k;
   int64_t nb_stride, l_stride;
@@ -261,34 +265,44 @@ struct Wave2Args {
   int32_t* tile_seq;
   int32_t* tile_blk;
   int32_t* counters;  // [1]: wave-2 tiles; [0] is cleared for the next step's wave 1
-  uint32_t* hist;     // [B][4096]: the wave-1 scores' key histogram
-  int hist_for_topk;
+  uint32_t* hist;     // [B][hist_segs][4096]: the wave-1 scores' key histograms, one per
+                      // 32768-key segment of the row
+  int hist_segs;
   unsigned long long* stats;
 };
 
 __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
-  extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words
+  extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words, then the row's flags
   __shared__ uint32_t h[kKeyHistBins];
   __shared__ uint32_t wtot[32];
   __shared__ uint32_t sbase[4];
   __shared__ unsigned long long acc[5];
   __shared__ float s_tau;
   __shared__ uint32_t s_bin, s_rank;
+  __shared__ uint32_t seg_pruned[kMaxHistSegs];  // pruned keys per segment
   const int seq = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nb = (a.length + a.bs - 1) / a.bs;
   const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
-  const int8_t* flag = a.flag + brow;
+  int8_t* sflag = reinterpret_cast<int8_t*>(hcopies + kHistCopies * kKeyHistBins);  // [nb]
   float* srow = a.scores + static_cast<int64_t>(seq) * a.l_stride;
-  uint32_t* grow = a.hist + static_cast<int64_t>(seq) * kKeyHistBins;
+  uint32_t* grow = a.hist + static_cast<int64_t>(seq) * a.hist_segs * kKeyHistBins;
+  // the row in 16-byte pieces when its base allows (bs is a multiple of 4, so a piece lies
+  // in one block): 4 keys per load or store, all of a thread's pieces in flight at once
+  const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0u;
+  const int nvec = vec ? a.length >> 2 : 0;
+  const int bshift = __ffs(a.bs) - 1;  // block sizes are powers of two
   if (seq == 0 && threadIdx.x == 0) a.counters[0] = 0;  // wave 1 of this step is done
   if (threadIdx.x < 5) acc[threadIdx.x] = 0ull;
-  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {
-    h[i] = grow[i];
-    if (!a.hist_for_topk) grow[i] = 0u;
+  if (threadIdx.x < kMaxHistSegs) seg_pruned[threadIdx.x] = 0u;
+  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {  // the row's counts
+    uint32_t t = 0;
+    for (int g = 0; g < a.hist_segs; ++g) t += grow[g * kKeyHistBins + i];
+    h[i] = t;
   }
+  for (int b = threadIdx.x; b < nb; b += kThreads) sflag[b] = a.flag[brow + b];
   __syncthreads();
   // thread t owns bins 4095-4t .. 4092-4t: keys above a thread's bins by a CTA scan
   uint32_t c[4], tot = 0;
@@ -328,17 +342,38 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
     for (int i = threadIdx.x; i < kHistCopies * kKeyHistBins; i += kThreads) hcopies[i] = 0u;
     __syncthreads();
     uint32_t* mine = hcopies + (warp & (kHistCopies - 1)) * kKeyHistBins;
-    // 8 independent loads per thread in flight (the pass is bound by load latency)
+    // only the wave-1 blocks' scores are read; 8 independent loads per thread in flight
+    // (the pass is bound by load latency)
     constexpr int kUnroll = 8;
-    for (int base = 0; base < a.length; base += kThreads * kUnroll) {
+    for (int base = 0; base < nvec; base += kThreads * kUnroll) {
+      float4 v[kUnroll];
+      bool scored[kUnroll];
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) {
+        const int i = base + j * kThreads + static_cast<int>(threadIdx.x);
+        scored[j] = i < nvec && sflag[(4 * i) >> bshift] == 1;
+        v[j] = scored[j] ? reinterpret_cast<const float4*>(srow)[i]
+                         : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) {
+        const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t key = float_to_key(e[u]);
+          add_to_bin(mine, scored[j] && (key >> 20) == bin1, (key >> 8) & 0xFFFu);
+        }
+      }
+    }
+    // the keys past the 16-byte pieces (all of them when the row is not 16-byte aligned)
+    for (int base = 4 * nvec; base < a.length; base += kThreads * kUnroll) {
       float v[kUnroll];
       bool scored[kUnroll];
 #pragma unroll
       for (int j = 0; j < kUnroll; ++j) {
         const int i = base + j * kThreads + static_cast<int>(threadIdx.x);
-        const bool in_row = i < a.length;
-        scored[j] = in_row && flag[i / a.bs] == 1;
-        v[j] = in_row ? srow[i] : -INFINITY;
+        scored[j] = i < a.length && sflag[i >> bshift] == 1;
+        v[j] = scored[j] ? srow[i] : -INFINITY;
       }
 #pragma unroll
       for (int j = 0; j < kUnroll; ++j) {
@@ -386,13 +421,13 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
   }
   const float t = s_tau;
   if (threadIdx.x == 0) a.tau[seq] = t;
-  int8_t* fl = a.flag + brow;
   unsigned long long scored = 0, keys = 0, hot = 0, second = 0, pruned_keys = 0;
   for (int b = threadIdx.x; b < nb; b += kThreads) {
-    int8_t f = fl[b];
+    int8_t f = sflag[b];
     if (f == 0 && a.bound[brow + b] >= t) {
       f = 2;
-      fl[b] = 2;
+      sflag[b] = 2;
+      a.flag[brow + b] = 2;
     }
     const unsigned long long n = static_cast<unsigned long long>(min(a.bs, a.length - b * a.bs));
     if (f) {
@@ -402,6 +437,7 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
       second += f == 2;
     } else {
       pruned_keys += n;
+      atomicAdd(&seg_pruned[(b * a.bs) >> 15], static_cast<uint32_t>(n));
     }
   }
   // warp sums first: 64-bit shared atomics from every thread on one word serialise
@@ -423,11 +459,15 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
   __syncthreads();
   // pruned keys score -inf (the top-k reads the whole row)
   if (acc[4]) {
-    for (int i = threadIdx.x; i < a.length; i += kThreads)
-      if (fl[i / a.bs] == 0) srow[i] = -INFINITY;
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    for (int i = threadIdx.x; i < nvec; i += kThreads)
+      if (sflag[(4 * i) >> bshift] == 0) reinterpret_cast<float4*>(srow)[i] = ninf;
+    for (int i = 4 * nvec + static_cast<int>(threadIdx.x); i < a.length; i += kThreads)
+      if (sflag[i >> bshift] == 0) srow[i] = -INFINITY;
   }
   if (threadIdx.x == 0) {
-    if (a.hist_for_topk && acc[4]) atomicAdd(&grow[kNegInfBin], static_cast<uint32_t>(acc[4]));
+    for (int g = 0; g < a.hist_segs; ++g)
+      if (seg_pruned[g]) atomicAdd(&grow[g * kKeyHistBins + kNegInfBin], seg_pruned[g]);
     unsigned long long* st = a.stats + static_cast<int64_t>(seq) * 8;
     st[0] += 1;                                    // steps
     st[1] += static_cast<unsigned long long>(nb);  // blocks visited
@@ -438,7 +478,7 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
     st[6] += acc[2];                               // first-wave (hot) blocks
     st[7] += acc[3];                               // second-wave blocks
   }
-  emit_tiles(fl, nb, 2, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters + 1, wtot, sbase);
+  emit_tiles(sflag, nb, 2, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters + 1, wtot, sbase);
 }
 
 // Part of a row's key histogram, added to hist[seq] (zero before the launch): CTA
@@ -507,7 +547,8 @@ ExactLayout exact_layout(int batch, int max_length, int k, int block_size) {
   L.tile_seq = take(static_cast<size_t>(L.tcap) * 4);
   L.tile_blk = take(static_cast<size_t>(L.tcap) * L.bpt * 4);
   L.counters = take(16);
-  L.hist = take(static_cast<size_t>(batch) * kKeyHistBins * 4);
+  const size_t segs = (static_cast<size_t>(max_length) + kTopkSegment - 1) / kTopkSegment;
+  L.hist = take(static_cast<size_t>(batch) * segs * kKeyHistBins * 4);
   L.topk_ws_bytes = topk_workspace_bytes(batch, max_length, k);
   L.topk_ws = take(L.topk_ws_bytes);
   L.total = off;
@@ -536,16 +577,20 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   int32_t* counters = reinterpret_cast<int32_t*>(state + L.counters);
   uint32_t* hist = reinterpret_cast<uint32_t*>(state + L.hist);
   void* tws = state + L.topk_ws;
-  // rows of one top-k segment select from the histogram the score waves build
-  const bool hist_for_topk = length <= kTopkSegment;
+  // the score waves build one key histogram per 32768-key segment of a row, which the
+  // top-k's first level starts from (and clears)
+  const int hsegs = (length + kTopkSegment - 1) / kTopkSegment;
+  const int max_segs = (max_length + kTopkSegment - 1) / kTopkSegment;
+  if (hsegs > kMaxHistSegs)
+    return fail(TDSA_ERR_UNSUPPORTED, "exact progressive: at most 2^21 keys per sequence");
 
   if (init) {
     TDSA_CUDA_CHECK(cudaMemsetAsync(maxsq, 0, static_cast<size_t>(batch) * L.nb_stride * 4,
                                     stream));
     TDSA_CUDA_CHECK(cudaMemsetAsync(stats, 0, static_cast<size_t>(batch) * 64, stream));
     TDSA_CUDA_CHECK(cudaMemsetAsync(counters, 0, 16, stream));
-    TDSA_CUDA_CHECK(cudaMemsetAsync(hist, 0, static_cast<size_t>(batch) * kKeyHistBins * 4,
-                                    stream));
+    TDSA_CUDA_CHECK(cudaMemsetAsync(
+        hist, 0, static_cast<size_t>(batch) * max_segs * kKeyHistBins * 4, stream));
   }
   // 1. norms of the appended keys: many (the first step) in a kernel of their own, a few
   // inside prepare
@@ -608,10 +653,11 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   ba.status = device_status_ptr();
   if (!ba.status) return fail(TDSA_ERR_CUDA, "device status word not available");
   const int grid = device_sm_count(current_device());
-  // 3. wave 1 (every block at the first step), its scores into the row histogram; the
-  // first step keeps the histogram only for the top-k
+  // 3. wave 1 (every block at the first step), its scores into the row's segment
+  // histograms
   ba.tile_count = counters;
-  ba.hist = (init && !hist_for_topk) ? nullptr : hist;
+  ba.hist = hist;
+  ba.hist_segs = hsegs;
   int rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
                                stream);
   if (rc) return rc;
@@ -635,25 +681,28 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
     wa.tile_blk = tile_blk;
     wa.counters = counters;
     wa.hist = hist;
-    wa.hist_for_topk = hist_for_topk ? 1 : 0;
+    wa.hist_segs = hsegs;
     wa.stats = stats;
+    // the histogram copies, then the row's block flags
+    const int w2_smem = kHistCopyBytes + ((ba.nblocks + 15) & ~15);
+    if (w2_smem > kWave2MaxSmem)
+      return fail(TDSA_ERR_UNSUPPORTED, "exact progressive: too many blocks per sequence");
     TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_wave2_kernel),
-                                        kHistCopyBytes));
-    TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), kHistCopyBytes,
+                                        w2_smem));
+    TDSA_CUDA_CHECK(launch_pdl(exact_wave2_kernel, dim3(batch), dim3(kThreads), w2_smem,
                                stream, wa));
     TDSA_CUDA_CHECK(cudaGetLastError());
     ba.tile_count = counters + 1;
-    ba.hist = hist_for_topk ? hist : nullptr;
     rc = launch_score_blocks(kModeExact, q, q_bs, keys, k_bs, k_rs, dtype, batch, ba, grid,
                              stream);
     if (rc) return rc;
   }
-  // 6. top-k over the row (from its histogram when it is one segment); the indices are also
-  // kept as the next step's seeds
+  // 6. top-k over the row, each first-level segment from its histogram; the indices are
+  // also kept as the next step's seeds
   void* oi = out_idx ? out_idx : topk;
   return launch_topk(scores, max_length, nullptr, 0, batch, length, k, sorted, oi,
                      out_idx ? idx_bytes : 4, out_idx ? idx_bs : k, out_val, val_bs, tws,
-                     L.topk_ws_bytes, stream, nullptr, hist_for_topk ? hist : nullptr,
+                     L.topk_ws_bytes, stream, nullptr, hist,
                      out_idx ? topk : nullptr, k);
 }
 

@@ -60,9 +60,11 @@ struct BlockArgs {
   int mask_invert = 0;                   // H8: a block is cold where the mask is zero
   const float* accept_max = nullptr;     // masked: keep = mask || accept_max >= *threshold
                                          // ([batch][bm_stride]), written to `accepted`
-  uint32_t* hist = nullptr;              // exact: [batch][4096] key histogram (top 12 bits
-                                         // of the order-preserving key) the epilogue adds
+  uint32_t* hist = nullptr;              // exact: [batch][hist_segs][4096] key histograms
+                                         // (top 12 bits of the order-preserving key), one
+                                         // per 32768-key segment of a row, the epilogue adds
                                          // every scored key to
+  int hist_segs = 1;
   int* status = nullptr;
 };
 

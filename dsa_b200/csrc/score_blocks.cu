@@ -39,6 +39,7 @@ constexpr int kBarrierBytes = 1024;
 constexpr int kSmemBytes = kStages * kStageBytes + 2 * kQBytes + kBarrierBytes + 1024;
 constexpr int kHistSmemBytes = kKeyHistBins * 4;  // exact mode with a key histogram
 constexpr int kMaxSlots = 8;  // blocks per tile at bs = 16
+static_assert(kTopkSegment == 1 << 15, "a key's histogram segment is its index >> 15");
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -296,7 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       restmask = a.remaining ? head_mask(a.remaining, kHeads - kVerifierHeads) : ~selmask;
     }
     const float thr = (kMode == kModeProgressive) ? *a.threshold : 0.f;
-    int prev_seq = -1;
+    int prev_seq = -1, prev_slot = -1;  // prev_slot: the (sequence, segment) histogram the
+                                        // shared counts belong to
     uint32_t acc_it = 0, hph = 0;
     float wr[kHeads];
     Tile tile;
@@ -309,10 +311,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++hph;
       return ok;
     };
-    // adds this CTA's counts of sequence `seq` to its row histogram and clears them
-    auto hist_flush = [&](int seq) -> bool {
+    // adds this CTA's counts of histogram `slot` (sequence * hist_segs + segment) to it and
+    // clears them
+    auto hist_flush = [&](int slot) -> bool {
       if (!hist_sync()) return false;
-      uint32_t* dst = a.hist + static_cast<int64_t>(seq) * kKeyHistBins;
+      uint32_t* dst = a.hist + static_cast<int64_t>(slot) * kKeyHistBins;
       for (int i = etid; i < kKeyHistBins; i += 128) {
         const uint32_t c = shist[i];
         if (c) {
@@ -326,9 +329,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       get_tile(a, t, tile);
       const int seq = tile.seq;
       if (seq != prev_seq) {
-        if (use_hist && prev_seq >= 0 && !hist_flush(prev_seq)) break;
         load_head_weights(a.w + static_cast<int64_t>(seq) * a.w_stride, wr);
         prev_seq = seq;
+      }
+      if (use_hist) {  // the slot of the tile's first block (a tile may end in the next one)
+        const int tslot = seq * a.hist_segs + ((max(tile.block[0], 0) * bs) >> 15);
+        if (tslot != prev_slot) {
+          if (prev_slot >= 0 && !hist_flush(prev_slot)) break;
+          prev_slot = tslot;
+        }
       }
       const int blk = tile.block[slot_j];
       const int key = blk * bs + ingroup;
@@ -396,7 +405,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (valid && (kMode != kModeH8 || a.out != nullptr))
         a.out[static_cast<int64_t>(seq) * a.out_stride + key] = out;
-      if (use_hist) add_to_bin(shist, valid, float_to_key(out) >> 20);
+      if (use_hist) {
+        const uint32_t bin = float_to_key(out) >> 20;
+        const int kslot = seq * a.hist_segs + (key >> 15);
+        add_to_bin(shist, valid && kslot == prev_slot, bin);
+        if (valid && kslot != prev_slot)
+          atomicAdd(a.hist + static_cast<int64_t>(kslot) * kKeyHistBins + bin, 1u);
+      }
       if (blk >= 0 && ingroup == 0) {
         if (kMode == kModeMasked) {
           if (a.accepted) a.accepted[static_cast<int64_t>(seq) * a.bm_stride + blk] = flag ? 1 : 0;
@@ -408,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       ++acc_it;
-      if (use_hist && t + 1 == t1) hist_flush(seq);
+      if (use_hist && t + 1 == t1) hist_flush(prev_slot);
     }
   }
 

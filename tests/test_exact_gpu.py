@@ -107,6 +107,54 @@ def test_exact_plan_matches_function_form(block_size):
         plan.step(l0)  # append-only
 
 
+@pytest.mark.parametrize("block_size,structured,l0", [
+    (64, True, 32760),     # crosses into a second 32768-key segment
+    (16, True, 65530),     # crosses into a third segment at block size 16
+    (128, False, 70001),   # three segments, i.i.d. keys, an odd score-row stride
+    (32, True, 98300),     # crosses into a fourth segment
+])
+def test_exact_long_rows_segment_histograms(block_size, structured, l0):
+    """Rows longer than one 32768-key top-k segment: the score waves keep one key
+    histogram per segment (pruned keys counted in its -inf bin) and the top-k's first level
+    starts every segment from its own; exact == dense bit for bit at every step, sorted and
+    unsorted, including the steps that open a new segment."""
+    from dsa_b200.indexer import ScoreTopkPlan
+    from dsa_b200.progressive_exact import ExactProgressivePlan
+
+    batch, steps, k = 3, 8, 2048
+    g = torch.Generator().manual_seed(l0 + block_size)
+    total = l0 + steps
+    keys = torch.randn(batch, total, 128, generator=g)
+    w = torch.randn(batch, 64, generator=g).abs() / 8 if structured else \
+        torch.randn(batch, 64, generator=g) / 8
+    if structured:
+        nb = (total + block_size - 1) // block_size
+        scale = torch.where(torch.rand(batch, nb, generator=g) < 0.25, 3.0, 0.05)
+        keys *= scale.repeat_interleave(block_size, dim=1)[:, :total, None]
+    cache = keys.to(torch.bfloat16).cuda()
+    q = torch.randn(batch, 64, 128, generator=g) / math.sqrt(128)
+    rho, innov = (0.999, 0.02) if structured else (0.95, math.sqrt(1 - 0.95 ** 2))
+    qbuf = q.to(torch.bfloat16).cuda()
+    wc = w.cuda()
+    plans = {}
+    for sorted_ in (False, True):
+        plans[sorted_] = ExactProgressivePlan(qbuf, wc, cache, k, block_size=block_size,
+                                              sorted=sorted_)
+        plans[sorted_].init(l0)
+    for t in range(1, steps + 1):
+        q = rho * q + innov * torch.randn(batch, 64, 128, generator=g) / math.sqrt(128)
+        qbuf.copy_(q.to(torch.bfloat16))
+        length = l0 + t
+        for sorted_, plan in plans.items():
+            got_i, got_v = plan.step(length)
+            want_i, want_v = ScoreTopkPlan(qbuf, wc, cache[:, :length], k, sorted=sorted_).run()
+            assert torch.equal(got_i.long(), want_i.long()), (t, sorted_)
+            assert torch.equal(got_v, want_v), (t, sorted_)
+    st = plans[False].stats()
+    if structured:
+        assert all(s["blocks_pruned"] > 0 for s in st)
+
+
 def test_exact_progressive_prunes_structured_cache_and_stays_exact():
     """Blocks of small-norm keys next to a few large ones: the bound must skip them."""
     from dsa_b200 import score_dense, topk
