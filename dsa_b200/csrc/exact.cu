@@ -99,121 +99,164 @@ struct PrepArgs {
   int init;  // 1: every block is scored (first step)
 };
 
+// Blocks (and previous top-k entries) whose loads a thread issues before any barrier: the
+// whole state of a sequence of up to 2048 blocks arrives in one round trip.
+constexpr int kPrepUnroll = 2;
+
 __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs a) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
-  __shared__ double coeff[64];
-  __shared__ double c_total;
+  extern __shared__ int8_t hot[];  // [nb]: this step's wave-1 flags
+  __shared__ double wsum[32];
   static_assert(kThreads == 8192 / 8, "one thread per 8 query elements");
   __shared__ uint32_t wtot[32];
   __shared__ uint32_t sbase[4];
   const int seq = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nb = (a.length + a.bs - 1) / a.bs;
-  const int prev_nb = (a.prev_length + a.bs - 1) / a.bs;
   // blocks holding keys appended since the last step are never pruned (replay.py:263-266)
   const int first_new = a.init ? 0 : (a.length > a.prev_length ? a.prev_length / a.bs : nb);
   const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
-  int8_t* flag = a.flag + brow;
-  if (seq == 0 && threadIdx.x == 0) a.counters[1] = 0;  // wave 2's list (used after this)
+  if (seq == 0 && tid == 0) a.counters[1] = 0;  // wave 2's list (used after this)
 
+  // ---- every load of the step's state, issued before the first barrier.  Thread t owns q
+  // elements [8t, 8t + 8) (one 16-byte load; rows are 16-byte aligned: the scoring kernels'
+  // TMA rules), 16 threads per head, blocks t + 1024 j and previous top-k entries t + 1024 j.
+  const int h = tid >> 4;
+  const uint4 qv = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.q) +
+                                                  static_cast<int64_t>(seq) * a.q_bs)[tid];
+  uint4* qp4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.qprev) +
+                                        static_cast<int64_t>(seq) * 8192) + tid;
+  const float wn = a.w[static_cast<int64_t>(seq) * a.w_bs + h];
+  float* wp_row = a.wprev + static_cast<int64_t>(seq) * 64;
+  uint4 pv = make_uint4(0u, 0u, 0u, 0u);
+  float wp = 0.f;
+  int8_t pflag[kPrepUnroll] = {};
+  float pmax[kPrepUnroll] = {}, pbound[kPrepUnroll] = {};
+  uint32_t pnsq[kPrepUnroll] = {};
+  int32_t ptop[kPrepUnroll] = {-1, -1};
+  if (!a.init) {
+    pv = *qp4;
+    wp = wp_row[h];
+#pragma unroll
+    for (int j = 0; j < kPrepUnroll; ++j) {
+      const int b = tid + j * kThreads;
+      if (b < first_new) {
+        pflag[j] = a.flag[brow + b];
+        pmax[j] = a.bmax[brow + b];
+        pbound[j] = a.bound[brow + b];
+        pnsq[j] = a.maxsq[brow + b];
+      }
+      const int i = tid + j * kThreads;
+      ptop[j] = i < a.k ? a.prev_topk[static_cast<int64_t>(seq) * a.k + i] : -1;
+    }
+  }
   if (a.fold_norms) {  // few appended keys: one warp per key, into blocks >= first_new
-    for (int key = a.prev_length + (threadIdx.x >> 5); key < a.length; key += kThreads / 32)
+    for (int key = a.prev_length + warp; key < a.length; key += kThreads / 32)
       fold_key_norm(a.keys, static_cast<int64_t>(seq) * a.k_bs, a.k_rs, a.dtype, key, a.bs,
                     a.maxsq + brow);
   }
-  // Thread t owns q elements [8t, 8t + 8) (one 16-byte load; rows are 16-byte aligned: the
-  // scoring kernels' TMA rules): 16 threads per head.  It reads the previous step's copy of
-  // the same elements, then stores the current ones in its place for the next step.
-  {
-    const int h = threadIdx.x >> 4;
-    const uint4 qv = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.q) +
-                                                    static_cast<int64_t>(seq) * a.q_bs)[threadIdx.x];
-    uint4* qp4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.qprev) +
-                                          static_cast<int64_t>(seq) * 8192) + threadIdx.x;
-    const float wn = a.w[static_cast<int64_t>(seq) * a.w_bs + h];
-    float* wp_row = a.wprev + static_cast<int64_t>(seq) * 64;
-    if (!a.init) {
-      // coefficient in float64
-      const uint4 pv = *qp4;
-      const double wp = wp_row[h];
-      const uint32_t nw[4] = {qv.x, qv.y, qv.z, qv.w}, pw[4] = {pv.x, pv.y, pv.z, pv.w};
-      double dd = 0.0, pp = 0.0, nn = 0.0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint16_t nb16 = static_cast<uint16_t>(nw[j >> 1] >> (16 * (j & 1)));
-        const uint16_t pb16 = static_cast<uint16_t>(pw[j >> 1] >> (16 * (j & 1)));
-        const double qn = a.dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(nb16) << 16)
-                                               : __half2float(__ushort_as_half(nb16));
-        const double qpv = a.dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(pb16) << 16)
-                                                : __half2float(__ushort_as_half(pb16));
-        dd += (qn - qpv) * (qn - qpv);
-        pp += qpv * qpv;
-        nn += qn * qn;
-      }
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) {
-        dd += __shfl_xor_sync(0xffffffffu, dd, o);
-        pp += __shfl_xor_sync(0xffffffffu, pp, o);
-        nn += __shfl_xor_sync(0xffffffffu, nn, o);
-      }
-      if ((threadIdx.x & 15) == 0) {
-        const double nqp = sqrt(pp), nqn = sqrt(nn), ndq = sqrt(dd);
-        coeff[h] = fabs(wn - wp) * nqp + fabs(wn) * ndq +
-                   kGamma * (fabs(wn) * nqn + fabs(wp) * nqp);
-      }
-    }
-    *qp4 = qv;
-    __syncthreads();  // every read of wprev (and coeff written)
-    if ((threadIdx.x & 15) == 0) wp_row[h] = wn;
-    if (!a.init && threadIdx.x < 32) {
-      // the 64 head terms summed in a fixed order (lane l: heads l and l + 32)
-      double c = coeff[threadIdx.x] + coeff[threadIdx.x + 32];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-      if (threadIdx.x == 0) c_total = c * (1.0 + 0x1p-40);
-    }
-  }
-  __syncthreads();
-  // the previous step's state update, then this step's bounds and flags (block b is
-  // updated and read by the same thread)
-  for (int b = threadIdx.x; b < nb; b += kThreads) {
-    float bnd = INFINITY;
-    if (b < first_new) {
-      float u = a.upper[brow + b];
-      if (b < prev_nb) {
-        u = flag[b] ? a.bmax[brow + b] : a.bound[brow + b];
-        a.upper[brow + b] = u;
-      }
-      const double nrm = static_cast<double>(__fsqrt_ru(__uint_as_float(a.maxsq[brow + b])));
-      bnd = __double2float_ru(static_cast<double>(u) + nrm * c_total);
-    }
-    a.bound[brow + b] = bnd;
-    flag[b] = (a.init || b >= first_new) ? 1 : 0;
-  }
-  __syncthreads();
+
+  // ---- certified coefficient c = sum_h |w_t-w_p| ||q_p,h|| + |w_t| ||q_t,h-q_p,h|| plus
+  // the rounding slack, in float64; the 64 head terms are summed in a fixed order (pairs
+  // of heads per warp, then the 32 warp sums)
   if (!a.init) {
-    const int32_t* top = a.prev_topk + static_cast<int64_t>(seq) * a.k;
-    for (int i = threadIdx.x; i < a.k; i += kThreads) {
-      const int blk = top[i] / a.bs;
-      if (blk >= 0 && blk < nb) flag[blk] = 1;
+    const uint32_t nw[4] = {qv.x, qv.y, qv.z, qv.w}, pw[4] = {pv.x, pv.y, pv.z, pv.w};
+    double dd = 0.0, pp = 0.0, nn = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint16_t nb16 = static_cast<uint16_t>(nw[j >> 1] >> (16 * (j & 1)));
+      const uint16_t pb16 = static_cast<uint16_t>(pw[j >> 1] >> (16 * (j & 1)));
+      const double qn = a.dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(nb16) << 16)
+                                             : __half2float(__ushort_as_half(nb16));
+      const double qpv = a.dtype == TDSA_BF16 ? __uint_as_float(static_cast<uint32_t>(pb16) << 16)
+                                              : __half2float(__ushort_as_half(pb16));
+      dd += (qn - qpv) * (qn - qpv);
+      pp += qpv * qpv;
+      nn += qn * qn;
     }
-  } else if (threadIdx.x == 0) {  // the first step scores every block
-    unsigned long long* st = a.stats + static_cast<int64_t>(seq) * 8;
-    st[0] += 1;
-    st[1] += static_cast<unsigned long long>(nb);
-    st[2] += static_cast<unsigned long long>(nb);
-    st[4] += static_cast<unsigned long long>(a.length);
-    st[5] += static_cast<unsigned long long>(a.length);
-    st[6] += static_cast<unsigned long long>(nb);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      dd += __shfl_xor_sync(0xffffffffu, dd, o);
+      pp += __shfl_xor_sync(0xffffffffu, pp, o);
+      nn += __shfl_xor_sync(0xffffffffu, nn, o);
+    }
+    double term = 0.0;
+    if ((tid & 15) == 0) {
+      const double wpd = wp;
+      const double nqp = sqrt(pp), nqn = sqrt(nn), ndq = sqrt(dd);
+      term = fabs(wn - wpd) * nqp + fabs(wn) * ndq + kGamma * (fabs(wn) * nqn + fabs(wpd) * nqp);
+    }
+    term += __shfl_xor_sync(0xffffffffu, term, 16);  // heads 2 warp and 2 warp + 1
+    if (lane == 0) wsum[warp] = term;
   }
-  __syncthreads();
-  emit_tiles(flag, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters, wtot, sbase);
+  *qp4 = qv;  // kept for the next step (this thread read the old copy above)
+  // wave 1 starts as the blocks with new keys (every block at the first step)
+  for (int b = tid; b < nb; b += kThreads) hot[b] = (a.init || b >= first_new) ? 1 : 0;
+  __syncthreads();  // every read of wprev; the warp sums; hot[] prefilled
+  if ((tid & 15) == 0) wp_row[h] = wn;
+  if (!a.init) {
+    // the 32 warp sums reduced by a butterfly in a fixed order (every warp alike)
+    double c = wsum[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    const double c_total = c * (1.0 + 0x1p-40);
+    // the blocks holding a previous top-k key join wave 1 (hot first, replay.py:153-169)
+#pragma unroll
+    for (int j = 0; j < kPrepUnroll; ++j) {
+      const int blk = ptop[j] >= 0 ? ptop[j] / a.bs : -1;
+      if (blk >= 0 && blk < nb) hot[blk] = 1;
+    }
+    for (int i = tid + kPrepUnroll * kThreads; i < a.k; i += kThreads) {
+      const int32_t t = a.prev_topk[static_cast<int64_t>(seq) * a.k + i];
+      const int blk = t >= 0 ? t / a.bs : -1;
+      if (blk >= 0 && blk < nb) hot[blk] = 1;
+    }
+    // the previous step's state update (U_b <- exact block max of a scored block, its
+    // bound when pruned), then this step's bound U_b + maxnorm_b * c; a block below
+    // first_new (<= the previous step's block count) existed at the previous step
+    auto update = [&](int b, int8_t f, float bm, float bo, uint32_t nsq) {
+      float bnd = INFINITY;
+      if (b < first_new) {
+        const float u = f ? bm : bo;
+        a.upper[brow + b] = u;
+        const double nrm = static_cast<double>(__fsqrt_ru(__uint_as_float(nsq)));
+        bnd = __double2float_ru(static_cast<double>(u) + nrm * c_total);
+      }
+      a.bound[brow + b] = bnd;
+    };
+#pragma unroll
+    for (int j = 0; j < kPrepUnroll; ++j) {
+      const int b = tid + j * kThreads;
+      if (b < nb) update(b, pflag[j], pmax[j], pbound[j], pnsq[j]);
+    }
+    for (int b = tid + kPrepUnroll * kThreads; b < nb; b += kThreads) {
+      if (b < first_new)
+        update(b, a.flag[brow + b], a.bmax[brow + b], a.bound[brow + b], a.maxsq[brow + b]);
+      else
+        update(b, 0, 0.f, 0.f, 0u);
+    }
+  } else {
+    for (int b = tid; b < nb; b += kThreads) a.bound[brow + b] = INFINITY;
+    if (tid == 0) {  // the first step scores every block (adds that return nothing)
+      unsigned long long* st = a.stats + static_cast<int64_t>(seq) * 8;
+      atomicAdd(&st[0], 1ull);
+      atomicAdd(&st[1], static_cast<unsigned long long>(nb));
+      atomicAdd(&st[2], static_cast<unsigned long long>(nb));
+      atomicAdd(&st[4], static_cast<unsigned long long>(a.length));
+      atomicAdd(&st[5], static_cast<unsigned long long>(a.length));
+      atomicAdd(&st[6], static_cast<unsigned long long>(nb));
+    }
+  }
+  __syncthreads();  // hot[] complete
+  for (int b = tid; b < nb; b += kThreads) a.flag[brow + b] = hot[b];
+  emit_tiles(hot, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters, wtot, sbase);
 }
 
 constexpr int kHistCopies = 8;  // private copies of the row histogram (one per 4 warps)
 constexpr int kHistCopyBytes = kHistCopies * kKeyHistBins * 4;
-// dynamic shared memory of the wave-2 kernel: the copies plus one flag byte per block (the
-// static part holds another 16 KB histogram)
+// largest dynamic shared memory of the prepare and wave-2 kernels (one flag byte per block,
+// after wave 2's 16 KB of sub-bin counts)
 constexpr int kWave2MaxSmem = 200 * 1024;
 constexpr int kMaxHistSegs = 64;  // 32768-key histogram segments per sequence (2^21 keys)
 static_assert(kTopkSegment == 1 << 15, "a key's histogram segment is its index >> 15");
@@ -271,46 +314,17 @@ struct Wave2Args {
   unsigned long long* stats;
 };
 
-__global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a) {
-  pdl_wait();  // every global access follows the previous kernel
-  pdl_launch_dependents();
-  extern __shared__ uint32_t hcopies[];  // kHistCopies x 4096 words, then the row's flags
-  __shared__ uint32_t h[kKeyHistBins];
-  __shared__ uint32_t wtot[32];
-  __shared__ uint32_t sbase[4];
-  __shared__ unsigned long long acc[5];
-  __shared__ float s_tau;
-  __shared__ uint32_t s_bin, s_rank;
-  __shared__ uint32_t seg_pruned[kMaxHistSegs];  // pruned keys per segment
-  const int seq = blockIdx.x;
+constexpr int kW2Vec = 8;  // 16-byte score pieces per thread per pass (32768 keys per CTA)
+
+// One step of a CTA-wide selection from the top of a 4096-bin histogram: thread t holds bins
+// 4095-4t .. 4092-4t in c[0..3].  Returns true in the one thread whose bins hold the kk-th
+// largest key, with that bin and the key's rank inside it (from the top); no thread does
+// when fewer than kk keys are counted.  `wtot` (32 words) is free on entry; the caller
+// passes a barrier before it is reused.
+__device__ __forceinline__ bool select_bin(const uint32_t (&c)[4], uint32_t kk, uint32_t* wtot,
+                                           uint32_t& bin, uint32_t& rank) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nb = (a.length + a.bs - 1) / a.bs;
-  const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
-  int8_t* sflag = reinterpret_cast<int8_t*>(hcopies + kHistCopies * kKeyHistBins);  // [nb]
-  float* srow = a.scores + static_cast<int64_t>(seq) * a.l_stride;
-  uint32_t* grow = a.hist + static_cast<int64_t>(seq) * a.hist_segs * kKeyHistBins;
-  // the row in 16-byte pieces when its base allows (bs is a multiple of 4, so a piece lies
-  // in one block): 4 keys per load or store, all of a thread's pieces in flight at once
-  const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0u;
-  const int nvec = vec ? a.length >> 2 : 0;
-  const int bshift = __ffs(a.bs) - 1;  // block sizes are powers of two
-  if (seq == 0 && threadIdx.x == 0) a.counters[0] = 0;  // wave 1 of this step is done
-  if (threadIdx.x < 5) acc[threadIdx.x] = 0ull;
-  if (threadIdx.x < kMaxHistSegs) seg_pruned[threadIdx.x] = 0u;
-  for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {  // the row's counts
-    uint32_t t = 0;
-    for (int g = 0; g < a.hist_segs; ++g) t += grow[g * kKeyHistBins + i];
-    h[i] = t;
-  }
-  for (int b = threadIdx.x; b < nb; b += kThreads) sflag[b] = a.flag[brow + b];
-  __syncthreads();
-  // thread t owns bins 4095-4t .. 4092-4t: keys above a thread's bins by a CTA scan
-  uint32_t c[4], tot = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    c[i] = h[kKeyHistBins - 1 - (4 * threadIdx.x + i)];
-    tot += c[i];
-  }
+  const uint32_t tot = c[0] + c[1] + c[2] + c[3];
   uint32_t x = tot;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -318,118 +332,196 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
     if (lane >= o) x += y;
   }
   if (lane == 31) wtot[warp] = x;
-  if (threadIdx.x == 0) s_tau = -INFINITY;  // fewer than k wave-1 scores: prune nothing
   __syncthreads();
-  uint32_t above = x - tot;
-  for (int i = 0; i < warp; ++i) above += wtot[i];
-  const uint32_t kk = static_cast<uint32_t>(a.k);
-  if (threadIdx.x == 0) s_bin = 0xFFFFFFFFu;
+  // keys in the earlier warps: an inclusive scan of the 32 warp totals, read at warp - 1
+  uint32_t wt = wtot[lane];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, wt, o);
+    if (lane >= o) wt += y;
+  }
+  const uint32_t earlier = __shfl_sync(0xffffffffu, wt, (warp + 31) & 31);
+  uint32_t above = x - tot + (warp ? earlier : 0u);
+  bool found = false;
   if (above < kk && kk <= above + tot) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      if (above < kk && kk <= above + c[i]) {
-        s_bin = kKeyHistBins - 1 - (4 * threadIdx.x + i);
-        s_rank = kk - above;  // rank of the k-th key inside its bin, from the top
+      if (!found && kk <= above + c[i]) {
+        bin = kKeyHistBins - 1 - (4 * threadIdx.x + i);
+        rank = kk - above;
+        found = true;
       }
       above += c[i];
     }
   }
+  return found;
+}
+
+// Adds the scored keys of bin `bin1` among four scores to the sub-bin histogram (the next 12
+// key bits).  The keys of one bin are few (a few percent of the row) and spread over 4096
+// sub-bins, so every lane adds alone.  With kFloat the bin test compares the floats with the
+// bin's smallest and largest float [f_lo, f_hi] (two compares per key; the key is formed
+// only for the keys inside), which is exact for bins of finite nonzero floats: the key map is
+// monotone there.  The pass runs on one SM per sequence and is bound by its integer pipe.
+template <bool kFloat>
+__device__ __forceinline__ void add_sub_bins(uint32_t* h2, float4 v, bool scored, uint32_t bin1,
+                                             float f_lo, float f_hi) {
+  const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const bool in = kFloat ? scored && e[u] >= f_lo && e[u] <= f_hi
+                           : scored && (float_to_key(e[u]) >> 20) == bin1;
+    if (in) atomicAdd(&h2[(float_to_key(e[u]) >> 8) & 0xFFFu], 1u);
+  }
+}
+
+// Level 2 of tau over a row held partly in registers (v: pieces tid + 1024 j of the first
+// 32768 keys) and the rest read here.
+template <bool kFloat>
+__device__ __forceinline__ void sub_bin_pass(uint32_t* h2, const float4 (&v)[8], const float* srow,
+                                             int nvec, const int8_t* sflag, int bshift,
+                                             uint32_t bin1, float f_lo, float f_hi) {
+  const int tid = threadIdx.x;
+  const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (j * 1024 < nvec) {  // uniform: rows shorter than 32768 keys skip the empty pieces
+      const int i = tid + j * 1024;
+      add_sub_bins<kFloat>(h2, v[j], i < nvec && sflag[(4 * i) >> bshift] == 1, bin1, f_lo, f_hi);
+    }
+  }
+  for (int base = 8 * 1024; base < nvec; base += 8 * 1024) {
+    float4 w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + tid + j * 1024;
+      w[j] = i < nvec ? reinterpret_cast<const float4*>(srow)[i] : ninf;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + tid + j * 1024;
+      add_sub_bins<kFloat>(h2, w[j], i < nvec && sflag[(4 * i) >> bshift] == 1, bin1, f_lo, f_hi);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a) {
+  pdl_wait();  // every global access follows the previous kernel
+  pdl_launch_dependents();
+  extern __shared__ uint32_t dyn[];  // the 4096 sub-bin counts, then the row's block flags
+  uint32_t* h2 = dyn;
+  int8_t* sflag = reinterpret_cast<int8_t*>(dyn + kKeyHistBins);  // [nb]
+  __shared__ uint32_t wtot[32];
+  __shared__ uint32_t sbase[4];
+  __shared__ uint32_t acc[5];
+  __shared__ float s_tau;
+  __shared__ uint32_t s_bin, s_rank;
+  __shared__ uint32_t seg_pruned[kMaxHistSegs];  // pruned keys per segment
+  const int seq = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nb = (a.length + a.bs - 1) / a.bs;
+  const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
+  float* srow = a.scores + static_cast<int64_t>(seq) * a.l_stride;
+  uint32_t* grow = a.hist + static_cast<int64_t>(seq) * a.hist_segs * kKeyHistBins;
+  // the row in 16-byte pieces when its base allows (bs is a multiple of 4, so a piece lies
+  // in one block)
+  const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0u;
+  const int nvec = vec ? a.length >> 2 : 0;
+  const int bshift = __ffs(a.bs) - 1;  // block sizes are powers of two
+  const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+
+  // ---- loads issued together: this thread's 4 bins of every segment histogram, the
+  // bounds of blocks tid and tid + 1024, the row's flags and its first 32768 scores
+  // (pieces tid + 1024 j, read whatever their block: unscored ones are masked later)
+  uint32_t c[4] = {0u, 0u, 0u, 0u};
+  for (int g = 0; g < a.hist_segs; ++g) {
+    const uint4 t = reinterpret_cast<const uint4*>(grow + g * kKeyHistBins)[kThreads - 1 - tid];
+    c[0] += t.w;
+    c[1] += t.z;
+    c[2] += t.y;
+    c[3] += t.x;
+  }
+  float pb[2];
+  int8_t pf[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int b = tid + j * kThreads;
+    pb[j] = b < nb ? a.bound[brow + b] : 0.f;
+    pf[j] = b < nb ? a.flag[brow + b] : 0;
+  }
+  float4 v[kW2Vec];
+#pragma unroll
+  for (int j = 0; j < kW2Vec; ++j) {
+    const int i = tid + j * kThreads;
+    v[j] = i < nvec ? reinterpret_cast<const float4*>(srow)[i] : ninf;
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+    if (tid + j * kThreads < nb) sflag[tid + j * kThreads] = pf[j];
+  for (int b = tid + 2 * kThreads; b < nb; b += kThreads) sflag[b] = a.flag[brow + b];
+  for (int i = tid; i < kKeyHistBins; i += kThreads) h2[i] = 0u;
+  if (seq == 0 && tid == 0) a.counters[0] = 0;  // wave 1 of this step is done
+  if (tid < 5) acc[tid] = 0u;
+  if (tid < kMaxHistSegs) seg_pruned[tid] = 0u;
+  if (tid == 0) {
+    s_bin = 0xFFFFFFFFu;
+    s_tau = -INFINITY;  // fewer than k wave-1 scores: prune nothing
+  }
+  // a row whose blocks were all scored in wave 1 has nothing to prune: no tau
+  bool unscored = false;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) unscored |= tid + j * kThreads < nb && pf[j] == 0;
+  for (int b = tid + 2 * kThreads; b < nb; b += kThreads) unscored |= sflag[b] == 0;
+  const bool any_unscored = __syncthreads_or(unscored) != 0;
+
+  // ---- level 1: the bin holding the k-th largest wave-1 score
+  uint32_t bin, rank;
+  if (any_unscored && select_bin(c, static_cast<uint32_t>(a.k), wtot, bin, rank)) {
+    s_bin = bin;
+    s_rank = rank;
+  }
   __syncthreads();
   const uint32_t bin1 = s_bin;
   if (bin1 != 0xFFFFFFFFu && bin1 != 0u) {
-    // second level: the next 12 key bits of the wave-1 keys in that bin (the row holds
-    // stale scores outside the wave-1 blocks) narrow tau to 2^8 keys
-    for (int i = threadIdx.x; i < kHistCopies * kKeyHistBins; i += kThreads) hcopies[i] = 0u;
-    __syncthreads();
-    uint32_t* mine = hcopies + (warp & (kHistCopies - 1)) * kKeyHistBins;
-    // only the wave-1 blocks' scores are read; 8 independent loads per thread in flight
-    // (the pass is bound by load latency)
-    constexpr int kUnroll = 8;
-    for (int base = 0; base < nvec; base += kThreads * kUnroll) {
-      float4 v[kUnroll];
-      bool scored[kUnroll];
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const int i = base + j * kThreads + static_cast<int>(threadIdx.x);
-        scored[j] = i < nvec && sflag[(4 * i) >> bshift] == 1;
-        v[j] = scored[j] ? reinterpret_cast<const float4*>(srow)[i]
-                         : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      }
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t key = float_to_key(e[u]);
-          add_to_bin(mine, scored[j] && (key >> 20) == bin1, (key >> 8) & 0xFFFu);
-        }
-      }
-    }
+    // level 2: the next 12 key bits of the wave-1 keys in that bin (the row holds stale
+    // scores outside the wave-1 blocks) narrow tau to 2^8 keys.  Bins of finite nonzero
+    // floats (8 .. 0xFF7 but not the two holding zero) test the floats themselves.
+    static_assert(kW2Vec == 8 && kThreads == 1024, "sub_bin_pass layout");
+    const float f_lo = key_to_float(bin1 << 20), f_hi = key_to_float((bin1 << 20) | 0xFFFFFu);
+    if (bin1 >= 8u && bin1 <= 0xFF7u && bin1 != 0x7FFu && bin1 != 0x800u)
+      sub_bin_pass<true>(h2, v, srow, nvec, sflag, bshift, bin1, f_lo, f_hi);
+    else
+      sub_bin_pass<false>(h2, v, srow, nvec, sflag, bshift, bin1, f_lo, f_hi);
     // the keys past the 16-byte pieces (all of them when the row is not 16-byte aligned)
-    for (int base = 4 * nvec; base < a.length; base += kThreads * kUnroll) {
-      float v[kUnroll];
-      bool scored[kUnroll];
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const int i = base + j * kThreads + static_cast<int>(threadIdx.x);
-        scored[j] = i < a.length && sflag[i >> bshift] == 1;
-        v[j] = scored[j] ? srow[i] : -INFINITY;
-      }
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const uint32_t key = float_to_key(v[j]);
-        add_to_bin(mine, scored[j] && (key >> 20) == bin1, (key >> 8) & 0xFFFu);
-      }
+    for (int base = 4 * nvec; base < a.length; base += kThreads) {
+      const int i = base + tid;
+      const bool scored = i < a.length && sflag[i >> bshift] == 1;
+      const uint32_t key = float_to_key(scored ? srow[i] : -INFINITY);
+      if (scored && (key >> 20) == bin1) atomicAdd(&h2[(key >> 8) & 0xFFFu], 1u);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) {
-      uint32_t t = 0;
-#pragma unroll
-      for (int cc = 0; cc < kHistCopies; ++cc) t += hcopies[cc * kKeyHistBins + i];
-      h[i] = t;
-    }
-    __syncthreads();
-    const uint32_t r = s_rank;
-    uint32_t d[4], dt = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      d[i] = h[kKeyHistBins - 1 - (4 * threadIdx.x + i)];
-      dt += d[i];
-    }
-    uint32_t y = dt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t z = __shfl_up_sync(0xffffffffu, y, o);
-      if (lane >= o) y += z;
-    }
-    if (lane == 31) wtot[warp] = y;
-    __syncthreads();
-    uint32_t ab = y - dt;
-    for (int i = 0; i < warp; ++i) ab += wtot[i];
-    if (ab < r && r <= ab + dt) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (ab < r && r <= ab + d[i]) {
-          const uint32_t lo = (bin1 << 20) | ((kKeyHistBins - 1 - (4 * threadIdx.x + i)) << 8);
-          // the smallest key of the sub-bin as a float (past +inf only NaN: +inf)
-          s_tau = lo > 0xFF800000u ? INFINITY : key_to_float(lo);
-        }
-        ab += d[i];
-      }
+    const uint4 t = reinterpret_cast<const uint4*>(h2)[kThreads - 1 - tid];
+    const uint32_t d[4] = {t.w, t.z, t.y, t.x};
+    if (select_bin(d, s_rank, wtot, bin, rank)) {
+      const uint32_t lo = (bin1 << 20) | (bin << 8);
+      // the smallest key of the sub-bin as a float (past +inf only NaN: +inf)
+      s_tau = lo > 0xFF800000u ? INFINITY : key_to_float(lo);
     }
     __syncthreads();
   }
-  const float t = s_tau;
-  if (threadIdx.x == 0) a.tau[seq] = t;
-  unsigned long long scored = 0, keys = 0, hot = 0, second = 0, pruned_keys = 0;
-  for (int b = threadIdx.x; b < nb; b += kThreads) {
+  const float tau = s_tau;
+  if (tid == 0) a.tau[seq] = tau;
+
+  // ---- wave 2: unscored blocks whose bound reaches tau; the rest are pruned
+  uint32_t scored = 0, keys = 0, hot = 0, second = 0, pruned_keys = 0;
+  auto decide = [&](int b, float bound) -> uint32_t {
     int8_t f = sflag[b];
-    if (f == 0 && a.bound[brow + b] >= t) {
+    if (f == 0 && bound >= tau) {
       f = 2;
       sflag[b] = 2;
       a.flag[brow + b] = 2;
     }
-    const unsigned long long n = static_cast<unsigned long long>(min(a.bs, a.length - b * a.bs));
+    const uint32_t n = static_cast<uint32_t>(min(a.bs, a.length - b * a.bs));
     if (f) {
       ++scored;
       keys += n;
@@ -437,18 +529,36 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
       second += f == 2;
     } else {
       pruned_keys += n;
-      atomicAdd(&seg_pruned[(b * a.bs) >> 15], static_cast<uint32_t>(n));
     }
-  }
-  // warp sums first: 64-bit shared atomics from every thread on one word serialise
+    return f ? 0u : n;
+  };
+  // pruned keys per histogram segment: a warp's 32 consecutive blocks span at most two
+  auto seg_add = [&](int b, uint32_t n) {
+    const int seg = b < nb ? (b * a.bs) >> 15 : -1;
+    const int seg0 = __shfl_sync(0xffffffffu, seg, 0);
+    const uint32_t lo = __reduce_add_sync(0xffffffffu, seg == seg0 ? n : 0u);
+    const uint32_t hi = __reduce_add_sync(0xffffffffu, seg != seg0 ? n : 0u);
+    const int seg31 = __shfl_sync(0xffffffffu, seg, 31);
+    if (lane == 0) {
+      if (lo && seg0 >= 0) atomicAdd(&seg_pruned[seg0], lo);
+      if (hi) atomicAdd(&seg_pruned[seg31 >= 0 ? seg31 : seg0 + 1], hi);
+    }
+  };
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    scored += __shfl_xor_sync(0xffffffffu, scored, o);
-    keys += __shfl_xor_sync(0xffffffffu, keys, o);
-    hot += __shfl_xor_sync(0xffffffffu, hot, o);
-    second += __shfl_xor_sync(0xffffffffu, second, o);
-    pruned_keys += __shfl_xor_sync(0xffffffffu, pruned_keys, o);
+  for (int j = 0; j < 2; ++j) {
+    const int b = tid + j * kThreads;
+    if (j * kThreads < nb) seg_add(b, b < nb ? decide(b, pb[j]) : 0u);
   }
+  for (int b0 = 2 * kThreads; b0 < nb; b0 += kThreads) {
+    const int b = b0 + tid;
+    seg_add(b, b < nb ? decide(b, a.bound[brow + b]) : 0u);
+  }
+  // warp sums first (a row's counts fit 32 bits), then one shared add per warp and count
+  scored = __reduce_add_sync(0xffffffffu, scored);
+  keys = __reduce_add_sync(0xffffffffu, keys);
+  hot = __reduce_add_sync(0xffffffffu, hot);
+  second = __reduce_add_sync(0xffffffffu, second);
+  pruned_keys = __reduce_add_sync(0xffffffffu, pruned_keys);
   if (lane == 0) {
     atomicAdd(&acc[0], scored);
     atomicAdd(&acc[1], keys);
@@ -457,28 +567,40 @@ __global__ void __launch_bounds__(kThreads) exact_wave2_kernel(const Wave2Args a
     atomicAdd(&acc[4], pruned_keys);
   }
   __syncthreads();
+  // the wave-2 list's place: the atomic is in flight while the pruned keys are filled
+  if (tid == 0) {
+    const uint32_t ntiles = (acc[3] + a.bpt - 1) / a.bpt;
+    if (gridDim.x == 1) {
+      sbase[3] = 0u;
+      a.counters[1] = static_cast<int32_t>(ntiles);  // zeroed by this step's prepare
+    } else {
+      sbase[3] = ntiles ? static_cast<uint32_t>(atomicAdd(&a.counters[1], static_cast<int>(ntiles)))
+                        : 0u;
+    }
+  }
   // pruned keys score -inf (the top-k reads the whole row)
   if (acc[4]) {
-    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    for (int i = threadIdx.x; i < nvec; i += kThreads)
+    for (int i = tid; i < nvec; i += kThreads)
       if (sflag[(4 * i) >> bshift] == 0) reinterpret_cast<float4*>(srow)[i] = ninf;
-    for (int i = 4 * nvec + static_cast<int>(threadIdx.x); i < a.length; i += kThreads)
+    for (int i = 4 * nvec + tid; i < a.length; i += kThreads)
       if (sflag[i >> bshift] == 0) srow[i] = -INFINITY;
   }
-  if (threadIdx.x == 0) {
-    for (int g = 0; g < a.hist_segs; ++g)
-      if (seg_pruned[g]) atomicAdd(&grow[g * kKeyHistBins + kNegInfBin], seg_pruned[g]);
+  if (tid < a.hist_segs && seg_pruned[tid])
+    atomicAdd(&grow[tid * kKeyHistBins + kNegInfBin], seg_pruned[tid]);
+  if (tid == 0) {  // adds that return nothing: no thread waits on a read
     unsigned long long* st = a.stats + static_cast<int64_t>(seq) * 8;
-    st[0] += 1;                                    // steps
-    st[1] += static_cast<unsigned long long>(nb);  // blocks visited
-    st[2] += acc[0];                               // blocks scored
-    st[3] += static_cast<unsigned long long>(nb) - acc[0];  // blocks pruned
-    st[4] += acc[1];                               // keys scored (read)
-    st[5] += static_cast<unsigned long long>(a.length);     // keys in the cache
-    st[6] += acc[2];                               // first-wave (hot) blocks
-    st[7] += acc[3];                               // second-wave blocks
+    using ull = unsigned long long;
+    atomicAdd(&st[0], 1ull);                                // steps
+    atomicAdd(&st[1], static_cast<ull>(nb));                // blocks visited
+    atomicAdd(&st[2], static_cast<ull>(acc[0]));            // blocks scored
+    atomicAdd(&st[3], static_cast<ull>(nb - acc[0]));       // blocks pruned
+    atomicAdd(&st[4], static_cast<ull>(acc[1]));            // keys scored (read)
+    atomicAdd(&st[5], static_cast<ull>(a.length));          // keys in the cache
+    atomicAdd(&st[6], static_cast<ull>(acc[2]));            // first-wave (hot) blocks
+    atomicAdd(&st[7], static_cast<ull>(acc[3]));            // second-wave blocks
   }
-  emit_tiles(sflag, nb, 2, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters + 1, wtot, sbase);
+  emit_tiles(sflag, nb, 2, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters + 1, wtot, sbase,
+             &sbase[3]);
 }
 
 // Part of a row's key histogram, added to hist[seq] (zero before the launch): CTA
@@ -634,7 +756,14 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
   pa.counters = counters;
   pa.stats = stats;
   pa.init = init;
-  TDSA_CUDA_CHECK(launch_pdl(exact_prepare_kernel, dim3(batch), dim3(kThreads), 0, stream, pa));
+  // dynamic shared memory: one wave-1 flag byte per block
+  const int prep_smem = ((length + block_size - 1) / block_size + 15) & ~15;
+  if (prep_smem > kWave2MaxSmem)
+    return fail(TDSA_ERR_UNSUPPORTED, "exact progressive: too many blocks per sequence");
+  TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_prepare_kernel),
+                                      prep_smem));
+  TDSA_CUDA_CHECK(launch_pdl(exact_prepare_kernel, dim3(batch), dim3(kThreads), prep_smem,
+                             stream, pa));
   TDSA_CUDA_CHECK(cudaGetLastError());
 
   BlockArgs ba;
@@ -683,8 +812,8 @@ int run_exact(int init, uint8_t* state, const ExactLayout& L, const void* q, int
     wa.hist = hist;
     wa.hist_segs = hsegs;
     wa.stats = stats;
-    // the histogram copies, then the row's block flags
-    const int w2_smem = kHistCopyBytes + ((ba.nblocks + 15) & ~15);
+    // the sub-bin counts, then the row's block flags
+    const int w2_smem = kKeyHistBins * 4 + ((ba.nblocks + 15) & ~15);
     if (w2_smem > kWave2MaxSmem)
       return fail(TDSA_ERR_UNSUPPORTED, "exact progressive: too many blocks per sequence");
     TDSA_CUDA_CHECK(ensure_dynamic_smem(reinterpret_cast<const void*>(exact_wave2_kernel),
