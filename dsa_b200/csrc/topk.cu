@@ -19,6 +19,9 @@
 //      == T are taken -- the tie rule of the reference's stable_topk (metrics.py:9-22).
 //      Unsorted output is in ascending index order; sorted output is a bitonic sort of the
 //      k taken (key, index) pairs in shared memory.
+// Unsorted rows whose histogram gave the k-th key's bin take a shorter road (take_from_bin):
+// one compare per key against the bin's lower edge fills the list, two histogram levels
+// over the bin's list entries (11 + 9 key bits) give T, and one ordered pass takes.
 //
 // Rows longer than one segment run in levels: every segment emits its local top-k in index
 // order, and the candidates (the global top-k is a subset of their union) are selected
@@ -164,6 +167,188 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* wa, ui
   }
   __syncthreads();
   return wb[warp] + x - v;
+}
+
+// The bin of the k_rem-th key counted from the top, thread t holding the counts c[0..3] of
+// bins nbins-1-4t .. nbins-4-4t (zeros past nbins): res = {bin, k_rem within the bin, the
+// bin's count, 1}, or res[3] = 0 when the counts total less than k_rem.  Three CTA
+// barriers; all threads return with res readable.
+__device__ __forceinline__ void pick_bin(const uint32_t (&c)[4], int nbins, uint32_t k_rem,
+                                         uint32_t* wa, uint32_t* wb, uint32_t* res) {
+  const int tid = threadIdx.x;
+  const uint32_t tot = c[0] + c[1] + c[2] + c[3];
+  if (tid == 0) res[3] = 0u;
+  uint32_t dummy;
+  uint32_t above = block_excl_scan(tot, wa, wb, &dummy);
+  if (above < k_rem && k_rem <= above + tot) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (above < k_rem && k_rem <= above + c[i]) {
+        res[0] = static_cast<uint32_t>(nbins - 1 - (4 * tid + i));
+        res[1] = k_rem - above;
+        res[2] = c[i];
+        res[3] = 1u;
+      }
+      above += c[i];
+    }
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void bins_from_top(const uint32_t* h, int nbins, uint32_t (&c)[4]) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = 4 * tid + i < nbins ? h[nbins - 1 - (4 * tid + i)] : 0u;
+}
+
+// Unsorted selection once the score kernel's histogram has given the 12-bit key bin
+// [clo, chi] of the k-th key (k_rem of its in_range keys are taken, and k - k_rem keys lie
+// above it): every key >= clo goes to the list in index order -- straight to the output
+// when the whole bin is taken -- the list is narrowed to the exact k-th key by two
+// histogram levels over the bin's keys (key bits 19..9 in 2048 bins, then 8..0 in 512),
+// and one ordered pass takes the keys above the final range and the lowest-index keys
+// inside it that complete k (the tie rule of stable_topk, metrics.py:9-22).  Output in
+// ascending index order, as the general path.  `hists` (2048 words) is zero on entry; the
+// list holds k - k_rem + in_range <= a.cap entries.  A row copy of kPer keys per thread sits
+// in `rowf`.
+template <int kPer>
+__device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int seg, int start,
+                                              int n, int k, const float* rowf,
+                                              const int32_t* irow, uint32_t* list_key,
+                                              uint32_t* list_idx, uint32_t* hists,
+                                              uint32_t* wa, uint32_t* wb, uint32_t* res,
+                                              uint32_t* s_total, uint32_t clo, uint32_t chi,
+                                              uint32_t k_rem, uint32_t in_range) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  constexpr int kLog = kPer == 32 ? 5 : kPer == 16 ? 4 : kPer == 8 ? 3 : 2;
+  const int rot = lane >> (5 - kLog);
+  const int tbase = tid * kPer;
+  const uint32_t uk = static_cast<uint32_t>(k);
+  const bool whole = in_range == k_rem;  // every key >= clo is taken
+  const int64_t out_row = static_cast<int64_t>(row) * gridDim.x + seg;
+  int32_t* oi32 = a.idx_bytes == 4 ? static_cast<int32_t*>(a.out_idx) + out_row * a.out_idx_stride
+                                   : nullptr;
+  int64_t* oi64 = a.idx_bytes == 8 ? static_cast<int64_t*>(a.out_idx) + out_row * a.out_idx_stride
+                                   : nullptr;
+  float* ov = a.out_val ? a.out_val + out_row * a.out_val_stride : nullptr;
+  int32_t* om = a.mirror ? a.mirror + out_row * a.mirror_stride : nullptr;
+  auto put = [&](uint32_t p, uint32_t gi, uint32_t u) {
+    if (p < uk) {
+      if (oi32) oi32[p] = static_cast<int32_t>(gi);
+      if (oi64) oi64[p] = static_cast<int64_t>(gi);
+      if (om) om[p] = static_cast<int32_t>(gi);
+      if (ov) ov[p] = key_to_float(u);
+    }
+  };
+  auto gidx = [&](int e) -> uint32_t {
+    return irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(start + e);
+  };
+
+  // ---- the thread's keys >= clo, bit j = element tbase + j
+  uint32_t take = 0u;
+  if (clo >= 0x00800000u && clo <= 0xFF800000u) {
+    // key(x) >= clo  <=>  !(x < float(clo)) for a bin edge of finite floats or +inf, exact
+    // for +-0 (one key) and NaN (above every key): one compare per key
+    const float f_lo = key_to_float(clo);
+    if (kPer == 32 && tbase + 32 <= n) {
+      // eight conflict-free 16-byte reads per thread, rotated by lane
+      const float4* r4 = reinterpret_cast<const float4*>(rowf) + tid * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int qq = (j + lane) & 7;
+        const float4 v = r4[qq];
+        const uint32_t nib = (!(v.x < f_lo) ? 1u : 0u) | (!(v.y < f_lo) ? 2u : 0u) |
+                             (!(v.z < f_lo) ? 4u : 0u) | (!(v.w < f_lo) ? 8u : 0u);
+        take |= nib << (4 * qq);
+      }
+    } else {
+#pragma unroll 8
+      for (int j = 0; j < kPer; ++j) {
+        const int jj = (j + rot) & (kPer - 1);
+        const int e = tbase + jj;
+        if (e < n && !(rowf[e] < f_lo)) take |= 1u << jj;
+      }
+    }
+  } else {
+#pragma unroll 8
+    for (int j = 0; j < kPer; ++j) {
+      const int jj = (j + rot) & (kPer - 1);
+      const int e = tbase + jj;
+      if (e < n && float_to_key(rowf[e]) >= clo) take |= 1u << jj;
+    }
+  }
+  // list (or output) positions in index order
+  uint32_t pos = block_excl_scan(static_cast<uint32_t>(__popc(take)), wa, wb, s_total);
+  for (uint32_t t = take; t; t &= t - 1u) {
+    const int e = tbase + __ffs(t) - 1;
+    const uint32_t u = float_to_key(rowf[e]);
+    if (whole) {
+      put(pos, gidx(e), u);
+    } else if (pos < static_cast<uint32_t>(a.cap)) {
+      list_key[pos] = u;
+      list_idx[pos] = gidx(e);
+    }
+    ++pos;
+  }
+  if (whole) return;
+  __syncthreads();  // the list, in index order
+  const uint32_t m = min(*s_total, static_cast<uint32_t>(a.cap));
+
+  // ---- the exact k-th key inside the bin: bits 19..9, then 8..0
+  for (uint32_t i = tid; i < m; i += kThreads) {
+    const uint32_t u = list_key[i];
+    if (u <= chi) atomicAdd(&hists[(u >> 9) & 0x7FFu], 1u);  // the bin's keys (>= clo)
+  }
+  __syncthreads();
+  uint32_t c4[4];
+  bins_from_top(hists, 2048, c4);
+  pick_bin(c4, 2048, k_rem, wa, wb, res);
+  uint32_t flo = clo, fhi = chi, fk = k_rem;  // final range, and how many of it are taken
+  if (res[3]) {
+    flo = clo | (res[0] << 9);
+    fhi = flo | 0x1FFu;
+    fk = res[1];
+    if (res[2] != fk) {
+      if (tid < 512) hists[tid] = 0u;  // every thread holds its level-2 counts already
+      __syncthreads();
+      for (uint32_t i = tid; i < m; i += kThreads) {
+        const uint32_t u = list_key[i];
+        if (u >= flo && u <= fhi) atomicAdd(&hists[u & 0x1FFu], 1u);
+      }
+      __syncthreads();
+      bins_from_top(hists, 512, c4);
+      pick_bin(c4, 512, fk, wa, wb, res);
+      if (res[3]) {
+        flo |= res[0];
+        fhi = flo;
+        fk = res[1];
+      }
+    }
+  }
+
+  // ---- the taken keys: above the final range, and the first fk inside it; thread t takes
+  // list entries [t * per, t * per + per)
+  const int per = (static_cast<int>(m) + kThreads - 1) / kThreads;
+  const int i0 = min(static_cast<int>(m), tid * per), i1 = min(static_cast<int>(m), i0 + per);
+  uint32_t gc = 0u, ec = 0u;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t u = list_key[i];
+    gc += u > fhi ? 1u : 0u;
+    ec += (u >= flo && u <= fhi) ? 1u : 0u;
+  }
+  // a list holds <= 8192 entries, so the packed halves do not carry
+  const uint32_t b2 = block_excl_scan(gc | (ec << 16), wa, wb, s_total);
+  uint32_t g = b2 & 0xFFFFu, eb = b2 >> 16;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t u = list_key[i];
+    if (u > fhi) {
+      put(g + min(eb, fk), list_idx[i], u);
+      ++g;
+    } else if (u >= flo) {
+      if (eb < fk) put(g + eb, list_idx[i], u);
+      ++eb;
+    }
+  }
 }
 
 // Merge of an exchange (topk_segment_kernel with a.gather set), before the selection:
@@ -329,6 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   // ---- 1. initial live range [clo, chi] holding the k-th key; k - k_rem keys lie above
   uint32_t k_rem = static_cast<uint32_t>(k), in_range = static_cast<uint32_t>(n);
   uint32_t clo = 0u, chi = 0xFFFFFFFFu;
+  bool hist_hit = false;  // the histogram gave the k-th key's 12-bit bin
   if (a.hist) {
     // The score kernel already counted this row's keys by their top 12 bits: find the bin of
     // the k-th key (thread t owns bins 4095-4t .. 4092-4t).
@@ -362,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       chi = clo | 0xFFFFFu;
       k_rem = res[1];
       in_range = res[2];
+      hist_hit = true;
     }
   }
   if (bulk && tbase < n) mbar_wait(&s_bar[(tbase * 4) >> 15], 0, &s_abort);
@@ -404,6 +591,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   if (stored) {
     clo = __reduce_min_sync(0xffffffffu, wa[lane]);
     chi = __reduce_max_sync(0xffffffffu, wc[lane]);
+  }
+  if (hist_hit && !a.sorted && !a.pad_to_k && !a.kth_out && !a.next_hist && a.out_idx &&
+      static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
+    take_from_bin<kPer>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx, hists, wa, wc,
+                        res, &s_total, clo, chi, k_rem, in_range);
+    return;
   }
 
   // ---- 2. narrow over the segment until the keys >= clo fit the list.  A k larger than
@@ -670,38 +863,6 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
 //      CTA scan of their totals, lanes by a warp scan per chunk.
 // The row's histogram is zeroed for the next score launch after every CTA has read it.
 constexpr int kClusterHistWords = 2 * kKeyHistBins + 256;  // cluster levels 2 and 3
-
-// The bin of the k_rem-th key counted from the top, thread t holding the counts c[0..3] of
-// bins nbins-1-4t .. nbins-4-4t (zeros past nbins): res = {bin, k_rem within the bin, the
-// bin's count, 1}, or res[3] = 0 when the counts total less than k_rem.  Three CTA
-// barriers; all threads return with res readable.
-__device__ __forceinline__ void pick_bin(const uint32_t (&c)[4], int nbins, uint32_t k_rem,
-                                         uint32_t* wa, uint32_t* wb, uint32_t* res) {
-  const int tid = threadIdx.x;
-  const uint32_t tot = c[0] + c[1] + c[2] + c[3];
-  if (tid == 0) res[3] = 0u;
-  uint32_t dummy;
-  uint32_t above = block_excl_scan(tot, wa, wb, &dummy);
-  if (above < k_rem && k_rem <= above + tot) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (above < k_rem && k_rem <= above + c[i]) {
-        res[0] = static_cast<uint32_t>(nbins - 1 - (4 * tid + i));
-        res[1] = k_rem - above;
-        res[2] = c[i];
-        res[3] = 1u;
-      }
-      above += c[i];
-    }
-  }
-  __syncthreads();
-}
-
-__device__ __forceinline__ void bins_from_top(const uint32_t* h, int nbins, uint32_t (&c)[4]) {
-  const int tid = threadIdx.x;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) c[i] = 4 * tid + i < nbins ? h[nbins - 1 - (4 * tid + i)] : 0u;
-}
 
 template <int kPer, int kC>
 __global__ void __cluster_dims__(kC, 1, 1) __launch_bounds__(kThreads, 1)

@@ -471,6 +471,80 @@ def test_cluster_topk_rows_match_oracle(batch, length, k):
     assert int(hist.abs().sum()) == 0  # consumed and zeroed
 
 
+@pytest.mark.parametrize("batch,length,k", [
+    (24, 32768, 1),      # one CTA per row (too many rows for clusters), 32 keys per thread
+    (24, 32768, 8192),   # the list at its capacity
+    (24, 32768, 9000),   # keys >= the k-th key's bin overflow the list: the general path
+    (80, 20000, 2048),   # 32 keys per thread, the last threads partly outside the row
+    (80, 12000, 1000),   # 16 keys per thread
+    (80, 6000, 700),     # 8 keys per thread
+    (80, 7001, 64),      # odd row stride (unaligned rows: loads instead of bulk copies)
+])
+def test_segment_topk_from_histogram_matches_oracle(batch, length, k):
+    """The one-CTA top-k started from the score kernel's histogram (rows too many for the
+    cluster top-k): every key at or above the k-th key's 12-bit bin goes to the list, two
+    histogram levels over the bin find the exact k-th key, one ordered pass takes.  Rounded
+    normals (heavy ties), +-0, +-inf, denormals, rows of one value and of -inf only, a row
+    whose k-th bin holds most keys, against stable_topk in index order."""
+    from dsa_b200 import _capi as capi
+
+    rng = np.random.default_rng(batch * 5 + length + k)
+    s = np.round(rng.normal(size=(batch, length)) * 64).astype(np.float32) / 64
+    s[0, rng.integers(0, length, length // 50)] = -0.0
+    s[0, rng.integers(0, length, length // 50)] = 0.0
+    s[1] = 0.25  # one value: the tie rule alone decides
+    s[2, rng.integers(0, length, 50)] = np.inf
+    s[2, rng.integers(0, length, length // 3)] = -np.inf
+    s[3] = -np.inf  # the k-th key is -inf: every key of the row ties
+    s[4, rng.integers(0, length, 400)] = np.float32(1e-45)
+    s[4, rng.integers(0, length, 400)] = np.float32(-1e-45)
+    s[5] = np.float32(1.0) + rng.integers(0, 4096, length).astype(np.float32) * np.float32(2 ** -23)
+    s[6, : length // 2] = np.float32(3.0)  # ties straddling the k-th key in one sub-bin
+    s[7] = rng.normal(size=length).astype(np.float32)  # distinct values
+    dev = cuda(s)
+    hist = cuda(_key_hist(s))
+    idx = torch.empty(batch, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(batch, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist", dev.data_ptr(), dev.stride(0), batch, length, k, 0,
+              idx.data_ptr(), 4, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(hist.abs().sum()) == 0  # consumed and zeroed
+
+
+@pytest.mark.parametrize("length,k", [(40000, 2048), (70000, 512), (32769, 2048)])
+def test_segment_topk_merge_level_from_histogram(length, k):
+    """Rows longer than one segment on a batch too large for clusters: each segment's top-k
+    and then the merge level (explicit indices, started from the bins the first level
+    passes on) against stable_topk."""
+    from dsa_b200 import _capi as capi
+
+    batch = 24
+    rng = np.random.default_rng(length + k)
+    s = np.round(rng.normal(size=(batch, length)) * 32).astype(np.float32) / 32
+    s[0, rng.integers(0, length, 60)] = np.inf
+    s[1] = -np.inf
+    s[1, rng.integers(0, length, 100)] = 2.0
+    s[2, -1000:] = 5.0  # ties at the top of the last segment
+    dev = cuda(s)
+    hist = cuda(_key_hist_segments(s))
+    lib = capi.lib()
+    assert lib.tdsa_topk_levels(batch, length, k, 1) == 2
+    nbytes = lib.tdsa_topk_workspace_bytes(batch, length, k)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device="cuda")
+    idx = torch.empty(batch, k, dtype=torch.int64, device="cuda")
+    val = torch.empty(batch, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist_ws", dev.data_ptr(), dev.stride(0), batch, length, k, 0,
+              idx.data_ptr(), 8, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(hist.abs().sum()) == 0
+
+
 def test_cluster_topk_falls_back_when_histogram_is_short():
     """A histogram whose counts total less than k does not describe the row: the cluster
     kernel narrows from the full key range itself and still returns stable_topk."""
