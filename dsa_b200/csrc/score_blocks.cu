@@ -2,8 +2,9 @@
 //
 // A 128-key MMA tile is assembled from 128/bs key blocks (bs = 16, 32, 64, 128) of one
 // sequence; each block is its own TMA box, and a block whose keys are not needed is never
-// loaded.  The pipeline is the dense kernel's (TMA producer warp, tcgen05 issuer warp, four
-// epilogue warps owning one key each, TMEM double buffer); the epilogue differs by mode:
+// loaded.  The pipeline is the dense kernel's (TMA producer warp, tcgen05 issuer warp, two
+// epilogue groups of four warps taking alternate tiles, each thread owning one key, four
+// TMEM accumulators); the epilogue differs by mode:
 //
 //   kModeH8           8-head probe score on cold blocks, -inf elsewhere, per-block max
 //                     (reference _h8_block_max_kernel, progressive_kernel.py:218-246)
@@ -27,17 +28,18 @@ namespace tdsa {
 namespace {
 
 constexpr int kTileKeys = 128;
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kStageBytes = kTileKeys * kHeadDim * 2;
 constexpr int kHalfBytes = kStageBytes / 2;
 constexpr int kQBytes = kHeads * kHeadDim * 2;
 constexpr int kQHalf = kQBytes / 2;
-constexpr int kAccBufs = 2;
-constexpr int kTmemCols = 128;
-constexpr int kThreads = 192;
+constexpr int kEpiGroups = 2;  // epilogue groups of four warps, alternate tiles
+constexpr int kAccBufs = 4;    // TMEM accumulators: two per epilogue group
+constexpr int kTmemCols = kAccBufs * kHeads;
+constexpr int kThreads = 64 + 128 * kEpiGroups;
 constexpr int kBarrierBytes = 1024;
 constexpr int kSmemBytes = kStages * kStageBytes + 2 * kQBytes + kBarrierBytes + 1024;
-constexpr int kHistSmemBytes = kKeyHistBins * 4;  // exact mode with a key histogram
+constexpr int kHistSmemBytes = kKeyHistBins * 4 * kEpiGroups;  // exact mode: one per group
 constexpr int kMaxSlots = 8;  // blocks per tile at bs = 16
 static_assert(kTopkSegment == 1 << 15, "a key's histogram segment is its index >> 15");
 
@@ -135,15 +137,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accempty = accfull + kAccBufs;
   uint64_t* grp = accempty + kAccBufs;  // epilogue group-max exchange, one per TMEM buffer
   uint64_t* done = grp + kAccBufs;
-  uint64_t* hbar = done + 1;  // epilogue-warp handshake around histogram flushes
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hbar + 1);
+  uint64_t* hbar = done + 1;  // [kEpiGroups] epilogue-group handshakes around histogram flushes
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hbar + kEpiGroups);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* gmax = reinterpret_cast<float*>(tmem_holder + 4);  // [kAccBufs][8]
-  // exact mode with a histogram: 4096 bins behind the barrier region
+  // exact mode with a histogram: 4096 bins per epilogue group behind the barrier region
   uint32_t* shist = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
   const bool use_hist = kMode == kModeExact && a.hist != nullptr;
   if (use_hist)
-    for (int i = threadIdx.x; i < kKeyHistBins; i += kThreads) shist[i] = 0u;
+    for (int i = threadIdx.x; i < kKeyHistBins * kEpiGroups; i += kThreads) shist[i] = 0u;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&grp[s], 4);
     }
     mbar_init(done, 1);
-    mbar_init(hbar, 4);
+    for (int g = 0; g < kEpiGroups; ++g) mbar_init(&hbar[g], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++qcount;
           prev_seq = seq;
         }
-        const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
+        const uint32_t acc = acc_it % kAccBufs, aph = (acc_it / kAccBufs) & 1u;
         if (!mbar_wait(&accempty[acc], aph ^ 1u, abort_flag)) break;
         const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
         if (!mbar_wait(&full[s], ph, abort_flag)) break;
@@ -287,7 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- epilogue
+    // group g (warps 2 + 4g .. 5 + 4g, one per TMEM lane quadrant) takes the CTA's local
+    // tiles i = g, g + 2, ... from accumulator i % 4
     const uint32_t quad = static_cast<uint32_t>(warp & 3);
+    const int group = (warp - 2) >> 2;
     const int row = static_cast<int>(quad) * 32 + lane;  // row of the 128-key tile
     const int slot_j = row / bs;
     const int ingroup = row % bs;
@@ -298,16 +303,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const float thr = (kMode == kModeProgressive) ? *a.threshold : 0.f;
     int prev_seq = -1, prev_slot = -1;  // prev_slot: the (sequence, segment) histogram the
-                                        // shared counts belong to
-    uint32_t acc_it = 0, hph = 0;
+                                        // group's shared counts belong to
+    uint32_t hph = 0;
+    uint32_t* ghist = shist + group * kKeyHistBins;
+    uint64_t* gbar = hbar + group;
     float wr[kHeads];
     Tile tile;
-    const int etid = (warp - 2) * 32 + lane;  // 0..127 over the epilogue warps
-    // all four epilogue warps meet (bounded wait); false when the CTA aborts
+    const int etid = (warp - 2 - 4 * group) * 32 + lane;  // 0..127 within the group
+    // the group's four warps meet (bounded wait); false when the CTA aborts
     auto hist_sync = [&]() -> bool {
       __syncwarp();
-      if (lane == 0) mbar_arrive(hbar);
-      const bool ok = mbar_wait(hbar, hph & 1u, abort_flag);
+      if (lane == 0) mbar_arrive(gbar);
+      const bool ok = mbar_wait(gbar, hph & 1u, abort_flag);
       ++hph;
       return ok;
     };
@@ -317,15 +324,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!hist_sync()) return false;
       uint32_t* dst = a.hist + static_cast<int64_t>(slot) * kKeyHistBins;
       for (int i = etid; i < kKeyHistBins; i += 128) {
-        const uint32_t c = shist[i];
+        const uint32_t c = ghist[i];
         if (c) {
           atomicAdd(dst + i, c);
-          shist[i] = 0u;
+          ghist[i] = 0u;
         }
       }
       return hist_sync();
     };
-    for (int64_t t = t0; t < t1; ++t) {
+    bool ok = true;
+    for (int64_t t = t0 + group; t < t1; t += kEpiGroups) {
+      const uint32_t acc_it = static_cast<uint32_t>(t - t0);
       get_tile(a, t, tile);
       const int seq = tile.seq;
       if (seq != prev_seq) {
@@ -335,7 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (use_hist) {  // the slot of the tile's first block (a tile may end in the next one)
         const int tslot = seq * a.hist_segs + ((max(tile.block[0], 0) * bs) >> 15);
         if (tslot != prev_slot) {
-          if (prev_slot >= 0 && !hist_flush(prev_slot)) break;
+          if (prev_slot >= 0 && !hist_flush(prev_slot)) {
+            ok = false;
+            break;
+          }
           prev_slot = tslot;
         }
       }
@@ -344,8 +356,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = blk >= 0 && key < a.length;
       const bool flag = (kMode != kModeExact && blk >= 0) ? mask_set<kMode>(a, seq, blk) : false;
 
-      const uint32_t acc = acc_it & 1u, aph = (acc_it >> 1) & 1u;
-      if (!mbar_wait(&accfull[acc], aph, abort_flag)) break;
+      const uint32_t acc = acc_it % kAccBufs, aph = (acc_it / kAccBufs) & 1u;
+      if (!mbar_wait(&accfull[acc], aph, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t r0[32], r1[32];
       const uint32_t taddr = tmem_base + ((quad * 32u) << 16) + acc * kHeads;
@@ -394,7 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((lane & 15) == 0) gmax[acc * 8 + quad * 2 + (lane >> 4)] = m;
         __syncwarp();
         if (lane == 0) mbar_arrive(&grp[acc]);
-        if (!mbar_wait(&grp[acc], aph, abort_flag)) break;
+        if (!mbar_wait(&grp[acc], aph, abort_flag)) {
+          ok = false;
+          break;
+        }
         const int g0 = (slot_j * bs) >> 4, ng = bs >> 4;
         for (int g = 0; g < ng; ++g) bmax = fmaxf(bmax, gmax[acc * 8 + g0 + g]);
       }
@@ -408,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (use_hist) {
         const uint32_t bin = float_to_key(out) >> 20;
         const int kslot = seq * a.hist_segs + (key >> 15);
-        add_to_bin(shist, valid && kslot == prev_slot, bin);
+        add_to_bin(ghist, valid && kslot == prev_slot, bin);
         if (valid && kslot != prev_slot)
           atomicAdd(a.hist + static_cast<int64_t>(kslot) * kKeyHistBins + bin, 1u);
       }
@@ -422,9 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           a.accepted[static_cast<int64_t>(seq) * a.bm_stride + blk] = accept ? 1 : 0;
         }
       }
-      ++acc_it;
-      if (use_hist && t + 1 == t1) hist_flush(prev_slot);
     }
+    if (use_hist && ok && prev_slot >= 0) hist_flush(prev_slot);
   }
 
   __syncthreads();
