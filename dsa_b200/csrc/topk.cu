@@ -208,7 +208,9 @@ __device__ __forceinline__ void bins_from_top(const uint32_t* h, int nbins, uint
 // histogram levels over the bin's keys (key bits 19..9 in 2048 bins, then 8..0 in 512),
 // and one ordered pass takes the keys above the final range and the lowest-index keys
 // inside it that complete k (the tie rule of stable_topk, metrics.py:9-22).  Output in
-// ascending index order, as the general path.  `hists` (2048 words) is zero on entry; the
+// ascending index order, as the general path; a level feeding a merge level pads a segment
+// shorter than k and adds its output's key bins to the next level's histogram, as the
+// general path does.  `hists` (2048 words) is zero on entry; the
 // list holds k - k_rem + in_range <= a.cap entries.  A row copy of kPer keys per thread sits
 // in `rowf`.
 template <int kPer>
@@ -232,14 +234,27 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
                                    : nullptr;
   float* ov = a.out_val ? a.out_val + out_row * a.out_val_stride : nullptr;
   int32_t* om = a.mirror ? a.mirror + out_row * a.mirror_stride : nullptr;
-  auto put = [&](uint32_t p, uint32_t gi, uint32_t u) {
+  // a level feeding a one-segment next level adds the bins of what it passes on
+  uint32_t* nh = a.next_hist ? a.next_hist + static_cast<int64_t>(row) * kKeyHistBins : nullptr;
+  // one output entry; `count` adds its key bin to the next level's histogram alone (the
+  // ordered take below adds them per warp instead)
+  auto put = [&](uint32_t p, uint32_t gi, uint32_t u, bool count) {
     if (p < uk) {
       if (oi32) oi32[p] = static_cast<int32_t>(gi);
       if (oi64) oi64[p] = static_cast<int64_t>(gi);
       if (om) om[p] = static_cast<int32_t>(gi);
       if (ov) ov[p] = key_to_float(u);
+      if (nh && count) atomicAdd(&nh[u >> 20], 1u);
     }
   };
+  if (a.pad_to_k && n < a.k) {
+    // pads rank below every real candidate of the next level (-inf, then the largest index)
+    for (int j = n + tid; j < a.k; j += kThreads) {
+      if (oi32) oi32[j] = 0x7FFFFFFF;
+      if (ov) ov[j] = -INFINITY;
+    }
+    if (tid == 0 && nh) atomicAdd(&nh[float_to_key(-INFINITY) >> 20], static_cast<uint32_t>(a.k - n));
+  }
   auto gidx = [&](int e) -> uint32_t {
     return irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(start + e);
   };
@@ -283,7 +298,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     const int e = tbase + __ffs(t) - 1;
     const uint32_t u = float_to_key(rowf[e]);
     if (whole) {
-      put(pos, gidx(e), u);
+      put(pos, gidx(e), u, true);
     } else if (pos < static_cast<uint32_t>(a.cap)) {
       list_key[pos] = u;
       list_idx[pos] = gidx(e);
@@ -339,15 +354,19 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
   // a list holds <= 8192 entries, so the packed halves do not carry
   const uint32_t b2 = block_excl_scan(gc | (ec << 16), wa, wb, s_total);
   uint32_t g = b2 & 0xFFFFu, eb = b2 >> 16;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t u = list_key[i];
-    if (u > fhi) {
-      put(g + min(eb, fk), list_idx[i], u);
+  for (int j = 0; j < per; ++j) {  // uniform trip count: the bins are added per warp
+    const int i = i0 + j;
+    const uint32_t u = i < i1 ? list_key[i] : 0u;
+    uint32_t p = 0xFFFFFFFFu;
+    if (i < i1 && u > fhi) {
+      p = g + min(eb, fk);
       ++g;
-    } else if (u >= flo) {
-      if (eb < fk) put(g + eb, list_idx[i], u);
+    } else if (i < i1 && u >= flo) {
+      if (eb < fk) p = g + eb;
       ++eb;
     }
+    if (p != 0xFFFFFFFFu) put(p, list_idx[i], u, false);
+    if (nh) add_to_bin(nh, p < uk, u >> 20);
   }
 }
 
@@ -592,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     clo = __reduce_min_sync(0xffffffffu, wa[lane]);
     chi = __reduce_max_sync(0xffffffffu, wc[lane]);
   }
-  if (hist_hit && !a.sorted && !a.pad_to_k && !a.kth_out && !a.next_hist && a.out_idx &&
+  if (hist_hit && !a.sorted && !a.kth_out && a.out_idx &&
       static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
     take_from_bin<kPer>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx, hists, wa, wc,
                         res, &s_total, clo, chi, k_rem, in_range);

@@ -241,7 +241,10 @@ class ScoreTopkPlan:
         if not 0 < k <= self.length:
             raise ValueError(f"k={k} is invalid for {self.length} keys")
         dev = kk.device
-        self.scores = torch.empty(self.batch, self.length, device=dev, dtype=torch.float32)
+        # score rows padded to 16 bytes, so the top-k copies every row with bulk copies
+        padded = (self.length + 3) // 4 * 4
+        self.scores = torch.empty(self.batch, padded, device=dev,
+                                  dtype=torch.float32)[:, :self.length]
         self.indices = torch.empty(self.batch, k, device=dev, dtype=index_dtype)
         self.values = torch.empty(self.batch, k, device=dev, dtype=torch.float32)
         lib = capi.lib()
