@@ -21,6 +21,7 @@ TDSA_ERR_TIMEOUT = 4
 TDSA_ERR_ALIGN = 5
 TDSA_ERR_WORKSPACE = 6
 TDSA_STATUS_RANGE = 8  # device status bit: a device-side index was out of range
+TDSA_STATUS_HIST = 16  # device status bit: a key histogram did not describe its row
 
 TDSA_F32 = 0
 TDSA_F16 = 1

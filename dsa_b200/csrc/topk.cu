@@ -292,10 +292,22 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
       if (e < n && float_to_key(rowf[e]) >= clo) take |= 1u << jj;
     }
   }
-  // list (or output) positions in index order
-  uint32_t pos = block_excl_scan(static_cast<uint32_t>(__popc(take)), wa, wb, s_total);
-  for (uint32_t t = take; t; t &= t - 1u) {
-    const int e = tbase + __ffs(t) - 1;
+  // a wide row's tail keys [kPer * 1024 + 4 tid, + 4) (rows past one segment, kPer = 32)
+  const int tail0 = kPer * kThreads + 4 * tid;
+  uint32_t take_tail = 0u;
+  if (kPer == 32 && n > kPer * kThreads) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if (tail0 + c < n && float_to_key(rowf[tail0 + c]) >= clo) take_tail |= 1u << c;
+  }
+  // list (or output) positions in index order: the main keys, then the tail keys (a segment
+  // holds < 65536 keys, so the packed halves do not carry)
+  const uint32_t before = block_excl_scan(static_cast<uint32_t>(__popc(take)) |
+                                              (static_cast<uint32_t>(__popc(take_tail)) << 16),
+                                          wa, wb, s_total);
+  const uint32_t main_total = *s_total & 0xFFFFu;
+  const uint32_t m_all = main_total + (*s_total >> 16);
+  auto place = [&](uint32_t pos, int e) {
     const uint32_t u = float_to_key(rowf[e]);
     if (whole) {
       put(pos, gidx(e), u, true);
@@ -303,11 +315,14 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
       list_key[pos] = u;
       list_idx[pos] = gidx(e);
     }
-    ++pos;
-  }
+  };
+  uint32_t pos = before & 0xFFFFu;
+  for (uint32_t t = take; t; t &= t - 1u) place(pos++, tbase + __ffs(t) - 1);
+  pos = main_total + (before >> 16);
+  for (uint32_t t = take_tail; t; t &= t - 1u) place(pos++, tail0 + __ffs(t) - 1);
   if (whole) return;
   __syncthreads();  // the list, in index order
-  const uint32_t m = min(*s_total, static_cast<uint32_t>(a.cap));
+  const uint32_t m = min(m_all, static_cast<uint32_t>(a.cap));
 
   // ---- the exact k-th key inside the bin: bits 19..9, then 8..0
   for (uint32_t i = tid; i < m; i += kThreads) {
@@ -368,6 +383,160 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     if (p != 0xFFFFFFFFu) put(p, list_idx[i], u, false);
     if (nh) add_to_bin(nh, p < uk, u >> 20);
   }
+}
+
+// key(x) >= c for an order-preserving key threshold c, as float compares where that is exact:
+// c in [key(-FLT_MAX's bin edge), key(+inf)] compares against float(c) (+-0 one key, NaN
+// above all keys), c at or below the key of -inf holds for every x, c above +inf's key only
+// for NaN.
+struct KeyGE {
+  float f;
+  int mode;  // 0: !(x < f), 1: always, 2: NaN only
+};
+__device__ __forceinline__ KeyGE key_ge_of(uint64_t c) {
+  if (c <= 0x007FFFFFull) return {0.f, 1};
+  if (c > 0xFF800000ull) return {0.f, 2};
+  return {key_to_float(static_cast<uint32_t>(c)), 0};
+}
+__device__ __forceinline__ bool key_ge(float x, const KeyGE& g) {
+  return g.mode == 0 ? !(x < g.f) : (g.mode == 1 ? true : x != x);
+}
+
+constexpr int kWideTail = 4 * kThreads;  // keys past one segment a single CTA also takes
+
+// Unsorted selection for a row of up to 32768 + 4096 keys in one CTA (a row just past one
+// histogram segment, started from the summed histograms of its two segments): thread t owns
+// its 32 keys [32t, 32t + 32) and the four tail keys [32768 + 4t, 32768 + 4t + 4), so thread
+// order is index order within each part.  There is no candidate list: both narrowing levels
+// (key bits 19..9 in 2048 bins, then 8..0 in 512, counted over the row copy itself) and the
+// ordered take run over the row, so the k-th key's bin may hold any number of keys.  The
+// take writes the keys above the final range and the lowest-index keys inside it that
+// complete k, in ascending index order, like the general path.  `hists` (2048 words) is zero
+// on entry.
+__device__ void take_wide(const TopkArgs& a, int row, int n, int k, const float* rowf,
+                          const int32_t* irow, uint32_t* hists, uint32_t* wa, uint32_t* wb,
+                          uint32_t* res, uint32_t* s_total, uint32_t clo, uint32_t chi,
+                          uint32_t k_rem) {
+  constexpr int kMain = 32 * kThreads;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int tbase = tid * 32, tail0 = kMain + 4 * tid;
+  const uint32_t uk = static_cast<uint32_t>(k);
+  // the thread's keys as floats: register slot (j, c) holds element tbase + 4 qq + c with
+  // qq = (j + lane) & 7 (rotated, conflict-free 16-byte reads); bit b of a main mask is
+  // element tbase + b, so masks are in index order whatever the slot order
+  float xm[32], xt[4];
+  uint32_t vm = 0u;  // slots inside the row, bit 4 j + c
+  {
+    const float4* r4 = reinterpret_cast<const float4*>(rowf) + tid * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int qq = (j + lane) & 7;
+      const float4 v = r4[qq];
+      xm[4 * j] = v.x;
+      xm[4 * j + 1] = v.y;
+      xm[4 * j + 2] = v.z;
+      xm[4 * j + 3] = v.w;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) vm |= (tbase + 4 * qq + c < n ? 1u : 0u) << (4 * j + c);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) xt[c] = tail0 + c < n ? rowf[tail0 + c] : -INFINITY;
+  }
+  const uint32_t vtail = tail0 + 4 <= n ? 0xFu : (tail0 >= n ? 0u : (1u << (n - tail0)) - 1u);
+
+  // ---- the exact k-th key inside [clo, chi]: bits 19..9, then 8..0
+  uint32_t flo = clo, fhi = chi, fk = k_rem;
+  for (int level = 0; level < 2; ++level) {
+    const int sh = level == 0 ? 9 : 0;
+    const uint32_t mask = level == 0 ? 0x7FFu : 0x1FFu;
+    const int nb = level == 0 ? 2048 : 512;
+    if (level == 1) {
+      if (tid < 512) hists[tid] = 0u;  // every thread holds its level-1 counts already
+      __syncthreads();
+    }
+    const KeyGE lo = key_ge_of(flo), hi = key_ge_of(static_cast<uint64_t>(fhi) + 1u);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (((vm >> j) & 1u) && key_ge(xm[j], lo) && !key_ge(xm[j], hi))
+        atomicAdd(&hists[(float_to_key(xm[j]) >> sh) & mask], 1u);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if (((vtail >> c) & 1u) && key_ge(xt[c], lo) && !key_ge(xt[c], hi))
+        atomicAdd(&hists[(float_to_key(xt[c]) >> sh) & mask], 1u);
+    __syncthreads();
+    uint32_t c4[4];
+    bins_from_top(hists, nb, c4);
+    pick_bin(c4, nb, fk, wa, wb, res);
+    if (!res[3]) break;  // counts short of fk: the histogram did not describe the row
+    flo |= res[0] << sh;
+    fhi = level == 0 ? (flo | 0x1FFu) : flo;
+    const bool done = res[2] == res[1];  // every key of the range is taken
+    fk = res[1];
+    if (done) break;
+  }
+
+  // ---- the take: keys above [flo, fhi], and the first fk inside it, in index order
+  const KeyGE lo = key_ge_of(flo), hi = key_ge_of(static_cast<uint64_t>(fhi) + 1u);
+  uint32_t gm = 0u, em = 0u, gtl = 0u, etl = 0u;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const bool v = (vm >> j) & 1u;
+    const bool gt = v && key_ge(xm[j], hi), ge = v && key_ge(xm[j], lo);
+    const int b = 4 * (((j >> 2) + lane) & 7) + (j & 3);  // the slot's element, as a bit
+    gm |= (gt ? 1u : 0u) << b;
+    em |= (ge && !gt ? 1u : 0u) << b;
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const bool v = (vtail >> c) & 1u;
+    const bool gt = v && key_ge(xt[c], hi), ge = v && key_ge(xt[c], lo);
+    gtl |= (gt ? 1u : 0u) << c;
+    etl |= (ge && !gt ? 1u : 0u) << c;
+  }
+  // the main part's counts, then the tail's after all of it; a row holds < 65536 keys, so
+  // the packed halves do not carry
+  const uint32_t bm = block_excl_scan(static_cast<uint32_t>(__popc(gm)) |
+                                          (static_cast<uint32_t>(__popc(em)) << 16),
+                                      wa, wb, s_total);
+  const uint32_t main_total = *s_total;
+  const uint32_t bt = block_excl_scan(static_cast<uint32_t>(__popc(gtl)) |
+                                          (static_cast<uint32_t>(__popc(etl)) << 16),
+                                      wa, wb, s_total);
+  int32_t* oi32 = a.idx_bytes == 4
+                      ? static_cast<int32_t*>(a.out_idx) + static_cast<int64_t>(row) * a.out_idx_stride
+                      : nullptr;
+  int64_t* oi64 = a.idx_bytes == 8
+                      ? static_cast<int64_t*>(a.out_idx) + static_cast<int64_t>(row) * a.out_idx_stride
+                      : nullptr;
+  float* ov = a.out_val ? a.out_val + static_cast<int64_t>(row) * a.out_val_stride : nullptr;
+  int32_t* om = a.mirror ? a.mirror + static_cast<int64_t>(row) * a.mirror_stride : nullptr;
+  auto emit = [&](uint32_t& g, uint32_t& eb, bool gt, int e, float x) {
+    uint32_t p = 0xFFFFFFFFu;
+    if (gt) {
+      p = g + min(eb, fk);
+      ++g;
+    } else {
+      if (eb < fk) p = g + eb;
+      ++eb;
+    }
+    if (p < uk) {
+      const uint32_t gi = irow ? static_cast<uint32_t>(irow[e]) : static_cast<uint32_t>(e);
+      if (oi32) oi32[p] = static_cast<int32_t>(gi);
+      if (oi64) oi64[p] = static_cast<int64_t>(gi);
+      if (om) om[p] = static_cast<int32_t>(gi);
+      if (ov) ov[p] = key_to_float(float_to_key(x));
+    }
+  };
+  uint32_t g = bm & 0xFFFFu, eb = bm >> 16;
+  for (uint32_t t = gm | em; t; t &= t - 1u) {  // index order
+    const int b = __ffs(t) - 1;
+    emit(g, eb, (gm >> b) & 1u, tbase + b, rowf[tbase + b]);
+  }
+  g = (main_total & 0xFFFFu) + (bt & 0xFFFFu);
+  eb = (main_total >> 16) + (bt >> 16);
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    if (((gtl | etl) >> c) & 1u) emit(g, eb, (gtl >> c) & 1u, tail0 + c, xt[c]);
 }
 
 // Merge of an exchange (topk_segment_kernel with a.gather set), before the selection:
@@ -466,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   __shared__ uint32_t res[4];
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t s_kth, s_total;
-  __shared__ __align__(8) uint64_t s_bar[4];
+  __shared__ __align__(8) uint64_t s_bar[5];  // a wide row (chunk > kPer * 1024) needs five
   __shared__ int s_abort;
 
   const int row = blockIdx.y, seg = blockIdx.x;
@@ -492,10 +661,13 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   const int k = min(a.k, n);
 
   // ---- 0. the segment into shared memory: bulk copies on the TMA engine (32 KB per
-  // mbarrier) when the row is 16-byte aligned, issued before the histogram prologue so
-  // the two overlap; else coalesced loads.  Warp w's elements lie in one 32 KB piece.
-  const bool bulk = ((reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u) && (n % 4 == 0);
-  const uint32_t bytes = static_cast<uint32_t>(n) * 4u;
+  // mbarrier) of its first n & ~3 keys when the row is 16-byte aligned, issued before the
+  // histogram prologue so the two overlap, each thread then loading its own keys past them
+  // (fewer than four in a row); else coalesced loads.  A thread's elements lie in one 32 KB
+  // piece.
+  const int nbulk = (reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u ? (n & ~3) : 0;
+  const bool bulk = nbulk > 0;
+  const uint32_t bytes = static_cast<uint32_t>(nbulk) * 4u;
   const int npieces = static_cast<int>((bytes + 32767u) / 32768u);
   if (tid == 0) {
     s_abort = 0;
@@ -527,6 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       const int e = w0 + j * 32 + lane;
       if (e < n) rowf[e] = __ldg(vrow + e);
     }
+    for (int e = kPer * kThreads + tid; e < n; e += kThreads) rowf[e] = __ldg(vrow + e);
     __syncwarp();
   }
 
@@ -537,11 +710,14 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   if (a.hist) {
     // The score kernel already counted this row's keys by their top 12 bits: find the bin of
     // the k-th key (thread t owns bins 4095-4t .. 4092-4t).
-    uint32_t* rh = a.hist + (static_cast<int64_t>(row) * gridDim.x + seg) * kKeyHistBins;
+    // (a wide row covers two histogram segments: their sum)
+    const int hsegs = (a.chunk + kTopkSegment - 1) / kTopkSegment;
+    uint32_t* rh = a.hist + (static_cast<int64_t>(row) * gridDim.x + seg) * hsegs * kKeyHistBins;
     uint32_t c[4], tot = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      c[i] = rh[kKeyHistBins - 1 - (4 * tid + i)];
+      c[i] = 0u;
+      for (int g = 0; g < hsegs; ++g) c[i] += rh[g * kKeyHistBins + kKeyHistBins - 1 - (4 * tid + i)];
       tot += c[i];
     }
     if (tid == 0) res[3] = 0u;
@@ -560,7 +736,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) rh[kKeyHistBins - 1 - (4 * tid + i)] = 0u;  // ready for reuse
+    for (int i = 0; i < 4; ++i)  // ready for reuse
+      for (int g = 0; g < hsegs; ++g) rh[g * kKeyHistBins + kKeyHistBins - 1 - (4 * tid + i)] = 0u;
     __syncthreads();
     if (res[3]) {  // (a histogram that does not describe the row leaves the full range)
       clo = res[0] << 20;
@@ -570,7 +747,14 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       hist_hit = true;
     }
   }
-  if (bulk && tbase < n) mbar_wait(&s_bar[(tbase * 4) >> 15], 0, &s_abort);
+  const int tail0 = kPer * kThreads + 4 * tid;  // a wide row's four tail keys of this thread
+  if (bulk) {
+    if (tbase < nbulk) mbar_wait(&s_bar[(tbase * 4) >> 15], 0, &s_abort);
+    if (n > kPer * kThreads && tail0 < nbulk) mbar_wait(&s_bar[(tail0 * 4) >> 15], 0, &s_abort);
+    for (int e = max(tbase, nbulk); e < min(tbase + kPer, n); ++e) rowf[e] = __ldg(vrow + e);
+    if (n > kPer * kThreads)
+      for (int e = max(tail0, nbulk); e < min(tail0 + 4, n); ++e) rowf[e] = __ldg(vrow + e);
+  }
 
   // Keys are computed from the floats on the fly, or (no histogram: the min/max pass
   // visits every element anyway) converted once in place.
@@ -610,6 +794,19 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   if (stored) {
     clo = __reduce_min_sync(0xffffffffu, wa[lane]);
     chi = __reduce_max_sync(0xffffffffu, wc[lane]);
+  }
+  if constexpr (kPer == 32) {
+    if (n > kPer * kThreads) {  // a wide row: the host routes only unsorted final levels here
+      if (hist_hit && static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
+        take_from_bin<kPer>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx, hists, wa,
+                            wc, res, &s_total, clo, chi, k_rem, in_range);
+      } else if (hist_hit) {  // the k-th key's bin holds more keys than the list: no list
+        take_wide(a, row, n, k, rowf, irow, hists, wa, wc, res, &s_total, clo, chi, k_rem);
+      } else if (tid == 0) {
+        atomicOr(a.status, TDSA_STATUS_HIST);  // the histograms did not describe the row
+      }
+      return;
+    }
   }
   if (hist_hit && !a.sorted && !a.kth_out && a.out_idx &&
       static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
@@ -1186,9 +1383,17 @@ struct Plan {
 // First level: at least ceil(length / 32768) segments; more (up to one per 8k keys, so the
 // merge level stays <= length / 8) when rows are too few to fill the GPU.
 // With per-segment key histograms (`hist`) the first level uses the histograms' fixed
-// 32768-key segments.
-Plan make_plan(int batch, int length, int k, bool hist = false) {
+// 32768-key segments; an unsorted final selection (`wide`) of a row just past one segment
+// (up to 32768 + 4096 keys) is one level of one CTA per row started from both histograms.
+Plan make_plan(int batch, int length, int k, bool hist = false, bool wide = false) {
   Plan p;
+  if (hist && wide && length > kTopkSegment && length <= kTopkSegment + kWideTail) {
+    p.levels = 1;
+    p.nseg[0] = 1;
+    p.chunk[0] = length;
+    p.count[0] = length;
+    return p;
+  }
   int count = length;
   const int nmin = (length + kTopkSegment - 1) / kTopkSegment;
   const int nmax = std::max(nmin, length / std::max(8 * k, 4096));
@@ -1223,8 +1428,9 @@ size_t topk_workspace_bytes(int batch, int length, int k) {
   return 2 * cand * 8 + 256 + static_cast<size_t>(batch) * kKeyHistBins * 4;
 }
 
-int topk_levels(int batch, int length, int k, int hist) {
-  return make_plan(batch, length, k, hist != 0).levels;
+int topk_levels(int batch, int length, int k, int flags) {
+  const bool hist = (flags & 1) != 0, sorted = (flags & 2) != 0;
+  return make_plan(batch, length, k, hist, hist && !sorted).levels;
 }
 
 int topk_check(int length, int k, int sorted) {
@@ -1241,7 +1447,9 @@ int launch_topk(const float* scores, int64_t s_stride, const int32_t* idx, int64
                 int64_t mirror_stride) {
   int rc = topk_check(length, k, sorted);
   if (rc) return rc;
-  const Plan p = make_plan(batch, length, k, key_hist != nullptr);
+  // an unsorted final selection of rows just past one segment: one level (take_wide)
+  const bool wide = key_hist && !idx && !sorted && !kth_out && out_idx;
+  const Plan p = make_plan(batch, length, k, key_hist != nullptr, wide);
   if (p.levels > 1 && ws_bytes < topk_workspace_bytes(batch, length, k))
     return fail(TDSA_ERR_WORKSPACE, "top-k workspace too small");
   if (key_hist && !idx && !sorted && !kth_out) {

@@ -279,8 +279,8 @@ class ScoreTopkPlan:
                                self.workspace.data_ptr(), nbytes)
         self.device = dev
         # kernels per run(): score + top-k (one level, or more when the row splits)
-        self.launches_per_run = 1 + capi.lib().tdsa_topk_levels(self.batch, self.length, k,
-                                                                int(self.use_hist))
+        self.launches_per_run = 1 + capi.lib().tdsa_topk_levels(
+            self.batch, self.length, k, int(self.use_hist) | (int(bool(sorted)) << 1))
         self.trace = trace
         if trace is not None:
             if kk.dtype == torch.float32:

@@ -35,6 +35,10 @@ enum tdsa_status {
 /* Device status bit (tdsa_device_status) besides TDSA_ERR_TIMEOUT: a device-side index
  * (a key-append slot) was outside its buffer; that store was skipped. */
 #define TDSA_STATUS_RANGE 8
+/* Device status bit: a top-k over rows just past one 32768-key segment, started from the
+ * caller's key histograms, found histograms that do not describe the row (their counts
+ * miss the k-th key); that row's output was not written. */
+#define TDSA_STATUS_HIST 16
 
 enum tdsa_dtype { TDSA_F32 = 0, TDSA_F16 = 1, TDSA_BF16 = 2 };
 
@@ -196,7 +200,8 @@ const char* tdsa_last_error(void);
 
 /* Reads (and with reset != 0 clears) the device status word of the current device: the
  * OR of error bits kernels raised (TDSA_ERR_TIMEOUT when a bounded wait ran out,
- * TDSA_STATUS_RANGE when a device-side index was out of range).
+ * TDSA_STATUS_RANGE when a device-side index was out of range, TDSA_STATUS_HIST when a key
+ * histogram did not describe its row).
  * Synchronous. */
 int tdsa_device_status(int* status_out, int reset);
 
@@ -343,7 +348,9 @@ int tdsa_score_topk_noalloc(const void* queries, int64_t q_batch_stride, const f
  * one-segment merge level from the bins the first level passes on).
  */
 size_t tdsa_key_hist_bytes(int batch, int length);
-/* Kernel launches (levels) of one top-k call; with_key_hist: tdsa_topk_hist_ws's plan. */
+/* Kernel launches (levels) of one top-k call.  with_key_hist: bit 0 -- tdsa_topk_hist_ws's
+ * plan (key histograms given), bit 1 -- sorted output.  An unsorted call with histograms on
+ * rows of up to 32768 + 4096 keys is one level. */
 int tdsa_topk_levels(int batch, int length, int k, int with_key_hist);
 int tdsa_topk_hist_ws(const float* scores, int64_t s_batch_stride, int batch, int length,
                       int k, int sorted, void* out_indices, int index_bytes,

@@ -514,7 +514,7 @@ def test_segment_topk_from_histogram_matches_oracle(batch, length, k):
     assert int(hist.abs().sum()) == 0  # consumed and zeroed
 
 
-@pytest.mark.parametrize("length,k", [(40000, 2048), (70000, 512), (32769, 2048)])
+@pytest.mark.parametrize("length,k", [(40000, 2048), (70000, 512), (36865, 2048)])
 def test_segment_topk_merge_level_from_histogram(length, k):
     """Rows longer than one segment on a batch too large for clusters: each segment's top-k
     and then the merge level (explicit indices, started from the bins the first level
@@ -538,6 +538,47 @@ def test_segment_topk_merge_level_from_histogram(length, k):
     val = torch.empty(batch, k, dtype=torch.float32, device="cuda")
     capi.call("tdsa_topk_hist_ws", dev.data_ptr(), dev.stride(0), batch, length, k, 0,
               idx.data_ptr(), 8, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
+              ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+    want_i, want_v = oracle.topk_rows(s, k, sorted=False)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), want_v)
+    assert int(hist.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("length,k", [(32769, 2048), (33001, 1), (34567, 8192),
+                                      (36864, 2048), (36000, 36000 // 5)])
+def test_wide_row_topk_one_level_from_two_histograms(length, k):
+    """Rows just past one 32768-key segment on a batch too large for clusters: one CTA per
+    row takes the row's 32768 + up to 4096 keys in one level, started from the sum of its
+    two segment histograms, with no candidate list (any number of keys may tie in the k-th
+    key's bin).  Heavy ties, +-0, +-inf, denormals, a row of one value, a row of -inf only,
+    against stable_topk in index order; the histograms end zeroed."""
+    from dsa_b200 import _capi as capi
+
+    batch = 24
+    rng = np.random.default_rng(length * 3 + k)
+    s = np.round(rng.normal(size=(batch, length)) * 64).astype(np.float32) / 64
+    s[0, rng.integers(0, length, length // 50)] = -0.0
+    s[0, rng.integers(0, length, length // 50)] = 0.0
+    s[1] = 0.25
+    s[2, rng.integers(0, length, 50)] = np.inf
+    s[2, rng.integers(0, length, length // 3)] = -np.inf
+    s[3] = -np.inf
+    s[4, rng.integers(0, length, 400)] = np.float32(1e-45)
+    s[5, 32700:] = np.float32(7.0)  # ties straddling the segment edge and the tail
+    s[6] = rng.normal(size=length).astype(np.float32)
+    s[7, -3:] = np.float32(100.0)  # the largest keys in the tail
+    dev = cuda(s)
+    hist = cuda(_key_hist_segments(s))
+    lib = capi.lib()
+    assert lib.tdsa_topk_levels(batch, length, k, 1) == 1  # unsorted: one level
+    assert lib.tdsa_topk_levels(batch, length, k, 3) == 2  # sorted: segments + merge
+    nbytes = lib.tdsa_topk_workspace_bytes(batch, length, k)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device="cuda")
+    idx = torch.empty(batch, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(batch, k, dtype=torch.float32, device="cuda")
+    capi.call("tdsa_topk_hist_ws", dev.data_ptr(), dev.stride(0), batch, length, k, 0,
+              idx.data_ptr(), 4, idx.stride(0), val.data_ptr(), val.stride(0), hist.data_ptr(),
               ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
     want_i, want_v = oracle.topk_rows(s, k, sorted=False)
     np.testing.assert_array_equal(idx.cpu().numpy(), want_i)

@@ -107,13 +107,14 @@ def test_exact_plan_matches_function_form(block_size):
         plan.step(l0)  # append-only
 
 
-@pytest.mark.parametrize("block_size,structured,l0", [
-    (64, True, 32760),     # crosses into a second 32768-key segment
-    (16, True, 65530),     # crosses into a third segment at block size 16
-    (128, False, 70001),   # three segments, i.i.d. keys, an odd score-row stride
-    (32, True, 98300),     # crosses into a fourth segment
+@pytest.mark.parametrize("block_size,structured,l0,batch", [
+    (64, True, 32760, 3),     # crosses into a second 32768-key segment
+    (64, False, 32762, 20),   # the same on a batch too large for clusters: wide one-CTA rows
+    (16, True, 65530, 3),     # crosses into a third segment at block size 16
+    (128, False, 70001, 3),   # three segments, i.i.d. keys, an odd score-row stride
+    (32, True, 98300, 3),     # crosses into a fourth segment
 ])
-def test_exact_long_rows_segment_histograms(block_size, structured, l0):
+def test_exact_long_rows_segment_histograms(block_size, structured, l0, batch):
     """Rows longer than one 32768-key top-k segment: the score waves keep one key
     histogram per segment (pruned keys counted in its -inf bin) and the top-k's first level
     starts every segment from its own; exact == dense bit for bit at every step, sorted and
@@ -121,7 +122,7 @@ def test_exact_long_rows_segment_histograms(block_size, structured, l0):
     from dsa_b200.indexer import ScoreTopkPlan
     from dsa_b200.progressive_exact import ExactProgressivePlan
 
-    batch, steps, k = 3, 8, 2048
+    steps, k = 8, 2048
     g = torch.Generator().manual_seed(l0 + block_size)
     total = l0 + steps
     keys = torch.randn(batch, total, 128, generator=g)
