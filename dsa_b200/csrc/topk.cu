@@ -213,7 +213,7 @@ __device__ __forceinline__ void bins_from_top(const uint32_t* h, int nbins, uint
 // general path does.  `hists` (2048 words) is zero on entry; the
 // list holds k - k_rem + in_range <= a.cap entries.  A row copy of kPer keys per thread sits
 // in `rowf`.
-template <int kPer>
+template <int kPer, bool kTail>
 __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int seg, int start,
                                               int n, int k, const float* rowf,
                                               const int32_t* irow, uint32_t* list_key,
@@ -292,10 +292,11 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
       if (e < n && float_to_key(rowf[e]) >= clo) take |= 1u << jj;
     }
   }
-  // a wide row's tail keys [kPer * 1024 + 4 tid, + 4) (rows past one segment, kPer = 32)
+  // kTail: a wide row's tail keys [kPer * 1024 + 4 tid, + 4) (rows past one segment,
+  // kPer = 32), listed after all the main keys
   const int tail0 = kPer * kThreads + 4 * tid;
   uint32_t take_tail = 0u;
-  if (kPer == 32 && n > kPer * kThreads) {
+  if constexpr (kTail) {
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       if (tail0 + c < n && float_to_key(rowf[tail0 + c]) >= clo) take_tail |= 1u << c;
@@ -305,8 +306,8 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
   const uint32_t before = block_excl_scan(static_cast<uint32_t>(__popc(take)) |
                                               (static_cast<uint32_t>(__popc(take_tail)) << 16),
                                           wa, wb, s_total);
-  const uint32_t main_total = *s_total & 0xFFFFu;
-  const uint32_t m_all = main_total + (*s_total >> 16);
+  const uint32_t main_total = kTail ? (*s_total & 0xFFFFu) : *s_total;
+  const uint32_t m_all = kTail ? main_total + (*s_total >> 16) : main_total;
   auto place = [&](uint32_t pos, int e) {
     const uint32_t u = float_to_key(rowf[e]);
     if (whole) {
@@ -316,10 +317,12 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
       list_idx[pos] = gidx(e);
     }
   };
-  uint32_t pos = before & 0xFFFFu;
+  uint32_t pos = kTail ? (before & 0xFFFFu) : before;
   for (uint32_t t = take; t; t &= t - 1u) place(pos++, tbase + __ffs(t) - 1);
-  pos = main_total + (before >> 16);
-  for (uint32_t t = take_tail; t; t &= t - 1u) place(pos++, tail0 + __ffs(t) - 1);
+  if constexpr (kTail) {
+    pos = main_total + (before >> 16);
+    for (uint32_t t = take_tail; t; t &= t - 1u) place(pos++, tail0 + __ffs(t) - 1);
+  }
   if (whole) return;
   __syncthreads();  // the list, in index order
   const uint32_t m = min(m_all, static_cast<uint32_t>(a.cap));
@@ -413,10 +416,13 @@ constexpr int kWideTail = 4 * kThreads;  // keys past one segment a single CTA a
 // take writes the keys above the final range and the lowest-index keys inside it that
 // complete k, in ascending index order, like the general path.  `hists` (2048 words) is zero
 // on entry.
-__device__ void take_wide(const TopkArgs& a, int row, int n, int k, const float* rowf,
-                          const int32_t* irow, uint32_t* hists, uint32_t* wa, uint32_t* wb,
-                          uint32_t* res, uint32_t* s_total, uint32_t clo, uint32_t chi,
-                          uint32_t k_rem) {
+// (a separate function, so that its registers do not weigh on the common path; the output
+// row pointers come in by value)
+__device__ __noinline__ void take_wide(int n, int k, const float* rowf, const int32_t* irow,
+                                       uint32_t* hists, uint32_t* wa, uint32_t* wb,
+                                       uint32_t* res, uint32_t* s_total, uint32_t clo,
+                                       uint32_t chi, uint32_t k_rem, int32_t* oi32,
+                                       int64_t* oi64, float* ov, int32_t* om) {
   constexpr int kMain = 32 * kThreads;
   const int tid = threadIdx.x, lane = tid & 31;
   const int tbase = tid * 32, tail0 = kMain + 4 * tid;
@@ -502,14 +508,6 @@ __device__ void take_wide(const TopkArgs& a, int row, int n, int k, const float*
   const uint32_t bt = block_excl_scan(static_cast<uint32_t>(__popc(gtl)) |
                                           (static_cast<uint32_t>(__popc(etl)) << 16),
                                       wa, wb, s_total);
-  int32_t* oi32 = a.idx_bytes == 4
-                      ? static_cast<int32_t*>(a.out_idx) + static_cast<int64_t>(row) * a.out_idx_stride
-                      : nullptr;
-  int64_t* oi64 = a.idx_bytes == 8
-                      ? static_cast<int64_t*>(a.out_idx) + static_cast<int64_t>(row) * a.out_idx_stride
-                      : nullptr;
-  float* ov = a.out_val ? a.out_val + static_cast<int64_t>(row) * a.out_val_stride : nullptr;
-  int32_t* om = a.mirror ? a.mirror + static_cast<int64_t>(row) * a.mirror_stride : nullptr;
   auto emit = [&](uint32_t& g, uint32_t& eb, bool gt, int e, float x) {
     uint32_t p = 0xFFFFFFFFu;
     if (gt) {
@@ -628,14 +626,18 @@ __device__ void gather_peer_row(const TopkArgs& a, int row) {
 // kPer keys per thread: segments of up to kPer * 1024 keys.  Thread t owns the kPer
 // consecutive elements [kPer*t, kPer*t + kPer) (thread order is index order) and visits
 // them rotated by its lane group, so a warp's 32 shared-memory reads hit 32 banks.
-template <int kPer>
+// kWide (kPer = 32): a row of up to 32768 + 4096 keys in one CTA, the unsorted final level of
+// a row just past one histogram segment (launch_segments picks it by the chunk); the common
+// instantiations carry none of its code.
+template <int kPer, bool kWide>
 __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArgs a) {
+  static_assert(!kWide || kPer == 32, "wide rows run 32 keys per thread");
   extern __shared__ __align__(16) uint32_t sm[];
   __shared__ uint32_t wa[kWarps], wb[kWarps], wc[kWarps];
   __shared__ uint32_t res[4];
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t s_kth, s_total;
-  __shared__ __align__(8) uint64_t s_bar[5];  // a wide row (chunk > kPer * 1024) needs five
+  __shared__ __align__(8) uint64_t s_bar[kWide ? 5 : 4];  // 32 KB pieces of the row
   __shared__ int s_abort;
 
   const int row = blockIdx.y, seg = blockIdx.x;
@@ -665,7 +667,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   // histogram prologue so the two overlap, each thread then loading its own keys past them
   // (fewer than four in a row); else coalesced loads.  A thread's elements lie in one 32 KB
   // piece.
-  const int nbulk = (reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u ? (n & ~3) : 0;
+  // (common rows: whole rows of a multiple of four keys only, loads otherwise)
+  const bool aligned = (reinterpret_cast<uintptr_t>(vrow) & 15u) == 0u;
+  const int nbulk = kWide ? (aligned ? (n & ~3) : 0) : ((aligned && n % 4 == 0) ? n : 0);
   const bool bulk = nbulk > 0;
   const uint32_t bytes = static_cast<uint32_t>(nbulk) * 4u;
   const int npieces = static_cast<int>((bytes + 32767u) / 32768u);
@@ -699,7 +703,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       const int e = w0 + j * 32 + lane;
       if (e < n) rowf[e] = __ldg(vrow + e);
     }
-    for (int e = kPer * kThreads + tid; e < n; e += kThreads) rowf[e] = __ldg(vrow + e);
+    if constexpr (kWide)
+      for (int e = kPer * kThreads + tid; e < n; e += kThreads) rowf[e] = __ldg(vrow + e);
     __syncwarp();
   }
 
@@ -711,15 +716,18 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     // The score kernel already counted this row's keys by their top 12 bits: find the bin of
     // the k-th key (thread t owns bins 4095-4t .. 4092-4t).
     // (a wide row covers two histogram segments: their sum)
-    const int hsegs = (a.chunk + kTopkSegment - 1) / kTopkSegment;
+    constexpr int hsegs = kWide ? 2 : 1;
     uint32_t* rh = a.hist + (static_cast<int64_t>(row) * gridDim.x + seg) * hsegs * kKeyHistBins;
+    // the first segment's four bins outside any loop, so their loads go out together
     uint32_t c[4], tot = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      c[i] = 0u;
-      for (int g = 0; g < hsegs; ++g) c[i] += rh[g * kKeyHistBins + kKeyHistBins - 1 - (4 * tid + i)];
-      tot += c[i];
+    for (int i = 0; i < 4; ++i) c[i] = rh[kKeyHistBins - 1 - (4 * tid + i)];
+    for (int g = 1; g < hsegs; ++g) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c[i] += rh[g * kKeyHistBins + kKeyHistBins - 1 - (4 * tid + i)];
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) tot += c[i];
     if (tid == 0) res[3] = 0u;
     uint32_t dummy;
     uint32_t above = block_excl_scan(tot, wa, wb, &dummy);
@@ -735,9 +743,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
         above += c[i];
       }
     }
+    for (int g = 0; g < hsegs; ++g)  // ready for reuse
 #pragma unroll
-    for (int i = 0; i < 4; ++i)  // ready for reuse
-      for (int g = 0; g < hsegs; ++g) rh[g * kKeyHistBins + kKeyHistBins - 1 - (4 * tid + i)] = 0u;
+      for (int i = 0; i < 4; ++i) rh[g * kKeyHistBins + kKeyHistBins - 1 - (4 * tid + i)] = 0u;
     __syncthreads();
     if (res[3]) {  // (a histogram that does not describe the row leaves the full range)
       clo = res[0] << 20;
@@ -747,13 +755,16 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
       hist_hit = true;
     }
   }
-  const int tail0 = kPer * kThreads + 4 * tid;  // a wide row's four tail keys of this thread
-  if (bulk) {
-    if (tbase < nbulk) mbar_wait(&s_bar[(tbase * 4) >> 15], 0, &s_abort);
-    if (n > kPer * kThreads && tail0 < nbulk) mbar_wait(&s_bar[(tail0 * 4) >> 15], 0, &s_abort);
-    for (int e = max(tbase, nbulk); e < min(tbase + kPer, n); ++e) rowf[e] = __ldg(vrow + e);
-    if (n > kPer * kThreads)
+  if constexpr (kWide) {
+    const int tail0 = kPer * kThreads + 4 * tid;  // this thread's four tail keys
+    if (bulk) {
+      if (tbase < nbulk) mbar_wait(&s_bar[(tbase * 4) >> 15], 0, &s_abort);
+      if (tail0 < nbulk) mbar_wait(&s_bar[(tail0 * 4) >> 15], 0, &s_abort);
+      for (int e = max(tbase, nbulk); e < min(tbase + kPer, n); ++e) rowf[e] = __ldg(vrow + e);
       for (int e = max(tail0, nbulk); e < min(tail0 + 4, n); ++e) rowf[e] = __ldg(vrow + e);
+    }
+  } else {
+    if (bulk && tbase < n) mbar_wait(&s_bar[(tbase * 4) >> 15], 0, &s_abort);
   }
 
   // Keys are computed from the floats on the fly, or (no histogram: the min/max pass
@@ -795,13 +806,20 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     clo = __reduce_min_sync(0xffffffffu, wa[lane]);
     chi = __reduce_max_sync(0xffffffffu, wc[lane]);
   }
-  if constexpr (kPer == 32) {
-    if (n > kPer * kThreads) {  // a wide row: the host routes only unsorted final levels here
+  if constexpr (kWide) {
+    {  // the host routes only unsorted final levels here
       if (hist_hit && static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
-        take_from_bin<kPer>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx, hists, wa,
-                            wc, res, &s_total, clo, chi, k_rem, in_range);
+        take_from_bin<kPer, true>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx,
+                                  hists, wa, wc, res, &s_total, clo, chi, k_rem, in_range);
       } else if (hist_hit) {  // the k-th key's bin holds more keys than the list: no list
-        take_wide(a, row, n, k, rowf, irow, hists, wa, wc, res, &s_total, clo, chi, k_rem);
+        const int64_t orow = row;  // one segment per row
+        take_wide(n, k, rowf, irow, hists, wa, wc, res, &s_total, clo, chi, k_rem,
+                  a.idx_bytes == 4 ? static_cast<int32_t*>(a.out_idx) + orow * a.out_idx_stride
+                                   : nullptr,
+                  a.idx_bytes == 8 ? static_cast<int64_t*>(a.out_idx) + orow * a.out_idx_stride
+                                   : nullptr,
+                  a.out_val ? a.out_val + orow * a.out_val_stride : nullptr,
+                  a.mirror ? a.mirror + orow * a.mirror_stride : nullptr);
       } else if (tid == 0) {
         atomicOr(a.status, TDSA_STATUS_HIST);  // the histograms did not describe the row
       }
@@ -810,8 +828,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   }
   if (hist_hit && !a.sorted && !a.kth_out && a.out_idx &&
       static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
-    take_from_bin<kPer>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx, hists, wa, wc,
-                        res, &s_total, clo, chi, k_rem, in_range);
+    take_from_bin<kPer, false>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx, hists,
+                               wa, wc, res, &s_total, clo, chi, k_rem, in_range);
     return;
   }
 
@@ -1308,10 +1326,11 @@ int launch_segments(TopkArgs a, int rows, int nseg, cudaStream_t stream) {
     TDSA_CUDA_CHECK(cudaGetLastError());
     return TDSA_OK;
   };
-  if (a.chunk <= 4 * kThreads) return run(topk_segment_kernel<4>);
-  if (a.chunk <= 8 * kThreads) return run(topk_segment_kernel<8>);
-  if (a.chunk <= 16 * kThreads) return run(topk_segment_kernel<16>);
-  return run(topk_segment_kernel<32>);
+  if (a.chunk <= 4 * kThreads) return run(topk_segment_kernel<4, false>);
+  if (a.chunk <= 8 * kThreads) return run(topk_segment_kernel<8, false>);
+  if (a.chunk <= 16 * kThreads) return run(topk_segment_kernel<16, false>);
+  if (a.chunk <= 32 * kThreads) return run(topk_segment_kernel<32, false>);
+  return run(topk_segment_kernel<32, true>);  // a row just past one segment (make_plan)
 }
 
 template <int kC>
