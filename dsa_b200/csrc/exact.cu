@@ -9,7 +9,7 @@
 //      one key vector shared by the heads) plus a rounding slack, q/w kept for the next
 //      step, per-block bounds U_b + maxnorm_b * c (blocks with new keys: +inf, as
 //      replay.py:263-266), and wave 1 = the blocks holding a previous top-k key or new keys
-//      (hot first, replay.py:153-169);
+//      (hot first, replay.py:153-169) -- every block when those leave at most 1/16 out;
 //   2. wave 1 scored on the tensor cores; the epilogue adds every score to the row's key
 //      histogram and writes the exact block maxima;
 //   3. wave2 (one CTA per sequence): tau = the lower edge of the key bin holding the k-th
@@ -102,12 +102,18 @@ struct PrepArgs {
 // Blocks (and previous top-k entries) whose loads a thread issues before any barrier: the
 // whole state of a sequence of up to 2048 blocks arrives in one round trip.
 constexpr int kPrepUnroll = 2;
+// When wave 1 already covers all but at most 1/kAllHotFraction of a sequence's blocks, the
+// rest join wave 1 too: the few blocks left could not pay for tau and a second wave (on
+// i.i.d. caches the previous top-2048 touch nearly every block and nothing is pruned), and
+// scoring a block never changes the top-k.
+constexpr int kAllHotFraction = 16;
 
 __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs a) {
   pdl_wait();  // every global access follows the previous kernel
   pdl_launch_dependents();
   extern __shared__ int8_t hot[];  // [nb]: this step's wave-1 flags
   __shared__ double wsum[32];
+  __shared__ int s_cold;  // blocks outside wave 1
   static_assert(kThreads == 8192 / 8, "one thread per 8 query elements");
   __shared__ uint32_t wtot[32];
   __shared__ uint32_t sbase[4];
@@ -118,6 +124,7 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
   const int first_new = a.init ? 0 : (a.length > a.prev_length ? a.prev_length / a.bs : nb);
   const int64_t brow = static_cast<int64_t>(seq) * a.nb_stride;
   if (seq == 0 && tid == 0) a.counters[1] = 0;  // wave 2's list (used after this)
+  if (tid == 0) s_cold = 0;
 
   // ---- every load of the step's state, issued before the first barrier.  Thread t owns q
   // elements [8t, 8t + 8) (one 16-byte load; rows are 16-byte aligned: the scoring kernels'
@@ -249,6 +256,17 @@ __global__ void __launch_bounds__(kThreads) exact_prepare_kernel(const PrepArgs 
     }
   }
   __syncthreads();  // hot[] complete
+  if (!a.init) {
+    int cold = 0;
+    for (int b = tid; b < nb; b += kThreads) cold += hot[b] == 0;
+    cold = __reduce_add_sync(0xffffffffu, cold);
+    if ((tid & 31) == 0 && cold) atomicAdd(&s_cold, cold);
+    __syncthreads();
+    if (s_cold > 0 && s_cold * kAllHotFraction <= nb) {  // (the same for the whole CTA)
+      for (int b = tid; b < nb; b += kThreads) hot[b] = 1;
+      __syncthreads();
+    }
+  }
   for (int b = tid; b < nb; b += kThreads) a.flag[brow + b] = hot[b];
   emit_tiles(hot, nb, 1, a.bpt, seq, a.tile_seq, a.tile_blk, a.counters, wtot, sbase);
 }

@@ -13,7 +13,8 @@ Schedule of one step (per sequence):
      rounding of the two computed scores the bound links.
   2. bound_b = U_b + maxnorm_b * (c + slack) for blocks fully seen last step; +inf for
      blocks holding keys that are new at this step (replay.py:263-266).
-  3. wave 1 scores the hot blocks (those holding a previous top-k key) and new blocks;
+  3. wave 1 scores the hot blocks (those holding a previous top-k key) and new blocks --
+     every block when those leave at most 1/16 of the blocks out;
      tau = the lower edge of the key bin (the top 24 bits of the order-preserving float
      key, found with two 4096-bin histograms) that holds the k-th largest wave-1 score --
      a lower bound of that score, read from histograms instead of a second top-k;
@@ -33,6 +34,7 @@ from .indexer import full_scores
 from .topk import stable_topk
 
 GAMMA = 2.0 ** -12
+ALL_HOT_FRACTION = 16  # wave 1 takes every block when at most 1/16 of them would be left
 
 
 def _float_to_key(v: float) -> int:
@@ -122,6 +124,9 @@ def exact_step(state: ExactState, q, w, keys):
     hot = np.zeros(nblocks, dtype=bool)
     hot[state.topk // bs] = True
     hot[first_new:] = True
+    cold = int((~hot).sum())
+    if 0 < cold and cold * ALL_HOT_FRACTION <= nblocks:  # the last few cold blocks join wave 1
+        hot[:] = True
     full = full_scores(q, w, keys)
     key_block = np.arange(length) // bs
     wave1 = hot[key_block]
