@@ -23,8 +23,15 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
+#include "timeline.cuh"
 
 namespace tdsa {
+
+// (outside the unnamed namespace: the timeline readers keep external C linkage)
+// timeline builds, per CTA: 0 entry, 1 past the dependency wait (thread 0); 2 first stage
+// landed, 3 first refilled stage landed, 4 last MMA issued (MMA thread); 5 GEMM complete,
+// 6 peer's partial sums received (first epilogue thread); 7 exit (thread 0)
+TDSA_TL_DECL(proj, 128, 8)
 
 namespace {
 
@@ -457,8 +464,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int split = (nk + 1) >> 1;
   const int kbeg = rank ? split : 0, kend = rank ? nk : split;
   const int nloc = kend - kbeg;
+  __shared__ unsigned int tl_launch;
 
   if (threadIdx.x == 0) {
+    tl_launch = TDSA_TL_TICKET(proj);
+    TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 0);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 5);  // the MMA commit + one arrival per epilogue warp
@@ -518,6 +528,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sinv[jj] = powf(a.theta, -static_cast<float>(jj) / static_cast<float>(hf));
   }
   pdl_wait();  // hidden states and positions may come from the previous kernel
+  if (threadIdx.x == 0) TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 1);
   pdl_launch_dependents();
 
   if (warp == 0) {
@@ -555,6 +566,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int it = 0; it < nloc; ++it) {
         const int s = it % kStages;
         if (!mbar_wait(&full[s], (it / kStages) & 1u, abort_flag)) break;
+        if (it == 0) TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 2);
+        if (it == pre) TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 3);
         tc_fence_after();
         const uint32_t w_addr = smem_u32(smem + s * kStage);
         const uint32_t x_addr = w_addr + kWTileBytes;
@@ -565,6 +578,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         umma_commit(&empty[s]);
       }
+      TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 4);
       umma_commit(accfull);
       umma_commit(done);
       volatile int no_abort = 0;
@@ -639,6 +653,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // every epilogue warp is past its last read of the ring (the GEMV) before the ring is
     // reused for staging; the MMA commit alone does not order those reads
     ok = epi_all(ok) && mbar_wait(accfull, 0, abort_flag);
+    if (et == 0) TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 5);
     float* stage = reinterpret_cast<float*>(smem);
     if (ok) {
       tc_fence_after();
@@ -678,6 +693,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool j_ok = epi_all(ok && !*abort_flag);
       if (j_ok && !early) build_rope_table(spos, sinv, half, kN, kTabStride, tcos, tsin);
       const bool got = j_ok && mbar_wait_cluster(recv, 0, abort_flag);
+      if (et == 0) TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 6);
       if (epi_all(got && !*abort_flag)) {
         const float* rbuf = recv_buf;
 #pragma unroll
@@ -751,6 +767,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem_base, kN);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, TDSA_ERR_TIMEOUT);
+  if (threadIdx.x == 0) TDSA_TL_REC(proj, 128, 8, tl_launch, blockIdx.x, 7);
 }
 
 template <bool kBF16>

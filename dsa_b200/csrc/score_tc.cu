@@ -20,8 +20,14 @@
 #include "kernels.cuh"
 #include "ptx.cuh"
 #include "score_epilogue.cuh"
+#include "timeline.cuh"
 
 namespace tdsa {
+
+// (outside the unnamed namespace: the timeline readers keep external C linkage)
+// timeline builds: per CTA (thread 0, the TMA producer) entry, past the dependency wait,
+// last key tile issued, exit
+TDSA_TL_DECL(score, 148, 4)
 
 namespace {
 
@@ -86,6 +92,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hbar + kEpiGroups);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint32_t* shist = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(full) + kBarrierBytes);
+  unsigned int tl_launch = 0;
+  if (threadIdx.x == 0) {
+    tl_launch = TDSA_TL_TICKET(score);
+    TDSA_TL_REC(score, 148, 4, tl_launch, blockIdx.x, 0);
+  }
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -126,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   pdl_wait();  // q, w and the histogram may come from the previous kernel
+  if (threadIdx.x == 0) TDSA_TL_REC(score, 148, 4, tl_launch, blockIdx.x, 1);
   pdl_launch_dependents();
 
   if (warp == 0) {
@@ -156,6 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(dst + kHalfBytes, &kmap, &full[s], 64, tt * kTileKeys, b, pol_k);
         ++it;
       }
+      TDSA_TL_REC(score, 148, 4, tl_launch, blockIdx.x, 2);
       // Let every issued copy land before the CTA can exit (bounded, abort or not).
       volatile int no_abort = 0;
       for (uint32_t s = 0; s < kStages && s < it; ++s) {
@@ -291,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, TDSA_ERR_TIMEOUT);
+  if (threadIdx.x == 0) TDSA_TL_REC(score, 148, 4, tl_launch, blockIdx.x, 3);
 }
 
 template <bool kBF16>

@@ -33,8 +33,15 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
+#include "timeline.cuh"
 
 namespace tdsa {
+
+// (outside the unnamed namespace: the timeline readers keep external C linkage)
+// timeline builds, per row of a one-segment launch (thread 0): 0 entry, 1 past the
+// dependency wait, 2 row copy landed and the histogram's bin read, 3 candidate list written,
+// 4 the k-th key found, 5 output written (the histogram-started unsorted path)
+TDSA_TL_DECL(topk, 64, 6)
 
 namespace {
 
@@ -212,7 +219,7 @@ __device__ __forceinline__ void bins_from_top(const uint32_t* h, int nbins, uint
 // shorter than k and adds its output's key bins to the next level's histogram, as the
 // general path does.  `hists` (2048 words) is zero on entry; the
 // list holds k - k_rem + in_range <= a.cap entries.  A row copy of kPer keys per thread sits
-// in `rowf`.
+// in `rowf`.  `tl_launch`: the launch number of a timeline build (unused otherwise).
 template <int kPer, bool kTail>
 __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int seg, int start,
                                               int n, int k, const float* rowf,
@@ -220,7 +227,8 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
                                               uint32_t* list_idx, uint32_t* hists,
                                               uint32_t* wa, uint32_t* wb, uint32_t* res,
                                               uint32_t* s_total, uint32_t clo, uint32_t chi,
-                                              uint32_t k_rem, uint32_t in_range) {
+                                              uint32_t k_rem, uint32_t in_range,
+                                              unsigned int tl_launch) {
   const int tid = threadIdx.x, lane = tid & 31;
   constexpr int kLog = kPer == 32 ? 5 : kPer == 16 ? 4 : kPer == 8 ? 3 : 2;
   const int rot = lane >> (5 - kLog);
@@ -325,6 +333,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
   }
   if (whole) return;
   __syncthreads();  // the list, in index order
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 3);
   const uint32_t m = min(m_all, static_cast<uint32_t>(a.cap));
 
   // ---- the exact k-th key inside the bin: bits 19..9, then 8..0
@@ -359,6 +368,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     }
   }
 
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 4);
   // ---- the taken keys: above the final range, and the first fk inside it; thread t takes
   // list entries [t * per, t * per + per)
   const int per = (static_cast<int>(m) + kThreads - 1) / kThreads;
@@ -386,6 +396,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     if (p != 0xFFFFFFFFu) put(p, list_idx[i], u, false);
     if (nh) add_to_bin(nh, p < uk, u >> 20);
   }
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 5);
 }
 
 // key(x) >= c for an order-preserving key threshold c, as float compares where that is exact:
@@ -673,7 +684,10 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   const bool bulk = nbulk > 0;
   const uint32_t bytes = static_cast<uint32_t>(nbulk) * 4u;
   const int npieces = static_cast<int>((bytes + 32767u) / 32768u);
+  unsigned int tl_launch = 0;
   if (tid == 0) {
+    tl_launch = TDSA_TL_TICKET(topk);
+    if (seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 0);
     s_abort = 0;
     s_kth = 0xFFFFFFFFu;
     if (bulk) {
@@ -684,6 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
   __syncthreads();
   pdl_wait();  // the scores and the histogram come from the previous kernel
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 1);
   pdl_launch_dependents();
   if (a.gather) gather_peer_row(a, row);
   if (bulk) {
@@ -793,6 +808,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     }
   }
   __syncthreads();
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 2);
   if (s_abort) {
     // a bulk copy did not land in time: report, and let the copies in flight finish
     if (tid == 0) {
@@ -810,7 +826,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     {  // the host routes only unsorted final levels here
       if (hist_hit && static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
         take_from_bin<kPer, true>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx,
-                                  hists, wa, wc, res, &s_total, clo, chi, k_rem, in_range);
+                                  hists, wa, wc, res, &s_total, clo, chi, k_rem, in_range,
+                                  tl_launch);
       } else if (hist_hit) {  // the k-th key's bin holds more keys than the list: no list
         const int64_t orow = row;  // one segment per row
         take_wide(n, k, rowf, irow, hists, wa, wc, res, &s_total, clo, chi, k_rem,
@@ -829,7 +846,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   if (hist_hit && !a.sorted && !a.kth_out && a.out_idx &&
       static_cast<uint32_t>(k) - k_rem + in_range <= static_cast<uint32_t>(a.cap)) {
     take_from_bin<kPer, false>(a, row, seg, start, n, k, rowf, irow, list_key, list_idx, hists,
-                               wa, wc, res, &s_total, clo, chi, k_rem, in_range);
+                               wa, wc, res, &s_total, clo, chi, k_rem, in_range, tl_launch);
     return;
   }
 
