@@ -41,7 +41,6 @@ constexpr int kWTileBytes = 128 * kKChunk * 2;     // 16 KiB
 constexpr int kRingBytes = 192 * 1024;             // stage ring budget
 constexpr int kWwChunkBytes = kKChunk * 4;       // the head's W_w slice per stage (f32)
 constexpr int kBarrierBytes = 2048;  // barriers, then positions [kN] and frequencies [64]
-constexpr int kExStride = 33;                      // padded row of the RoPE exchange buffer
 
 struct ProjArgs {
   const float* ww;          // [64][hidden] float32
