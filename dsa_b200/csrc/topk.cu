@@ -316,6 +316,8 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
                                           wa, wb, s_total);
   const uint32_t main_total = kTail ? (*s_total & 0xFFFFu) : *s_total;
   const uint32_t m_all = kTail ? main_total + (*s_total >> 16) : main_total;
+  // a listed key inside the bin is also counted at once by key bits 19..9 (the first
+  // narrowing level below), so the level needs no pass of its own over the list
   auto place = [&](uint32_t pos, int e) {
     const uint32_t u = float_to_key(rowf[e]);
     if (whole) {
@@ -323,6 +325,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     } else if (pos < static_cast<uint32_t>(a.cap)) {
       list_key[pos] = u;
       list_idx[pos] = gidx(e);
+      if (u <= chi) atomicAdd(&hists[(u >> 9) & 0x7FFu], 1u);  // the bin's keys (>= clo)
     }
   };
   uint32_t pos = kTail ? (before & 0xFFFFu) : before;
@@ -332,16 +335,11 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     for (uint32_t t = take_tail; t; t &= t - 1u) place(pos++, tail0 + __ffs(t) - 1);
   }
   if (whole) return;
-  __syncthreads();  // the list, in index order
+  __syncthreads();  // the list, in index order, and its first-level counts
   if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 3);
   const uint32_t m = min(m_all, static_cast<uint32_t>(a.cap));
 
-  // ---- the exact k-th key inside the bin: bits 19..9, then 8..0
-  for (uint32_t i = tid; i < m; i += kThreads) {
-    const uint32_t u = list_key[i];
-    if (u <= chi) atomicAdd(&hists[(u >> 9) & 0x7FFu], 1u);  // the bin's keys (>= clo)
-  }
-  __syncthreads();
+  // ---- the exact k-th key inside the bin: bits 19..9 (counted while listing), then 8..0
   uint32_t c4[4];
   bins_from_top(hists, 2048, c4);
   pick_bin(c4, 2048, k_rem, wa, wb, res);
