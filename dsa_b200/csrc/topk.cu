@@ -40,8 +40,9 @@ namespace tdsa {
 // (outside the unnamed namespace: the timeline readers keep external C linkage)
 // timeline builds, per row of a one-segment launch (thread 0): 0 entry, 1 past the
 // dependency wait, 2 row copy landed and the histogram's bin read, 3 candidate list written,
-// 4 the k-th key found, 5 output written (the histogram-started unsorted path)
-TDSA_TL_DECL(topk, 64, 6)
+// 4 the k-th key found, 5 output written, 6 this thread's classification pass done (the
+// histogram-started unsorted path)
+TDSA_TL_DECL(topk, 64, 7)
 
 namespace {
 
@@ -300,6 +301,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
       if (e < n && float_to_key(rowf[e]) >= clo) take |= 1u << jj;
     }
   }
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 7, tl_launch, row, 6);
   // kTail: a wide row's tail keys [kPer * 1024 + 4 tid, + 4) (rows past one segment,
   // kPer = 32), listed after all the main keys
   const int tail0 = kPer * kThreads + 4 * tid;
@@ -336,7 +338,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
   }
   if (whole) return;
   __syncthreads();  // the list, in index order, and its first-level counts
-  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 3);
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 7, tl_launch, row, 3);
   const uint32_t m = min(m_all, static_cast<uint32_t>(a.cap));
 
   // ---- the exact k-th key inside the bin: bits 19..9 (counted while listing), then 8..0
@@ -366,7 +368,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     }
   }
 
-  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 4);
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 7, tl_launch, row, 4);
   // ---- the taken keys: above the final range, and the first fk inside it; thread t takes
   // list entries [t * per, t * per + per)
   const int per = (static_cast<int>(m) + kThreads - 1) / kThreads;
@@ -394,7 +396,7 @@ __device__ __forceinline__ void take_from_bin(const TopkArgs& a, int row, int se
     if (p != 0xFFFFFFFFu) put(p, list_idx[i], u, false);
     if (nh) add_to_bin(nh, p < uk, u >> 20);
   }
-  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 5);
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 7, tl_launch, row, 5);
 }
 
 // key(x) >= c for an order-preserving key threshold c, as float compares where that is exact:
@@ -685,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   unsigned int tl_launch = 0;
   if (tid == 0) {
     tl_launch = TDSA_TL_TICKET(topk);
-    if (seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 0);
+    if (seg == 0) TDSA_TL_REC(topk, 64, 7, tl_launch, row, 0);
     s_abort = 0;
     s_kth = 0xFFFFFFFFu;
     if (bulk) {
@@ -696,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
   for (int i = tid; i < kHists * kBins; i += kThreads) hists[i] = 0u;
   __syncthreads();
   pdl_wait();  // the scores and the histogram come from the previous kernel
-  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 1);
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 7, tl_launch, row, 1);
   // Full-segment rows started from the histogram let the next kernel launch only once their
   // row copy has landed (below): a dependent query projection that starts staging its
   // weights during the copy slows this kernel's later phases more than it gains (config-4
@@ -811,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_segment_kernel(const TopkArg
     }
   }
   __syncthreads();
-  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 6, tl_launch, row, 2);
+  if (tid == 0 && seg == 0) TDSA_TL_REC(topk, 64, 7, tl_launch, row, 2);
   if (late_trigger) pdl_launch_dependents();
   if (s_abort) {
     // a bulk copy did not land in time: report, and let the copies in flight finish

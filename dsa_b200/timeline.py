@@ -15,8 +15,13 @@ kernel).  For every layer it reports, as medians over layers and steps:
 - inside the projection: first ring stage landed, first refilled stage landed, last MMA
   issued, GEMM complete, the peer's partial sums received, exit (median CTA; exit the last);
 - inside the score: last key tile issued (median CTA), exit (last CTA);
-- inside the top-k: row copy landed, candidate list written, k-th key found, output
-  written (median row; and the last row).
+- inside the top-k: row copy landed, classification pass done (thread 0; median, 75th
+  percentile and slowest row), candidate list written, k-th key found, output written
+  (median row; and the last row).
+
+``--no-projection`` issues the chain without the query projection (run once before, so
+that every layer has its queries): score and top-k only, to see each one without the
+projection's launches beside it.
 
 Then the read ceiling of the same key bytes: the score kernel's key-tile stream with no
 arithmetic (a 4-stage ring per SM of two 64-column swizzled boxes per tile, as the score
@@ -35,7 +40,7 @@ import torch
 from . import _capi as capi
 from .build import LIB_TIMELINE
 
-SLOTS = {"proj": (128, 8), "score": (148, 4), "topk": (64, 6)}
+SLOTS = {"proj": (128, 8), "score": (148, 4), "topk": (64, 7)}
 
 
 def _reader(lib, name):
@@ -58,7 +63,8 @@ def _launch_rows(arr, tickets, name, launch):
     return [arr[(e * ncta + c) * nslot:(e * ncta + c + 1) * nslot] for c in range(ncta)]
 
 
-def chain(layers: int, batch: int, length: int, steps: int, device: torch.device) -> dict:
+def chain(layers: int, batch: int, length: int, steps: int, device: torch.device,
+          projection: bool = True) -> dict:
     from .indexer import ScoreTopkPlan
     from .sidecar import QueryProjector
 
@@ -78,9 +84,13 @@ def chain(layers: int, batch: int, length: int, steps: int, device: torch.device
     proj = [QueryProjector(wq[i], ww[i], batch) for i in range(layers)]
     plans = [ScoreTopkPlan(proj[i].q, proj[i].w, keys[i], k) for i in range(layers)]
 
+    for i in range(layers):
+        proj[i].project(x[i], pos)
+
     def step():
         for i in range(layers):
-            proj[i].project(x[i], pos)
+            if projection:
+                proj[i].project(x[i], pos)
             plans[i].score()
             plans[i].select()
 
@@ -101,29 +111,35 @@ def chain(layers: int, batch: int, length: int, steps: int, device: torch.device
         arr = {name: rd[name]()[0] for name in SLOTS}
         prev_end = None
         for i in range(layers):
-            p = _launch_rows(arr["proj"], tick["proj"], "proj", i)
             s = _launch_rows(arr["score"], tick["score"], "score", i)
             t = _launch_rows(arr["topk"], tick["topk"], "topk", i)
-            p_wait = min(r[1] for r in p)
-            p_exit = max(r[7] for r in p)
             s_wait = min(r[1] for r in s)
             s_exit = max(r[3] for r in s)
             t_wait = min(r[1] for r in t)
             t_end = max(r[5] for r in t)
             if prev_end is not None:
-                add("hand-off top-k -> projection", p_wait - prev_end)
                 add("layer (top-k end to top-k end)", t_end - prev_end)
-            for j, name in ((2, "first stage landed"), (3, "first refilled stage landed"),
-                            (4, "last MMA issued"), (5, "GEMM complete"),
-                            (6, "peer partial sums received")):
-                add(f"projection: wait -> {name}", S.median(r[j] - r[1] for r in p))
-            add("projection: wait -> exit (last CTA)", p_exit - p_wait)
-            add("hand-off projection -> score", s_wait - p_exit)
+            if projection:
+                p = _launch_rows(arr["proj"], tick["proj"], "proj", i)
+                p_wait = min(r[1] for r in p)
+                p_exit = max(r[7] for r in p)
+                if prev_end is not None:
+                    add("hand-off top-k -> projection", p_wait - prev_end)
+                for j, name in ((2, "first stage landed"), (3, "first refilled stage landed"),
+                                (4, "last MMA issued"), (5, "GEMM complete"),
+                                (6, "peer partial sums received")):
+                    add(f"projection: wait -> {name}", S.median(r[j] - r[1] for r in p))
+                add("projection: wait -> exit (last CTA)", p_exit - p_wait)
+                add("hand-off projection -> score", s_wait - p_exit)
             add("score: wait -> last key tile issued", S.median(r[2] - r[1] for r in s))
             add("score: wait -> exit (last CTA)", s_exit - s_wait)
             add("score: exit spread (last - first CTA)",
                 s_exit - min(r[3] for r in s))
             add("hand-off score -> top-k", t_wait - s_exit)
+            classify = sorted(r[6] - r[2] for r in t)
+            add("top-k: row copy landed -> classification done", S.median(classify))
+            add("top-k: ... (75th percentile row)", classify[(3 * len(classify)) // 4])
+            add("top-k: ... (slowest row)", classify[-1])
             for j, name in ((2, "row copy landed"), (3, "candidate list written"),
                             (4, "k-th key found"), (5, "output written")):
                 add(f"top-k: wait -> {name}", S.median(r[j] - r[1] for r in t))
@@ -197,20 +213,26 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--length", type=int, default=32768)
     ap.add_argument("--steps", type=int, default=6)
+    ap.add_argument("--no-projection", action="store_true",
+                    help="score and top-k only (the projection runs once, before)")
     args = ap.parse_args()
     if not LIB_TIMELINE.exists():
         raise SystemExit(f"{LIB_TIMELINE} is missing: python -m dsa_b200.build --timeline")
     capi.LIB_PATH = LIB_TIMELINE  # before the first library call
     device = torch.device("cuda", torch.cuda.current_device())
-    res = chain(args.layers, args.batch, args.length, args.steps, device)
-    print(f"config-4 layer chain, batch {args.batch}, {args.length} keys, {args.layers} layers, "
-          f"medians over {args.steps} steps (us)")
+    res = chain(args.layers, args.batch, args.length, args.steps, device,
+                projection=not args.no_projection)
+    what = "score + top-k only" if args.no_projection else "project, score, top-k"
+    print(f"config-4 layer chain ({what}), batch {args.batch}, {args.length} keys, "
+          f"{args.layers} layers, medians over {args.steps} steps (us)")
     for name, v in res.items():
         print(f"  {name:48s} {v:8.2f}")
-    print("key stream of one score launch "
-          f"({args.batch * args.length * 256 / 1e6:.1f} MB), 8 rotating caches (us, GB/s)")
-    for name, (us, gbs) in read_ceiling(args.batch, args.length, device).items():
-        print(f"  {name:64s} {us:8.2f} {gbs:8.0f}")
+    if not args.no_projection:
+        print("key stream of one score launch "
+              f"({args.batch * args.length * 256 / 1e6:.1f} MB), 8 rotating caches (us, GB/s)")
+    if not args.no_projection:
+        for name, (us, gbs) in read_ceiling(args.batch, args.length, device).items():
+            print(f"  {name:64s} {us:8.2f} {gbs:8.0f}")
     status = capi.device_status(True)
     print(f"device status {status}")
     if status:
