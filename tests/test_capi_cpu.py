@@ -25,6 +25,17 @@ def test_library_exports_every_declared_function(lib):
         assert name in capi.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def test_library_carries_no_timeline_instrumentation(lib):
+    # the device timeline (TDSA_TIMELINE) belongs to the measurement build
+    # libtdsa_timeline.so only; the product library must not record or export it
+    from dsa_b200.build import LIB, LIB_TIMELINE
+
+    assert capi.LIB_PATH == LIB and LIB_TIMELINE != LIB
+    for name in ("tdsa_timeline_proj", "tdsa_timeline_score", "tdsa_timeline_topk",
+                 "tdsa_timeline_read_stream"):
+        assert not hasattr(lib, name), f"{name} is exported by the product library"
+
+
 def test_version_and_empty_error(lib):
     assert b"sm_100a" in lib.tdsa_version()
 
